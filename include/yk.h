@@ -1,0 +1,201 @@
+/*
+ * yk.h -- C-ABI of the B200 speculative draft->verify module (libyk.so).
+ *
+ * This is the boundary the reference's Swift host would bind (module map +
+ * thin Swift shim).  Everything above it -- Scheduler's
+ * draft/verify loop, SequenceRequest, PagedKVCache page tables and the
+ * BlockAllocator free list -- stays on the host; everything below it runs as
+ * hand-written sm_100a kernels on one CUDA stream per engine.
+ *
+ * Conventions
+ *   - Plain C types only; every call returns a yk_status (YK_OK == 0) and never
+ *     aborts.  yk_last_error() returns the calling thread's last message.
+ *   - Host arrays passed in are borrowed for the duration of the call.
+ *     Results written to host arrays are complete when the call returns
+ *     (the call synchronises its stream, like the reference's
+ *     commit(); waitUntilCompleted()).
+ *   - Device memory (weights, KV pool, logits, draft probabilities) is owned by
+ *     the handles and freed by the matching *_destroy.
+ *   - A handle is not re-entrant: one host thread (the Scheduler actor) drives
+ *     it.  One engine per GPU; sequences shard across engines/processes.
+ *
+ * Reference citations are relative to the reference project root,
+ * S/ = Sources/yanaiengine/.
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t yk_status;
+#define YK_OK               0
+#define YK_ERR_ARG          1  /* bad shape, token >= vocab, block id outside the pool ... */
+#define YK_ERR_OOM          2  /* device allocation failed                               */
+#define YK_ERR_CUDA         3  /* CUDA runtime/driver error                              */
+#define YK_ERR_NCCL         4  /* NCCL error (tensor-parallel target only)               */
+#define YK_ERR_TIMEOUT      5  /* a bounded device-side wait gave up                     */
+#define YK_ERR_DEVICE_CHECK 6  /* an in-kernel bounds check fired                        */
+#define YK_ERR_UNSUPPORTED  7  /* shape/dtype combination this build does not run        */
+
+#define YK_DTYPE_F32  0
+#define YK_DTYPE_BF16 1
+
+#define YK_ACT_SILU      0 /* SwiGLU, silu_kernel S/gemm.metal:405-413           */
+#define YK_ACT_GELU_TANH 1 /* GeGLU, gelu_kernel S/gemm.metal:231-241 (Gemma-2)  */
+
+#define YK_BLOCK_SIZE 16   /* tokens per KV page, S/LlamaModel.swift:47         */
+
+typedef struct yk_engine  yk_engine;
+typedef struct yk_model   yk_model;
+typedef struct yk_kv_pool yk_kv_pool;
+typedef struct yk_sampler yk_sampler;
+
+/*
+ * Model shape and numerics.  Replaces LlamaConfig (S/LlamaModel.swift:301-362)
+ * and GemmaConfig (S/GemmaModel.swift:98-118) with explicit head_dim / ffn_dim
+ * (the reference derives them: S/LlamaBlock.swift:69-72) and the constants the
+ * reference hard-codes (RoPE base, eps, caps, window schedule).
+ */
+typedef struct yk_model_config {
+    int32_t vocab_size;
+    int32_t d_model;
+    int32_t n_layers;
+    int32_t n_heads;
+    int32_t n_kv_heads;
+    int32_t head_dim;            /* 64, 128 or 256                                   */
+    int32_t ffn_dim;
+    float   rope_theta;          /* 1e4 (S/gemm.metal:675) or 5e5 (Llama-3)           */
+    float   rms_eps;             /* 1e-5 Llama (S/LlamaModel.swift:283), 1e-6 Gemma   */
+    float   attn_cap;            /* 0 = off; 50 Gemma-2 (S/GemmaModel.swift:44)       */
+    float   final_cap;           /* 0 = off; 30 (S/LMHead.swift:34)                   */
+    int32_t window;              /* 0 = global; sliding window (S/gemm.metal:572)     */
+    int32_t window_layer_parity; /* window on layers l%2==parity (0: even, as
+                                    S/GemmaModel.swift:39-43); -1 = every layer      */
+    int32_t act;                 /* YK_ACT_*                                          */
+    int32_t ref_compat;          /* 1 = reproduce LinearLayer's bias 0.1 + ReLU on
+                                    every projection and the unconditional LM-head
+                                    cap 30 (S/LinearLayer.swift:29,61; S/LMHead.swift:20-35) */
+    int32_t dtype;               /* YK_DTYPE_*: weights, activations and KV pool      */
+    int32_t max_tokens;          /* largest T of one forward step (sizes workspaces)  */
+    int32_t max_seqs;            /* largest batch B of one forward step               */
+} yk_model_config;
+
+/* Logical tensors of a model, all [out x in] row-major unless noted. */
+#define YK_T_EMBED      0  /* [vocab x d]          EmbeddingLayer.weights        */
+#define YK_T_WQ         1  /* [H*dh x d]           queryProj                     */
+#define YK_T_WK         2  /* [Hkv*dh x d]         keyProj                       */
+#define YK_T_WV         3  /* [Hkv*dh x d]         valueProj                     */
+#define YK_T_WO         4  /* [d x H*dh]           outputProj                    */
+#define YK_T_WGATE      5  /* [ffn x d]            gateProj                      */
+#define YK_T_WUP        6  /* [ffn x d]            upProj                        */
+#define YK_T_WDOWN      7  /* [d x ffn]            downProj                      */
+#define YK_T_NORM1      8  /* [d]                  rmsGamma1                     */
+#define YK_T_NORM2      9  /* [d]                  rmsGamma2                     */
+#define YK_T_FINAL_NORM 10 /* [d]                  finalNormGamma                */
+#define YK_T_LM_HEAD    11 /* [vocab x d]          LMHead.projection             */
+
+#define YK_LAYOUT_OUT_IN 0 /* [out x in], this module's layout                     */
+#define YK_LAYOUT_IN_OUT 1 /* [in x out], the reference's LinearLayer layout
+                              (S/LinearLayer.swift:33-38); transposed on upload    */
+
+/* ---- errors -------------------------------------------------------------- */
+/* Copies the calling thread's last error message (NUL-terminated); returns its length. */
+int32_t yk_last_error(char* buf, size_t buf_len);
+
+/* ---- engine: one GPU, one stream.  Replaces MetalEngine (S/MetalEngine.swift:6-25). */
+yk_status yk_engine_create(int32_t device, yk_engine** out);
+void      yk_engine_destroy(yk_engine* e);
+/* The engine's cudaStream_t, for callers that time work with CUDA events. */
+yk_status yk_engine_stream(yk_engine* e, void** stream);
+yk_status yk_engine_sync(yk_engine* e);
+/* Reads and clears the device error word set by in-kernel checks and bounded waits. */
+yk_status yk_engine_device_error(yk_engine* e, uint32_t* code);
+/* Number of kernels this engine has launched (all of this module's kernels). */
+uint64_t  yk_engine_launch_count(yk_engine* e);
+
+/* ---- model: LlamaModel / GemmaModel weights + forward workspaces. -------- */
+/* Random init on the device: matrices N(0, init_std) from Philox(seed), norms 1
+ * (the reference fills U(-1,1): S/Tensor.swift:47-52 -- the configs ask for N(0,0.02)). */
+yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, uint64_t seed, float init_std,
+                          yk_model** out);
+void      yk_model_destroy(yk_model* m);
+yk_status yk_model_get_config(const yk_model* m, yk_model_config* out);
+yk_status yk_model_tensor_shape(const yk_model* m, int32_t tensor, int64_t* rows, int64_t* cols);
+/* Upload one logical tensor from fp32 host memory (converted to the model dtype). */
+yk_status yk_model_set_tensor(yk_model* m, int32_t tensor, int32_t layer, const float* host,
+                              int32_t layout);
+/* Download one logical tensor as fp32 [out x in]. */
+yk_status yk_model_get_tensor(yk_model* m, int32_t tensor, int32_t layer, float* host);
+
+/* ---- paged KV pool.  Replaces BlockAllocator's MTLBuffers
+ * (S/BlockAllocator.swift:13-36).  Block ids, the free list and the page
+ * tables stay with the caller (BlockAllocator / PagedKVCache); a block id
+ * covers every layer: pool layout [block][layer][K|V][kv_head][16][head_dim]. */
+yk_status yk_kv_pool_create(yk_engine* e, const yk_model_config* cfg, int32_t num_blocks,
+                            yk_kv_pool** out);
+void      yk_kv_pool_destroy(yk_kv_pool* p);
+int32_t   yk_kv_pool_num_blocks(const yk_kv_pool* p);
+/* Fills every slot with N(0, std) values (synthetic context for benchmarks). */
+yk_status yk_kv_pool_fill_random(yk_kv_pool* p, uint64_t seed, float std);
+/* Copies one page [n_kv_heads x 16 x head_dim] of layer `layer`, kv 0=K 1=V, as fp32. */
+yk_status yk_kv_pool_read_page(yk_kv_pool* p, int32_t block, int32_t layer, int32_t kv, float* host);
+
+/* ---- forward.  Replaces LlamaModel.forwardStep(batch:allocator:isDraft:)
+ * (S/LlamaModel.swift:134-244).  tokens[T] concatenated per sequence;
+ * q_starts[B+1] (:137,147); context_lens[B] = length of each sequence after
+ * this step (:149-150); block_tables[B x max_blocks] int32 page tables
+ * (:154-162).  Token i of sequence b sits at position
+ * context_lens[b] - n_b + i (S/gemm.metal:656-659); its K (rotated) and V are
+ * written to its page before attention reads the pool.  Every page covering
+ * positions < context_lens[b] must be in the table.
+ * Logits stay on the device ([rows x vocab] fp32): all T rows when
+ * last_n == 0, else the last min(last_n, n_b) rows of each sequence in
+ * sequence order (the rows Scheduler.step reads, S/Scheduler.swift:177,225).
+ * *n_rows receives the row count. */
+yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
+                          const uint32_t* q_starts, const uint32_t* context_lens, int32_t B,
+                          const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
+                          int32_t* n_rows);
+/* Copies logits rows [row0, row0+rows) of the last forward step to host (tests). */
+yk_status yk_logits_copy_to_host(yk_model* m, int32_t row0, int32_t rows, float* host);
+
+/* ---- sampler.  Replaces SpeculativeSampler (S/SpeculativeSampler.swift) and
+ * the Scheduler's draft sampling (S/Scheduler.swift:171-189).  Uniform draws
+ * are Philox4x32-10 keyed by seed, counter (step, seq_id, position, slot) with
+ * slot 0 draft / 1 accept / 2 resample / 3 bonus; u = (x0 >> 8) * 2^-24.
+ * temperature T > 0 scales logits by 1/T (S/Sampler.swift:19-23); T == 0 is
+ * greedy (argmax, first maximum wins). */
+yk_status yk_sampler_create(yk_engine* e, int32_t max_seqs, int32_t k, int32_t vocab, yk_sampler** out);
+void      yk_sampler_destroy(yk_sampler* s);
+/* Draft iteration j: p = softmax(draft logits row b / T) kept on the device for
+ * verification, token = sampleFromProbs(p) (S/SpeculativeSampler.swift:63-91).
+ * Reads rows 0..B-1 of `draft`'s logits (forward with last_n = 1). */
+yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, int32_t j, float temperature,
+                          uint64_t seed, uint32_t step, const uint32_t* seq_ids, uint32_t* out_tokens);
+/* verifySequence (S/SpeculativeSampler.swift:95-129) for B sequences against
+ * `target`'s logits rows b*(k+1)+i (forward with last_n = k+1) and the draft
+ * probabilities kept by yk_draft_sample.  out_tokens[B x (k+1)], out_counts[B]. */
+yk_status yk_spec_verify(yk_sampler* s, yk_model* target, int32_t B, float temperature, uint64_t seed,
+                         uint32_t step, const uint32_t* seq_ids, const uint32_t* draft_tokens,
+                         uint32_t* out_tokens, int32_t* out_counts);
+/* Bit-exact parity entry: verifySequence on probability tensors.
+ * p[B x k x V] draft probs, q[B x (k+1) x V] target probs, host fp32. */
+yk_status yk_spec_verify_probs(yk_sampler* s, int32_t B, const float* p, const float* q,
+                               const uint32_t* draft_tokens, uint64_t seed, uint32_t step,
+                               const uint32_t* seq_ids, uint32_t* out_tokens, int32_t* out_counts);
+/* Whole sampler phase of one step from host logits (draft sampling of k tokens
+ * per sequence, then verification): draft_logits[B x k x V],
+ * target_logits[B x (k+1) x V]. */
+yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float* draft_logits,
+                                const float* target_logits, float temperature, uint64_t seed,
+                                uint32_t step, const uint32_t* seq_ids, uint32_t* draft_tokens_out,
+                                uint32_t* out_tokens, int32_t* out_counts);
+/* Copies draft probabilities p[b][j][0..V) kept by yk_draft_sample (tests). */
+yk_status yk_sampler_read_probs(yk_sampler* s, int32_t b, int32_t j, float* host);
+
+#ifdef __cplusplus
+}
+#endif

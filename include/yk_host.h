@@ -1,0 +1,60 @@
+/*
+ * yk_host.h -- C++ restatement of the reference's host side of the path, the
+ * caller of yk.h: Scheduler's speculative step (S/Scheduler.swift:155-268),
+ * SequenceRequest (S/Scheduler.swift:5-80), PagedKVCache page tables
+ * (S/PagedKVCache.swift) and the 16-token BlockAllocator free list
+ * (S/BlockAllocator.swift).  In a Swift deployment those classes stay Swift
+ * and call yk.h directly; this library exists because no Swift toolchain is
+ * available to build them here, and it is what the tests and the benchmark
+ * drive end to end (libyk_host.so).
+ *
+ * Cache-position accounting follows the standard speculative invariant (each
+ * cache holds every token of the sequence except the last emitted one) rather
+ * than the reference's context-length and rollback arithmetic
+ * (S/LlamaModel.swift:149, S/Scheduler.swift:242), which double-count the
+ * prompt on the first step and drop one cached token per step.
+ */
+#pragma once
+#include <stdint.h>
+
+#include "yk.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct ykh_scheduler ykh_scheduler;
+
+/* One scheduler per GPU: a target and a draft model, each with its own KV pool
+ * and BlockAllocator (S/Scheduler.swift:96-102; draft allocator from
+ * S/Scheduler.swift:172).  k = draft tokens per step (gamma, :162). */
+yk_status ykh_scheduler_create(yk_model* target, yk_kv_pool* target_pool, yk_model* draft, yk_kv_pool* draft_pool,
+                               yk_sampler* sampler, int32_t k, float temperature, uint64_t seed,
+                               ykh_scheduler** out);
+void ykh_scheduler_destroy(ykh_scheduler* s);
+
+/* Scheduler.submit (S/Scheduler.swift:105).  stop_token < 0: none.  seq_id is
+ * the Philox stream id of the request. */
+yk_status ykh_submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens, int64_t stop_token,
+                     uint32_t seq_id);
+/* Like ykh_submit, but the first n-1 prompt tokens are treated as already in
+ * both KV caches (their pages are allocated; the pool holds whatever it holds,
+ * e.g. yk_kv_pool_fill_random).  Used for steady-state benchmarks that exclude
+ * prefill. */
+yk_status ykh_submit_cached(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
+                            int64_t stop_token, uint32_t seq_id);
+/* One speculative step over the running batch (admission as runLoop,
+ * S/Scheduler.swift:122-129).  *emitted = tokens appended across the batch. */
+yk_status ykh_step(ykh_scheduler* s, int32_t* emitted);
+int32_t   ykh_num_running(const ykh_scheduler* s);
+int32_t   ykh_num_waiting(const ykh_scheduler* s);
+/* Generated tokens of request seq_id (prompt excluded); *n = total count. */
+yk_status ykh_generated(const ykh_scheduler* s, uint32_t seq_id, uint32_t* out, int32_t cap, int32_t* n);
+/* Counters since creation: steps, emitted tokens, accepted draft tokens. */
+yk_status ykh_counters(const ykh_scheduler* s, int64_t* steps, int64_t* emitted, int64_t* accepted);
+/* BlockAllocator.usage of the target / draft pools (S/BlockAllocator.swift:56-58). */
+float     ykh_usage(const ykh_scheduler* s, int32_t draft);
+
+#ifdef __cplusplus
+}
+#endif

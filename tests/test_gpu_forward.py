@@ -1,0 +1,124 @@
+"""Verify forward (yk_forward_step) vs the fp32 oracle forward on the same weights.
+
+Tolerances:
+  fp32 model: max |dlogit| <= 2e-4 * max|logit| (accumulation order only);
+  bf16 model vs the oracle emulating the bf16 storage points:
+      max |dlogit| <= 2e-2 * max|logit| (accumulation order and P/rotation rounding);
+  bf16 model vs the pure fp32 oracle: max |dlogit| <= 5e-2 * max|logit|.
+Greedy tokens must agree wherever the oracle's top-2 gap exceeds the error bound.
+"""
+import numpy as np
+import pytest
+
+from helpers import TINY, PageTables, forward_pair, gpu_model, oracle_twin
+from yanaiengine_b200 import abi
+
+pytestmark = pytest.mark.gpu
+NB = 64
+
+
+def _rel(g, o):
+    return np.abs(g - o).max() / max(np.abs(o).max(), 1e-6)
+
+
+def _greedy_agree(g, o, tol_abs):
+    top2 = np.sort(o, axis=1)[:, -2:]
+    clear = (top2[:, 1] - top2[:, 0]) > 4 * tol_abs
+    assert (np.argmax(g, 1)[clear] == np.argmax(o, 1)[clear]).all()
+
+
+def _drive(engine, oracle, cfg, dtype, emulate, tol, init_std=0.02, steps=3, k=4):
+    m, pool = gpu_model(engine, cfg, dtype, seed=3, num_blocks=NB, init_std=init_std)
+    try:
+        orc = oracle_twin(oracle, m, cfg, NB, emulate_bf16=emulate)
+        pt = PageTables(NB)
+        rng = np.random.default_rng(1)
+        V = cfg["vocab_size"]
+        lens = {0: 0, 1: 0, 2: 0}
+        # ragged prefill: 3 sequences, 17 / 40 / 5 tokens (page-boundary crossings)
+        batch = []
+        for sid, n in ((0, 17), (1, 40), (2, 5)):
+            batch.append((sid, rng.integers(0, V, n).tolist(), 0))
+            lens[sid] = n
+        g, o = forward_pair(m, pool, orc, pt, batch)
+        assert np.isfinite(g).all()
+        assert _rel(g, o) < tol, f"prefill rel err {_rel(g, o):.3e}"
+        _greedy_agree(g, o, tol * np.abs(o).max())
+        # verify-shaped steps: k+1 new tokens per sequence, logits for the last k+1
+        for _ in range(steps):
+            batch = []
+            for sid in (0, 1, 2):
+                batch.append((sid, rng.integers(0, V, k + 1).tolist(), lens[sid]))
+                lens[sid] += k + 1
+            g, o = forward_pair(m, pool, orc, pt, batch, last_n=k + 1)
+            assert g.shape == (3 * (k + 1), V)
+            assert _rel(g, o) < tol, f"step rel err {_rel(g, o):.3e}"
+            _greedy_agree(g, o, tol * np.abs(o).max())
+        # KV page contents (K stored rotated, V as projected)
+        blk = pt.tables[1][0]
+        for layer in range(cfg["n_layers"]):
+            for kv in (0, 1):
+                page = pool.read_page(blk, layer, kv)
+                ref = _oracle_page(orc, cfg, blk, layer, kv)
+                assert np.abs(page - ref).max() <= tol * max(np.abs(ref).max(), 1e-3) * 4
+        assert engine.device_error() == 0
+    finally:
+        pool.close()
+        m.close()
+
+
+def _oracle_page(orc, cfg, blk, layer, kv):
+    L, Hkv, dh = cfg["n_layers"], cfg["n_kv_heads"], cfg["head_dim"]
+    per_layer = 2 * Hkv * 16 * dh
+    base = blk * L * per_layer + layer * per_layer + kv * Hkv * 16 * dh
+    return orc.pool[base: base + Hkv * 16 * dh].reshape(Hkv, 16, dh)
+
+
+def test_fp32_tiny(engine, oracle):
+    _drive(engine, oracle, TINY, abi.DTYPE_F32, False, 2e-4)
+
+
+def test_bf16_tiny_vs_bf16_emulating_oracle(engine, oracle):
+    _drive(engine, oracle, TINY, abi.DTYPE_BF16, True, 2e-2)
+
+
+def test_bf16_tiny_vs_fp32_oracle(engine, oracle):
+    _drive(engine, oracle, TINY, abi.DTYPE_BF16, False, 5e-2)
+
+
+@pytest.mark.parametrize("dh", [128, 256])
+def test_bf16_head_dims(engine, oracle, dh):
+    cfg = dict(TINY, head_dim=dh, n_heads=4, n_kv_heads=1)
+    _drive(engine, oracle, cfg, abi.DTYPE_BF16, True, 2e-2, steps=2)
+
+
+def test_gemma_variant(engine, oracle):
+    """GeGLU, attention cap 50, final cap 30, window 8 on even layers, head_dim 256, eps 1e-6."""
+    cfg = dict(TINY, act=abi.ACT_GELU_TANH, attn_cap=50.0, final_cap=30.0, window=8, window_layer_parity=0,
+               head_dim=256, n_heads=2, n_kv_heads=1, rms_eps=1e-6)
+    _drive(engine, oracle, cfg, abi.DTYPE_BF16, True, 2e-2, init_std=0.08, steps=3)
+
+
+def test_gemma_variant_fp32(engine, oracle):
+    cfg = dict(TINY, act=abi.ACT_GELU_TANH, attn_cap=5.0, final_cap=3.0, window=8, window_layer_parity=0,
+               head_dim=128, n_heads=4, n_kv_heads=2, rms_eps=1e-6)
+    _drive(engine, oracle, cfg, abi.DTYPE_F32, False, 2e-4, init_std=0.08, steps=3)
+
+
+def test_ref_compat(engine, oracle):
+    """bias 0.1 + ReLU on every projection and LM-head cap 30 (S/LinearLayer.swift:61,99-121)."""
+    cfg = dict(TINY, ref_compat=1)
+    _drive(engine, oracle, cfg, abi.DTYPE_F32, False, 2e-4, steps=2)
+
+
+def test_rejects_bad_block_id(engine):
+    m, pool = gpu_model(engine, TINY, abi.DTYPE_BF16, seed=1, num_blocks=4)
+    try:
+        with pytest.raises(abi.YKError) as ei:
+            m.forward(pool, [1, 2, 3], [0, 3], [3], np.array([[7]], np.int32))
+        assert ei.value.status == abi.YK_ERR_ARG
+        with pytest.raises(abi.YKError):
+            m.forward(pool, [1, 2, 10**6], [0, 3], [3], np.array([[0]], np.int32))
+    finally:
+        pool.close()
+        m.close()

@@ -1,0 +1,135 @@
+"""Fused rejection sampler vs the oracle.
+
+Bit-exact contract: identical probability tensors + identical (Philox) uniforms
+give identical acceptance decisions and emitted tokens (yk_spec_verify_probs).
+Logits entry points: the probabilities are computed on the device (expf and a
+parallel max/sum), so they are compared within a tolerance and the decisions
+are compared exactly (a flip would need a uniform within ~1e-7 of a cdf value).
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from yanaiengine_b200 import abi
+
+pytestmark = pytest.mark.gpu
+KAT = json.loads((Path(__file__).parent / "golden" / "sampler_kat.json").read_text())
+
+
+def test_golden_verify_sequences(engine):
+    for c in KAT["verify_sequence"]:
+        s = abi.Sampler(engine, 1, c["k"], c["V"])
+        try:
+            out, cnt = s.verify_probs(np.array(c["p"])[None], np.array(c["q"])[None], [c["drafts"]], c["seed"],
+                                      c["step"], [c["seq"]])
+        finally:
+            s.close()
+        assert out[0, : cnt[0]].tolist() == c["expect"]
+
+
+def _c1_probs(oracle, B, k, V, seed):
+    rng = np.random.default_rng(seed)
+    dl = rng.normal(0, 2.0, (B, k, V)).astype(np.float32)
+    tl = rng.normal(0, 2.0, (B, k + 1, V)).astype(np.float32)
+    p = np.stack([np.stack([oracle.softmax(dl[b, j]) for j in range(k)]) for b in range(B)])
+    q = np.stack([np.stack([oracle.softmax(tl[b, j]) for j in range(k + 1)]) for b in range(B)])
+    drafts = np.array([[oracle.sample_from_probs(p[b, j], oracle.uniform(seed, 3, b, j, 0)) for j in range(k)]
+                       for b in range(B)], np.uint32)
+    return p, q, drafts
+
+
+def test_verify_probs_bit_exact_c1(engine, oracle):
+    """Config 1 shapes: 64 sequences, k=4, V=128256, N(0, 2^2) logits."""
+    B, k, V = 64, 4, 128256
+    p, q, drafts = _c1_probs(oracle, B, k, V, 1234)
+    seq_ids = np.arange(B, dtype=np.uint32)
+    s = abi.Sampler(engine, B, k, V)
+    try:
+        for step in (3, 4):
+            out, cnt = s.verify_probs(p, q, drafts, 1234, step, seq_ids)
+            ref_out, ref_cnt = oracle.verify_batch_probs(drafts, p, q, 1234, step, seq_ids)
+            np.testing.assert_array_equal(cnt, ref_cnt)
+            for b in range(B):
+                assert out[b, : cnt[b]].tolist() == ref_out[b, : ref_cnt[b]].tolist(), f"seq {b}"
+    finally:
+        s.close()
+
+
+def test_verify_probs_edge_cases(engine, oracle):
+    """Rows built to hit every branch of verifyToken / sampleFromProbs."""
+    k, V = 4, 4099
+    rng = np.random.default_rng(7)
+    rows_p, rows_q, drafts = [], [], []
+    for case in range(12):
+        p = rng.random((k, V)).astype(np.float32) ** 4
+        q = rng.random((k + 1, V)).astype(np.float32) ** 4
+        p /= p.sum(1, keepdims=True)
+        q /= q.sum(1, keepdims=True)
+        d = rng.integers(0, V, k)
+        if case == 0:
+            q[:k] = p                      # ratio 1: all accepted, bonus
+        if case == 1:
+            p[:, d] = 0.0                  # p[d] = 0 -> ratio inf -> accept
+        if case == 2:
+            p[0, d[0]] = 0.0
+            q[0, d[0]] = 0.0               # 0/0 -> NaN -> reject
+        if case == 3:
+            q[0] = p[0] * 0.5              # residual sums to 0 -> fallback to q
+        if case == 4:
+            q[0] = 0.0
+            q[0, -1] = 1e-30               # residual concentrated on the last index
+            p[0, d[0]] = 1.0
+        if case == 5:
+            q[k] *= 0.5                    # bonus cdf short of r -> fallback V-1 often
+            q[:k] = p
+        if case == 6:
+            q[1] = np.float32(1.0 / V)     # exact ties everywhere
+            p[1] = np.float32(1.0 / V)
+            p[1, d[1]] = np.float32(2.0 / V)
+        rows_p.append(p)
+        rows_q.append(q)
+        drafts.append(d)
+    p = np.stack(rows_p).astype(np.float32)
+    q = np.stack(rows_q).astype(np.float32)
+    drafts = np.stack(drafts).astype(np.uint32)
+    B = p.shape[0]
+    seq_ids = np.arange(100, 100 + B, dtype=np.uint32)
+    s = abi.Sampler(engine, B, k, V)
+    try:
+        for step in range(6):
+            out, cnt = s.verify_probs(p, q, drafts, 99, step, seq_ids)
+            ref_out, ref_cnt = oracle.verify_batch_probs(drafts, p, q, 99, step, seq_ids)
+            np.testing.assert_array_equal(cnt, ref_cnt)
+            np.testing.assert_array_equal(np.where(np.arange(k + 1)[None] < cnt[:, None], out, 0),
+                                          np.where(np.arange(k + 1)[None] < ref_cnt[:, None], ref_out, 0))
+    finally:
+        s.close()
+
+
+@pytest.mark.parametrize("T", [1.0, 0.8, 0.0])
+def test_sample_logits_matches_oracle(engine, oracle, T):
+    B, k, V = 16, 4, 128256
+    rng = np.random.default_rng(11)
+    dl = rng.normal(0, 2.0, (B, k, V)).astype(np.float32)
+    tl = rng.normal(0, 2.0, (B, k + 1, V)).astype(np.float32)
+    seq_ids = np.arange(B, dtype=np.uint32)
+    s = abi.Sampler(engine, B, k, V)
+    try:
+        drafts, out, cnt = s.sample_logits(dl, tl, T, 5, 1, seq_ids)
+        # device probabilities vs the reference softmax
+        for b in (0, B - 1):
+            ref = oracle.softmax(dl[b, 1], T if T > 0 else 1.0)
+            got = s.read_probs(b, 1)
+            if T > 0:
+                np.testing.assert_allclose(got, ref, rtol=2e-5, atol=1e-12)
+            else:
+                assert got[np.argmax(dl[b, 1])] == 1.0 and got.sum() == 1.0
+    finally:
+        s.close()
+    r_drafts, r_out, r_cnt = oracle.spec_sample_batch(dl, tl, T, 5, 1, seq_ids)
+    np.testing.assert_array_equal(drafts, r_drafts)
+    np.testing.assert_array_equal(cnt, r_cnt)
+    for b in range(B):
+        assert out[b, : cnt[b]].tolist() == r_out[b, : r_cnt[b]].tolist()

@@ -1,0 +1,129 @@
+"""End-to-end draft->verify through libyk_host.so's Scheduler vs the oracle.
+
+Config 2 of the benchmark spec (tiny fp32 target + draft, batch 1, k=4, greedy,
+prompt of 128 uniform ids, 16-token pages): the emitted tokens must be
+identical to the oracle's speculative run, and -- the defining property of
+greedy speculative decoding -- identical to plain greedy decoding of the target.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from helpers import C2_DRAFT, C2_TARGET, TINY, PageTables, gpu_model, oracle_twin, step_inputs
+from yanaiengine_b200 import abi
+
+pytestmark = pytest.mark.gpu
+NTHREADS = max(4, os.cpu_count() or 4)
+
+
+def oracle_greedy_spec(orc_t, orc_d, prompt, k, steps):
+    """Restates ykh_step for one sequence with greedy draft sampling and verification."""
+    pt_t, pt_d = PageTables(orc_t.num_blocks), PageTables(orc_d.num_blocks)
+    tokens = list(prompt)
+    tpos = dpos = 0
+    for _ in range(steps):
+        N = len(tokens)
+        drafts = []
+        for j in range(k):
+            inp = tokens[dpos:N] if j == 0 else [drafts[-1]]
+            lg = orc_d.forward(*step_inputs(pt_d, [(0, inp, dpos)]), last_n=1)
+            dpos += len(inp)
+            drafts.append(int(np.argmax(lg[-1])))
+        inp = tokens[tpos:N] + drafts
+        lg = orc_t.forward(*step_inputs(pt_t, [(0, inp, tpos)]), last_n=k + 1)
+        out = []
+        for i in range(k):
+            a = int(np.argmax(lg[i]))
+            out.append(a)
+            if a != drafts[i]:
+                break
+        else:
+            out.append(int(np.argmax(lg[k])))
+        acc = len(out) - 1
+        tpos = N + acc
+        dpos = min(dpos, N + acc)
+        tokens += out
+    return tokens[len(prompt):]
+
+
+def oracle_greedy_plain(orc_t, prompt, n_new):
+    pt = PageTables(orc_t.num_blocks)
+    tokens = list(prompt)
+    pos = 0
+    while len(tokens) < len(prompt) + n_new:
+        lg = orc_t.forward(*step_inputs(pt, [(0, tokens[pos:], pos)]), last_n=1)
+        pos = len(tokens)
+        tokens.append(int(np.argmax(lg[-1])))
+    return tokens[len(prompt):]
+
+
+def _run(engine, oracle, tcfg, dcfg, dtype, prompt_len, k, steps, seed_t, seed_d, nb=64):
+    t, tp = gpu_model(engine, tcfg, dtype, seed=seed_t, num_blocks=nb, max_tokens=prompt_len + 8, max_seqs=4)
+    d, dp = gpu_model(engine, dcfg, dtype, seed=seed_d, num_blocks=nb, max_tokens=prompt_len + 8, max_seqs=4)
+    s = abi.Sampler(engine, 4, k, tcfg["vocab_size"])
+    sch = abi.Scheduler(t, tp, d, dp, s, k, 0.0, 77)
+    try:
+        prompt = np.random.default_rng(128).integers(0, tcfg["vocab_size"], prompt_len).tolist()
+        sch.submit(prompt, max_tokens=10**6, stop_token=-1, seq_id=0)
+        for _ in range(steps):
+            sch.step()
+        got = sch.generated(0)
+        orc_t = oracle_twin(oracle, t, tcfg, nb, emulate_bf16=False, nthreads=NTHREADS)
+        orc_d = oracle_twin(oracle, d, dcfg, nb, emulate_bf16=False, nthreads=NTHREADS)
+        return got, orc_t, orc_d, prompt
+    finally:
+        sch.close()
+        s.close()
+        dp.close()
+        d.close()
+        tp.close()
+        t.close()
+
+
+def test_c2_greedy_token_identical(engine, oracle):
+    got, orc_t, orc_d, prompt = _run(engine, oracle, C2_TARGET, C2_DRAFT, abi.DTYPE_F32, 128, 4, 5, 1, 2)
+    ref = oracle_greedy_spec(orc_t, orc_d, prompt, 4, 5)
+    assert got == ref
+    # greedy speculative decoding == greedy decoding of the target alone
+    assert got == oracle_greedy_plain(orc_t, prompt, len(got))
+
+
+def test_tiny_greedy_spec_equals_plain_greedy(engine, oracle):
+    """Same property with a draft that disagrees often (different seed): many rejections."""
+    got, orc_t, orc_d, prompt = _run(engine, oracle, TINY, dict(TINY, n_layers=1), abi.DTYPE_F32, 40, 4, 12, 5, 9)
+    assert len(got) >= 12
+    assert got == oracle_greedy_spec(orc_t, orc_d, prompt, 4, 12)
+    assert got == oracle_greedy_plain(orc_t, prompt, len(got))
+
+
+def test_scheduler_sampled_batch_runs(engine):
+    """T > 0, several sequences of different lengths, stop on max_tokens, pages returned."""
+    t, tp = gpu_model(engine, TINY, abi.DTYPE_BF16, seed=1, num_blocks=128, max_tokens=256, max_seqs=8)
+    d, dp = gpu_model(engine, dict(TINY, n_layers=1), abi.DTYPE_BF16, seed=2, num_blocks=128, max_tokens=256,
+                      max_seqs=8)
+    s = abi.Sampler(engine, 8, 5, TINY["vocab_size"])
+    sch = abi.Scheduler(t, tp, d, dp, s, 5, 0.8, 3)
+    try:
+        rng = np.random.default_rng(0)
+        for i in range(6):
+            sch.submit(rng.integers(0, 512, 10 + 7 * i).tolist(), max_tokens=20, stop_token=-1, seq_id=i)
+        total = 0
+        for _ in range(30):
+            if sch.running() == 0 and sch.waiting() == 0:
+                break
+            total += sch.step()
+        assert sch.running() == 0 and sch.waiting() == 0
+        steps, emitted, accepted = sch.counters()
+        assert emitted == total and emitted >= 6 * 20
+        for i in range(6):
+            g = sch.generated(i)
+            assert 20 <= len(g) <= 25 and all(0 <= x < 512 for x in g)
+        assert sch.usage() == 0.0 and sch.usage(draft=True) == 0.0
+    finally:
+        sch.close()
+        s.close()
+        dp.close()
+        d.close()
+        tp.close()
+        t.close()

@@ -1,0 +1,382 @@
+"""ctypes binding of include/yk.h (libyk.so) and include/yk_host.h (libyk_host.so).
+
+The CUDA module is the only implementation: if the in-tree libraries are
+missing this raises instead of falling back to anything else.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libyk.so"
+HOST_LIB_PATH = PKG / "libyk_host.so"
+
+YK_OK, YK_ERR_ARG, YK_ERR_OOM, YK_ERR_CUDA, YK_ERR_NCCL, YK_ERR_TIMEOUT, YK_ERR_DEVICE_CHECK, YK_ERR_UNSUPPORTED = range(8)
+DTYPE_F32, DTYPE_BF16 = 0, 1
+ACT_SILU, ACT_GELU_TANH = 0, 1
+BLOCK_SIZE = 16
+(T_EMBED, T_WQ, T_WK, T_WV, T_WO, T_WGATE, T_WUP, T_WDOWN, T_NORM1, T_NORM2, T_FINAL_NORM,
+ T_LM_HEAD) = range(12)
+LAYOUT_OUT_IN, LAYOUT_IN_OUT = 0, 1
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [
+        ("vocab_size", C.c_int32), ("d_model", C.c_int32), ("n_layers", C.c_int32), ("n_heads", C.c_int32),
+        ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("ffn_dim", C.c_int32),
+        ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("attn_cap", C.c_float), ("final_cap", C.c_float),
+        ("window", C.c_int32), ("window_layer_parity", C.c_int32), ("act", C.c_int32), ("ref_compat", C.c_int32),
+        ("dtype", C.c_int32), ("max_tokens", C.c_int32), ("max_seqs", C.c_int32),
+    ]
+
+    def to_dict(self) -> dict:
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
+
+def make_config(**kw) -> ModelConfig:
+    defaults = dict(rope_theta=10000.0, rms_eps=1e-5, attn_cap=0.0, final_cap=0.0, window=0,
+                    window_layer_parity=-1, act=ACT_SILU, ref_compat=0, dtype=DTYPE_BF16, max_tokens=256,
+                    max_seqs=64)
+    defaults.update(kw)
+    c = ModelConfig()
+    for k, v in defaults.items():
+        setattr(c, k, v)
+    return c
+
+
+class YKError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"yk status {status}: {msg}")
+        self.status = status
+
+
+_P = C.c_void_p
+_U32P = C.POINTER(C.c_uint32)
+_I32P = C.POINTER(C.c_int32)
+_F32P = C.POINTER(C.c_float)
+
+_PROTOS = {
+    "yk_last_error": (C.c_int32, [C.c_char_p, C.c_size_t]),
+    "yk_engine_create": (C.c_int32, [C.c_int32, C.POINTER(_P)]),
+    "yk_engine_destroy": (None, [_P]),
+    "yk_engine_stream": (C.c_int32, [_P, C.POINTER(_P)]),
+    "yk_engine_sync": (C.c_int32, [_P]),
+    "yk_engine_device_error": (C.c_int32, [_P, _U32P]),
+    "yk_engine_launch_count": (C.c_uint64, [_P]),
+    "yk_model_create": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_uint64, C.c_float, C.POINTER(_P)]),
+    "yk_model_destroy": (None, [_P]),
+    "yk_model_get_config": (C.c_int32, [_P, C.POINTER(ModelConfig)]),
+    "yk_model_tensor_shape": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "yk_model_set_tensor": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P, C.c_int32]),
+    "yk_model_get_tensor": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P]),
+    "yk_kv_pool_create": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_int32, C.POINTER(_P)]),
+    "yk_kv_pool_destroy": (None, [_P]),
+    "yk_kv_pool_num_blocks": (C.c_int32, [_P]),
+    "yk_kv_pool_fill_random": (C.c_int32, [_P, C.c_uint64, C.c_float]),
+    "yk_kv_pool_read_page": (C.c_int32, [_P, C.c_int32, C.c_int32, C.c_int32, _F32P]),
+    "yk_forward_step": (C.c_int32, [_P, _P, _U32P, C.c_int32, _U32P, _U32P, C.c_int32, _I32P, C.c_int32,
+                                    C.c_int32, _I32P]),
+    "yk_logits_copy_to_host": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P]),
+    "yk_sampler_create": (C.c_int32, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_P)]),
+    "yk_sampler_destroy": (None, [_P]),
+    "yk_draft_sample": (C.c_int32, [_P, _P, C.c_int32, C.c_int32, C.c_float, C.c_uint64, C.c_uint32, _U32P,
+                                    _U32P]),
+    "yk_spec_verify": (C.c_int32, [_P, _P, C.c_int32, C.c_float, C.c_uint64, C.c_uint32, _U32P, _U32P, _U32P,
+                                   _I32P]),
+    "yk_spec_verify_probs": (C.c_int32, [_P, C.c_int32, _F32P, _F32P, _U32P, C.c_uint64, C.c_uint32, _U32P,
+                                         _U32P, _I32P]),
+    "yk_spec_sample_logits": (C.c_int32, [_P, C.c_int32, _F32P, _F32P, C.c_float, C.c_uint64, C.c_uint32, _U32P,
+                                          _U32P, _U32P, _I32P]),
+    "yk_sampler_read_probs": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P]),
+    # include/yk_testing.h
+    "ykt_gemm_bf16": (C.c_int32, [_P, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int32, C.c_int32,
+                                  C.c_int32, C.c_int32, _F32P]),
+}
+
+_HOST_PROTOS = {
+    "ykh_scheduler_create": (C.c_int32, [_P, _P, _P, _P, _P, C.c_int32, C.c_float, C.c_uint64, C.POINTER(_P)]),
+    "ykh_scheduler_destroy": (None, [_P]),
+    "ykh_submit": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
+    "ykh_submit_cached": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
+    "ykh_step": (C.c_int32, [_P, _I32P]),
+    "ykh_num_running": (C.c_int32, [_P]),
+    "ykh_num_waiting": (C.c_int32, [_P]),
+    "ykh_generated": (C.c_int32, [_P, C.c_uint32, _U32P, C.c_int32, _I32P]),
+    "ykh_counters": (C.c_int32, [_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "ykh_usage": (C.c_float, [_P, C.c_int32]),
+}
+
+_lib = None
+_host = None
+
+
+def _load(path: Path, protos: dict):
+    if not path.exists():
+        raise RuntimeError(f"{path.name} is not built; run __graft_entry__.build() (the CUDA module is required)")
+    lib = C.CDLL(str(path))
+    for name, (res, args) in protos.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        _lib = _load(LIB_PATH, _PROTOS)
+    return _lib
+
+
+def host_lib():
+    global _host
+    if _host is None:
+        lib()
+        _host = _load(HOST_LIB_PATH, _HOST_PROTOS)
+    return _host
+
+
+def exported_symbols() -> list[str]:
+    return list(_PROTOS) + list(_HOST_PROTOS)
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(4096)
+    lib().yk_last_error(buf, 4096)
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int):
+    if status != YK_OK:
+        raise YKError(status, last_error())
+
+
+def ptr(a: np.ndarray, ctype):
+    return a.ctypes.data_as(C.POINTER(ctype))
+
+
+def u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
+
+
+def i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+def f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def bf16_bits(a) -> np.ndarray:
+    """fp32 -> bf16 bit patterns (round to nearest even)."""
+    u = f32(a).view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF).astype(np.uint16)
+
+
+def bf16_value(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def gemm_bf16_test(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, splits: int = 0) -> np.ndarray:
+    """Y = X W^T through the tcgen05 GEMM (test hook of include/yk_testing.h)."""
+    n_out, K = W_bits.shape
+    m_tok = X_bits.shape[0]
+    W_bits = np.ascontiguousarray(W_bits, dtype=np.uint16)
+    X_bits = np.ascontiguousarray(X_bits, dtype=np.uint16)
+    Y = np.zeros((m_tok, n_out), np.float32)
+    check(lib().ykt_gemm_bf16(engine.h, ptr(W_bits, C.c_uint16), ptr(X_bits, C.c_uint16), n_out, K, m_tok, splits,
+                              ptr(Y, C.c_float)))
+    return Y
+
+
+# ---------------------------------------------------------------------------
+# Thin object wrappers.
+# ---------------------------------------------------------------------------
+class Engine:
+    def __init__(self, device: int = 0):
+        self.h = _P()
+        check(lib().yk_engine_create(device, C.byref(self.h)))
+        self.device = device
+
+    def stream(self) -> int:
+        s = _P()
+        check(lib().yk_engine_stream(self.h, C.byref(s)))
+        return s.value or 0
+
+    def sync(self):
+        check(lib().yk_engine_sync(self.h))
+
+    def device_error(self) -> int:
+        v = C.c_uint32()
+        check(lib().yk_engine_device_error(self.h, C.byref(v)))
+        return v.value
+
+    def launches(self) -> int:
+        return int(lib().yk_engine_launch_count(self.h))
+
+    def close(self):
+        if self.h:
+            lib().yk_engine_destroy(self.h)
+            self.h = _P()
+
+
+class Model:
+    def __init__(self, engine: Engine, cfg: ModelConfig, seed: int = 1, init_std: float = 0.02):
+        self.engine = engine
+        self.cfg = cfg
+        self.h = _P()
+        check(lib().yk_model_create(engine.h, C.byref(cfg), seed, init_std, C.byref(self.h)))
+
+    def shape(self, t: int) -> tuple[int, int]:
+        r, c = C.c_int64(), C.c_int64()
+        check(lib().yk_model_tensor_shape(self.h, t, C.byref(r), C.byref(c)))
+        return r.value, c.value
+
+    def get(self, t: int, layer: int = 0) -> np.ndarray:
+        r, c = self.shape(t)
+        out = np.empty((r, c), dtype=np.float32)
+        check(lib().yk_model_get_tensor(self.h, t, layer, ptr(out, C.c_float)))
+        return out[0] if r == 1 else out
+
+    def set(self, t: int, layer: int, host: np.ndarray, layout: int = LAYOUT_OUT_IN):
+        a = f32(host)
+        check(lib().yk_model_set_tensor(self.h, t, layer, ptr(a, C.c_float), layout))
+
+    def forward(self, pool: "KVPool", tokens, q_starts, ctx, block_tables: np.ndarray, last_n: int = 0) -> int:
+        tok, qs, cl = u32(tokens), u32(q_starts), u32(ctx)
+        bt = i32(block_tables)
+        rows = C.c_int32()
+        check(lib().yk_forward_step(self.h, pool.h, ptr(tok, C.c_uint32), len(tok), ptr(qs, C.c_uint32),
+                                    ptr(cl, C.c_uint32), len(cl), ptr(bt, C.c_int32), bt.shape[1], last_n,
+                                    C.byref(rows)))
+        return rows.value
+
+    def logits(self, row0: int, rows: int) -> np.ndarray:
+        out = np.empty((rows, self.cfg.vocab_size), dtype=np.float32)
+        check(lib().yk_logits_copy_to_host(self.h, row0, rows, ptr(out, C.c_float)))
+        return out
+
+    def close(self):
+        if self.h:
+            lib().yk_model_destroy(self.h)
+            self.h = _P()
+
+
+class KVPool:
+    def __init__(self, engine: Engine, cfg: ModelConfig, num_blocks: int):
+        self.cfg = cfg
+        self.h = _P()
+        check(lib().yk_kv_pool_create(engine.h, C.byref(cfg), num_blocks, C.byref(self.h)))
+
+    def fill_random(self, seed: int, std: float):
+        check(lib().yk_kv_pool_fill_random(self.h, seed, std))
+
+    def read_page(self, block: int, layer: int, kv: int) -> np.ndarray:
+        out = np.empty((self.cfg.n_kv_heads, BLOCK_SIZE, self.cfg.head_dim), dtype=np.float32)
+        check(lib().yk_kv_pool_read_page(self.h, block, layer, kv, ptr(out, C.c_float)))
+        return out
+
+    def close(self):
+        if self.h:
+            lib().yk_kv_pool_destroy(self.h)
+            self.h = _P()
+
+
+class Sampler:
+    def __init__(self, engine: Engine, max_seqs: int, k: int, vocab: int):
+        self.k, self.vocab = k, vocab
+        self.h = _P()
+        check(lib().yk_sampler_create(engine.h, max_seqs, k, vocab, C.byref(self.h)))
+
+    def verify_probs(self, p: np.ndarray, q: np.ndarray, drafts, seed: int, step: int, seq_ids):
+        B = p.shape[0]
+        p, q, d, s = f32(p), f32(q), u32(drafts), u32(seq_ids)
+        out = np.zeros((B, self.k + 1), dtype=np.uint32)
+        cnt = np.zeros(B, dtype=np.int32)
+        check(lib().yk_spec_verify_probs(self.h, B, ptr(p, C.c_float), ptr(q, C.c_float), ptr(d, C.c_uint32), seed,
+                                         step, ptr(s, C.c_uint32), ptr(out, C.c_uint32), ptr(cnt, C.c_int32)))
+        return out, cnt
+
+    def sample_logits(self, dl: np.ndarray, tl: np.ndarray, T: float, seed: int, step: int, seq_ids):
+        B = dl.shape[0]
+        dl, tl, s = f32(dl), f32(tl), u32(seq_ids)
+        drafts = np.zeros((B, self.k), dtype=np.uint32)
+        out = np.zeros((B, self.k + 1), dtype=np.uint32)
+        cnt = np.zeros(B, dtype=np.int32)
+        check(lib().yk_spec_sample_logits(self.h, B, ptr(dl, C.c_float), ptr(tl, C.c_float), T, seed, step,
+                                          ptr(s, C.c_uint32), ptr(drafts, C.c_uint32), ptr(out, C.c_uint32),
+                                          ptr(cnt, C.c_int32)))
+        return drafts, out, cnt
+
+    def draft_sample(self, model: Model, B: int, j: int, T: float, seed: int, step: int, seq_ids):
+        s = u32(seq_ids)
+        out = np.zeros(B, dtype=np.uint32)
+        check(lib().yk_draft_sample(self.h, model.h, B, j, T, seed, step, ptr(s, C.c_uint32), ptr(out, C.c_uint32)))
+        return out
+
+    def verify(self, model: Model, B: int, T: float, seed: int, step: int, seq_ids, drafts):
+        s, d = u32(seq_ids), u32(drafts)
+        out = np.zeros((B, self.k + 1), dtype=np.uint32)
+        cnt = np.zeros(B, dtype=np.int32)
+        check(lib().yk_spec_verify(self.h, model.h, B, T, seed, step, ptr(s, C.c_uint32), ptr(d, C.c_uint32),
+                                   ptr(out, C.c_uint32), ptr(cnt, C.c_int32)))
+        return out, cnt
+
+    def read_probs(self, b: int, j: int) -> np.ndarray:
+        out = np.empty(self.vocab, dtype=np.float32)
+        check(lib().yk_sampler_read_probs(self.h, b, j, ptr(out, C.c_float)))
+        return out
+
+    def close(self):
+        if self.h:
+            lib().yk_sampler_destroy(self.h)
+            self.h = _P()
+
+
+class Scheduler:
+    """libyk_host.so's Scheduler (restates S/Scheduler.swift's speculative loop)."""
+
+    def __init__(self, target: Model, tpool: KVPool, draft: Model, dpool: KVPool, sampler: Sampler, k: int,
+                 temperature: float, seed: int):
+        self.h = _P()
+        check(host_lib().ykh_scheduler_create(target.h, tpool.h, draft.h, dpool.h, sampler.h, k, temperature, seed,
+                                              C.byref(self.h)))
+
+    def submit(self, prompt, max_tokens: int, stop_token: int = -1, seq_id: int = 0, cached: bool = False):
+        p = u32(prompt)
+        fn = host_lib().ykh_submit_cached if cached else host_lib().ykh_submit
+        check(fn(self.h, ptr(p, C.c_uint32), len(p), max_tokens, stop_token, seq_id))
+
+    def step(self) -> int:
+        e = C.c_int32()
+        check(host_lib().ykh_step(self.h, C.byref(e)))
+        return e.value
+
+    def running(self) -> int:
+        return host_lib().ykh_num_running(self.h)
+
+    def waiting(self) -> int:
+        return host_lib().ykh_num_waiting(self.h)
+
+    def generated(self, seq_id: int) -> list[int]:
+        n = C.c_int32()
+        check(host_lib().ykh_generated(self.h, seq_id, None, 0, C.byref(n)))
+        out = np.zeros(max(n.value, 1), dtype=np.uint32)
+        check(host_lib().ykh_generated(self.h, seq_id, ptr(out, C.c_uint32), n.value, C.byref(n)))
+        return out[: n.value].tolist()
+
+    def counters(self) -> tuple[int, int, int]:
+        a, b, c = C.c_int64(), C.c_int64(), C.c_int64()
+        check(host_lib().ykh_counters(self.h, C.byref(a), C.byref(b), C.byref(c)))
+        return a.value, b.value, c.value
+
+    def usage(self, draft: bool = False) -> float:
+        return float(host_lib().ykh_usage(self.h, 1 if draft else 0))
+
+    def close(self):
+        if self.h:
+            host_lib().ykh_scheduler_destroy(self.h)
+            self.h = _P()

@@ -1,0 +1,550 @@
+// yk_api.cu -- engine / model / KV pool handles and the forward step
+// (LlamaModel.forwardStep, S/LlamaModel.swift:134-244; block order of
+// LlamaBlock.forwardBatched, S/LlamaBlock.swift:178-276).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "yk_common.cuh"
+#include "yk_internal.h"
+
+static thread_local std::string g_last_error;
+void yk_set_error(const std::string& msg) { g_last_error = msg; }
+
+extern "C" int32_t yk_last_error(char* buf, size_t n) {
+    if (buf && n) {
+        const size_t k = std::min(n - 1, g_last_error.size());
+        std::memcpy(buf, g_last_error.data(), k);
+        buf[k] = 0;
+    }
+    return (int32_t)g_last_error.size();
+}
+
+yk_status yk_engine::ensure_pinned(size_t bytes) {
+    if (bytes <= pinned_bytes) return YK_OK;
+    YK_CHECK_CUDA(cudaStreamSynchronize(stream));
+    if (pinned) cudaFreeHost(pinned);
+    pinned = nullptr;
+    pinned_bytes = 0;
+    const size_t want = std::max(bytes, (size_t)1 << 20);
+    YK_CHECK_CUDA(cudaMallocHost((void**)&pinned, want));
+    pinned_bytes = want;
+    return YK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// engine
+// ---------------------------------------------------------------------------
+extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
+    YK_ARG(out != nullptr, "out is null");
+    *out = nullptr;
+    int ndev = 0;
+    YK_CHECK_CUDA(cudaGetDeviceCount(&ndev));
+    YK_ARG(device >= 0 && device < ndev, "device index");
+    YK_CHECK_CUDA(cudaSetDevice(device));
+    int major = 0, minor = 0;
+    YK_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    YK_CHECK_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+    if (major != 10 || minor != 0) {
+        yk_set_error("libyk.so is built for sm_100a (B200); device is sm_" + std::to_string(major * 10 + minor));
+        return YK_ERR_UNSUPPORTED;
+    }
+    auto* e = new yk_engine();
+    e->device = device;
+    YK_CHECK_CUDA(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device));
+    YK_CHECK_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    YK_CHECK_CUDA(cudaMalloc(&e->d_err, sizeof(uint32_t)));
+    YK_CHECK_CUDA(cudaMemset(e->d_err, 0, sizeof(uint32_t)));
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    YK_CHECK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess) {
+        yk_set_error("cuTensorMapEncodeTiled not available from the driver");
+        delete e;
+        return YK_ERR_CUDA;
+    }
+    e->encode_tiled = (PFN_tmapEncodeTiled)fn;
+    yk_status s = e->ensure_pinned((size_t)4 << 20);
+    if (s != YK_OK) { delete e; return s; }
+    *out = e;
+    return YK_OK;
+}
+
+extern "C" void yk_engine_destroy(yk_engine* e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    cudaStreamSynchronize(e->stream);
+    if (e->pinned) cudaFreeHost(e->pinned);
+    if (e->d_err) cudaFree(e->d_err);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+extern "C" yk_status yk_engine_stream(yk_engine* e, void** stream) {
+    YK_ARG(e && stream, "null handle");
+    *stream = (void*)e->stream;
+    return YK_OK;
+}
+
+extern "C" yk_status yk_engine_sync(yk_engine* e) {
+    YK_ARG(e, "null handle");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    return YK_OK;
+}
+
+extern "C" yk_status yk_engine_device_error(yk_engine* e, uint32_t* code) {
+    YK_ARG(e && code, "null handle");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    YK_CHECK_CUDA(cudaMemcpy(code, e->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    YK_CHECK_CUDA(cudaMemset(e->d_err, 0, sizeof(uint32_t)));
+    return YK_OK;
+}
+
+extern "C" uint64_t yk_engine_launch_count(yk_engine* e) { return e ? e->launches : 0; }
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+static uint16_t host_bf16(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u) return (uint16_t)((u >> 16) | ((u & 0x7fffffu) ? 0x40u : 0u));
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+static float host_from_bf16(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+static yk_status dalloc(yk_model* m, void** p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, std::max<size_t>(bytes, 256));
+    if (e != cudaSuccess) {
+        yk_set_error(std::string("cudaMalloc(") + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? YK_ERR_OOM : YK_ERR_CUDA;
+    }
+    m->allocations.push_back(*p);
+    return YK_OK;
+}
+
+static yk_status validate_cfg(const yk_model_config* c) {
+    YK_ARG(c, "config is null");
+    YK_ARG(c->vocab_size > 0 && c->vocab_size % 2 == 0, "vocab_size must be positive and even");
+    YK_ARG(c->d_model > 0 && c->d_model % 8 == 0, "d_model must be a positive multiple of 8");
+    YK_ARG(c->n_layers > 0 && c->n_heads > 0 && c->n_kv_heads > 0 && c->n_heads % c->n_kv_heads == 0,
+           "n_heads must be a positive multiple of n_kv_heads");
+    YK_ARG(c->head_dim == 64 || c->head_dim == 128 || c->head_dim == 256, "head_dim must be 64, 128 or 256");
+    YK_ARG(c->ffn_dim > 0 && c->ffn_dim % 8 == 0, "ffn_dim must be a positive multiple of 8");
+    YK_ARG(c->dtype == YK_DTYPE_F32 || c->dtype == YK_DTYPE_BF16, "dtype");
+    YK_ARG(c->act == YK_ACT_SILU || c->act == YK_ACT_GELU_TANH, "act");
+    YK_ARG(c->max_tokens > 0 && c->max_seqs > 0, "max_tokens / max_seqs");
+    YK_ARG(c->rope_theta > 0.f && c->rms_eps >= 0.f && c->attn_cap >= 0.f && c->final_cap >= 0.f && c->window >= 0,
+           "numeric parameters");
+    return YK_OK;
+}
+
+extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, uint64_t seed, float init_std,
+                                     yk_model** out) {
+    YK_ARG(e && out, "null handle");
+    *out = nullptr;
+    YK_TRY(validate_cfg(cfg));
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    auto* m = new yk_model();
+    m->e = e;
+    m->cfg = *cfg;
+    const auto& c = m->cfg;
+    const size_t es = c.dtype == YK_DTYPE_BF16 ? 2 : 4;
+    m->esize = es;
+    const size_t d = c.d_model, V = c.vocab_size, F = c.ffn_dim, dh = c.head_dim;
+    const size_t qd = (size_t)c.n_heads * dh, kvd = (size_t)c.n_kv_heads * dh;
+    const size_t T = c.max_tokens;
+    auto fail = [&](yk_status s) { yk_model_destroy(m); return s; };
+    yk_status s;
+#define ALLOC(ptr, bytes) \
+    if ((s = dalloc(m, (void**)&(ptr), (bytes))) != YK_OK) return fail(s)
+    ALLOC(m->embed, V * d * es);
+    ALLOC(m->lm_head, V * d * es);
+    ALLOC(m->final_norm, d * 4);
+    m->layers.resize(c.n_layers);
+    for (auto& L : m->layers) {
+        ALLOC(L.wqkv, (qd + 2 * kvd) * d * es);
+        ALLOC(L.wo, d * qd * es);
+        ALLOC(L.wgu, 2 * F * d * es);
+        ALLOC(L.wdown, d * F * es);
+        ALLOC(L.n1, d * 4);
+        ALLOC(L.n2, d * 4);
+    }
+    ALLOC(m->h, T * d * 4);
+    ALLOC(m->xn, T * d * es);
+    ALLOC(m->q, T * qd * es);
+    ALLOC(m->att, T * qd * es);
+    ALLOC(m->act, T * F * es);
+    ALLOC(m->logits, T * V * 4);
+    ALLOC(m->rope_denom, dh / 2 * 4);
+    m->gemm_ws_floats = (size_t)2 * e->num_sms * 128 * 256;
+    ALLOC(m->gemm_ws, m->gemm_ws_floats * 4);
+    m->gemm_counter_cap = 4096;
+    ALLOC(m->gemm_counters, (size_t)m->gemm_counter_cap * 4);
+#undef ALLOC
+    if (cudaMemsetAsync(m->gemm_counters, 0, (size_t)m->gemm_counter_cap * 4, e->stream) != cudaSuccess ||
+        cudaMemsetAsync(m->xn, 0, T * d * es, e->stream) != cudaSuccess ||
+        cudaMemsetAsync(m->att, 0, T * qd * es, e->stream) != cudaSuccess ||
+        cudaMemsetAsync(m->act, 0, T * F * es, e->stream) != cudaSuccess) {
+        yk_set_error("cudaMemsetAsync failed");
+        return fail(YK_ERR_CUDA);
+    }
+    // RoPE denominators base^(2p/dh) in fp32 (S/gemm.metal:675).
+    std::vector<float> den(dh / 2);
+    for (size_t p = 0; p < dh / 2; ++p) den[p] = std::pow(c.rope_theta, (float)(2 * p) / (float)dh);
+    if (cudaMemcpy(m->rope_denom, den.data(), den.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        yk_set_error("rope table upload failed");
+        return fail(YK_ERR_CUDA);
+    }
+    // Random init: matrices N(0, init_std), norms 1.
+    uint32_t stream_id = 1;
+    auto rnd = [&](void* p, size_t n) { return yk::launch_init(e, p, n, c.dtype, seed, stream_id++, init_std, false); };
+    auto one = [&](float* p, size_t n) { return yk::launch_init(e, p, n, YK_DTYPE_F32, 0, 0, 1.0f, true); };
+    if ((s = rnd(m->embed, V * d)) || (s = rnd(m->lm_head, V * d)) || (s = one(m->final_norm, d))) return fail(s);
+    for (auto& L : m->layers) {
+        if ((s = rnd(L.wqkv, (qd + 2 * kvd) * d)) || (s = rnd(L.wo, d * qd)) || (s = rnd(L.wgu, 2 * F * d)) ||
+            (s = rnd(L.wdown, d * F)) || (s = one(L.n1, d)) || (s = one(L.n2, d)))
+            return fail(s);
+    }
+    if (c.dtype == YK_DTYPE_BF16) {
+        for (auto& L : m->layers) {
+            if ((s = yk::make_weight_map(e, &L.tm_qkv, L.wqkv, (int)(qd + 2 * kvd), (int)d)) ||
+                (s = yk::make_weight_map(e, &L.tm_o, L.wo, (int)d, (int)qd)) ||
+                (s = yk::make_weight_map(e, &L.tm_gu, L.wgu, (int)(2 * F), (int)d)) ||
+                (s = yk::make_weight_map(e, &L.tm_down, L.wdown, (int)d, (int)F)))
+                return fail(s);
+        }
+        if ((s = yk::make_weight_map(e, &m->tm_lm, m->lm_head, (int)V, (int)d))) return fail(s);
+    }
+    if (cudaStreamSynchronize(e->stream) != cudaSuccess) {
+        yk_set_error("model init failed");
+        return fail(YK_ERR_CUDA);
+    }
+    *out = m;
+    return YK_OK;
+}
+
+extern "C" void yk_model_destroy(yk_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->e->device);
+    cudaStreamSynchronize(m->e->stream);
+    for (void* p : m->allocations) cudaFree(p);
+    if (m->meta) cudaFree(m->meta);
+    delete m;
+}
+
+extern "C" yk_status yk_model_get_config(const yk_model* m, yk_model_config* out) {
+    YK_ARG(m && out, "null handle");
+    *out = m->cfg;
+    return YK_OK;
+}
+
+// Where a logical tensor lives: base pointer, first row, row pitch (in rows), rows, cols, element size.
+struct TensorLoc {
+    uint8_t* base;
+    size_t row0, pitch_rows, rows, cols, es;
+};
+
+static yk_status locate(const yk_model* m, int32_t t, int32_t layer, TensorLoc* L) {
+    const auto& c = m->cfg;
+    const size_t d = c.d_model, dh = c.head_dim, qd = (size_t)c.n_heads * dh, kvd = (size_t)c.n_kv_heads * dh;
+    const size_t es = m->esize;
+    const bool per_layer = t >= YK_T_WQ && t <= YK_T_NORM2;
+    YK_ARG(t >= 0 && t <= YK_T_LM_HEAD, "tensor id");
+    if (per_layer) YK_ARG(layer >= 0 && layer < c.n_layers, "layer index");
+    const LayerWeights* W = per_layer ? &m->layers[layer] : nullptr;
+    switch (t) {
+        case YK_T_EMBED: *L = {(uint8_t*)m->embed, 0, 1, (size_t)c.vocab_size, d, es}; break;
+        case YK_T_WQ: *L = {(uint8_t*)W->wqkv, 0, 1, qd, d, es}; break;
+        case YK_T_WK: *L = {(uint8_t*)W->wqkv, qd, 1, kvd, d, es}; break;
+        case YK_T_WV: *L = {(uint8_t*)W->wqkv, qd + kvd, 1, kvd, d, es}; break;
+        case YK_T_WO: *L = {(uint8_t*)W->wo, 0, 1, d, qd, es}; break;
+        case YK_T_WGATE: *L = {(uint8_t*)W->wgu, 0, 2, (size_t)c.ffn_dim, d, es}; break;
+        case YK_T_WUP: *L = {(uint8_t*)W->wgu, 1, 2, (size_t)c.ffn_dim, d, es}; break;
+        case YK_T_WDOWN: *L = {(uint8_t*)W->wdown, 0, 1, d, (size_t)c.ffn_dim, es}; break;
+        case YK_T_NORM1: *L = {(uint8_t*)W->n1, 0, 1, 1, d, 4}; break;
+        case YK_T_NORM2: *L = {(uint8_t*)W->n2, 0, 1, 1, d, 4}; break;
+        case YK_T_FINAL_NORM: *L = {(uint8_t*)m->final_norm, 0, 1, 1, d, 4}; break;
+        case YK_T_LM_HEAD: *L = {(uint8_t*)m->lm_head, 0, 1, (size_t)c.vocab_size, d, es}; break;
+    }
+    return YK_OK;
+}
+
+extern "C" yk_status yk_model_tensor_shape(const yk_model* m, int32_t t, int64_t* rows, int64_t* cols) {
+    YK_ARG(m && rows && cols, "null handle");
+    TensorLoc L;
+    YK_TRY(locate(m, t, 0, &L));
+    *rows = (int64_t)L.rows;
+    *cols = (int64_t)L.cols;
+    return YK_OK;
+}
+
+extern "C" yk_status yk_model_set_tensor(yk_model* m, int32_t t, int32_t layer, const float* host, int32_t layout) {
+    YK_ARG(m && host, "null handle");
+    YK_ARG(layout == YK_LAYOUT_OUT_IN || layout == YK_LAYOUT_IN_OUT, "layout");
+    TensorLoc L;
+    YK_TRY(locate(m, t, layer, &L));
+    yk_engine* e = m->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t n = L.rows * L.cols;
+    YK_TRY(e->ensure_pinned(n * L.es));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    for (size_t r = 0; r < L.rows; ++r)
+        for (size_t k = 0; k < L.cols; ++k) {
+            const float v = layout == YK_LAYOUT_OUT_IN ? host[r * L.cols + k] : host[k * L.rows + r];
+            if (L.es == 2) ((uint16_t*)e->pinned)[r * L.cols + k] = host_bf16(v);
+            else ((float*)e->pinned)[r * L.cols + k] = v;
+        }
+    YK_CHECK_CUDA(cudaMemcpy2DAsync(L.base + L.row0 * L.cols * L.es, L.pitch_rows * L.cols * L.es, e->pinned,
+                                    L.cols * L.es, L.cols * L.es, L.rows, cudaMemcpyHostToDevice, e->stream));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    return YK_OK;
+}
+
+extern "C" yk_status yk_model_get_tensor(yk_model* m, int32_t t, int32_t layer, float* host) {
+    YK_ARG(m && host, "null handle");
+    TensorLoc L;
+    YK_TRY(locate(m, t, layer, &L));
+    yk_engine* e = m->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t n = L.rows * L.cols;
+    YK_TRY(e->ensure_pinned(n * L.es));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    YK_CHECK_CUDA(cudaMemcpy2DAsync(e->pinned, L.cols * L.es, L.base + L.row0 * L.cols * L.es,
+                                    L.pitch_rows * L.cols * L.es, L.cols * L.es, L.rows, cudaMemcpyDeviceToHost,
+                                    e->stream));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    for (size_t i = 0; i < n; ++i)
+        host[i] = L.es == 2 ? host_from_bf16(((uint16_t*)e->pinned)[i]) : ((float*)e->pinned)[i];
+    return YK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// KV pool
+// ---------------------------------------------------------------------------
+extern "C" yk_status yk_kv_pool_create(yk_engine* e, const yk_model_config* cfg, int32_t num_blocks, yk_kv_pool** out) {
+    YK_ARG(e && out, "null handle");
+    *out = nullptr;
+    YK_TRY(validate_cfg(cfg));
+    YK_ARG(num_blocks > 0, "num_blocks");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    auto* p = new yk_kv_pool();
+    p->e = e;
+    p->cfg = *cfg;
+    p->num_blocks = num_blocks;
+    p->esize = cfg->dtype == YK_DTYPE_BF16 ? 2 : 4;
+    p->layer_elems = (size_t)2 * cfg->n_kv_heads * YK_BLOCK_SIZE * cfg->head_dim;
+    p->block_elems = p->layer_elems * cfg->n_layers;
+    const size_t bytes = p->block_elems * num_blocks * p->esize;
+    cudaError_t err = cudaMalloc(&p->data, bytes);
+    if (err != cudaSuccess) {
+        delete p;
+        yk_set_error("KV pool cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(err));
+        return err == cudaErrorMemoryAllocation ? YK_ERR_OOM : YK_ERR_CUDA;
+    }
+    err = cudaMemset(p->data, 0, bytes);
+    if (err != cudaSuccess) {
+        cudaFree(p->data);
+        delete p;
+        yk_set_error(std::string("KV pool memset: ") + cudaGetErrorString(err));
+        return YK_ERR_CUDA;
+    }
+    *out = p;
+    return YK_OK;
+}
+
+extern "C" void yk_kv_pool_destroy(yk_kv_pool* p) {
+    if (!p) return;
+    cudaSetDevice(p->e->device);
+    cudaStreamSynchronize(p->e->stream);
+    cudaFree(p->data);
+    delete p;
+}
+
+extern "C" int32_t yk_kv_pool_num_blocks(const yk_kv_pool* p) { return p ? p->num_blocks : 0; }
+
+extern "C" yk_status yk_kv_pool_fill_random(yk_kv_pool* p, uint64_t seed, float std) {
+    YK_ARG(p, "null handle");
+    YK_CHECK_CUDA(cudaSetDevice(p->e->device));
+    YK_TRY(yk::launch_init(p->e, p->data, p->block_elems * p->num_blocks, p->cfg.dtype, seed, 0x4B56u, std, false));
+    YK_CHECK_CUDA(cudaStreamSynchronize(p->e->stream));
+    return YK_OK;
+}
+
+extern "C" yk_status yk_kv_pool_read_page(yk_kv_pool* p, int32_t block, int32_t layer, int32_t kv, float* host) {
+    YK_ARG(p && host, "null handle");
+    YK_ARG(block >= 0 && block < p->num_blocks && layer >= 0 && layer < p->cfg.n_layers && (kv == 0 || kv == 1),
+           "page index");
+    yk_engine* e = p->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t n = (size_t)p->cfg.n_kv_heads * YK_BLOCK_SIZE * p->cfg.head_dim;
+    YK_TRY(e->ensure_pinned(n * p->esize));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    const uint8_t* src = (const uint8_t*)p->data + ((size_t)block * p->block_elems + (size_t)layer * p->layer_elems +
+                                                    (size_t)kv * n) * p->esize;
+    YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, src, n * p->esize, cudaMemcpyDeviceToHost, e->stream));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    for (size_t i = 0; i < n; ++i)
+        host[i] = p->esize == 2 ? host_from_bf16(((uint16_t*)e->pinned)[i]) : ((float*)e->pinned)[i];
+    return YK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// forward step
+// ---------------------------------------------------------------------------
+extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
+                                     const uint32_t* q_starts, const uint32_t* ctx, int32_t B,
+                                     const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
+                                     int32_t* n_rows) {
+    YK_ARG(m && pool && tokens && q_starts && ctx && block_tables, "null argument");
+    const auto& c = m->cfg;
+    yk_engine* e = m->e;
+    YK_ARG(pool->e == e, "pool belongs to another engine");
+    YK_ARG(pool->cfg.n_layers == c.n_layers && pool->cfg.n_kv_heads == c.n_kv_heads &&
+               pool->cfg.head_dim == c.head_dim && pool->cfg.dtype == c.dtype,
+           "pool shape does not match the model");
+    YK_ARG(T > 0 && T <= c.max_tokens, "T must be in [1, max_tokens]");
+    YK_ARG(B > 0 && B <= c.max_seqs, "B must be in [1, max_seqs]");
+    YK_ARG(max_blocks > 0 && last_n >= 0, "max_blocks / last_n");
+    YK_ARG(q_starts[0] == 0 && (int32_t)q_starts[B] == T, "q_starts must run from 0 to T");
+    // Host-side validation and per-token metadata.
+    int R = 0;
+    for (int b = 0; b < B; ++b) {
+        YK_ARG(q_starts[b + 1] >= q_starts[b], "q_starts must be non-decreasing");
+        const uint32_t n = q_starts[b + 1] - q_starts[b];
+        YK_ARG(ctx[b] >= n, "context_lens[b] must cover the new tokens");
+        YK_ARG((int64_t)(ctx[b] + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE <= max_blocks, "page table too short");
+        for (uint32_t p = 0; p < (ctx[b] + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE; ++p) {
+            const int32_t blk = block_tables[(size_t)b * max_blocks + p];
+            YK_ARG(blk >= 0 && blk < pool->num_blocks, "block id outside the pool");
+        }
+        R += last_n > 0 ? std::min<int>(last_n, (int)n) : (int)n;
+    }
+    for (int t = 0; t < T; ++t) YK_ARG(tokens[t] < (uint32_t)c.vocab_size, "token id >= vocab_size");
+    YK_ARG(R > 0, "no logit rows");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R;
+    YK_TRY(e->ensure_pinned(nmeta * 4));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));  // staging buffer is free again
+    if (nmeta > m->meta_cap) {
+        if (m->meta) cudaFree(m->meta);
+        m->meta = nullptr;
+        m->meta_cap = 0;
+        YK_CHECK_CUDA(cudaMalloc(&m->meta, std::max<size_t>(nmeta * 2, 4096) * 4));
+        m->meta_cap = std::max<size_t>(nmeta * 2, 4096);
+    }
+    int32_t* hm = (int32_t*)e->pinned;
+    int32_t* h_tok = hm;
+    int32_t* h_pos = h_tok + T;
+    int32_t* h_slot = h_pos + T;
+    int32_t* h_seq = h_slot + T;
+    int32_t* h_qs = h_seq + T;
+    int32_t* h_ctx = h_qs + (B + 1);
+    int32_t* h_bt = h_ctx + B;
+    int32_t* h_rows = h_bt + (size_t)B * max_blocks;
+    int r = 0;
+    for (int b = 0; b <= B; ++b) h_qs[b] = (int32_t)q_starts[b];
+    for (int b = 0; b < B; ++b) {
+        const int n = (int)(q_starts[b + 1] - q_starts[b]);
+        h_ctx[b] = (int32_t)ctx[b];
+        for (int i = 0; i < n; ++i) {
+            const int t = (int)q_starts[b] + i;
+            const int pos = (int)ctx[b] - n + i;
+            h_tok[t] = (int32_t)tokens[t];
+            h_pos[t] = pos;
+            h_seq[t] = b;
+            h_slot[t] = block_tables[(size_t)b * max_blocks + pos / YK_BLOCK_SIZE] * YK_BLOCK_SIZE + pos % YK_BLOCK_SIZE;
+        }
+        const int take = last_n > 0 ? std::min(last_n, n) : n;
+        for (int i = n - take; i < n; ++i) h_rows[r++] = (int)q_starts[b] + i;
+    }
+    std::memcpy(h_bt, block_tables, (size_t)B * max_blocks * 4);
+    YK_CHECK_CUDA(cudaMemcpyAsync(m->meta, hm, nmeta * 4, cudaMemcpyHostToDevice, e->stream));
+    const int32_t* dm = m->meta;
+    m->cur.tokens = dm;
+    m->cur.pos = dm + T;
+    m->cur.slot = dm + 2 * T;
+    m->cur.seq = dm + 3 * T;
+    m->cur.q_starts = dm + 4 * T;
+    m->cur.ctx = m->cur.q_starts + (B + 1);
+    m->cur.bt = m->cur.ctx + B;
+    m->cur.rows = m->cur.bt + (size_t)B * max_blocks;
+
+    using namespace yk;
+    const int d = c.d_model, dh = c.head_dim, qd = c.n_heads * dh, kvd = c.n_kv_heads * dh, F = c.ffn_dim;
+    YK_TRY(launch_embed(m, m->cur.tokens, T));
+    for (int l = 0; l < c.n_layers; ++l) {
+        LayerWeights& L = m->layers[l];
+        YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr));
+        EpiParams eq;
+        eq.kind = EPI_QKV;
+        eq.ref_compat = c.ref_compat;
+        eq.out = m->q;
+        eq.q_dim = qd;
+        eq.kv_dim = kvd;
+        eq.head_dim = dh;
+        eq.n_kv = c.n_kv_heads;
+        eq.pos = m->cur.pos;
+        eq.slot = m->cur.slot;
+        eq.rope_denom = m->rope_denom;
+        eq.pool = pool->data;
+        eq.block_elems = (long long)pool->block_elems;
+        eq.layer_off = (long long)l * (long long)pool->layer_elems;
+        eq.pool_blocks = pool->num_blocks;
+        YK_TRY(gemm_run(m, L.wqkv, &L.tm_qkv, m->xn, qd + 2 * kvd, d, T, eq));
+        YK_TRY(attention_run(m, pool, l, T, B, max_blocks));
+        EpiParams er;
+        er.kind = EPI_RESID;
+        er.ref_compat = c.ref_compat;
+        er.h = m->h;
+        er.ld = d;
+        YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, er));
+        YK_TRY(launch_rmsnorm(m, L.n2, T, nullptr));
+        EpiParams eg;
+        eg.kind = EPI_GLU;
+        eg.ref_compat = c.ref_compat;
+        eg.out = m->act;
+        eg.act = c.act;
+        YK_TRY(gemm_run(m, L.wgu, &L.tm_gu, m->xn, 2 * F, d, T, eg));
+        YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, er));
+    }
+    YK_TRY(launch_rmsnorm(m, m->final_norm, R, m->cur.rows));
+    EpiParams el;
+    el.kind = EPI_LOGITS;
+    el.ref_compat = c.ref_compat;
+    el.out = m->logits;
+    el.cap = c.ref_compat ? 30.0f : c.final_cap;
+    YK_TRY(gemm_run(m, m->lm_head, &m->tm_lm, m->xn, c.vocab_size, d, R, el));
+    m->last_rows = R;
+    if (n_rows) *n_rows = R;
+    return YK_OK;
+}
+
+extern "C" yk_status yk_logits_copy_to_host(yk_model* m, int32_t row0, int32_t rows, float* host) {
+    YK_ARG(m && host, "null handle");
+    YK_ARG(row0 >= 0 && rows >= 0 && row0 + rows <= m->last_rows, "rows outside the last step's logits");
+    yk_engine* e = m->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t bytes = (size_t)rows * m->cfg.vocab_size * 4;
+    YK_CHECK_CUDA(cudaMemcpyAsync(host, m->logits + (size_t)row0 * m->cfg.vocab_size, bytes, cudaMemcpyDeviceToHost,
+                                  e->stream));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    uint32_t err = 0;
+    YK_CHECK_CUDA(cudaMemcpy(&err, e->d_err, 4, cudaMemcpyDeviceToHost));
+    if (err) {
+        yk_set_error("device check fired (code " + std::to_string(err) + ")");
+        cudaMemset(e->d_err, 0, 4);
+        return (err & YK_DEV_ERR_TIMEOUT) ? YK_ERR_TIMEOUT : YK_ERR_DEVICE_CHECK;
+    }
+    return YK_OK;
+}

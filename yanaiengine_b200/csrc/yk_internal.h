@@ -1,0 +1,163 @@
+// yk_internal.h -- host-side structures behind the opaque handles of yk.h.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/yk.h"
+
+// ---- error plumbing --------------------------------------------------------
+void yk_set_error(const std::string& msg);
+#define YK_CHECK_CUDA(call)                                                              \
+    do {                                                                                 \
+        cudaError_t e_ = (call);                                                         \
+        if (e_ != cudaSuccess) {                                                         \
+            yk_set_error(std::string(#call) + ": " + cudaGetErrorString(e_));            \
+            return e_ == cudaErrorMemoryAllocation ? YK_ERR_OOM : YK_ERR_CUDA;           \
+        }                                                                                \
+    } while (0)
+#define YK_ARG(cond, msg)                                                                \
+    do {                                                                                 \
+        if (!(cond)) {                                                                   \
+            yk_set_error(std::string("invalid argument: ") + (msg));                     \
+            return YK_ERR_ARG;                                                           \
+        }                                                                                \
+    } while (0)
+#define YK_TRY(call)                                                                     \
+    do {                                                                                 \
+        yk_status s_ = (call);                                                           \
+        if (s_ != YK_OK) return s_;                                                      \
+    } while (0)
+
+typedef CUresult (*PFN_tmapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                        const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                        CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                        CUtensorMapFloatOOBfill);
+
+struct yk_engine {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    uint32_t* d_err = nullptr;           // device error word
+    uint8_t* pinned = nullptr;           // host staging (uploads / downloads)
+    size_t pinned_bytes = 0;
+    uint64_t launches = 0;
+    PFN_tmapEncodeTiled encode_tiled = nullptr;
+    yk_status ensure_pinned(size_t bytes);
+};
+
+// Element counts of the device workspaces.
+struct LayerWeights {
+    void* wqkv = nullptr;   // [(H + 2Hkv)*dh x d]: Q rows, then K rows, then V rows
+    void* wo = nullptr;     // [d x H*dh]
+    void* wgu = nullptr;    // [2F x d]: row 2j = gate j, row 2j+1 = up j
+    void* wdown = nullptr;  // [d x F]
+    float* n1 = nullptr;    // [d]
+    float* n2 = nullptr;    // [d]
+    CUtensorMap tm_qkv, tm_o, tm_gu, tm_down;
+};
+
+struct yk_model {
+    yk_engine* e = nullptr;
+    yk_model_config cfg{};
+    size_t esize = 4;  // bytes per weight / activation element
+    // weights
+    void* embed = nullptr;     // [V x d]
+    void* lm_head = nullptr;   // [V x d]
+    float* final_norm = nullptr;
+    std::vector<LayerWeights> layers;
+    CUtensorMap tm_lm;
+    // activations
+    float* h = nullptr;        // [T x d] fp32 residual stream
+    void* xn = nullptr;        // [T x d] normed input of the next GEMM
+    void* q = nullptr;         // [T x H*dh]
+    void* att = nullptr;       // [T x H*dh]
+    void* act = nullptr;       // [T x F]
+    float* logits = nullptr;   // [T x V]
+    float* rope_denom = nullptr;  // [dh/2]
+    // step metadata (device), packed as int32
+    int32_t* meta = nullptr;
+    size_t meta_cap = 0;       // int32 elements
+    int32_t last_rows = 0;
+    struct {
+        const int32_t *tokens, *pos, *slot, *seq, *q_starts, *ctx, *bt, *rows;
+    } cur{};
+    // split-K partials + per-tile arrival counters
+    float* gemm_ws = nullptr;
+    size_t gemm_ws_floats = 0;
+    uint32_t* gemm_counters = nullptr;
+    int gemm_counter_cap = 0;
+    // attention split-KV partials
+    float* attn_ws = nullptr;
+    size_t attn_ws_floats = 0;
+    // TMA maps of activation buffers, keyed by (buffer, token-box rows)
+    std::map<std::pair<const void*, int>, CUtensorMap> xmaps;
+    std::vector<void*> allocations;
+};
+
+struct yk_kv_pool {
+    yk_engine* e = nullptr;
+    yk_model_config cfg{};
+    int32_t num_blocks = 0;
+    size_t esize = 4;
+    void* data = nullptr;      // [block][layer][2][Hkv][16][dh]
+    size_t block_elems = 0;    // elements per block (all layers)
+    size_t layer_elems = 0;    // elements per layer within a block
+};
+
+struct yk_sampler {
+    yk_engine* e = nullptr;
+    int32_t max_seqs = 0, k = 0, vocab = 0;
+    float* probs = nullptr;     // [max_seqs x k x V] draft probabilities
+    float* q = nullptr;         // [max_seqs x (k+1) x V] target probs (probs entry) or logits
+    float* dlogits = nullptr;   // [max_seqs x k x V] draft logits (yk_spec_sample_logits)
+    float* stats = nullptr;     // [max_seqs x (2k+1) x 4] (max, sum, argmax, -)
+    uint32_t* io = nullptr;     // small device io area
+};
+
+// ---- internal launchers ----------------------------------------------------
+namespace yk {
+
+enum EpiKind : int { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GLU = 3, EPI_LOGITS = 4 };
+
+// Everything a GEMM epilogue needs.  Row n = output feature, column j = token.
+struct EpiParams {
+    int kind = EPI_STORE;
+    int n_out = 0;          // valid output rows
+    int m_tok = 0;          // valid tokens
+    int ref_compat = 0;
+    // EPI_STORE: out[j * n_out + n] (activation dtype)
+    void* out = nullptr;
+    // EPI_QKV
+    int q_dim = 0, kv_dim = 0, head_dim = 0, n_kv = 0;
+    const int32_t* pos = nullptr;    // [m_tok] token positions
+    const int32_t* slot = nullptr;   // [m_tok] pool slot = block*16 + offset
+    const float* rope_denom = nullptr;
+    void* pool = nullptr;
+    long long block_elems = 0, layer_off = 0;
+    int pool_blocks = 0;
+    // EPI_RESID: h[j * ld + n] += v
+    float* h = nullptr;
+    int ld = 0;
+    // EPI_GLU: out[j * (n_out/2) + n/2] = act(gate) * up
+    int act = 0;
+    // EPI_LOGITS: logits[j * n_out + n]
+    float cap = 0.f;
+    uint32_t* err = nullptr;
+};
+
+yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const void* X, int n_out, int K, int m_tok,
+                   const EpiParams& ep, int force_splits = 0);
+yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
+yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks);
+yk_status launch_embed(yk_model* m, const int32_t* tokens, int T);
+yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx);
+yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed, uint32_t stream, float std,
+                      bool constant);
+
+}  // namespace yk

@@ -1,0 +1,535 @@
+// yk_sampler.cu -- fused speculative sampling on the device.  Replaces the
+// CPU SpeculativeSampler (S/SpeculativeSampler.swift:4-130) and the
+// Scheduler's per-sequence draft sampling (S/Scheduler.swift:171-189).
+//
+// Bit-exact contract: given identical probability tensors and uniforms, every
+// acceptance decision and emitted token equals the reference's, because every
+// value the reference derives from the probabilities is derived here with the
+// same single IEEE fp32 operation (__fdiv_rn, __fsub_rn, __fadd_rn; no FMA
+// contraction) in the same order:
+//   ratio = q[d] / p[d]; accept iff r < ratio                    (:25-34)
+//   residual = max(0, q - p) summed sequentially, divided by the sum (:37-55)
+//   cdf += prob[i] sequentially; first i with r <= cdf, else V-1  (:63-73)
+// The two sequential sums are "chains": one thread adds in index order while
+// the rest of the CTA stages the next chunk of summands in shared memory.
+#include <algorithm>
+#include <cstring>
+
+#include "yk_common.cuh"
+#include "yk_internal.h"
+
+namespace yk {
+
+constexpr int SMP_THREADS = 512;
+constexpr int CHAIN_CH = 2048;
+
+// Swift's max(0, y): y if y >= 0 else 0 (max(0, NaN) = 0, max(0, -0.0) = -0.0).
+__device__ __forceinline__ float swift_max0(float y) { return (y >= 0.0f) ? y : 0.0f; }
+
+// softmax element from logits with row stats (max m and sum s of exp(x - m)):
+// exp(x/T - m) / s  (S/SpeculativeSampler.swift:80-88, temperature per
+// S/Sampler.swift:19-23).
+__device__ __forceinline__ float scale_t(float l, float T) { return (T == 1.0f) ? l : __fdiv_rn(l, T); }
+__device__ __forceinline__ float q_from_logit(float l, float T, float m, float s) {
+    return __fdiv_rn(expf(__fsub_rn(scale_t(l, T), m)), s);
+}
+
+struct RowStats {
+    float m, s;
+    int arg;
+};
+
+// Block-wide (max, sum-exp, first argmax) of x_i = l_i / T over one row.
+__device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, float T) {
+    float m = -INFINITY, s = 0.f, best = -INFINITY;
+    int arg = 0x7fffffff;
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+        const float raw = row[i];
+        const float x = scale_t(raw, T);
+        if (raw > best) { best = raw; arg = (int)i; }
+        if (x > m) {
+            s = s * expf(m - x) + 1.0f;
+            m = x;
+        } else {
+            s += expf(x - m);
+        }
+    }
+    __shared__ float sm_m[32], sm_s[32], sm_b[32];
+    __shared__ int sm_a[32];
+    // warp reduce
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const int a2 = __shfl_xor_sync(0xffffffffu, arg, o);
+        const float M = fmaxf(m, m2);
+        if (M != -INFINITY) s = s * expf(m - M) + s2 * expf(m2 - M);
+        m = M;
+        if (b2 > best || (b2 == best && a2 < arg)) { best = b2; arg = a2; }
+    }
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    if (ln == 0) { sm_m[w] = m; sm_s[w] = s; sm_b[w] = best; sm_a[w] = arg; }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        m = ln < nw ? sm_m[ln] : -INFINITY;
+        s = ln < nw ? sm_s[ln] : 0.f;
+        best = ln < nw ? sm_b[ln] : -INFINITY;
+        arg = ln < nw ? sm_a[ln] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+            const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+            const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+            const int a2 = __shfl_xor_sync(0xffffffffu, arg, o);
+            const float M = fmaxf(m, m2);
+            if (M != -INFINITY) s = s * expf(m - M) + s2 * expf(m2 - M);
+            m = M;
+            if (b2 > best || (b2 == best && a2 < arg)) { best = b2; arg = a2; }
+        }
+        if (ln == 0) { sm_m[0] = m; sm_s[0] = s; sm_a[0] = (arg == 0x7fffffff) ? 0 : arg; }
+    }
+    __syncthreads();
+    RowStats r{sm_m[0], sm_s[0], sm_a[0]};
+    __syncthreads();
+    return r;
+}
+
+// The reference's sequential fp32 chain c = fl(c + f(i)), i = 0..n-1.
+// search: returns the first i with r <= c (sampleFromProbs), or n-1.
+// !search: returns -1 and the final sum in *sum.
+// Thread 0 adds in index order; threads 1.. stage the next chunk meanwhile.
+struct ChainSmem {
+    __align__(16) float buf[2][CHAIN_CH];
+    long long found_slot[2];
+    float cdf;
+};
+
+template <class F>
+__device__ int64_t block_chain(ChainSmem& cs, F f, int64_t n, bool search, float r, float* sum) {
+    auto& buf = cs.buf;
+    auto& found_slot = cs.found_slot;
+    float& s_cdf = cs.cdf;
+    const int64_t nch = (n + CHAIN_CH - 1) / CHAIN_CH;
+    for (int i = threadIdx.x; i < CHAIN_CH; i += blockDim.x) buf[0][i] = i < n ? f((int64_t)i) : 0.f;
+    if (threadIdx.x == 0) { s_cdf = 0.f; found_slot[0] = -1; found_slot[1] = -1; }
+    __syncthreads();
+    int64_t found = -1;
+    for (int64_t c = 0; c < nch; ++c) {
+        const float* cur = buf[c & 1];
+        float* nxt = buf[(c + 1) & 1];
+        if (threadIdx.x == 0) {
+            float cdf = s_cdf;
+            const int64_t rem = n - c * CHAIN_CH;
+            const int len = rem < CHAIN_CH ? (int)rem : CHAIN_CH;
+            long long hit = -1;
+            int i = 0;
+            for (; i + 4 <= len; i += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(cur + i);
+                cdf = __fadd_rn(cdf, v.x);
+                if (search && r <= cdf) { hit = c * CHAIN_CH + i; break; }
+                cdf = __fadd_rn(cdf, v.y);
+                if (search && r <= cdf) { hit = c * CHAIN_CH + i + 1; break; }
+                cdf = __fadd_rn(cdf, v.z);
+                if (search && r <= cdf) { hit = c * CHAIN_CH + i + 2; break; }
+                cdf = __fadd_rn(cdf, v.w);
+                if (search && r <= cdf) { hit = c * CHAIN_CH + i + 3; break; }
+            }
+            if (hit < 0)
+                for (; i < len; ++i) {
+                    cdf = __fadd_rn(cdf, cur[i]);
+                    if (search && r <= cdf) { hit = c * CHAIN_CH + i; break; }
+                }
+            s_cdf = cdf;
+            found_slot[c & 1] = hit;
+        } else if (c + 1 < nch) {
+            const int64_t base = (c + 1) * CHAIN_CH;
+            for (int i = threadIdx.x - 1; i < CHAIN_CH; i += blockDim.x - 1)
+                nxt[i] = (base + i < n) ? f(base + i) : 0.f;
+        }
+        __syncthreads();
+        found = found_slot[c & 1];  // written by thread 0 every chunk; double-buffered
+        if (found >= 0) break;
+    }
+    const float total = s_cdf;
+    __syncthreads();
+    if (sum) *sum = total;
+    if (!search) return -1;
+    return found >= 0 ? found : n - 1;  // :72 fallback to the last token
+}
+
+// ---------------------------------------------------------------------------
+// Row statistics for many rows: stats[r] = (max, sum, argmax).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(SMP_THREADS) row_stats_kernel(const float* __restrict__ logits, int64_t V, float T,
+                                                                 float* __restrict__ stats) {
+    const int r = blockIdx.x;
+    const RowStats st = block_row_stats(logits + (size_t)r * V, V, T);
+    if (threadIdx.x == 0) {
+        stats[r * 4 + 0] = st.m;
+        stats[r * 4 + 1] = st.s;
+        stats[r * 4 + 2] = __int_as_float(st.arg);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Draft sampling: one CTA per (sequence b, draft iteration j).
+// p row -> probs[(b*k + j) * V]; token -> tokens[b*k + j] (or tokens[b]).
+// ---------------------------------------------------------------------------
+struct DraftArgs {
+    const float* logits;   // row for CTA x: logits + row(x) * V
+    int logit_row_stride;  // rows between consecutive sequences
+    int logit_row_j_mul;   // rows between consecutive draft iterations
+    int64_t V;
+    int k, j_fixed;        // j_fixed >= 0: single iteration j for all CTAs
+    float T;
+    uint64_t seed;
+    uint32_t step;
+    const uint32_t* seq_ids;
+    float* probs;
+    uint32_t* tokens_out;
+};
+
+__global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) {
+    __shared__ ChainSmem cs;
+    const int b = a.j_fixed >= 0 ? blockIdx.x : blockIdx.x / a.k;
+    const int j = a.j_fixed >= 0 ? a.j_fixed : blockIdx.x % a.k;
+    const float* row = a.logits + ((size_t)b * a.logit_row_stride + (size_t)j * a.logit_row_j_mul) * a.V;
+    float* p = a.probs + ((size_t)b * a.k + j) * a.V;
+    const int64_t V = a.V;
+    const RowStats st = block_row_stats(row, V, a.T > 0.f ? a.T : 1.0f);
+    uint32_t tok;
+    if (a.T <= 0.f) {  // greedy: one-hot p
+        for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = (i == st.arg) ? 1.0f : 0.0f;
+        tok = (uint32_t)st.arg;
+    } else {
+        const float T = a.T, m = st.m, s = st.s;
+        for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = q_from_logit(row[i], T, m, s);
+        const float r = uniform_at(a.seed, a.step, a.seq_ids[b], (uint32_t)j, SLOT_DRAFT);
+        tok = (uint32_t)block_chain(cs, [&](int64_t i) { return q_from_logit(row[i], T, m, s); }, V, true, r,
+                                    nullptr);
+    }
+    if (threadIdx.x == 0) {
+        if (a.j_fixed >= 0) a.tokens_out[b] = tok;
+        else a.tokens_out[(size_t)b * a.k + j] = tok;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// verifySequence: one CTA per sequence.
+// ---------------------------------------------------------------------------
+struct VerifyArgs {
+    const float* q;         // probs mode: q rows; logits mode: target logits rows
+    const float* stats;     // logits mode: per target row (max, sum, argmax)
+    const float* p;         // draft probs [B x k x V]
+    const uint32_t* drafts; // [B x k]
+    int64_t V;
+    int k;
+    int from_logits;
+    float T;
+    uint64_t seed;
+    uint32_t step;
+    const uint32_t* seq_ids;
+    uint32_t* out;          // [B x (k+1)]
+    int32_t* counts;        // [B]
+};
+
+__global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
+    __shared__ ChainSmem cs;
+    const int b = blockIdx.x;
+    const int k = a.k;
+    const int64_t V = a.V;
+    const uint32_t seq = a.seq_ids[b];
+    const bool greedy = a.from_logits && a.T <= 0.f;
+    const float T = a.T > 0.f ? a.T : 1.0f;
+    auto qrow = [&](int i) { return a.q + ((size_t)b * (k + 1) + i) * V; };
+    auto st = [&](int i) { return a.stats + ((size_t)b * (k + 1) + i) * 4; };
+    auto qval = [&](int i, int64_t x) -> float {
+        if (!a.from_logits) return qrow(i)[x];
+        return q_from_logit(qrow(i)[x], T, st(i)[0], st(i)[1]);
+    };
+    __shared__ int s_rej;
+    if (threadIdx.x == 0) {
+        int rej = k;
+        for (int i = 0; i < k; ++i) {
+            const uint32_t d = a.drafts[(size_t)b * k + i];
+            bool acc;
+            if (greedy) {
+                acc = (uint32_t)__float_as_int(st(i)[2]) == d;
+            } else {
+                const float px = a.p[((size_t)b * k + i) * V + d];
+                const float qx = qval(i, d);
+                const float ratio = __fdiv_rn(qx, px);
+                const float r = uniform_at(a.seed, a.step, seq, (uint32_t)i, SLOT_ACCEPT);
+                acc = r < ratio;
+            }
+            if (!acc) { rej = i; break; }
+        }
+        s_rej = rej;
+    }
+    __syncthreads();
+    const int rej = s_rej;
+    uint32_t tok;
+    if (greedy) {
+        tok = (uint32_t)__float_as_int(st(rej)[2]);
+    } else if (rej < k) {
+        const float* pr = a.p + ((size_t)b * k + rej) * V;
+        float S = 0.f;
+        auto diff = [&](int64_t x) { return swift_max0(__fsub_rn(qval(rej, x), pr[x])); };
+        block_chain(cs, diff, V, false, 0.f, &S);
+        const float r = uniform_at(a.seed, a.step, seq, (uint32_t)rej, SLOT_RESAMPLE);
+        if (S > 0.0f)
+            tok = (uint32_t)block_chain(cs, [&](int64_t x) { return __fdiv_rn(diff(x), S); }, V, true, r, nullptr);
+        else
+            tok = (uint32_t)block_chain(cs, [&](int64_t x) { return qval(rej, x); }, V, true, r, nullptr);
+    } else {
+        const float r = uniform_at(a.seed, a.step, seq, (uint32_t)k, SLOT_BONUS);
+        tok = (uint32_t)block_chain(cs, [&](int64_t x) { return qval(k, x); }, V, true, r, nullptr);
+    }
+    if (threadIdx.x == 0) {
+        uint32_t* o = a.out + (size_t)b * (k + 1);
+        for (int i = 0; i < rej; ++i) o[i] = a.drafts[(size_t)b * k + i];
+        o[rej] = tok;
+        a.counts[b] = rej + 1;
+    }
+}
+
+}  // namespace yk
+
+// ---------------------------------------------------------------------------
+// C-ABI
+// ---------------------------------------------------------------------------
+using namespace yk;
+
+extern "C" yk_status yk_sampler_create(yk_engine* e, int32_t max_seqs, int32_t k, int32_t vocab, yk_sampler** out) {
+    YK_ARG(e && out, "null handle");
+    YK_ARG(max_seqs > 0 && k > 0 && k <= 16 && vocab > 0, "sampler shape");
+    *out = nullptr;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    auto* s = new yk_sampler();
+    s->e = e;
+    s->max_seqs = max_seqs;
+    s->k = k;
+    s->vocab = vocab;
+    const size_t V = vocab;
+    cudaError_t err = cudaSuccess;
+    if ((err = cudaMalloc(&s->probs, (size_t)max_seqs * k * V * 4)) != cudaSuccess ||
+        (err = cudaMalloc(&s->q, (size_t)max_seqs * (k + 1) * V * 4)) != cudaSuccess ||
+        (err = cudaMalloc(&s->stats, (size_t)max_seqs * (2 * k + 1) * 4 * 4)) != cudaSuccess ||
+        (err = cudaMalloc(&s->io, (size_t)max_seqs * (3 * k + 8) * 4 + 4096)) != cudaSuccess) {
+        yk_sampler_destroy(s);
+        yk_set_error(std::string("sampler cudaMalloc: ") + cudaGetErrorString(err));
+        return err == cudaErrorMemoryAllocation ? YK_ERR_OOM : YK_ERR_CUDA;
+    }
+    *out = s;
+    return YK_OK;
+}
+
+extern "C" void yk_sampler_destroy(yk_sampler* s) {
+    if (!s) return;
+    cudaSetDevice(s->e->device);
+    cudaStreamSynchronize(s->e->stream);
+    if (s->probs) cudaFree(s->probs);
+    if (s->q) cudaFree(s->q);
+    if (s->dlogits) cudaFree(s->dlogits);
+    if (s->stats) cudaFree(s->stats);
+    if (s->io) cudaFree(s->io);
+    delete s;
+}
+
+// io area layout (uint32): [0, B) seq ids | [B, B + B*k) drafts | then out B*(k+1) | counts B | err 1
+struct IoLayout {
+    uint32_t *seq, *drafts, *out;
+    int32_t* counts;
+};
+static IoLayout io_layout(yk_sampler* s, int B) {
+    IoLayout L;
+    L.seq = s->io;
+    L.drafts = L.seq + B;
+    L.out = L.drafts + (size_t)B * s->k;
+    L.counts = (int32_t*)(L.out + (size_t)B * (s->k + 1));
+    return L;
+}
+
+static yk_status finish_verify(yk_sampler* s, int B, const IoLayout& L, uint32_t* out_tokens, int32_t* out_counts) {
+    yk_engine* e = s->e;
+    const int k = s->k;
+    const size_t nout = (size_t)B * (k + 1) + B;
+    YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, nout * 4, cudaMemcpyDeviceToHost, e->stream));
+    YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + nout * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    uint32_t err;
+    std::memcpy(&err, e->pinned + nout * 4, 4);
+    if (err) {
+        cudaMemset(e->d_err, 0, 4);
+        yk_set_error("device check fired during the step (code " + std::to_string(err) + ")");
+        return (err & YK_DEV_ERR_TIMEOUT) ? YK_ERR_TIMEOUT : YK_ERR_DEVICE_CHECK;
+    }
+    std::memcpy(out_tokens, e->pinned, (size_t)B * (k + 1) * 4);
+    std::memcpy(out_counts, e->pinned + (size_t)B * (k + 1) * 4, (size_t)B * 4);
+    return YK_OK;
+}
+
+static yk_status upload_small(yk_sampler* s, int B, const uint32_t* seq_ids, const uint32_t* drafts,
+                              const IoLayout& L) {
+    yk_engine* e = s->e;
+    const size_t n = (size_t)B + (drafts ? (size_t)B * s->k : 0);
+    YK_TRY(e->ensure_pinned(std::max<size_t>(n * 4, (size_t)B * (s->k + 2) * 4 + 64)));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    std::memcpy(e->pinned, seq_ids, (size_t)B * 4);
+    if (drafts) std::memcpy(e->pinned + (size_t)B * 4, drafts, (size_t)B * s->k * 4);
+    YK_CHECK_CUDA(cudaMemcpyAsync(L.seq, e->pinned, n * 4, cudaMemcpyHostToDevice, e->stream));
+    // The pinned buffer is reused for the results; order the reuse after this copy.
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    return YK_OK;
+}
+
+extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, int32_t j, float temperature,
+                                     uint64_t seed, uint32_t step, const uint32_t* seq_ids, uint32_t* out_tokens) {
+    YK_ARG(s && draft && seq_ids && out_tokens, "null argument");
+    YK_ARG(B > 0 && B <= s->max_seqs && j >= 0 && j < s->k, "B / j");
+    YK_ARG(draft->cfg.vocab_size == s->vocab, "vocab mismatch");
+    YK_ARG(draft->last_rows >= B, "draft logits hold fewer rows than B (forward with last_n = 1)");
+    yk_engine* e = s->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    IoLayout L = io_layout(s, B);
+    YK_TRY(upload_small(s, B, seq_ids, nullptr, L));
+    DraftArgs a;
+    a.logits = draft->logits;
+    a.logit_row_stride = 1;
+    a.logit_row_j_mul = 0;
+    a.V = s->vocab;
+    a.k = s->k;
+    a.j_fixed = j;
+    a.T = temperature;
+    a.seed = seed;
+    a.step = step;
+    a.seq_ids = L.seq;
+    a.probs = s->probs;
+    a.tokens_out = L.out;
+    draft_sample_kernel<<<B, SMP_THREADS, 0, e->stream>>>(a);
+    e->launches++;
+    YK_CHECK_CUDA(cudaGetLastError());
+    YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, (size_t)B * 4, cudaMemcpyDeviceToHost, e->stream));
+    YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + (size_t)B * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    uint32_t err;
+    std::memcpy(&err, e->pinned + (size_t)B * 4, 4);
+    if (err) {
+        cudaMemset(e->d_err, 0, 4);
+        yk_set_error("device check fired during the draft step (code " + std::to_string(err) + ")");
+        return (err & YK_DEV_ERR_TIMEOUT) ? YK_ERR_TIMEOUT : YK_ERR_DEVICE_CHECK;
+    }
+    std::memcpy(out_tokens, e->pinned, (size_t)B * 4);
+    return YK_OK;
+}
+
+static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_logits, float T, uint64_t seed,
+                            uint32_t step, const IoLayout& L) {
+    yk_engine* e = s->e;
+    const int k = s->k;
+    if (from_logits) {
+        row_stats_kernel<<<B * (k + 1), SMP_THREADS, 0, e->stream>>>(qsrc, s->vocab, T > 0.f ? T : 1.0f, s->stats);
+        e->launches++;
+        YK_CHECK_CUDA(cudaGetLastError());
+    }
+    VerifyArgs a;
+    a.q = qsrc;
+    a.stats = s->stats;
+    a.p = s->probs;
+    a.drafts = L.drafts;
+    a.V = s->vocab;
+    a.k = k;
+    a.from_logits = from_logits;
+    a.T = T;
+    a.seed = seed;
+    a.step = step;
+    a.seq_ids = L.seq;
+    a.out = L.out;
+    a.counts = L.counts;
+    verify_kernel<<<B, SMP_THREADS, 0, e->stream>>>(a);
+    e->launches++;
+    YK_CHECK_CUDA(cudaGetLastError());
+    return YK_OK;
+}
+
+extern "C" yk_status yk_spec_verify(yk_sampler* s, yk_model* target, int32_t B, float temperature, uint64_t seed,
+                                    uint32_t step, const uint32_t* seq_ids, const uint32_t* draft_tokens,
+                                    uint32_t* out_tokens, int32_t* out_counts) {
+    YK_ARG(s && target && seq_ids && draft_tokens && out_tokens && out_counts, "null argument");
+    YK_ARG(B > 0 && B <= s->max_seqs, "B");
+    YK_ARG(target->cfg.vocab_size == s->vocab, "vocab mismatch");
+    YK_ARG(target->last_rows == B * (s->k + 1), "target logits must hold k+1 rows per sequence (last_n = k+1)");
+    for (int i = 0; i < B * s->k; ++i) YK_ARG(draft_tokens[i] < (uint32_t)s->vocab, "draft token >= vocab");
+    yk_engine* e = s->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    IoLayout L = io_layout(s, B);
+    YK_TRY(upload_small(s, B, seq_ids, draft_tokens, L));
+    YK_TRY(run_verify(s, B, target->logits, 1, temperature, seed, step, L));
+    return finish_verify(s, B, L, out_tokens, out_counts);
+}
+
+extern "C" yk_status yk_spec_verify_probs(yk_sampler* s, int32_t B, const float* p, const float* q,
+                                          const uint32_t* draft_tokens, uint64_t seed, uint32_t step,
+                                          const uint32_t* seq_ids, uint32_t* out_tokens, int32_t* out_counts) {
+    YK_ARG(s && p && q && draft_tokens && seq_ids && out_tokens && out_counts, "null argument");
+    YK_ARG(B > 0 && B <= s->max_seqs, "B");
+    for (int i = 0; i < B * s->k; ++i) YK_ARG(draft_tokens[i] < (uint32_t)s->vocab, "draft token >= vocab");
+    yk_engine* e = s->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t V = s->vocab;
+    IoLayout L = io_layout(s, B);
+    YK_TRY(upload_small(s, B, seq_ids, draft_tokens, L));
+    YK_CHECK_CUDA(cudaMemcpyAsync(s->probs, p, (size_t)B * s->k * V * 4, cudaMemcpyHostToDevice, e->stream));
+    YK_CHECK_CUDA(cudaMemcpyAsync(s->q, q, (size_t)B * (s->k + 1) * V * 4, cudaMemcpyHostToDevice, e->stream));
+    YK_TRY(run_verify(s, B, s->q, 0, 1.0f, seed, step, L));
+    return finish_verify(s, B, L, out_tokens, out_counts);
+}
+
+extern "C" yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float* draft_logits,
+                                           const float* target_logits, float temperature, uint64_t seed,
+                                           uint32_t step, const uint32_t* seq_ids, uint32_t* draft_tokens_out,
+                                           uint32_t* out_tokens, int32_t* out_counts) {
+    YK_ARG(s && draft_logits && target_logits && seq_ids && draft_tokens_out && out_tokens && out_counts,
+           "null argument");
+    YK_ARG(B > 0 && B <= s->max_seqs, "B");
+    yk_engine* e = s->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t V = s->vocab;
+    const int k = s->k;
+    if (!s->dlogits) YK_CHECK_CUDA(cudaMalloc(&s->dlogits, (size_t)s->max_seqs * k * V * 4));
+    IoLayout L = io_layout(s, B);
+    YK_TRY(upload_small(s, B, seq_ids, nullptr, L));
+    YK_CHECK_CUDA(cudaMemcpyAsync(s->dlogits, draft_logits, (size_t)B * k * V * 4, cudaMemcpyHostToDevice, e->stream));
+    YK_CHECK_CUDA(cudaMemcpyAsync(s->q, target_logits, (size_t)B * (k + 1) * V * 4, cudaMemcpyHostToDevice, e->stream));
+    DraftArgs a;
+    a.logits = s->dlogits;
+    a.logit_row_stride = k;
+    a.logit_row_j_mul = 1;
+    a.V = V;
+    a.k = k;
+    a.j_fixed = -1;
+    a.T = temperature;
+    a.seed = seed;
+    a.step = step;
+    a.seq_ids = L.seq;
+    a.probs = s->probs;
+    a.tokens_out = L.drafts;
+    draft_sample_kernel<<<B * k, SMP_THREADS, 0, e->stream>>>(a);
+    e->launches++;
+    YK_CHECK_CUDA(cudaGetLastError());
+    YK_TRY(run_verify(s, B, s->q, 1, temperature, seed, step, L));
+    YK_CHECK_CUDA(cudaMemcpyAsync(draft_tokens_out, L.drafts, (size_t)B * k * 4, cudaMemcpyDeviceToHost, e->stream));
+    return finish_verify(s, B, L, out_tokens, out_counts);
+}
+
+extern "C" yk_status yk_sampler_read_probs(yk_sampler* s, int32_t b, int32_t j, float* host) {
+    YK_ARG(s && host, "null argument");
+    YK_ARG(b >= 0 && b < s->max_seqs && j >= 0 && j < s->k, "index");
+    YK_CHECK_CUDA(cudaSetDevice(s->e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(s->e->stream));
+    YK_CHECK_CUDA(cudaMemcpy(host, s->probs + ((size_t)b * s->k + j) * s->vocab, (size_t)s->vocab * 4,
+                             cudaMemcpyDeviceToHost));
+    return YK_OK;
+}

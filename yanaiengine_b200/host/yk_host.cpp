@@ -1,0 +1,336 @@
+// yk_host.cpp -- host-side Scheduler / SequenceRequest / PagedKVCache /
+// BlockAllocator (see include/yk_host.h), driving libyk.so through yk.h only.
+#include "../../include/yk_host.h"
+
+#include <algorithm>
+#include <cstring>
+#include <deque>
+#include <memory>
+#include <optional>
+#include <set>
+#include <string>
+#include <vector>
+
+#define YK_TRY(call)                   \
+    do {                               \
+        yk_status s_ = (call);         \
+        if (s_ != YK_OK) return s_;    \
+    } while (0)
+
+namespace {
+
+// BlockAllocator (S/BlockAllocator.swift:6-65): LIFO free list, block 0 first.
+class BlockAllocator {
+  public:
+    explicit BlockAllocator(int num_blocks) : num_blocks_(num_blocks) { reset(); }
+    std::optional<int> allocate() {
+        if (free_.empty()) return std::nullopt;
+        const int b = free_.back();
+        free_.pop_back();
+        allocated_.insert(b);
+        return b;
+    }
+    void deallocate(int b) {
+        if (allocated_.erase(b)) free_.push_back(b);
+    }
+    float usage() const { return (float)allocated_.size() / (float)num_blocks_; }
+    void reset() {
+        free_.clear();
+        for (int i = num_blocks_ - 1; i >= 0; --i) free_.push_back(i);
+        allocated_.clear();
+    }
+    int num_blocks() const { return num_blocks_; }
+
+  private:
+    int num_blocks_;
+    std::vector<int> free_;
+    std::set<int> allocated_;
+};
+
+// PagedKVCache (S/PagedKVCache.swift:6-90).  One page table per sequence and
+// model covers every layer (the pool is [block][layer][K|V]...).
+class PagedKVCache {
+  public:
+    explicit PagedKVCache(BlockAllocator* a) : alloc_(a) {}
+    ~PagedKVCache() { reset(); }
+    // Pages for positions < n (appendFromFull allocates at pos % 16 == 0, :29-35).
+    bool reserve(int n) {
+        const int need = (n + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE;
+        while ((int)page_table.size() < need) {
+            auto b = alloc_->allocate();
+            if (!b) return false;
+            page_table.push_back(*b);
+        }
+        return true;
+    }
+    // rollback(to:) :65-76.
+    void rollback(int position) {
+        if (position > current_position) return;
+        const int need = (position + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE;
+        while ((int)page_table.size() > need) {
+            alloc_->deallocate(page_table.back());
+            page_table.pop_back();
+        }
+        current_position = position;
+    }
+    void reset() {
+        for (int b : page_table) alloc_->deallocate(b);
+        page_table.clear();
+        current_position = 0;
+    }
+    std::vector<int> page_table;
+    int current_position = 0;
+
+  private:
+    BlockAllocator* alloc_;
+};
+
+// SequenceRequest (S/Scheduler.swift:5-80).
+struct SequenceRequest {
+    uint32_t id = 0;
+    std::vector<uint32_t> prompt, generated;
+    std::unique_ptr<PagedKVCache> cache, draft_cache;
+    int max_tokens = 0;
+    int64_t stop_token = -1;
+    bool finished = false;
+    int total() const { return (int)(prompt.size() + generated.size()); }
+    uint32_t at(int i) const { return i < (int)prompt.size() ? prompt[i] : generated[i - prompt.size()]; }
+};
+
+}  // namespace
+
+struct ykh_scheduler {
+    yk_model* target = nullptr;
+    yk_model* draft = nullptr;
+    yk_kv_pool* tpool = nullptr;
+    yk_kv_pool* dpool = nullptr;
+    yk_sampler* sampler = nullptr;
+    int k = 4;
+    float temperature = 1.0f;
+    uint64_t seed = 0;
+    uint32_t step_no = 0;
+    std::unique_ptr<BlockAllocator> talloc, dalloc;
+    std::deque<std::unique_ptr<SequenceRequest>> waiting;
+    std::vector<std::unique_ptr<SequenceRequest>> running, done;
+    int64_t n_steps = 0, n_emitted = 0, n_accepted = 0;
+    // per-step scratch
+    std::vector<uint32_t> tokens, qstarts, ctx, seq_ids, drafts, out_tokens;
+    std::vector<int32_t> tables, counts;
+};
+
+extern "C" yk_status ykh_scheduler_create(yk_model* target, yk_kv_pool* tpool, yk_model* draft, yk_kv_pool* dpool,
+                                          yk_sampler* sampler, int32_t k, float temperature, uint64_t seed,
+                                          ykh_scheduler** out) {
+    if (!target || !tpool || !draft || !dpool || !sampler || !out || k <= 0) return YK_ERR_ARG;
+    auto* s = new ykh_scheduler();
+    s->target = target;
+    s->draft = draft;
+    s->tpool = tpool;
+    s->dpool = dpool;
+    s->sampler = sampler;
+    s->k = k;
+    s->temperature = temperature;
+    s->seed = seed;
+    s->talloc = std::make_unique<BlockAllocator>(yk_kv_pool_num_blocks(tpool));
+    s->dalloc = std::make_unique<BlockAllocator>(yk_kv_pool_num_blocks(dpool));
+    *out = s;
+    return YK_OK;
+}
+
+extern "C" void ykh_scheduler_destroy(ykh_scheduler* s) {
+    if (!s) return;
+    s->waiting.clear();
+    s->running.clear();
+    s->done.clear();
+    delete s;
+}
+
+static yk_status submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens, int64_t stop,
+                        uint32_t seq_id, bool cached) {
+    if (!s || !prompt || n <= 0) return YK_ERR_ARG;
+    auto r = std::make_unique<SequenceRequest>();
+    r->id = seq_id;
+    r->prompt.assign(prompt, prompt + n);
+    r->max_tokens = max_tokens;
+    r->stop_token = stop;
+    r->cache = std::make_unique<PagedKVCache>(s->talloc.get());
+    r->draft_cache = std::make_unique<PagedKVCache>(s->dalloc.get());
+    if (cached) {
+        if (!r->cache->reserve(n - 1) || !r->draft_cache->reserve(n - 1)) return YK_ERR_OOM;
+        r->cache->current_position = n - 1;
+        r->draft_cache->current_position = n - 1;
+        s->running.push_back(std::move(r));
+    } else {
+        s->waiting.push_back(std::move(r));
+    }
+    return YK_OK;
+}
+
+extern "C" yk_status ykh_submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
+                                int64_t stop_token, uint32_t seq_id) {
+    return submit(s, prompt, n, max_tokens, stop_token, seq_id, false);
+}
+extern "C" yk_status ykh_submit_cached(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
+                                       int64_t stop_token, uint32_t seq_id) {
+    return submit(s, prompt, n, max_tokens, stop_token, seq_id, true);
+}
+
+// Builds the ragged batch for one forward: for each sequence the token list
+// `inputs[b]`, starting at cache position `start[b]`; reserves pages.
+static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std::vector<uint32_t>>& inputs,
+                         int last_n) {
+    const int B = (int)s->running.size();
+    s->tokens.clear();
+    s->qstarts.assign(1, 0);
+    s->ctx.clear();
+    size_t max_pages = 1;
+    for (int b = 0; b < B; ++b) {
+        PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
+        const int n = (int)inputs[b].size();
+        if (!c->reserve(c->current_position + n)) return YK_ERR_OOM;  // S/PagedKVCache.swift:31-33
+        s->tokens.insert(s->tokens.end(), inputs[b].begin(), inputs[b].end());
+        s->qstarts.push_back((uint32_t)s->tokens.size());
+        s->ctx.push_back((uint32_t)(c->current_position + n));
+        max_pages = std::max(max_pages, c->page_table.size());
+    }
+    s->tables.assign((size_t)B * max_pages, 0);
+    for (int b = 0; b < B; ++b) {
+        PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
+        std::copy(c->page_table.begin(), c->page_table.end(), s->tables.begin() + (size_t)b * max_pages);
+    }
+    int32_t rows = 0;
+    yk_status st = yk_forward_step(is_draft ? s->draft : s->target, is_draft ? s->dpool : s->tpool, s->tokens.data(),
+                                   (int32_t)s->tokens.size(), s->qstarts.data(), s->ctx.data(), B, s->tables.data(),
+                                   (int32_t)max_pages, last_n, &rows);
+    if (st != YK_OK) return st;
+    for (int b = 0; b < B; ++b) {
+        PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
+        c->current_position += (int)inputs[b].size();
+    }
+    return YK_OK;
+}
+
+// Scheduler.step, speculative branch (S/Scheduler.swift:161-267).
+extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
+    if (!s) return YK_ERR_ARG;
+    if (emitted_out) *emitted_out = 0;
+    // Admission (runLoop :122-129): move waiting requests while usage < 0.9.
+    yk_model_config tc{}, dc{};
+    YK_TRY(yk_model_get_config(s->target, &tc));
+    YK_TRY(yk_model_get_config(s->draft, &dc));
+    const int max_batch = std::min(tc.max_seqs, dc.max_seqs);
+    while (!s->waiting.empty() && s->talloc->usage() < 0.9f && s->dalloc->usage() < 0.9f &&
+           (int)s->running.size() < max_batch) {
+        s->running.push_back(std::move(s->waiting.front()));
+        s->waiting.pop_front();
+    }
+    if (s->running.empty()) return YK_OK;
+    const int B = (int)s->running.size();
+    const int k = s->k;
+    s->seq_ids.resize(B);
+    std::vector<int> N(B);
+    for (int b = 0; b < B; ++b) {
+        s->seq_ids[b] = s->running[b]->id;
+        N[b] = s->running[b]->total();
+    }
+    // 1. DRAFT PHASE (:171-190): k draft forwards, sampling after each.
+    s->drafts.assign((size_t)B * k, 0);
+    std::vector<std::vector<uint32_t>> inputs(B);
+    std::vector<uint32_t> tok(B);
+    for (int j = 0; j < k; ++j) {
+        for (int b = 0; b < B; ++b) {
+            SequenceRequest* r = s->running[b].get();
+            inputs[b].clear();
+            if (j == 0) {
+                // every token the draft cache has not seen (the prompt on the first step)
+                for (int i = r->draft_cache->current_position; i < N[b]; ++i) inputs[b].push_back(r->at(i));
+            } else {
+                inputs[b].push_back(s->drafts[(size_t)b * k + j - 1]);
+            }
+        }
+        YK_TRY(forward(s, true, inputs, 1));
+        YK_TRY(yk_draft_sample(s->sampler, s->draft, B, j, s->temperature, s->seed, s->step_no, s->seq_ids.data(),
+                               tok.data()));
+        for (int b = 0; b < B; ++b) s->drafts[(size_t)b * k + j] = tok[b];
+    }
+    // 2-3. VERIFICATION SETUP + TARGET FORWARD (:192-210): unseen tokens + drafts.
+    for (int b = 0; b < B; ++b) {
+        SequenceRequest* r = s->running[b].get();
+        inputs[b].clear();
+        for (int i = r->cache->current_position; i < N[b]; ++i) inputs[b].push_back(r->at(i));
+        for (int j = 0; j < k; ++j) inputs[b].push_back(s->drafts[(size_t)b * k + j]);
+    }
+    YK_TRY(forward(s, false, inputs, k + 1));
+    // 4. VERIFICATION & ROLLBACK (:212-267).
+    s->out_tokens.assign((size_t)B * (k + 1), 0);
+    s->counts.assign(B, 0);
+    YK_TRY(yk_spec_verify(s->sampler, s->target, B, s->temperature, s->seed, s->step_no, s->seq_ids.data(),
+                          s->drafts.data(), s->out_tokens.data(), s->counts.data()));
+    int emitted = 0;
+    for (int b = 0; b < B; ++b) {
+        SequenceRequest* r = s->running[b].get();
+        const int cnt = s->counts[b];
+        const int a = cnt - 1;  // accepted drafts
+        r->cache->rollback(N[b] + a);
+        r->draft_cache->rollback(std::min(r->draft_cache->current_position, N[b] + a));
+        for (int i = 0; i < cnt; ++i) r->generated.push_back(s->out_tokens[(size_t)b * (k + 1) + i]);
+        for (int i = 0; i < cnt; ++i)
+            if (r->stop_token >= 0 && s->out_tokens[(size_t)b * (k + 1) + i] == (uint32_t)r->stop_token) {
+                r->finished = true;
+                break;
+            }
+        if ((int)r->generated.size() >= r->max_tokens) r->finished = true;
+        emitted += cnt;
+        s->n_accepted += a;
+    }
+    s->n_emitted += emitted;
+    s->n_steps++;
+    s->step_no++;
+    // Cleanup (:141-148): finished requests release their pages.
+    for (auto it = s->running.begin(); it != s->running.end();) {
+        if ((*it)->finished) {
+            (*it)->cache->reset();
+            (*it)->draft_cache->reset();
+            s->done.push_back(std::move(*it));
+            it = s->running.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    if (emitted_out) *emitted_out = emitted;
+    return YK_OK;
+}
+
+extern "C" int32_t ykh_num_running(const ykh_scheduler* s) { return s ? (int32_t)s->running.size() : 0; }
+extern "C" int32_t ykh_num_waiting(const ykh_scheduler* s) { return s ? (int32_t)s->waiting.size() : 0; }
+
+extern "C" yk_status ykh_generated(const ykh_scheduler* s, uint32_t seq_id, uint32_t* out, int32_t cap, int32_t* n) {
+    if (!s || !n) return YK_ERR_ARG;
+    auto find = [&](const std::vector<std::unique_ptr<SequenceRequest>>& v) -> const SequenceRequest* {
+        for (auto& r : v)
+            if (r->id == seq_id) return r.get();
+        return nullptr;
+    };
+    const SequenceRequest* r = find(s->running);
+    if (!r) r = find(s->done);
+    if (!r)
+        for (auto& w : s->waiting)
+            if (w->id == seq_id) r = w.get();
+    if (!r) return YK_ERR_ARG;
+    *n = (int32_t)r->generated.size();
+    if (out) std::memcpy(out, r->generated.data(), sizeof(uint32_t) * std::min<size_t>(cap, r->generated.size()));
+    return YK_OK;
+}
+
+extern "C" yk_status ykh_counters(const ykh_scheduler* s, int64_t* steps, int64_t* emitted, int64_t* accepted) {
+    if (!s) return YK_ERR_ARG;
+    if (steps) *steps = s->n_steps;
+    if (emitted) *emitted = s->n_emitted;
+    if (accepted) *accepted = s->n_accepted;
+    return YK_OK;
+}
+
+extern "C" float ykh_usage(const ykh_scheduler* s, int32_t draft) {
+    if (!s) return 0.f;
+    return draft ? s->dalloc->usage() : s->talloc->usage();
+}
