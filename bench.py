@@ -1,0 +1,404 @@
+"""Benchmark: accepted tokens/s of the speculative draft->verify step.
+
+Workload (the benchmark spec's 8B/1B configuration): Llama-3-8B-shape target
+(32 layers, d 4096, 32/8 heads x 128, FFN 14336) with a Llama-3.2-1B-shape
+draft (16 layers, d 2048, 32/8 x 64, FFN 8192), bf16 weights N(0, 0.02), fp32
+accumulation, RoPE theta 5e5, vocab 128256, k = 5, temperature 0.8, 16-token
+KV pages; 32 sequences per GPU with prompt lengths uniform in [512, 2048]
+(random token ids), continuously batched.  Prefill is excluded: the prompts'
+KV pages are allocated and filled with synthetic N(0, 1) values, then steady-
+state speculative steps are timed.  A step = k draft forwards + k draft
+samples + one (k+1)-token target verify forward + rejection sampling + cache
+rollback, driven by libyk_host.so's Scheduler through the C-ABI.
+
+Multi-GPU: one process per GPU (torchrun), each an independent replica with
+its own 32 sequences (weak scaling, no data-path collective); the timed region
+is bracketed by barriers and the max over ranks is reported.
+
+--impl reference: the reference's CPU implementation of the same step (the
+oracle restatement, all host threads), one bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+TARGET = dict(vocab_size=128256, d_model=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336,
+              rope_theta=500000.0, rms_eps=1e-5, attn_cap=0.0, final_cap=0.0, window=0, window_layer_parity=-1,
+              act=0, ref_compat=0)
+DRAFT = dict(TARGET, d_model=2048, n_layers=16, n_heads=32, n_kv_heads=8, head_dim=64, ffn_dim=8192)
+METRIC = "accepted tokens/sec, 8B/1B-shape k=5 batch 32, at 1/2/4/8 B200; verify HBM GB/s"
+WORKLOAD = "spec-decode step: 8B-shape target + 1B-shape draft, bf16, k=5, T=0.8, 32 seqs/GPU, ctx U[512,2048]"
+
+
+def params_bytes(c: dict, es: int = 2) -> float:
+    d, dh, F, V, L = c["d_model"], c["head_dim"], c["ffn_dim"], c["vocab_size"], c["n_layers"]
+    per_layer = d * (c["n_heads"] + 2 * c["n_kv_heads"]) * dh + c["n_heads"] * dh * d + 3 * F * d
+    return float(L * per_layer + V * d) * es  # streamed weights (LM head included; embedding is a gather)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices):
+        self.devices = devices
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", ",".join(map(str, self.devices))],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (the reference's algorithm restated in C++), timed
+# on a bounded sample of one step and extrapolated layer-by-layer.
+# ---------------------------------------------------------------------------
+def _oracle_layer_model(oracle, cfg: dict, n_layers: int, vocab: int, rng):
+    c = dict(cfg, n_layers=n_layers, vocab_size=vocab)
+    d, dh, F = c["d_model"], c["head_dim"], c["ffn_dim"]
+    H, Hkv = c["n_heads"], c["n_kv_heads"]
+
+    def nrm(*s):
+        return (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))
+
+    w = dict(embed=nrm(vocab, d), lm_head=nrm(vocab, d), final_norm=np.ones(d, np.float32))
+    for name, shp in (("wq", (H * dh, d)), ("wk", (Hkv * dh, d)), ("wv", (Hkv * dh, d)), ("wo", (d, H * dh)),
+                      ("wg", (F, d)), ("wu", (F, d)), ("wd", (d, F))):
+        w[name] = [nrm(*shp) for _ in range(n_layers)]
+    w["n1"] = [np.ones(d, np.float32) for _ in range(n_layers)]
+    w["n2"] = [np.ones(d, np.float32) for _ in range(n_layers)]
+    return c, w
+
+
+def cpu_step_sample(ctx_lens, k: int, T: float, nthreads: int, seed: int = 0) -> dict:
+    """Times the oracle on: one target layer (verify shape), a 1/16 slice of the
+    target LM head, one draft layer (draft shape), a 1/16 slice of the draft LM
+    head, and the full sampler phase; returns the extrapolated step time."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_ffi as oracle
+
+    rng = np.random.default_rng(seed)
+    B = len(ctx_lens)
+    out = {}
+
+    def time_forward(cfg, n_layers, vocab, n_new, last_n):
+        c, w = _oracle_layer_model(oracle, cfg, n_layers, vocab, rng)
+        blocks = [int(np.ceil((L + n_new) / 16)) for L in ctx_lens] if n_layers else [1] * B
+        nb = int(sum(blocks))
+        om = oracle.OracleModel(c, w, max(nb, 1), nthreads=nthreads)
+        if n_layers:
+            om.pool[:] = rng.standard_normal(om.pool.size, dtype=np.float32)
+        bt = np.zeros((B, max(blocks)), np.int32)
+        nxt = 0
+        for b, n in enumerate(blocks):
+            bt[b, :n] = np.arange(nxt, nxt + n)
+            nxt += n
+        toks = rng.integers(0, vocab, B * n_new).tolist()
+        qs = list(range(0, B * n_new + 1, n_new))
+        ctx = [(L + n_new) if n_layers else n_new for L in ctx_lens]
+        t0 = time.perf_counter()
+        om.forward(toks, qs, ctx, bt, last_n=last_n)
+        return time.perf_counter() - t0
+
+    V = TARGET["vocab_size"]
+    out["target_layer_s"] = time_forward(TARGET, 1, 2, k + 1, k + 1)
+    out["target_lm_slice_s"] = time_forward(TARGET, 0, V // 16, k + 1, k + 1)
+    out["draft_layer_s"] = time_forward(DRAFT, 1, 2, 1, 1)
+    out["draft_lm_slice_s"] = time_forward(DRAFT, 0, V // 16, 1, 1)
+    # sampler phase on logits with the spread of random-init models (std 0.02 * sqrt(d) ~ 1.3)
+    dl = rng.normal(0, 1.3, (B, k, V)).astype(np.float32)
+    tl = rng.normal(0, 1.3, (B, k + 1, V)).astype(np.float32)
+    t0 = time.perf_counter()
+    _, _, cnt = oracle.spec_sample_batch(dl, tl, T, 1, 0, np.arange(B, dtype=np.uint32), nthreads)
+    out["sampler_s"] = time.perf_counter() - t0
+    out["emitted_per_step"] = float(cnt.sum())
+    step = (TARGET["n_layers"] * out["target_layer_s"] + 16 * out["target_lm_slice_s"] +
+            k * (DRAFT["n_layers"] * out["draft_layer_s"] + 16 * out["draft_lm_slice_s"]) + out["sampler_s"])
+    out["step_s"] = step
+    return out
+
+
+def cpu_baseline_dict(sample: dict, nthreads: int, emitted_per_step: float) -> dict:
+    return {
+        "value": emitted_per_step / sample["step_s"],
+        "unit": "tokens/s",
+        "cores": nthreads,
+        "kind": "port",
+        "sample": ("oracle (C++ restatement of S/SpeculativeSampler.swift, the draft sampling of "
+                   "S/Scheduler.swift and the fp32 verify forward) timed on 1 target layer at the verify shape, "
+                   "1 draft layer, 1/16 of each LM head and the full sampler phase for the same 32 sequences; "
+                   f"extrapolated to 32+5x16 layers; measured step {sample['step_s']:.1f} s"),
+    }
+
+
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def allreduce_max(world, x: float) -> float:
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allreduce_sum(world, x: float) -> float:
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def run_yk(args, world, rank, local):
+    from yanaiengine_b200 import abi
+
+    k, B, T = args.k, args.batch, args.temperature
+    eng = abi.Engine(local)
+    tcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
+    dcfg = abi.make_config(**DRAFT, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
+    rng = np.random.default_rng(7 + 1000 * rank)
+    lens = rng.integers(512, 2049, B)
+    grow = (args.warmup + 2 * args.steps + 4) * (k + 1) + 32
+    blocks = int(sum(np.ceil((lens + grow) / 16))) + 64
+    target = abi.Model(eng, tcfg, seed=1, init_std=0.02)
+    draft = abi.Model(eng, dcfg, seed=2, init_std=0.02)
+    tpool = abi.KVPool(eng, tcfg, blocks)
+    dpool = abi.KVPool(eng, dcfg, blocks)
+    tpool.fill_random(11, 1.0)
+    dpool.fill_random(12, 1.0)
+    sampler = abi.Sampler(eng, B, k, TARGET["vocab_size"])
+    sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + rank)
+    for i, L in enumerate(lens):
+        sch.submit(rng.integers(0, TARGET["vocab_size"], int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
+                   seq_id=rank * B + i, cached=True)
+    for _ in range(args.warmup):
+        sch.step()
+    eng.sync()
+
+    import torch
+
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.5)
+    _, em0, acc0 = sch.counters()
+    launches0 = eng.launches()
+    h2d = d2h = 0
+    barrier(world)
+    eng.sync()
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        n_running = sch.running()
+        # per-step host traffic through the C-ABI: token ids, positions, page tables in; tokens out
+        sch.step()
+        h2d += n_running * (2 * (k + 1) + 8) * 4 * (k + 1)
+        d2h += n_running * (k + 2) * 4 * (k + 1)
+    ev1.record(stream)
+    eng.sync()
+    wall = time.perf_counter() - t0
+    barrier(world)
+    dev_ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop() if rank == 0 else None
+    _, em1, acc1 = sch.counters()
+    emitted = em1 - em0
+    launches = eng.launches() - launches0
+    max_dev_s = allreduce_max(world, dev_ms / 1e3)
+    max_wall = allreduce_max(world, wall)
+    tot_emitted = allreduce_sum(world, float(emitted))
+
+    # kernel roofline: a second pass of the same steps with per-launch CUDA events
+    eng.profile(True)
+    for _ in range(max(1, min(args.steps, 4))):
+        sch.step()
+    gemm = eng.profile_read(0)
+    attn = eng.profile_read(1)
+    eng.profile(False)
+
+    peaks = measured_peaks()
+    res = None
+    if rank == 0:
+        gemm_gbs = gemm["bytes"] / (gemm["ms"] / 1e3) / 1e9 if gemm["ms"] > 0 else 0.0
+        attn_gbs = attn["bytes"] / (attn["ms"] / 1e3) / 1e9 if attn["ms"] > 0 else 0.0
+        step_ms = max_dev_s * 1e3 / args.steps
+        res = {
+            "metric": METRIC,
+            "value": tot_emitted / max_dev_s,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: random-init weights N(0,0.02), random token ids, synthetic N(0,1) KV context",
+            "config": {"workload": WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B, "k": k,
+                       "temperature": T, "ctx": "U[512,2048] + growth", "parallelism": f"dp{world} (replicas)",
+                       "l2": "inputs larger than L2 (17.5 GB of weights streamed per step)"},
+            "e2e": {"value": tot_emitted / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d / args.steps),
+                    "d2h_bytes_per_step": int(d2h / args.steps)},
+            "gpu_launches": int(launches),
+            "accept_rate": float((acc1 - acc0) / max(1, args.steps * B * k)),
+            "emitted_per_step": float(emitted / args.steps),
+            "roofline": {"bound": "hbm", "achieved": gemm_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gemm_gbs / peaks["hbm_gbs"], "traffic": None, "kernel": "gemm_tc_kernel",
+                         "peak_src": peaks["src"],
+                         "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])},
+            "attention": {"achieved_gbs": attn_gbs, "frac": attn_gbs / peaks["hbm_gbs"], "launches": attn["launches"]},
+            "clocks": clk,
+        }
+    sch.close()
+    sampler.close()
+    dpool.close()
+    tpool.close()
+    draft.close()
+    target.close()
+    eng.close()
+    return res, lens
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="yk", choices=["yk", "reference"])
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--k", type=int, default=5)
+    ap.add_argument("--temperature", type=float, default=0.8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    nthreads = os.cpu_count() or 1
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        lens = np.random.default_rng(7).integers(512, 2049, args.batch)
+        for _ in range(args.warmup):
+            pass  # the CPU path has no warm-up state worth priming beyond the first sample
+        samples = [cpu_step_sample(lens, args.k, args.temperature, nthreads, seed=s) for s in range(args.steps)]
+        step_s = float(np.mean([s["step_s"] for s in samples]))
+        emitted = float(np.mean([s["emitted_per_step"] for s in samples]))
+        val = emitted / step_s
+        cb = cpu_baseline_dict(samples[0], nthreads, emitted)
+        cb["value"] = val
+        print(json.dumps({
+            "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": args.batch, "k": args.k,
+                       "temperature": args.temperature},
+            "cpu_baseline": cb,
+            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    res, lens = run_yk(args, world, rank, local)
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            sample = cpu_step_sample(lens, args.k, args.temperature, nthreads)
+            res["cpu_baseline"] = cpu_baseline_dict(sample, nthreads, sample["emitted_per_step"])
+        print(json.dumps(res))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -115,6 +115,17 @@ yk_status yk_engine_sync(yk_engine* e);
 yk_status yk_engine_device_error(yk_engine* e, uint32_t* code);
 /* Number of kernels this engine has launched (all of this module's kernels). */
 uint64_t  yk_engine_launch_count(yk_engine* e);
+/* Kernel timing: while enabled, every launch of the classes below is bracketed
+ * by CUDA events on the engine stream and its algorithmic bytes / flops are
+ * accumulated.  Class 0 = tcgen05/SIMT GEMM, 1 = paged attention, 2 = sampler,
+ * 3 = other (embedding, RMSNorm).  Reading resolves pending events (syncs). */
+#define YK_PROF_GEMM    0
+#define YK_PROF_ATTN    1
+#define YK_PROF_SAMPLER 2
+#define YK_PROF_OTHER   3
+yk_status yk_engine_profile(yk_engine* e, int32_t enable);
+yk_status yk_engine_profile_read(yk_engine* e, int32_t kernel_class, double* total_ms, double* total_bytes,
+                                 double* total_flops, int64_t* launches);
 
 /* ---- model: LlamaModel / GemmaModel weights + forward workspaces. -------- */
 /* Random init on the device: matrices N(0, init_std) from Philox(seed), norms 1

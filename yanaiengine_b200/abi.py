@@ -66,6 +66,9 @@ _PROTOS = {
     "yk_engine_sync": (C.c_int32, [_P]),
     "yk_engine_device_error": (C.c_int32, [_P, _U32P]),
     "yk_engine_launch_count": (C.c_uint64, [_P]),
+    "yk_engine_profile": (C.c_int32, [_P, C.c_int32]),
+    "yk_engine_profile_read": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                           C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
     "yk_model_create": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_uint64, C.c_float, C.POINTER(_P)]),
     "yk_model_destroy": (None, [_P]),
     "yk_model_get_config": (C.c_int32, [_P, C.POINTER(ModelConfig)]),
@@ -216,6 +219,14 @@ class Engine:
 
     def launches(self) -> int:
         return int(lib().yk_engine_launch_count(self.h))
+
+    def profile(self, enable: bool):
+        check(lib().yk_engine_profile(self.h, 1 if enable else 0))
+
+    def profile_read(self, cls: int) -> dict:
+        ms, b, f, n = C.c_double(), C.c_double(), C.c_double(), C.c_int64()
+        check(lib().yk_engine_profile_read(self.h, cls, C.byref(ms), C.byref(b), C.byref(f), C.byref(n)))
+        return {"ms": ms.value, "bytes": b.value, "flops": f.value, "launches": n.value}
 
     def close(self):
         if self.h:

@@ -106,6 +106,61 @@ extern "C" yk_status yk_engine_device_error(yk_engine* e, uint32_t* code) {
 
 extern "C" uint64_t yk_engine_launch_count(yk_engine* e) { return e ? e->launches : 0; }
 
+void yk_engine::prof_begin(int cls, double bytes, double flops) {
+    ProfRecord r{cls, nullptr, nullptr, bytes, flops};
+    for (cudaEvent_t* ev : {&r.start, &r.stop}) {
+        if (!prof_free.empty()) {
+            *ev = prof_free.back();
+            prof_free.pop_back();
+        } else {
+            cudaEventCreate(ev);
+        }
+    }
+    cudaEventRecord(r.start, stream);
+    prof_pending.push_back(r);
+}
+
+void yk_engine::prof_end() {
+    if (!prof_pending.empty()) cudaEventRecord(prof_pending.back().stop, stream);
+}
+
+void yk_engine::prof_resolve() {
+    cudaStreamSynchronize(stream);
+    for (auto& r : prof_pending) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, r.start, r.stop);
+        ProfTotals& t = prof[r.cls & 3];
+        t.ms += ms;
+        t.bytes += r.bytes;
+        t.flops += r.flops;
+        t.launches++;
+        prof_free.push_back(r.start);
+        prof_free.push_back(r.stop);
+    }
+    prof_pending.clear();
+}
+
+extern "C" yk_status yk_engine_profile(yk_engine* e, int32_t enable) {
+    YK_ARG(e, "null handle");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    e->prof_resolve();
+    for (auto& t : e->prof) t = ProfTotals{};
+    e->profiling = enable != 0;
+    return YK_OK;
+}
+
+extern "C" yk_status yk_engine_profile_read(yk_engine* e, int32_t cls, double* ms, double* bytes, double* flops,
+                                            int64_t* launches) {
+    YK_ARG(e && cls >= 0 && cls < 4, "arguments");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    e->prof_resolve();
+    if (ms) *ms = e->prof[cls].ms;
+    if (bytes) *bytes = e->prof[cls].bytes;
+    if (flops) *flops = e->prof[cls].flops;
+    if (launches) *launches = e->prof[cls].launches;
+    return YK_OK;
+}
+
 // ---------------------------------------------------------------------------
 // model
 // ---------------------------------------------------------------------------
@@ -482,6 +537,15 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
 
     using namespace yk;
     const int d = c.d_model, dh = c.head_dim, qd = c.n_heads * dh, kvd = c.n_kv_heads * dh, F = c.ffn_dim;
+    // Algorithmic KV bytes one attention launch must read: every cached key/value
+    // of each sequence once (windowed layers: at most window + new tokens).
+    double kv_full = 0, kv_win = 0;
+    for (int b = 0; b < B; ++b) {
+        const double n = (double)(q_starts[b + 1] - q_starts[b]);
+        kv_full += (double)ctx[b];
+        kv_win += c.window > 0 ? std::min((double)ctx[b], (double)c.window + n - 1) : (double)ctx[b];
+    }
+    const double kv_tok_bytes = 2.0 * kvd * (double)m->esize;
     YK_TRY(launch_embed(m, m->cur.tokens, T));
     for (int l = 0; l < c.n_layers; ++l) {
         LayerWeights& L = m->layers[l];
@@ -502,7 +566,8 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         eq.layer_off = (long long)l * (long long)pool->layer_elems;
         eq.pool_blocks = pool->num_blocks;
         YK_TRY(gemm_run(m, L.wqkv, &L.tm_qkv, m->xn, qd + 2 * kvd, d, T, eq));
-        YK_TRY(attention_run(m, pool, l, T, B, max_blocks));
+        const bool windowed = c.window > 0 && (c.window_layer_parity < 0 || (l % 2) == c.window_layer_parity);
+        YK_TRY(attention_run(m, pool, l, T, B, max_blocks, (windowed ? kv_win : kv_full) * kv_tok_bytes));
         EpiParams er;
         er.kind = EPI_RESID;
         er.ref_compat = c.ref_compat;

@@ -113,9 +113,11 @@ static void launch_simt(const AttnParams& p, cudaStream_t st) {
     }
 }
 
-yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks) {
+yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks, double kv_bytes) {
     (void)B;
     const auto& c = m->cfg;
+    const double es = c.dtype == YK_DTYPE_BF16 ? 2.0 : 4.0;
+    ProfScope prof(m->e, YK_PROF_ATTN, kv_bytes + 2.0 * T * c.n_heads * c.head_dim * es, 0.0);
     AttnParams p;
     p.q = m->q;
     p.out = m->att;

@@ -300,6 +300,13 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     ep.m_tok = m_tok;
     ep.err = e->d_err;
     YK_ARG(n_out % 2 == 0 && m_tok > 0 && m_tok <= m->cfg.max_tokens, "gemm shape");
+    // Algorithmic traffic of this launch: weights + activations once, plus the epilogue's outputs.
+    const double es = m->cfg.dtype == YK_DTYPE_BF16 ? 2.0 : 4.0;
+    double out_bytes = (double)m_tok * n_out * 4.0;
+    if (ep.kind == EPI_QKV) out_bytes = (double)m_tok * n_out * es;
+    else if (ep.kind == EPI_RESID) out_bytes = (double)m_tok * n_out * 8.0;
+    else if (ep.kind == EPI_GLU) out_bytes = (double)m_tok * (n_out / 2) * es;
+    ProfScope prof(e, YK_PROF_GEMM, ((double)n_out + m_tok) * K * es + out_bytes, 2.0 * n_out * K * m_tok);
     if (m->cfg.dtype == YK_DTYPE_F32) {
         dim3 grid((n_out + 15) / 16, (m_tok + 7) / 8);
         gemm_simt_kernel<float, float><<<grid, 256, 0, e->stream>>>((const float*)W, (const float*)X, n_out, K, m_tok, ep);

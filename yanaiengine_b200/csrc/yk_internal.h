@@ -39,6 +39,17 @@ typedef CUresult (*PFN_tmapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuin
                                         CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
                                         CUtensorMapFloatOOBfill);
 
+// Per-kernel-class timing with CUDA events on the engine stream (yk_engine_profile).
+struct ProfRecord {
+    int cls;
+    cudaEvent_t start, stop;
+    double bytes, flops;
+};
+struct ProfTotals {
+    double ms = 0, bytes = 0, flops = 0;
+    int64_t launches = 0;
+};
+
 struct yk_engine {
     int device = 0;
     int num_sms = 148;
@@ -48,7 +59,25 @@ struct yk_engine {
     size_t pinned_bytes = 0;
     uint64_t launches = 0;
     PFN_tmapEncodeTiled encode_tiled = nullptr;
+    bool profiling = false;
+    std::vector<ProfRecord> prof_pending;
+    std::vector<cudaEvent_t> prof_free;
+    ProfTotals prof[4];
     yk_status ensure_pinned(size_t bytes);
+    void prof_begin(int cls, double bytes, double flops);
+    void prof_end();
+    void prof_resolve();
+};
+
+// RAII bracket for one profiled launch.
+struct ProfScope {
+    yk_engine* e;
+    ProfScope(yk_engine* e_, int cls, double bytes, double flops) : e(e_) {
+        if (e->profiling) e->prof_begin(cls, bytes, flops);
+    }
+    ~ProfScope() {
+        if (e->profiling) e->prof_end();
+    }
 };
 
 // Element counts of the device workspaces.
@@ -154,7 +183,8 @@ struct EpiParams {
 yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const void* X, int n_out, int K, int m_tok,
                    const EpiParams& ep, int force_splits = 0);
 yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
-yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks);
+yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks,
+                        double kv_bytes);
 yk_status launch_embed(yk_model* m, const int32_t* tokens, int T);
 yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx);
 yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed, uint32_t stream, float std,
