@@ -18,6 +18,7 @@ SHAPES = [
     (6144, 4096, 192, 0),    # verify QKV shape, heuristic split
     (4096, 14336, 32, 0),    # down-proj shape at draft batch
     (512, 256, 300, 1),      # two token tiles (BN = 256)
+    (28672, 4096, 192, 0),   # verify gate/up shape: 235 MB of weights (> L2), the profiling case
 ]
 
 

@@ -295,6 +295,7 @@ extern "C" void yk_model_destroy(yk_model* m) {
     cudaStreamSynchronize(m->e->stream);
     for (void* p : m->allocations) cudaFree(p);
     if (m->meta) cudaFree(m->meta);
+    if (m->attn_ws) cudaFree(m->attn_ws);
     delete m;
 }
 
@@ -488,7 +489,25 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
     for (int t = 0; t < T; ++t) YK_ARG(tokens[t] < (uint32_t)c.vocab_size, "token id >= vocab_size");
     YK_ARG(R > 0, "no logit rows");
     YK_CHECK_CUDA(cudaSetDevice(e->device));
-    const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R;
+    // Attention work lists (bf16 tensor-core path): global and windowed layers.
+    static thread_local std::vector<int32_t> it_g, cb_g, it_w, cb_w;
+    int slots_g = 0, slots_w = 0;
+    it_g.clear(); cb_g.clear(); it_w.clear(); cb_w.clear();
+    if (c.dtype == YK_DTYPE_BF16) {
+        yk::plan_attention(c, e->num_sms, q_starts, ctx, B, false, it_g, cb_g, &slots_g);
+        if (c.window > 0) yk::plan_attention(c, e->num_sms, q_starts, ctx, B, true, it_w, cb_w, &slots_w);
+        const size_t need = (size_t)std::max(slots_g, slots_w) * yk::attention_ws_floats_per_slot(c.head_dim);
+        if (need > m->attn_ws_floats) {
+            YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+            if (m->attn_ws) cudaFree(m->attn_ws);
+            m->attn_ws = nullptr;
+            m->attn_ws_floats = 0;
+            YK_CHECK_CUDA(cudaMalloc(&m->attn_ws, need * 2 * 4));
+            m->attn_ws_floats = need * 2;
+        }
+    }
+    const size_t nattn = it_g.size() + cb_g.size() + it_w.size() + cb_w.size();
+    const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R + nattn;
     YK_TRY(e->ensure_pinned(nmeta * 4));
     YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));  // staging buffer is free again
     if (nmeta > m->meta_cap) {
@@ -524,7 +543,30 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         for (int i = n - take; i < n; ++i) h_rows[r++] = (int)q_starts[b] + i;
     }
     std::memcpy(h_bt, block_tables, (size_t)B * max_blocks * 4);
+    int32_t* h_attn = h_rows + R;
+    const size_t attn_off = (size_t)(h_attn - hm);
+    {
+        int32_t* w = h_attn;
+        for (auto* v : {&it_g, &cb_g, &it_w, &cb_w}) {
+            if (!v->empty()) std::memcpy(w, v->data(), v->size() * 4);
+            w += v->size();
+        }
+    }
     YK_CHECK_CUDA(cudaMemcpyAsync(m->meta, hm, nmeta * 4, cudaMemcpyHostToDevice, e->stream));
+    {
+        const int32_t* a = m->meta + attn_off;
+        m->cur.attn_items[0] = a;
+        m->cur.n_items[0] = (int)(it_g.size() / 6);
+        a += it_g.size();
+        m->cur.attn_comb[0] = a;
+        m->cur.n_comb[0] = (int)(cb_g.size() / 5);
+        a += cb_g.size();
+        m->cur.attn_items[1] = a;
+        m->cur.n_items[1] = (int)(it_w.size() / 6);
+        a += it_w.size();
+        m->cur.attn_comb[1] = a;
+        m->cur.n_comb[1] = (int)(cb_w.size() / 5);
+    }
     const int32_t* dm = m->meta;
     m->cur.tokens = dm;
     m->cur.pos = dm + T;

@@ -97,4 +97,29 @@ __device__ __forceinline__ void epi_pair(const EpiParams& p, int n, int j, float
     }
 }
 
+// NB consecutive tokens j0.. of one row pair.  The residual epilogue issues all
+// its loads of the fp32 stream before any store, so a warp keeps NB
+// read-modify-writes in flight instead of one.
+template <typename AT, int NB>
+__device__ __forceinline__ void epi_batch(const EpiParams& p, int n, int j0, const float (&v0)[NB],
+                                          const float (&v1)[NB]) {
+    if (p.kind == EPI_RESID) {
+        if (n >= p.n_out) return;
+        float2 hv[NB];
+#pragma unroll
+        for (int i = 0; i < NB; ++i)
+            if (j0 + i < p.m_tok) hv[i] = *reinterpret_cast<const float2*>(p.h + (size_t)(j0 + i) * p.ld + n);
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+            if (j0 + i >= p.m_tok) continue;
+            float a = v0[i], b = v1[i];
+            if (p.ref_compat) { a = compat_relu(a); b = compat_relu(b); }
+            *reinterpret_cast<float2*>(p.h + (size_t)(j0 + i) * p.ld + n) = make_float2(hv[i].x + a, hv[i].y + b);
+        }
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < NB; ++i) epi_pair<AT>(p, n, j0 + i, v0[i], v1[i]);
+}
+
 }  // namespace yk

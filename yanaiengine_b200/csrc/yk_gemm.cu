@@ -139,54 +139,69 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int j_base = tn * BN;
     const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
 
-    if (!aborted) {
-        if (a.splits == 1) {
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld16(t_lane + (uint32_t)c, r);
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj) {
-                    const float v = __uint_as_float(r[jj]);
-                    const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-                    if ((lane & 1) == 0) epi_pair<__nv_bfloat16>(a.epi, n_base + row, j_base + c + jj, v, partner);
-                }
-            }
-        } else {
-            float* part = a.ws + (size_t)unit * TC_BM * BN;
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld16(t_lane + (uint32_t)c, r);
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj) __stcg(part + (size_t)(c + jj) * TC_BM + row, __uint_as_float(r[jj]));
-            }
-            __threadfence();
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                const uint32_t prev = atomicAdd(&a.counters[tile], 1u);
-                flags[1] = (prev == (uint32_t)(a.splits - 1)) ? 1 : 0;
-            }
-            __syncthreads();
-            if (flags[1]) {
-                __threadfence();
-                const float* base = a.ws + (size_t)tile * a.splits * TC_BM * BN;
-                for (int c = 0; c < BN; ++c) {
-                    float v = 0.f;
-                    for (int sp = 0; sp < a.splits; ++sp)
-                        v += __ldcg(base + (size_t)sp * TC_BM * BN + (size_t)c * TC_BM + row);
-                    const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-                    if ((lane & 1) == 0) epi_pair<__nv_bfloat16>(a.epi, n_base + row, j_base + c, v, partner);
-                }
-                if (threadIdx.x == 0) a.counters[tile] = 0u;
-            }
-        }
-    }
-
-    // ---------------- teardown ----------------
     if (threadIdx.x == 0 && aborted) {
-        // Let every TMA copy this CTA issued land before shared memory is released.
+        // Let every TMA copy this CTA issued land before the stage buffers are reused.
         for (int s = 0; s < S && s < 8; ++s)
             if (issued_round[s] >= 0) (void)mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)(issued_round[s] & 1));
     }
+    __syncthreads();
+    // Accumulator -> shared memory [BN][128] fp32 (the stage buffers are free now:
+    // every TMA load was consumed and every MMA completed before accb fired).
+    float* red = reinterpret_cast<float*>(smem);
+    if (!aborted) {
+        for (int c = 0; c < BN; c += 16) {
+            uint32_t r[16];
+            tmem_ld16(t_lane + (uint32_t)c, r);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) red[(c + jj) * TC_BM + row] = __uint_as_float(r[jj]);
+        }
+    } else {
+        for (int c = 0; c < BN; ++c) red[c * TC_BM + row] = 0.f;
+    }
+    // Split-K: the `splits` CTAs of a tile form one cluster.  After the barrier
+    // each CTA reduces its share of the tile's columns over every CTA's partial
+    // through distributed shared memory, always in rank order (deterministic),
+    // and runs the epilogue for those columns.
+    const int S_k = a.splits;
+    const uint32_t rank = S_k > 1 ? cluster_ctarank() : 0u;
+    if (S_k > 1) cluster_sync_all(); else __syncthreads();
+    const int c0 = (int)((rank * (uint32_t)BN) / (uint32_t)S_k);
+    const int c1 = (int)(((rank + 1) * (uint32_t)BN) / (uint32_t)S_k);
+    const uint32_t red_addr = smem_u32(red);
+    constexpr int NB = 8;
+    for (int c = c0; c < c1; c += NB) {
+        float v[NB], w[NB];
+#pragma unroll
+        for (int i = 0; i < NB; ++i) v[i] = 0.f;
+        if (S_k == 1) {
+#pragma unroll
+            for (int i = 0; i < NB; ++i)
+                if (c + i < c1) v[i] = red[(c + i) * TC_BM + row];
+        } else {
+            for (int sp = 0; sp < S_k; ++sp) {
+                const uint32_t base = mapa_shared(red_addr, (uint32_t)sp);
+                float t[NB];
+#pragma unroll
+                for (int i = 0; i < NB; ++i)
+                    t[i] = (c + i < c1) ? ld_shared_cluster_f32(base + (uint32_t)(((c + i) * TC_BM + row) * 4)) : 0.f;
+#pragma unroll
+                for (int i = 0; i < NB; ++i) v[i] += t[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < NB; ++i) w[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
+        if (!aborted && (lane & 1) == 0) {
+            if (c + NB <= c1) {
+                epi_batch<__nv_bfloat16, NB>(a.epi, n_base + row, j_base + c, v, w);
+            } else {
+                for (int i = 0; i < c1 - c; ++i) epi_pair<__nv_bfloat16>(a.epi, n_base + row, j_base + c + i, v[i], w[i]);
+            }
+        }
+    }
+    // No CTA may leave while a peer still reads its shared memory.
+    if (S_k > 1) cluster_sync_all();
+
+    // ---------------- teardown ----------------
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -278,15 +293,43 @@ static yk_status get_x_map(yk_model* m, const void* X, int K, int BN, const CUte
     return YK_OK;
 }
 
-// Split-K choice: minimise (waves x k-blocks per unit + fixed per-unit cost).
-static int choose_splits(int tiles, int kb, int sms, size_t ws_cap_units) {
+// How many clusters of `s` GEMM CTAs (one CTA per SM) the device runs at once.
+static int cluster_capacity(yk_engine* e, int s) {
+    static int cap[9] = {0};
+    static int dev = -1;
+    if (dev != e->device) {
+        for (int i = 0; i < 9; ++i) cap[i] = 0;
+        dev = e->device;
+    }
+    if (cap[s] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(s * 64);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = TC_SMEM_BUDGET + 1280;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = s;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = std::max(1, e->num_sms / s / 2);
+        }
+        cap[s] = n;
+    }
+    return cap[s];
+}
+
+// Split-K choice (cluster size): minimise waves x (k-blocks per CTA + fixed cost).
+static int choose_splits(yk_engine* e, int tiles, int kb) {
     int best = 1;
     double best_cost = 1e30;
-    for (int s = 1; s <= std::min(kb, 32); ++s) {
-        if (s > 1 && (size_t)tiles * s > ws_cap_units) break;
-        const int units = tiles * s;
-        const int waves = (units + sms - 1) / sms;
-        const double cost = waves * ((double)((kb + s - 1) / s) + 3.0 + (s > 1 ? 2.0 : 0.0));
+    for (int s = 1; s <= std::min(kb, 8); ++s) {
+        const int waves = (tiles + cluster_capacity(e, s) - 1) / cluster_capacity(e, s);
+        const double cost = waves * ((double)((kb + s - 1) / s) + 3.0 + (s > 1 ? 1.0 : 0.0));
         if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
     }
     return best;
@@ -320,15 +363,17 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     const int tiles_m = (n_out + TC_BM - 1) / TC_BM;
     const int kb = (K + TC_BK - 1) / TC_BK;
     const int tiles = tiles_m * tiles_n;
-    const size_t unit_floats = (size_t)TC_BM * BN;
-    const size_t cap_units = std::min(m->gemm_ws_floats / unit_floats, (size_t)m->gemm_counter_cap * 32);
-    int splits = choose_splits(tiles, kb, e->num_sms, cap_units);
+    static bool attr_set = false;
+    if (!attr_set) {
+        YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           TC_SMEM_BUDGET + 16384 + 2048));
+        attr_set = true;
+    }
+    int splits = choose_splits(e, tiles, kb);
     if (force_splits > 0) {
-        YK_ARG(force_splits <= kb && (force_splits == 1 || (size_t)tiles * force_splits <= cap_units),
-               "forced split count");
+        YK_ARG(force_splits <= kb && force_splits <= 8, "forced split count must be <= min(k-blocks, 8)");
         splits = force_splits;
     }
-    if (splits > 1 && tiles > m->gemm_counter_cap) splits = 1;
     const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
     int stages = std::min(8, (int)(TC_SMEM_BUDGET / stage_bytes));
     stages = std::max(2, std::min(stages, std::max(2, kb)));
@@ -347,15 +392,20 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     a.ws = m->gemm_ws;
     a.counters = m->gemm_counters;
     a.epi = ep;
-    static bool attr_set = false;
-    if (!attr_set) {
-        YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           TC_SMEM_BUDGET + 16384 + 2048));
-        attr_set = true;
-    }
-    gemm_tc_kernel<<<tiles * splits, TC_THREADS, smem, e->stream>>>(*tmW, *tmX, a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles * splits);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = e->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = splits;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel, *tmW, *tmX, a));
     e->launches++;
-    YK_CHECK_CUDA(cudaGetLastError());
     return YK_OK;
 }
 

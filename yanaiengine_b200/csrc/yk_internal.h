@@ -115,6 +115,9 @@ struct yk_model {
     int32_t last_rows = 0;
     struct {
         const int32_t *tokens, *pos, *slot, *seq, *q_starts, *ctx, *bt, *rows;
+        const int32_t* attn_items[2];  // [0] global layers, [1] windowed layers
+        const int32_t* attn_comb[2];
+        int n_items[2], n_comb[2];
     } cur{};
     // split-K partials + per-tile arrival counters
     float* gemm_ws = nullptr;
@@ -185,6 +188,9 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
 yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
 yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks,
                         double kv_bytes);
+void plan_attention(const yk_model_config& c, int num_sms, const uint32_t* q_starts, const uint32_t* ctx, int B,
+                    bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots);
+size_t attention_ws_floats_per_slot(int head_dim);
 yk_status launch_embed(yk_model* m, const int32_t* tokens, int T);
 yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx);
 yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed, uint32_t stream, float std,
