@@ -1,7 +1,7 @@
 /*
  * yk_testing.h -- test hooks of libyk.so.  Not part of the reference-facing
  * boundary (no reference counterpart): they run one internal kernel in
- * isolation so GPU tests can localise a failure.
+ * isolation so GPU tests can localise a failure and time a kernel alone.
  */
 #pragma once
 #include <stdint.h>
@@ -13,10 +13,18 @@ extern "C" {
 #endif
 
 /* Y[m_tok x n_out] (fp32, host) = X[m_tok x K] * W[n_out x K]^T through the
- * tcgen05 GEMM; W and X are host bf16 bit patterns.  splits > 0 forces the
- * split-K factor (0 = the heuristic). */
+ * tcgen05 GEMM; W and X are host bf16 bit patterns.  grid: 0 = the production
+ * heuristic; > 0 = stream-K over that many persistent CTAs (moves where tiles
+ * are cut); < 0 = cluster split-K with -grid CTAs per tile. */
 yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K, int32_t m_tok,
-                        int32_t splits, float* Y);
+                        int32_t grid, float* Y);
+/* Same, then `reps` back-to-back launches timed with CUDA events
+ * (*ms_per_rep); stamps (grid x 8, may be null) receives the last launch's
+ * per-CTA %globaltimer phase stamps: start, first TMA issued, first stage
+ * landed, last MMA issued, last accumulator ready, epilogue done, segments. */
+yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K,
+                              int32_t m_tok, int32_t grid, int32_t reps, float* Y, float* ms_per_rep,
+                              uint64_t* stamps, int32_t* grid_used);
 
 #ifdef __cplusplus
 }

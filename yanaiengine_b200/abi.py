@@ -97,6 +97,9 @@ _PROTOS = {
     # include/yk_testing.h
     "ykt_gemm_bf16": (C.c_int32, [_P, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int32, C.c_int32,
                                   C.c_int32, C.c_int32, _F32P]),
+    "ykt_gemm_bf16_timed": (C.c_int32, [_P, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int32, C.c_int32,
+                                        C.c_int32, C.c_int32, C.c_int32, _F32P, _F32P, C.POINTER(C.c_uint64),
+                                        _I32P]),
 }
 
 _HOST_PROTOS = {
@@ -183,16 +186,32 @@ def bf16_value(bits: np.ndarray) -> np.ndarray:
     return (bits.astype(np.uint32) << 16).view(np.float32)
 
 
-def gemm_bf16_test(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, splits: int = 0) -> np.ndarray:
+def gemm_bf16_test(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, grid: int = 0) -> np.ndarray:
     """Y = X W^T through the tcgen05 GEMM (test hook of include/yk_testing.h)."""
     n_out, K = W_bits.shape
     m_tok = X_bits.shape[0]
     W_bits = np.ascontiguousarray(W_bits, dtype=np.uint16)
     X_bits = np.ascontiguousarray(X_bits, dtype=np.uint16)
     Y = np.zeros((m_tok, n_out), np.float32)
-    check(lib().ykt_gemm_bf16(engine.h, ptr(W_bits, C.c_uint16), ptr(X_bits, C.c_uint16), n_out, K, m_tok, splits,
+    check(lib().ykt_gemm_bf16(engine.h, ptr(W_bits, C.c_uint16), ptr(X_bits, C.c_uint16), n_out, K, m_tok, grid,
                               ptr(Y, C.c_float)))
     return Y
+
+
+def gemm_bf16_timed(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, grid: int = 0, reps: int = 10):
+    """(Y, ms per launch, per-CTA phase stamps [grid x 8], grid used) of the tcgen05 GEMM test hook."""
+    n_out, K = W_bits.shape
+    m_tok = X_bits.shape[0]
+    W_bits = np.ascontiguousarray(W_bits, dtype=np.uint16)
+    X_bits = np.ascontiguousarray(X_bits, dtype=np.uint16)
+    Y = np.zeros((m_tok, n_out), np.float32)
+    ms = C.c_float()
+    cap = max(4096, grid, 8 * ((n_out + 127) // 128) * ((m_tok + 255) // 256))  # >= any grid the hook uses
+    st = np.zeros((cap, 8), np.uint64)
+    g = C.c_int32()
+    check(lib().ykt_gemm_bf16_timed(engine.h, ptr(W_bits, C.c_uint16), ptr(X_bits, C.c_uint16), n_out, K, m_tok,
+                                    grid, reps, ptr(Y, C.c_float), C.byref(ms), ptr(st, C.c_uint64), C.byref(g)))
+    return Y, ms.value, st[: g.value], g.value
 
 
 # ---------------------------------------------------------------------------

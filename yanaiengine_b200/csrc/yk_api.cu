@@ -190,7 +190,7 @@ static yk_status dalloc(yk_model* m, void** p, size_t bytes) {
 
 static yk_status validate_cfg(const yk_model_config* c) {
     YK_ARG(c, "config is null");
-    YK_ARG(c->vocab_size > 0 && c->vocab_size % 2 == 0, "vocab_size must be positive and even");
+    YK_ARG(c->vocab_size > 0 && c->vocab_size % 4 == 0, "vocab_size must be a positive multiple of 4");
     YK_ARG(c->d_model > 0 && c->d_model % 8 == 0, "d_model must be a positive multiple of 8");
     YK_ARG(c->n_layers > 0 && c->n_heads > 0 && c->n_kv_heads > 0 && c->n_heads % c->n_kv_heads == 0,
            "n_heads must be a positive multiple of n_kv_heads");
@@ -245,7 +245,11 @@ extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, u
     m->gemm_ws_floats = (size_t)2 * e->num_sms * 128 * 256;
     ALLOC(m->gemm_ws, m->gemm_ws_floats * 4);
     m->gemm_counter_cap = 4096;
-    ALLOC(m->gemm_counters, (size_t)m->gemm_counter_cap * 4);
+    if (cudaMalloc(&m->gemm_counters, (size_t)m->gemm_counter_cap * 4) != cudaSuccess) {  // may grow: owned apart
+        m->gemm_counters = nullptr;
+        yk_set_error("cudaMalloc(gemm counters) failed");
+        return fail(YK_ERR_OOM);
+    }
 #undef ALLOC
     if (cudaMemsetAsync(m->gemm_counters, 0, (size_t)m->gemm_counter_cap * 4, e->stream) != cudaSuccess ||
         cudaMemsetAsync(m->xn, 0, T * d * es, e->stream) != cudaSuccess ||
@@ -296,6 +300,7 @@ extern "C" void yk_model_destroy(yk_model* m) {
     for (void* p : m->allocations) cudaFree(p);
     if (m->meta) cudaFree(m->meta);
     if (m->attn_ws) cudaFree(m->attn_ws);
+    if (m->gemm_counters) cudaFree(m->gemm_counters);
     delete m;
 }
 

@@ -196,6 +196,18 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
 }
+__device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+// Cluster barrier that warps may reach divergently (no .aligned).
+__device__ __forceinline__ void cluster_sync_any() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
 
 // Shared-memory matrix descriptor, K-major operand tile written by TMA with
 // 128-byte swizzle: rows of 128 B, 8-row swizzle atoms of 1024 B stacked

@@ -1,5 +1,5 @@
 // yk_epilogue.cuh -- fused GEMM epilogues, shared by the tcgen05 and SIMT GEMMs.
-// Each call handles an adjacent output-row pair (n, n+1), n even, for token j:
+// Row n = output feature, column j = token:
 //   EPI_QKV    RoPE on (2p, 2p+1) pairs of Q and K (S/gemm.metal:674-682,704-713);
 //              Q -> q buffer, K/V -> their KV-pool page slot (replaces the CPU
 //              PagedKVCache.appendFromFull, S/PagedKVCache.swift:24-62).
@@ -7,7 +7,10 @@
 //   EPI_GLU    silu(gate)*up or gelu_tanh(gate)*up (S/LlamaBlock.swift:262-268,
 //              S/GemmaBlock.swift:135-146); rows are interleaved gate/up.
 //   EPI_LOGITS LM-head logits with optional soft-cap cap*tanh(x/cap) (S/LMHead.swift:20-46).
+//   EPI_STORE  plain fp32 result (test hook).
 // ref_compat reproduces LinearLayer's bias 0.1 + ReLU (S/LinearLayer.swift:61,99-121).
+// The kind is a template parameter: each GEMM instantiation carries only its own
+// epilogue, which keeps the fully unrolled drain loops small and in cache.
 #pragma once
 #include "yk_common.cuh"
 #include "yk_internal.h"
@@ -25,101 +28,169 @@ __device__ __forceinline__ float act_gelu_tanh(float x) {
     return x * cdf;
 }
 
+__device__ __forceinline__ float logit_out(const EpiParams& p, float v) {
+    if (p.ref_compat) v = v + 0.1f;
+    if (p.cap > 0.f) v = p.cap * tanhf(v / p.cap);
+    return v;
+}
+
+// RoPE angle of pair (c, c+1) of a head at token j.
+__device__ __forceinline__ void rope_cs(const EpiParams& p, int c, int j, float& cs, float& sn) {
+    const float th = __fdiv_rn((float)p.pos[j], p.rope_denom[c >> 1]);
+    sincosf(th, &sn, &cs);
+}
+
+// KV-pool address of element (kv, head, dim c) of token j; null (and error bit)
+// if the slot's page lies outside the pool.
 template <typename AT>
+__device__ __forceinline__ AT* pool_elem(const EpiParams& p, int kv, int hh, int c, int j) {
+    const int slot = p.slot[j];
+    const int blk = slot >> 4, off = slot & 15;
+    if (blk < 0 || blk >= p.pool_blocks) {
+        raise_err(p.err, YK_DEV_ERR_BOUNDS);
+        return nullptr;
+    }
+    return reinterpret_cast<AT*>(p.pool) + (size_t)blk * p.block_elems + p.layer_off +
+           ((size_t)(kv * p.n_kv + hh) * 16 + off) * p.head_dim + c;
+}
+
+// Row pair (n, n+1), n even, of token j (SIMT GEMM).
+template <int KIND, typename AT>
 __device__ __forceinline__ void epi_pair(const EpiParams& p, int n, int j, float v0, float v1) {
     if (j >= p.m_tok || n >= p.n_out) return;
-    switch (p.kind) {
-        case EPI_STORE: {  // plain fp32 result (test hook)
-            float* o = reinterpret_cast<float*>(p.out) + (size_t)j * p.n_out + n;
-            o[0] = v0;
-            if (n + 1 < p.n_out) o[1] = v1;
-            break;
+    if constexpr (KIND == EPI_STORE || KIND == EPI_LOGITS) {
+        if constexpr (KIND == EPI_LOGITS) { v0 = logit_out(p, v0); v1 = logit_out(p, v1); }
+        float* o = reinterpret_cast<float*>(p.out) + (size_t)j * p.n_out + n;
+        o[0] = v0;
+        if (n + 1 < p.n_out) o[1] = v1;
+    } else if constexpr (KIND == EPI_RESID) {
+        if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
+        float* o = p.h + (size_t)j * p.ld + n;
+        o[0] = o[0] + v0;
+        o[1] = o[1] + v1;
+    } else if constexpr (KIND == EPI_GLU) {
+        if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
+        const float a = (p.act == 1 ? act_gelu_tanh(v0) : act_silu(v0)) * v1;
+        reinterpret_cast<AT*>(p.out)[(size_t)j * (p.n_out >> 1) + (n >> 1)] = from_f32<AT>(a);
+    } else if constexpr (KIND == EPI_QKV) {
+        if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
+        const int dh = p.head_dim;
+        if (n < p.q_dim + p.kv_dim) {
+            const int c = (n < p.q_dim ? n : n - p.q_dim) % dh;
+            float cs, sn;
+            rope_cs(p, c, j, cs, sn);
+            const float r0 = v0 * cs - v1 * sn, r1 = v0 * sn + v1 * cs;
+            v0 = r0;
+            v1 = r1;
         }
-        case EPI_QKV: {
-            if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
-            const int dh = p.head_dim;
-            if (n < p.q_dim + p.kv_dim) {  // Q or K: rotate the pair
-                const int c = (n < p.q_dim ? n : n - p.q_dim) % dh;
-                const float th = __fdiv_rn((float)p.pos[j], p.rope_denom[c >> 1]);
-                float sn, cs;
-                sincosf(th, &sn, &cs);
-                const float r0 = v0 * cs - v1 * sn;
-                const float r1 = v0 * sn + v1 * cs;
-                v0 = r0;
-                v1 = r1;
-            }
-            if (n < p.q_dim) {
-                AT* o = reinterpret_cast<AT*>(p.out) + (size_t)j * p.q_dim + n;
-                o[0] = from_f32<AT>(v0);
-                o[1] = from_f32<AT>(v1);
-            } else {
-                const int kv = n < p.q_dim + p.kv_dim ? 0 : 1;
-                const int nn = n - p.q_dim - kv * p.kv_dim;
-                const int hh = nn / dh, c = nn % dh;
-                const int slot = p.slot[j];
-                const int blk = slot >> 4, off = slot & 15;
-                if (blk < 0 || blk >= p.pool_blocks) {
-                    raise_err(p.err, YK_DEV_ERR_BOUNDS);
-                    return;
-                }
-                AT* o = reinterpret_cast<AT*>(p.pool) + (size_t)blk * p.block_elems + p.layer_off +
-                        ((size_t)(kv * p.n_kv + hh) * 16 + off) * dh + c;
-                o[0] = from_f32<AT>(v0);
-                o[1] = from_f32<AT>(v1);
-            }
-            break;
+        if (n < p.q_dim) {
+            AT* o = reinterpret_cast<AT*>(p.out) + (size_t)j * p.q_dim + n;
+            o[0] = from_f32<AT>(v0);
+            o[1] = from_f32<AT>(v1);
+        } else {
+            const int kv = n < p.q_dim + p.kv_dim ? 0 : 1;
+            const int nn = n - p.q_dim - kv * p.kv_dim;
+            AT* o = pool_elem<AT>(p, kv, nn / dh, nn % dh, j);
+            if (o) { o[0] = from_f32<AT>(v0); o[1] = from_f32<AT>(v1); }
         }
-        case EPI_RESID: {
-            if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
-            float* o = p.h + (size_t)j * p.ld + n;
-            o[0] = o[0] + v0;
-            o[1] = o[1] + v1;
-            break;
-        }
-        case EPI_GLU: {
-            if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
-            const float a = (p.act == 1 ? act_gelu_tanh(v0) : act_silu(v0)) * v1;
-            reinterpret_cast<AT*>(p.out)[(size_t)j * (p.n_out >> 1) + (n >> 1)] = from_f32<AT>(a);
-            break;
-        }
-        case EPI_LOGITS: {
-            if (p.ref_compat) { v0 = v0 + 0.1f; v1 = v1 + 0.1f; }
-            if (p.cap > 0.f) {
-                v0 = p.cap * tanhf(v0 / p.cap);
-                v1 = p.cap * tanhf(v1 / p.cap);
-            }
-            float* o = reinterpret_cast<float*>(p.out) + (size_t)j * p.n_out + n;
-            o[0] = v0;
-            if (n + 1 < p.n_out) o[1] = v1;
-            break;
-        }
-        default: break;
     }
 }
 
-// NB consecutive tokens j0.. of one row pair.  The residual epilogue issues all
-// its loads of the fp32 stream before any store, so a warp keeps NB
-// read-modify-writes in flight instead of one.
-template <typename AT, int NB>
-__device__ __forceinline__ void epi_batch(const EpiParams& p, int n, int j0, const float (&v0)[NB],
-                                          const float (&v1)[NB]) {
-    if (p.kind == EPI_RESID) {
-        if (n >= p.n_out) return;
-        float2 hv[NB];
-#pragma unroll
-        for (int i = 0; i < NB; ++i)
-            if (j0 + i < p.m_tok) hv[i] = *reinterpret_cast<const float2*>(p.h + (size_t)(j0 + i) * p.ld + n);
-#pragma unroll
-        for (int i = 0; i < NB; ++i) {
-            if (j0 + i >= p.m_tok) continue;
-            float a = v0[i], b = v1[i];
-            if (p.ref_compat) { a = compat_relu(a); b = compat_relu(b); }
-            *reinterpret_cast<float2*>(p.h + (size_t)(j0 + i) * p.ld + n) = make_float2(hv[i].x + a, hv[i].y + b);
+// One output element per lane: row n of token j with value v; `partner` is the
+// value of row n^1 (the other half of a RoPE pair, or gate/up of a GLU pair).
+template <int KIND, typename AT>
+__device__ __forceinline__ void epi_elem(const EpiParams& p, int n, int j, float v, float partner) {
+    if constexpr (KIND == EPI_QKV) {
+        if (p.ref_compat) { v = compat_relu(v); partner = compat_relu(partner); }
+        const int dh = p.head_dim;
+        const bool odd = n & 1;
+        if (n < p.q_dim + p.kv_dim) {  // rotate (x0, x1) = (even row, odd row)
+            const int c = (n < p.q_dim ? n : n - p.q_dim) % dh;
+            float cs, sn;
+            rope_cs(p, c, j, cs, sn);
+            const float x0 = odd ? partner : v, x1 = odd ? v : partner;
+            v = odd ? (x0 * sn + x1 * cs) : (x0 * cs - x1 * sn);
         }
-        return;
+        if (n < p.q_dim) {
+            reinterpret_cast<AT*>(p.out)[(size_t)j * p.q_dim + n] = from_f32<AT>(v);
+        } else {
+            const int kv = n < p.q_dim + p.kv_dim ? 0 : 1;
+            const int nn = n - p.q_dim - kv * p.kv_dim;
+            AT* o = pool_elem<AT>(p, kv, nn / dh, nn % dh, j);
+            if (o) *o = from_f32<AT>(v);
+        }
+    } else if constexpr (KIND == EPI_GLU) {
+        if (n & 1) return;  // the even row (gate) writes act(gate) * up
+        float g = v, u = partner;
+        if (p.ref_compat) { g = compat_relu(g); u = compat_relu(u); }
+        const float a = (p.act == 1 ? act_gelu_tanh(g) : act_silu(g)) * u;
+        reinterpret_cast<AT*>(p.out)[(size_t)j * (p.n_out >> 1) + (n >> 1)] = from_f32<AT>(a);
     }
+}
+
+// Drains 16 consecutive tokens j0.. of row n: one row per lane, all 32 lanes of
+// the warp call it together.  Fully unrolled; the residual epilogue issues its
+// 16 loads of the fp32 stream before any store.
+template <int KIND, typename AT>
+__device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const float (&v)[16]) {
+    if constexpr (KIND == EPI_QKV || KIND == EPI_GLU) {
+        float w[16];
 #pragma unroll
-    for (int i = 0; i < NB; ++i) epi_pair<AT>(p, n, j0 + i, v0[i], v1[i]);
+        for (int i = 0; i < 16; ++i) w[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
+        if (n >= p.n_out) return;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (j0 + i < p.m_tok) epi_elem<KIND, AT>(p, n, j0 + i, v[i], w[i]);
+    } else if constexpr (KIND == EPI_RESID) {
+        if (n >= p.n_out) return;
+        float hv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (j0 + i < p.m_tok) hv[i] = p.h[(size_t)(j0 + i) * p.ld + n];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (j0 + i < p.m_tok) p.h[(size_t)(j0 + i) * p.ld + n] = hv[i] + (p.ref_compat ? compat_relu(v[i]) : v[i]);
+    } else {  // EPI_STORE, EPI_LOGITS
+        if (n >= p.n_out) return;
+        float* o = reinterpret_cast<float*>(p.out);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            if (j0 + i < p.m_tok) {
+                float a = v[i];
+                if constexpr (KIND == EPI_LOGITS) a = logit_out(p, a);
+                o[(size_t)(j0 + i) * p.n_out + n] = a;
+            }
+        }
+    }
+}
+
+// Rows n..n+3 (n % 4 == 0; n_out is a multiple of 4) of token j with one vector
+// store (split-tile reductions).
+template <int KIND, typename AT>
+__device__ __forceinline__ void epi_quad(const EpiParams& p, int n, int j, float4 v) {
+    if (j >= p.m_tok || n >= p.n_out) return;
+    if constexpr (KIND == EPI_RESID) {
+        if (p.ref_compat) { v.x = compat_relu(v.x); v.y = compat_relu(v.y); v.z = compat_relu(v.z); v.w = compat_relu(v.w); }
+        float4* o = reinterpret_cast<float4*>(p.h + (size_t)j * p.ld + n);
+        const float4 h = *o;
+        *o = make_float4(h.x + v.x, h.y + v.y, h.z + v.z, h.w + v.w);
+    } else if constexpr (KIND == EPI_STORE || KIND == EPI_LOGITS) {
+        if constexpr (KIND == EPI_LOGITS) {
+            v.x = logit_out(p, v.x); v.y = logit_out(p, v.y); v.z = logit_out(p, v.z); v.w = logit_out(p, v.w);
+        }
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)j * p.n_out + n) = v;
+    } else if constexpr (KIND == EPI_GLU) {
+        float g0 = v.x, u0 = v.y, g1 = v.z, u1 = v.w;
+        if (p.ref_compat) { g0 = compat_relu(g0); u0 = compat_relu(u0); g1 = compat_relu(g1); u1 = compat_relu(u1); }
+        const float a0 = (p.act == 1 ? act_gelu_tanh(g0) : act_silu(g0)) * u0;
+        const float a1 = (p.act == 1 ? act_gelu_tanh(g1) : act_silu(g1)) * u1;
+        AT* o = reinterpret_cast<AT*>(p.out) + (size_t)j * (p.n_out >> 1) + (n >> 1);
+        o[0] = from_f32<AT>(a0);
+        o[1] = from_f32<AT>(a1);
+    } else if constexpr (KIND == EPI_QKV) {
+        epi_pair<KIND, AT>(p, n, j, v.x, v.y);
+        epi_pair<KIND, AT>(p, n + 2, j, v.z, v.w);
+    }
 }
 
 }  // namespace yk

@@ -1,15 +1,24 @@
 // yk_gemm.cu -- the verify-forward linear layers (replaces LinearLayer.forward /
 // gemm_kernel, S/LinearLayer.swift:71-128, S/gemm.metal:6-34).
 //
-// bf16: swap-AB tcgen05 GEMM.  D[n][j] = sum_k W[n][k] * X[j][k]: the weight
-// tile (128 output rows x 64 k) is the MMA "A" operand, the tokens (BN <= 256)
-// are the MMA "N" dimension, so at verify batch sizes every weight byte is
-// streamed from HBM exactly once.  TMA (no multicast) stages W and X tiles with
-// 128-byte swizzle into a multi-stage mbarrier pipeline; one thread issues
-// tcgen05.mma into a TMEM accumulator; all four warps drain TMEM through the
-// fused epilogue.  Split-K spreads skinny layers over all SMs; the last CTA of
-// a tile sums the fp32 partials in fixed split order (deterministic) and runs
-// the epilogue.
+// bf16: persistent, warp-specialised tcgen05 GEMM.
+//   D[n][j] = sum_k W[n][k] * X[j][k] ("swap-AB"): a 128-row weight tile is the
+//   MMA A operand and the tokens (BN <= 256) are the MMA N dimension, so at
+//   verify batch sizes every weight byte crosses HBM once.
+//   Warp 0 streams W and X k-blocks with TMA (128-byte swizzle, no multicast)
+//   into a shared-memory ring; warp 1 issues tcgen05.mma into one of two TMEM
+//   accumulators; warps 2-5 drain the other accumulator through the fused
+//   epilogue, so the epilogue of one segment overlaps the next mainloop.
+//   Work split, chosen per layer shape:
+//   * stream-K (tiles >= SMs/2): the (tile x 64-wide k-block) space is cut into
+//     equal contiguous ranges, one per CTA, so every SM streams the same number
+//     of weight bytes.  A tile cut across CTAs is finished by the segment that
+//     arrives last: it sums the published fp32 partials in k order and runs the
+//     epilogue.  No CTA waits for another.
+//   * cluster split-K (few tiles): the CS CTAs sharing a tile form a cluster; each
+//     parks its partial in shared memory and reduces 1/CS of the tile's columns
+//     over distributed shared memory, in rank order.
+//   Both reductions are deterministic.
 //
 // fp32: a SIMT kernel with the same epilogues (the fp32 reference-numerics
 // config; tensor cores have no fp32 x fp32 mode).
@@ -24,196 +33,345 @@ namespace yk {
 
 constexpr int TC_BM = 128;       // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;        // k per stage: one 128-byte swizzle row of bf16
-constexpr int TC_THREADS = 128;  // 4 warps: TMA producer lane, MMA lane, 4 epilogue warps
+constexpr int TC_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
 constexpr int TC_SMEM_BUDGET = 200 * 1024;
 
 struct TcArgs {
     int n_out, K, m_tok;
-    int tiles_m, splits, kb_total;
+    int tiles_m, kb_total;      // k-blocks per tile
     int BN, stages;
-    uint32_t idesc, tmem_cols;
-    float* ws;
-    uint32_t* counters;
+    long long units;            // tiles * kb_total
+    int grid;
+    int cluster_s;              // > 0: cluster split-K with cluster_s CTAs per tile
+    uint32_t idesc, tmem_cols;  // columns of one accumulator stage
+    float* ws;                  // stream-K partials: slot (2*cta + first/last) x [BN][128]
+    uint32_t* counters;         // per-tile arrival counters (zero between launches)
     EpiParams epi;
+    unsigned long long* stamps;  // optional per-CTA phase timestamps (test hook), else null
 };
 
+// Phase timestamps of one CTA (ns, %globaltimer), recorded only when a.stamps != null.
+enum : int { ST_START = 0, ST_FIRST_TMA, ST_FIRST_FULL, ST_LAST_MMA, ST_LAST_ACC, ST_EPI_DONE, ST_SEGS, ST_N = 8 };
+__device__ __forceinline__ void stamp(const TcArgs& a, int what) {
+    if (a.stamps) a.stamps[(size_t)blockIdx.x * ST_N + what] = globaltimer_ns();
+}
+
+__device__ __forceinline__ long long unit_begin(int c, long long U, int G) { return ((long long)c * U) / G; }
+// CTA whose range contains unit u (inverse of unit_begin).
+__device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
+    return (int)(((u + 1) * G + U - 1) / U) - 1;
+}
+__device__ __forceinline__ int partial_slot(int cta, int tile, long long U, int G, int KB) {
+    return 2 * cta + ((long long)tile == unit_begin(cta, U, G) / KB ? 0 : 1);
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void epi_bar_sync() {  // named barrier over the 4 epilogue warps
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <int KIND>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int BN = a.BN, S = a.stages;
     const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
-    uint64_t* full = bars;
-    uint64_t* empty = bars + S;
-    uint64_t* accb = bars + 2 * S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 1);
-    volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] last
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+    uint64_t* empty = full + S;
+    uint64_t* acc_full = empty + S;      // [2]
+    uint64_t* acc_empty = acc_full + 2;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    // [0] abort, [1] last arriver of a cut tile, [2..3] epilogue's broadcast of [0] by segment parity
+    volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int unit = blockIdx.x;
-    const int split = unit % a.splits;
-    const int tile = unit / a.splits;
-    const int tm = tile % a.tiles_m, tn = tile / a.tiles_m;
-    const int kb0 = (int)(((long long)split * a.kb_total) / a.splits);
-    const int kb1 = (int)(((long long)(split + 1) * a.kb_total) / a.splits);
-    const int nkb = kb1 - kb0;
+    const int c = blockIdx.x, G = a.grid, KB = a.kb_total;
+    const long long U = a.units;
+    const int CS = a.cluster_s;
+    long long u0, u1;
+    if (CS > 0) {  // CTA r of cluster t owns k-blocks [r*KB/CS, (r+1)*KB/CS) of tile t
+        const long long t = c / CS, r = c % CS;
+        u0 = t * KB + r * KB / CS;
+        u1 = t * KB + (r + 1) * KB / CS;
+    } else {       // an equal contiguous share of all (tile, k-block) units
+        u0 = unit_begin(c, U, G);
+        u1 = unit_begin(c + 1, U, G);
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&empty[s]), 1);
         }
-        mbar_init(smem_u32(accb), 1);
-        flags[0] = 0;
-        flags[1] = 0;
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&acc_full[s]), 1);
+            mbar_init(smem_u32(&acc_empty[s]), 128);
+        }
+        flags[0] = flags[1] = flags[2] = flags[3] = 0;
         mbar_fence_init();
     }
-    if (warp == 0) tmem_alloc(smem_u32(tmem_slot), a.tmem_cols);
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 2 * a.tmem_cols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) stamp(a, ST_START);
 
-    int issued_round[8];
-#pragma unroll
-    for (int s = 0; s < 8; ++s) issued_round[s] = -1;
-
-    if (threadIdx.x == 0) {
-        // ---------------- TMA producer ----------------
-        const uint64_t pol_w = policy_evict_first();
-        const uint64_t pol_x = policy_evict_last();
-        for (int i = 0; i < nkb; ++i) {
-            const int s = i % S;
-            const int r = i / S;
-            if (r > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (uint32_t)((r - 1) & 1))) {
-                flags[0] = 1;
-                raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
-                break;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            long long g = 0;
+            for (long long u = u0; u < u1 && !flags[0];) {
+                const int t = (int)(u / KB);
+                const long long e = min(u1, (long long)(t + 1) * KB);
+                const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+                for (long long uu = u; uu < e; ++uu, ++g) {
+                    const int s = (int)(g % S);
+                    const long long r = g / S;
+                    if (r > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (uint32_t)((r - 1) & 1))) {
+                        flags[0] = 1;
+                        raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
+                        break;
+                    }
+                    const uint32_t wdst = smem_u32(smem + (size_t)s * stage_bytes);
+                    const uint32_t fb = smem_u32(&full[s]);
+                    const int kb = (int)(uu - (long long)t * KB);
+                    mbar_arrive_expect_tx(fb, stage_bytes);
+                    tma_load_2d(wdst, &tmW, kb * TC_BK, tm * TC_BM, fb, pol_w);
+                    tma_load_2d(wdst + 16384u, &tmX, kb * TC_BK, tn * BN, fb, pol_x);
+                    if (g == 0) stamp(a, ST_FIRST_TMA);
+                }
+                u = e;
             }
-            if (flags[0]) break;
-            const uint32_t wdst = smem_u32(smem + (size_t)s * stage_bytes);
-            const uint32_t xdst = wdst + 16384u;
-            const uint32_t fb = smem_u32(&full[s]);
-            mbar_arrive_expect_tx(fb, stage_bytes);
-            tma_load_2d(wdst, &tmW, (kb0 + i) * TC_BK, tm * TC_BM, fb, pol_w);
-            tma_load_2d(xdst, &tmX, (kb0 + i) * TC_BK, tn * BN, fb, pol_x);
-            if (s < 8) issued_round[s] = r;
+            // Every issued copy must land before shared memory is reused or released.
+            const long long issued = g;
+            for (long long i = max(0LL, issued - S); i < issued; ++i)
+                (void)mbar_wait_bounded(smem_u32(&full[i % S]), (uint32_t)((i / S) & 1));
         }
-    } else if (threadIdx.x == 32) {
-        // ---------------- MMA issuer ----------------
-        for (int i = 0; i < nkb; ++i) {
-            const int s = i % S;
-            const int r = i / S;
-            if (!mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)(r & 1))) {
-                flags[0] = 1;
-                raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
-                break;
-            }
-            tc_fence_after();
-            const uint32_t wsm = smem_u32(smem + (size_t)s * stage_bytes);
-            const uint32_t xsm = wsm + 16384u;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            long long g = 0;
+            int seg = 0;
+            for (long long u = u0; u < u1 && !flags[0]; ++seg) {
+                const int t = (int)(u / KB);
+                const long long e = min(u1, (long long)(t + 1) * KB);
+                const int st = seg & 1;
+                if (seg >= 2 && !mbar_wait_bounded(smem_u32(&acc_empty[st]), (uint32_t)(((seg >> 1) - 1) & 1))) {
+                    flags[0] = 1;
+                    raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)st * a.tmem_cols;
+                bool ok = true;
+                for (long long uu = u; uu < e; ++uu, ++g) {
+                    const int s = (int)(g % S);
+                    if (!mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)((g / S) & 1))) {
+                        flags[0] = 1;
+                        raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (g == 0) stamp(a, ST_FIRST_FULL);
+                    const uint32_t wsm = smem_u32(smem + (size_t)s * stage_bytes);
 #pragma unroll
-            for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                const uint64_t ad = sw128_kmajor_desc(wsm + kk * 32);
-                const uint64_t bd = sw128_kmajor_desc(xsm + kk * 32);
-                tc_mma_bf16(tmem, ad, bd, a.idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < TC_BK / 16; ++kk)
+                        tc_mma_bf16(d, sw128_kmajor_desc(wsm + kk * 32), sw128_kmajor_desc(wsm + 16384u + kk * 32),
+                                    a.idesc, (uu > u || kk > 0) ? 1u : 0u);
+                    tc_commit(smem_u32(&empty[s]));
+                }
+                tc_commit(smem_u32(&acc_full[st]));
+                if (!ok) break;
+                u = e;
             }
-            tc_commit(smem_u32(&empty[s]));
-        }
-        tc_commit(smem_u32(accb));
-    }
-    __syncwarp();
-
-    // ---------------- epilogue: all 4 warps ----------------
-    const bool acc_ok = mbar_wait_bounded(smem_u32(accb), 0);
-    if (!acc_ok) {
-        flags[0] = 1;
-        raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
-    }
-    tc_fence_after();
-    __syncthreads();
-    const bool aborted = flags[0] != 0;
-    const int row = warp * 32 + lane;  // TMEM lane == output row within the tile
-    const int n_base = tm * TC_BM;
-    const int j_base = tn * BN;
-    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
-
-    if (threadIdx.x == 0 && aborted) {
-        // Let every TMA copy this CTA issued land before the stage buffers are reused.
-        for (int s = 0; s < S && s < 8; ++s)
-            if (issued_round[s] >= 0) (void)mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)(issued_round[s] & 1));
-    }
-    __syncthreads();
-    // Accumulator -> shared memory [BN][128] fp32 (the stage buffers are free now:
-    // every TMA load was consumed and every MMA completed before accb fired).
-    float* red = reinterpret_cast<float*>(smem);
-    if (!aborted) {
-        for (int c = 0; c < BN; c += 16) {
-            uint32_t r[16];
-            tmem_ld16(t_lane + (uint32_t)c, r);
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) red[(c + jj) * TC_BM + row] = __uint_as_float(r[jj]);
+            stamp(a, ST_LAST_MMA);
+            if (a.stamps) a.stamps[(size_t)blockIdx.x * ST_N + ST_SEGS] = (unsigned long long)seg;
         }
     } else {
-        for (int c = 0; c < BN; ++c) red[c * TC_BM + row] = 0.f;
-    }
-    // Split-K: the `splits` CTAs of a tile form one cluster.  After the barrier
-    // each CTA reduces its share of the tile's columns over every CTA's partial
-    // through distributed shared memory, always in rank order (deterministic),
-    // and runs the epilogue for those columns.
-    const int S_k = a.splits;
-    const uint32_t rank = S_k > 1 ? cluster_ctarank() : 0u;
-    if (S_k > 1) cluster_sync_all(); else __syncthreads();
-    const int c0 = (int)((rank * (uint32_t)BN) / (uint32_t)S_k);
-    const int c1 = (int)(((rank + 1) * (uint32_t)BN) / (uint32_t)S_k);
-    const uint32_t red_addr = smem_u32(red);
-    constexpr int NB = 8;
-    for (int c = c0; c < c1; c += NB) {
-        float v[NB], w[NB];
-#pragma unroll
-        for (int i = 0; i < NB; ++i) v[i] = 0.f;
-        if (S_k == 1) {
-#pragma unroll
-            for (int i = 0; i < NB; ++i)
-                if (c + i < c1) v[i] = red[(c + i) * TC_BM + row];
-        } else {
-            for (int sp = 0; sp < S_k; ++sp) {
-                const uint32_t base = mapa_shared(red_addr, (uint32_t)sp);
-                float t[NB];
-#pragma unroll
-                for (int i = 0; i < NB; ++i)
-                    t[i] = (c + i < c1) ? ld_shared_cluster_f32(base + (uint32_t)(((c + i) * TC_BM + row) * 4)) : 0.f;
-#pragma unroll
-                for (int i = 0; i < NB; ++i) v[i] += t[i];
+        // ---------------- epilogue: warps 2..5 ----------------
+        const int q = warp & 3;           // TMEM lane quadrant this warp may read
+        const int row = q * 32 + lane;    // output row within the tile
+        const int et = threadIdx.x - 64;  // 0..127
+        int seg = 0;
+        for (long long u = u0; u < u1; ++seg) {
+            const int t = (int)(u / KB);
+            const long long e = min(u1, (long long)(t + 1) * KB);
+            const int kb_b = (int)(u - (long long)t * KB), kb_e = (int)(e - (long long)t * KB);
+            const int st = seg & 1;
+            // One thread waits (bounded) and broadcasts, so the epilogue warps always
+            // take the same path through their named barriers.
+            if (et == 0) {
+                if (!mbar_wait_bounded(smem_u32(&acc_full[st]), (uint32_t)((seg >> 1) & 1))) {
+                    flags[0] = 1;
+                    raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
+                }
+                flags[2 + st] = flags[0];  // per-parity slot: rewritten only after the next barrier
             }
-        }
+            epi_bar_sync();
+            if (flags[2 + st]) break;
+            tc_fence_after();
+            if (et == 0 && e == u1) stamp(a, ST_LAST_ACC);
+            const uint32_t taddr = tmem + (uint32_t)st * a.tmem_cols + ((uint32_t)(q * 32) << 16);
+            const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+            const int n = tm * TC_BM + row;
+            const int j_base = tn * BN;
+            if (CS > 0) {
+                // park the partial in shared memory [BN][128] fp32; the ring is idle
+                // (every staged k-block was consumed before acc_full fired)
+                float* red = reinterpret_cast<float*>(smem);
+                for (int cc = 0; cc < BN; cc += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr + (uint32_t)cc, r);
 #pragma unroll
-        for (int i = 0; i < NB; ++i) w[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
-        if (!aborted && (lane & 1) == 0) {
-            if (c + NB <= c1) {
-                epi_batch<__nv_bfloat16, NB>(a.epi, n_base + row, j_base + c, v, w);
+                    for (int i = 0; i < 16; ++i) red[(cc + i) * TC_BM + row] = __uint_as_float(r[i]);
+                }
+            } else if (kb_b == 0 && kb_e == KB) {
+                // whole tile in this segment: straight from TMEM, one row per lane
+                for (int cc = 0; cc < BN; cc += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr + (uint32_t)cc, r);
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+                    drain16<KIND, __nv_bfloat16>(a.epi, n, j_base + cc, v);
+                }
             } else {
-                for (int i = 0; i < c1 - c; ++i) epi_pair<__nv_bfloat16>(a.epi, n_base + row, j_base + c + i, v[i], w[i]);
+                // tile cut across CTAs: publish this partial; the last arriver finishes the tile
+                const int c_lo = cta_of_unit((long long)t * KB, U, G);
+                const int c_hi = cta_of_unit((long long)(t + 1) * KB - 1, U, G);
+                const int nseg = c_hi - c_lo + 1;
+                float* mine = a.ws + (size_t)partial_slot(c, t, U, G, KB) * TC_BM * BN;
+                for (int cc = 0; cc < BN; cc += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr + (uint32_t)cc, r);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) __stcg(mine + (size_t)(cc + i) * TC_BM + row, __uint_as_float(r[i]));
+                }
+                __threadfence();
+                epi_bar_sync();
+                if (et == 0) flags[1] = (atomicAdd(&a.counters[t], 1u) == (uint32_t)(nseg - 1)) ? 1 : 0;
+                epi_bar_sync();
+                if (flags[1]) {
+                    // Sum the nseg partials in k order (deterministic).  Thread et owns rows
+                    // 4*(et&31)..+3 of columns (et>>5) + 4i, i < 8: float4 loads, 8 columns x
+                    // up to 4 segments in flight per round, one vector store per quad.
+                    __threadfence();
+                    const int r4 = (et & 31) * 4, cq = et >> 5;
+                    for (int cc = 0; cc < BN; cc += 32) {
+                        float4 acc[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int sg0 = 0; sg0 < nseg; sg0 += 4) {
+                            float4 tv[4][8];
+#pragma unroll
+                            for (int s4 = 0; s4 < 4; ++s4) {
+                                if (sg0 + s4 < nseg) {
+                                    const float* src =
+                                        a.ws + (size_t)partial_slot(c_lo + sg0 + s4, t, U, G, KB) * TC_BM * BN + r4;
+#pragma unroll
+                                    for (int i = 0; i < 8; ++i) {
+                                        const int col = cc + cq + 4 * i;
+                                        if (col < BN)
+                                            tv[s4][i] = __ldcg(reinterpret_cast<const float4*>(src + (size_t)col * TC_BM));
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int s4 = 0; s4 < 4; ++s4) {
+                                if (sg0 + s4 < nseg) {
+#pragma unroll
+                                    for (int i = 0; i < 8; ++i) {
+                                        acc[i].x += tv[s4][i].x;
+                                        acc[i].y += tv[s4][i].y;
+                                        acc[i].z += tv[s4][i].z;
+                                        acc[i].w += tv[s4][i].w;
+                                    }
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int col = cc + cq + 4 * i;
+                            if (col < BN) epi_quad<KIND, __nv_bfloat16>(a.epi, tm * TC_BM + r4, j_base + col, acc[i]);
+                        }
+                    }
+                    if (et == 0) a.counters[t] = 0u;
+                }
+                epi_bar_sync();  // flags[1] is rewritten by the next cut tile
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acc_empty[st]));
+            u = e;
+        }
+        if (et == 0) stamp(a, ST_EPI_DONE);
+    }
+
+    if (CS > 0) {
+        // ---------------- cluster reduction ----------------
+        // Every CTA of the cluster holds its partial of tile t in shared memory after
+        // the barrier.  Rank r sums columns [r*BN/CS, (r+1)*BN/CS) over all ranks in
+        // rank order through distributed shared memory and runs their epilogue.
+        cluster_sync_any();
+        const uint32_t rank = cluster_ctarank();
+        const int t = c / CS;
+        const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+        const int c0 = (int)(rank * (uint32_t)BN / (uint32_t)CS);
+        const int c1 = (int)((rank + 1) * (uint32_t)BN / (uint32_t)CS);
+        const int nitems = (c1 - c0) * 32;  // (column, 4-row group) items
+        const uint32_t red_addr = smem_u32(smem);
+        const bool ok = flags[0] == 0;
+        for (int base = threadIdx.x; base < nitems; base += TC_THREADS * 4) {
+            float4 acc[4];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) acc[q4] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < CS; ++s) {
+                const uint32_t rb = mapa_shared(red_addr, (uint32_t)s);
+                float4 tv[4];
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    const int it = base + q4 * TC_THREADS;
+                    if (it < nitems)
+                        tv[q4] = ld_shared_cluster_v4(rb + (uint32_t)(((c0 + it / 32) * TC_BM + (it % 32) * 4) * 4));
+                }
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    if (base + q4 * TC_THREADS < nitems) {
+                        acc[q4].x += tv[q4].x;
+                        acc[q4].y += tv[q4].y;
+                        acc[q4].z += tv[q4].z;
+                        acc[q4].w += tv[q4].w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+                const int it = base + q4 * TC_THREADS;
+                if (ok && it < nitems)
+                    epi_quad<KIND, __nv_bfloat16>(a.epi, tm * TC_BM + (it % 32) * 4, tn * BN + c0 + it / 32, acc[q4]);
             }
         }
+        cluster_sync_any();  // no CTA releases shared memory a peer still reads
+        if (threadIdx.x == 64) stamp(a, ST_EPI_DONE);
     }
-    // No CTA may leave while a peer still reads its shared memory.
-    if (S_k > 1) cluster_sync_all();
 
     // ---------------- teardown ----------------
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem, a.tmem_cols);
+    if (warp == 1) tmem_dealloc(tmem, 2 * a.tmem_cols);
 }
 
 // ---------------------------------------------------------------------------
 // SIMT GEMM: each warp owns an output-row pair, lanes stride over k; a CTA
-// covers 16 rows x 8 tokens.  Used for fp32 weights (and as the GPU-side
-// cross-check of the tensor-core path in tests).
+// covers 16 rows x 8 tokens.  Used for fp32 weights.
 // ---------------------------------------------------------------------------
-template <typename WT, typename XT>
+template <int KIND, typename WT, typename XT>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const WT* __restrict__ W, const XT* __restrict__ X, int n_out,
                                                          int K, int m_tok, EpiParams ep) {
     constexpr int TOK = 8;
@@ -248,7 +406,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const WT* __restrict__ W
     if (lane == 0) {
 #pragma unroll
         for (int t = 0; t < TOK; ++t)
-            if (j0 + t < m_tok) epi_pair<XT>(ep, n, j0 + t, acc0[t], acc1[t]);
+            if (j0 + t < m_tok) epi_pair<KIND, XT>(ep, n, j0 + t, acc0[t], acc1[t]);
     }
 }
 
@@ -293,15 +451,31 @@ static yk_status get_x_map(yk_model* m, const void* X, int K, int BN, const CUte
     return YK_OK;
 }
 
-// How many clusters of `s` GEMM CTAs (one CTA per SM) the device runs at once.
+template <int KIND>
+static yk_status launch_tc(const cudaLaunchConfig_t& cfg, const CUtensorMap* tmW, const CUtensorMap* tmX,
+                           const TcArgs& a) {
+    static bool attr = false;
+    if (!attr) {
+        YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           TC_SMEM_BUDGET + 16384 + 2048));
+        attr = true;
+    }
+    YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<KIND>, *tmW, *tmX, a));
+    return YK_OK;
+}
+
+// How many clusters of `s` GEMM CTAs (one per SM, full shared-memory budget) the
+// device holds at once; queried once per size.
 static int cluster_capacity(yk_engine* e, int s) {
     static int cap[9] = {0};
     static int dev = -1;
     if (dev != e->device) {
-        for (int i = 0; i < 9; ++i) cap[i] = 0;
+        for (int& c : cap) c = 0;
         dev = e->device;
     }
     if (cap[s] == 0) {
+        cudaFuncSetAttribute(gemm_tc_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TC_SMEM_BUDGET + 16384 + 2048);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(s * 64);
         cfg.blockDim = dim3(TC_THREADS);
@@ -314,35 +488,31 @@ static int cluster_capacity(yk_engine* e, int s) {
         cfg.attrs = at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EPI_STORE>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
-            n = std::max(1, e->num_sms / s / 2);
+            n = 1;
         }
         cap[s] = n;
     }
     return cap[s];
 }
 
-// Split-K choice (cluster size): minimise waves x (k-blocks per CTA + fixed cost).
-static int choose_splits(yk_engine* e, int tiles, int kb) {
-    int best = 1;
-    double best_cost = 1e30;
-    for (int s = 1; s <= std::min(kb, 8); ++s) {
-        const int waves = (tiles + cluster_capacity(e, s) - 1) / cluster_capacity(e, s);
-        const double cost = waves * ((double)((kb + s - 1) / s) + 3.0 + (s > 1 ? 1.0 : 0.0));
-        if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
-    }
-    return best;
+template <int KIND>
+static void launch_simt(dim3 grid, cudaStream_t st, const void* W, const void* X, int n_out, int K, int m_tok,
+                        const EpiParams& ep) {
+    gemm_simt_kernel<KIND, float, float><<<grid, 256, 0, st>>>((const float*)W, (const float*)X, n_out, K, m_tok, ep);
 }
 
+// force_grid: 0 = heuristic; > 0 = stream-K with that many CTAs; < 0 = cluster
+// split-K with -force_grid CTAs per tile (test hook).
 yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const void* X, int n_out, int K, int m_tok,
-                   const EpiParams& ep_in, int force_splits) {
+                   const EpiParams& ep_in, int force_grid) {
     yk_engine* e = m->e;
     EpiParams ep = ep_in;
     ep.n_out = n_out;
     ep.m_tok = m_tok;
     ep.err = e->d_err;
-    YK_ARG(n_out % 2 == 0 && m_tok > 0 && m_tok <= m->cfg.max_tokens, "gemm shape");
+    YK_ARG(n_out % 4 == 0 && m_tok > 0 && m_tok <= m->cfg.max_tokens, "gemm shape");
     // Algorithmic traffic of this launch: weights + activations once, plus the epilogue's outputs.
     const double es = m->cfg.dtype == YK_DTYPE_BF16 ? 2.0 : 4.0;
     double out_bytes = (double)m_tok * n_out * 4.0;
@@ -352,31 +522,49 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     ProfScope prof(e, YK_PROF_GEMM, ((double)n_out + m_tok) * K * es + out_bytes, 2.0 * n_out * K * m_tok);
     if (m->cfg.dtype == YK_DTYPE_F32) {
         dim3 grid((n_out + 15) / 16, (m_tok + 7) / 8);
-        gemm_simt_kernel<float, float><<<grid, 256, 0, e->stream>>>((const float*)W, (const float*)X, n_out, K, m_tok, ep);
+        switch (ep.kind) {
+            case EPI_QKV: launch_simt<EPI_QKV>(grid, e->stream, W, X, n_out, K, m_tok, ep); break;
+            case EPI_RESID: launch_simt<EPI_RESID>(grid, e->stream, W, X, n_out, K, m_tok, ep); break;
+            case EPI_GLU: launch_simt<EPI_GLU>(grid, e->stream, W, X, n_out, K, m_tok, ep); break;
+            case EPI_LOGITS: launch_simt<EPI_LOGITS>(grid, e->stream, W, X, n_out, K, m_tok, ep); break;
+            default: launch_simt<EPI_STORE>(grid, e->stream, W, X, n_out, K, m_tok, ep); break;
+        }
         e->launches++;
         YK_CHECK_CUDA(cudaGetLastError());
         return YK_OK;
     }
-    // bf16: tcgen05 path.
+    // bf16: persistent tcgen05 path.
     const int BN = m_tok <= 256 ? ((m_tok + 15) / 16) * 16 : 256;
     const int tiles_n = (m_tok + BN - 1) / BN;
     const int tiles_m = (n_out + TC_BM - 1) / TC_BM;
     const int kb = (K + TC_BK - 1) / TC_BK;
-    const int tiles = tiles_m * tiles_n;
-    static bool attr_set = false;
-    if (!attr_set) {
-        YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           TC_SMEM_BUDGET + 16384 + 2048));
-        attr_set = true;
+    const long long tiles = (long long)tiles_m * tiles_n;
+    const long long units = tiles * kb;
+    // Few tiles (fewer than half the SMs): cluster split-K with the largest cluster
+    // size whose clusters all run at once.  Otherwise stream-K with at least ~8
+    // k-blocks per CTA so each pipeline fills before its epilogue.
+    int cs = 0;
+    if (force_grid < 0) {
+        cs = std::min(-force_grid, std::min(8, kb));
+    } else if (force_grid == 0 && tiles * 2 < e->num_sms) {
+        for (int s = (int)std::min<long long>(std::min(8, kb), e->num_sms / tiles); s >= 2 && cs == 0; --s)
+            if (tiles <= cluster_capacity(e, s)) cs = s;
     }
-    int splits = choose_splits(e, tiles, kb);
-    if (force_splits > 0) {
-        YK_ARG(force_splits <= kb && force_splits <= 8, "forced split count must be <= min(k-blocks, 8)");
-        splits = force_splits;
+    int grid = (int)std::min<long long>(e->num_sms, std::max<long long>(1, units / 8));
+    if (force_grid > 0) grid = (int)std::min<long long>(force_grid, units);
+    if (cs > 0) grid = (int)(tiles * cs);
+    YK_ARG(cs > 0 || (size_t)2 * grid * TC_BM * BN <= m->gemm_ws_floats, "split workspace too small");
+    if (tiles > m->gemm_counter_cap) {
+        YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+        if (m->gemm_counters) cudaFree(m->gemm_counters);
+        m->gemm_counters = nullptr;
+        m->gemm_counter_cap = 0;
+        YK_CHECK_CUDA(cudaMalloc(&m->gemm_counters, (size_t)tiles * 2 * 4));
+        YK_CHECK_CUDA(cudaMemset(m->gemm_counters, 0, (size_t)tiles * 2 * 4));
+        m->gemm_counter_cap = (int)(tiles * 2);
     }
     const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
-    int stages = std::min(8, (int)(TC_SMEM_BUDGET / stage_bytes));
-    stages = std::max(2, std::min(stages, std::max(2, kb)));
+    const int stages = std::max(2, std::min(8, (int)(TC_SMEM_BUDGET / stage_bytes)));
     const size_t smem = (size_t)stages * stage_bytes + 1024 + 256;
     uint32_t cols = 32;
     while ((int)cols < BN) cols <<= 1;
@@ -385,26 +573,35 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     YK_TRY(get_x_map(m, X, K, BN, &tmX));
     TcArgs a;
     a.n_out = n_out; a.K = K; a.m_tok = m_tok;
-    a.tiles_m = tiles_m; a.splits = splits; a.kb_total = kb;
+    a.tiles_m = tiles_m; a.kb_total = kb;
     a.BN = BN; a.stages = stages;
+    a.units = units; a.grid = grid; a.cluster_s = cs;
     a.idesc = idesc_bf16_f32(TC_BM, BN);
     a.tmem_cols = cols;
     a.ws = m->gemm_ws;
     a.counters = m->gemm_counters;
     a.epi = ep;
+    a.stamps = m->gemm_stamps;
+    m->gemm_last_grid = grid;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles * splits);
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = e->stream;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = splits;
+    at[0].val.clusterDim.x = cs > 0 ? cs : 1;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel, *tmW, *tmX, a));
+    switch (ep.kind) {
+        case EPI_QKV: YK_TRY(launch_tc<EPI_QKV>(cfg, tmW, tmX, a)); break;
+        case EPI_RESID: YK_TRY(launch_tc<EPI_RESID>(cfg, tmW, tmX, a)); break;
+        case EPI_GLU: YK_TRY(launch_tc<EPI_GLU>(cfg, tmW, tmX, a)); break;
+        case EPI_LOGITS: YK_TRY(launch_tc<EPI_LOGITS>(cfg, tmW, tmX, a)); break;
+        default: YK_TRY(launch_tc<EPI_STORE>(cfg, tmW, tmX, a)); break;
+    }
     e->launches++;
     return YK_OK;
 }
@@ -412,13 +609,14 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
 }  // namespace yk
 
 // ---------------------------------------------------------------------------
-// Test hook (include/yk_testing.h): one tcgen05 GEMM with a plain fp32 store.
+// Test hooks (include/yk_testing.h): one tcgen05 GEMM with a plain fp32 store.
 // ---------------------------------------------------------------------------
 #include "../../include/yk_testing.h"
 
-extern "C" yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K,
-                                   int32_t m_tok, int32_t splits, float* Y) {
-    YK_ARG(e && W && X && Y && n_out > 0 && K > 0 && m_tok > 0, "arguments");
+extern "C" yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out,
+                                         int32_t K, int32_t m_tok, int32_t grid, int32_t reps, float* Y,
+                                         float* ms_per_rep, uint64_t* stamps, int32_t* grid_used) {
+    YK_ARG(e && W && X && Y && n_out > 0 && K > 0 && m_tok > 0 && reps > 0, "arguments");
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     yk_model m;
     m.e = e;
@@ -432,8 +630,14 @@ extern "C" yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16
         if (dY) cudaFree(dY);
         if (m.gemm_ws) cudaFree(m.gemm_ws);
         if (m.gemm_counters) cudaFree(m.gemm_counters);
+        if (m.gemm_stamps) cudaFree(m.gemm_stamps);
+        m.gemm_counters = nullptr;
+        m.gemm_stamps = nullptr;
     };
-    m.gemm_ws_floats = (size_t)2 * e->num_sms * 128 * 256;
+    // largest grid the launch can use: a forced stream-K grid, or a cluster grid
+    // (tiles x CS with tiles < SMs/2 and CS <= 8, or a forced CS on any tile count)
+    const int max_grid = std::max(std::max(grid, 4 * e->num_sms), 8 * ((n_out + 127) / 128) * ((m_tok + 255) / 256));
+    m.gemm_ws_floats = (size_t)2 * std::max(grid, e->num_sms) * 128 * 256;
     m.gemm_counter_cap = 4096;
     if (cudaMalloc(&dW, (size_t)n_out * K * 2) != cudaSuccess || cudaMalloc(&dX, (size_t)m_tok * K * 2) != cudaSuccess ||
         cudaMalloc(&dY, (size_t)m_tok * n_out * 4) != cudaSuccess ||
@@ -448,12 +652,31 @@ extern "C" yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16
     cudaMemcpy(dX, X, (size_t)m_tok * K * 2, cudaMemcpyHostToDevice);
     CUtensorMap tmW;
     yk_status s = yk::make_weight_map(e, &tmW, dW, n_out, K);
-    if (s == YK_OK) {
-        yk::EpiParams ep;
-        ep.kind = yk::EPI_STORE;
-        ep.out = dY;
-        s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, splits);
+    yk::EpiParams ep;
+    ep.kind = yk::EPI_STORE;
+    ep.out = dY;
+    if (s == YK_OK) s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, grid);  // result (and warm-up)
+    if (s == YK_OK && (reps > 1 || ms_per_rep || stamps)) {
+        if (stamps && cudaMalloc(&m.gemm_stamps, (size_t)max_grid * 8 * 8) != cudaSuccess) {
+            m.gemm_stamps = nullptr;
+            s = YK_ERR_OOM;
+        }
+        cudaEvent_t t0, t1;
+        cudaEventCreate(&t0);
+        cudaEventCreate(&t1);
+        cudaEventRecord(t0, e->stream);
+        for (int r = 0; r < reps && s == YK_OK; ++r) s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, grid);
+        cudaEventRecord(t1, e->stream);
+        cudaEventSynchronize(t1);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, t0, t1);
+        if (ms_per_rep) *ms_per_rep = ms / reps;
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+        if (stamps && m.gemm_stamps)
+            cudaMemcpy(stamps, m.gemm_stamps, (size_t)m.gemm_last_grid * 8 * 8, cudaMemcpyDeviceToHost);
     }
+    if (grid_used) *grid_used = m.gemm_last_grid;
     if (s == YK_OK) {
         cudaError_t ce = cudaStreamSynchronize(e->stream);
         if (ce == cudaSuccess) ce = cudaMemcpy(Y, dY, (size_t)m_tok * n_out * 4, cudaMemcpyDeviceToHost);
@@ -471,4 +694,9 @@ extern "C" yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16
     }
     cleanup();
     return s;
+}
+
+extern "C" yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K,
+                                   int32_t m_tok, int32_t grid, float* Y) {
+    return ykt_gemm_bf16_timed(e, W, X, n_out, K, m_tok, grid, 1, Y, nullptr, nullptr, nullptr);
 }

@@ -122,8 +122,11 @@ struct yk_model {
     // split-K partials + per-tile arrival counters
     float* gemm_ws = nullptr;
     size_t gemm_ws_floats = 0;
-    uint32_t* gemm_counters = nullptr;
+    uint32_t* gemm_counters = nullptr;  // owned apart from `allocations`: may grow
     int gemm_counter_cap = 0;
+    // GEMM phase timestamps (test hook only; null otherwise) and the last grid used
+    unsigned long long* gemm_stamps = nullptr;
+    int gemm_last_grid = 0;
     // attention split-KV partials
     float* attn_ws = nullptr;
     size_t attn_ws_floats = 0;
@@ -184,7 +187,7 @@ struct EpiParams {
 };
 
 yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const void* X, int n_out, int K, int m_tok,
-                   const EpiParams& ep, int force_splits = 0);
+                   const EpiParams& ep, int force_grid = 0);
 yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
 yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks,
                         double kv_bytes);
