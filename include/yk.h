@@ -207,6 +207,27 @@ yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float* draft_log
 /* Copies draft probabilities p[b][j][0..V) kept by yk_draft_sample (tests). */
 yk_status yk_sampler_read_probs(yk_sampler* s, int32_t b, int32_t j, float* host);
 
+/* Verification that allocates no device memory.  No counterpart in the
+ * reference: it exists for hosts that own all device memory themselves (a
+ * serving loop that carves every free byte of HBM into its own arenas at
+ * start-up cannot let a call allocate -- cudaMalloc may fail once the arenas
+ * own the memory, and it can synchronise the device mid-step).
+ * Same result as yk_spec_verify: verifySequence over target logits
+ * [B x (k+1) x V] and draft probabilities [B x k x V] (as yk_draft_sample
+ * keeps them), draft tokens [B x k], Philox stream ids [B]; outputs tokens
+ * [B x (k+1)] and counts [B].  Every pointer is DEVICE memory of `device`;
+ * the work is queued on `stream` (a cudaStream_t) and is complete when that
+ * stream is.  Its only scratch is a fixed 64 KB static device array (held by
+ * every GPU that loads libyk.so until exit), so B*(k+1) is limited to 4096
+ * rows; larger calls fail with YK_ERR_ARG.  The first call on a device looks
+ * the array's device address up (cudaGetSymbolAddress) and caches it.  All
+ * calls on a device share the array: calls that overlap on the GPU race. */
+yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream, const float* target_logits,
+                                        const float* draft_probs, const uint32_t* draft_tokens,
+                                        const uint32_t* seq_ids, int32_t B, int32_t k, int32_t V,
+                                        float temperature, uint64_t seed, uint32_t step, uint32_t* out_tokens,
+                                        int32_t* out_counts);
+
 #ifdef __cplusplus
 }
 #endif

@@ -94,6 +94,8 @@ _PROTOS = {
     "yk_spec_sample_logits": (C.c_int32, [_P, C.c_int32, _F32P, _F32P, C.c_float, C.c_uint64, C.c_uint32, _U32P,
                                           _U32P, _U32P, _I32P]),
     "yk_sampler_read_probs": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P]),
+    "yk_spec_verify_logits_noalloc": (C.c_int32, [C.c_int32, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32,
+                                                  C.c_float, C.c_uint64, C.c_uint32, _P, _P]),
     # include/yk_testing.h
     "ykt_gemm_bf16": (C.c_int32, [_P, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int32, C.c_int32,
                                   C.c_int32, C.c_int32, _F32P]),

@@ -14,6 +14,8 @@
 // the rest of the CTA stages the next chunk of summands in shared memory.
 #include <algorithm>
 #include <cstring>
+#include <mutex>
+#include <string>
 
 #include "yk_common.cuh"
 #include "yk_internal.h"
@@ -532,4 +534,93 @@ extern "C" yk_status yk_sampler_read_probs(yk_sampler* s, int32_t b, int32_t j, 
     YK_CHECK_CUDA(cudaMemcpy(host, s->probs + ((size_t)b * s->k + j) * s->vocab, (size_t)s->vocab * 4,
                              cudaMemcpyDeviceToHost));
     return YK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Verification that allocates nothing (yk_spec_verify_logits_noalloc in yk.h).
+//
+// For callers that cannot allocate device memory at this point: a serving host
+// that has handed all free HBM to its own arenas (weights, KV pages, its own
+// logit and probability buffers) at start-up.  For such a host a per-call
+// cudaMalloc is not an option: it can fail once the arenas own the memory, and
+// it may synchronise the whole device in the middle of a step.  This entry point
+// runs the same two kernels as yk_spec_verify on buffers the caller already owns
+// and keeps its only scratch -- the per-row softmax statistics -- in the fixed
+// array below.
+// ---------------------------------------------------------------------------
+// Largest B * (k+1) (target logit rows) one call may verify.
+constexpr int YK_NOALLOC_MAX_ROWS = 4096;
+
+// (max, sum, argmax, unused) per target row: 64 KB that every GPU loading
+// libyk.so holds until the process exits.  Every call on a device shares it and
+// each call rewrites every row it reads before reading it, so nothing has to
+// start at zero; calls that overlap on the GPU race on it.
+static __device__ __align__(256) float g_noalloc_row_stats[YK_NOALLOC_MAX_ROWS * 4];
+
+// Device address of g_noalloc_row_stats per device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per device
+// with that device current, on the first call there.
+static float* g_noalloc_stats_addr[64] = {};
+static std::mutex g_noalloc_mu;
+
+static yk_status noalloc_stats_address(int device, float** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    YK_ARG(device >= 0 && device < 64, "device index");
+    if (!g_noalloc_stats_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_row_stats);
+        if (e != cudaSuccess || !p) {
+            yk_set_error(std::string("cudaGetSymbolAddress(row statistics): ") + cudaGetErrorString(e));
+            return YK_ERR_CUDA;
+        }
+        g_noalloc_stats_addr[device] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_stats_addr[device];
+    return YK_OK;
+}
+
+extern "C" yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream, const float* target_logits,
+                                                   const float* draft_probs, const uint32_t* draft_tokens,
+                                                   const uint32_t* seq_ids, int32_t B, int32_t k, int32_t V,
+                                                   float temperature, uint64_t seed, uint32_t step,
+                                                   uint32_t* out_tokens, int32_t* out_counts) {
+    YK_ARG(target_logits && draft_probs && draft_tokens && seq_ids && out_tokens && out_counts, "null argument");
+    YK_ARG(B > 0 && k > 0 && k <= 16 && V > 0, "B, k or V out of range");
+    if ((int64_t)B * (k + 1) > YK_NOALLOC_MAX_ROWS) {
+        yk_set_error("yk_spec_verify_logits_noalloc: B*(k+1) = " + std::to_string((int64_t)B * (k + 1)) +
+                     " target rows exceed the fixed limit of " + std::to_string(YK_NOALLOC_MAX_ROWS));
+        return YK_ERR_ARG;
+    }
+    int prev = 0;
+    YK_CHECK_CUDA(cudaGetDevice(&prev));
+    YK_CHECK_CUDA(cudaSetDevice(device));
+    float* stats = nullptr;
+    yk_status s = noalloc_stats_address(device, &stats);
+    if (s == YK_OK) {
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        row_stats_kernel<<<B * (k + 1), SMP_THREADS, 0, st>>>(target_logits, V, temperature > 0.f ? temperature : 1.0f,
+                                                              stats);
+        VerifyArgs a;
+        a.q = target_logits;
+        a.stats = stats;
+        a.p = draft_probs;
+        a.drafts = draft_tokens;
+        a.V = V;
+        a.k = k;
+        a.from_logits = 1;
+        a.T = temperature;
+        a.seed = seed;
+        a.step = step;
+        a.seq_ids = seq_ids;
+        a.out = out_tokens;
+        a.counts = out_counts;
+        verify_kernel<<<B, SMP_THREADS, 0, st>>>(a);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            yk_set_error(std::string("yk_spec_verify_logits_noalloc launch: ") + cudaGetErrorString(e));
+            s = YK_ERR_CUDA;
+        }
+    }
+    cudaSetDevice(prev);
+    return s;
 }
