@@ -149,3 +149,70 @@ def test_sample_logits_matches_oracle(engine, oracle, T):
         if cnt[b] == r_cnt[b]:
             assert out[b, : cnt[b] - 1].tolist() == r_out[b, : cnt[b] - 1].tolist()
             assert abs(int(out[b, cnt[b] - 1]) - int(r_out[b, cnt[b] - 1])) <= 64
+
+
+def _stress_rows(rng, V):
+    """Probability rows that drive the exact chain through its special cases."""
+    rows = []
+    r = rng.integers(0, 16, V).astype(np.float32) / np.float32(4096)  # dyadic: frequent rounding ties
+    rows.append(r)
+    r = rng.random(V).astype(np.float32)
+    r[:3000] = 0.0                                                    # long +0 prefix
+    rows.append(r)
+    r = rng.random(V).astype(np.float32)
+    r[:200] = np.float32(1e-30)                                       # tiny head (c below 2^-100)
+    rows.append(r)
+    r = (10.0 ** rng.uniform(-20, 0, V)).astype(np.float32)           # huge dynamic range
+    rows.append(r)
+    r = np.full(V, 1e-8, np.float32)
+    r[V // 3] = 0.9                                                   # one dominant value mid-row
+    rows.append(r)
+    r = rng.random(V).astype(np.float32)
+    r[::7] = np.float32(1e-40)                                        # subnormals sprinkled in
+    rows.append(r)
+    r = np.zeros(V, np.float32)
+    r[-1] = 1.0                                                       # all mass on the last id
+    rows.append(r)
+    r = rng.random(V).astype(np.float32) * np.float32(0.5) / np.float32(V)  # sums to ~0.25: CDF fallback
+    rows.append(r)
+    return [x / np.float32(x.sum(dtype=np.float64)) if i not in (7,) else x for i, x in enumerate(rows)]
+
+
+def test_chain_exact_on_adversarial_rows(engine, oracle):
+    """Residual normaliser, residual CDF and bonus CDF on rows built to hit binade
+    crossings, ties, zero/tiny/subnormal states: bit-exact against the oracle."""
+    V, k = 20011, 1
+    rng = np.random.default_rng(77)
+    rows = _stress_rows(rng, V)
+    P, Q, D = [], [], []
+    for i, q0 in enumerate(rows):
+        for mode in range(3):
+            p = rng.random((k, V)).astype(np.float32)
+            p /= p.sum(dtype=np.float64)
+            q = np.stack([q0, rows[(i + 3) % len(rows)]]).astype(np.float32)
+            d = int(rng.integers(V))
+            if mode == 0:      # reject at position 0: residual chain over max(0, q - p)
+                p[0, d] = 1.0
+                q[0, d] = 0.0
+            elif mode == 1:    # accept everything: bonus chain over q[1]
+                p[0] = q[0]
+            else:              # residual sums to zero: fallback to q
+                p[0] = np.maximum(q[0], p[0])
+                p[0, d] = 1.0
+                q[0, d] = 0.0
+            P.append(p)
+            Q.append(q)
+            D.append([d])
+    P, Q, D = np.stack(P), np.stack(Q), np.array(D, np.uint32)
+    B = P.shape[0]
+    seq = np.arange(B, dtype=np.uint32)
+    s = abi.Sampler(engine, B, k, V)
+    try:
+        for step in range(4):
+            out, cnt = s.verify_probs(P, Q, D, 2024, step, seq)
+            r_out, r_cnt = oracle.verify_batch_probs(D, P, Q, 2024, step, seq)
+            np.testing.assert_array_equal(cnt, r_cnt)
+            for b in range(B):
+                assert out[b, : cnt[b]].tolist() == r_out[b, : r_cnt[b]].tolist(), f"row {b} step {step}"
+    finally:
+        s.close()

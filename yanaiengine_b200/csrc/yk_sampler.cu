@@ -17,13 +17,13 @@
 #include <mutex>
 #include <string>
 
+#include "yk_chain.cuh"
 #include "yk_common.cuh"
 #include "yk_internal.h"
 
 namespace yk {
 
-constexpr int SMP_THREADS = 512;
-constexpr int CHAIN_CH = 2048;
+constexpr int SMP_THREADS = CHAIN_THREADS;  // block_chain needs the whole block
 
 // Swift's max(0, y): y if y >= 0 else 0 (max(0, NaN) = 0, max(0, -0.0) = -0.0).
 __device__ __forceinline__ float swift_max0(float y) { return (y >= 0.0f) ? y : 0.0f; }
@@ -42,19 +42,45 @@ struct RowStats {
 };
 
 // Block-wide (max, sum-exp, first argmax) of x_i = l_i / T over one row.
+// Each thread visits its indices in increasing order (first maximum wins);
+// float4 loads, two in flight per iteration, when the row is 16-byte aligned.
+__device__ __forceinline__ void stats_update(float raw, int idx, float T, float& m, float& s, float& best, int& arg) {
+    const float x = scale_t(raw, T);
+    if (raw > best) { best = raw; arg = idx; }
+    if (x > m) {
+        s = s * expf(m - x) + 1.0f;
+        m = x;
+    } else {
+        s += expf(x - m);
+    }
+}
+
 __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, float T) {
     float m = -INFINITY, s = 0.f, best = -INFINITY;
     int arg = 0x7fffffff;
-    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-        const float raw = row[i];
-        const float x = scale_t(raw, T);
-        if (raw > best) { best = raw; arg = (int)i; }
-        if (x > m) {
-            s = s * expf(m - x) + 1.0f;
-            m = x;
-        } else {
-            s += expf(x - m);
+    if ((V & 3) == 0 && ((uintptr_t)row & 15) == 0) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        const int64_t n4 = V >> 2;
+        const int64_t step = 2 * (int64_t)blockDim.x;
+        for (int64_t i = threadIdx.x; i < n4; i += step) {
+            const float4 a = __ldg(r4 + i);
+            const bool has_b = i + blockDim.x < n4;
+            const float4 b = has_b ? __ldg(r4 + i + blockDim.x) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int ia = (int)(i * 4);
+            stats_update(a.x, ia, T, m, s, best, arg);
+            stats_update(a.y, ia + 1, T, m, s, best, arg);
+            stats_update(a.z, ia + 2, T, m, s, best, arg);
+            stats_update(a.w, ia + 3, T, m, s, best, arg);
+            if (has_b) {
+                const int ib = (int)((i + blockDim.x) * 4);
+                stats_update(b.x, ib, T, m, s, best, arg);
+                stats_update(b.y, ib + 1, T, m, s, best, arg);
+                stats_update(b.z, ib + 2, T, m, s, best, arg);
+                stats_update(b.w, ib + 3, T, m, s, best, arg);
+            }
         }
+    } else {
+        for (int64_t i = threadIdx.x; i < V; i += blockDim.x) stats_update(row[i], (int)i, T, m, s, best, arg);
     }
     __shared__ float sm_m[32], sm_s[32], sm_b[32];
     __shared__ int sm_a[32];
@@ -96,69 +122,6 @@ __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, fl
     RowStats r{sm_m[0], sm_s[0], sm_a[0]};
     __syncthreads();
     return r;
-}
-
-// The reference's sequential fp32 chain c = fl(c + f(i)), i = 0..n-1.
-// search: returns the first i with r <= c (sampleFromProbs), or n-1.
-// !search: returns -1 and the final sum in *sum.
-// Thread 0 adds in index order; threads 1.. stage the next chunk meanwhile.
-struct ChainSmem {
-    __align__(16) float buf[2][CHAIN_CH];
-    long long found_slot[2];
-    float cdf;
-};
-
-template <class F>
-__device__ int64_t block_chain(ChainSmem& cs, F f, int64_t n, bool search, float r, float* sum) {
-    auto& buf = cs.buf;
-    auto& found_slot = cs.found_slot;
-    float& s_cdf = cs.cdf;
-    const int64_t nch = (n + CHAIN_CH - 1) / CHAIN_CH;
-    for (int i = threadIdx.x; i < CHAIN_CH; i += blockDim.x) buf[0][i] = i < n ? f((int64_t)i) : 0.f;
-    if (threadIdx.x == 0) { s_cdf = 0.f; found_slot[0] = -1; found_slot[1] = -1; }
-    __syncthreads();
-    int64_t found = -1;
-    for (int64_t c = 0; c < nch; ++c) {
-        const float* cur = buf[c & 1];
-        float* nxt = buf[(c + 1) & 1];
-        if (threadIdx.x == 0) {
-            float cdf = s_cdf;
-            const int64_t rem = n - c * CHAIN_CH;
-            const int len = rem < CHAIN_CH ? (int)rem : CHAIN_CH;
-            long long hit = -1;
-            int i = 0;
-            for (; i + 4 <= len; i += 4) {
-                const float4 v = *reinterpret_cast<const float4*>(cur + i);
-                cdf = __fadd_rn(cdf, v.x);
-                if (search && r <= cdf) { hit = c * CHAIN_CH + i; break; }
-                cdf = __fadd_rn(cdf, v.y);
-                if (search && r <= cdf) { hit = c * CHAIN_CH + i + 1; break; }
-                cdf = __fadd_rn(cdf, v.z);
-                if (search && r <= cdf) { hit = c * CHAIN_CH + i + 2; break; }
-                cdf = __fadd_rn(cdf, v.w);
-                if (search && r <= cdf) { hit = c * CHAIN_CH + i + 3; break; }
-            }
-            if (hit < 0)
-                for (; i < len; ++i) {
-                    cdf = __fadd_rn(cdf, cur[i]);
-                    if (search && r <= cdf) { hit = c * CHAIN_CH + i; break; }
-                }
-            s_cdf = cdf;
-            found_slot[c & 1] = hit;
-        } else if (c + 1 < nch) {
-            const int64_t base = (c + 1) * CHAIN_CH;
-            for (int i = threadIdx.x - 1; i < CHAIN_CH; i += blockDim.x - 1)
-                nxt[i] = (base + i < n) ? f(base + i) : 0.f;
-        }
-        __syncthreads();
-        found = found_slot[c & 1];  // written by thread 0 every chunk; double-buffered
-        if (found >= 0) break;
-    }
-    const float total = s_cdf;
-    __syncthreads();
-    if (sum) *sum = total;
-    if (!search) return -1;
-    return found >= 0 ? found : n - 1;  // :72 fallback to the last token
 }
 
 // ---------------------------------------------------------------------------
@@ -207,10 +170,20 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
         tok = (uint32_t)st.arg;
     } else {
         const float T = a.T, m = st.m, s = st.s;
-        for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = q_from_logit(row[i], T, m, s);
+        if ((V & 3) == 0 && ((uintptr_t)row & 15) == 0 && ((uintptr_t)p & 15) == 0) {
+            const float4* r4 = reinterpret_cast<const float4*>(row);
+            float4* p4 = reinterpret_cast<float4*>(p);
+            for (int64_t i = threadIdx.x; i < (V >> 2); i += blockDim.x) {
+                const float4 l = __ldg(r4 + i);
+                p4[i] = make_float4(q_from_logit(l.x, T, m, s), q_from_logit(l.y, T, m, s), q_from_logit(l.z, T, m, s),
+                                    q_from_logit(l.w, T, m, s));
+            }
+        } else {
+            for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = q_from_logit(row[i], T, m, s);
+        }
+        __syncthreads();  // p is complete and visible to the whole block
         const float r = uniform_at(a.seed, a.step, a.seq_ids[b], (uint32_t)j, SLOT_DRAFT);
-        tok = (uint32_t)block_chain(cs, [&](int64_t i) { return q_from_logit(row[i], T, m, s); }, V, true, r,
-                                    nullptr);
+        tok = (uint32_t)block_chain(cs, [&](int64_t i) { return p[i]; }, V, true, r, nullptr);
     }
     if (threadIdx.x == 0) {
         if (a.j_fixed >= 0) a.tokens_out[b] = tok;
