@@ -19,9 +19,13 @@ extern "C" {
 yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K, int32_t m_tok,
                         int32_t grid, float* Y);
 /* Same, then `reps` back-to-back launches timed with CUDA events
- * (*ms_per_rep); stamps (grid x 8, may be null) receives the last launch's
+ * (*ms_per_rep).  reps < 0: -reps launches, each after a 256 MB write that
+ * evicts the weights from L2, timed one by one (mean of the single-launch
+ * times: the cold-weight case of a forward step).  stamps (grid x 8, may be
+ * null) receives the last launch's
  * per-CTA %globaltimer phase stamps: start, first TMA issued, first stage
- * landed, last MMA issued, last accumulator ready, epilogue done, segments. */
+ * landed, last MMA issued, last accumulator ready, epilogue done, segments,
+ * cluster barrier passed (cluster split-K). */
 yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K,
                               int32_t m_tok, int32_t grid, int32_t reps, float* Y, float* ms_per_rep,
                               uint64_t* stamps, int32_t* grid_used);

@@ -201,7 +201,8 @@ def gemm_bf16_test(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, gri
 
 
 def gemm_bf16_timed(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, grid: int = 0, reps: int = 10):
-    """(Y, ms per launch, per-CTA phase stamps [grid x 8], grid used) of the tcgen05 GEMM test hook."""
+    """(Y, ms per launch, per-CTA phase stamps [grid x 8], grid used) of the tcgen05 GEMM test hook.
+    reps < 0 times -reps launches one by one, each after an L2 flush."""
     n_out, K = W_bits.shape
     m_tok = X_bits.shape[0]
     W_bits = np.ascontiguousarray(W_bits, dtype=np.uint16)

@@ -3,6 +3,7 @@
 // LlamaBlock.forwardBatched, S/LlamaBlock.swift:178-276).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -66,6 +67,8 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
         return YK_ERR_CUDA;
     }
     e->encode_tiled = (PFN_tmapEncodeTiled)fn;
+    if (const char* v = std::getenv("YK_PDL")) e->pdl = std::strcmp(v, "0") != 0;
+    if (const char* v = std::getenv("YK_GEMM_VARIANT")) e->gemm_variant = std::atoi(v);
     yk_status s = e->ensure_pinned((size_t)4 << 20);
     if (s != YK_OK) { delete e; return s; }
     *out = e;

@@ -58,6 +58,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 // ---------------------------------------------------------------------------
 template <typename AT, int DPL>
 __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gw = blockIdx.x * 4 + warp;
     if (gw >= p.T * p.H) return;
@@ -176,6 +178,8 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
     __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
     __nv_bfloat16* sK = sQ + C::Q_ELEMS;        // [2][KC][LD]
     __nv_bfloat16* sV = sK + 2 * C::KV_ELEMS;   // [2][KC][LD]
+    pdl_trigger();
+    pdl_wait();
 
     const int32_t* it = p.items + (size_t)blockIdx.x * 6;
     const int b = it[0], g = it[1], qt = it[2], kbeg = it[3], kend = it[4], slot = it[5];
@@ -404,6 +408,8 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
 // Split-KV merge: one CTA per (sequence, KV head, query tile) with > 1 split.
 template <int DH>
 __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int32_t* e = p.comb + (size_t)blockIdx.x * 5;
     const int b = e[0], g = e[1], qt = e[2], first = e[3], ns = e[4];
     const int G = p.H / p.Hkv;
@@ -430,13 +436,13 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
 }
 
 template <typename AT>
-static void launch_simt(const AttnParams& p, cudaStream_t st) {
+static cudaError_t launch_simt(const AttnParams& p, yk_engine* e) {
     const int warps = p.T * p.H;
     const int blocks = (warps + 3) / 4;
     switch (p.dh) {
-        case 64: attn_simt_kernel<AT, 2><<<blocks, 128, 0, st>>>(p); break;
-        case 128: attn_simt_kernel<AT, 4><<<blocks, 128, 0, st>>>(p); break;
-        default: attn_simt_kernel<AT, 8><<<blocks, 128, 0, st>>>(p); break;
+        case 64: return launch_pdl(e, attn_simt_kernel<AT, 2>, blocks, 128, 0, p);
+        case 128: return launch_pdl(e, attn_simt_kernel<AT, 4>, blocks, 128, 0, p);
+        default: return launch_pdl(e, attn_simt_kernel<AT, 8>, blocks, 128, 0, p);
     }
 }
 
@@ -448,13 +454,11 @@ static yk_status launch_mma(const AttnParams& p, int n_items, int n_comb, yk_eng
         YK_CHECK_CUDA(cudaFuncSetAttribute(attn_mma_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr = true;
     }
-    attn_mma_kernel<DH><<<n_items, 128, smem, e->stream>>>(p);
+    YK_CHECK_CUDA(launch_pdl(e, attn_mma_kernel<DH>, n_items, 128, smem, p));
     e->launches++;
-    YK_CHECK_CUDA(cudaGetLastError());
     if (n_comb > 0) {
-        attn_combine_kernel<DH><<<n_comb, 128, 0, e->stream>>>(p);
+        YK_CHECK_CUDA(launch_pdl(e, attn_combine_kernel<DH>, n_comb, 128, 0, p));
         e->launches++;
-        YK_CHECK_CUDA(cudaGetLastError());
     }
     return YK_OK;
 }
@@ -533,9 +537,8 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
     p.err = m->e->d_err;
     p.ws = m->attn_ws;
     if (c.dtype != YK_DTYPE_BF16) {
-        launch_simt<float>(p, m->e->stream);
+        YK_CHECK_CUDA(launch_simt<float>(p, m->e));
         m->e->launches++;
-        YK_CHECK_CUDA(cudaGetLastError());
         return YK_OK;
     }
     const int w = windowed ? 1 : 0;

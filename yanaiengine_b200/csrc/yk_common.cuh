@@ -73,6 +73,18 @@ __device__ __forceinline__ void raise_err(uint32_t* err, uint32_t bits) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of the forward step is launched
+// so that it may start while the previous kernel of the stream finishes:
+// pdl_trigger lets the next kernel launch, pdl_wait blocks until the previous
+// kernel has completed and its writes are visible.  Each kernel calls pdl_wait
+// on every path before it reads or writes data another kernel touches (and
+// before it exits), so completion stays ordered along the stream.  Both are
+// no-ops for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // mbarrier (shared::cta) helpers.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

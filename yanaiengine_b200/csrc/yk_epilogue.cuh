@@ -164,6 +164,12 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
     }
 }
 
+// Residual add of rows n..n+3 of token j whose current values h were loaded by the caller.
+__device__ __forceinline__ void epi_quad_resid(const EpiParams& p, int n, int j, float4 v, float4 h) {
+    if (p.ref_compat) { v.x = compat_relu(v.x); v.y = compat_relu(v.y); v.z = compat_relu(v.z); v.w = compat_relu(v.w); }
+    *reinterpret_cast<float4*>(p.h + (size_t)j * p.ld + n) = make_float4(h.x + v.x, h.y + v.y, h.z + v.z, h.w + v.w);
+}
+
 // Rows n..n+3 (n % 4 == 0; n_out is a multiple of 4) of token j with one vector
 // store (split-tile reductions).
 template <int KIND, typename AT>

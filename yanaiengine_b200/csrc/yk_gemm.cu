@@ -40,9 +40,10 @@ struct TcArgs {
     int n_out, K, m_tok;
     int tiles_m, kb_total;      // k-blocks per tile
     int BN, stages;
-    long long units;            // tiles * kb_total
+    int tiles;                  // tiles_m * tiles_n
     int grid;
     int cluster_s;              // > 0: cluster split-K with cluster_s CTAs per tile
+    int sk_tiles, sk_ctas;      // stream-K part: tiles [0, sk_tiles) cut over CTAs [0, sk_ctas)
     uint32_t idesc, tmem_cols;  // columns of one accumulator stage
     float* ws;                  // stream-K partials: slot (2*cta + first/last) x [BN][128]
     uint32_t* counters;         // per-tile arrival counters (zero between launches)
@@ -51,7 +52,9 @@ struct TcArgs {
 };
 
 // Phase timestamps of one CTA (ns, %globaltimer), recorded only when a.stamps != null.
-enum : int { ST_START = 0, ST_FIRST_TMA, ST_FIRST_FULL, ST_LAST_MMA, ST_LAST_ACC, ST_EPI_DONE, ST_SEGS, ST_N = 8 };
+enum : int {
+    ST_START = 0, ST_FIRST_TMA, ST_FIRST_FULL, ST_LAST_MMA, ST_LAST_ACC, ST_EPI_DONE, ST_SEGS, ST_CLUSTER, ST_N = 8
+};
 __device__ __forceinline__ void stamp(const TcArgs& a, int what) {
     if (a.stamps) a.stamps[(size_t)blockIdx.x * ST_N + what] = globaltimer_ns();
 }
@@ -61,14 +64,122 @@ __device__ __forceinline__ long long unit_begin(int c, long long U, int G) { ret
 __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
     return (int)(((u + 1) * G + U - 1) / U) - 1;
 }
-__device__ __forceinline__ int partial_slot(int cta, int tile, long long U, int G, int KB) {
-    return 2 * cta + ((long long)tile == unit_begin(cta, U, G) / KB ? 0 : 1);
+
+// This CTA's work, fixed at kernel start:
+//  * cluster split-K: one segment, k-blocks [r*KB/CS, (r+1)*KB/CS) of tile c/CS.
+//  * otherwise: first this CTA's equal share of the stream-K units of tiles
+//    [0, sk_tiles) (nrem segments, the first and last possibly cut with a
+//    neighbour), then whole tiles sk_tiles + c + w*grid.  Cut tiles are
+//    finished early, while the whole tiles stream, so no fix-up sits at the end.
+struct TcSched {
+    int nrem, t0, kbf, kbl;  // remainder segments: tiles t0.., first from kbf, last up to kbl
+};
+__device__ __forceinline__ TcSched tc_sched(const TcArgs& a, int c) {
+    TcSched r;
+    const int KB = a.kb_total;
+    r.nrem = 0;
+    r.t0 = 0;
+    r.kbf = 0;
+    r.kbl = KB;
+    if (a.cluster_s > 0) {
+        const int q = c % a.cluster_s;
+        r.nrem = 1;
+        r.t0 = c / a.cluster_s;
+        r.kbf = q * KB / a.cluster_s;
+        r.kbl = (q + 1) * KB / a.cluster_s;
+    } else if (c < a.sk_ctas) {
+        const long long RU = (long long)a.sk_tiles * KB;
+        const long long u0 = unit_begin(c, RU, a.sk_ctas), u1 = unit_begin(c + 1, RU, a.sk_ctas);
+        if (u1 > u0) {
+            r.t0 = (int)(u0 / KB);
+            r.nrem = (int)((u1 - 1) / KB) - r.t0 + 1;
+            r.kbf = (int)(u0 - (long long)r.t0 * KB);
+            r.kbl = (int)(u1 - (long long)(r.t0 + r.nrem - 1) * KB);
+        }
+    }
+    return r;
+}
+// Segment i: tile and k-block range [kb0, kb1); false past the end.
+__device__ __forceinline__ bool tc_segment(const TcArgs& a, const TcSched& sc, int c, int i, int& tile, int& kb0,
+                                           int& kb1) {
+    if (i < sc.nrem) {
+        tile = sc.t0 + i;
+        kb0 = i == 0 ? sc.kbf : 0;
+        kb1 = i == sc.nrem - 1 ? sc.kbl : a.kb_total;
+        return true;
+    }
+    if (a.cluster_s > 0) return false;
+    tile = a.sk_tiles + c + (i - sc.nrem) * a.grid;
+    kb0 = 0;
+    kb1 = a.kb_total;
+    return tile < a.tiles;
+}
+// Partial slot of stream-K CTA cta for cut tile `tile`.
+__device__ __forceinline__ int partial_slot(const TcArgs& a, int cta, int tile) {
+    const long long RU = (long long)a.sk_tiles * a.kb_total;
+    return 2 * cta + ((long long)tile == unit_begin(cta, RU, a.sk_ctas) / a.kb_total ? 0 : 1);
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void epi_bar_sync() {  // named barrier over the 4 epilogue warps
     asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Cluster reduction of columns [c0, c1) of tile (tm, tn): sums the CS partials
+// parked in the cluster's shared memory in rank order.  QN items per thread and
+// round keep QN*CS distributed-shared-memory loads in flight.
+template <int KIND, int CS>
+__device__ __forceinline__ void cluster_reduce(const TcArgs& a, uint32_t red_addr, int tm, int tn, int c0, int c1,
+                                               bool ok) {
+    constexpr int QN = CS >= 16 ? 1 : 16 / CS;
+    const int nitems = (c1 - c0) * 32;  // (column, 4-row group) items
+    uint32_t rb[CS];
+#pragma unroll
+    for (int s = 0; s < CS; ++s) rb[s] = mapa_shared(red_addr, (uint32_t)s);
+    for (int base = threadIdx.x; base < nitems; base += TC_THREADS * QN) {
+        float4 tv[QN][CS];
+        float4 hv[KIND == EPI_RESID ? QN : 1];
+        if constexpr (KIND == EPI_RESID) {
+            // the residual stream values, in flight together with the partials
+#pragma unroll
+            for (int q = 0; q < QN; ++q) {
+                const int it = base + q * TC_THREADS;
+                const int n = tm * TC_BM + (it % 32) * 4, j = tn * a.BN + c0 + it / 32;
+                if (ok && it < nitems && j < a.epi.m_tok && n < a.epi.n_out)
+                    hv[q] = *reinterpret_cast<const float4*>(a.epi.h + (size_t)j * a.epi.ld + n);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < QN; ++q) {
+            const int it = base + q * TC_THREADS;
+            if (it < nitems) {
+                const uint32_t off = (uint32_t)(((c0 + it / 32) * TC_BM + (it % 32) * 4) * 4);
+#pragma unroll
+                for (int s = 0; s < CS; ++s) tv[q][s] = ld_shared_cluster_v4(rb[s] + off);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < QN; ++q) {
+            const int it = base + q * TC_THREADS;
+            if (ok && it < nitems) {
+                float4 acc = tv[q][0];
+#pragma unroll
+                for (int s = 1; s < CS; ++s) {
+                    acc.x += tv[q][s].x;
+                    acc.y += tv[q][s].y;
+                    acc.z += tv[q][s].z;
+                    acc.w += tv[q][s].w;
+                }
+                const int n = tm * TC_BM + (it % 32) * 4, j = tn * a.BN + c0 + it / 32;
+                if constexpr (KIND == EPI_RESID) {
+                    if (j < a.epi.m_tok && n < a.epi.n_out) epi_quad_resid(a.epi, n, j, acc, hv[q]);
+                } else {
+                    epi_quad<KIND, __nv_bfloat16>(a.epi, n, j, acc);
+                }
+            }
+        }
+    }
 }
 
 template <int KIND>
@@ -87,18 +198,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int c = blockIdx.x, G = a.grid, KB = a.kb_total;
-    const long long U = a.units;
+    const int c = blockIdx.x, KB = a.kb_total;
     const int CS = a.cluster_s;
-    long long u0, u1;
-    if (CS > 0) {  // CTA r of cluster t owns k-blocks [r*KB/CS, (r+1)*KB/CS) of tile t
-        const long long t = c / CS, r = c % CS;
-        u0 = t * KB + r * KB / CS;
-        u1 = t * KB + (r + 1) * KB / CS;
-    } else {       // an equal contiguous share of all (tile, k-block) units
-        u0 = unit_begin(c, U, G);
-        u1 = unit_begin(c + 1, U, G);
-    }
+    const TcSched sc = tc_sched(a, c);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -116,50 +218,63 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_trigger();
     const uint32_t tmem = *tmem_slot;
     if (threadIdx.x == 0) stamp(a, ST_START);
+    // Everything but the weight prefetch below reads or writes what earlier kernels touch.
+    if (threadIdx.x != 0) pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
-            long long g = 0;
-            for (long long u = u0; u < u1 && !flags[0];) {
-                const int t = (int)(u / KB);
-                const long long e = min(u1, (long long)(t + 1) * KB);
-                const int tm = t % a.tiles_m, tn = t / a.tiles_m;
-                for (long long uu = u; uu < e; ++uu, ++g) {
-                    const int s = (int)(g % S);
-                    const long long r = g / S;
-                    if (r > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (uint32_t)((r - 1) & 1))) {
-                        flags[0] = 1;
-                        raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
-                        break;
-                    }
-                    const uint32_t wdst = smem_u32(smem + (size_t)s * stage_bytes);
-                    const uint32_t fb = smem_u32(&full[s]);
-                    const int kb = (int)(uu - (long long)t * KB);
+            int t, k0, k1;
+            // The weights do not depend on the previous kernel: fill the ring with
+            // them while that kernel finishes.
+            long long pre = 0;
+            for (int i = 0; pre < S && tc_segment(a, sc, c, i, t, k0, k1); ++i)
+                for (int kb = k0; kb < k1 && pre < S; ++kb, ++pre) {
+                    const uint32_t fb = smem_u32(&full[pre]);
                     mbar_arrive_expect_tx(fb, stage_bytes);
-                    tma_load_2d(wdst, &tmW, kb * TC_BK, tm * TC_BM, fb, pol_w);
-                    tma_load_2d(wdst + 16384u, &tmX, kb * TC_BK, tn * BN, fb, pol_x);
+                    tma_load_2d(smem_u32(smem + (size_t)pre * stage_bytes), &tmW, kb * TC_BK, (t % a.tiles_m) * TC_BM,
+                                fb, pol_w);
+                }
+            pdl_wait();  // the activations are the previous kernel's output
+            long long g = 0;
+            bool stop = false;
+            for (int i = 0; !stop && tc_segment(a, sc, c, i, t, k0, k1); ++i) {
+                const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+                for (int kb = k0; kb < k1; ++kb, ++g) {
+                    const int s = (int)(g % S);
+                    const uint32_t sdst = smem_u32(smem + (size_t)s * stage_bytes);
+                    const uint32_t fb = smem_u32(&full[s]);
+                    if (g >= pre) {
+                        const long long r = g / S;
+                        if (flags[0] || (r > 0 && !mbar_wait_bounded(smem_u32(&empty[s]), (uint32_t)((r - 1) & 1)))) {
+                            if (!flags[0]) raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
+                            flags[0] = 1;
+                            stop = true;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(fb, stage_bytes);
+                        tma_load_2d(sdst, &tmW, kb * TC_BK, tm * TC_BM, fb, pol_w);
+                    }
+                    tma_load_2d(sdst + 16384u, &tmX, kb * TC_BK, tn * BN, fb, pol_x);
                     if (g == 0) stamp(a, ST_FIRST_TMA);
                 }
-                u = e;
             }
             // Every issued copy must land before shared memory is reused or released.
             const long long issued = g;
-            for (long long i = max(0LL, issued - S); i < issued; ++i)
-                (void)mbar_wait_bounded(smem_u32(&full[i % S]), (uint32_t)((i / S) & 1));
+            for (long long j = max(0LL, issued - S); j < issued; ++j)
+                (void)mbar_wait_bounded(smem_u32(&full[j % S]), (uint32_t)((j / S) & 1));
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             long long g = 0;
-            int seg = 0;
-            for (long long u = u0; u < u1 && !flags[0]; ++seg) {
-                const int t = (int)(u / KB);
-                const long long e = min(u1, (long long)(t + 1) * KB);
+            int seg = 0, t, k0, k1;
+            for (; !flags[0] && tc_segment(a, sc, c, seg, t, k0, k1); ++seg) {
                 const int st = seg & 1;
                 if (seg >= 2 && !mbar_wait_bounded(smem_u32(&acc_empty[st]), (uint32_t)(((seg >> 1) - 1) & 1))) {
                     flags[0] = 1;
@@ -169,7 +284,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)st * a.tmem_cols;
                 bool ok = true;
-                for (long long uu = u; uu < e; ++uu, ++g) {
+                for (int kb = k0; kb < k1; ++kb, ++g) {
                     const int s = (int)(g % S);
                     if (!mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)((g / S) & 1))) {
                         flags[0] = 1;
@@ -183,12 +298,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk)
                         tc_mma_bf16(d, sw128_kmajor_desc(wsm + kk * 32), sw128_kmajor_desc(wsm + 16384u + kk * 32),
-                                    a.idesc, (uu > u || kk > 0) ? 1u : 0u);
+                                    a.idesc, (kb > k0 || kk > 0) ? 1u : 0u);
                     tc_commit(smem_u32(&empty[s]));
                 }
                 tc_commit(smem_u32(&acc_full[st]));
                 if (!ok) break;
-                u = e;
             }
             stamp(a, ST_LAST_MMA);
             if (a.stamps) a.stamps[(size_t)blockIdx.x * ST_N + ST_SEGS] = (unsigned long long)seg;
@@ -198,11 +312,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;           // TMEM lane quadrant this warp may read
         const int row = q * 32 + lane;    // output row within the tile
         const int et = threadIdx.x - 64;  // 0..127
-        int seg = 0;
-        for (long long u = u0; u < u1; ++seg) {
-            const int t = (int)(u / KB);
-            const long long e = min(u1, (long long)(t + 1) * KB);
-            const int kb_b = (int)(u - (long long)t * KB), kb_e = (int)(e - (long long)t * KB);
+        int t, kb_b, kb_e;
+        for (int seg = 0; tc_segment(a, sc, c, seg, t, kb_b, kb_e); ++seg) {
             const int st = seg & 1;
             // One thread waits (bounded) and broadcasts, so the epilogue warps always
             // take the same path through their named barriers.
@@ -216,7 +327,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             epi_bar_sync();
             if (flags[2 + st]) break;
             tc_fence_after();
-            if (et == 0 && e == u1) stamp(a, ST_LAST_ACC);
+            if (et == 0) stamp(a, ST_LAST_ACC);
             const uint32_t taddr = tmem + (uint32_t)st * a.tmem_cols + ((uint32_t)(q * 32) << 16);
             const int tm = t % a.tiles_m, tn = t / a.tiles_m;
             const int n = tm * TC_BM + row;
@@ -243,10 +354,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             } else {
                 // tile cut across CTAs: publish this partial; the last arriver finishes the tile
-                const int c_lo = cta_of_unit((long long)t * KB, U, G);
-                const int c_hi = cta_of_unit((long long)(t + 1) * KB - 1, U, G);
+                const long long RU = (long long)a.sk_tiles * KB;
+                const int c_lo = cta_of_unit((long long)t * KB, RU, a.sk_ctas);
+                const int c_hi = cta_of_unit((long long)(t + 1) * KB - 1, RU, a.sk_ctas);
                 const int nseg = c_hi - c_lo + 1;
-                float* mine = a.ws + (size_t)partial_slot(c, t, U, G, KB) * TC_BM * BN;
+                float* mine = a.ws + (size_t)partial_slot(a, c, t) * TC_BM * BN;
                 for (int cc = 0; cc < BN; cc += 16) {
                     uint32_t r[16];
                     tmem_ld16(taddr + (uint32_t)cc, r);
@@ -273,7 +385,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             for (int s4 = 0; s4 < 4; ++s4) {
                                 if (sg0 + s4 < nseg) {
                                     const float* src =
-                                        a.ws + (size_t)partial_slot(c_lo + sg0 + s4, t, U, G, KB) * TC_BM * BN + r4;
+                                        a.ws + (size_t)partial_slot(a, c_lo + sg0 + s4, t) * TC_BM * BN + r4;
 #pragma unroll
                                     for (int i = 0; i < 8; ++i) {
                                         const int col = cc + cq + 4 * i;
@@ -307,7 +419,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             tc_fence_before();
             mbar_arrive(smem_u32(&acc_empty[st]));
-            u = e;
         }
         if (et == 0) stamp(a, ST_EPI_DONE);
     }
@@ -318,43 +429,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // the barrier.  Rank r sums columns [r*BN/CS, (r+1)*BN/CS) over all ranks in
         // rank order through distributed shared memory and runs their epilogue.
         cluster_sync_any();
+        if (threadIdx.x == 64) stamp(a, ST_CLUSTER);
         const uint32_t rank = cluster_ctarank();
         const int t = c / CS;
         const int tm = t % a.tiles_m, tn = t / a.tiles_m;
         const int c0 = (int)(rank * (uint32_t)BN / (uint32_t)CS);
         const int c1 = (int)((rank + 1) * (uint32_t)BN / (uint32_t)CS);
-        const int nitems = (c1 - c0) * 32;  // (column, 4-row group) items
         const uint32_t red_addr = smem_u32(smem);
         const bool ok = flags[0] == 0;
-        for (int base = threadIdx.x; base < nitems; base += TC_THREADS * 4) {
-            float4 acc[4];
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) acc[q4] = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int s = 0; s < CS; ++s) {
-                const uint32_t rb = mapa_shared(red_addr, (uint32_t)s);
-                float4 tv[4];
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const int it = base + q4 * TC_THREADS;
-                    if (it < nitems)
-                        tv[q4] = ld_shared_cluster_v4(rb + (uint32_t)(((c0 + it / 32) * TC_BM + (it % 32) * 4) * 4));
-                }
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    if (base + q4 * TC_THREADS < nitems) {
-                        acc[q4].x += tv[q4].x;
-                        acc[q4].y += tv[q4].y;
-                        acc[q4].z += tv[q4].z;
-                        acc[q4].w += tv[q4].w;
-                    }
-                }
-            }
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                const int it = base + q4 * TC_THREADS;
-                if (ok && it < nitems)
-                    epi_quad<KIND, __nv_bfloat16>(a.epi, tm * TC_BM + (it % 32) * 4, tn * BN + c0 + it / 32, acc[q4]);
-            }
+        switch (CS) {
+            case 1: cluster_reduce<KIND, 1>(a, red_addr, tm, tn, c0, c1, ok); break;
+            case 2: cluster_reduce<KIND, 2>(a, red_addr, tm, tn, c0, c1, ok); break;
+            case 3: cluster_reduce<KIND, 3>(a, red_addr, tm, tn, c0, c1, ok); break;
+            case 4: cluster_reduce<KIND, 4>(a, red_addr, tm, tn, c0, c1, ok); break;
+            case 5: cluster_reduce<KIND, 5>(a, red_addr, tm, tn, c0, c1, ok); break;
+            case 6: cluster_reduce<KIND, 6>(a, red_addr, tm, tn, c0, c1, ok); break;
+            case 7: cluster_reduce<KIND, 7>(a, red_addr, tm, tn, c0, c1, ok); break;
+            default: cluster_reduce<KIND, 8>(a, red_addr, tm, tn, c0, c1, ok); break;
         }
         cluster_sync_any();  // no CTA releases shared memory a peer still reads
         if (threadIdx.x == 64) stamp(a, ST_EPI_DONE);
@@ -550,10 +641,25 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
         for (int s = (int)std::min<long long>(std::min(8, kb), e->num_sms / tiles); s >= 2 && cs == 0; --s)
             if (tiles <= cluster_capacity(e, s)) cs = s;
     }
+    // Otherwise: persistent CTAs (at least ~8 k-blocks each so each pipeline fills)
+    // take whole tiles round-robin; the tiles left over after the full waves are
+    // cut evenly over the CTAs (stream-K) and done first.
     int grid = (int)std::min<long long>(e->num_sms, std::max<long long>(1, units / 8));
     if (force_grid > 0) grid = (int)std::min<long long>(force_grid, units);
-    if (cs > 0) grid = (int)(tiles * cs);
-    YK_ARG(cs > 0 || (size_t)2 * grid * TC_BM * BN <= m->gemm_ws_floats, "split workspace too small");
+    int sk_tiles = 0, sk_ctas = 0;
+    if (cs > 0) {
+        grid = (int)(tiles * cs);
+    } else {
+        const long long waves = tiles / grid, rest = tiles % grid;
+        if (waves == 0 || (e->gemm_variant & 1)) {
+            sk_tiles = (int)tiles;
+            sk_ctas = grid;
+        } else if (rest > 0) {
+            sk_tiles = (int)rest;
+            sk_ctas = (int)std::min<long long>(grid, std::max<long long>(1, rest * kb / 8));
+        }
+    }
+    YK_ARG((size_t)2 * sk_ctas * TC_BM * BN <= m->gemm_ws_floats, "split workspace too small");
     if (tiles > m->gemm_counter_cap) {
         YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
         if (m->gemm_counters) cudaFree(m->gemm_counters);
@@ -575,7 +681,8 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     a.n_out = n_out; a.K = K; a.m_tok = m_tok;
     a.tiles_m = tiles_m; a.kb_total = kb;
     a.BN = BN; a.stages = stages;
-    a.units = units; a.grid = grid; a.cluster_s = cs;
+    a.tiles = (int)tiles; a.grid = grid; a.cluster_s = cs;
+    a.sk_tiles = sk_tiles; a.sk_ctas = sk_ctas;
     a.idesc = idesc_bf16_f32(TC_BM, BN);
     a.tmem_cols = cols;
     a.ws = m->gemm_ws;
@@ -588,13 +695,15 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = e->stream;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = cs > 0 ? cs : 1;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = (e->pdl && !e->profiling) ? 2 : 1;
     switch (ep.kind) {
         case EPI_QKV: YK_TRY(launch_tc<EPI_QKV>(cfg, tmW, tmX, a)); break;
         case EPI_RESID: YK_TRY(launch_tc<EPI_RESID>(cfg, tmW, tmX, a)); break;
@@ -616,18 +725,22 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
 extern "C" yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out,
                                          int32_t K, int32_t m_tok, int32_t grid, int32_t reps, float* Y,
                                          float* ms_per_rep, uint64_t* stamps, int32_t* grid_used) {
-    YK_ARG(e && W && X && Y && n_out > 0 && K > 0 && m_tok > 0 && reps > 0, "arguments");
+    YK_ARG(e && W && X && Y && n_out > 0 && K > 0 && m_tok > 0 && reps != 0, "arguments");
+    const bool cold = reps < 0;
+    if (cold) reps = -reps;
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     yk_model m;
     m.e = e;
     m.cfg.dtype = YK_DTYPE_BF16;
     m.cfg.max_tokens = m_tok;
-    void *dW = nullptr, *dX = nullptr, *dY = nullptr;
+    void *dW = nullptr, *dX = nullptr, *dY = nullptr, *dFlush = nullptr;
+    constexpr size_t kFlushBytes = size_t(256) << 20;
     auto cleanup = [&]() {
         cudaStreamSynchronize(e->stream);
         if (dW) cudaFree(dW);
         if (dX) cudaFree(dX);
         if (dY) cudaFree(dY);
+        if (dFlush) cudaFree(dFlush);
         if (m.gemm_ws) cudaFree(m.gemm_ws);
         if (m.gemm_counters) cudaFree(m.gemm_counters);
         if (m.gemm_stamps) cudaFree(m.gemm_stamps);
@@ -642,7 +755,8 @@ extern "C" yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const 
     if (cudaMalloc(&dW, (size_t)n_out * K * 2) != cudaSuccess || cudaMalloc(&dX, (size_t)m_tok * K * 2) != cudaSuccess ||
         cudaMalloc(&dY, (size_t)m_tok * n_out * 4) != cudaSuccess ||
         cudaMalloc(&m.gemm_ws, m.gemm_ws_floats * 4) != cudaSuccess ||
-        cudaMalloc(&m.gemm_counters, (size_t)m.gemm_counter_cap * 4) != cudaSuccess) {
+        cudaMalloc(&m.gemm_counters, (size_t)m.gemm_counter_cap * 4) != cudaSuccess ||
+        (cold && cudaMalloc(&dFlush, kFlushBytes) != cudaSuccess)) {
         cleanup();
         yk_set_error("ykt_gemm_bf16: cudaMalloc failed");
         return YK_ERR_OOM;
@@ -664,12 +778,25 @@ extern "C" yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const 
         cudaEvent_t t0, t1;
         cudaEventCreate(&t0);
         cudaEventCreate(&t1);
-        cudaEventRecord(t0, e->stream);
-        for (int r = 0; r < reps && s == YK_OK; ++r) s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, grid);
-        cudaEventRecord(t1, e->stream);
-        cudaEventSynchronize(t1);
         float ms = 0.f;
-        cudaEventElapsedTime(&ms, t0, t1);
+        if (cold) {
+            for (int r = 0; r < reps && s == YK_OK; ++r) {
+                cudaMemsetAsync(dFlush, r & 0xff, kFlushBytes, e->stream);
+                cudaEventRecord(t0, e->stream);
+                s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, grid);
+                cudaEventRecord(t1, e->stream);
+                cudaEventSynchronize(t1);
+                float one = 0.f;
+                cudaEventElapsedTime(&one, t0, t1);
+                ms += one;
+            }
+        } else {
+            cudaEventRecord(t0, e->stream);
+            for (int r = 0; r < reps && s == YK_OK; ++r) s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, grid);
+            cudaEventRecord(t1, e->stream);
+            cudaEventSynchronize(t1);
+            cudaEventElapsedTime(&ms, t0, t1);
+        }
         if (ms_per_rep) *ms_per_rep = ms / reps;
         cudaEventDestroy(t0);
         cudaEventDestroy(t1);

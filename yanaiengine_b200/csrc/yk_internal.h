@@ -59,6 +59,9 @@ struct yk_engine {
     size_t pinned_bytes = 0;
     uint64_t launches = 0;
     PFN_tmapEncodeTiled encode_tiled = nullptr;
+    bool pdl = true;                     // programmatic dependent launch (env YK_PDL=0 turns it off)
+    int gemm_variant = 0;                // GEMM schedule tuning knob (env YK_GEMM_VARIANT): bit 0 = pure
+                                         // stream-K instead of whole tiles + stream-K remainder
     bool profiling = false;
     std::vector<ProfRecord> prof_pending;
     std::vector<cudaEvent_t> prof_free;
@@ -157,6 +160,25 @@ struct yk_sampler {
 
 // ---- internal launchers ----------------------------------------------------
 namespace yk {
+
+// Launch on the engine stream with programmatic dependent launch (the kernel
+// must call pdl_wait before touching what earlier kernels wrote).  Off while
+// profiling: the per-launch events sit between kernels anyway.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(yk_engine* e, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = e->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = (e->pdl && !e->profiling) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 enum EpiKind : int { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GLU = 3, EPI_LOGITS = 4 };
 

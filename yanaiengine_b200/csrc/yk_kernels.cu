@@ -8,6 +8,8 @@ namespace yk {
 template <typename WT>
 __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict__ tokens, float* __restrict__ h,
                              int d, int V, uint32_t* err) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x;
     const int tok = tokens[t];
     if (tok < 0 || tok >= V) {
@@ -23,6 +25,8 @@ __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict
 template <typename AT>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ g, AT* __restrict__ y, int d,
                                float eps, const int32_t* __restrict__ rows) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const int src = rows ? rows[r] : r;
     const float* xr = x + (size_t)src * d;
@@ -67,25 +71,24 @@ __global__ void fill_kernel(T* __restrict__ out, size_t n, float v) {
 yk_status launch_embed(yk_model* m, const int32_t* tokens, int T) {
     const auto& c = m->cfg;
     if (c.dtype == YK_DTYPE_BF16)
-        embed_kernel<__nv_bfloat16><<<T, 256, 0, m->e->stream>>>((const __nv_bfloat16*)m->embed, tokens, m->h,
-                                                                  c.d_model, c.vocab_size, m->e->d_err);
+        YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<__nv_bfloat16>, T, 256, 0, (const __nv_bfloat16*)m->embed, tokens,
+                                 m->h, c.d_model, c.vocab_size, m->e->d_err));
     else
-        embed_kernel<float><<<T, 256, 0, m->e->stream>>>((const float*)m->embed, tokens, m->h, c.d_model, c.vocab_size,
-                                                         m->e->d_err);
+        YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<float>, T, 256, 0, (const float*)m->embed, tokens, m->h, c.d_model,
+                                 c.vocab_size, m->e->d_err));
     m->e->launches++;
-    YK_CHECK_CUDA(cudaGetLastError());
     return YK_OK;
 }
 
 yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx) {
     const auto& c = m->cfg;
     if (c.dtype == YK_DTYPE_BF16)
-        rmsnorm_kernel<__nv_bfloat16><<<rows, 256, 0, m->e->stream>>>(m->h, g, (__nv_bfloat16*)m->xn, c.d_model,
-                                                                       c.rms_eps, row_idx);
+        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<__nv_bfloat16>, rows, 256, 0, (const float*)m->h, g,
+                                 (__nv_bfloat16*)m->xn, c.d_model, c.rms_eps, row_idx));
     else
-        rmsnorm_kernel<float><<<rows, 256, 0, m->e->stream>>>(m->h, g, (float*)m->xn, c.d_model, c.rms_eps, row_idx);
+        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<float>, rows, 256, 0, (const float*)m->h, g, (float*)m->xn,
+                                 c.d_model, c.rms_eps, row_idx));
     m->e->launches++;
-    YK_CHECK_CUDA(cudaGetLastError());
     return YK_OK;
 }
 

@@ -129,6 +129,8 @@ __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, fl
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(SMP_THREADS) row_stats_kernel(const float* __restrict__ logits, int64_t V, float T,
                                                                  float* __restrict__ stats) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const RowStats st = block_row_stats(logits + (size_t)r * V, V, T);
     if (threadIdx.x == 0) {
@@ -158,6 +160,8 @@ struct DraftArgs {
 
 __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) {
     __shared__ ChainSmem cs;
+    pdl_trigger();
+    pdl_wait();
     const int b = a.j_fixed >= 0 ? blockIdx.x : blockIdx.x / a.k;
     const int j = a.j_fixed >= 0 ? a.j_fixed : blockIdx.x % a.k;
     const float* row = a.logits + ((size_t)b * a.logit_row_stride + (size_t)j * a.logit_row_j_mul) * a.V;
@@ -212,6 +216,8 @@ struct VerifyArgs {
 
 __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
     __shared__ ChainSmem cs;
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x;
     const int k = a.k;
     const int64_t V = a.V;
@@ -383,9 +389,8 @@ extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, 
     a.seq_ids = L.seq;
     a.probs = s->probs;
     a.tokens_out = L.out;
-    draft_sample_kernel<<<B, SMP_THREADS, 0, e->stream>>>(a);
+    YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B, SMP_THREADS, 0, a));
     e->launches++;
-    YK_CHECK_CUDA(cudaGetLastError());
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, (size_t)B * 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + (size_t)B * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
@@ -405,9 +410,9 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
     yk_engine* e = s->e;
     const int k = s->k;
     if (from_logits) {
-        row_stats_kernel<<<B * (k + 1), SMP_THREADS, 0, e->stream>>>(qsrc, s->vocab, T > 0.f ? T : 1.0f, s->stats);
+        YK_CHECK_CUDA(launch_pdl(e, row_stats_kernel, B * (k + 1), SMP_THREADS, 0, qsrc, (int64_t)s->vocab,
+                                 T > 0.f ? T : 1.0f, s->stats));
         e->launches++;
-        YK_CHECK_CUDA(cudaGetLastError());
     }
     VerifyArgs a;
     a.q = qsrc;
@@ -423,9 +428,8 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
     a.seq_ids = L.seq;
     a.out = L.out;
     a.counts = L.counts;
-    verify_kernel<<<B, SMP_THREADS, 0, e->stream>>>(a);
+    YK_CHECK_CUDA(launch_pdl(e, verify_kernel, B, SMP_THREADS, 0, a));
     e->launches++;
-    YK_CHECK_CUDA(cudaGetLastError());
     return YK_OK;
 }
 
@@ -491,9 +495,8 @@ extern "C" yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float
     a.seq_ids = L.seq;
     a.probs = s->probs;
     a.tokens_out = L.drafts;
-    draft_sample_kernel<<<B * k, SMP_THREADS, 0, e->stream>>>(a);
+    YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B * k, SMP_THREADS, 0, a));
     e->launches++;
-    YK_CHECK_CUDA(cudaGetLastError());
     YK_TRY(run_verify(s, B, s->q, 1, temperature, seed, step, L));
     YK_CHECK_CUDA(cudaMemcpyAsync(draft_tokens_out, L.drafts, (size_t)B * k * 4, cudaMemcpyDeviceToHost, e->stream));
     return finish_verify(s, B, L, out_tokens, out_counts);
