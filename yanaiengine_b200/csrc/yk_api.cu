@@ -303,6 +303,7 @@ extern "C" void yk_model_destroy(yk_model* m) {
     for (void* p : m->allocations) cudaFree(p);
     if (m->meta) cudaFree(m->meta);
     if (m->attn_ws) cudaFree(m->attn_ws);
+    if (m->attn_counters) cudaFree(m->attn_counters);
     if (m->gemm_counters) cudaFree(m->gemm_counters);
     delete m;
 }
@@ -423,6 +424,14 @@ extern "C" yk_status yk_kv_pool_create(yk_engine* e, const yk_model_config* cfg,
         yk_set_error(std::string("KV pool memset: ") + cudaGetErrorString(err));
         return YK_ERR_CUDA;
     }
+    if (cfg->dtype == YK_DTYPE_BF16) {
+        const yk_status s = yk::make_pool_map(e, p);
+        if (s != YK_OK) {
+            cudaFree(p->data);
+            delete p;
+            return s;
+        }
+    }
     *out = p;
     return YK_OK;
 }
@@ -513,6 +522,17 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
             YK_CHECK_CUDA(cudaMalloc(&m->attn_ws, need * 2 * 4));
             m->attn_ws_floats = need * 2;
         }
+        const int groups = (int)std::max(cb_g.size(), cb_w.size()) / 5;
+        if (groups > m->attn_counter_cap) {
+            YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+            if (m->attn_counters) cudaFree(m->attn_counters);
+            m->attn_counters = nullptr;
+            m->attn_counter_cap = 0;
+            const int cap = std::max(2 * groups, 1024);
+            YK_CHECK_CUDA(cudaMalloc(&m->attn_counters, (size_t)cap * 4));
+            YK_CHECK_CUDA(cudaMemset(m->attn_counters, 0, (size_t)cap * 4));
+            m->attn_counter_cap = cap;
+        }
     }
     const size_t nattn = it_g.size() + cb_g.size() + it_w.size() + cb_w.size();
     const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R + nattn;
@@ -564,13 +584,13 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
     {
         const int32_t* a = m->meta + attn_off;
         m->cur.attn_items[0] = a;
-        m->cur.n_items[0] = (int)(it_g.size() / 6);
+        m->cur.n_items[0] = (int)(it_g.size() / 7);
         a += it_g.size();
         m->cur.attn_comb[0] = a;
         m->cur.n_comb[0] = (int)(cb_g.size() / 5);
         a += cb_g.size();
         m->cur.attn_items[1] = a;
-        m->cur.n_items[1] = (int)(it_w.size() / 6);
+        m->cur.n_items[1] = (int)(it_w.size() / 7);
         a += it_w.size();
         m->cur.attn_comb[1] = a;
         m->cur.n_comb[1] = (int)(cb_w.size() / 5);

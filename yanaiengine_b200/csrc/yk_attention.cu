@@ -31,9 +31,11 @@ struct AttnParams {
     const int32_t* q_starts;
     const int32_t* ctx;
     const int32_t* block_tables;
-    const int32_t* items;  // bf16 path: work items (b, g, qt, kbeg, kend, slot)
-    const int32_t* comb;   // bf16 path: combine entries (b, g, qt, first slot, n slots)
-    float* ws;             // split partials [slot][64][dh + 2]
+    const int32_t* items;  // bf16 path: work items (b, g, qt, kbeg, kend, slot, combine group)
+    const int32_t* comb;   // bf16 path: combine groups (b, g, qt, first slot, n slots)
+    int32_t* counters;     // bf16 path: per combine group arrival counters (zero between launches)
+    float* ws;             // split partials [slot][64][dh + 4]: (M, L, -, -, O[dh])
+    int layer;
     int max_blocks, T, H, Hkv, dh;
     long long block_elems, layer_off;
     int pool_blocks;
@@ -123,6 +125,19 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p) {
 
 // ---------------------------------------------------------------------------
 // Tensor-core kernel (bf16 models).
+//
+// One CTA per work item (sequence b, KV head g, query tile qt, key range
+// [kbeg, kend)): 4 consumer warps + 1 producer warp.  The producer streams the
+// item's 16-token pages (K page, then V page) with TMA through a 3-D tensor map
+// over the pool (x = head dim, y = row within the block, z = block) into an
+// mbarrier ring, 128-byte swizzled so the ldmatrix reads below are conflict
+// free.  Pages that precede this step's new tokens were not written by the
+// previous kernel and are requested before the grid dependency wait.  Consumer
+// warp (m-tile mt, part) takes pages part, part + wpm, ... of the item for its
+// 16 query rows: S = Q K^T and O += P V on tensor cores (mma.sync m16n8k16
+// bf16, fp32 accumulate), online softmax in the log2 domain.  Items cut along
+// the keys publish (M, L, O) partials; the last of them to finish merges all
+// partials in split order (deterministic) and writes the output.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -154,51 +169,141 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
 }
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-constexpr int AT_ROWS = 64;  // query rows per CTA (4 m16 tiles)
+constexpr int AT_ROWS = 64;       // query rows per item (4 m16 tiles)
+constexpr int AT_THREADS = 160;   // warps 0-3 consumers, warp 4 producer
+constexpr int AT_ITEM_INTS = 7;   // b, g, qt, kbeg, kend, slot, combine group
+constexpr int AT_COMB_INTS = 5;   // b, g, qt, first slot, n slots
+constexpr int AT_MAX_SPLITS = 64; // key splits per (sequence, KV head, query tile)
 
 template <int DH>
 struct AttnCfg {
-    static constexpr int KC = DH == 256 ? 32 : 64;  // keys per staged chunk
-    static constexpr int LD = DH + 8;               // padded smem row (elements): conflict-free ldmatrix
-    static constexpr int Q_ELEMS = AT_ROWS * LD;
-    static constexpr int KV_ELEMS = KC * LD;        // one of K or V, one buffer
-    static constexpr size_t SMEM = (size_t)(Q_ELEMS + 4 * KV_ELEMS) * 2;
-    static constexpr size_t RED = (size_t)4 * 16 * (DH + 2) * 4;  // per-warp partials for the final merge
-    static constexpr size_t SMEM_TOTAL = SMEM > RED + (size_t)Q_ELEMS * 2 ? SMEM : RED + (size_t)Q_ELEMS * 2;
+    static constexpr int BOXES = DH / 64;                    // 64-column TMA boxes per K (or V) page
+    static constexpr uint32_t HALF = 16u * DH * 2u;          // bytes of one K (or V) page
+    static constexpr uint32_t STAGE = 2u * HALF;
+    // stages: a multiple of 4 (every warps-per-m-tile value), so a consumer that
+    // waits only on its own pages never waits two phases ahead of a stage
+    static constexpr int S = DH == 64 ? 12 : (DH == 128 ? 8 : 4);
+    static constexpr int CTAS_PER_SM = DH == 64 ? 3 : 2;
+    static constexpr int LDQ = DH + 8;                       // padded Q row (elements)
+    static constexpr size_t Q_BYTES = (size_t)AT_ROWS * LDQ * 2;
+    static constexpr size_t RED_BYTES = (size_t)4 * 16 * (DH + 2) * 4;  // per-warp (m, l, o) for the merge
+    static constexpr size_t RING = (size_t)S * STAGE > RED_BYTES ? (size_t)S * STAGE : RED_BYTES;
+    static constexpr size_t SMEM = 1024 + RING + Q_BYTES + (size_t)2 * S * 8 + 16;
 };
+// Split partial row: (M, L, -, -) then O[DH]; rows 16-byte aligned.
+__host__ __device__ constexpr int ws_row(int dh) { return dh + 4; }
+
+// Byte offset of 16-byte chunk c of row r (key within the page) in a K or V page
+// written by TMA with 128-byte swizzle: 64-column boxes of 16 rows x 128 B.
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+    return (uint32_t)((c >> 3) * 2048 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
 
 template <int DH>
-__global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
+__global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_constant__ CUtensorMap tmKV, AttnParams p) {
     using C = AttnCfg<DH>;
-    constexpr int KC = C::KC, LD = C::LD;
     constexpr int NT = DH / 8;   // n-tiles of the output
     constexpr int KS = DH / 16;  // k-steps of the score MMA
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-    __nv_bfloat16* sK = sQ + C::Q_ELEMS;        // [2][KC][LD]
-    __nv_bfloat16* sV = sK + 2 * C::KV_ELEMS;   // [2][KC][LD]
-    pdl_trigger();
-    pdl_wait();
+    constexpr int S = C::S;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(ring + C::RING);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::RING + C::Q_BYTES);
+    uint64_t* empty = full + S;
+    volatile int* flags = reinterpret_cast<volatile int*>(empty + S);  // [0] last arriver
 
-    const int32_t* it = p.items + (size_t)blockIdx.x * 6;
-    const int b = it[0], g = it[1], qt = it[2], kbeg = it[3], kend = it[4], slot = it[5];
+    const int32_t* it = p.items + (size_t)blockIdx.x * AT_ITEM_INTS;
+    const int b = it[0], g = it[1], qt = it[2], kbeg = it[3], kend = it[4], slot = it[5], cg = it[6];
     const int G = p.H / p.Hkv;
     const int qs0 = p.q_starts[b];
     const int n = p.q_starts[b + 1] - qs0;
     const int ctx = p.ctx[b];
     const int rows = min(AT_ROWS, n * G - qt * AT_ROWS);
     const int MT = (rows + 15) >> 4;
-    const int wpm = MT == 1 ? min(4, KC / 16) : (MT == 2 ? min(2, KC / 16) : 1);
-    const int KW = KC / wpm;  // keys per warp per chunk
+    const int wpm = MT == 1 ? 4 : (MT == 2 ? 2 : 1);
+    const int pg0 = kbeg >> 4;
+    const int npages = (kend - kbeg + 15) >> 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), (uint32_t)MT);
+        }
+        flags[0] = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (warp == 4) {
+        // ---------------- producer ----------------
+        const int32_t* bt = p.block_tables + (size_t)b * p.max_blocks;
+        // pages entirely before this step's first new token: untouched by the previous kernel
+        const int first_new = ctx - n;
+        int pre = 0;
+        while (pre < S && pre < npages && (pg0 + pre + 1) * 16 <= first_new) ++pre;
+        bool stop = false;
+        int issued = 0;
+        for (int c0 = 0; c0 < npages; c0 += 32) {
+            int bid = 0;
+            if (c0 + lane < npages) {
+                bid = bt[pg0 + c0 + lane];
+                if (bid < 0 || bid >= p.pool_blocks) {
+                    raise_err(p.err, YK_DEV_ERR_BOUNDS);
+                    bid = 0;
+                }
+            }
+            const int cend = min(npages, c0 + 32);
+            for (int i = c0; i < cend; ++i) {
+                if (i == pre) pdl_wait();
+                const int blk = __shfl_sync(0xffffffffu, bid, i - c0);
+                if (lane == 0 && !stop) {
+                    const int s = i % S;
+                    if (i >= S && !mbar_wait_bounded(smem_u32(&empty[s]), (uint32_t)(((i / S) - 1) & 1))) {
+                        raise_err(p.err, YK_DEV_ERR_TIMEOUT);
+                        stop = true;
+                    } else {
+                        const uint32_t fb = smem_u32(&full[s]);
+                        const uint32_t dst = smem_u32(ring + (size_t)s * C::STAGE);
+                        const int yk = ((p.layer * 2 + 0) * p.Hkv + g) * 16;
+                        const int yv = ((p.layer * 2 + 1) * p.Hkv + g) * 16;
+                        mbar_arrive_expect_tx(fb, C::STAGE);
+#pragma unroll
+                        for (int bx = 0; bx < C::BOXES; ++bx) {
+                            tma_load_3d(dst + bx * 2048u, &tmKV, bx * 64, yk, blk, fb);
+                            tma_load_3d(dst + C::HALF + bx * 2048u, &tmKV, bx * 64, yv, blk, fb);
+                        }
+                        issued = i + 1;
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        if (pre >= npages) pdl_wait();
+        // every issued page must land before the CTA may exit
+        if (lane == 0)
+            for (int i = max(0, issued - S); i < issued; ++i)
+                (void)mbar_wait_bounded(smem_u32(&full[i % S]), (uint32_t)((i / S) & 1));
+        return;
+    }
+
+    // ---------------- consumers: warps 0..3 ----------------
+    pdl_wait();
     const int my_mt = warp / wpm, my_part = warp % wpm;
     const bool active = my_mt < MT;
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);
-    const __nv_bfloat16* pool = reinterpret_cast<const __nv_bfloat16*>(p.pool);
-    const int32_t* bt = p.block_tables + (size_t)b * p.max_blocks;
-
-    // ---- stage Q (64 rows x DH), zero rows beyond `rows`
+    // stage Q (64 rows x DH, padded rows), zero rows beyond `rows`
     constexpr int CPR = DH / 8;  // 16-byte chunks per row
     for (int i = threadIdx.x; i < AT_ROWS * CPR; i += 128) {
         const int r = i / CPR, c = i % CPR;
@@ -206,42 +311,15 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
         const bool ok = r < rows;
         const __nv_bfloat16* src = q;
         if (ok) src = q + ((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + c * 8;
-        cp_async16(smem_u32(sQ + r * LD + c * 8), src, ok ? 16u : 0u);
+        cp_async16(smem_u32(sQ + r * C::LDQ + c * 8), src, ok ? 16u : 0u);
     }
-    // ---- K/V chunk loader: pages of 16 keys, rows beyond kend zero-filled
-    auto load_chunk = [&](int c0, int buf) {
-        __nv_bfloat16* dk = sK + buf * C::KV_ELEMS;
-        __nv_bfloat16* dv = sV + buf * C::KV_ELEMS;
-        for (int i = threadIdx.x; i < KC * CPR; i += 128) {
-            const int r = i / CPR, c = i % CPR;
-            const int j = c0 + r;
-            bool ok = j < kend;
-            const __nv_bfloat16* srck = pool;
-            const __nv_bfloat16* srcv = pool;
-            if (ok) {
-                const int blk = bt[j >> 4];
-                if (blk < 0 || blk >= p.pool_blocks) {
-                    raise_err(p.err, YK_DEV_ERR_BOUNDS);
-                    ok = false;
-                } else {
-                    const size_t base = (size_t)blk * p.block_elems + p.layer_off + (size_t)(j & 15) * DH + c * 8;
-                    srck = pool + base + (size_t)g * 16 * DH;
-                    srcv = pool + base + (size_t)(p.Hkv + g) * 16 * DH;
-                }
-            }
-            cp_async16(smem_u32(dk + r * LD + c * 8), srck, ok ? 16u : 0u);
-            cp_async16(smem_u32(dv + r * LD + c * 8), srcv, ok ? 16u : 0u);
-        }
-    };
-    const int nchunks = (kend - kbeg + KC - 1) / KC;
-    load_chunk(kbeg, 0);
     cp_async_commit();
+    cp_async_wait<0>();
+    consumer_bar();
 
-    // per-lane rows (m-tile rows lane/4 and lane/4+8) and their positions
     const int r0 = my_mt * 16 + (lane >> 2), r1 = r0 + 8;
     const int pos0 = (r0 < rows) ? ctx - n + (qt * AT_ROWS + r0) / G : -1;
     const int pos1 = (r1 < rows) ? ctx - n + (qt * AT_ROWS + r1) / G : -1;
-    // last key any row of this warp's m-tile can see (warp-uniform skip test)
     int wmaxpos = max(pos0, pos1);
 #pragma unroll
     for (int o2 = 16; o2 > 0; o2 >>= 1) wmaxpos = max(wmaxpos, __shfl_xor_sync(0xffffffffu, wmaxpos, o2));
@@ -251,28 +329,27 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
     for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     uint32_t qf[DH <= 128 ? KS : 1][4];
-
-    for (int c = 0; c < nchunks; ++c) {
-        if (c + 1 < nchunks) load_chunk(kbeg + (c + 1) * KC, (c + 1) & 1);
-        cp_async_commit();
-        cp_async_wait<1>();
-        __syncthreads();
-        if (c == 0 && DH <= 128 && active) {
+    if (DH <= 128 && active) {
 #pragma unroll
-            for (int ks = 0; ks < (DH <= 128 ? KS : 1); ++ks) {
-                const uint32_t a = smem_u32(sQ + (my_mt * 16 + (lane & 15)) * LD + ks * 16 + (lane >> 4) * 8);
-                ldsm_x4(a, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-            }
+        for (int ks = 0; ks < (DH <= 128 ? KS : 1); ++ks) {
+            const uint32_t a = smem_u32(sQ + (my_mt * 16 + (lane & 15)) * C::LDQ + ks * 16 + (lane >> 4) * 8);
+            ldsm_x4(a, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
         }
-        if (active) {
-            const __nv_bfloat16* ck = sK + (c & 1) * C::KV_ELEMS;
-            const __nv_bfloat16* cv = sV + (c & 1) * C::KV_ELEMS;
-            for (int sb = 0; sb < KW; sb += 16) {
-                const int kr = my_part * KW + sb;   // key row within the chunk
-                const int j0 = kbeg + c * KC + kr;  // first key of this 16-block
-                if (j0 >= kend || j0 > wmaxpos) continue;  // whole 16-key block masked for the m-tile
+    }
+    bool ok = true;
+    if (active) {
+        for (int i = my_part; i < npages; i += wpm) {
+            const int s = i % S;
+            if (ok && !mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)((i / S) & 1))) {
+                raise_err(p.err, YK_DEV_ERR_TIMEOUT);
+                ok = false;
+            }
+            const int j0 = (pg0 + i) * 16;
+            if (ok && j0 <= wmaxpos) {
+                const uint32_t kb = smem_u32(ring + (size_t)s * C::STAGE);
+                const uint32_t vb = kb + C::HALF;
                 // S = Q K^T : two n8 tiles (keys j0..j0+7, j0+8..j0+15)
-                float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
                 for (int ks = 0; ks < KS; ks += 2) {
                     uint32_t a[2][4];
@@ -283,17 +360,16 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
 #pragma unroll
                         for (int h2 = 0; h2 < 2; ++h2) {
                             const uint32_t aa =
-                                smem_u32(sQ + (my_mt * 16 + (lane & 15)) * LD + (ks + h2) * 16 + (lane >> 4) * 8);
+                                smem_u32(sQ + (my_mt * 16 + (lane & 15)) * C::LDQ + (ks + h2) * 16 + (lane >> 4) * 8);
                             ldsm_x4(aa, a[h2][0], a[h2][1], a[h2][2], a[h2][3]);
                         }
                     }
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
                         uint32_t b0, b1, b2, b3;
-                        const uint32_t ba = smem_u32(ck + (kr + nt * 8 + (lane & 7)) * LD + ks * 16 + (lane >> 3) * 8);
-                        ldsm_x4(ba, b0, b1, b2, b3);
-                        mma_bf16(s[nt], a[0][0], a[0][1], a[0][2], a[0][3], b0, b1);
-                        mma_bf16(s[nt], a[1][0], a[1][1], a[1][2], a[1][3], b2, b3);
+                        ldsm_x4(kb + sw_off(nt * 8 + (lane & 7), ks * 2 + (lane >> 3)), b0, b1, b2, b3);
+                        mma_bf16(sc[nt], a[0][0], a[0][1], a[0][2], a[0][3], b0, b1);
+                        mma_bf16(sc[nt], a[1][0], a[1][1], a[1][2], a[1][3], b2, b3);
                     }
                 }
                 // scale, cap, mask (log2 domain)
@@ -304,12 +380,12 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
                     for (int e = 0; e < 4; ++e) {
                         const int j = j0 + nt * 8 + 2 * (lane & 3) + (e & 1);
                         const int ps = (e < 2) ? pos0 : pos1;
-                        float x = s[nt][e] * p.scale;
+                        float x = sc[nt][e] * p.scale;
                         if (p.cap > 0.f) x = p.cap * tanhf(x / p.cap);
                         x *= LOG2E;
-                        const bool masked = j >= kend || j > ps || (p.window > 0 && ps - j >= p.window);
+                        const bool masked = j < kbeg || j >= kend || j > ps || (p.window > 0 && ps - j >= p.window);
                         x = masked ? -INFINITY : x;
-                        s[nt][e] = x;
+                        sc[nt][e] = x;
                         if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
                     }
                 }
@@ -323,10 +399,10 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
                 float ps[2][4];
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
-                    ps[nt][0] = exp2f(s[nt][0] - mu0);
-                    ps[nt][1] = exp2f(s[nt][1] - mu0);
-                    ps[nt][2] = exp2f(s[nt][2] - mu1);
-                    ps[nt][3] = exp2f(s[nt][3] - mu1);
+                    ps[nt][0] = exp2f(sc[nt][0] - mu0);
+                    ps[nt][1] = exp2f(sc[nt][1] - mu0);
+                    ps[nt][2] = exp2f(sc[nt][2] - mu1);
+                    ps[nt][3] = exp2f(sc[nt][3] - mu1);
                 }
                 l0 = l0 * c0f + ps[0][0] + ps[0][1] + ps[1][0] + ps[1][1];
                 l1 = l1 * c1f + ps[0][2] + ps[0][3] + ps[1][2] + ps[1][3];
@@ -339,27 +415,26 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
                 }
                 const uint32_t pa0 = pack_bf16(ps[0][0], ps[0][1]), pa1 = pack_bf16(ps[0][2], ps[0][3]);
                 const uint32_t pa2 = pack_bf16(ps[1][0], ps[1][1]), pa3 = pack_bf16(ps[1][2], ps[1][3]);
-                // O += P V : V rows kr..kr+15, output n-tiles in pairs
+                // O += P V : V rows 0..15 of the page, output n-tiles in pairs
 #pragma unroll
                 for (int t = 0; t < NT; t += 2) {
                     uint32_t b0, b1, b2, b3;
-                    const uint32_t va = smem_u32(cv + (kr + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + t * 8 + (lane >> 4) * 8);
-                    ldsm_x4_t(va, b0, b1, b2, b3);
+                    ldsm_x4_t(vb + sw_off((lane & 7) + ((lane >> 3) & 1) * 8, t + (lane >> 4)), b0, b1, b2, b3);
                     mma_bf16(o[t], pa0, pa1, pa2, pa3, b0, b1);
                     mma_bf16(o[t + 1], pa0, pa1, pa2, pa3, b2, b3);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
         }
-        __syncthreads();
     }
-    cp_async_wait<0>();
-    // ---- merge the warps of each m-tile through shared memory, then write
+    // ---- merge the warps of each m-tile through shared memory (the ring is idle now)
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    float* red = reinterpret_cast<float*>(smem_raw + (size_t)C::Q_ELEMS * 2);  // [4 warps][16][DH + 2]
-    __syncthreads();
+    float* red = reinterpret_cast<float*>(ring);  // [4 warps][16][DH + 2]
+    consumer_bar();
     if (active) {
         float* rw = red + (size_t)warp * 16 * (DH + 2);
         const int lr = lane >> 2;
@@ -378,8 +453,9 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
             rw[(lr + 8) * (DH + 2) + 1] = l1;
         }
     }
-    __syncthreads();
+    consumer_bar();
     __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.out);
+    const int WR = ws_row(DH);
     for (int i = threadIdx.x; i < rows * DH; i += 128) {
         const int r = i / DH, col = i % DH;
         const int mt = r >> 4, lr = r & 15;
@@ -398,41 +474,60 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(AttnParams p) {
             outp[((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + col] =
                 __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
         } else {
-            float* wsr = p.ws + ((size_t)slot * AT_ROWS + r) * (DH + 2);
-            wsr[2 + col] = O;
-            if (col == 0) { wsr[0] = M; wsr[1] = L; }
+            float* wsr = p.ws + ((size_t)slot * AT_ROWS + r) * WR;
+            __stcg(wsr + 4 + col, O);
+            if (col == 0) { __stcg(wsr, M); __stcg(wsr + 1, L); }
         }
     }
-}
-
-// Split-KV merge: one CTA per (sequence, KV head, query tile) with > 1 split.
-template <int DH>
-__global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
-    pdl_trigger();
-    pdl_wait();
-    const int32_t* e = p.comb + (size_t)blockIdx.x * 5;
-    const int b = e[0], g = e[1], qt = e[2], first = e[3], ns = e[4];
-    const int G = p.H / p.Hkv;
-    const int qs0 = p.q_starts[b];
-    const int n = p.q_starts[b + 1] - qs0;
-    const int rows = min(AT_ROWS, n * G - qt * AT_ROWS);
-    __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.out);
-    for (int i = threadIdx.x; i < rows * DH; i += 128) {
-        const int r = i / DH, col = i % DH;
+    if (slot < 0) return;
+    // ---- split item: the last of the group to finish merges all partials in split order
+    __threadfence();
+    consumer_bar();
+    const int32_t* ce = p.comb + (size_t)cg * AT_COMB_INTS;
+    const int first = ce[3], ns = ce[4];
+    if (threadIdx.x == 0) flags[0] = (atomicAdd(&p.counters[cg], 1) == ns - 1) ? 1 : 0;
+    consumer_bar();
+    if (!flags[0]) return;
+    __threadfence();
+    // per-row split weights f = exp2(M_s - max M) and the total L, then O = sum f O_s
+    float* fw = reinterpret_cast<float*>(ring);           // [64][AT_MAX_SPLITS]
+    float* lt = fw + AT_ROWS * AT_MAX_SPLITS;              // [64]
+    if (threadIdx.x < rows) {
+        const int r = threadIdx.x;
         float M = -INFINITY;
-        for (int s = 0; s < ns; ++s) M = fmaxf(M, p.ws[((size_t)(first + s) * AT_ROWS + r) * (DH + 2)]);
+        for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, __ldcg(p.ws + ((size_t)(first + sp) * AT_ROWS + r) * WR));
         const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < ns; ++s) {
-            const float* w = p.ws + ((size_t)(first + s) * AT_ROWS + r) * (DH + 2);
-            const float f = exp2f(w[0] - Mu);
-            L += f * w[1];
-            O += f * w[2 + col];
+        float L = 0.f;
+        for (int sp = 0; sp < ns; ++sp) {
+            const float* w = p.ws + ((size_t)(first + sp) * AT_ROWS + r) * WR;
+            const float f = exp2f(__ldcg(w) - Mu);
+            L += f * __ldcg(w + 1);
+            fw[r * AT_MAX_SPLITS + sp] = f;
         }
-        const int rr = qt * AT_ROWS + r;
-        outp[((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + col] =
-            __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+        lt[r] = L;
     }
+    consumer_bar();
+    constexpr int D4 = DH / 4;
+#pragma unroll 2
+    for (int i = threadIdx.x; i < rows * D4; i += 128) {
+        const int r = i / D4, c4 = (i % D4) * 4;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp = 0; sp < ns; ++sp) {
+            const float f = fw[r * AT_MAX_SPLITS + sp];
+            const float4 v =
+                __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(first + sp) * AT_ROWS + r) * WR + 4 + c4));
+            O.x += f * v.x;
+            O.y += f * v.y;
+            O.z += f * v.z;
+            O.w += f * v.w;
+        }
+        const float L = lt[r];
+        const int rr = qt * AT_ROWS + r;
+        __nv_bfloat16* dst = outp + ((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + c4;
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(L > 0.f ? O.x / L : 0.f, L > 0.f ? O.y / L : 0.f),
+                                                    pack_bf16(L > 0.f ? O.z / L : 0.f, L > 0.f ? O.w / L : 0.f));
+    }
+    if (threadIdx.x == 0) p.counters[cg] = 0;
 }
 
 template <typename AT>
@@ -447,30 +542,32 @@ static cudaError_t launch_simt(const AttnParams& p, yk_engine* e) {
 }
 
 template <int DH>
-static yk_status launch_mma(const AttnParams& p, int n_items, int n_comb, yk_engine* e) {
-    const size_t smem = AttnCfg<DH>::SMEM_TOTAL;
+static yk_status launch_tc(const CUtensorMap& tm, const AttnParams& p, int n_items, yk_engine* e) {
+    const size_t smem = AttnCfg<DH>::SMEM;
     static bool attr = false;
     if (!attr) {
-        YK_CHECK_CUDA(cudaFuncSetAttribute(attn_mma_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        YK_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr = true;
     }
-    YK_CHECK_CUDA(launch_pdl(e, attn_mma_kernel<DH>, n_items, 128, smem, p));
+    YK_CHECK_CUDA(launch_pdl(e, attn_tc_kernel<DH>, n_items, AT_THREADS, smem, tm, p));
     e->launches++;
-    if (n_comb > 0) {
-        YK_CHECK_CUDA(launch_pdl(e, attn_combine_kernel<DH>, n_comb, 128, 0, p));
-        e->launches++;
-    }
     return YK_OK;
 }
 
-// Work list for one forward step and one window setting (see yk_forward_step).
+int attention_ctas_per_sm(int head_dim) {
+    return head_dim == 64 ? AttnCfg<64>::CTAS_PER_SM : (head_dim == 128 ? AttnCfg<128>::CTAS_PER_SM : AttnCfg<256>::CTAS_PER_SM);
+}
+
+// Work list for one forward step and one window setting (see yk_forward_step):
+// spans (sequence, query tile) x KV heads, each cut into equal page-aligned
+// key ranges so the item count fills about one wave of resident CTAs; items
+// sorted longest first so the block scheduler balances the tail.
 void plan_attention(const yk_model_config& c, int num_sms, const uint32_t* q_starts, const uint32_t* ctx, int B,
                     bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots) {
     const int G = c.n_heads / c.n_kv_heads;
-    const int KC = c.head_dim == 256 ? 32 : 64;
     struct Span { int b, qt, kb, ke; };
     std::vector<Span> spans;
-    long long total = 0;
+    int max_pages = 1;
     for (int b = 0; b < B; ++b) {
         const int n = (int)(q_starts[b + 1] - q_starts[b]);
         if (n == 0) continue;
@@ -479,32 +576,53 @@ void plan_attention(const yk_model_config& c, int num_sms, const uint32_t* q_sta
             const int i_lo = (qt * AT_ROWS) / G, i_hi = (std::min(rows, qt * AT_ROWS + AT_ROWS) - 1) / G;
             const int pos_lo = (int)ctx[b] - n + i_lo, pos_hi = (int)ctx[b] - n + i_hi;
             int kb = windowed ? std::max(0, pos_lo - c.window + 1) : 0;
-            kb = (kb / KC) * KC;
+            kb = (kb / 16) * 16;
             const int ke = pos_hi + 1;
             spans.push_back({b, qt, kb, ke});
-            total += (long long)(ke - kb) * c.n_kv_heads;
+            max_pages = std::max(max_pages, (ke - kb + 15) / 16);
         }
     }
-    const long long target_items = 3LL * num_sms;
-    long long ks = (total + target_items - 1) / std::max(1LL, target_items);
-    ks = std::max<long long>(KC, ((ks + KC - 1) / KC) * KC);
-    items.clear();
+    const long long target = (long long)num_sms * attention_ctas_per_sm(c.head_dim);
+    auto splits = [&](const Span& s, int kp) {  // pieces of a span at kp pages per piece
+        const int pages = (s.ke - s.kb + 15) / 16;
+        return std::min(AT_MAX_SPLITS, (pages + kp - 1) / kp);
+    };
+    auto count = [&](int kp) {
+        long long nitems = 0;
+        for (const auto& s : spans) nitems += (long long)splits(s, kp) * c.n_kv_heads;
+        return nitems;
+    };
+    int lo = 1, hi = max_pages;  // smallest pages-per-piece whose item count fits the target
+    while (lo < hi) {
+        const int mid = (lo + hi) / 2;
+        if (count(mid) <= target) hi = mid; else lo = mid + 1;
+    }
+    const int kp = lo;
+    struct Item { int b, g, qt, kb, ke, slot, cg; };
+    std::vector<Item> list;
     comb.clear();
     int slot = 0;
     for (const auto& s : spans) {
-        const int ns = (int)((s.ke - s.kb + ks - 1) / ks);
+        const int ns = splits(s, kp);
+        const int pages = (s.ke - s.kb + 15) / 16;
         for (int g = 0; g < c.n_kv_heads; ++g) {
             if (ns <= 1) {
-                items.insert(items.end(), {s.b, g, s.qt, s.kb, s.ke, -1});
+                list.push_back({s.b, g, s.qt, s.kb, s.ke, -1, -1});
             } else {
+                const int cg = (int)(comb.size() / AT_COMB_INTS);
                 comb.insert(comb.end(), {s.b, g, s.qt, slot, ns});
                 for (int i = 0; i < ns; ++i) {
-                    const int kb = s.kb + (int)(i * ks), ke = std::min(s.ke, s.kb + (int)((i + 1) * ks));
-                    items.insert(items.end(), {s.b, g, s.qt, kb, ke, slot++});
+                    const int kb = s.kb + 16 * (int)((long long)i * pages / ns);
+                    const int ke = std::min(s.ke, s.kb + 16 * (int)((long long)(i + 1) * pages / ns));
+                    list.push_back({s.b, g, s.qt, kb, ke, slot++, cg});
                 }
             }
         }
     }
+    std::stable_sort(list.begin(), list.end(), [](const Item& x, const Item& y) { return x.ke - x.kb > y.ke - y.kb; });
+    items.clear();
+    items.reserve(list.size() * AT_ITEM_INTS);
+    for (const auto& t : list) items.insert(items.end(), {t.b, t.g, t.qt, t.kb, t.ke, t.slot, t.cg});
     *n_slots = slot;
 }
 
@@ -529,6 +647,7 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
     p.dh = c.head_dim;
     p.block_elems = (long long)pool->block_elems;
     p.layer_off = (long long)layer * (long long)pool->layer_elems;
+    p.layer = layer;
     p.pool_blocks = pool->num_blocks;
     p.scale = 1.0f / sqrtf((float)c.head_dim);
     p.cap = c.attn_cap;
@@ -536,22 +655,44 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
     p.window = windowed ? c.window : 0;
     p.err = m->e->d_err;
     p.ws = m->attn_ws;
+    p.counters = m->attn_counters;
     if (c.dtype != YK_DTYPE_BF16) {
         YK_CHECK_CUDA(launch_simt<float>(p, m->e));
         m->e->launches++;
         return YK_OK;
     }
+    YK_ARG(pool->has_tm, "KV pool has no tensor map");
     const int w = windowed ? 1 : 0;
     p.items = m->cur.attn_items[w];
     p.comb = m->cur.attn_comb[w];
-    const int ni = m->cur.n_items[w], nc = m->cur.n_comb[w];
+    const int ni = m->cur.n_items[w];
     switch (c.head_dim) {
-        case 64: return launch_mma<64>(p, ni, nc, m->e);
-        case 128: return launch_mma<128>(p, ni, nc, m->e);
-        default: return launch_mma<256>(p, ni, nc, m->e);
+        case 64: return launch_tc<64>(pool->tm, p, ni, m->e);
+        case 128: return launch_tc<128>(pool->tm, p, ni, m->e);
+        default: return launch_tc<256>(pool->tm, p, ni, m->e);
     }
 }
 
-size_t attention_ws_floats_per_slot(int head_dim) { return (size_t)AT_ROWS * (head_dim + 2); }
+size_t attention_ws_floats_per_slot(int head_dim) { return (size_t)AT_ROWS * ws_row(head_dim); }
+
+// Tensor map of a bf16 pool for the attention kernel: x = head dim, y = row
+// within a block ([layer][K|V][kv head][16 slots]), z = block; box 64 x 16 x 1.
+yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool) {
+    const auto& c = pool->cfg;
+    const cuuint64_t dims[3] = {(cuuint64_t)c.head_dim, (cuuint64_t)c.n_layers * 2 * c.n_kv_heads * 16,
+                                (cuuint64_t)pool->num_blocks};
+    const cuuint64_t strides[2] = {(cuuint64_t)c.head_dim * 2, (cuuint64_t)pool->block_elems * 2};
+    const cuuint32_t box[3] = {64, 16, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = e->encode_tiled(&pool->tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, pool->data, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        yk_set_error("cuTensorMapEncodeTiled(KV pool) failed: " + std::to_string((int)r));
+        return YK_ERR_CUDA;
+    }
+    pool->has_tm = true;
+    return YK_OK;
+}
 
 }  // namespace yk

@@ -119,9 +119,6 @@ __device__ __forceinline__ int partial_slot(const TcArgs& a, int cta, int tile) 
     const long long RU = (long long)a.sk_tiles * a.kb_total;
     return 2 * cta + ((long long)tile == unit_begin(cta, RU, a.sk_ctas) / a.kb_total ? 0 : 1);
 }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 __device__ __forceinline__ void epi_bar_sync() {  // named barrier over the 4 epilogue warps
     asm volatile("bar.sync 1, 128;" ::: "memory");
 }

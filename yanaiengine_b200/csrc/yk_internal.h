@@ -130,9 +130,11 @@ struct yk_model {
     // GEMM phase timestamps (test hook only; null otherwise) and the last grid used
     unsigned long long* gemm_stamps = nullptr;
     int gemm_last_grid = 0;
-    // attention split-KV partials
+    // attention split-KV partials and per combine group arrival counters
     float* attn_ws = nullptr;
     size_t attn_ws_floats = 0;
+    int32_t* attn_counters = nullptr;
+    int attn_counter_cap = 0;
     // TMA maps of activation buffers, keyed by (buffer, token-box rows)
     std::map<std::pair<const void*, int>, CUtensorMap> xmaps;
     std::vector<void*> allocations;
@@ -146,6 +148,8 @@ struct yk_kv_pool {
     void* data = nullptr;      // [block][layer][2][Hkv][16][dh]
     size_t block_elems = 0;    // elements per block (all layers)
     size_t layer_elems = 0;    // elements per layer within a block
+    CUtensorMap tm{};          // bf16 pools: 3-D TMA map (head dim, row in block, block)
+    bool has_tm = false;
 };
 
 struct yk_sampler {
@@ -216,6 +220,7 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
 void plan_attention(const yk_model_config& c, int num_sms, const uint32_t* q_starts, const uint32_t* ctx, int B,
                     bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots);
 size_t attention_ws_floats_per_slot(int head_dim);
+yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool);
 yk_status launch_embed(yk_model* m, const int32_t* tokens, int T);
 yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx);
 yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed, uint32_t stream, float std,
