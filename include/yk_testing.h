@@ -30,6 +30,14 @@ yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const uint16_t* X
                               int32_t m_tok, int32_t grid, int32_t reps, float* Y, float* ms_per_rep,
                               uint64_t* stamps, int32_t* grid_used);
 
+/* Per-CTA phase stamps of the paged-attention kernel.  After enable (cap CTAs,
+ * cap > 0; 0 disables), every bf16 attention launch of `m` overwrites a device
+ * record of 8 words per CTA: %globaltimer at start, first page landed (consumer
+ * warp 0), consumer loop done, output written; pages of the item; SM id;
+ * items in the launch.  read copies the last launch's records (cap x 8). */
+yk_status ykt_attention_stamps_enable(yk_model* m, int32_t cap);
+yk_status ykt_attention_stamps_read(yk_model* m, uint64_t* host, int32_t cap, int32_t* n_ctas);
+
 #ifdef __cplusplus
 }
 #endif

@@ -102,6 +102,8 @@ _PROTOS = {
     "ykt_gemm_bf16_timed": (C.c_int32, [_P, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int32, C.c_int32,
                                         C.c_int32, C.c_int32, C.c_int32, _F32P, _F32P, C.POINTER(C.c_uint64),
                                         _I32P]),
+    "ykt_attention_stamps_enable": (C.c_int32, [_P, C.c_int32]),
+    "ykt_attention_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, _I32P]),
 }
 
 _HOST_PROTOS = {
@@ -286,6 +288,17 @@ class Model:
                                     ptr(cl, C.c_uint32), len(cl), ptr(bt, C.c_int32), bt.shape[1], last_n,
                                     C.byref(rows)))
         return rows.value
+
+    def attention_stamps(self, cap: int = 0):
+        """Test hook: cap > 0 enables per-CTA attention stamps; cap == 0 returns the
+        last launch's records ([n_ctas x 8] uint64)."""
+        if cap > 0:
+            check(lib().ykt_attention_stamps_enable(self.h, cap))
+            return None
+        out = np.zeros((4096, 8), np.uint64)
+        n = C.c_int32()
+        check(lib().ykt_attention_stamps_read(self.h, ptr(out, C.c_uint64), 4096, C.byref(n)))
+        return out[: n.value]
 
     def logits(self, row0: int, rows: int) -> np.ndarray:
         out = np.empty((rows, self.cfg.vocab_size), dtype=np.float32)

@@ -15,6 +15,7 @@
 // partials are merged by a log-sum-exp combine kernel.
 // fp32 path: a SIMT kernel (one warp per token x head).
 #include <algorithm>
+#include <climits>
 #include <vector>
 
 #include "yk_common.cuh"
@@ -36,6 +37,7 @@ struct AttnParams {
     int32_t* counters;     // bf16 path: per combine group arrival counters (zero between launches)
     float* ws;             // split partials [slot][64][dh + 4]: (M, L, -, -, O[dh])
     int layer;
+    unsigned long long* stamps;  // test hook: 8 words per CTA, else null
     int max_blocks, T, H, Hkv, dh;
     long long block_elems, layer_off;
     int pool_blocks;
@@ -190,14 +192,20 @@ struct AttnCfg {
     static constexpr int BOXES = DH / 64;                    // 64-column TMA boxes per K (or V) page
     static constexpr uint32_t HALF = 16u * DH * 2u;          // bytes of one K (or V) page
     static constexpr uint32_t STAGE = 2u * HALF;
-    // stages: a multiple of 4 (every warps-per-m-tile value), so a consumer that
-    // waits only on its own pages never waits two phases ahead of a stage
-    static constexpr int S = DH == 64 ? 12 : (DH == 128 ? 8 : 4);
-    static constexpr int CTAS_PER_SM = DH == 64 ? 3 : 2;
+    // A consumer warp takes chunks of CP pages.  Stages: a multiple of 4*CP (4 =
+    // every warps-per-m-tile value), so a consumer that waits only on its own
+    // chunks never waits two phases ahead of a stage.
+    static constexpr int CP = DH == 256 ? 1 : 2;
+    static constexpr int S = DH == 256 ? 4 : 8;
+    static constexpr int CTAS_PER_SM = DH == 64 ? 3 : (DH == 128 ? 2 : 1);  // register-limited
     static constexpr int LDQ = DH + 8;                       // padded Q row (elements)
     static constexpr size_t Q_BYTES = (size_t)AT_ROWS * LDQ * 2;
-    static constexpr size_t RED_BYTES = (size_t)4 * 16 * (DH + 2) * 4;  // per-warp (m, l, o) for the merge
-    static constexpr size_t RING = (size_t)S * STAGE > RED_BYTES ? (size_t)S * STAGE : RED_BYTES;
+    // after the page loop the ring holds the merge: per-warp O and (m, l), per-row
+    // weights; or, for the last CTA of a split group, per-row split weights
+    static constexpr size_t RED_BYTES = ((size_t)4 * 16 * DH + 4 * 16 * 2 + 64 * 4 + 64 * 2) * 4;
+    static constexpr size_t SPLIT_BYTES = ((size_t)64 * 64 + 64) * 4;
+    static constexpr size_t RMAX = RED_BYTES > SPLIT_BYTES ? RED_BYTES : SPLIT_BYTES;
+    static constexpr size_t RING = (size_t)S * STAGE > RMAX ? (size_t)S * STAGE : RMAX;
     static constexpr size_t SMEM = 1024 + RING + Q_BYTES + (size_t)2 * S * 8 + 16;
 };
 // Split partial row: (M, L, -, -) then O[DH]; rows 16-byte aligned.
@@ -210,7 +218,8 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
 }
 
 template <int DH>
-__global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_constant__ CUtensorMap tmKV, AttnParams p) {
+__global__ void __launch_bounds__(AT_THREADS, AttnCfg<DH>::CTAS_PER_SM)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmKV, AttnParams p) {
     using C = AttnCfg<DH>;
     constexpr int NT = DH / 8;   // n-tiles of the output
     constexpr int KS = DH / 16;  // k-steps of the score MMA
@@ -245,6 +254,16 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
     }
     __syncthreads();
     pdl_trigger();
+    unsigned long long* stp = p.stamps ? p.stamps + (size_t)blockIdx.x * 8 : nullptr;
+    if (stp && threadIdx.x == 0) {
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        stp[0] = globaltimer_ns();
+        stp[1] = 0;
+        stp[4] = (unsigned long long)npages;
+        stp[5] = smid;
+        stp[6] = gridDim.x;
+    }
 
     if (warp == 4) {
         // ---------------- producer ----------------
@@ -320,10 +339,17 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
     const int r0 = my_mt * 16 + (lane >> 2), r1 = r0 + 8;
     const int pos0 = (r0 < rows) ? ctx - n + (qt * AT_ROWS + r0) / G : -1;
     const int pos1 = (r1 < rows) ? ctx - n + (qt * AT_ROWS + r1) / G : -1;
+    // last key any row of this warp's m-tile sees, and the first position of its
+    // valid rows (rows past `rows` are zero queries whose results are never written)
     int wmaxpos = max(pos0, pos1);
+    int wminpos = min(r0 < rows ? pos0 : INT_MAX, r1 < rows ? pos1 : INT_MAX);
 #pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) wmaxpos = max(wmaxpos, __shfl_xor_sync(0xffffffffu, wmaxpos, o2));
+    for (int o2 = 16; o2 > 0; o2 >>= 1) {
+        wmaxpos = max(wmaxpos, __shfl_xor_sync(0xffffffffu, wmaxpos, o2));
+        wminpos = min(wminpos, __shfl_xor_sync(0xffffffffu, wminpos, o2));
+    }
     const float LOG2E = 1.4426950408889634f;
+    const float qk2 = p.scale * LOG2E;  // score -> log2 domain in one multiply (no soft cap)
     float o[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
@@ -336,20 +362,39 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
             ldsm_x4(a, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
         }
     }
+    constexpr int CP = C::CP;          // pages per chunk
+    constexpr int NS = 2 * CP;         // n8 score tiles per chunk
+    const int nchunks = (npages + CP - 1) / CP;
     bool ok = true;
     if (active) {
-        for (int i = my_part; i < npages; i += wpm) {
-            const int s = i % S;
-            if (ok && !mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)((i / S) & 1))) {
-                raise_err(p.err, YK_DEV_ERR_TIMEOUT);
-                ok = false;
+        for (int ch = my_part; ch < nchunks; ch += wpm) {
+            const int i0 = ch * CP;
+            const int np = min(CP, npages - i0);  // pages in this chunk
+#pragma unroll
+            for (int u = 0; u < CP; ++u) {
+                const int i = i0 + u;
+                if (u < np && ok && !mbar_wait_bounded(smem_u32(&full[i % S]), (uint32_t)((i / S) & 1))) {
+                    raise_err(p.err, YK_DEV_ERR_TIMEOUT);
+                    ok = false;
+                }
             }
-            const int j0 = (pg0 + i) * 16;
+            if (stp && ch == 0 && lane == 0) stp[1] = globaltimer_ns();
+            const int j0 = (pg0 + i0) * 16;
             if (ok && j0 <= wmaxpos) {
-                const uint32_t kb = smem_u32(ring + (size_t)s * C::STAGE);
-                const uint32_t vb = kb + C::HALF;
-                // S = Q K^T : two n8 tiles (keys j0..j0+7, j0+8..j0+15)
-                float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                uint32_t kb[CP], vb[CP];
+#pragma unroll
+                for (int u = 0; u < CP; ++u) {
+                    // a missing second page (odd page count) reads the first again; its keys are masked
+                    const int i = i0 + (u < np ? u : 0);
+                    kb[u] = smem_u32(ring + (size_t)(i % S) * C::STAGE);
+                    vb[u] = kb[u] + C::HALF;
+                }
+                // S = Q K^T : NS n8 tiles, even and odd k-steps in separate accumulators
+                float sc[NS][4], sd[NS][4];
+#pragma unroll
+                for (int nt = 0; nt < NS; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sc[nt][e] = sd[nt][e] = 0.f;
 #pragma unroll
                 for (int ks = 0; ks < KS; ks += 2) {
                     uint32_t a[2][4];
@@ -365,28 +410,43 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
                         }
                     }
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
+                    for (int nt = 0; nt < NS; ++nt) {
                         uint32_t b0, b1, b2, b3;
-                        ldsm_x4(kb + sw_off(nt * 8 + (lane & 7), ks * 2 + (lane >> 3)), b0, b1, b2, b3);
+                        ldsm_x4(kb[nt >> 1] + sw_off((nt & 1) * 8 + (lane & 7), ks * 2 + (lane >> 3)), b0, b1, b2, b3);
                         mma_bf16(sc[nt], a[0][0], a[0][1], a[0][2], a[0][3], b0, b1);
-                        mma_bf16(sc[nt], a[1][0], a[1][1], a[1][2], a[1][3], b2, b3);
+                        mma_bf16(sd[nt], a[1][0], a[1][1], a[1][2], a[1][3], b2, b3);
                     }
                 }
-                // scale, cap, mask (log2 domain)
+                // scale, cap, mask (log2 domain).  Fast path: every key of the chunk is
+                // visible to every valid row of the warp and there is no soft cap.
                 float mx0 = -INFINITY, mx1 = -INFINITY;
+                const bool fast = np == CP && p.cap <= 0.f && j0 >= kbeg && j0 + 16 * CP <= kend &&
+                                  j0 + 16 * CP - 1 <= wminpos && (p.window <= 0 || wmaxpos - j0 < p.window);
+                if (fast) {
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
+                    for (int nt = 0; nt < NS; ++nt) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int j = j0 + nt * 8 + 2 * (lane & 3) + (e & 1);
-                        const int ps = (e < 2) ? pos0 : pos1;
-                        float x = sc[nt][e] * p.scale;
-                        if (p.cap > 0.f) x = p.cap * tanhf(x / p.cap);
-                        x *= LOG2E;
-                        const bool masked = j < kbeg || j >= kend || j > ps || (p.window > 0 && ps - j >= p.window);
-                        x = masked ? -INFINITY : x;
-                        sc[nt][e] = x;
-                        if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+                        for (int e = 0; e < 4; ++e) {
+                            const float x = (sc[nt][e] + sd[nt][e]) * qk2;
+                            sc[nt][e] = x;
+                            if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int nt = 0; nt < NS; ++nt) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int j = j0 + nt * 8 + 2 * (lane & 3) + (e & 1);
+                            const int ps = (e < 2) ? pos0 : pos1;
+                            float x = (sc[nt][e] + sd[nt][e]) * p.scale;
+                            if (p.cap > 0.f) x = p.cap * tanhf(x / p.cap);
+                            x *= LOG2E;
+                            const bool masked = j < kbeg || j >= kend || j > ps || (p.window > 0 && ps - j >= p.window);
+                            x = masked ? -INFINITY : x;
+                            sc[nt][e] = x;
+                            if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+                        }
                     }
                 }
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -396,89 +456,126 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
                 const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
                 const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
                 const float c0f = exp2f(m0 - mu0), c1f = exp2f(m1 - mu1);
-                float ps[2][4];
+                float ps[NS][4];
+                float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
+                for (int nt = 0; nt < NS; ++nt) {
                     ps[nt][0] = exp2f(sc[nt][0] - mu0);
                     ps[nt][1] = exp2f(sc[nt][1] - mu0);
                     ps[nt][2] = exp2f(sc[nt][2] - mu1);
                     ps[nt][3] = exp2f(sc[nt][3] - mu1);
+                    sum0 += ps[nt][0] + ps[nt][1];
+                    sum1 += ps[nt][2] + ps[nt][3];
                 }
-                l0 = l0 * c0f + ps[0][0] + ps[0][1] + ps[1][0] + ps[1][1];
-                l1 = l1 * c1f + ps[0][2] + ps[0][3] + ps[1][2] + ps[1][3];
+                l0 = l0 * c0f + sum0;
+                l1 = l1 * c1f + sum1;
                 m0 = mn0;
                 m1 = mn1;
+                // rescale O only when some row's running max moved (the common case
+                // after the first chunks is c == 1 for every row of the warp)
+                if (__any_sync(0xffffffffu, c0f != 1.0f || c1f != 1.0f)) {
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    o[t][0] *= c0f; o[t][1] *= c0f;
-                    o[t][2] *= c1f; o[t][3] *= c1f;
+                    for (int t = 0; t < NT; ++t) {
+                        o[t][0] *= c0f; o[t][1] *= c0f;
+                        o[t][2] *= c1f; o[t][3] *= c1f;
+                    }
                 }
-                const uint32_t pa0 = pack_bf16(ps[0][0], ps[0][1]), pa1 = pack_bf16(ps[0][2], ps[0][3]);
-                const uint32_t pa2 = pack_bf16(ps[1][0], ps[1][1]), pa3 = pack_bf16(ps[1][2], ps[1][3]);
-                // O += P V : V rows 0..15 of the page, output n-tiles in pairs
+                // O += P V : one 16-key k-step per page of the chunk, output n-tiles in pairs
 #pragma unroll
-                for (int t = 0; t < NT; t += 2) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4_t(vb + sw_off((lane & 7) + ((lane >> 3) & 1) * 8, t + (lane >> 4)), b0, b1, b2, b3);
-                    mma_bf16(o[t], pa0, pa1, pa2, pa3, b0, b1);
-                    mma_bf16(o[t + 1], pa0, pa1, pa2, pa3, b2, b3);
+                for (int u = 0; u < CP; ++u) {
+                    const uint32_t pa0 = pack_bf16(ps[2 * u][0], ps[2 * u][1]), pa1 = pack_bf16(ps[2 * u][2], ps[2 * u][3]);
+                    const uint32_t pa2 = pack_bf16(ps[2 * u + 1][0], ps[2 * u + 1][1]);
+                    const uint32_t pa3 = pack_bf16(ps[2 * u + 1][2], ps[2 * u + 1][3]);
+#pragma unroll
+                    for (int t = 0; t < NT; t += 2) {
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4_t(vb[u] + sw_off((lane & 7) + ((lane >> 3) & 1) * 8, t + (lane >> 4)), b0, b1, b2, b3);
+                        mma_bf16(o[t], pa0, pa1, pa2, pa3, b0, b1);
+                        mma_bf16(o[t + 1], pa0, pa1, pa2, pa3, b2, b3);
+                    }
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
+            if (lane == 0) {
+#pragma unroll
+                for (int u = 0; u < CP; ++u)
+                    if (u < np) mbar_arrive(smem_u32(&empty[(i0 + u) % S]));
+            }
         }
     }
+    if (stp && threadIdx.x == 0) stp[2] = globaltimer_ns();
     // ---- merge the warps of each m-tile through shared memory (the ring is idle now)
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    float* red = reinterpret_cast<float*>(ring);  // [4 warps][16][DH + 2]
+    float* red = reinterpret_cast<float*>(ring);      // [4 warps][16][DH] partial O
+    float* ml = red + 4 * 16 * DH;                     // [4 warps][16][2] (m, l)
+    float* fw = ml + 4 * 16 * 2;                       // [64][4] per-row weights of the warps
+    float* rml = fw + AT_ROWS * 4;                     // [64][2] merged (M, L)
     consumer_bar();
     if (active) {
-        float* rw = red + (size_t)warp * 16 * (DH + 2);
+        float* rw = red + (size_t)warp * 16 * DH;
         const int lr = lane >> 2;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             const int col = t * 8 + 2 * (lane & 3);
-            rw[lr * (DH + 2) + 2 + col] = o[t][0];
-            rw[lr * (DH + 2) + 3 + col] = o[t][1];
-            rw[(lr + 8) * (DH + 2) + 2 + col] = o[t][2];
-            rw[(lr + 8) * (DH + 2) + 3 + col] = o[t][3];
+            *reinterpret_cast<float2*>(rw + lr * DH + col) = make_float2(o[t][0], o[t][1]);
+            *reinterpret_cast<float2*>(rw + (lr + 8) * DH + col) = make_float2(o[t][2], o[t][3]);
         }
         if ((lane & 3) == 0) {
-            rw[lr * (DH + 2)] = m0;
-            rw[lr * (DH + 2) + 1] = l0;
-            rw[(lr + 8) * (DH + 2)] = m1;
-            rw[(lr + 8) * (DH + 2) + 1] = l1;
+            ml[(warp * 16 + lr) * 2] = m0;
+            ml[(warp * 16 + lr) * 2 + 1] = l0;
+            ml[(warp * 16 + lr + 8) * 2] = m1;
+            ml[(warp * 16 + lr + 8) * 2 + 1] = l1;
         }
+    }
+    consumer_bar();
+    if (threadIdx.x < rows) {
+        const int r = threadIdx.x, mt = r >> 4, lr = r & 15;
+        float M = -INFINITY;
+        for (int w = 0; w < wpm; ++w) M = fmaxf(M, ml[((mt * wpm + w) * 16 + lr) * 2]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float f[4] = {0.f, 0.f, 0.f, 0.f};
+        float L = 0.f;
+        for (int w = 0; w < wpm; ++w) {
+            f[w] = exp2f(ml[((mt * wpm + w) * 16 + lr) * 2] - Mu);
+            L += f[w] * ml[((mt * wpm + w) * 16 + lr) * 2 + 1];
+        }
+        // whole item: normalised weights; split item: raw weights and the (M, L) of the partial
+        const float sc = slot < 0 ? (L > 0.f ? 1.0f / L : 0.f) : 1.0f;
+        for (int w = 0; w < 4; ++w) fw[r * 4 + w] = f[w] * sc;
+        rml[r * 2] = M;
+        rml[r * 2 + 1] = L;
     }
     consumer_bar();
     __nv_bfloat16* outp = reinterpret_cast<__nv_bfloat16*>(p.out);
     const int WR = ws_row(DH);
-    for (int i = threadIdx.x; i < rows * DH; i += 128) {
-        const int r = i / DH, col = i % DH;
+    constexpr int D8 = DH / 8;
+    for (int i = threadIdx.x; i < rows * D8; i += 128) {
+        const int r = i / D8, c8 = (i % D8) * 8;
         const int mt = r >> 4, lr = r & 15;
-        float M = -INFINITY;
-        for (int w = 0; w < wpm; ++w) M = fmaxf(M, red[((size_t)(mt * wpm + w) * 16 + lr) * (DH + 2)]);
-        const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, O = 0.f;
+        float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
         for (int w = 0; w < wpm; ++w) {
-            const float* rw = red + ((size_t)(mt * wpm + w) * 16 + lr) * (DH + 2);
-            const float f = exp2f(rw[0] - Mu);
-            L += f * rw[1];
-            O += f * rw[2 + col];
+            const float f = fw[r * 4 + w];
+            const float* src = red + ((size_t)(mt * wpm + w) * 16 + lr) * DH + c8;
+            const float4 v0 = *reinterpret_cast<const float4*>(src), v1 = *reinterpret_cast<const float4*>(src + 4);
+            a0.x += f * v0.x; a0.y += f * v0.y; a0.z += f * v0.z; a0.w += f * v0.w;
+            a1.x += f * v1.x; a1.y += f * v1.y; a1.z += f * v1.z; a1.w += f * v1.w;
         }
-        const int rr = qt * AT_ROWS + r;
         if (slot < 0) {
-            outp[((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + col] =
-                __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+            const int rr = qt * AT_ROWS + r;
+            __nv_bfloat16* dst = outp + ((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + c8;
+            *reinterpret_cast<uint4*>(dst) =
+                make_uint4(pack_bf16(a0.x, a0.y), pack_bf16(a0.z, a0.w), pack_bf16(a1.x, a1.y), pack_bf16(a1.z, a1.w));
         } else {
             float* wsr = p.ws + ((size_t)slot * AT_ROWS + r) * WR;
-            __stcg(wsr + 4 + col, O);
-            if (col == 0) { __stcg(wsr, M); __stcg(wsr + 1, L); }
+            __stcg(reinterpret_cast<float4*>(wsr + 4 + c8), a0);
+            __stcg(reinterpret_cast<float4*>(wsr + 4 + c8 + 4), a1);
+            if (c8 == 0) __stcg(reinterpret_cast<float4*>(wsr), make_float4(rml[r * 2], rml[r * 2 + 1], 0.f, 0.f));
         }
     }
+    if (stp && threadIdx.x == 0) stp[3] = globaltimer_ns();
     if (slot < 0) return;
     // ---- split item: the last of the group to finish merges all partials in split order
     __threadfence();
@@ -490,8 +587,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
     if (!flags[0]) return;
     __threadfence();
     // per-row split weights f = exp2(M_s - max M) and the total L, then O = sum f O_s
-    float* fw = reinterpret_cast<float*>(ring);           // [64][AT_MAX_SPLITS]
-    float* lt = fw + AT_ROWS * AT_MAX_SPLITS;              // [64]
+    float* sfw = reinterpret_cast<float*>(ring);          // [64][AT_MAX_SPLITS]
+    float* lt = sfw + AT_ROWS * AT_MAX_SPLITS;             // [64]
     if (threadIdx.x < rows) {
         const int r = threadIdx.x;
         float M = -INFINITY;
@@ -502,7 +599,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
             const float* w = p.ws + ((size_t)(first + sp) * AT_ROWS + r) * WR;
             const float f = exp2f(__ldcg(w) - Mu);
             L += f * __ldcg(w + 1);
-            fw[r * AT_MAX_SPLITS + sp] = f;
+            sfw[r * AT_MAX_SPLITS + sp] = f;
         }
         lt[r] = L;
     }
@@ -513,7 +610,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_tc_kernel(const __grid_consta
         const int r = i / D4, c4 = (i % D4) * 4;
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int sp = 0; sp < ns; ++sp) {
-            const float f = fw[r * AT_MAX_SPLITS + sp];
+            const float f = sfw[r * AT_MAX_SPLITS + sp];
             const float4 v =
                 __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(first + sp) * AT_ROWS + r) * WR + 4 + c4));
             O.x += f * v.x;
@@ -560,10 +657,10 @@ int attention_ctas_per_sm(int head_dim) {
 
 // Work list for one forward step and one window setting (see yk_forward_step):
 // spans (sequence, query tile) x KV heads, each cut into equal page-aligned
-// key ranges so the item count fills about one wave of resident CTAs; items
+// key ranges so the item count fills about `waves` waves of resident CTAs; items
 // sorted longest first so the block scheduler balances the tail.
-void plan_attention(const yk_model_config& c, int num_sms, const uint32_t* q_starts, const uint32_t* ctx, int B,
-                    bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots) {
+void plan_attention(const yk_model_config& c, int num_sms, int waves, const uint32_t* q_starts, const uint32_t* ctx,
+                    int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots) {
     const int G = c.n_heads / c.n_kv_heads;
     struct Span { int b, qt, kb, ke; };
     std::vector<Span> spans;
@@ -582,7 +679,7 @@ void plan_attention(const yk_model_config& c, int num_sms, const uint32_t* q_sta
             max_pages = std::max(max_pages, (ke - kb + 15) / 16);
         }
     }
-    const long long target = (long long)num_sms * attention_ctas_per_sm(c.head_dim);
+    const long long target = (long long)num_sms * attention_ctas_per_sm(c.head_dim) * std::max(1, waves);
     auto splits = [&](const Span& s, int kp) {  // pieces of a span at kp pages per piece
         const int pages = (s.ke - s.kb + 15) / 16;
         return std::min(AT_MAX_SPLITS, (pages + kp - 1) / kp);
@@ -656,6 +753,7 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
     p.err = m->e->d_err;
     p.ws = m->attn_ws;
     p.counters = m->attn_counters;
+    p.stamps = nullptr;
     if (c.dtype != YK_DTYPE_BF16) {
         YK_CHECK_CUDA(launch_simt<float>(p, m->e));
         m->e->launches++;
@@ -666,6 +764,10 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
     p.items = m->cur.attn_items[w];
     p.comb = m->cur.attn_comb[w];
     const int ni = m->cur.n_items[w];
+    if (m->attn_stamps && ni <= m->attn_stamps_cap) {
+        p.stamps = m->attn_stamps;
+        m->attn_last_items = ni;
+    }
     switch (c.head_dim) {
         case 64: return launch_tc<64>(pool->tm, p, ni, m->e);
         case 128: return launch_tc<128>(pool->tm, p, ni, m->e);
@@ -696,3 +798,35 @@ yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool) {
 }
 
 }  // namespace yk
+
+// ---------------------------------------------------------------------------
+// Test hooks (include/yk_testing.h).
+// ---------------------------------------------------------------------------
+#include "../../include/yk_testing.h"
+
+extern "C" yk_status ykt_attention_stamps_enable(yk_model* m, int32_t cap) {
+    YK_ARG(m && cap >= 0, "arguments");
+    YK_CHECK_CUDA(cudaSetDevice(m->e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(m->e->stream));
+    if (m->attn_stamps) cudaFree(m->attn_stamps);
+    m->attn_stamps = nullptr;
+    m->attn_stamps_cap = 0;
+    m->attn_last_items = 0;
+    if (cap > 0) {
+        YK_CHECK_CUDA(cudaMalloc(&m->attn_stamps, (size_t)cap * 8 * 8));
+        YK_CHECK_CUDA(cudaMemset(m->attn_stamps, 0, (size_t)cap * 8 * 8));
+        m->attn_stamps_cap = cap;
+    }
+    return YK_OK;
+}
+
+extern "C" yk_status ykt_attention_stamps_read(yk_model* m, uint64_t* host, int32_t cap, int32_t* n_ctas) {
+    YK_ARG(m && host && n_ctas, "arguments");
+    YK_ARG(m->attn_stamps, "attention stamps are not enabled");
+    YK_CHECK_CUDA(cudaSetDevice(m->e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(m->e->stream));
+    const int n = std::min(cap, m->attn_last_items);
+    YK_CHECK_CUDA(cudaMemcpy(host, m->attn_stamps, (size_t)n * 8 * 8, cudaMemcpyDeviceToHost));
+    *n_ctas = n;
+    return YK_OK;
+}

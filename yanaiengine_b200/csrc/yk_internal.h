@@ -62,6 +62,7 @@ struct yk_engine {
     bool pdl = true;                     // programmatic dependent launch (env YK_PDL=0 turns it off)
     int gemm_variant = 0;                // GEMM schedule tuning knob (env YK_GEMM_VARIANT): bit 0 = pure
                                          // stream-K instead of whole tiles + stream-K remainder
+    int attn_waves = 1;                  // attention items per resident CTA slot (env YK_ATTN_WAVES)
     bool profiling = false;
     std::vector<ProfRecord> prof_pending;
     std::vector<cudaEvent_t> prof_free;
@@ -135,6 +136,8 @@ struct yk_model {
     size_t attn_ws_floats = 0;
     int32_t* attn_counters = nullptr;
     int attn_counter_cap = 0;
+    unsigned long long* attn_stamps = nullptr;  // test hook: per-CTA phase stamps, else null
+    int attn_stamps_cap = 0, attn_last_items = 0;
     // TMA maps of activation buffers, keyed by (buffer, token-box rows)
     std::map<std::pair<const void*, int>, CUtensorMap> xmaps;
     std::vector<void*> allocations;
@@ -217,8 +220,8 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
 yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
 yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks,
                         double kv_bytes);
-void plan_attention(const yk_model_config& c, int num_sms, const uint32_t* q_starts, const uint32_t* ctx, int B,
-                    bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots);
+void plan_attention(const yk_model_config& c, int num_sms, int waves, const uint32_t* q_starts, const uint32_t* ctx,
+                    int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots);
 size_t attention_ws_floats_per_slot(int head_dim);
 yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool);
 yk_status launch_embed(yk_model* m, const int32_t* tokens, int T);

@@ -1,0 +1,108 @@
+"""Small single-kernel workloads for profiling (ncu) and timing.
+
+    python -m yanaiengine_b200.kernel_cases attention [--dh 128 --group 4 --kv-heads 8 --seqs 32 --new 6]
+    python -m yanaiengine_b200.kernel_cases gemm [--n 28672 --k 4096 --m 192]
+
+`attention` builds a 2-layer bf16 model whose attention has the verify shape of
+the 8B-class target (or the 1B-class draft with --dh 64 --new 1), fills a KV
+pool with a synthetic context of U[512, 2048] tokens per sequence and runs
+forward steps; the pool holds about 1 GB, one layer's KV (170 MB at the target
+shape) is larger than L2.  `gemm` runs the tcgen05 GEMM test hook on one layer
+shape with an L2 flush before each launch.  Both print one timing line.
+"""
+from __future__ import annotations
+
+import argparse
+import time
+
+import numpy as np
+
+from . import abi
+
+
+def attention(args) -> None:
+    e = abi.Engine(0)
+    H = args.kv_heads * args.group
+    cfg = abi.make_config(vocab_size=1024, d_model=512, n_layers=2, n_heads=H, n_kv_heads=args.kv_heads,
+                          head_dim=args.dh, ffn_dim=1024, rope_theta=500000.0, rms_eps=1e-5, dtype=abi.DTYPE_BF16,
+                          max_tokens=max(64, args.seqs * args.new), max_seqs=args.seqs)
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(512, 2049, args.seqs)
+    pages = [(int(c) + args.new * args.steps + 15) // 16 for c in ctx]
+    nb = sum(pages) + 8
+    m = abi.Model(e, cfg, seed=1)
+    pool = abi.KVPool(e, cfg, nb)
+    pool.fill_random(3, 1.0)
+    tables = np.zeros((args.seqs, max(pages)), np.int32)
+    nxt = 0
+    for b, n in enumerate(pages):
+        tables[b, :n] = np.arange(nxt, nxt + n)
+        nxt += n
+    if args.stamps:
+        m.attention_stamps(4096)
+    times = []
+    for s in range(args.steps):
+        toks = rng.integers(0, 1024, args.seqs * args.new).tolist()
+        qs = list(range(0, args.seqs * args.new + 1, args.new))
+        cl = (ctx + args.new * (s + 1)).tolist()
+        e.sync()
+        t0 = time.perf_counter()
+        m.forward(pool, toks, qs, cl, tables, last_n=1)
+        e.sync()
+        times.append(time.perf_counter() - t0)
+    kv = float(sum(ctx)) * 2 * args.kv_heads * args.dh * 2
+    print(f"attention dh={args.dh} G={args.group} Hkv={args.kv_heads} seqs={args.seqs} new={args.new}: "
+          f"{kv / 1e6:.0f} MB KV per layer, forward step {1e3 * min(times):.3f} ms (2 layers + GEMMs)")
+    if args.stamps:
+        st = m.attention_stamps().astype(np.int64)
+        t0 = st[:, 0].min()
+        start, first, loop, end = ((st[:, i] - t0) / 1e3 for i in range(4))
+        pages = st[:, 4]
+        end = np.where(st[:, 3] > 0, end, loop)
+        print(f"  {len(st)} CTAs on {len(set(st[:, 5].tolist()))} SMs; kernel span {end.max():.1f} us")
+        print(f"  start: median {np.median(start):.1f} max {start.max():.1f} us;"
+              f" first page after start: median {np.median(first - start):.1f} us")
+        busy = loop - first
+        rate = pages * 16 * args.dh * 2 * 2 / np.maximum(busy, 1e-3) / 1e3  # K + V bytes per us -> GB/s
+        print(f"  loop: median {np.median(busy):.1f} max {busy.max():.1f} us; per-CTA GB/s median {np.median(rate):.1f}"
+              f" (pages median {np.median(pages):.0f} max {pages.max()}); merge+write median {np.median(end - loop):.1f} us")
+        for q in (0.1, 0.5, 0.9, 1.0):
+            print(f"  end quantile {q:.1f}: {np.quantile(end, q):.1f} us")
+    pool.close()
+    m.close()
+    e.close()
+
+
+def gemm(args) -> None:
+    e = abi.Engine(0)
+    rng = np.random.default_rng(0)
+    W = abi.bf16_bits(rng.normal(0, 0.05, (args.n, args.k)).astype(np.float32))
+    X = abi.bf16_bits(rng.normal(0, 1, (args.m, args.k)).astype(np.float32))
+    _, ms, _, g = abi.gemm_bf16_timed(e, W, X, 0, -args.reps)
+    gb = (args.n + args.m) * args.k * 2 / 1e9
+    print(f"gemm {args.n}x{args.k}x{args.m} grid={g}: {1e3 * ms:.1f} us cold-L2, {gb / ms:.0f} GB/s")
+    e.close()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="case", required=True)
+    a = sub.add_parser("attention")
+    a.add_argument("--dh", type=int, default=128)
+    a.add_argument("--group", type=int, default=4)
+    a.add_argument("--kv-heads", type=int, default=8)
+    a.add_argument("--seqs", type=int, default=32)
+    a.add_argument("--new", type=int, default=6)
+    a.add_argument("--steps", type=int, default=3)
+    a.add_argument("--stamps", action="store_true", help="per-CTA phase stamps of the last attention launch")
+    g = sub.add_parser("gemm")
+    g.add_argument("--n", type=int, default=28672)
+    g.add_argument("--k", type=int, default=4096)
+    g.add_argument("--m", type=int, default=192)
+    g.add_argument("--reps", type=int, default=3)
+    args = ap.parse_args()
+    attention(args) if args.case == "attention" else gemm(args)
+
+
+if __name__ == "__main__":
+    main()
