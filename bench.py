@@ -306,6 +306,9 @@ def run_yk(args, world, rank, local):
     gemm = eng.profile_read(0)
     attn = eng.profile_read(1)
     eng.profile(False)
+    # in-situ breakdown of one more step from the launch trace (first CTA past the
+    # grid dependency wait, last CTA exit per launch), programmatic launch on
+    breakdown = trace_breakdown(eng, sch)
 
     peaks = measured_peaks()
     res = None
@@ -339,6 +342,7 @@ def run_yk(args, world, rank, local):
                          "peak_src": peaks["src"],
                          "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])},
             "attention": {"achieved_gbs": attn_gbs, "frac": attn_gbs / peaks["hbm_gbs"], "launches": attn["launches"]},
+            "step_breakdown": breakdown,
             "clocks": clk,
         }
     sch.close()
@@ -349,6 +353,53 @@ def run_yk(args, world, rank, local):
     target.close()
     eng.close()
     return res, lens
+
+
+TRACE_KINDS = {1: "embed", 2: "rmsnorm", 3: "gemm", 4: "attention", 5: "draft_sample", 6: "row_stats", 7: "verify"}
+
+
+EPI_NAMES = {0: "store", 1: "qkv", 2: "resid", 3: "glu", 4: "logits"}
+
+
+def trace_name(k: int) -> str:
+    base = TRACE_KINDS.get(k & 15, "other")
+    if base == "gemm":
+        return f"gemm_{EPI_NAMES.get((k >> 4) & 15, '?')}_{128 * ((k >> 8) & 0xFFFF)}x{16 * (k >> 24)}"
+    if base == "attention":
+        return f"attention_dh{k >> 8}"
+    return base
+
+
+def trace_breakdown(eng, sch, cap: int = 8192) -> dict:
+    """One step under the launch trace.  Each launch's share of the step is
+    end[i] - end[i-1] (its kernels finish in stream order), attributed to its kind;
+    `idle` is the part of that share before its first CTA got past the dependency
+    wait (launch latency, host work between forward calls)."""
+    n0 = eng.launches()
+    eng.trace(cap)
+    sch.step()
+    rec, n1 = eng.trace_read()
+    eng.trace(0)
+    ids = [i % cap for i in range(n0, n1)]
+    if not ids or n1 - n0 > cap:
+        return {}
+    r = rec[ids].astype(np.int64)
+    start, end, kind = r[:, 1], r[:, 2], r[:, 3]
+    span = float(end.max() - start[0])
+    out = {"step_us": span / 1e3, "launches": int(len(ids)), "busy_us": {}, "idle_us": 0.0, "count": {}}
+    prev_end = start[0]
+    for k, s0, e0 in zip(kind, start, end):
+        share = max(0, e0 - prev_end)
+        idle = min(share, max(0, s0 - prev_end))
+        name = trace_name(int(k))
+        out["busy_us"][name] = out["busy_us"].get(name, 0.0) + (share - idle) / 1e3
+        out["count"][name] = out["count"].get(name, 0) + 1
+        out["idle_us"] += idle / 1e3
+        prev_end = max(prev_end, e0)
+    out["busy_us"] = {k: round(v, 1) for k, v in sorted(out["busy_us"].items(), key=lambda x: -x[1])}
+    out["idle_us"] = round(out["idle_us"], 1)
+    out["step_us"] = round(out["step_us"], 1)
+    return out
 
 
 def main():

@@ -30,6 +30,14 @@ yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const uint16_t* X
                               int32_t m_tok, int32_t grid, int32_t reps, float* Y, float* ms_per_rep,
                               uint64_t* stamps, int32_t* grid_used);
 
+/* Same timing with a fused epilogue: epi 0 store, 1 QKV (RoPE, K/V to a pool
+ * page per token, head_dim / kv_dim give the split of n_out), 2 residual add,
+ * 3 gate/up activation, 4 logits; outputs go to scratch buffers.  reps < 0:
+ * one launch per L2 flush as above. */
+yk_status ykt_gemm_bf16_epi_timed(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K,
+                                  int32_t m_tok, int32_t grid, int32_t reps, int32_t epi, int32_t head_dim,
+                                  int32_t kv_dim, float* ms_per_rep, uint64_t* stamps, int32_t* grid_used);
+
 /* Per-CTA phase stamps of the paged-attention kernel.  After enable (cap CTAs,
  * cap > 0; 0 disables), every bf16 attention launch of `m` overwrites a device
  * record of 8 words per CTA: %globaltimer at start, first page landed (consumer
@@ -37,6 +45,18 @@ yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const uint16_t* X
  * items in the launch.  read copies the last launch's records (cap x 8). */
 yk_status ykt_attention_stamps_enable(yk_model* m, int32_t cap);
 yk_status ykt_attention_stamps_read(yk_model* m, uint64_t* host, int32_t cap, int32_t* n_ctas);
+
+/* Launch trace of the kernels on the engine stream.  enable(cap) (cap > 0)
+ * resets cap records; launch i (the i-th launch counted by
+ * yk_engine_launches) writes record i % cap: first CTA entry, first CTA past
+ * its grid dependency wait, last CTA exit (%globaltimer ns) and kind (1 embed,
+ * 2 rmsnorm, 3 GEMM, 4 attention, 5 draft sample, 6 row statistics, 7 verify
+ * in the low 4 bits; GEMM adds epilogue << 4, 128-row tiles << 8 and
+ * tokens/16 << 24, attention adds head dim << 8).
+ * cap == 0 turns tracing off.  read copies cap x 4 words (entry, start, end,
+ * kind) and the number of launches so far. */
+yk_status ykt_trace_enable(yk_engine* e, int32_t cap);
+yk_status ykt_trace_read(yk_engine* e, uint64_t* host, int32_t cap, uint64_t* launches);
 
 #ifdef __cplusplus
 }

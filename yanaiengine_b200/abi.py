@@ -102,7 +102,12 @@ _PROTOS = {
     "ykt_gemm_bf16_timed": (C.c_int32, [_P, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int32, C.c_int32,
                                         C.c_int32, C.c_int32, C.c_int32, _F32P, _F32P, C.POINTER(C.c_uint64),
                                         _I32P]),
+    "ykt_gemm_bf16_epi_timed": (C.c_int32, [_P, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int32, C.c_int32,
+                                            C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _F32P,
+                                            C.POINTER(C.c_uint64), _I32P]),
     "ykt_attention_stamps_enable": (C.c_int32, [_P, C.c_int32]),
+    "ykt_trace_enable": (C.c_int32, [_P, C.c_int32]),
+    "ykt_trace_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, C.POINTER(C.c_uint64)]),
     "ykt_attention_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, _I32P]),
 }
 
@@ -219,6 +224,23 @@ def gemm_bf16_timed(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, gr
     return Y, ms.value, st[: g.value], g.value
 
 
+def gemm_bf16_epi_timed(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray, epi: int, grid: int = 0,
+                        reps: int = -5, head_dim: int = 128, kv_dim: int = 1024):
+    """(ms per launch, per-CTA phase stamps, grid used) of the GEMM test hook with a fused epilogue."""
+    n_out, K = W_bits.shape
+    m_tok = X_bits.shape[0]
+    W_bits = np.ascontiguousarray(W_bits, dtype=np.uint16)
+    X_bits = np.ascontiguousarray(X_bits, dtype=np.uint16)
+    ms = C.c_float()
+    cap = max(4096, grid, 8 * ((n_out + 127) // 128) * ((m_tok + 255) // 256))
+    st = np.zeros((cap, 8), np.uint64)
+    g = C.c_int32()
+    check(lib().ykt_gemm_bf16_epi_timed(engine.h, ptr(W_bits, C.c_uint16), ptr(X_bits, C.c_uint16), n_out, K, m_tok,
+                                        grid, reps, epi, head_dim, kv_dim, C.byref(ms), ptr(st, C.c_uint64),
+                                        C.byref(g)))
+    return ms.value, st[: g.value], g.value
+
+
 # ---------------------------------------------------------------------------
 # Thin object wrappers.
 # ---------------------------------------------------------------------------
@@ -232,6 +254,18 @@ class Engine:
         s = _P()
         check(lib().yk_engine_stream(self.h, C.byref(s)))
         return s.value or 0
+
+    def trace(self, cap: int) -> None:
+        """Test hook: (re)start the launch trace with `cap` records (0 stops it)."""
+        check(lib().ykt_trace_enable(self.h, cap))
+        self._trace_cap = cap
+
+    def trace_read(self) -> tuple[np.ndarray, int]:
+        """Launch trace records [cap x 4] (entry, start, end ns, kind) and the launch count."""
+        out = np.zeros((self._trace_cap, 4), np.uint64)
+        n = C.c_uint64()
+        check(lib().ykt_trace_read(self.h, ptr(out, C.c_uint64), self._trace_cap, C.byref(n)))
+        return out, int(n.value)
 
     def sync(self):
         check(lib().yk_engine_sync(self.h))

@@ -82,6 +82,7 @@ extern "C" void yk_engine_destroy(yk_engine* e) {
     cudaStreamSynchronize(e->stream);
     if (e->pinned) cudaFreeHost(e->pinned);
     if (e->d_err) cudaFree(e->d_err);
+    if (e->trace_rec) cudaFree(e->trace_rec);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
 }
@@ -246,6 +247,7 @@ extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, u
     ALLOC(m->act, T * F * es);
     ALLOC(m->logits, T * V * 4);
     ALLOC(m->rope_denom, dh / 2 * 4);
+    ALLOC(m->rope_tab, T * (dh / 2) * sizeof(float2));
     m->gemm_ws_floats = (size_t)2 * e->num_sms * 128 * 256;
     ALLOC(m->gemm_ws, m->gemm_ws_floats * 4);
     m->gemm_counter_cap = 4096;
@@ -619,7 +621,7 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         kv_win += c.window > 0 ? std::min((double)ctx[b], (double)c.window + n - 1) : (double)ctx[b];
     }
     const double kv_tok_bytes = 2.0 * kvd * (double)m->esize;
-    YK_TRY(launch_embed(m, m->cur.tokens, T));
+    YK_TRY(launch_embed(m, m->cur.tokens, m->cur.pos, T));
     for (int l = 0; l < c.n_layers; ++l) {
         LayerWeights& L = m->layers[l];
         YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr));
@@ -634,6 +636,7 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         eq.pos = m->cur.pos;
         eq.slot = m->cur.slot;
         eq.rope_denom = m->rope_denom;
+        eq.rope_tab = m->rope_tab;
         eq.pool = pool->data;
         eq.block_elems = (long long)pool->block_elems;
         eq.layer_off = (long long)l * (long long)pool->layer_elems;
@@ -684,5 +687,41 @@ extern "C" yk_status yk_logits_copy_to_host(yk_model* m, int32_t row0, int32_t r
         cudaMemset(e->d_err, 0, 4);
         return (err & YK_DEV_ERR_TIMEOUT) ? YK_ERR_TIMEOUT : YK_ERR_DEVICE_CHECK;
     }
+    return YK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Launch trace test hooks (include/yk_testing.h).
+// ---------------------------------------------------------------------------
+#include "../../include/yk_testing.h"
+
+extern "C" yk_status ykt_trace_enable(yk_engine* e, int32_t cap) {
+    YK_ARG(e && cap >= 0, "arguments");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    if (e->trace_rec) cudaFree(e->trace_rec);
+    e->trace_rec = nullptr;
+    e->trace_cap = 0;
+    if (cap == 0) return YK_OK;
+    std::vector<yk::TraceRec> init((size_t)cap);
+    for (auto& r : init) {
+        r.entry = ~0ull;
+        r.start = ~0ull;
+        r.end = 0;
+        r.kind = 0;
+    }
+    YK_CHECK_CUDA(cudaMalloc(&e->trace_rec, (size_t)cap * sizeof(yk::TraceRec)));
+    YK_CHECK_CUDA(cudaMemcpy(e->trace_rec, init.data(), (size_t)cap * sizeof(yk::TraceRec), cudaMemcpyHostToDevice));
+    e->trace_cap = (uint32_t)cap;
+    return YK_OK;
+}
+
+extern "C" yk_status ykt_trace_read(yk_engine* e, uint64_t* host, int32_t cap, uint64_t* launches) {
+    YK_ARG(e && host && launches, "arguments");
+    YK_ARG(e->trace_rec && (uint32_t)cap == e->trace_cap, "trace not enabled with this capacity");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    YK_CHECK_CUDA(cudaMemcpy(host, e->trace_rec, (size_t)cap * sizeof(yk::TraceRec), cudaMemcpyDeviceToHost));
+    *launches = e->launches;
     return YK_OK;
 }

@@ -38,6 +38,7 @@ struct AttnParams {
     float* ws;             // split partials [slot][64][dh + 4]: (M, L, -, -, O[dh])
     int layer;
     unsigned long long* stamps;  // test hook: 8 words per CTA, else null
+    Trace tr;
     int max_blocks, T, H, Hkv, dh;
     long long block_elems, layer_off;
     int pool_blocks;
@@ -245,6 +246,7 @@ __global__ void __launch_bounds__(AT_THREADS, AttnCfg<DH>::CTAS_PER_SM)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
+        trace_mark(p.tr, TR_ENTRY);
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&empty[s]), (uint32_t)MT);
@@ -319,6 +321,7 @@ __global__ void __launch_bounds__(AT_THREADS, AttnCfg<DH>::CTAS_PER_SM)
 
     // ---------------- consumers: warps 0..3 ----------------
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(p.tr, TR_START);
     const int my_mt = warp / wpm, my_part = warp % wpm;
     const bool active = my_mt < MT;
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);
@@ -576,6 +579,7 @@ __global__ void __launch_bounds__(AT_THREADS, AttnCfg<DH>::CTAS_PER_SM)
         }
     }
     if (stp && threadIdx.x == 0) stp[3] = globaltimer_ns();
+    if (threadIdx.x == 0) trace_mark(p.tr, TR_END);
     if (slot < 0) return;
     // ---- split item: the last of the group to finish merges all partials in split order
     __threadfence();
@@ -624,7 +628,10 @@ __global__ void __launch_bounds__(AT_THREADS, AttnCfg<DH>::CTAS_PER_SM)
         *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(L > 0.f ? O.x / L : 0.f, L > 0.f ? O.y / L : 0.f),
                                                     pack_bf16(L > 0.f ? O.z / L : 0.f, L > 0.f ? O.w / L : 0.f));
     }
-    if (threadIdx.x == 0) p.counters[cg] = 0;
+    if (threadIdx.x == 0) {
+        p.counters[cg] = 0;
+        trace_mark(p.tr, TR_END);
+    }
 }
 
 template <typename AT>
@@ -754,6 +761,7 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
     p.ws = m->attn_ws;
     p.counters = m->attn_counters;
     p.stamps = nullptr;
+    p.tr = trace_next(m->e, TK_ATTN | ((uint32_t)c.head_dim << 8));  // kind | head dim << 8
     if (c.dtype != YK_DTYPE_BF16) {
         YK_CHECK_CUDA(launch_simt<float>(p, m->e));
         m->e->launches++;

@@ -85,6 +85,34 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
+// Launch trace (test hook).  With tracing on, every kernel of the forward step
+// and the sampler records, for its launch, the first CTA's entry, the first
+// CTA past its grid dependency wait and the last CTA's exit (%globaltimer ns),
+// so gaps and overlap between launches can be read inside a real step.
+// ---------------------------------------------------------------------------
+struct TraceRec {
+    unsigned long long entry, start, end, kind;
+};
+struct Trace {
+    TraceRec* rec = nullptr;  // null: tracing off
+    uint32_t id = 0, kind = 0;
+};
+enum : int { TR_ENTRY = 0, TR_START = 1, TR_END = 2 };
+__device__ __forceinline__ void trace_mark(const Trace& t, int what) {
+    if (t.rec == nullptr) return;
+    TraceRec* r = t.rec + t.id;
+    const unsigned long long now = globaltimer_ns();
+    if (what == TR_ENTRY) {
+        atomicMin(&r->entry, now);
+        r->kind = t.kind;
+    } else if (what == TR_START) {
+        atomicMin(&r->start, now);
+    } else {
+        atomicMax(&r->end, now);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // mbarrier (shared::cta) helpers.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

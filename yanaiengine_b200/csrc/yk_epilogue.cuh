@@ -22,7 +22,9 @@ __device__ __forceinline__ float compat_relu(float v) {
     return v > 0.f ? v : 0.f;
 }
 
-__device__ __forceinline__ float act_silu(float x) { return x / (1.0f + expf(-x)); }
+// x * sigmoid(x) with the fast exponential and division intrinsics: relative
+// error ~1e-6, far below the bf16 rounding of the stored activation.
+__device__ __forceinline__ float act_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float act_gelu_tanh(float x) {
     const float cdf = 0.5f * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
     return x * cdf;
@@ -34,8 +36,15 @@ __device__ __forceinline__ float logit_out(const EpiParams& p, float v) {
     return v;
 }
 
-// RoPE angle of pair (c, c+1) of a head at token j.
+// RoPE angle of pair (c, c+1) of a head at token j: theta = pos / denom[c/2]
+// (fp32 division), cos and sin of theta; from the step's table when present.
 __device__ __forceinline__ void rope_cs(const EpiParams& p, int c, int j, float& cs, float& sn) {
+    if (p.rope_tab) {
+        const float2 t = p.rope_tab[(size_t)j * (p.head_dim >> 1) + (c >> 1)];
+        cs = t.x;
+        sn = t.y;
+        return;
+    }
     const float th = __fdiv_rn((float)p.pos[j], p.rope_denom[c >> 1]);
     sincosf(th, &sn, &cs);
 }
@@ -96,36 +105,40 @@ __device__ __forceinline__ void epi_pair(const EpiParams& p, int n, int j, float
     }
 }
 
-// One output element per lane: row n of token j with value v; `partner` is the
-// value of row n^1 (the other half of a RoPE pair, or gate/up of a GLU pair).
-template <int KIND, typename AT>
-__device__ __forceinline__ void epi_elem(const EpiParams& p, int n, int j, float v, float partner) {
-    if constexpr (KIND == EPI_QKV) {
-        if (p.ref_compat) { v = compat_relu(v); partner = compat_relu(partner); }
-        const int dh = p.head_dim;
-        const bool odd = n & 1;
-        if (n < p.q_dim + p.kv_dim) {  // rotate (x0, x1) = (even row, odd row)
-            const int c = (n < p.q_dim ? n : n - p.q_dim) % dh;
-            float cs, sn;
-            rope_cs(p, c, j, cs, sn);
-            const float x0 = odd ? partner : v, x1 = odd ? v : partner;
-            v = odd ? (x0 * sn + x1 * cs) : (x0 * cs - x1 * sn);
-        }
-        if (n < p.q_dim) {
-            reinterpret_cast<AT*>(p.out)[(size_t)j * p.q_dim + n] = from_f32<AT>(v);
-        } else {
-            const int kv = n < p.q_dim + p.kv_dim ? 0 : 1;
-            const int nn = n - p.q_dim - kv * p.kv_dim;
-            AT* o = pool_elem<AT>(p, kv, nn / dh, nn % dh, j);
-            if (o) *o = from_f32<AT>(v);
-        }
-    } else if constexpr (KIND == EPI_GLU) {
-        if (n & 1) return;  // the even row (gate) writes act(gate) * up
-        float g = v, u = partner;
-        if (p.ref_compat) { g = compat_relu(g); u = compat_relu(u); }
-        const float a = (p.act == 1 ? act_gelu_tanh(g) : act_silu(g)) * u;
-        reinterpret_cast<AT*>(p.out)[(size_t)j * (p.n_out >> 1) + (n >> 1)] = from_f32<AT>(a);
+// QKV rows (n, n+1), n even, of token j with the RoPE (cos, sin) of their pair
+// given (ignored for V rows): Q to the q buffer, K/V to the token's pool slot.
+template <typename AT>
+__device__ __forceinline__ void qkv_pair_cs(const EpiParams& p, int n, int j, float v0, float v1, float cs, float sn) {
+    if (j >= p.m_tok || n >= p.n_out) return;
+    if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
+    if (n < p.q_dim + p.kv_dim) {
+        const float r0 = v0 * cs - v1 * sn, r1 = v0 * sn + v1 * cs;
+        v0 = r0;
+        v1 = r1;
     }
+    AT* o;
+    if (n < p.q_dim) {
+        o = reinterpret_cast<AT*>(p.out) + (size_t)j * p.q_dim + n;
+    } else {
+        const int kv = n < p.q_dim + p.kv_dim ? 0 : 1;
+        const int nn = n - p.q_dim - kv * p.kv_dim;
+        const int sh = __ffs(p.head_dim) - 1;  // head_dim is a power of two
+        o = pool_elem<AT>(p, kv, nn >> sh, nn & (p.head_dim - 1), j);
+        if (!o) return;
+    }
+    o[0] = from_f32<AT>(v0);
+    o[1] = from_f32<AT>(v1);
+}
+// (cos, sin) of RoPE pair index i (= dim / 2) at token j: the step's table, or computed.
+__device__ __forceinline__ float2 rope_pair(const EpiParams& p, int i, int j) {
+    if (p.rope_tab) return p.rope_tab[(size_t)j * (p.head_dim >> 1) + i];
+    float sn, cs;
+    sincosf(__fdiv_rn((float)p.pos[j], p.rope_denom[i]), &sn, &cs);
+    return make_float2(cs, sn);
+}
+// RoPE dimension of row n within its head (Q and K rows; V rows give a value that is not used).
+__device__ __forceinline__ int rope_dim(const EpiParams& p, int n) {
+    return (n < p.q_dim ? n : n - p.q_dim) & (p.head_dim - 1);
 }
 
 // Drains 16 consecutive tokens j0.. of row n: one row per lane, all 32 lanes of
@@ -133,14 +146,52 @@ __device__ __forceinline__ void epi_elem(const EpiParams& p, int n, int j, float
 // 16 loads of the fp32 stream before any store.
 template <int KIND, typename AT>
 __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const float (&v)[16]) {
-    if constexpr (KIND == EPI_QKV || KIND == EPI_GLU) {
+    if constexpr (KIND == EPI_QKV) {
+        // rows (n, n^1) form one RoPE pair: the even lane writes the pair for tokens
+        // j0..j0+7, the odd lane for j0+8..j0+15 (both hold all 16 pairs)
         float w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) w[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
         if (n >= p.n_out) return;
+        const bool odd = n & 1;
+        const int ci = rope_dim(p, n) >> 1;
+        float2 r[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-            if (j0 + i < p.m_tok) epi_elem<KIND, AT>(p, n, j0 + i, v[i], w[i]);
+        for (int i = 0; i < 8; ++i) {  // table reads first, all in flight together
+            const int j = j0 + (odd ? i + 8 : i);
+            r[i] = j < p.m_tok ? rope_pair(p, ci, j) : make_float2(1.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int j = j0 + (odd ? i + 8 : i);
+            const float x0 = odd ? w[i + 8] : v[i], x1 = odd ? v[i + 8] : w[i];
+            if (j < p.m_tok) qkv_pair_cs<AT>(p, n & ~1, j, x0, x1, r[i].x, r[i].y);
+        }
+    } else if constexpr (KIND == EPI_GLU) {
+        // rows (n, n^1) = (gate, up) of one output column: the even lane writes
+        // tokens j0..j0+7, the odd lane j0+8..j0+15 (both hold all 16 pairs)
+        float w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
+        if (n >= p.n_out) return;
+        const bool odd = n & 1;
+        AT* o = reinterpret_cast<AT*>(p.out) + (n >> 1);
+        if (!p.ref_compat && p.act != 1) {  // SiLU, the common case: a compact loop
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int j = j0 + (odd ? i + 8 : i);
+                const float g = odd ? w[i + 8] : v[i], u = odd ? v[i + 8] : w[i];
+                if (j < p.m_tok) o[(size_t)j * (p.n_out >> 1)] = from_f32<AT>(act_silu(g) * u);
+            }
+        } else {
+#pragma unroll 1
+            for (int i = 0; i < 8; ++i) {
+                const int j = j0 + (odd ? i + 8 : i);
+                float g = odd ? w[i + 8] : v[i], u = odd ? v[i + 8] : w[i];
+                if (p.ref_compat) { g = compat_relu(g); u = compat_relu(u); }
+                if (j < p.m_tok) o[(size_t)j * (p.n_out >> 1)] = from_f32<AT>((p.act == 1 ? act_gelu_tanh(g) : act_silu(g)) * u);
+            }
+        }
     } else if constexpr (KIND == EPI_RESID) {
         if (n >= p.n_out) return;
         float hv[16];
@@ -153,13 +204,14 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
     } else {  // EPI_STORE, EPI_LOGITS
         if (n >= p.n_out) return;
         float* o = reinterpret_cast<float*>(p.out);
+        if (KIND == EPI_STORE || (!p.ref_compat && p.cap <= 0.f)) {  // plain store
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            if (j0 + i < p.m_tok) {
-                float a = v[i];
-                if constexpr (KIND == EPI_LOGITS) a = logit_out(p, a);
-                o[(size_t)(j0 + i) * p.n_out + n] = a;
-            }
+            for (int i = 0; i < 16; ++i)
+                if (j0 + i < p.m_tok) o[(size_t)(j0 + i) * p.n_out + n] = v[i];
+        } else {
+#pragma unroll 1
+            for (int i = 0; i < 16; ++i)
+                if (j0 + i < p.m_tok) o[(size_t)(j0 + i) * p.n_out + n] = logit_out(p, v[i]);
         }
     }
 }
@@ -181,22 +233,40 @@ __device__ __forceinline__ void epi_quad(const EpiParams& p, int n, int j, float
         const float4 h = *o;
         *o = make_float4(h.x + v.x, h.y + v.y, h.z + v.z, h.w + v.w);
     } else if constexpr (KIND == EPI_STORE || KIND == EPI_LOGITS) {
-        if constexpr (KIND == EPI_LOGITS) {
+        if (KIND == EPI_LOGITS && (p.ref_compat || p.cap > 0.f)) {
             v.x = logit_out(p, v.x); v.y = logit_out(p, v.y); v.z = logit_out(p, v.z); v.w = logit_out(p, v.w);
         }
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)j * p.n_out + n) = v;
     } else if constexpr (KIND == EPI_GLU) {
         float g0 = v.x, u0 = v.y, g1 = v.z, u1 = v.w;
-        if (p.ref_compat) { g0 = compat_relu(g0); u0 = compat_relu(u0); g1 = compat_relu(g1); u1 = compat_relu(u1); }
-        const float a0 = (p.act == 1 ? act_gelu_tanh(g0) : act_silu(g0)) * u0;
-        const float a1 = (p.act == 1 ? act_gelu_tanh(g1) : act_silu(g1)) * u1;
+        float a0, a1;
+        if (!p.ref_compat && p.act != 1) {
+            a0 = act_silu(g0) * u0;
+            a1 = act_silu(g1) * u1;
+        } else {
+            if (p.ref_compat) { g0 = compat_relu(g0); u0 = compat_relu(u0); g1 = compat_relu(g1); u1 = compat_relu(u1); }
+            a0 = (p.act == 1 ? act_gelu_tanh(g0) : act_silu(g0)) * u0;
+            a1 = (p.act == 1 ? act_gelu_tanh(g1) : act_silu(g1)) * u1;
+        }
         AT* o = reinterpret_cast<AT*>(p.out) + (size_t)j * (p.n_out >> 1) + (n >> 1);
         o[0] = from_f32<AT>(a0);
         o[1] = from_f32<AT>(a1);
     } else if constexpr (KIND == EPI_QKV) {
-        epi_pair<KIND, AT>(p, n, j, v.x, v.y);
-        epi_pair<KIND, AT>(p, n + 2, j, v.z, v.w);
+        const int ci = rope_dim(p, n) >> 1;
+        const float2 r0 = rope_pair(p, ci, j), r1 = rope_pair(p, ci + 1, j);
+        qkv_pair_cs<AT>(p, n, j, v.x, v.y, r0.x, r0.y);
+        qkv_pair_cs<AT>(p, n + 2, j, v.z, v.w, r1.x, r1.y);
     }
 }
 
+}  // namespace yk
+
+namespace yk {
+// QKV rows n..n+3 of token j with the (cos, sin) of their two RoPE pairs loaded by the caller.
+template <typename AT>
+__device__ __forceinline__ void epi_quad_qkv(const EpiParams& p, int n, int j, float4 v, float4 rope) {
+    if (j >= p.m_tok || n >= p.n_out) return;
+    qkv_pair_cs<AT>(p, n, j, v.x, v.y, rope.x, rope.y);
+    qkv_pair_cs<AT>(p, n + 2, j, v.z, v.w, rope.z, rope.w);
+}
 }  // namespace yk

@@ -35,6 +35,8 @@ constexpr int TC_BM = 128;       // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;        // k per stage: one 128-byte swizzle row of bf16
 constexpr int TC_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
 constexpr int TC_SMEM_BUDGET = 200 * 1024;
+constexpr int TC_QKV_STAGE_TOK = 256;  // tokens whose QKV epilogue metadata is staged in shared memory
+constexpr int TC_SMEM_TAIL = 1024 + 256 + (2 * TC_QKV_STAGE_TOK + 128) * 4;  // align slack, barriers, QKV staging
 
 struct TcArgs {
     int n_out, K, m_tok;
@@ -49,6 +51,7 @@ struct TcArgs {
     uint32_t* counters;         // per-tile arrival counters (zero between launches)
     EpiParams epi;
     unsigned long long* stamps;  // optional per-CTA phase timestamps (test hook), else null
+    Trace tr;
 };
 
 // Phase timestamps of one CTA (ns, %globaltimer), recorded only when a.stamps != null.
@@ -127,8 +130,8 @@ __device__ __forceinline__ void epi_bar_sync() {  // named barrier over the 4 ep
 // parked in the cluster's shared memory in rank order.  QN items per thread and
 // round keep QN*CS distributed-shared-memory loads in flight.
 template <int KIND, int CS>
-__device__ __forceinline__ void cluster_reduce(const TcArgs& a, uint32_t red_addr, int tm, int tn, int c0, int c1,
-                                               bool ok) {
+__device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams& ep, uint32_t red_addr, int tm, int tn,
+                                               int c0, int c1, bool ok) {
     constexpr int QN = CS >= 16 ? 1 : 16 / CS;
     const int nitems = (c1 - c0) * 32;  // (column, 4-row group) items
     uint32_t rb[CS];
@@ -136,7 +139,7 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, uint32_t red_add
     for (int s = 0; s < CS; ++s) rb[s] = mapa_shared(red_addr, (uint32_t)s);
     for (int base = threadIdx.x; base < nitems; base += TC_THREADS * QN) {
         float4 tv[QN][CS];
-        float4 hv[KIND == EPI_RESID ? QN : 1];
+        float4 hv[(KIND == EPI_RESID || KIND == EPI_QKV) ? QN : 1];
         if constexpr (KIND == EPI_RESID) {
             // the residual stream values, in flight together with the partials
 #pragma unroll
@@ -145,6 +148,23 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, uint32_t red_add
                 const int n = tm * TC_BM + (it % 32) * 4, j = tn * a.BN + c0 + it / 32;
                 if (ok && it < nitems && j < a.epi.m_tok && n < a.epi.n_out)
                     hv[q] = *reinterpret_cast<const float4*>(a.epi.h + (size_t)j * a.epi.ld + n);
+            }
+        } else if constexpr (KIND == EPI_QKV) {
+            // the RoPE (cos, sin) of the quad's two pairs, in flight with the partials
+#pragma unroll
+            for (int q = 0; q < QN; ++q) {
+                const int it = base + q * TC_THREADS;
+                const int n = tm * TC_BM + (it % 32) * 4, j = tn * a.BN + c0 + it / 32;
+                hv[q] = make_float4(1.f, 0.f, 1.f, 0.f);
+                if (ok && it < nitems && j < ep.m_tok && n < ep.q_dim + ep.kv_dim) {
+                    const int ci = rope_dim(ep, n) >> 1;
+                    if (ep.rope_tab) {
+                        hv[q] = *reinterpret_cast<const float4*>(ep.rope_tab + (size_t)j * (ep.head_dim >> 1) + ci);
+                    } else {
+                        const float2 r0 = rope_pair(ep, ci, j), r1 = rope_pair(ep, ci + 1, j);
+                        hv[q] = make_float4(r0.x, r0.y, r1.x, r1.y);
+                    }
+                }
             }
         }
 #pragma unroll
@@ -171,8 +191,10 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, uint32_t red_add
                 const int n = tm * TC_BM + (it % 32) * 4, j = tn * a.BN + c0 + it / 32;
                 if constexpr (KIND == EPI_RESID) {
                     if (j < a.epi.m_tok && n < a.epi.n_out) epi_quad_resid(a.epi, n, j, acc, hv[q]);
+                } else if constexpr (KIND == EPI_QKV) {
+                    epi_quad_qkv<__nv_bfloat16>(ep, n, j, acc, hv[q]);
                 } else {
-                    epi_quad<KIND, __nv_bfloat16>(a.epi, n, j, acc);
+                    epi_quad<KIND, __nv_bfloat16>(ep, n, j, acc);
                 }
             }
         }
@@ -198,6 +220,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int c = blockIdx.x, KB = a.kb_total;
     const int CS = a.cluster_s;
     const TcSched sc = tc_sched(a, c);
+    // The QKV epilogue's per-token positions / page slots and the RoPE
+    // denominators, staged in shared memory (verify-sized token counts).
+    EpiParams ep = a.epi;
+    constexpr bool kStageQkv = KIND == EPI_QKV;
+    int32_t* qkv_smem = reinterpret_cast<int32_t*>(tmem_slot + 8);  // past the slot and the 4 flags
+    const bool stage_qkv = kStageQkv && a.epi.m_tok <= TC_QKV_STAGE_TOK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -211,6 +239,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         flags[0] = flags[1] = flags[2] = flags[3] = 0;
         mbar_fence_init();
     }
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
+    if (stage_qkv) {
+        // step metadata is uploaded before the step's first kernel: no dependency wait needed
+        float* den = reinterpret_cast<float*>(qkv_smem + 2 * TC_QKV_STAGE_TOK);
+        for (int i = threadIdx.x; i < a.epi.m_tok; i += TC_THREADS) {
+            qkv_smem[i] = a.epi.pos[i];
+            qkv_smem[TC_QKV_STAGE_TOK + i] = a.epi.slot[i];
+        }
+        for (int i = threadIdx.x; i < a.epi.head_dim / 2; i += TC_THREADS) den[i] = a.epi.rope_denom[i];
+        ep.pos = qkv_smem;
+        ep.slot = qkv_smem + TC_QKV_STAGE_TOK;
+        ep.rope_denom = den;
+    }
     if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 2 * a.tmem_cols);
     tc_fence_before();
     __syncthreads();
@@ -220,6 +261,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) stamp(a, ST_START);
     // Everything but the weight prefetch below reads or writes what earlier kernels touch.
     if (threadIdx.x != 0) pdl_wait();
+    if (threadIdx.x == 32) trace_mark(a.tr, TR_START);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -347,7 +389,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     float v[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-                    drain16<KIND, __nv_bfloat16>(a.epi, n, j_base + cc, v);
+                    drain16<KIND, __nv_bfloat16>(ep, n, j_base + cc, v);
                 }
             } else {
                 // tile cut across CTAs: publish this partial; the last arriver finishes the tile
@@ -407,7 +449,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const int col = cc + cq + 4 * i;
-                            if (col < BN) epi_quad<KIND, __nv_bfloat16>(a.epi, tm * TC_BM + r4, j_base + col, acc[i]);
+                            if (col < BN) epi_quad<KIND, __nv_bfloat16>(ep, tm * TC_BM + r4, j_base + col, acc[i]);
                         }
                     }
                     if (et == 0) a.counters[t] = 0u;
@@ -435,14 +477,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t red_addr = smem_u32(smem);
         const bool ok = flags[0] == 0;
         switch (CS) {
-            case 1: cluster_reduce<KIND, 1>(a, red_addr, tm, tn, c0, c1, ok); break;
-            case 2: cluster_reduce<KIND, 2>(a, red_addr, tm, tn, c0, c1, ok); break;
-            case 3: cluster_reduce<KIND, 3>(a, red_addr, tm, tn, c0, c1, ok); break;
-            case 4: cluster_reduce<KIND, 4>(a, red_addr, tm, tn, c0, c1, ok); break;
-            case 5: cluster_reduce<KIND, 5>(a, red_addr, tm, tn, c0, c1, ok); break;
-            case 6: cluster_reduce<KIND, 6>(a, red_addr, tm, tn, c0, c1, ok); break;
-            case 7: cluster_reduce<KIND, 7>(a, red_addr, tm, tn, c0, c1, ok); break;
-            default: cluster_reduce<KIND, 8>(a, red_addr, tm, tn, c0, c1, ok); break;
+            case 1: cluster_reduce<KIND, 1>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+            case 2: cluster_reduce<KIND, 2>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+            case 3: cluster_reduce<KIND, 3>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+            case 4: cluster_reduce<KIND, 4>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+            case 5: cluster_reduce<KIND, 5>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+            case 6: cluster_reduce<KIND, 6>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+            case 7: cluster_reduce<KIND, 7>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+            default: cluster_reduce<KIND, 8>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
         }
         cluster_sync_any();  // no CTA releases shared memory a peer still reads
         if (threadIdx.x == 64) stamp(a, ST_EPI_DONE);
@@ -453,6 +495,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, 2 * a.tmem_cols);
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_END);
 }
 
 // ---------------------------------------------------------------------------
@@ -545,7 +588,7 @@ static yk_status launch_tc(const cudaLaunchConfig_t& cfg, const CUtensorMap* tmW
     static bool attr = false;
     if (!attr) {
         YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           TC_SMEM_BUDGET + 16384 + 2048));
+                                           TC_SMEM_BUDGET + 16384 + TC_SMEM_TAIL));
         attr = true;
     }
     YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<KIND>, *tmW, *tmX, a));
@@ -563,11 +606,11 @@ static int cluster_capacity(yk_engine* e, int s) {
     }
     if (cap[s] == 0) {
         cudaFuncSetAttribute(gemm_tc_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             TC_SMEM_BUDGET + 16384 + 2048);
+                             TC_SMEM_BUDGET + 16384 + TC_SMEM_TAIL);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(s * 64);
         cfg.blockDim = dim3(TC_THREADS);
-        cfg.dynamicSmemBytes = TC_SMEM_BUDGET + 1280;
+        cfg.dynamicSmemBytes = TC_SMEM_BUDGET + TC_SMEM_TAIL;
         cudaLaunchAttribute at[1];
         at[0].id = cudaLaunchAttributeClusterDimension;
         at[0].val.clusterDim.x = s;
@@ -668,7 +711,7 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     }
     const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
     const int stages = std::max(2, std::min(8, (int)(TC_SMEM_BUDGET / stage_bytes)));
-    const size_t smem = (size_t)stages * stage_bytes + 1024 + 256;
+    const size_t smem = (size_t)stages * stage_bytes + TC_SMEM_TAIL;
     uint32_t cols = 32;
     while ((int)cols < BN) cols <<= 1;
 
@@ -686,6 +729,9 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     a.counters = m->gemm_counters;
     a.epi = ep;
     a.stamps = m->gemm_stamps;
+    // trace kind: GEMM | epilogue << 4 | 128-row tiles << 8 | tokens / 16 << 24
+    a.tr = trace_next(e, TK_GEMM | ((uint32_t)ep.kind << 4) | ((uint32_t)tiles_m << 8) |
+                             ((uint32_t)((m_tok + 15) / 16) << 24));
     m->gemm_last_grid = grid;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -823,4 +869,132 @@ extern "C" yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const 
 extern "C" yk_status ykt_gemm_bf16(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out, int32_t K,
                                    int32_t m_tok, int32_t grid, float* Y) {
     return ykt_gemm_bf16_timed(e, W, X, n_out, K, m_tok, grid, 1, Y, nullptr, nullptr, nullptr);
+}
+
+extern "C" yk_status ykt_gemm_bf16_epi_timed(yk_engine* e, const uint16_t* W, const uint16_t* X, int32_t n_out,
+                                             int32_t K, int32_t m_tok, int32_t grid, int32_t reps, int32_t epi,
+                                             int32_t head_dim, int32_t kv_dim, float* ms_per_rep, uint64_t* stamps,
+                                             int32_t* grid_used) {
+    YK_ARG(e && W && X && n_out > 0 && K > 0 && m_tok > 0 && reps != 0 && epi >= 0 && epi <= 4, "arguments");
+    YK_ARG(epi != yk::EPI_QKV || (head_dim > 0 && kv_dim > 0 && n_out > 2 * kv_dim && kv_dim % head_dim == 0),
+           "QKV split");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const bool cold = reps < 0;
+    if (cold) reps = -reps;
+    yk_model m;
+    m.e = e;
+    m.cfg.dtype = YK_DTYPE_BF16;
+    m.cfg.max_tokens = m_tok;
+    std::vector<void*> bufs;
+    auto dmalloc = [&](size_t bytes) -> void* {
+        void* ptr = nullptr;
+        if (cudaMalloc(&ptr, bytes) != cudaSuccess) return nullptr;
+        cudaMemset(ptr, 0, bytes);
+        bufs.push_back(ptr);
+        return ptr;
+    };
+    constexpr size_t kFlushBytes = size_t(256) << 20;
+    const int max_grid = std::max(std::max(grid, 4 * e->num_sms), 8 * ((n_out + 127) / 128) * ((m_tok + 255) / 256));
+    m.gemm_ws_floats = (size_t)2 * std::max(grid, e->num_sms) * 128 * 256;
+    m.gemm_counter_cap = 4096;
+    void* dW = dmalloc((size_t)n_out * K * 2);
+    void* dX = dmalloc((size_t)m_tok * K * 2);
+    void* dY = dmalloc((size_t)m_tok * n_out * 4);
+    m.gemm_ws = (float*)dmalloc(m.gemm_ws_floats * 4);
+    m.gemm_counters = (uint32_t*)dmalloc((size_t)m.gemm_counter_cap * 4);
+    m.gemm_stamps = stamps ? (unsigned long long*)dmalloc((size_t)max_grid * 8 * 8) : nullptr;
+    void* dFlush = cold ? dmalloc(kFlushBytes) : nullptr;
+    yk::EpiParams ep;
+    ep.kind = epi;
+    ep.out = dY;
+    ep.h = (float*)dY;
+    ep.ld = n_out;
+    ep.act = YK_ACT_SILU;
+    int32_t *dpos = nullptr, *dslot = nullptr;
+    float* dden = nullptr;
+    void* dpool = nullptr;
+    if (epi == yk::EPI_QKV) {
+        const int n_kv = kv_dim / head_dim;
+        ep.q_dim = n_out - 2 * kv_dim;
+        ep.kv_dim = kv_dim;
+        ep.head_dim = head_dim;
+        ep.n_kv = n_kv;
+        ep.block_elems = (long long)2 * n_kv * 16 * head_dim;
+        ep.layer_off = 0;
+        ep.pool_blocks = m_tok;
+        dpool = dmalloc((size_t)ep.block_elems * m_tok * 2);
+        dpos = (int32_t*)dmalloc((size_t)m_tok * 4);
+        dslot = (int32_t*)dmalloc((size_t)m_tok * 4);
+        dden = (float*)dmalloc((size_t)head_dim / 2 * 4);
+        std::vector<int32_t> hp(m_tok), hs(m_tok);
+        for (int t = 0; t < m_tok; ++t) {
+            hp[t] = 1000 + t;
+            hs[t] = t * 16;
+        }
+        std::vector<float> hd(head_dim / 2);
+        for (int i = 0; i < head_dim / 2; ++i) hd[i] = powf(500000.0f, 2.0f * i / head_dim);
+        if (dpos && dslot && dden) {
+            cudaMemcpy(dpos, hp.data(), hp.size() * 4, cudaMemcpyHostToDevice);
+            cudaMemcpy(dslot, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice);
+            cudaMemcpy(dden, hd.data(), hd.size() * 4, cudaMemcpyHostToDevice);
+        }
+        ep.pool = dpool;
+        ep.pos = dpos;
+        ep.slot = dslot;
+        ep.rope_denom = dden;
+    }
+    yk_status s = YK_OK;
+    for (void* b : bufs)
+        if (!b) s = YK_ERR_OOM;
+    if (!dW || !dX || !dY || !m.gemm_ws || !m.gemm_counters || (stamps && !m.gemm_stamps) || (cold && !dFlush) ||
+        (epi == yk::EPI_QKV && (!dpool || !dpos || !dslot || !dden)))
+        s = YK_ERR_OOM;
+    CUtensorMap tmW;
+    if (s == YK_OK) {
+        cudaMemcpy(dW, W, (size_t)n_out * K * 2, cudaMemcpyHostToDevice);
+        cudaMemcpy(dX, X, (size_t)m_tok * K * 2, cudaMemcpyHostToDevice);
+        s = yk::make_weight_map(e, &tmW, dW, n_out, K);
+    }
+    if (s == YK_OK) s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, grid);  // warm-up
+    float ms = 0.f;
+    if (s == YK_OK) {
+        cudaEvent_t t0, t1;
+        cudaEventCreate(&t0);
+        cudaEventCreate(&t1);
+        for (int r = 0; r < reps && s == YK_OK; ++r) {
+            if (cold) cudaMemsetAsync(dFlush, r & 0xff, kFlushBytes, e->stream);
+            cudaEventRecord(t0, e->stream);
+            s = yk::gemm_run(&m, dW, &tmW, dX, n_out, K, m_tok, ep, grid);
+            cudaEventRecord(t1, e->stream);
+            cudaEventSynchronize(t1);
+            float one = 0.f;
+            cudaEventElapsedTime(&one, t0, t1);
+            ms += one;
+        }
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+        const cudaError_t ce = cudaStreamSynchronize(e->stream);
+        if (s == YK_OK && ce != cudaSuccess) {
+            yk_set_error(std::string("ykt_gemm_bf16_epi_timed: ") + cudaGetErrorString(ce));
+            s = YK_ERR_CUDA;
+        }
+        if (s == YK_OK && stamps)
+            cudaMemcpy(stamps, m.gemm_stamps, (size_t)m.gemm_last_grid * 8 * 8, cudaMemcpyDeviceToHost);
+    }
+    if (ms_per_rep) *ms_per_rep = ms / reps;
+    if (grid_used) *grid_used = m.gemm_last_grid;
+    uint32_t err = 0;
+    cudaMemcpy(&err, e->d_err, 4, cudaMemcpyDeviceToHost);
+    if (s == YK_OK && err) {
+        cudaMemset(e->d_err, 0, 4);
+        yk_set_error("ykt_gemm_bf16_epi_timed: device error word " + std::to_string(err));
+        s = (err & YK_DEV_ERR_TIMEOUT) ? YK_ERR_TIMEOUT : YK_ERR_DEVICE_CHECK;
+    }
+    cudaStreamSynchronize(e->stream);
+    for (void* b : bufs)
+        if (b) cudaFree(b);
+    m.gemm_ws = nullptr;
+    m.gemm_counters = nullptr;
+    m.gemm_stamps = nullptr;
+    return s;
 }

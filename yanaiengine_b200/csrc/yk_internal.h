@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "../../include/yk.h"
+#include "yk_common.cuh"
 
 // ---- error plumbing --------------------------------------------------------
 void yk_set_error(const std::string& msg);
@@ -64,6 +65,8 @@ struct yk_engine {
                                          // stream-K instead of whole tiles + stream-K remainder
     int attn_waves = 1;                  // attention items per resident CTA slot (env YK_ATTN_WAVES)
     bool profiling = false;
+    void* trace_rec = nullptr;           // launch trace records (test hook), else null
+    uint32_t trace_cap = 0;
     std::vector<ProfRecord> prof_pending;
     std::vector<cudaEvent_t> prof_free;
     ProfTotals prof[4];
@@ -113,6 +116,7 @@ struct yk_model {
     void* act = nullptr;       // [T x F]
     float* logits = nullptr;   // [T x V]
     float* rope_denom = nullptr;  // [dh/2]
+    float2* rope_tab = nullptr;   // [max_tokens x dh/2] (cos, sin) of this step's token positions
     // step metadata (device), packed as int32
     int32_t* meta = nullptr;
     size_t meta_cap = 0;       // int32 elements
@@ -168,6 +172,18 @@ struct yk_sampler {
 // ---- internal launchers ----------------------------------------------------
 namespace yk {
 
+// Trace handle for the launch about to be made (kinds: see TraceKind).
+enum TraceKind : uint32_t {
+    TK_EMBED = 1, TK_RMSNORM = 2, TK_GEMM = 3, TK_ATTN = 4, TK_DRAFT_SAMPLE = 5, TK_ROW_STATS = 6, TK_VERIFY = 7
+};
+inline Trace trace_next(yk_engine* e, uint32_t kind) {
+    Trace t;
+    t.rec = reinterpret_cast<TraceRec*>(e->trace_rec);
+    t.id = e->trace_cap ? (uint32_t)(e->launches % e->trace_cap) : 0u;
+    t.kind = kind;
+    return t;
+}
+
 // Launch on the engine stream with programmatic dependent launch (the kernel
 // must call pdl_wait before touching what earlier kernels wrote).  Off while
 // profiling: the per-launch events sit between kernels anyway.
@@ -202,6 +218,7 @@ struct EpiParams {
     const int32_t* pos = nullptr;    // [m_tok] token positions
     const int32_t* slot = nullptr;   // [m_tok] pool slot = block*16 + offset
     const float* rope_denom = nullptr;
+    const float2* rope_tab = nullptr;  // [m_tok x head_dim/2] (cos, sin); null: computed per element
     void* pool = nullptr;
     long long block_elems = 0, layer_off = 0;
     int pool_blocks = 0;
@@ -224,7 +241,7 @@ void plan_attention(const yk_model_config& c, int num_sms, int waves, const uint
                     int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots);
 size_t attention_ws_floats_per_slot(int head_dim);
 yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool);
-yk_status launch_embed(yk_model* m, const int32_t* tokens, int T);
+yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T);
 yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx);
 yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed, uint32_t stream, float std,
                       bool constant);

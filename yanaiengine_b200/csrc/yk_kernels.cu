@@ -5,12 +5,22 @@
 namespace yk {
 
 // embedding_lookup_kernel (S/gemm.metal:326-341): h[t] = E[tokens[t]], fp32 residual stream.
+// Also the step's RoPE table: rope[t][i] = (cos, sin)(pos[t] / denom[i]), the
+// angle of dimension pair i at token t that every layer's QKV epilogue uses.
 template <typename WT>
 __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict__ tokens, float* __restrict__ h,
-                             int d, int V, uint32_t* err) {
+                             int d, int V, const int32_t* __restrict__ pos, const float* __restrict__ denom,
+                             float2* __restrict__ rope, int half_dh, uint32_t* err, Trace tr) {
+    if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(tr, TR_START);
     const int t = blockIdx.x;
+    for (int i = threadIdx.x; i < half_dh; i += blockDim.x) {
+        float sn, cs;
+        sincosf(__fdiv_rn((float)pos[t], denom[i]), &sn, &cs);
+        rope[(size_t)t * half_dh + i] = make_float2(cs, sn);
+    }
     const int tok = tokens[t];
     if (tok < 0 || tok >= V) {
         if (threadIdx.x == 0) raise_err(err, YK_DEV_ERR_BOUNDS);
@@ -18,34 +28,70 @@ __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict
     }
     const WT* row = E + (size_t)tok * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) h[(size_t)t * d + i] = to_f32(row[i]);
+    if (threadIdx.x == 0) trace_mark(tr, TR_END);
 }
 
 // rmsnorm_kernel (S/gemm.metal:377-401): y = x * rsqrt(mean(x^2) + eps) * gamma,
-// one CTA per row, fp32 statistics.  rows != nullptr gathers input rows.
+// one CTA per row, fp32 statistics.  rows != nullptr gathers input rows.  The
+// row stays in registers (float4 loads, up to RN_VEC vectors per thread): one
+// read of x, one block reduction, one bf16/fp32 write.
+constexpr int RN_THREADS = 256, RN_VEC = 4;  // rows up to 4096 elements in registers
+__device__ __forceinline__ void store4(float* y, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(y) = make_float4(a, b, c, d);
+}
+__device__ __forceinline__ void store4(__nv_bfloat16* y, float a, float b, float c, float d) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    *reinterpret_cast<uint2*>(y) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
 template <typename AT>
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ g, AT* __restrict__ y, int d,
-                               float eps, const int32_t* __restrict__ rows) {
+__global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                                            AT* __restrict__ y, int d, float eps,
+                                                            const int32_t* __restrict__ rows, Trace tr) {
+    if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(tr, TR_START);
     const int r = blockIdx.x;
     const int src = rows ? rows[r] : r;
     const float* xr = x + (size_t)src * d;
+    __shared__ float red[RN_THREADS / 32];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) ss += xr[i] * xr[i];
-    __shared__ float red[32];
+    const bool vec = (d & 3) == 0 && d <= RN_THREADS * 4 * RN_VEC;
+    float4 xv[RN_VEC];
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < RN_VEC; ++k) {
+            const int i = (threadIdx.x + k * RN_THREADS) * 4;
+            xv[k] = i < d ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y + xv[k].z * xv[k].z + xv[k].w * xv[k].w;
+        }
+    } else {
+        for (int i = threadIdx.x; i < d; i += RN_THREADS) ss += xr[i] * xr[i];
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    float tot = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (threadIdx.x == 0) red[0] = v;
+    for (int w = 0; w < RN_THREADS / 32; ++w) tot += red[w];
+    const float rms = 1.0f / sqrtf(tot / (float)d + eps);
+    AT* yr = y + (size_t)r * d;
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < RN_VEC; ++k) {
+            const int i = (threadIdx.x + k * RN_THREADS) * 4;
+            if (i < d) {
+                const float4 gv = *reinterpret_cast<const float4*>(g + i);
+                store4(yr + i, xv[k].x * rms * gv.x, xv[k].y * rms * gv.y, xv[k].z * rms * gv.z,
+                       xv[k].w * rms * gv.w);
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < d; i += RN_THREADS) yr[i] = from_f32<AT>(xr[i] * rms * g[i]);
     }
-    __syncthreads();
-    const float rms = 1.0f / sqrtf(red[0] / (float)d + eps);
-    for (int i = threadIdx.x; i < d; i += blockDim.x) y[(size_t)r * d + i] = from_f32<AT>(xr[i] * rms * g[i]);
+    if (threadIdx.x == 0) trace_mark(tr, TR_END);
 }
 
 // N(0, std) from Philox (Box-Muller), counter = (index lo, index hi, stream, 0).
@@ -68,14 +114,16 @@ __global__ void fill_kernel(T* __restrict__ out, size_t n, float v) {
 }
 
 // Host launchers -------------------------------------------------------------
-yk_status launch_embed(yk_model* m, const int32_t* tokens, int T) {
+yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T) {
     const auto& c = m->cfg;
     if (c.dtype == YK_DTYPE_BF16)
         YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<__nv_bfloat16>, T, 256, 0, (const __nv_bfloat16*)m->embed, tokens,
-                                 m->h, c.d_model, c.vocab_size, m->e->d_err));
+                                 m->h, c.d_model, c.vocab_size, pos, (const float*)m->rope_denom, m->rope_tab,
+                                 c.head_dim / 2, m->e->d_err, trace_next(m->e, TK_EMBED)));
     else
         YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<float>, T, 256, 0, (const float*)m->embed, tokens, m->h, c.d_model,
-                                 c.vocab_size, m->e->d_err));
+                                 c.vocab_size, pos, (const float*)m->rope_denom, m->rope_tab, c.head_dim / 2,
+                                 m->e->d_err, trace_next(m->e, TK_EMBED)));
     m->e->launches++;
     return YK_OK;
 }
@@ -83,11 +131,11 @@ yk_status launch_embed(yk_model* m, const int32_t* tokens, int T) {
 yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx) {
     const auto& c = m->cfg;
     if (c.dtype == YK_DTYPE_BF16)
-        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<__nv_bfloat16>, rows, 256, 0, (const float*)m->h, g,
-                                 (__nv_bfloat16*)m->xn, c.d_model, c.rms_eps, row_idx));
+        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<__nv_bfloat16>, rows, RN_THREADS, 0, (const float*)m->h, g,
+                                 (__nv_bfloat16*)m->xn, c.d_model, c.rms_eps, row_idx, trace_next(m->e, TK_RMSNORM)));
     else
-        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<float>, rows, 256, 0, (const float*)m->h, g, (float*)m->xn,
-                                 c.d_model, c.rms_eps, row_idx));
+        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<float>, rows, RN_THREADS, 0, (const float*)m->h, g, (float*)m->xn,
+                                 c.d_model, c.rms_eps, row_idx, trace_next(m->e, TK_RMSNORM)));
     m->e->launches++;
     return YK_OK;
 }

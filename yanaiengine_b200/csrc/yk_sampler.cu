@@ -128,9 +128,11 @@ __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, fl
 // Row statistics for many rows: stats[r] = (max, sum, argmax).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(SMP_THREADS) row_stats_kernel(const float* __restrict__ logits, int64_t V, float T,
-                                                                 float* __restrict__ stats) {
+                                                                 float* __restrict__ stats, Trace tr) {
+    if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(tr, TR_START);
     const int r = blockIdx.x;
     const RowStats st = block_row_stats(logits + (size_t)r * V, V, T);
     if (threadIdx.x == 0) {
@@ -138,6 +140,7 @@ __global__ void __launch_bounds__(SMP_THREADS) row_stats_kernel(const float* __r
         stats[r * 4 + 1] = st.s;
         stats[r * 4 + 2] = __int_as_float(st.arg);
     }
+    if (threadIdx.x == 0) trace_mark(tr, TR_END);
 }
 
 // ---------------------------------------------------------------------------
@@ -156,12 +159,15 @@ struct DraftArgs {
     const uint32_t* seq_ids;
     float* probs;
     uint32_t* tokens_out;
+    Trace tr;
 };
 
 __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) {
     __shared__ ChainSmem cs;
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_START);
     const int b = a.j_fixed >= 0 ? blockIdx.x : blockIdx.x / a.k;
     const int j = a.j_fixed >= 0 ? a.j_fixed : blockIdx.x % a.k;
     const float* row = a.logits + ((size_t)b * a.logit_row_stride + (size_t)j * a.logit_row_j_mul) * a.V;
@@ -192,6 +198,7 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
     if (threadIdx.x == 0) {
         if (a.j_fixed >= 0) a.tokens_out[b] = tok;
         else a.tokens_out[(size_t)b * a.k + j] = tok;
+        trace_mark(a.tr, TR_END);
     }
 }
 
@@ -212,12 +219,15 @@ struct VerifyArgs {
     const uint32_t* seq_ids;
     uint32_t* out;          // [B x (k+1)]
     int32_t* counts;        // [B]
+    Trace tr;
 };
 
 __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
     __shared__ ChainSmem cs;
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_START);
     const int b = blockIdx.x;
     const int k = a.k;
     const int64_t V = a.V;
@@ -274,6 +284,7 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
         o[rej] = tok;
         a.counts[b] = rej + 1;
     }
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_END);
 }
 
 }  // namespace yk
@@ -389,6 +400,7 @@ extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, 
     a.seq_ids = L.seq;
     a.probs = s->probs;
     a.tokens_out = L.out;
+    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
     YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B, SMP_THREADS, 0, a));
     e->launches++;
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, (size_t)B * 4, cudaMemcpyDeviceToHost, e->stream));
@@ -411,7 +423,7 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
     const int k = s->k;
     if (from_logits) {
         YK_CHECK_CUDA(launch_pdl(e, row_stats_kernel, B * (k + 1), SMP_THREADS, 0, qsrc, (int64_t)s->vocab,
-                                 T > 0.f ? T : 1.0f, s->stats));
+                                 T > 0.f ? T : 1.0f, s->stats, trace_next(e, TK_ROW_STATS)));
         e->launches++;
     }
     VerifyArgs a;
@@ -428,6 +440,7 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
     a.seq_ids = L.seq;
     a.out = L.out;
     a.counts = L.counts;
+    a.tr = trace_next(e, TK_VERIFY);
     YK_CHECK_CUDA(launch_pdl(e, verify_kernel, B, SMP_THREADS, 0, a));
     e->launches++;
     return YK_OK;
@@ -495,6 +508,7 @@ extern "C" yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float
     a.seq_ids = L.seq;
     a.probs = s->probs;
     a.tokens_out = L.drafts;
+    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
     YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B * k, SMP_THREADS, 0, a));
     e->launches++;
     YK_TRY(run_verify(s, B, s->q, 1, temperature, seed, step, L));
@@ -575,7 +589,7 @@ extern "C" yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream,
     if (s == YK_OK) {
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         row_stats_kernel<<<B * (k + 1), SMP_THREADS, 0, st>>>(target_logits, V, temperature > 0.f ? temperature : 1.0f,
-                                                              stats);
+                                                              stats, Trace{});
         VerifyArgs a;
         a.q = target_logits;
         a.stats = stats;
