@@ -107,6 +107,8 @@ _PROTOS = {
                                             C.POINTER(C.c_uint64), _I32P]),
     "ykt_attention_stamps_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_trace_enable": (C.c_int32, [_P, C.c_int32]),
+    "ykt_sampler_stamps_enable": (C.c_int32, [_P, C.c_int32]),
+    "ykt_sampler_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32]),
     "ykt_trace_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, C.POINTER(C.c_uint64)]),
     "ykt_attention_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, _I32P]),
 }
@@ -409,6 +411,16 @@ class Sampler:
         out = np.empty(self.vocab, dtype=np.float32)
         check(lib().yk_sampler_read_probs(self.h, b, j, ptr(out, C.c_float)))
         return out
+
+    def stamps(self, cap: int = 0):
+        """Test hook: cap > 0 enables phase stamps; cap == 0 returns ([cap x 8] draft, [cap x 8] verify)."""
+        if cap > 0:
+            check(lib().ykt_sampler_stamps_enable(self.h, cap))
+            self._stamps_cap = cap
+            return None
+        out = np.zeros((2 * self._stamps_cap, 8), np.uint64)
+        check(lib().ykt_sampler_stamps_read(self.h, ptr(out, C.c_uint64), self._stamps_cap))
+        return out[: self._stamps_cap], out[self._stamps_cap:]
 
     def close(self):
         if self.h:

@@ -17,7 +17,7 @@
 //   * binade crossings (m + k would reach 2^24 - 1),
 //   * exact ties (x/u = j + 1/2: the result depends on the parity of m + j),
 //   * negative, NaN or huge x, and states where c is 0, tiny or not finite.
-// A round covers 4096 elements (512 threads x 8); a special step ends the round
+// A round covers 8192 elements (512 threads x 16); a special step ends the round
 // and the next round restarts right after it.  Every result is the one the
 // sequential loop produces.
 #pragma once
@@ -28,7 +28,7 @@
 namespace yk {
 
 constexpr int CHAIN_THREADS = 512;  // block size of every kernel that calls block_chain
-constexpr int CHAIN_EPT = 8;        // elements per thread per round
+constexpr int CHAIN_EPT = 16;       // elements per thread per round
 constexpr int CHAIN_ROUND = CHAIN_THREADS * CHAIN_EPT;
 constexpr uint32_t CHAIN_SAT = 1u << 30;    // saturation of the integer prefix sums
 constexpr uint32_t CHAIN_TOP = (1u << 24) - 1;  // m + k at or above this: treat as a crossing
@@ -46,6 +46,8 @@ struct ChainSmem {
     float c_seq;
     long long pos_seq;
     long long found_seq;
+    float seg[CHAIN_ROUND];  // terms of a sequential segment, staged by the whole block
+    int n_rounds, n_special, n_seq;  // work counters (read by the sampler's stamp test hook)
 };
 
 __device__ __forceinline__ uint32_t chain_sat(uint32_t a, uint32_t b) {
@@ -124,20 +126,26 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         m = (uint32_t)__fmul_rn(cn, scale);  // exact integer in [2^23, 2^24)
     };
 
-    // One thread sums up to `limit` elements in order (head of the chain, and
-    // the rare zero / tiny / non-finite states).  NaN is absorbing.
+    // One thread sums up to `limit` (<= CHAIN_ROUND) elements in order (head of
+    // the chain, and the rare zero / tiny / non-finite states).  The block first
+    // evaluates the terms into shared memory, so the ordered loop never waits on
+    // global memory.  NaN is absorbing.
     auto sequential = [&](long long limit) {
+        if (threadIdx.x == 0) ++cs.n_seq;
+        const int cnt = (int)min(n - pos, limit);
+        for (int t = threadIdx.x; t < cnt; t += CHAIN_THREADS) cs.seg[t] = f(pos + t);
+        __syncthreads();
         if (threadIdx.x == 0) {
             float cc = c;
-            long long i = pos, fnd = -1;
-            const long long end = min(n, pos + limit);
-            for (; i < end; ++i) {
-                cc = __fadd_rn(cc, f(i));
-                if (search && r <= cc) { fnd = i; ++i; break; }
-                if (isnan(cc)) { i = n; break; }
+            long long fnd = -1;
+            int t = 0;
+            for (; t < cnt; ++t) {
+                cc = __fadd_rn(cc, cs.seg[t]);
+                if (search && r <= cc) { fnd = pos + t; ++t; break; }
+                if (isnan(cc)) { t = (int)(n - pos); break; }
             }
             cs.c_seq = cc;
-            cs.pos_seq = i;
+            cs.pos_seq = pos + t;
             cs.found_seq = fnd;
         }
         __syncthreads();
@@ -157,6 +165,7 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         }
         const long long base = pos;
         const long long i0 = base + (long long)threadIdx.x * CHAIN_EPT;
+        if (threadIdx.x == 0) ++cs.n_rounds;
         if (mode == ZERO) {
             // c stays +0 until the first non-zero element (x = -0 adds nothing).
             if (search && r <= 0.0f) {  // the next step decides; let the exact path take it
@@ -256,6 +265,7 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         const int pure_hit = cs.pure_hit;
         __syncthreads();
         if (pure_hit) { found = js; done = true; break; }
+        if (threadIdx.x == 0) ++cs.n_special;
         const float cprev = __fmul_rn((float)(m + pex), u);
         const float cn = __fadd_rn(cprev, xs);
         pos = js + 1;

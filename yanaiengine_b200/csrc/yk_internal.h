@@ -167,6 +167,8 @@ struct yk_sampler {
     float* dlogits = nullptr;   // [max_seqs x k x V] draft logits (yk_spec_sample_logits)
     float* stats = nullptr;     // [max_seqs x (2k+1) x 4] (max, sum, argmax, -)
     uint32_t* io = nullptr;     // small device io area
+    unsigned long long* stamps = nullptr;  // test hook: per-CTA phase stamps of draft sampling / verify
+    int stamps_cap = 0;
 };
 
 // ---- internal launchers ----------------------------------------------------

@@ -42,8 +42,9 @@ struct RowStats {
 };
 
 // Block-wide (max, sum-exp, first argmax) of x_i = l_i / T over one row.
-// Each thread visits its indices in increasing order (first maximum wins);
-// float4 loads, two in flight per iteration, when the row is 16-byte aligned.
+// Each accumulator visits its indices in increasing order and merges keep the
+// smallest index among equal maxima (first maximum wins); float4 loads when the
+// row is 16-byte aligned.
 __device__ __forceinline__ void stats_update(float raw, int idx, float T, float& m, float& s, float& best, int& arg) {
     const float x = scale_t(raw, T);
     if (raw > best) { best = raw; arg = idx; }
@@ -59,25 +60,41 @@ __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, fl
     float m = -INFINITY, s = 0.f, best = -INFINITY;
     int arg = 0x7fffffff;
     if ((V & 3) == 0 && ((uintptr_t)row & 15) == 0) {
+        // eight float4 loads per thread in flight before any use; the four lanes
+        // of a float4 feed four independent (max, sum, argmax) accumulators, so the
+        // exp/rescale chains run side by side, merged at the end
         const float4* r4 = reinterpret_cast<const float4*>(row);
         const int64_t n4 = V >> 2;
-        const int64_t step = 2 * (int64_t)blockDim.x;
-        for (int64_t i = threadIdx.x; i < n4; i += step) {
-            const float4 a = __ldg(r4 + i);
-            const bool has_b = i + blockDim.x < n4;
-            const float4 b = has_b ? __ldg(r4 + i + blockDim.x) : make_float4(0.f, 0.f, 0.f, 0.f);
-            const int ia = (int)(i * 4);
-            stats_update(a.x, ia, T, m, s, best, arg);
-            stats_update(a.y, ia + 1, T, m, s, best, arg);
-            stats_update(a.z, ia + 2, T, m, s, best, arg);
-            stats_update(a.w, ia + 3, T, m, s, best, arg);
-            if (has_b) {
-                const int ib = (int)((i + blockDim.x) * 4);
-                stats_update(b.x, ib, T, m, s, best, arg);
-                stats_update(b.y, ib + 1, T, m, s, best, arg);
-                stats_update(b.z, ib + 2, T, m, s, best, arg);
-                stats_update(b.w, ib + 3, T, m, s, best, arg);
+        constexpr int U = 8;
+        float am[4], as[4], ab[4];
+        int aa[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) { am[q] = -INFINITY; as[q] = 0.f; ab[q] = -INFINITY; aa[q] = 0x7fffffff; }
+        for (int64_t i0 = threadIdx.x; i0 < n4; i0 += (int64_t)U * blockDim.x) {
+            float4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t i = i0 + (int64_t)u * blockDim.x;
+                if (i < n4) v[u] = __ldg(r4 + i);
             }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t i = i0 + (int64_t)u * blockDim.x;
+                if (i < n4) {
+                    const int ia = (int)(i * 4);
+                    stats_update(v[u].x, ia, T, am[0], as[0], ab[0], aa[0]);
+                    stats_update(v[u].y, ia + 1, T, am[1], as[1], ab[1], aa[1]);
+                    stats_update(v[u].z, ia + 2, T, am[2], as[2], ab[2], aa[2]);
+                    stats_update(v[u].w, ia + 3, T, am[3], as[3], ab[3], aa[3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float M = fmaxf(m, am[q]);
+            if (M != -INFINITY) s = s * expf(m - M) + as[q] * expf(am[q] - M);
+            m = M;
+            if (ab[q] > best || (ab[q] == best && aa[q] < arg)) { best = ab[q]; arg = aa[q]; }
         }
     } else {
         for (int64_t i = threadIdx.x; i < V; i += blockDim.x) stats_update(row[i], (int)i, T, m, s, best, arg);
@@ -159,6 +176,7 @@ struct DraftArgs {
     const uint32_t* seq_ids;
     float* probs;
     uint32_t* tokens_out;
+    unsigned long long* stamps = nullptr;  // test hook: 8 words per CTA
     Trace tr;
 };
 
@@ -167,13 +185,19 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
     if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
-    if (threadIdx.x == 0) trace_mark(a.tr, TR_START);
+    unsigned long long* stp = a.stamps ? a.stamps + (size_t)blockIdx.x * 8 : nullptr;
+    if (threadIdx.x == 0) {
+        trace_mark(a.tr, TR_START);
+        cs.n_rounds = cs.n_special = cs.n_seq = 0;
+        if (stp) stp[0] = globaltimer_ns();
+    }
     const int b = a.j_fixed >= 0 ? blockIdx.x : blockIdx.x / a.k;
     const int j = a.j_fixed >= 0 ? a.j_fixed : blockIdx.x % a.k;
     const float* row = a.logits + ((size_t)b * a.logit_row_stride + (size_t)j * a.logit_row_j_mul) * a.V;
     float* p = a.probs + ((size_t)b * a.k + j) * a.V;
     const int64_t V = a.V;
     const RowStats st = block_row_stats(row, V, a.T > 0.f ? a.T : 1.0f);
+    if (stp && threadIdx.x == 0) stp[1] = globaltimer_ns();
     uint32_t tok;
     if (a.T <= 0.f) {  // greedy: one-hot p
         for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = (i == st.arg) ? 1.0f : 0.0f;
@@ -183,15 +207,28 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
         if ((V & 3) == 0 && ((uintptr_t)row & 15) == 0 && ((uintptr_t)p & 15) == 0) {
             const float4* r4 = reinterpret_cast<const float4*>(row);
             float4* p4 = reinterpret_cast<float4*>(p);
-            for (int64_t i = threadIdx.x; i < (V >> 2); i += blockDim.x) {
-                const float4 l = __ldg(r4 + i);
-                p4[i] = make_float4(q_from_logit(l.x, T, m, s), q_from_logit(l.y, T, m, s), q_from_logit(l.z, T, m, s),
-                                    q_from_logit(l.w, T, m, s));
+            const int64_t n4 = V >> 2;
+            constexpr int U = 8;  // eight float4 loads per thread in flight
+            for (int64_t i0 = threadIdx.x; i0 < n4; i0 += (int64_t)U * blockDim.x) {
+                float4 l[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t i = i0 + (int64_t)u * blockDim.x;
+                    if (i < n4) l[u] = __ldg(r4 + i);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t i = i0 + (int64_t)u * blockDim.x;
+                    if (i < n4)
+                        p4[i] = make_float4(q_from_logit(l[u].x, T, m, s), q_from_logit(l[u].y, T, m, s),
+                                            q_from_logit(l[u].z, T, m, s), q_from_logit(l[u].w, T, m, s));
+                }
             }
         } else {
             for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = q_from_logit(row[i], T, m, s);
         }
         __syncthreads();  // p is complete and visible to the whole block
+        if (stp && threadIdx.x == 0) stp[2] = globaltimer_ns();
         const float r = uniform_at(a.seed, a.step, a.seq_ids[b], (uint32_t)j, SLOT_DRAFT);
         tok = (uint32_t)block_chain(cs, [&](int64_t i) { return p[i]; }, V, true, r, nullptr);
     }
@@ -199,6 +236,13 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
         if (a.j_fixed >= 0) a.tokens_out[b] = tok;
         else a.tokens_out[(size_t)b * a.k + j] = tok;
         trace_mark(a.tr, TR_END);
+        if (stp) {
+            stp[3] = globaltimer_ns();
+            stp[4] = (unsigned long long)cs.n_rounds;
+            stp[5] = (unsigned long long)cs.n_special;
+            stp[6] = (unsigned long long)cs.n_seq;
+            stp[7] = tok;
+        }
     }
 }
 
@@ -219,6 +263,7 @@ struct VerifyArgs {
     const uint32_t* seq_ids;
     uint32_t* out;          // [B x (k+1)]
     int32_t* counts;        // [B]
+    unsigned long long* stamps = nullptr;  // test hook: 8 words per CTA
     Trace tr;
 };
 
@@ -227,7 +272,12 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
     if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
-    if (threadIdx.x == 0) trace_mark(a.tr, TR_START);
+    unsigned long long* stp = a.stamps ? a.stamps + (size_t)blockIdx.x * 8 : nullptr;
+    if (threadIdx.x == 0) {
+        trace_mark(a.tr, TR_START);
+        cs.n_rounds = cs.n_special = cs.n_seq = 0;
+        if (stp) stp[0] = globaltimer_ns();
+    }
     const int b = blockIdx.x;
     const int k = a.k;
     const int64_t V = a.V;
@@ -284,6 +334,12 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
         o[rej] = tok;
         a.counts[b] = rej + 1;
     }
+    if (stp && threadIdx.x == 0) {
+        stp[3] = globaltimer_ns();
+        stp[4] = (unsigned long long)cs.n_rounds;
+        stp[5] = (unsigned long long)cs.n_special;
+        stp[6] = (unsigned long long)cs.n_seq;
+    }
     if (threadIdx.x == 0) trace_mark(a.tr, TR_END);
 }
 
@@ -327,6 +383,7 @@ extern "C" void yk_sampler_destroy(yk_sampler* s) {
     if (s->dlogits) cudaFree(s->dlogits);
     if (s->stats) cudaFree(s->stats);
     if (s->io) cudaFree(s->io);
+    if (s->stamps) cudaFree(s->stamps);
     delete s;
 }
 
@@ -401,6 +458,7 @@ extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, 
     a.probs = s->probs;
     a.tokens_out = L.out;
     a.tr = trace_next(e, TK_DRAFT_SAMPLE);
+    a.stamps = (s->stamps && B <= s->stamps_cap) ? s->stamps : nullptr;
     YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B, SMP_THREADS, 0, a));
     e->launches++;
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, (size_t)B * 4, cudaMemcpyDeviceToHost, e->stream));
@@ -441,6 +499,7 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
     a.out = L.out;
     a.counts = L.counts;
     a.tr = trace_next(e, TK_VERIFY);
+    a.stamps = (s->stamps && B <= s->stamps_cap) ? s->stamps + (size_t)s->stamps_cap * 8 : nullptr;
     YK_CHECK_CUDA(launch_pdl(e, verify_kernel, B, SMP_THREADS, 0, a));
     e->launches++;
     return YK_OK;
@@ -509,6 +568,7 @@ extern "C" yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float
     a.probs = s->probs;
     a.tokens_out = L.drafts;
     a.tr = trace_next(e, TK_DRAFT_SAMPLE);
+    a.stamps = (s->stamps && B * k <= s->stamps_cap) ? s->stamps : nullptr;
     YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B * k, SMP_THREADS, 0, a));
     e->launches++;
     YK_TRY(run_verify(s, B, s->q, 1, temperature, seed, step, L));
@@ -613,4 +673,32 @@ extern "C" yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream,
     }
     cudaSetDevice(prev);
     return s;
+}
+
+// ---------------------------------------------------------------------------
+// Test hooks (include/yk_testing.h).
+// ---------------------------------------------------------------------------
+#include "../../include/yk_testing.h"
+
+extern "C" yk_status ykt_sampler_stamps_enable(yk_sampler* s, int32_t cap) {
+    YK_ARG(s && cap >= 0, "arguments");
+    YK_CHECK_CUDA(cudaSetDevice(s->e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(s->e->stream));
+    if (s->stamps) cudaFree(s->stamps);
+    s->stamps = nullptr;
+    s->stamps_cap = 0;
+    if (cap > 0) {
+        YK_CHECK_CUDA(cudaMalloc(&s->stamps, (size_t)cap * 2 * 8 * 8));
+        YK_CHECK_CUDA(cudaMemset(s->stamps, 0, (size_t)cap * 2 * 8 * 8));
+        s->stamps_cap = cap;
+    }
+    return YK_OK;
+}
+
+extern "C" yk_status ykt_sampler_stamps_read(yk_sampler* s, uint64_t* host, int32_t cap) {
+    YK_ARG(s && host && cap == s->stamps_cap && s->stamps, "stamps not enabled with this capacity");
+    YK_CHECK_CUDA(cudaSetDevice(s->e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(s->e->stream));
+    YK_CHECK_CUDA(cudaMemcpy(host, s->stamps, (size_t)cap * 2 * 8 * 8, cudaMemcpyDeviceToHost));
+    return YK_OK;
 }

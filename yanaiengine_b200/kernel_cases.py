@@ -2,6 +2,7 @@
 
     python -m yanaiengine_b200.kernel_cases attention [--dh 128 --group 4 --kv-heads 8 --seqs 32 --new 6]
     python -m yanaiengine_b200.kernel_cases gemm [--n 28672 --k 4096 --m 192]
+    python -m yanaiengine_b200.kernel_cases sampler [--seqs 32 --k 5 --vocab 128256]
 
 `attention` builds a 2-layer bf16 model whose attention has the verify shape of
 the 8B-class target (or the 1B-class draft with --dh 64 --new 1), fills a KV
@@ -73,6 +74,35 @@ def attention(args) -> None:
     e.close()
 
 
+def sampler(args) -> None:
+    """Draft sampling of B x k rows and verification of B sequences from synthetic
+    N(0, 2^2) logits (yk_spec_sample_logits), with per-CTA phase stamps."""
+    e = abi.Engine(0)
+    B, k, V = args.seqs, args.k, args.vocab
+    rng = np.random.default_rng(0)
+    dl = rng.normal(0, 2.0, (B, k, V)).astype(np.float32)
+    tl = rng.normal(0, 2.0, (B, k + 1, V)).astype(np.float32)
+    s = abi.Sampler(e, B, k, V)
+    s.stamps(B * k)
+    seq = np.arange(B, dtype=np.uint32)
+    times = []
+    for step in range(args.steps):
+        t0 = time.perf_counter()
+        s.sample_logits(dl, tl, args.temperature, 7, step, seq)
+        times.append(time.perf_counter() - t0)
+    d, v = s.stamps()
+    d, v = d.astype(np.int64), v[:B].astype(np.int64)
+    ph = lambda a, i, j: np.median((a[:, j] - a[:, i]) / 1e3)
+    print(f"sampler B={B} k={k} V={V} T={args.temperature}: call {1e3 * min(times):.2f} ms (with host copies)")
+    print(f"  draft CTAs {len(d)}: stats {ph(d, 0, 1):.1f} us, p write {ph(d, 1, 2):.1f} us, chain {ph(d, 2, 3):.1f} us "
+          f"(max {np.max((d[:, 3] - d[:, 2]) / 1e3):.1f}); rounds median {np.median(d[:, 4]):.0f} max {d[:, 4].max()}, "
+          f"special {np.median(d[:, 5]):.0f}, sequential {np.median(d[:, 6]):.0f}; span {(d[:, 3].max() - d[:, 0].min()) / 1e3:.1f} us")
+    print(f"  verify CTAs {len(v)}: total {ph(v, 0, 3):.1f} us (max {np.max((v[:, 3] - v[:, 0]) / 1e3):.1f}); "
+          f"rounds median {np.median(v[:, 4]):.0f} max {v[:, 4].max()}, special {np.median(v[:, 5]):.0f}")
+    s.close()
+    e.close()
+
+
 def gemm(args) -> None:
     e = abi.Engine(0)
     rng = np.random.default_rng(0)
@@ -95,13 +125,19 @@ def main() -> None:
     a.add_argument("--new", type=int, default=6)
     a.add_argument("--steps", type=int, default=3)
     a.add_argument("--stamps", action="store_true", help="per-CTA phase stamps of the last attention launch")
+    sp = sub.add_parser("sampler")
+    sp.add_argument("--seqs", type=int, default=32)
+    sp.add_argument("--k", type=int, default=5)
+    sp.add_argument("--vocab", type=int, default=128256)
+    sp.add_argument("--temperature", type=float, default=0.8)
+    sp.add_argument("--steps", type=int, default=3)
     g = sub.add_parser("gemm")
     g.add_argument("--n", type=int, default=28672)
     g.add_argument("--k", type=int, default=4096)
     g.add_argument("--m", type=int, default=192)
     g.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
-    attention(args) if args.case == "attention" else gemm(args)
+    {"attention": attention, "sampler": sampler, "gemm": gemm}[args.case](args)
 
 
 if __name__ == "__main__":
