@@ -70,6 +70,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     if (const char* v = std::getenv("YK_PDL")) e->pdl = std::strcmp(v, "0") != 0;
     if (const char* v = std::getenv("YK_GEMM_VARIANT")) e->gemm_variant = std::atoi(v);
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
+    if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
     yk_status s = e->ensure_pinned((size_t)4 << 20);
     if (s != YK_OK) { delete e; return s; }
     *out = e;
@@ -515,9 +516,11 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
     int slots_g = 0, slots_w = 0;
     it_g.clear(); cb_g.clear(); it_w.clear(); cb_w.clear();
     if (c.dtype == YK_DTYPE_BF16) {
-        yk::plan_attention(c, e->num_sms, e->attn_waves, q_starts, ctx, B, false, it_g, cb_g, &slots_g);
+        yk::plan_attention(c, e->num_sms, e->attn_waves, e->attn_balanced, q_starts, ctx, B, false, it_g, cb_g,
+                           &slots_g);
         if (c.window > 0)
-            yk::plan_attention(c, e->num_sms, e->attn_waves, q_starts, ctx, B, true, it_w, cb_w, &slots_w);
+            yk::plan_attention(c, e->num_sms, e->attn_waves, e->attn_balanced, q_starts, ctx, B, true, it_w, cb_w,
+                               &slots_w);
         const size_t need = (size_t)std::max(slots_g, slots_w) * yk::attention_ws_floats_per_slot(c.head_dim);
         if (need > m->attn_ws_floats) {
             YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));

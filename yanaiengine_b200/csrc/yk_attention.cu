@@ -664,10 +664,12 @@ int attention_ctas_per_sm(int head_dim) {
 
 // Work list for one forward step and one window setting (see yk_forward_step):
 // spans (sequence, query tile) x KV heads, each cut into equal page-aligned
-// key ranges so the item count fills about `waves` waves of resident CTAs; items
-// sorted longest first so the block scheduler balances the tail.
-void plan_attention(const yk_model_config& c, int num_sms, int waves, const uint32_t* q_starts, const uint32_t* ctx,
-                    int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots) {
+// key ranges so the item count fills about `waves` waves of resident CTAs (or,
+// balanced, no piece is longer than the average load of a resident slot);
+// items sorted longest first so the block scheduler balances the tail.
+void plan_attention(const yk_model_config& c, int num_sms, int waves, bool balanced, const uint32_t* q_starts,
+                    const uint32_t* ctx, int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb,
+                    int* n_slots) {
     const int G = c.n_heads / c.n_kv_heads;
     struct Span { int b, qt, kb, ke; };
     std::vector<Span> spans;
@@ -696,12 +698,21 @@ void plan_attention(const yk_model_config& c, int num_sms, int waves, const uint
         for (const auto& s : spans) nitems += (long long)splits(s, kp) * c.n_kv_heads;
         return nitems;
     };
-    int lo = 1, hi = max_pages;  // smallest pages-per-piece whose item count fits the target
-    while (lo < hi) {
-        const int mid = (lo + hi) / 2;
-        if (count(mid) <= target) hi = mid; else lo = mid + 1;
+    int kp;
+    if (balanced) {
+        // pieces of at most the average load of a resident slot: the longest item
+        // is no longer than that average, the scheduler fills slots longest first
+        long long pages = 0;
+        for (const auto& s : spans) pages += (long long)((s.ke - s.kb + 15) / 16) * c.n_kv_heads;
+        kp = (int)std::max<long long>(1, (pages + target - 1) / target);
+    } else {
+        int lo = 1, hi = max_pages;  // smallest pages-per-piece whose item count fits the target
+        while (lo < hi) {
+            const int mid = (lo + hi) / 2;
+            if (count(mid) <= target) hi = mid; else lo = mid + 1;
+        }
+        kp = lo;
     }
-    const int kp = lo;
     struct Item { int b, g, qt, kb, ke, slot, cg; };
     std::vector<Item> list;
     comb.clear();

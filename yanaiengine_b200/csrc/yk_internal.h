@@ -64,6 +64,7 @@ struct yk_engine {
     int gemm_variant = 0;                // GEMM schedule tuning knob (env YK_GEMM_VARIANT): bit 0 = pure
                                          // stream-K instead of whole tiles + stream-K remainder
     int attn_waves = 1;                  // attention items per resident CTA slot (env YK_ATTN_WAVES)
+    bool attn_balanced = false;          // attention pieces <= average slot load (env YK_ATTN_PLAN=1)
     bool profiling = false;
     void* trace_rec = nullptr;           // launch trace records (test hook), else null
     uint32_t trace_cap = 0;
@@ -166,6 +167,7 @@ struct yk_sampler {
     float* q = nullptr;         // [max_seqs x (k+1) x V] target probs (probs entry) or logits
     float* dlogits = nullptr;   // [max_seqs x k x V] draft logits (yk_spec_sample_logits)
     float* stats = nullptr;     // [max_seqs x (2k+1) x 4] (max, sum, argmax, -)
+    float4* part = nullptr;     // [max_seqs x (k+1) x chunks] per-chunk row statistics (draft, then target)
     uint32_t* io = nullptr;     // small device io area
     unsigned long long* stamps = nullptr;  // test hook: per-CTA phase stamps of draft sampling / verify
     int stamps_cap = 0;
@@ -239,8 +241,9 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
 yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
 yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks,
                         double kv_bytes);
-void plan_attention(const yk_model_config& c, int num_sms, int waves, const uint32_t* q_starts, const uint32_t* ctx,
-                    int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb, int* n_slots);
+void plan_attention(const yk_model_config& c, int num_sms, int waves, bool balanced, const uint32_t* q_starts,
+                    const uint32_t* ctx, int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb,
+                    int* n_slots);
 size_t attention_ws_floats_per_slot(int head_dim);
 yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool);
 yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T);

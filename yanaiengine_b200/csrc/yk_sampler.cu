@@ -56,7 +56,18 @@ __device__ __forceinline__ void stats_update(float raw, int idx, float T, float&
     }
 }
 
+struct RowStats4 {
+    float m, s, best;
+    int arg;
+};
+__device__ RowStats4 block_stats4(const float* __restrict__ row, int64_t V, int idx0, float T);
 __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, float T) {
+    const RowStats4 r = block_stats4(row, V, 0, T);
+    return RowStats{r.m, r.s, r.arg == 0x7fffffff ? 0 : r.arg};
+}
+// (max, sum-exp, best raw value, first argmax) over row[0, V) whose first element
+// has index idx0 in its full row.
+__device__ RowStats4 block_stats4(const float* __restrict__ row, int64_t V, int idx0, float T) {
     float m = -INFINITY, s = 0.f, best = -INFINITY;
     int arg = 0x7fffffff;
     if ((V & 3) == 0 && ((uintptr_t)row & 15) == 0) {
@@ -81,7 +92,7 @@ __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, fl
             for (int u = 0; u < U; ++u) {
                 const int64_t i = i0 + (int64_t)u * blockDim.x;
                 if (i < n4) {
-                    const int ia = (int)(i * 4);
+                    const int ia = idx0 + (int)(i * 4);
                     stats_update(v[u].x, ia, T, am[0], as[0], ab[0], aa[0]);
                     stats_update(v[u].y, ia + 1, T, am[1], as[1], ab[1], aa[1]);
                     stats_update(v[u].z, ia + 2, T, am[2], as[2], ab[2], aa[2]);
@@ -97,7 +108,7 @@ __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, fl
             if (ab[q] > best || (ab[q] == best && aa[q] < arg)) { best = ab[q]; arg = aa[q]; }
         }
     } else {
-        for (int64_t i = threadIdx.x; i < V; i += blockDim.x) stats_update(row[i], (int)i, T, m, s, best, arg);
+        for (int64_t i = threadIdx.x; i < V; i += blockDim.x) stats_update(row[i], idx0 + (int)i, T, m, s, best, arg);
     }
     __shared__ float sm_m[32], sm_s[32], sm_b[32];
     __shared__ int sm_a[32];
@@ -133,11 +144,28 @@ __device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, fl
             m = M;
             if (b2 > best || (b2 == best && a2 < arg)) { best = b2; arg = a2; }
         }
-        if (ln == 0) { sm_m[0] = m; sm_s[0] = s; sm_a[0] = (arg == 0x7fffffff) ? 0 : arg; }
+        if (ln == 0) { sm_m[0] = m; sm_s[0] = s; sm_b[0] = best; sm_a[0] = arg; }
     }
     __syncthreads();
-    RowStats r{sm_m[0], sm_s[0], sm_a[0]};
+    RowStats4 r{sm_m[0], sm_s[0], sm_b[0], sm_a[0]};
     __syncthreads();
+    return r;
+}
+
+// Merge of per-chunk statistics in chunk order (deterministic); first maximum wins.
+constexpr int SMP_CHUNKS = 8;  // CTAs per row for the draft statistics and probability passes
+__device__ __forceinline__ RowStats4 merge_chunks(const float4* __restrict__ part) {
+    RowStats4 r{-INFINITY, 0.f, -INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int c = 0; c < SMP_CHUNKS; ++c) {
+        const float4 q = part[c];
+        const float M = fmaxf(r.m, q.x);
+        if (M != -INFINITY) r.s = r.s * expf(r.m - M) + q.y * expf(q.x - M);
+        r.m = M;
+        const int qa = __float_as_int(q.w);
+        if (q.z > r.best || (q.z == r.best && qa < r.arg)) { r.best = q.z; r.arg = qa; }
+    }
+    if (r.arg == 0x7fffffff) r.arg = 0;
     return r;
 }
 
@@ -176,39 +204,55 @@ struct DraftArgs {
     const uint32_t* seq_ids;
     float* probs;
     uint32_t* tokens_out;
+    float4* part = nullptr;  // [rows x SMP_CHUNKS] per-chunk (max, sum, best, argmax bits)
     unsigned long long* stamps = nullptr;  // test hook: 8 words per CTA
     Trace tr;
 };
 
-__global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) {
-    __shared__ ChainSmem cs;
+__device__ __forceinline__ void draft_row(const DraftArgs& a, int x, int& b, int& j) {
+    b = a.j_fixed >= 0 ? x : x / a.k;
+    j = a.j_fixed >= 0 ? a.j_fixed : x % a.k;
+}
+__device__ __forceinline__ int64_t draft_chunk(int64_t V) { return ((V + SMP_CHUNKS - 1) / SMP_CHUNKS + 3) & ~int64_t(3); }
+
+// Draft rows, pass 1: statistics of chunk blockIdx.y of row blockIdx.x.
+__global__ void __launch_bounds__(SMP_THREADS) draft_partial_kernel(DraftArgs a) {
     if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
-    unsigned long long* stp = a.stamps ? a.stamps + (size_t)blockIdx.x * 8 : nullptr;
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_START);
+    int b, j;
+    draft_row(a, blockIdx.x, b, j);
+    const float* row = a.logits + ((size_t)b * a.logit_row_stride + (size_t)j * a.logit_row_j_mul) * a.V;
+    const int64_t ch = draft_chunk(a.V), c0 = (int64_t)blockIdx.y * ch, c1 = min(a.V, c0 + ch);
+    const RowStats4 st = block_stats4(row + c0, max((int64_t)0, c1 - c0), (int)c0, a.T > 0.f ? a.T : 1.0f);
     if (threadIdx.x == 0) {
-        trace_mark(a.tr, TR_START);
-        cs.n_rounds = cs.n_special = cs.n_seq = 0;
-        if (stp) stp[0] = globaltimer_ns();
+        a.part[(size_t)blockIdx.x * SMP_CHUNKS + blockIdx.y] = make_float4(st.m, st.s, st.best, __int_as_float(st.arg));
+        trace_mark(a.tr, TR_END);
     }
-    const int b = a.j_fixed >= 0 ? blockIdx.x : blockIdx.x / a.k;
-    const int j = a.j_fixed >= 0 ? a.j_fixed : blockIdx.x % a.k;
+}
+
+// Draft rows, pass 2: p = softmax(row / T) for chunk blockIdx.y (one-hot argmax when T <= 0).
+__global__ void __launch_bounds__(SMP_THREADS) draft_prob_kernel(DraftArgs a) {
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_START);
+    int b, j;
+    draft_row(a, blockIdx.x, b, j);
     const float* row = a.logits + ((size_t)b * a.logit_row_stride + (size_t)j * a.logit_row_j_mul) * a.V;
     float* p = a.probs + ((size_t)b * a.k + j) * a.V;
-    const int64_t V = a.V;
-    const RowStats st = block_row_stats(row, V, a.T > 0.f ? a.T : 1.0f);
-    if (stp && threadIdx.x == 0) stp[1] = globaltimer_ns();
-    uint32_t tok;
-    if (a.T <= 0.f) {  // greedy: one-hot p
-        for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = (i == st.arg) ? 1.0f : 0.0f;
-        tok = (uint32_t)st.arg;
+    const RowStats4 st = merge_chunks(a.part + (size_t)blockIdx.x * SMP_CHUNKS);
+    const int64_t ch = draft_chunk(a.V), c0 = (int64_t)blockIdx.y * ch, c1 = min(a.V, c0 + ch);
+    if (a.T <= 0.f) {
+        for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) p[i] = (i == st.arg) ? 1.0f : 0.0f;
     } else {
         const float T = a.T, m = st.m, s = st.s;
-        if ((V & 3) == 0 && ((uintptr_t)row & 15) == 0 && ((uintptr_t)p & 15) == 0) {
-            const float4* r4 = reinterpret_cast<const float4*>(row);
-            float4* p4 = reinterpret_cast<float4*>(p);
-            const int64_t n4 = V >> 2;
-            constexpr int U = 8;  // eight float4 loads per thread in flight
+        if (((uintptr_t)(row + c0) & 15) == 0 && ((uintptr_t)(p + c0) & 15) == 0 && ((c1 - c0) & 3) == 0) {
+            const float4* r4 = reinterpret_cast<const float4*>(row + c0);
+            float4* p4 = reinterpret_cast<float4*>(p + c0);
+            const int64_t n4 = (c1 - c0) >> 2;
+            constexpr int U = 4;
             for (int64_t i0 = threadIdx.x; i0 < n4; i0 += (int64_t)U * blockDim.x) {
                 float4 l[U];
 #pragma unroll
@@ -225,10 +269,33 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
                 }
             }
         } else {
-            for (int64_t i = threadIdx.x; i < V; i += blockDim.x) p[i] = q_from_logit(row[i], T, m, s);
+            for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) p[i] = q_from_logit(row[i], T, m, s);
         }
-        __syncthreads();  // p is complete and visible to the whole block
-        if (stp && threadIdx.x == 0) stp[2] = globaltimer_ns();
+    }
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_END);
+}
+
+// Draft rows, pass 3: the token, sampleFromProbs over p (first maximum when T <= 0).
+__global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) {
+    __shared__ ChainSmem cs;
+    if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
+    pdl_trigger();
+    pdl_wait();
+    unsigned long long* stp = a.stamps ? a.stamps + (size_t)blockIdx.x * 8 : nullptr;
+    if (threadIdx.x == 0) {
+        trace_mark(a.tr, TR_START);
+        cs.n_rounds = cs.n_special = cs.n_seq = 0;
+        if (stp) stp[0] = globaltimer_ns();
+    }
+    int b, j;
+    draft_row(a, blockIdx.x, b, j);
+    const float* p = a.probs + ((size_t)b * a.k + j) * a.V;
+    const int64_t V = a.V;
+    if (stp && threadIdx.x == 0) stp[1] = stp[2] = globaltimer_ns();
+    uint32_t tok;
+    if (a.T <= 0.f) {  // greedy: the merged first maximum
+        tok = (uint32_t)merge_chunks(a.part + (size_t)blockIdx.x * SMP_CHUNKS).arg;
+    } else {
         const float r = uniform_at(a.seed, a.step, a.seq_ids[b], (uint32_t)j, SLOT_DRAFT);
         tok = (uint32_t)block_chain(cs, [&](int64_t i) { return p[i]; }, V, true, r, nullptr);
     }
@@ -263,6 +330,7 @@ struct VerifyArgs {
     const uint32_t* seq_ids;
     uint32_t* out;          // [B x (k+1)]
     int32_t* counts;        // [B]
+    const float4* qpart = nullptr;  // logits mode: per-chunk target row statistics (else `stats`)
     unsigned long long* stamps = nullptr;  // test hook: 8 words per CTA
     Trace tr;
 };
@@ -285,7 +353,19 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
     const bool greedy = a.from_logits && a.T <= 0.f;
     const float T = a.T > 0.f ? a.T : 1.0f;
     auto qrow = [&](int i) { return a.q + ((size_t)b * (k + 1) + i) * V; };
-    auto st = [&](int i) { return a.stats + ((size_t)b * (k + 1) + i) * 4; };
+    __shared__ float s_stats[17 * 4];  // k + 1 <= 17 target rows: merged (max, sum, argmax bits, -)
+    if (a.qpart) {
+        if (threadIdx.x <= k) {
+            const RowStats4 r = merge_chunks(a.qpart + ((size_t)b * (k + 1) + threadIdx.x) * SMP_CHUNKS);
+            s_stats[threadIdx.x * 4 + 0] = r.m;
+            s_stats[threadIdx.x * 4 + 1] = r.s;
+            s_stats[threadIdx.x * 4 + 2] = __int_as_float(r.arg);
+        }
+        __syncthreads();
+    }
+    auto st = [&](int i) -> const float* {
+        return a.qpart ? s_stats + i * 4 : a.stats + ((size_t)b * (k + 1) + i) * 4;
+    };
     auto qval = [&](int i, int64_t x) -> float {
         if (!a.from_logits) return qrow(i)[x];
         return q_from_logit(qrow(i)[x], T, st(i)[0], st(i)[1]);
@@ -365,6 +445,7 @@ extern "C" yk_status yk_sampler_create(yk_engine* e, int32_t max_seqs, int32_t k
     if ((err = cudaMalloc(&s->probs, (size_t)max_seqs * k * V * 4)) != cudaSuccess ||
         (err = cudaMalloc(&s->q, (size_t)max_seqs * (k + 1) * V * 4)) != cudaSuccess ||
         (err = cudaMalloc(&s->stats, (size_t)max_seqs * (2 * k + 1) * 4 * 4)) != cudaSuccess ||
+        (err = cudaMalloc(&s->part, (size_t)max_seqs * (k + 1) * SMP_CHUNKS * sizeof(float4))) != cudaSuccess ||
         (err = cudaMalloc(&s->io, (size_t)max_seqs * (3 * k + 8) * 4 + 4096)) != cudaSuccess) {
         yk_sampler_destroy(s);
         yk_set_error(std::string("sampler cudaMalloc: ") + cudaGetErrorString(err));
@@ -382,6 +463,7 @@ extern "C" void yk_sampler_destroy(yk_sampler* s) {
     if (s->q) cudaFree(s->q);
     if (s->dlogits) cudaFree(s->dlogits);
     if (s->stats) cudaFree(s->stats);
+    if (s->part) cudaFree(s->part);
     if (s->io) cudaFree(s->io);
     if (s->stamps) cudaFree(s->stamps);
     delete s;
@@ -434,6 +516,22 @@ static yk_status upload_small(yk_sampler* s, int B, const uint32_t* seq_ids, con
     return YK_OK;
 }
 
+// Draft sampling of `rows` rows: chunked statistics, chunked probabilities, token.
+static yk_status launch_draft(yk_sampler* s, DraftArgs a, int rows) {
+    yk_engine* e = s->e;
+    a.tr = trace_next(e, TK_ROW_STATS);
+    YK_CHECK_CUDA(launch_pdl(e, draft_partial_kernel, dim3(rows, SMP_CHUNKS), SMP_THREADS, 0, a));
+    e->launches++;
+    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
+    YK_CHECK_CUDA(launch_pdl(e, draft_prob_kernel, dim3(rows, SMP_CHUNKS), SMP_THREADS, 0, a));
+    e->launches++;
+    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
+    a.stamps = (s->stamps && rows <= s->stamps_cap) ? s->stamps : nullptr;
+    YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, rows, SMP_THREADS, 0, a));
+    e->launches++;
+    return YK_OK;
+}
+
 extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, int32_t j, float temperature,
                                      uint64_t seed, uint32_t step, const uint32_t* seq_ids, uint32_t* out_tokens) {
     YK_ARG(s && draft && seq_ids && out_tokens, "null argument");
@@ -457,10 +555,8 @@ extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, 
     a.seq_ids = L.seq;
     a.probs = s->probs;
     a.tokens_out = L.out;
-    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
-    a.stamps = (s->stamps && B <= s->stamps_cap) ? s->stamps : nullptr;
-    YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B, SMP_THREADS, 0, a));
-    e->launches++;
+    a.part = s->part;
+    YK_TRY(launch_draft(s, a, B));
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, (size_t)B * 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + (size_t)B * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
@@ -479,14 +575,24 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
                             uint32_t step, const IoLayout& L) {
     yk_engine* e = s->e;
     const int k = s->k;
-    if (from_logits) {
-        YK_CHECK_CUDA(launch_pdl(e, row_stats_kernel, B * (k + 1), SMP_THREADS, 0, qsrc, (int64_t)s->vocab,
-                                 T > 0.f ? T : 1.0f, s->stats, trace_next(e, TK_ROW_STATS)));
+    if (from_logits) {  // chunked statistics of the k + 1 target rows of each sequence
+        DraftArgs d;
+        d.logits = qsrc;
+        d.logit_row_stride = k + 1;
+        d.logit_row_j_mul = 1;
+        d.V = s->vocab;
+        d.k = k + 1;
+        d.j_fixed = -1;
+        d.T = T;
+        d.part = s->part;
+        d.tr = trace_next(e, TK_ROW_STATS);
+        YK_CHECK_CUDA(launch_pdl(e, draft_partial_kernel, dim3(B * (k + 1), SMP_CHUNKS), SMP_THREADS, 0, d));
         e->launches++;
     }
     VerifyArgs a;
     a.q = qsrc;
     a.stats = s->stats;
+    a.qpart = from_logits ? s->part : nullptr;
     a.p = s->probs;
     a.drafts = L.drafts;
     a.V = s->vocab;
@@ -567,10 +673,8 @@ extern "C" yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float
     a.seq_ids = L.seq;
     a.probs = s->probs;
     a.tokens_out = L.drafts;
-    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
-    a.stamps = (s->stamps && B * k <= s->stamps_cap) ? s->stamps : nullptr;
-    YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, B * k, SMP_THREADS, 0, a));
-    e->launches++;
+    a.part = s->part;
+    YK_TRY(launch_draft(s, a, B * k));
     YK_TRY(run_verify(s, B, s->q, 1, temperature, seed, step, L));
     YK_CHECK_CUDA(cudaMemcpyAsync(draft_tokens_out, L.drafts, (size_t)B * k * 4, cudaMemcpyDeviceToHost, e->stream));
     return finish_verify(s, B, L, out_tokens, out_counts);

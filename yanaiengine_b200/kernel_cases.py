@@ -94,7 +94,7 @@ def sampler(args) -> None:
     d, v = d.astype(np.int64), v[:B].astype(np.int64)
     ph = lambda a, i, j: np.median((a[:, j] - a[:, i]) / 1e3)
     print(f"sampler B={B} k={k} V={V} T={args.temperature}: call {1e3 * min(times):.2f} ms (with host copies)")
-    print(f"  draft CTAs {len(d)}: stats {ph(d, 0, 1):.1f} us, p write {ph(d, 1, 2):.1f} us, chain {ph(d, 2, 3):.1f} us "
+    print(f"  draft token CTAs {len(d)}: chain {ph(d, 2, 3):.1f} us "
           f"(max {np.max((d[:, 3] - d[:, 2]) / 1e3):.1f}); rounds median {np.median(d[:, 4]):.0f} max {d[:, 4].max()}, "
           f"special {np.median(d[:, 5]):.0f}, sequential {np.median(d[:, 6]):.0f}; span {(d[:, 3].max() - d[:, 0].min()) / 1e3:.1f} us")
     print(f"  verify CTAs {len(v)}: total {ph(v, 0, 3):.1f} us (max {np.max((v[:, 3] - v[:, 0]) / 1e3):.1f}); "
