@@ -209,25 +209,15 @@ def barrier(world):
 
 
 def allreduce_max(world, x: float) -> float:
-    if world <= 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from yanaiengine_b200 import dp
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return dp.all_max(world, x)
 
 
 def allreduce_sum(world, x: float) -> float:
-    if world <= 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from yanaiengine_b200 import dp
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return dp.all_sum(world, x)
 
 
 def measured_peaks() -> dict:
@@ -245,8 +235,13 @@ def run_yk(args, world, rank, local):
     eng = abi.Engine(local)
     tcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
     dcfg = abi.make_config(**DRAFT, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
+    from yanaiengine_b200 import dp
+
+    # the job's B x world sequences, split across ranks longest-first (B per rank)
+    glens = dp.global_lengths(B, world, seed=7)
+    mine = dp.partition(glens, world)[rank]
+    lens = glens[mine]
     rng = np.random.default_rng(7 + 1000 * rank)
-    lens = rng.integers(512, 2049, B)
     grow = (args.warmup + 2 * args.steps + 4) * (k + 1) + 32
     blocks = int(sum(np.ceil((lens + grow) / 16))) + 64
     target = abi.Model(eng, tcfg, seed=1, init_std=0.02)
