@@ -254,7 +254,7 @@ def run_yk(args, world, rank, local):
     sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + rank)
     for i, L in enumerate(lens):
         sch.submit(rng.integers(0, TARGET["vocab_size"], int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
-                   seq_id=rank * B + i, cached=True)
+                   seq_id=int(mine[i]), cached=True)
     for _ in range(args.warmup):
         sch.step()
     eng.sync()

@@ -228,6 +228,25 @@ yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream, const floa
                                         float temperature, uint64_t seed, uint32_t step, uint32_t* out_tokens,
                                         int32_t* out_counts);
 
+/* ---- tensor parallelism: the 70B-shape target (Llama-3-70B, TP over the 8
+ * GPUs of a box).  Replaces nothing in the reference (its models run on one
+ * Metal device); the layer math is LlamaBlock.forwardBatched with o_proj and
+ * down_proj split by input columns and summed by an NCCL all-reduce over
+ * NVLink.  NCCL is loaded at run time (libnccl.so.2). */
+/* A new NCCL unique id (128 bytes) for rank 0 to hand to every rank. */
+yk_status yk_tp_unique_id(uint8_t id_out[128]);
+/* Joins the group: one engine per rank, all with the same id and world. */
+yk_status yk_tp_init(yk_engine* e, const uint8_t id[128], int32_t rank, int32_t world);
+/* Shard tp_rank of tp_world of the model `cfg`: query heads, KV heads and FFN
+ * columns split evenly (n_kv_heads and ffn_dim divisible by tp_world); the
+ * embedding, the norms and the LM head are replicated (same seed on every
+ * rank).  yk_model_get_config and the tensor shapes report the shard, which is
+ * also the config its KV pool is created with.  The engine must have joined a
+ * group of tp_world ranks; yk_forward_step then all-reduces after o_proj and
+ * down_proj, so every rank must run the same steps. */
+yk_status yk_model_create_tp(yk_engine* e, const yk_model_config* cfg, int32_t tp_rank, int32_t tp_world,
+                             uint64_t seed, float init_std, yk_model** out);
+
 #ifdef __cplusplus
 }
 #endif

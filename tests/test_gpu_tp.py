@@ -1,0 +1,131 @@
+"""Tensor-parallel target (the 70B-shape path): two ranks, one GPU each, NCCL
+all-reduce after o_proj and down_proj.  Each rank loads its slice of one full
+set of weights; the logits of both ranks must be identical (replicated LM head
+on the all-reduced stream) and must match the bf16-emulating oracle forward of
+the full model: max |dlogit| <= 2e-2 * max |logit|, as for the 1-GPU forward.
+Needs two GPUs (skipped otherwise)."""
+import os
+
+import numpy as np
+import pytest
+
+from helpers import TINY, PageTables, step_inputs
+from yanaiengine_b200 import abi
+
+pytestmark = pytest.mark.gpu
+CFG = dict(TINY, n_heads=8, n_kv_heads=2, ffn_dim=384)  # TP2: 4 query heads, 1 KV head, 192 FFN columns per rank
+NB = 64
+WORLD = 2
+
+
+def _bf16(x):
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+def _full_weights(cfg, seed=3):
+    rng = np.random.default_rng(seed)
+    d, V, F, dh = cfg["d_model"], cfg["vocab_size"], cfg["ffn_dim"], cfg["head_dim"]
+    qd, kvd, L = cfg["n_heads"] * dh, cfg["n_kv_heads"] * dh, cfg["n_layers"]
+    n = lambda *s: _bf16(rng.normal(0, 0.02, s))
+    w = dict(embed=n(V, d), lm_head=n(V, d), final_norm=rng.uniform(0.8, 1.2, d).astype(np.float32))
+    for name, shape in (("wq", (qd, d)), ("wk", (kvd, d)), ("wv", (kvd, d)), ("wo", (d, qd)), ("wg", (F, d)),
+                        ("wu", (F, d)), ("wd", (d, F))):
+        w[name] = [n(*shape) for _ in range(L)]
+    for name in ("n1", "n2"):
+        w[name] = [rng.uniform(0.8, 1.2, d).astype(np.float32) for _ in range(L)]
+    return w
+
+
+def _steps(seed=1):
+    rng = np.random.default_rng(seed)
+    V = CFG["vocab_size"]
+    steps = [[(0, rng.integers(0, V, 17).tolist(), 0), (1, rng.integers(0, V, 40).tolist(), 0),
+              (2, rng.integers(0, V, 5).tolist(), 0)]]
+    lens = {0: 17, 1: 40, 2: 5}
+    for _ in range(2):
+        s = []
+        for sid in (0, 1, 2):
+            s.append((sid, rng.integers(0, V, 5).tolist(), lens[sid]))
+            lens[sid] += 5
+        steps.append(s)
+    return steps
+
+
+def _worker(rank, uid, q):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        e = abi.Engine(rank)
+        e.tp_init(uid, rank, WORLD)
+        c = abi.make_config(**CFG, dtype=abi.DTYPE_BF16, max_tokens=128, max_seqs=8)
+        m = abi.Model(e, c, seed=3, tp=(rank, WORLD))
+        w = _full_weights(CFG)
+        dh, F = CFG["head_dim"], CFG["ffn_dim"]
+        hq, hk, fl = CFG["n_heads"] // WORLD * dh, CFG["n_kv_heads"] // WORLD * dh, F // WORLD
+        m.set(abi.T_EMBED, 0, w["embed"])
+        m.set(abi.T_LM_HEAD, 0, w["lm_head"])
+        m.set(abi.T_FINAL_NORM, 0, w["final_norm"])
+        for l in range(CFG["n_layers"]):
+            m.set(abi.T_WQ, l, w["wq"][l][rank * hq:(rank + 1) * hq])
+            m.set(abi.T_WK, l, w["wk"][l][rank * hk:(rank + 1) * hk])
+            m.set(abi.T_WV, l, w["wv"][l][rank * hk:(rank + 1) * hk])
+            m.set(abi.T_WO, l, np.ascontiguousarray(w["wo"][l][:, rank * hq:(rank + 1) * hq]))
+            m.set(abi.T_WGATE, l, w["wg"][l][rank * fl:(rank + 1) * fl])
+            m.set(abi.T_WUP, l, w["wu"][l][rank * fl:(rank + 1) * fl])
+            m.set(abi.T_WDOWN, l, np.ascontiguousarray(w["wd"][l][:, rank * fl:(rank + 1) * fl]))
+            m.set(abi.T_NORM1, l, w["n1"][l])
+            m.set(abi.T_NORM2, l, w["n2"][l])
+        pool = abi.KVPool(e, m.cfg, NB)
+        pt = PageTables(NB)
+        out = []
+        for i, batch in enumerate(_steps()):
+            toks, qs, ctx, bt = step_inputs(pt, batch)
+            rows = m.forward(pool, toks, qs, ctx, bt, 0 if i == 0 else 5)
+            out.append(m.logits(0, rows))
+        err = e.device_error()
+        pool.close()
+        m.close()
+        e.close()
+        q.put((rank, out, err, None))
+    except Exception as ex:  # reported to the parent, which fails the test
+        q.put((rank, None, None, repr(ex)))
+
+
+def test_tp2_forward_matches_oracle(oracle):
+    import torch
+
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    uid = abi.tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, uid, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(WORLD):
+            rank, out, err, exc = q.get(timeout=240)
+            res[rank] = (out, err, exc)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank in range(WORLD):
+        assert res[rank][2] is None, res[rank][2]
+        assert res[rank][1] == 0
+    # the oracle forward of the full model on the same steps
+    w = _full_weights(CFG)
+    orc = oracle.OracleModel(CFG, w, NB, emulate_bf16=True, nthreads=8)
+    pt = PageTables(NB)
+    for i, batch in enumerate(_steps()):
+        toks, qs, cl, bt = step_inputs(pt, batch)
+        o = orc.forward(toks, qs, cl, bt, 0 if i == 0 else 5)
+        g0, g1 = res[0][0][i], res[1][0][i]
+        np.testing.assert_array_equal(g0, g1)  # both ranks hold the same all-reduced stream
+        err = np.abs(g0 - o).max() / np.abs(o).max()
+        assert err < 2e-2, f"step {i}: rel err {err:.3e}"

@@ -70,6 +70,10 @@ _PROTOS = {
     "yk_engine_profile_read": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                            C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
     "yk_model_create": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_uint64, C.c_float, C.POINTER(_P)]),
+    "yk_model_create_tp": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_int32, C.c_int32, C.c_uint64, C.c_float,
+                                       C.POINTER(_P)]),
+    "yk_tp_unique_id": (C.c_int32, [C.POINTER(C.c_uint8)]),
+    "yk_tp_init": (C.c_int32, [_P, C.POINTER(C.c_uint8), C.c_int32, C.c_int32]),
     "yk_model_destroy": (None, [_P]),
     "yk_model_get_config": (C.c_int32, [_P, C.POINTER(ModelConfig)]),
     "yk_model_tensor_shape": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
@@ -243,6 +247,13 @@ def gemm_bf16_epi_timed(engine: "Engine", W_bits: np.ndarray, X_bits: np.ndarray
     return ms.value, st[: g.value], g.value
 
 
+def tp_unique_id() -> bytes:
+    """A new NCCL unique id (128 bytes) for a tensor-parallel group."""
+    buf = (C.c_uint8 * 128)()
+    check(lib().yk_tp_unique_id(buf))
+    return bytes(buf)
+
+
 # ---------------------------------------------------------------------------
 # Thin object wrappers.
 # ---------------------------------------------------------------------------
@@ -268,6 +279,11 @@ class Engine:
         n = C.c_uint64()
         check(lib().ykt_trace_read(self.h, ptr(out, C.c_uint64), self._trace_cap, C.byref(n)))
         return out, int(n.value)
+
+    def tp_init(self, uid: bytes, rank: int, world: int) -> None:
+        """Join a tensor-parallel NCCL group (uid from tp_unique_id on rank 0)."""
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        check(lib().yk_tp_init(self.h, buf, rank, world))
 
     def sync(self):
         check(lib().yk_engine_sync(self.h))
@@ -295,11 +311,18 @@ class Engine:
 
 
 class Model:
-    def __init__(self, engine: Engine, cfg: ModelConfig, seed: int = 1, init_std: float = 0.02):
+    def __init__(self, engine: Engine, cfg: ModelConfig, seed: int = 1, init_std: float = 0.02, tp=None):
+        """tp = (rank, world): shard `rank` of a tensor-parallel target (the engine joined the group)."""
         self.engine = engine
         self.cfg = cfg
         self.h = _P()
-        check(lib().yk_model_create(engine.h, C.byref(cfg), seed, init_std, C.byref(self.h)))
+        if tp is None:
+            check(lib().yk_model_create(engine.h, C.byref(cfg), seed, init_std, C.byref(self.h)))
+        else:
+            check(lib().yk_model_create_tp(engine.h, C.byref(cfg), tp[0], tp[1], seed, init_std, C.byref(self.h)))
+            shard = ModelConfig()
+            check(lib().yk_model_get_config(self.h, C.byref(shard)))
+            self.cfg = shard  # the shard's heads / FFN: the config its KV pool is created with
 
     def shape(self, t: int) -> tuple[int, int]:
         r, c = C.c_int64(), C.c_int64()

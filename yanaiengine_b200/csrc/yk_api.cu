@@ -84,6 +84,7 @@ extern "C" void yk_engine_destroy(yk_engine* e) {
     if (e->pinned) cudaFreeHost(e->pinned);
     if (e->d_err) cudaFree(e->d_err);
     if (e->trace_rec) cudaFree(e->trace_rec);
+    yk::tp_destroy(e);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
 }
@@ -210,15 +211,32 @@ static yk_status validate_cfg(const yk_model_config* c) {
     return YK_OK;
 }
 
-extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, uint64_t seed, float init_std,
-                                     yk_model** out) {
+// A model, or shard tp_rank of tp_world of it (query heads, KV heads and FFN
+// columns split; embedding, norms and LM head replicated).
+static yk_status create_model(yk_engine* e, const yk_model_config* cfg, int tp_rank, int tp_world, uint64_t seed,
+                              float init_std, yk_model** out) {
     YK_ARG(e && out, "null handle");
     *out = nullptr;
     YK_TRY(validate_cfg(cfg));
+    YK_ARG(tp_world >= 1 && tp_rank >= 0 && tp_rank < tp_world, "tp_rank / tp_world");
+    if (tp_world > 1) {
+        YK_ARG(e->nccl_comm && e->tp_world == tp_world && e->tp_rank == tp_rank,
+               "the engine must have joined the tensor-parallel group as this rank (yk_tp_init)");
+        YK_ARG(cfg->n_kv_heads % tp_world == 0 && cfg->ffn_dim % (8 * tp_world) == 0,
+               "n_kv_heads and ffn_dim / 8 must be divisible by tp_world");
+        YK_ARG(cfg->ref_compat == 0, "ref_compat (ReLU on projections) needs the full sum: not tensor-parallel");
+    }
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     auto* m = new yk_model();
     m->e = e;
     m->cfg = *cfg;
+    m->cfg.n_heads /= tp_world;
+    m->cfg.n_kv_heads /= tp_world;
+    m->cfg.ffn_dim /= tp_world;
+    m->tp_rank = tp_rank;
+    m->tp_world = tp_world;
+    // replicated tensors use `seed` on every rank; each shard its own stream
+    const uint64_t shard_seed = tp_world > 1 ? seed ^ (0x9E3779B97F4A7C15ull * (uint64_t)(tp_rank + 1)) : seed;
     const auto& c = m->cfg;
     const size_t es = c.dtype == YK_DTYPE_BF16 ? 2 : 4;
     m->esize = es;
@@ -249,6 +267,7 @@ extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, u
     ALLOC(m->logits, T * V * 4);
     ALLOC(m->rope_denom, dh / 2 * 4);
     ALLOC(m->rope_tab, T * (dh / 2) * sizeof(float2));
+    if (tp_world > 1) ALLOC(m->tp_y, T * d * 4);
     m->gemm_ws_floats = (size_t)2 * e->num_sms * 128 * 256;
     ALLOC(m->gemm_ws, m->gemm_ws_floats * 4);
     m->gemm_counter_cap = 4096;
@@ -275,11 +294,15 @@ extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, u
     // Random init: matrices N(0, init_std), norms 1.
     uint32_t stream_id = 1;
     auto rnd = [&](void* p, size_t n) { return yk::launch_init(e, p, n, c.dtype, seed, stream_id++, init_std, false); };
+    auto rnd_shard = [&](void* p, size_t n) {
+        return yk::launch_init(e, p, n, c.dtype, shard_seed, stream_id++, init_std, false);
+    };
     auto one = [&](float* p, size_t n) { return yk::launch_init(e, p, n, YK_DTYPE_F32, 0, 0, 1.0f, true); };
     if ((s = rnd(m->embed, V * d)) || (s = rnd(m->lm_head, V * d)) || (s = one(m->final_norm, d))) return fail(s);
     for (auto& L : m->layers) {
-        if ((s = rnd(L.wqkv, (qd + 2 * kvd) * d)) || (s = rnd(L.wo, d * qd)) || (s = rnd(L.wgu, 2 * F * d)) ||
-            (s = rnd(L.wdown, d * F)) || (s = one(L.n1, d)) || (s = one(L.n2, d)))
+        if ((s = rnd_shard(L.wqkv, (qd + 2 * kvd) * d)) || (s = rnd_shard(L.wo, d * qd)) ||
+            (s = rnd_shard(L.wgu, 2 * F * d)) || (s = rnd_shard(L.wdown, d * F)) || (s = one(L.n1, d)) ||
+            (s = one(L.n2, d)))
             return fail(s);
     }
     if (c.dtype == YK_DTYPE_BF16) {
@@ -298,6 +321,16 @@ extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, u
     }
     *out = m;
     return YK_OK;
+}
+
+extern "C" yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, uint64_t seed, float init_std,
+                                     yk_model** out) {
+    return create_model(e, cfg, 0, 1, seed, init_std, out);
+}
+
+extern "C" yk_status yk_model_create_tp(yk_engine* e, const yk_model_config* cfg, int32_t tp_rank, int32_t tp_world,
+                                        uint64_t seed, float init_std, yk_model** out) {
+    return create_model(e, cfg, tp_rank, tp_world, seed, init_std, out);
 }
 
 extern "C" void yk_model_destroy(yk_model* m) {
@@ -624,10 +657,18 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         kv_win += c.window > 0 ? std::min((double)ctx[b], (double)c.window + n - 1) : (double)ctx[b];
     }
     const double kv_tok_bytes = 2.0 * kvd * (double)m->esize;
+    // Tensor parallel: o_proj / down_proj write fp32 partials that are summed
+    // across the group; the sum is added to the residual stream by the next RMSNorm.
+    const bool tp = m->tp_world > 1;
+    const float* pend = nullptr;  // all-reduced partial not yet added to h
+    EpiParams es;
+    es.kind = EPI_STORE;
+    es.out = m->tp_y;
     YK_TRY(launch_embed(m, m->cur.tokens, m->cur.pos, T));
     for (int l = 0; l < c.n_layers; ++l) {
         LayerWeights& L = m->layers[l];
-        YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr));
+        YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr, pend));
+        pend = nullptr;
         EpiParams eq;
         eq.kind = EPI_QKV;
         eq.ref_compat = c.ref_compat;
@@ -652,17 +693,30 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         er.ref_compat = c.ref_compat;
         er.h = m->h;
         er.ld = d;
-        YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, er));
-        YK_TRY(launch_rmsnorm(m, L.n2, T, nullptr));
+        if (tp) {
+            YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, es));
+            YK_TRY(tp_allreduce_f32(e, m->tp_y, (size_t)T * d));
+            pend = m->tp_y;
+        } else {
+            YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, er));
+        }
+        YK_TRY(launch_rmsnorm(m, L.n2, T, nullptr, pend));
+        pend = nullptr;
         EpiParams eg;
         eg.kind = EPI_GLU;
         eg.ref_compat = c.ref_compat;
         eg.out = m->act;
         eg.act = c.act;
         YK_TRY(gemm_run(m, L.wgu, &L.tm_gu, m->xn, 2 * F, d, T, eg));
-        YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, er));
+        if (tp) {
+            YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, es));
+            YK_TRY(tp_allreduce_f32(e, m->tp_y, (size_t)T * d));
+            pend = m->tp_y;
+        } else {
+            YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, er));
+        }
     }
-    YK_TRY(launch_rmsnorm(m, m->final_norm, R, m->cur.rows));
+    YK_TRY(launch_rmsnorm(m, m->final_norm, R, m->cur.rows, pend));
     EpiParams el;
     el.kind = EPI_LOGITS;
     el.ref_compat = c.ref_compat;

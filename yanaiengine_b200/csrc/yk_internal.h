@@ -66,6 +66,8 @@ struct yk_engine {
     int attn_waves = 1;                  // attention items per resident CTA slot (env YK_ATTN_WAVES)
     bool attn_balanced = false;          // attention pieces <= average slot load (env YK_ATTN_PLAN=1)
     bool profiling = false;
+    void* nccl_comm = nullptr;           // tensor-parallel group (yk_tp_init), else null
+    int tp_rank = 0, tp_world = 1;
     void* trace_rec = nullptr;           // launch trace records (test hook), else null
     uint32_t trace_cap = 0;
     std::vector<ProfRecord> prof_pending;
@@ -108,6 +110,8 @@ struct yk_model {
     void* lm_head = nullptr;   // [V x d]
     float* final_norm = nullptr;
     std::vector<LayerWeights> layers;
+    int tp_rank = 0, tp_world = 1;  // tensor-parallel shard (cfg holds the shard's heads / FFN)
+    float* tp_y = nullptr;          // [T x d] fp32 partial of o_proj / down_proj, all-reduced
     CUtensorMap tm_lm;
     // activations
     float* h = nullptr;        // [T x d] fp32 residual stream
@@ -247,7 +251,9 @@ void plan_attention(const yk_model_config& c, int num_sms, int waves, bool balan
 size_t attention_ws_floats_per_slot(int head_dim);
 yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool);
 yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T);
-yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx);
+yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx, const float* add = nullptr);
+yk_status tp_allreduce_f32(yk_engine* e, float* buf, size_t count);
+void tp_destroy(yk_engine* e);
 yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed, uint32_t stream, float std,
                       bool constant);
 

@@ -45,16 +45,18 @@ __device__ __forceinline__ void store4(__nv_bfloat16* y, float a, float b, float
         make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
 }
 template <typename AT>
-__global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
+__global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ g,
                                                             AT* __restrict__ y, int d, float eps,
-                                                            const int32_t* __restrict__ rows, Trace tr) {
+                                                            const int32_t* __restrict__ rows,
+                                                            const float* __restrict__ add, Trace tr) {
     if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0) trace_mark(tr, TR_START);
     const int r = blockIdx.x;
     const int src = rows ? rows[r] : r;
-    const float* xr = x + (size_t)src * d;
+    float* xr = x + (size_t)src * d;
+    const float* ar = add ? add + (size_t)src * d : nullptr;  // pending residual: x += add first
     __shared__ float red[RN_THREADS / 32];
     float ss = 0.f;
     const bool vec = (d & 3) == 0 && d <= RN_THREADS * 4 * RN_VEC;
@@ -64,10 +66,18 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const float* __rest
         for (int k = 0; k < RN_VEC; ++k) {
             const int i = (threadIdx.x + k * RN_THREADS) * 4;
             xv[k] = i < d ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ar && i < d) {
+                const float4 av = *reinterpret_cast<const float4*>(ar + i);
+                xv[k] = make_float4(xv[k].x + av.x, xv[k].y + av.y, xv[k].z + av.z, xv[k].w + av.w);
+                *reinterpret_cast<float4*>(xr + i) = xv[k];
+            }
             ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y + xv[k].z * xv[k].z + xv[k].w * xv[k].w;
         }
     } else {
-        for (int i = threadIdx.x; i < d; i += RN_THREADS) ss += xr[i] * xr[i];
+        for (int i = threadIdx.x; i < d; i += RN_THREADS) {
+            if (ar) xr[i] += ar[i];
+            ss += xr[i] * xr[i];
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -128,14 +138,15 @@ yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, i
     return YK_OK;
 }
 
-yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx) {
+yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx, const float* add) {
     const auto& c = m->cfg;
     if (c.dtype == YK_DTYPE_BF16)
-        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<__nv_bfloat16>, rows, RN_THREADS, 0, (const float*)m->h, g,
-                                 (__nv_bfloat16*)m->xn, c.d_model, c.rms_eps, row_idx, trace_next(m->e, TK_RMSNORM)));
+        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<__nv_bfloat16>, rows, RN_THREADS, 0, m->h, g,
+                                 (__nv_bfloat16*)m->xn, c.d_model, c.rms_eps, row_idx, add,
+                                 trace_next(m->e, TK_RMSNORM)));
     else
-        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<float>, rows, RN_THREADS, 0, (const float*)m->h, g, (float*)m->xn,
-                                 c.d_model, c.rms_eps, row_idx, trace_next(m->e, TK_RMSNORM)));
+        YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<float>, rows, RN_THREADS, 0, m->h, g, (float*)m->xn, c.d_model,
+                                 c.rms_eps, row_idx, add, trace_next(m->e, TK_RMSNORM)));
     m->e->launches++;
     return YK_OK;
 }
