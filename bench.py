@@ -38,6 +38,11 @@ TARGET = dict(vocab_size=128256, d_model=4096, n_layers=32, n_heads=32, n_kv_hea
               rope_theta=500000.0, rms_eps=1e-5, attn_cap=0.0, final_cap=0.0, window=0, window_layer_parity=-1,
               act=0, ref_compat=0)
 DRAFT = dict(TARGET, d_model=2048, n_layers=16, n_heads=32, n_kv_heads=8, head_dim=64, ffn_dim=8192)
+# --workload 70b-tp: Llama-3-70B-shape target, tensor parallel over all ranks, 8B-shape draft replicated
+TARGET_70B = dict(TARGET, d_model=8192, n_layers=80, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672)
+METRIC_70B = "accepted tokens/sec, 70B-shape target (TP over all GPUs) + 8B-shape draft, k=4 batch 128"
+WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (NCCL all-reduce after o_proj / down_proj) + "
+                "8B-shape draft replicated, bf16, k=4, T=0.8, 128 seqs x 4096 ctx")
 METRIC = "accepted tokens/sec, 8B/1B-shape k=5 batch 32, at 1/2/4/8 B200; verify HBM GB/s"
 WORKLOAD = "spec-decode step: 8B-shape target + 1B-shape draft, bf16, k=5, T=0.8, 32 seqs/GPU, ctx U[512,2048]"
 
@@ -229,29 +234,45 @@ def measured_peaks() -> dict:
 
 
 def run_yk(args, world, rank, local):
-    from yanaiengine_b200 import abi
+    from yanaiengine_b200 import abi, dp
 
     k, B, T = args.k, args.batch, args.temperature
+    tp = args.workload == "70b-tp"
     eng = abi.Engine(local)
-    tcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
-    dcfg = abi.make_config(**DRAFT, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
-    from yanaiengine_b200 import dp
+    if tp:
+        # every rank holds one shard of the target and runs the whole batch
+        import torch
+        import torch.distributed as dist
 
-    # the job's B x world sequences, split across ranks longest-first (B per rank)
-    glens = dp.global_lengths(B, world, seed=7)
-    mine = dp.partition(glens, world)[rank]
-    lens = glens[mine]
-    rng = np.random.default_rng(7 + 1000 * rank)
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(abi.tp_unique_id()), dtype=torch.uint8))
+        if world > 1:
+            dist.broadcast(uid, 0)
+        eng.tp_init(bytes(uid.cpu().numpy()), rank, world)
+        tcfg = abi.make_config(**TARGET_70B, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
+        dcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
+        lens = np.full(B, 4096, dtype=np.int64)
+        mine = np.arange(B)
+        rng = np.random.default_rng(7)
+    else:
+        tcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
+        dcfg = abi.make_config(**DRAFT, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
+        # the job's B x world sequences, split across ranks longest-first (B per rank)
+        glens = dp.global_lengths(B, world, seed=7)
+        mine = dp.partition(glens, world)[rank]
+        lens = glens[mine]
+        rng = np.random.default_rng(7 + 1000 * rank)
     grow = (args.warmup + 2 * args.steps + 4) * (k + 1) + 32
     blocks = int(sum(np.ceil((lens + grow) / 16))) + 64
-    target = abi.Model(eng, tcfg, seed=1, init_std=0.02)
+    target = abi.Model(eng, tcfg, seed=1, init_std=0.02, tp=(rank, world) if tp else None)
     draft = abi.Model(eng, dcfg, seed=2, init_std=0.02)
-    tpool = abi.KVPool(eng, tcfg, blocks)
+    tpool = abi.KVPool(eng, target.cfg, blocks)
     dpool = abi.KVPool(eng, dcfg, blocks)
-    tpool.fill_random(11, 1.0)
+    tpool.fill_random(11 + (rank if tp else 0), 1.0)
     dpool.fill_random(12, 1.0)
     sampler = abi.Sampler(eng, B, k, TARGET["vocab_size"])
-    sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + rank)
+    sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + (0 if tp else rank))
     for i, L in enumerate(lens):
         sch.submit(rng.integers(0, TARGET["vocab_size"], int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
                    seq_id=int(mine[i]), cached=True)
@@ -292,7 +313,9 @@ def run_yk(args, world, rank, local):
     launches = eng.launches() - launches0
     max_dev_s = allreduce_max(world, dev_ms / 1e3)
     max_wall = allreduce_max(world, wall)
-    tot_emitted = allreduce_sum(world, float(emitted))
+    # data parallel: every rank emits its own sequences' tokens; tensor parallel:
+    # all ranks emit the same tokens, counted once
+    tot_emitted = float(emitted) if tp else allreduce_sum(world, float(emitted))
 
     # kernel roofline: a second pass of the same steps with per-launch CUDA events
     eng.profile(True)
@@ -312,7 +335,7 @@ def run_yk(args, world, rank, local):
         attn_gbs = attn["bytes"] / (attn["ms"] / 1e3) / 1e9 if attn["ms"] > 0 else 0.0
         step_ms = max_dev_s * 1e3 / args.steps
         res = {
-            "metric": METRIC,
+            "metric": METRIC_70B if tp else METRIC,
             "value": tot_emitted / max_dev_s,
             "unit": "tokens/s",
             "n_gpus": world,
@@ -320,13 +343,17 @@ def run_yk(args, world, rank, local):
             "warmup": args.warmup,
             "ms_per_step": step_ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: random-init weights N(0,0.02), random token ids, synthetic N(0,1) KV context",
-            "config": {"workload": WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B, "k": k,
-                       "temperature": T, "ctx": "U[512,2048] + growth", "parallelism": f"dp{world} (replicas)",
-                       "l2": "inputs larger than L2 (17.5 GB of weights streamed per step)"},
+            "config": ({"workload": WORKLOAD_70B, "global_batch": B, "k": k, "temperature": T, "ctx": "4096 + growth",
+                        "parallelism": f"tp{world} target, draft replicated",
+                        "l2": "inputs larger than L2 (17.5 GB target shard + 16 GB draft per GPU per step)"}
+                       if tp else
+                       {"workload": WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B, "k": k,
+                        "temperature": T, "ctx": "U[512,2048] + growth", "parallelism": f"dp{world} (replicas)",
+                        "l2": "inputs larger than L2 (17.5 GB of weights streamed per step)"}),
             "e2e": {"value": tot_emitted / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d / args.steps),
                     "d2h_bytes_per_step": int(d2h / args.steps)},
             "gpu_launches": int(launches),
@@ -407,7 +434,15 @@ def main():
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--temperature", type=float, default=0.8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="8b-dp", choices=["8b-dp", "70b-tp"],
+                    help="8b-dp: the headline 8B/1B data-parallel step; 70b-tp: 70B-shape target over all GPUs")
     args = ap.parse_args()
+    if args.workload == "70b-tp":
+        # the 70B configuration: batch 128, k = 4 (other flags as given)
+        if "--batch" not in sys.argv:
+            args.batch = 128
+        if "--k" not in sys.argv:
+            args.k = 4
     world, rank, local = dist_setup(args.gpus)
     nthreads = os.cpu_count() or 1
 
@@ -436,7 +471,7 @@ def main():
 
     res, lens = run_yk(args, world, rank, local)
     if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.workload == "8b-dp":
             sample = cpu_step_sample(lens, args.k, args.temperature, nthreads)
             res["cpu_baseline"] = cpu_baseline_dict(sample, nthreads, sample["emitted_per_step"])
         print(json.dumps(res))
