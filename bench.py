@@ -39,6 +39,7 @@ TARGET = dict(vocab_size=128256, d_model=4096, n_layers=32, n_heads=32, n_kv_hea
               act=0, ref_compat=0)
 DRAFT = dict(TARGET, d_model=2048, n_layers=16, n_heads=32, n_kv_heads=8, head_dim=64, ffn_dim=8192)
 # --workload 70b-tp: Llama-3-70B-shape target, tensor parallel over all ranks, 8B-shape draft replicated
+GEMM_TRAFFIC_RATIO = 1.018  # measured DRAM bytes / algorithmic bytes of a GEMM launch (ncu capture)
 TARGET_70B = dict(TARGET, d_model=8192, n_layers=80, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672)
 METRIC_70B = "accepted tokens/sec, 70B-shape target (TP over all GPUs) + 8B-shape draft, k=4 batch 128"
 WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (NCCL all-reduce after o_proj / down_proj) + "
@@ -360,7 +361,12 @@ def run_yk(args, world, rank, local):
             "accept_rate": float((acc1 - acc0) / max(1, args.steps * B * k)),
             "emitted_per_step": float(emitted / args.steps),
             "roofline": {"bound": "hbm", "achieved": gemm_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gemm_gbs / peaks["hbm_gbs"], "traffic": None, "kernel": "gemm_tc_kernel",
+                         "frac": gemm_gbs / peaks["hbm_gbs"],
+                         # ncu, 28672x4096x192 gate/up launch: DRAM read+write / algorithmic bytes = 1.018
+                         "traffic": GEMM_TRAFFIC_RATIO * gemm["bytes"] / max(1, gemm["launches"]),
+                         "traffic_src": "ncu dram bytes of the 28672x4096x192 gate/up launch / its algorithmic "
+                                        "bytes (1.018), applied to the average launch's algorithmic bytes",
+                         "kernel": "gemm_tc_kernel",
                          "peak_src": peaks["src"],
                          "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])},
             "attention": {"achieved_gbs": attn_gbs, "frac": attn_gbs / peaks["hbm_gbs"], "launches": attn["launches"]},

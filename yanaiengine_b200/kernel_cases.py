@@ -110,7 +110,7 @@ def gemm(args) -> None:
     X = abi.bf16_bits(rng.normal(0, 1, (args.m, args.k)).astype(np.float32))
     _, ms, _, g = abi.gemm_bf16_timed(e, W, X, 0, -args.reps)
     gb = (args.n + args.m) * args.k * 2 / 1e9
-    print(f"gemm {args.n}x{args.k}x{args.m} grid={g}: {1e3 * ms:.1f} us cold-L2, {gb / ms:.0f} GB/s")
+    print(f"gemm {args.n}x{args.k}x{args.m} grid={g}: {1e3 * ms:.1f} us cold-L2, {gb / (ms / 1e3):.0f} GB/s")
     e.close()
 
 
