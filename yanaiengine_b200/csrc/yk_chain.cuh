@@ -129,10 +129,23 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         const int q = (int)(i & (CHAIN_ROUND - 1));
         return cs.ring[q + (q >> 4)];
     };
-    // Ring := terms [pos, min(pos + ROUND, n)), loading only what is missing (coalesced).
+    // Ring := terms [pos, min(pos + ROUND, n)), loading only what is missing
+    // (coalesced; a thread's up to CHAIN_EPT terms are all evaluated, their loads
+    // in flight together, before any is stored).
     auto fill = [&]() {
         const long long want = min(pos + (long long)CHAIN_ROUND, n);
-        for (long long i = max(hi, pos) + threadIdx.x; i < want; i += CHAIN_THREADS) slot(i) = f(i);
+        const long long from = max(hi, pos) + threadIdx.x;
+        float v[CHAIN_EPT];
+#pragma unroll
+        for (int u = 0; u < CHAIN_EPT; ++u) {
+            const long long i = from + (long long)u * CHAIN_THREADS;
+            v[u] = i < want ? f(i) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < CHAIN_EPT; ++u) {
+            const long long i = from + (long long)u * CHAIN_THREADS;
+            if (i < want) slot(i) = v[u];
+        }
         hi = max(hi, want);
         __syncthreads();
     };
