@@ -172,13 +172,24 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         fill();
         const int cnt = (int)min(n - pos, limit);
         if (threadIdx.x == 0) {
+            // eight terms loaded ahead of the eight dependent additions
             float cc = c;
             long long fnd = -1;
             int t = 0;
-            for (; t < cnt; ++t) {
-                cc = __fadd_rn(cc, slot(pos + t));
-                if (search && r <= cc) { fnd = pos + t; ++t; break; }
-                if (isnan(cc)) { t = (int)(n - pos); break; }
+            bool stop = false;
+            for (int t0 = 0; t0 < cnt && !stop; t0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = t0 + u < cnt ? slot(pos + t0 + u) : 0.f;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (!stop && t0 + u < cnt) {
+                        cc = __fadd_rn(cc, v[u]);
+                        t = t0 + u + 1;
+                        if (search && r <= cc) { fnd = pos + t0 + u; stop = true; }
+                        else if (isnan(cc)) { t = (int)(n - pos); stop = true; }
+                    }
+                }
             }
             cs.c_seq = cc;
             cs.pos_seq = pos + t;
