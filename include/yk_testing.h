@@ -46,6 +46,16 @@ yk_status ykt_gemm_bf16_epi_timed(yk_engine* e, const uint16_t* W, const uint16_
 yk_status ykt_attention_stamps_enable(yk_model* m, int32_t cap);
 yk_status ykt_attention_stamps_read(yk_model* m, uint64_t* host, int32_t cap, int32_t* n_ctas);
 
+/* Per-CTA phase stamps of the bf16 GEMM launches of one trace kind (as in
+ * ykt_trace_enable: 3 | epilogue << 4 | 128-row tiles << 8 | tokens/16 << 24;
+ * 0 disables) inside normal forward steps.  Each matching launch overwrites 8
+ * words per CTA (%globaltimer ns): start (before the grid dependency wait),
+ * first activation copy issued (after it), first k-block landed, last MMA
+ * issued, accumulator ready, epilogue done, segments, cluster barrier passed.
+ * read copies the last matching launch's records. */
+yk_status ykt_gemm_stamps_enable(yk_model* m, uint32_t kind);
+yk_status ykt_gemm_stamps_read(yk_model* m, uint64_t* host, int32_t cap, int32_t* n_ctas);
+
 /* Launch trace of the kernels on the engine stream.  enable(cap) (cap > 0)
  * resets cap records; launch i (the i-th launch counted by
  * yk_engine_launches) writes record i % cap: first CTA entry, first CTA past

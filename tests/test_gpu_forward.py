@@ -122,3 +122,17 @@ def test_rejects_bad_block_id(engine):
     finally:
         pool.close()
         m.close()
+
+
+@pytest.mark.parametrize("knob", [("YK_GEMM_PUSH_MIN", "0"), ("YK_GEMM_VARIANT", "8")])
+def test_bf16_cluster_reduction_modes(oracle, monkeypatch, knob):
+    """Every cluster split-K reduction by copy-engine exchange (with the QKV RoPE rows
+    staged in shared memory), then every one by distributed-shared-memory loads;
+    64 prefill tokens and head_dim 128 give 128-token tiles split over 2+ CTAs."""
+    monkeypatch.setenv(*knob)
+    e = abi.Engine(0)  # reads the knob at creation
+    try:
+        cfg = dict(TINY, head_dim=128, n_heads=4, n_kv_heads=2)
+        _drive(e, oracle, cfg, abi.DTYPE_BF16, True, 2e-2, steps=2)
+    finally:
+        e.close()

@@ -18,13 +18,14 @@ SHAPES = [
     (256, 200, 33, 1),       # K tail inside a 64-wide k-block (TMA zero fill)
     (512, 1024, 192, 3),     # 4 tiles x 16 k-blocks over 3 CTAs: cut tiles, 2-way fix-up
     (512, 1024, 192, 37),    # each tile cut across ~9 CTAs
-    (512, 1024, 192, -3),    # cluster mode: 3-CTA clusters reduce through distributed shared memory
+    (512, 1024, 192, -3),    # cluster mode: 3-CTA clusters, 32 KB column shares exchanged by copy engine
     (1000, 320, 7, -5),      # cluster mode, one k-block per CTA, row and token tails
     (384, 512, 40, -8),      # cluster mode, 8-CTA clusters
     (256, 200, 33, -4),      # cluster mode with a K tail
     (6144, 4096, 192, 0),    # verify QKV shape (heuristic: cluster mode)
     (4096, 14336, 32, 0),    # down-proj shape at draft batch (cluster mode)
     (512, 256, 300, 0),      # two token tiles (BN = 256)
+    (512, 512, 256, -4),     # cluster mode, BN = 256: no room for receive slots, shares loaded over DSMEM
     (28672, 4096, 192, 0),   # verify gate/up: 235 MB of weights (> L2), stream-K; the profiling case
 ]
 

@@ -110,6 +110,8 @@ _PROTOS = {
                                             C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _F32P,
                                             C.POINTER(C.c_uint64), _I32P]),
     "ykt_attention_stamps_enable": (C.c_int32, [_P, C.c_int32]),
+    "ykt_gemm_stamps_enable": (C.c_int32, [_P, C.c_uint32]),
+    "ykt_gemm_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, _I32P]),
     "ykt_trace_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_sampler_stamps_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_sampler_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32]),
@@ -357,6 +359,17 @@ class Model:
         out = np.zeros((4096, 8), np.uint64)
         n = C.c_int32()
         check(lib().ykt_attention_stamps_read(self.h, ptr(out, C.c_uint64), 4096, C.byref(n)))
+        return out[: n.value]
+
+    def gemm_stamps(self, kind: int | None = None):
+        """Test hook: kind (a GEMM trace kind; 0 disables) selects the launches that
+        record per-CTA stamps; kind None returns the last one's ([n_ctas x 8] uint64)."""
+        if kind is not None:
+            check(lib().ykt_gemm_stamps_enable(self.h, kind))
+            return None
+        out = np.zeros((1024, 8), np.uint64)
+        n = C.c_int32()
+        check(lib().ykt_gemm_stamps_read(self.h, ptr(out, C.c_uint64), 1024, C.byref(n)))
         return out[: n.value]
 
     def logits(self, row0: int, rows: int) -> np.ndarray:

@@ -69,6 +69,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     e->encode_tiled = (PFN_tmapEncodeTiled)fn;
     if (const char* v = std::getenv("YK_PDL")) e->pdl = std::strcmp(v, "0") != 0;
     if (const char* v = std::getenv("YK_GEMM_VARIANT")) e->gemm_variant = std::atoi(v);
+    if (const char* v = std::getenv("YK_GEMM_PUSH_MIN")) e->gemm_push_min = std::max(0, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
     yk_status s = e->ensure_pinned((size_t)4 << 20);
@@ -342,6 +343,7 @@ extern "C" void yk_model_destroy(yk_model* m) {
     if (m->attn_ws) cudaFree(m->attn_ws);
     if (m->attn_counters) cudaFree(m->attn_counters);
     if (m->attn_stamps) cudaFree(m->attn_stamps);
+    if (m->gemm_stamps) cudaFree(m->gemm_stamps);
     if (m->gemm_counters) cudaFree(m->gemm_counters);
     delete m;
 }

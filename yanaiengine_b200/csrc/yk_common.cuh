@@ -247,6 +247,31 @@ __device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
                  : "memory");
     return v;
 }
+// Bulk copy (copy engine) of `bytes` (a multiple of 16; both addresses 16-byte
+// aligned) from this CTA's shared memory into the shared memory of a CTA of
+// the cluster (dst and bar: shared::cluster addresses from mapa); completes
+// with complete_tx on that CTA's mbarrier.  Point to point.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "r"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory; completes with complete_tx on
+// this CTA's mbarrier.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (bulk copy) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ float4 lds_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
 // Cluster barrier that warps may reach divergently (no .aligned).
 __device__ __forceinline__ void cluster_sync_any() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");

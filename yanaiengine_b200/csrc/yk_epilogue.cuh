@@ -30,6 +30,14 @@ __device__ __forceinline__ float act_gelu_tanh(float x) {
     return x * cdf;
 }
 
+// RoPE rotation of the pair (x, y) by (cos, sin): (x cos - y sin, x sin + y cos),
+// each product rounded before the sum (no contraction into FMA, so the result
+// does not depend on where the compiler inlines it; the reference's fp32
+// expression).
+__device__ __forceinline__ float2 rope_rot(float x, float y, float cs, float sn) {
+    return make_float2(__fsub_rn(__fmul_rn(x, cs), __fmul_rn(y, sn)), __fadd_rn(__fmul_rn(x, sn), __fmul_rn(y, cs)));
+}
+
 __device__ __forceinline__ float logit_out(const EpiParams& p, float v) {
     if (p.ref_compat) v = v + 0.1f;
     if (p.cap > 0.f) v = p.cap * tanhf(v / p.cap);
@@ -88,9 +96,9 @@ __device__ __forceinline__ void epi_pair(const EpiParams& p, int n, int j, float
             const int c = (n < p.q_dim ? n : n - p.q_dim) % dh;
             float cs, sn;
             rope_cs(p, c, j, cs, sn);
-            const float r0 = v0 * cs - v1 * sn, r1 = v0 * sn + v1 * cs;
-            v0 = r0;
-            v1 = r1;
+            const float2 r = rope_rot(v0, v1, cs, sn);
+            v0 = r.x;
+            v1 = r.y;
         }
         if (n < p.q_dim) {
             AT* o = reinterpret_cast<AT*>(p.out) + (size_t)j * p.q_dim + n;
@@ -105,6 +113,30 @@ __device__ __forceinline__ void epi_pair(const EpiParams& p, int n, int j, float
     }
 }
 
+// Two / four consecutive outputs with one store (o aligned to 2 / 4 elements).
+__device__ __forceinline__ void store2(float* o, float a, float b) { *reinterpret_cast<float2*>(o) = make_float2(a, b); }
+__device__ __forceinline__ void store2(__nv_bfloat16* o, float a, float b) {
+    *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(a, b);
+}
+__device__ __forceinline__ void store4(float* o, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(o) = make_float4(a, b, c, d);
+}
+__device__ __forceinline__ void store4(__nv_bfloat16* o, float a, float b, float c, float d) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    *reinterpret_cast<uint2*>(o) = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+// Destination of QKV row n (an aligned group of rows within one head) for token
+// j: the q buffer, or the token's KV-pool slot (null if its page is outside the pool).
+template <typename AT>
+__device__ __forceinline__ AT* qkv_dst(const EpiParams& p, int n, int j) {
+    if (n < p.q_dim) return reinterpret_cast<AT*>(p.out) + (size_t)j * p.q_dim + n;
+    const int kv = n < p.q_dim + p.kv_dim ? 0 : 1;
+    const int nn = n - p.q_dim - kv * p.kv_dim;
+    const int sh = __ffs(p.head_dim) - 1;  // head_dim is a power of two
+    return pool_elem<AT>(p, kv, nn >> sh, nn & (p.head_dim - 1), j);
+}
+
 // QKV rows (n, n+1), n even, of token j with the RoPE (cos, sin) of their pair
 // given (ignored for V rows): Q to the q buffer, K/V to the token's pool slot.
 template <typename AT>
@@ -112,22 +144,12 @@ __device__ __forceinline__ void qkv_pair_cs(const EpiParams& p, int n, int j, fl
     if (j >= p.m_tok || n >= p.n_out) return;
     if (p.ref_compat) { v0 = compat_relu(v0); v1 = compat_relu(v1); }
     if (n < p.q_dim + p.kv_dim) {
-        const float r0 = v0 * cs - v1 * sn, r1 = v0 * sn + v1 * cs;
-        v0 = r0;
-        v1 = r1;
+        const float2 r = rope_rot(v0, v1, cs, sn);
+        v0 = r.x;
+        v1 = r.y;
     }
-    AT* o;
-    if (n < p.q_dim) {
-        o = reinterpret_cast<AT*>(p.out) + (size_t)j * p.q_dim + n;
-    } else {
-        const int kv = n < p.q_dim + p.kv_dim ? 0 : 1;
-        const int nn = n - p.q_dim - kv * p.kv_dim;
-        const int sh = __ffs(p.head_dim) - 1;  // head_dim is a power of two
-        o = pool_elem<AT>(p, kv, nn >> sh, nn & (p.head_dim - 1), j);
-        if (!o) return;
-    }
-    o[0] = from_f32<AT>(v0);
-    o[1] = from_f32<AT>(v1);
+    AT* o = qkv_dst<AT>(p, n, j);
+    if (o) store2(o, v0, v1);
 }
 // (cos, sin) of RoPE pair index i (= dim / 2) at token j: the step's table, or computed.
 __device__ __forceinline__ float2 rope_pair(const EpiParams& p, int i, int j) {
@@ -164,7 +186,8 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int j = j0 + (odd ? i + 8 : i);
-            const float x0 = odd ? w[i + 8] : v[i], x1 = odd ? v[i + 8] : w[i];
+            const float vl = v[i], vh = v[i + 8], wl = w[i], wh = w[i + 8];
+            const float x0 = odd ? wh : vl, x1 = odd ? vh : wl;
             if (j < p.m_tok) qkv_pair_cs<AT>(p, n & ~1, j, x0, x1, r[i].x, r[i].y);
         }
     } else if constexpr (KIND == EPI_GLU) {
@@ -176,18 +199,22 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
         if (n >= p.n_out) return;
         const bool odd = n & 1;
         AT* o = reinterpret_cast<AT*>(p.out) + (n >> 1);
-        if (!p.ref_compat && p.act != 1) {  // SiLU, the common case: a compact loop
+        // (every array index is a compile-time constant and the selects are on
+        // values, so v and w stay in registers)
+        if (!p.ref_compat && p.act != 1) {  // SiLU, the common case
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int j = j0 + (odd ? i + 8 : i);
-                const float g = odd ? w[i + 8] : v[i], u = odd ? v[i + 8] : w[i];
+                const float vl = v[i], vh = v[i + 8], wl = w[i], wh = w[i + 8];
+                const float g = odd ? wh : vl, u = odd ? vh : wl;
                 if (j < p.m_tok) o[(size_t)j * (p.n_out >> 1)] = from_f32<AT>(act_silu(g) * u);
             }
         } else {
-#pragma unroll 1
+#pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int j = j0 + (odd ? i + 8 : i);
-                float g = odd ? w[i + 8] : v[i], u = odd ? v[i + 8] : w[i];
+                const float vl = v[i], vh = v[i + 8], wl = w[i], wh = w[i + 8];
+                float g = odd ? wh : vl, u = odd ? vh : wl;
                 if (p.ref_compat) { g = compat_relu(g); u = compat_relu(u); }
                 if (j < p.m_tok) o[(size_t)j * (p.n_out >> 1)] = from_f32<AT>((p.act == 1 ? act_gelu_tanh(g) : act_silu(g)) * u);
             }
@@ -209,7 +236,7 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
             for (int i = 0; i < 16; ++i)
                 if (j0 + i < p.m_tok) o[(size_t)(j0 + i) * p.n_out + n] = v[i];
         } else {
-#pragma unroll 1
+#pragma unroll
             for (int i = 0; i < 16; ++i)
                 if (j0 + i < p.m_tok) o[(size_t)(j0 + i) * p.n_out + n] = logit_out(p, v[i]);
         }
@@ -220,6 +247,20 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
 __device__ __forceinline__ void epi_quad_resid(const EpiParams& p, int n, int j, float4 v, float4 h) {
     if (p.ref_compat) { v.x = compat_relu(v.x); v.y = compat_relu(v.y); v.z = compat_relu(v.z); v.w = compat_relu(v.w); }
     *reinterpret_cast<float4*>(p.h + (size_t)j * p.ld + n) = make_float4(h.x + v.x, h.y + v.y, h.z + v.z, h.w + v.w);
+}
+
+// QKV rows n..n+3 (n % 4 == 0) of token j with the (cos, sin) of their two RoPE
+// pairs loaded by the caller; one 4-element store.
+template <typename AT>
+__device__ __forceinline__ void epi_quad_qkv(const EpiParams& p, int n, int j, float4 v, float4 rope) {
+    if (j >= p.m_tok || n >= p.n_out) return;
+    if (p.ref_compat) { v.x = compat_relu(v.x); v.y = compat_relu(v.y); v.z = compat_relu(v.z); v.w = compat_relu(v.w); }
+    if (n < p.q_dim + p.kv_dim) {
+        const float2 r0 = rope_rot(v.x, v.y, rope.x, rope.y), r1 = rope_rot(v.z, v.w, rope.z, rope.w);
+        v = make_float4(r0.x, r0.y, r1.x, r1.y);
+    }
+    AT* o = qkv_dst<AT>(p, n, j);
+    if (o) store4(o, v.x, v.y, v.z, v.w);
 }
 
 // Rows n..n+3 (n % 4 == 0; n_out is a multiple of 4) of token j with one vector
@@ -248,25 +289,12 @@ __device__ __forceinline__ void epi_quad(const EpiParams& p, int n, int j, float
             a0 = (p.act == 1 ? act_gelu_tanh(g0) : act_silu(g0)) * u0;
             a1 = (p.act == 1 ? act_gelu_tanh(g1) : act_silu(g1)) * u1;
         }
-        AT* o = reinterpret_cast<AT*>(p.out) + (size_t)j * (p.n_out >> 1) + (n >> 1);
-        o[0] = from_f32<AT>(a0);
-        o[1] = from_f32<AT>(a1);
+        store2(reinterpret_cast<AT*>(p.out) + (size_t)j * (p.n_out >> 1) + (n >> 1), a0, a1);
     } else if constexpr (KIND == EPI_QKV) {
         const int ci = rope_dim(p, n) >> 1;
         const float2 r0 = rope_pair(p, ci, j), r1 = rope_pair(p, ci + 1, j);
-        qkv_pair_cs<AT>(p, n, j, v.x, v.y, r0.x, r0.y);
-        qkv_pair_cs<AT>(p, n + 2, j, v.z, v.w, r1.x, r1.y);
+        epi_quad_qkv<AT>(p, n, j, v, make_float4(r0.x, r0.y, r1.x, r1.y));
     }
 }
 
-}  // namespace yk
-
-namespace yk {
-// QKV rows n..n+3 of token j with the (cos, sin) of their two RoPE pairs loaded by the caller.
-template <typename AT>
-__device__ __forceinline__ void epi_quad_qkv(const EpiParams& p, int n, int j, float4 v, float4 rope) {
-    if (j >= p.m_tok || n >= p.n_out) return;
-    qkv_pair_cs<AT>(p, n, j, v.x, v.y, rope.x, rope.y);
-    qkv_pair_cs<AT>(p, n + 2, j, v.z, v.w, rope.z, rope.w);
-}
 }  // namespace yk

@@ -16,8 +16,10 @@
 //     arrives last: it sums the published fp32 partials in k order and runs the
 //     epilogue.  No CTA waits for another.
 //   * cluster split-K (few tiles): the CS CTAs sharing a tile form a cluster; each
-//     parks its partial in shared memory and reduces 1/CS of the tile's columns
-//     over distributed shared memory, in rank order.
+//     parks its partial in shared memory and each rank sums 1/CS of the tile's
+//     columns over all ranks, in rank order: through distributed-shared-memory
+//     loads, or, for large column shares, after the copy engine has moved every
+//     rank's share into that rank's shared memory (all loads then local).
 //   Both reductions are deterministic.
 //
 // fp32: a SIMT kernel with the same epilogues (the fp32 reference-numerics
@@ -52,6 +54,8 @@ struct TcArgs {
     EpiParams epi;
     unsigned long long* stamps;  // optional per-CTA phase timestamps (test hook), else null
     Trace tr;
+    int push;                    // cluster split-K: exchange column shares by copy engine (else DSMEM loads)
+    int rope_stage;              // push, QKV: copy the RoPE table rows of a rank's columns into shared memory
 };
 
 // Phase timestamps of one CTA (ns, %globaltimer), recorded only when a.stamps != null.
@@ -126,17 +130,30 @@ __device__ __forceinline__ void epi_bar_sync() {  // named barrier over the 4 ep
     asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-// Cluster reduction of columns [c0, c1) of tile (tm, tn): sums the CS partials
-// parked in the cluster's shared memory in rank order.  QN items per thread and
-// round keep QN*CS distributed-shared-memory loads in flight.
-template <int KIND, int CS>
-__device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams& ep, uint32_t red_addr, int tm, int tn,
-                                               int c0, int c1, bool ok) {
-    constexpr int QN = CS >= 16 ? 1 : 16 / CS;
+// Cluster reduction of columns [c0, c1) of tile (tm, tn) by rank `rank`: sums
+// the CS partials ([BN][128] fp32, parked at red_addr in each CTA) in rank
+// order.  !LOCAL: loads them from the ranks' shared memory (distributed shared
+// memory).  LOCAL: the other ranks' copies of these columns sit in this CTA's
+// receive slots at recv_addr (slot s or s - 1 for rank s, slot_cols columns
+// each).  QN items per thread and round keep QN*CS loads in flight; with every
+// operand local (the QKV RoPE rows of tokens c0.. staged at rope_addr) short
+// rounds do, and their small unrolled body runs from a warm instruction cache
+// after the first round.
+template <int KIND, int CS, bool LOCAL>
+__device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams& ep, uint32_t red_addr,
+                                               uint32_t recv_addr, uint32_t rope_addr, int rank, int slot_cols, int tm,
+                                               int tn, int c0, int c1, bool ok) {
+    constexpr int QN = (LOCAL && KIND == EPI_QKV) ? 2 : (CS >= 16 ? 1 : 16 / CS);
     const int nitems = (c1 - c0) * 32;  // (column, 4-row group) items
-    uint32_t rb[CS];
+    uint32_t rb[CS];  // address of column c0 of rank s's partial (shared::cta if LOCAL, else shared::cluster)
 #pragma unroll
-    for (int s = 0; s < CS; ++s) rb[s] = mapa_shared(red_addr, (uint32_t)s);
+    for (int s = 0; s < CS; ++s) {
+        if (LOCAL)
+            rb[s] = s == rank ? red_addr + (uint32_t)c0 * (TC_BM * 4)
+                              : recv_addr + (uint32_t)((s < rank ? s : s - 1) * slot_cols) * (TC_BM * 4);
+        else
+            rb[s] = mapa_shared(red_addr + (uint32_t)c0 * (TC_BM * 4), (uint32_t)s);
+    }
     for (int base = threadIdx.x; base < nitems; base += TC_THREADS * QN) {
         float4 tv[QN][CS];
         float4 hv[(KIND == EPI_RESID || KIND == EPI_QKV) ? QN : 1];
@@ -158,7 +175,9 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams&
                 hv[q] = make_float4(1.f, 0.f, 1.f, 0.f);
                 if (ok && it < nitems && j < ep.m_tok && n < ep.q_dim + ep.kv_dim) {
                     const int ci = rope_dim(ep, n) >> 1;
-                    if (ep.rope_tab) {
+                    if (rope_addr) {
+                        hv[q] = lds_v4(rope_addr + (uint32_t)(((it / 32) * (ep.head_dim >> 1) + ci) * 8));
+                    } else if (ep.rope_tab) {
                         hv[q] = *reinterpret_cast<const float4*>(ep.rope_tab + (size_t)j * (ep.head_dim >> 1) + ci);
                     } else {
                         const float2 r0 = rope_pair(ep, ci, j), r1 = rope_pair(ep, ci + 1, j);
@@ -171,9 +190,9 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams&
         for (int q = 0; q < QN; ++q) {
             const int it = base + q * TC_THREADS;
             if (it < nitems) {
-                const uint32_t off = (uint32_t)(((c0 + it / 32) * TC_BM + (it % 32) * 4) * 4);
+                const uint32_t off = (uint32_t)(((it / 32) * TC_BM + (it % 32) * 4) * 4);
 #pragma unroll
-                for (int s = 0; s < CS; ++s) tv[q][s] = ld_shared_cluster_v4(rb[s] + off);
+                for (int s = 0; s < CS; ++s) tv[q][s] = LOCAL ? lds_v4(rb[s] + off) : ld_shared_cluster_v4(rb[s] + off);
             }
         }
 #pragma unroll
@@ -212,7 +231,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* empty = full + S;
     uint64_t* acc_full = empty + S;      // [2]
     uint64_t* acc_empty = acc_full + 2;  // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* recv_bar = acc_empty + 2;  // cluster split-K: the other ranks' column copies have landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
     // [0] abort, [1] last arriver of a cut tile, [2..3] epilogue's broadcast of [0] by segment parity
     volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -236,6 +256,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(smem_u32(&acc_full[s]), 1);
             mbar_init(smem_u32(&acc_empty[s]), 128);
         }
+        mbar_init(smem_u32(recv_bar), 1);
         flags[0] = flags[1] = flags[2] = flags[3] = 0;
         mbar_fence_init();
     }
@@ -381,6 +402,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) red[(cc + i) * TC_BM + row] = __uint_as_float(r[i]);
                 }
+                fence_proxy_async_smem();  // the copy engine reads the parked partial
             } else if (kb_b == 0 && kb_e == KB) {
                 // whole tile in this segment: straight from TMEM, one row per lane
                 for (int cc = 0; cc < BN; cc += 16) {
@@ -411,17 +433,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (flags[1]) {
                     // Sum the nseg partials in k order (deterministic).  Thread et owns rows
                     // 4*(et&31)..+3 of columns (et>>5) + 4i, i < 8: float4 loads, 8 columns x
-                    // up to 4 segments in flight per round, one vector store per quad.
+                    // up to FIX segments in flight per round, one vector store per quad.
+                    constexpr int FIX = 4;
                     __threadfence();
                     const int r4 = (et & 31) * 4, cq = et >> 5;
                     for (int cc = 0; cc < BN; cc += 32) {
                         float4 acc[8];
 #pragma unroll
                         for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        for (int sg0 = 0; sg0 < nseg; sg0 += 4) {
-                            float4 tv[4][8];
+                        for (int sg0 = 0; sg0 < nseg; sg0 += FIX) {
+                            float4 tv[FIX][8];
 #pragma unroll
-                            for (int s4 = 0; s4 < 4; ++s4) {
+                            for (int s4 = 0; s4 < FIX; ++s4) {
                                 if (sg0 + s4 < nseg) {
                                     const float* src =
                                         a.ws + (size_t)partial_slot(a, c_lo + sg0 + s4, t) * TC_BM * BN + r4;
@@ -434,7 +457,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                 }
                             }
 #pragma unroll
-                            for (int s4 = 0; s4 < 4; ++s4) {
+                            for (int s4 = 0; s4 < FIX; ++s4) {
                                 if (sg0 + s4 < nseg) {
 #pragma unroll
                                     for (int i = 0; i < 8; ++i) {
@@ -464,29 +487,66 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     if (CS > 0) {
         // ---------------- cluster reduction ----------------
-        // Every CTA of the cluster holds its partial of tile t in shared memory after
-        // the barrier.  Rank r sums columns [r*BN/CS, (r+1)*BN/CS) over all ranks in
-        // rank order through distributed shared memory and runs their epilogue.
-        cluster_sync_any();
-        if (threadIdx.x == 64) stamp(a, ST_CLUSTER);
-        const uint32_t rank = cluster_ctarank();
+        // Rank r owns columns [r*BN/CS, (r+1)*BN/CS) of tile t.  After the barrier every
+        // CTA's partial is parked and every ring idle.  a.push: each CTA's copy engine
+        // sends each other rank its partial's share of that rank's columns (receive
+        // slots past the parked partial).  Each rank then sums its columns in rank
+        // order and runs their epilogue.
+        const int rank = (int)cluster_ctarank();
         const int t = c / CS;
         const int tm = t % a.tiles_m, tn = t / a.tiles_m;
-        const int c0 = (int)(rank * (uint32_t)BN / (uint32_t)CS);
-        const int c1 = (int)((rank + 1) * (uint32_t)BN / (uint32_t)CS);
+        const int c0 = rank * BN / CS, c1 = (rank + 1) * BN / CS;
+        const int slot_cols = (BN + CS - 1) / CS;
         const uint32_t red_addr = smem_u32(smem);
-        const bool ok = flags[0] == 0;
-        switch (CS) {
-            case 1: cluster_reduce<KIND, 1>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
-            case 2: cluster_reduce<KIND, 2>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
-            case 3: cluster_reduce<KIND, 3>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
-            case 4: cluster_reduce<KIND, 4>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
-            case 5: cluster_reduce<KIND, 5>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
-            case 6: cluster_reduce<KIND, 6>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
-            case 7: cluster_reduce<KIND, 7>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
-            default: cluster_reduce<KIND, 8>(a, ep, red_addr, tm, tn, c0, c1, ok); break;
+        const uint32_t recv_addr = red_addr + (uint32_t)BN * (TC_BM * 4);
+        const uint32_t rbar = smem_u32(recv_bar);
+        // QKV rows that take RoPE: this rank's tokens' rows of the RoPE table, copied
+        // in past the receive slots
+        const bool push = a.push != 0;
+        const int rrows = min(c1, a.epi.m_tok - tn * BN) - c0;
+        const bool stage_rope =
+            KIND == EPI_QKV && push && a.rope_stage && rrows > 0 && tm * TC_BM < ep.q_dim + ep.kv_dim;
+        const uint32_t rope_addr = stage_rope ? recv_addr + (uint32_t)((CS - 1) * slot_cols) * (TC_BM * 4) : 0u;
+        const uint32_t rope_bytes = stage_rope ? (uint32_t)(rrows * ep.head_dim * 4) : 0u;
+        if (push && threadIdx.x == 0)
+            mbar_arrive_expect_tx(rbar, (uint32_t)((CS - 1) * (c1 - c0) * TC_BM * 4) + rope_bytes);
+        // After the barrier every ring of the cluster is idle: the epilogue warps parked
+        // each partial only after the tile's last MMA (the ring's last reader) completed.
+        cluster_sync_any();
+        if (threadIdx.x == 64) stamp(a, ST_CLUSTER);
+        if (push && threadIdx.x == 0) {
+            if (stage_rope)
+                bulk_load(rope_addr, ep.rope_tab + (size_t)(tn * BN + c0) * (ep.head_dim >> 1), rope_bytes, rbar);
+            // sent even after an abort, so that no peer waits for bytes that never come
+            for (int r = 0; r < CS; ++r) {
+                if (r == rank) continue;
+                const int r0 = r * BN / CS, r1 = (r + 1) * BN / CS;
+                const int slot = rank < r ? rank : rank - 1;
+                bulk_copy_to_peer(mapa_shared(recv_addr + (uint32_t)(slot * slot_cols) * (TC_BM * 4), (uint32_t)r),
+                                  red_addr + (uint32_t)r0 * (TC_BM * 4), (uint32_t)((r1 - r0) * TC_BM * 4),
+                                  mapa_shared(rbar, (uint32_t)r));
+            }
         }
-        cluster_sync_any();  // no CTA releases shared memory a peer still reads
+        bool ok = flags[0] == 0;
+        if (push && !mbar_wait_bounded(rbar, 0u)) {
+            raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
+            ok = false;
+        }
+#define YK_CLUSTER_REDUCE(N)                                                                                        \
+    (push ? cluster_reduce<KIND, N, true>(a, ep, red_addr, recv_addr, rope_addr, rank, slot_cols, tm, tn, c0, c1, ok) \
+          : cluster_reduce<KIND, N, false>(a, ep, red_addr, recv_addr, rope_addr, rank, slot_cols, tm, tn, c0, c1, ok))
+        switch (CS) {
+            case 1: YK_CLUSTER_REDUCE(1); break;
+            case 2: YK_CLUSTER_REDUCE(2); break;
+            case 3: YK_CLUSTER_REDUCE(3); break;
+            case 4: YK_CLUSTER_REDUCE(4); break;
+            case 5: YK_CLUSTER_REDUCE(5); break;
+            case 6: YK_CLUSTER_REDUCE(6); break;
+            case 7: YK_CLUSTER_REDUCE(7); break;
+            default: YK_CLUSTER_REDUCE(8); break;
+        }
+#undef YK_CLUSTER_REDUCE
+        cluster_sync_any();  // no peer still reads (or copies out of) this CTA's shared memory
         if (threadIdx.x == 64) stamp(a, ST_EPI_DONE);
     }
 
@@ -674,12 +734,25 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     // Few tiles (fewer than half the SMs): cluster split-K with the largest cluster
     // size whose clusters all run at once.  Otherwise stream-K with at least ~8
     // k-blocks per CTA so each pipeline fills before its epilogue.
+    const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
+    const int stages = std::max(2, std::min(8, (int)(TC_SMEM_BUDGET / stage_bytes)));
+    // cluster split-K reuses the idle ring: the parked partial, plus with the
+    // copy-engine exchange CS-1 receive slots (plus, QKV, the RoPE rows of a rank's tokens)
+    const bool want_rope = ep.kind == EPI_QKV && ep.rope_tab != nullptr;
+    const size_t ring = (size_t)stages * stage_bytes;
+    const auto ring_need = [&](int s, bool push, bool rope) {
+        const size_t slot = (size_t)((BN + s - 1) / s);
+        return (size_t)(BN + (push ? (s - 1) * slot : 0)) * TC_BM * 4 + (rope ? slot * ep.head_dim * 4 : 0);
+    };
+    const auto cluster_fits = [&](int s) { return ring_need(s, false, false) <= ring; };
     int cs = 0;
     if (force_grid < 0) {
-        cs = std::min(-force_grid, std::min(8, kb));
+        for (int s = std::min(-force_grid, std::min(8, kb)); s >= 2 && cs == 0; --s)
+            if (cluster_fits(s)) cs = s;
+        YK_ARG(cs > 0, "no cluster size fits the shared-memory ring");
     } else if (force_grid == 0 && tiles * 2 < e->num_sms) {
         for (int s = (int)std::min<long long>(std::min(8, kb), e->num_sms / tiles); s >= 2 && cs == 0; --s)
-            if (tiles <= cluster_capacity(e, s)) cs = s;
+            if (tiles <= cluster_capacity(e, s) && cluster_fits(s)) cs = s;
     }
     // Otherwise: persistent CTAs (at least ~8 k-blocks each so each pipeline fills)
     // take whole tiles round-robin; the tiles left over after the full waves are
@@ -709,8 +782,6 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
         YK_CHECK_CUDA(cudaMemset(m->gemm_counters, 0, (size_t)tiles * 2 * 4));
         m->gemm_counter_cap = (int)(tiles * 2);
     }
-    const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
-    const int stages = std::max(2, std::min(8, (int)(TC_SMEM_BUDGET / stage_bytes)));
     const size_t smem = (size_t)stages * stage_bytes + TC_SMEM_TAIL;
     uint32_t cols = 32;
     while ((int)cols < BN) cols <<= 1;
@@ -723,30 +794,52 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     a.BN = BN; a.stages = stages;
     a.tiles = (int)tiles; a.grid = grid; a.cluster_s = cs;
     a.sk_tiles = sk_tiles; a.sk_ctas = sk_ctas;
+    // large column shares: the copy engine moves them (distributed-shared-memory
+    // loads of a large share need many loads in flight, a long unrolled epilogue body)
+    a.push = cs > 0 && !(e->gemm_variant & 8) && (size_t)(BN / cs) * TC_BM * 4 >= (size_t)e->gemm_push_min &&
+                     ring_need(cs, true, false) <= ring
+                 ? 1
+                 : 0;
+    a.rope_stage = a.push && want_rope && ring_need(cs, true, true) <= ring ? 1 : 0;
     a.idesc = idesc_bf16_f32(TC_BM, BN);
     a.tmem_cols = cols;
     a.ws = m->gemm_ws;
     a.counters = m->gemm_counters;
     a.epi = ep;
-    a.stamps = m->gemm_stamps;
     // trace kind: GEMM | epilogue << 4 | 128-row tiles << 8 | tokens / 16 << 24
-    a.tr = trace_next(e, TK_GEMM | ((uint32_t)ep.kind << 4) | ((uint32_t)tiles_m << 8) |
-                             ((uint32_t)((m_tok + 15) / 16) << 24));
+    const uint32_t tkind = TK_GEMM | ((uint32_t)ep.kind << 4) | ((uint32_t)tiles_m << 8) |
+                           ((uint32_t)((m_tok + 15) / 16) << 24);
+    a.stamps = m->gemm_stamps;
+    if (m->gemm_stamp_kind != 0) {  // test hook: stamps of the launches of one kind only
+        if (m->gemm_stamp_kind == tkind && grid <= m->gemm_stamp_cap) m->gemm_stamp_grid = grid;
+        else a.stamps = nullptr;
+    }
+    a.tr = trace_next(e, tkind);
     m->gemm_last_grid = grid;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = e->stream;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = cs > 0 ? cs : 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[3];
+    int na = 0;
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = cs > 0 ? cs : 1;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+    if (cs > 0 && (e->gemm_variant & 4)) {  // (tuning knob) spread a cluster's CTAs over SMs
+        at[na].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+        at[na].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicySpread;
+        ++na;
+    }
+    if (e->pdl && !e->profiling) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
     cfg.attrs = at;
-    cfg.numAttrs = (e->pdl && !e->profiling) ? 2 : 1;
+    cfg.numAttrs = na;
     switch (ep.kind) {
         case EPI_QKV: YK_TRY(launch_tc<EPI_QKV>(cfg, tmW, tmX, a)); break;
         case EPI_RESID: YK_TRY(launch_tc<EPI_RESID>(cfg, tmW, tmX, a)); break;
@@ -997,4 +1090,34 @@ extern "C" yk_status ykt_gemm_bf16_epi_timed(yk_engine* e, const uint16_t* W, co
     m.gemm_counters = nullptr;
     m.gemm_stamps = nullptr;
     return s;
+}
+
+extern "C" yk_status ykt_gemm_stamps_enable(yk_model* m, uint32_t kind) {
+    YK_ARG(m, "arguments");
+    YK_CHECK_CUDA(cudaSetDevice(m->e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(m->e->stream));
+    if (m->gemm_stamps) cudaFree(m->gemm_stamps);
+    m->gemm_stamps = nullptr;
+    m->gemm_stamp_kind = 0;
+    m->gemm_stamp_cap = 0;
+    m->gemm_stamp_grid = 0;
+    if (kind != 0) {
+        const int cap = 2 * m->e->num_sms;
+        YK_CHECK_CUDA(cudaMalloc(&m->gemm_stamps, (size_t)cap * 8 * 8));
+        YK_CHECK_CUDA(cudaMemset(m->gemm_stamps, 0, (size_t)cap * 8 * 8));
+        m->gemm_stamp_kind = kind;
+        m->gemm_stamp_cap = cap;
+    }
+    return YK_OK;
+}
+
+extern "C" yk_status ykt_gemm_stamps_read(yk_model* m, uint64_t* host, int32_t cap, int32_t* n_ctas) {
+    YK_ARG(m && host && n_ctas, "arguments");
+    YK_ARG(m->gemm_stamps && m->gemm_stamp_kind, "GEMM stamps are not enabled");
+    YK_CHECK_CUDA(cudaSetDevice(m->e->device));
+    YK_CHECK_CUDA(cudaStreamSynchronize(m->e->stream));
+    const int n = std::min(cap, m->gemm_stamp_grid);
+    YK_CHECK_CUDA(cudaMemcpy(host, m->gemm_stamps, (size_t)n * 8 * 8, cudaMemcpyDeviceToHost));
+    *n_ctas = n;
+    return YK_OK;
 }

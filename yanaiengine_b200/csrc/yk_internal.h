@@ -62,7 +62,11 @@ struct yk_engine {
     PFN_tmapEncodeTiled encode_tiled = nullptr;
     bool pdl = true;                     // programmatic dependent launch (env YK_PDL=0 turns it off)
     int gemm_variant = 0;                // GEMM schedule tuning knob (env YK_GEMM_VARIANT): bit 0 = pure
-                                         // stream-K instead of whole tiles + stream-K remainder
+                                         // stream-K instead of whole tiles + stream-K remainder; bit 2 =
+                                         // cluster scheduling policy "spread"; bit 3 = cluster split-K
+                                         // reduction always by distributed-shared-memory loads
+    int gemm_push_min = 32768;           // cluster split-K: column shares of at least this many bytes are
+                                         // exchanged by copy engine (env YK_GEMM_PUSH_MIN)
     int attn_waves = 1;                  // attention items per resident CTA slot (env YK_ATTN_WAVES)
     bool attn_balanced = false;          // attention pieces <= average slot load (env YK_ATTN_PLAN=1)
     bool profiling = false;
@@ -140,6 +144,8 @@ struct yk_model {
     // GEMM phase timestamps (test hook only; null otherwise) and the last grid used
     unsigned long long* gemm_stamps = nullptr;
     int gemm_last_grid = 0;
+    uint32_t gemm_stamp_kind = 0;  // test hook: only launches of this trace kind write gemm_stamps
+    int gemm_stamp_cap = 0, gemm_stamp_grid = 0;
     // attention split-KV partials and per combine group arrival counters
     float* attn_ws = nullptr;
     size_t attn_ws_floats = 0;
