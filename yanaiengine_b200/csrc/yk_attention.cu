@@ -196,8 +196,11 @@ struct AttnCfg {
     // A consumer warp takes chunks of CP pages.  Stages: a multiple of 4*CP (4 =
     // every warps-per-m-tile value), so a consumer that waits only on its own
     // chunks never waits two phases ahead of a stage.
+    // Ring depth: with one query m-tile (decode-like, head_dim 64) each of the 4
+    // consumer warps owns every 4th chunk, so 16 pages keep two of its chunks in
+    // flight (a warp's chunk time is mostly page latency).
     static constexpr int CP = DH == 256 ? 1 : 2;
-    static constexpr int S = DH == 256 ? 4 : 8;
+    static constexpr int S = DH == 256 ? 4 : (DH == 64 ? 16 : 8);
     static constexpr int CTAS_PER_SM = DH == 64 ? 3 : (DH == 128 ? 2 : 1);  // register-limited
     static constexpr int LDQ = DH + 8;                       // padded Q row (elements)
     static constexpr size_t Q_BYTES = (size_t)AT_ROWS * LDQ * 2;
