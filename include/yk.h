@@ -170,6 +170,15 @@ yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens,
                           const uint32_t* q_starts, const uint32_t* context_lens, int32_t B,
                           const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
                           int32_t* n_rows);
+/* yk_forward_step whose last nd input tokens of every sequence are the draft
+ * tokens j0..j0+nd-1 that yk_draft_sample kept on the device for this batch
+ * (tokens[] holds placeholders there).  The speculative loop's draft inputs
+ * (S/Scheduler.swift:180-188) and the verify batch's drafts (:196-201) without
+ * a device-to-host round trip: the host can queue the whole draft phase. */
+yk_status yk_forward_step_drafts(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
+                                 const uint32_t* q_starts, const uint32_t* context_lens, int32_t B,
+                                 const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
+                                 yk_sampler* s, int32_t j0, int32_t nd, int32_t* n_rows);
 /* Copies logits rows [row0, row0+rows) of the last forward step to host (tests). */
 yk_status yk_logits_copy_to_host(yk_model* m, int32_t row0, int32_t rows, float* host);
 
@@ -183,12 +192,15 @@ yk_status yk_sampler_create(yk_engine* e, int32_t max_seqs, int32_t k, int32_t v
 void      yk_sampler_destroy(yk_sampler* s);
 /* Draft iteration j: p = softmax(draft logits row b / T) kept on the device for
  * verification, token = sampleFromProbs(p) (S/SpeculativeSampler.swift:63-91).
- * Reads rows 0..B-1 of `draft`'s logits (forward with last_n = 1). */
+ * Reads rows 0..B-1 of `draft`'s logits (forward with last_n = 1).  The tokens
+ * are also kept on the device (draft column j of the batch); out_tokens NULL:
+ * returns without waiting for the device (errors surface at verification). */
 yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, int32_t j, float temperature,
                           uint64_t seed, uint32_t step, const uint32_t* seq_ids, uint32_t* out_tokens);
 /* verifySequence (S/SpeculativeSampler.swift:95-129) for B sequences against
  * `target`'s logits rows b*(k+1)+i (forward with last_n = k+1) and the draft
- * probabilities kept by yk_draft_sample.  out_tokens[B x (k+1)], out_counts[B]. */
+ * probabilities kept by yk_draft_sample.  out_tokens[B x (k+1)], out_counts[B].
+ * draft_tokens NULL: the drafts yk_draft_sample kept on the device. */
 yk_status yk_spec_verify(yk_sampler* s, yk_model* target, int32_t B, float temperature, uint64_t seed,
                          uint32_t step, const uint32_t* seq_ids, const uint32_t* draft_tokens,
                          uint32_t* out_tokens, int32_t* out_counts);

@@ -86,6 +86,8 @@ _PROTOS = {
     "yk_kv_pool_read_page": (C.c_int32, [_P, C.c_int32, C.c_int32, C.c_int32, _F32P]),
     "yk_forward_step": (C.c_int32, [_P, _P, _U32P, C.c_int32, _U32P, _U32P, C.c_int32, _I32P, C.c_int32,
                                     C.c_int32, _I32P]),
+    "yk_forward_step_drafts": (C.c_int32, [_P, _P, _U32P, C.c_int32, _U32P, _U32P, C.c_int32, _I32P, C.c_int32,
+                                    C.c_int32, _P, C.c_int32, C.c_int32, _I32P]),
     "yk_logits_copy_to_host": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P]),
     "yk_sampler_create": (C.c_int32, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_P)]),
     "yk_sampler_destroy": (None, [_P]),

@@ -35,6 +35,32 @@ yk_status yk_engine::ensure_pinned(size_t bytes) {
     return YK_OK;
 }
 
+yk_status yk_engine::up_acquire(size_t bytes, int* slot, uint8_t** host) {
+    const int i = up_next;
+    up_next = (up_next + 1) % UP_SLOTS;
+    UpSlot& u = up[i];
+    if (!u.done) YK_CHECK_CUDA(cudaEventCreateWithFlags(&u.done, cudaEventDisableTiming));
+    YK_CHECK_CUDA(cudaEventSynchronize(u.done));  // this slot's previous copy has been read
+    if (bytes > u.bytes) {
+        if (u.host) cudaFreeHost(u.host);
+        u.host = nullptr;
+        u.bytes = 0;
+        const size_t want = std::max(bytes * 2, (size_t)1 << 20);
+        YK_CHECK_CUDA(cudaMallocHost((void**)&u.host, want));
+        u.bytes = want;
+    }
+    *slot = i;
+    *host = u.host;
+    return YK_OK;
+}
+
+yk_status yk_engine::up_submit(int slot, void* dst, size_t bytes) {
+    UpSlot& u = up[slot];
+    YK_CHECK_CUDA(cudaMemcpyAsync(dst, u.host, bytes, cudaMemcpyHostToDevice, stream));
+    YK_CHECK_CUDA(cudaEventRecord(u.done, stream));
+    return YK_OK;
+}
+
 // ---------------------------------------------------------------------------
 // engine
 // ---------------------------------------------------------------------------
@@ -83,6 +109,10 @@ extern "C" void yk_engine_destroy(yk_engine* e) {
     cudaSetDevice(e->device);
     cudaStreamSynchronize(e->stream);
     if (e->pinned) cudaFreeHost(e->pinned);
+    for (auto& u : e->up) {
+        if (u.host) cudaFreeHost(u.host);
+        if (u.done) cudaEventDestroy(u.done);
+    }
     if (e->d_err) cudaFree(e->d_err);
     if (e->trace_rec) cudaFree(e->trace_rec);
     yk::tp_destroy(e);
@@ -515,10 +545,11 @@ extern "C" yk_status yk_kv_pool_read_page(yk_kv_pool* p, int32_t block, int32_t 
 // ---------------------------------------------------------------------------
 // forward step
 // ---------------------------------------------------------------------------
-extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
-                                     const uint32_t* q_starts, const uint32_t* ctx, int32_t B,
-                                     const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
-                                     int32_t* n_rows) {
+// dt.d: the last dt.nd tokens of every sequence come from device-resident draft
+// tokens (tokens[] holds placeholders there); the host never waits for them.
+static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
+                              const uint32_t* q_starts, const uint32_t* ctx, int32_t B, const int32_t* block_tables,
+                              int32_t max_blocks, int32_t last_n, int32_t* n_rows, const yk::DraftTokens& dt) {
     YK_ARG(m && pool && tokens && q_starts && ctx && block_tables, "null argument");
     const auto& c = m->cfg;
     yk_engine* e = m->e;
@@ -543,7 +574,11 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         }
         R += last_n > 0 ? std::min<int>(last_n, (int)n) : (int)n;
     }
-    for (int t = 0; t < T; ++t) YK_ARG(tokens[t] < (uint32_t)c.vocab_size, "token id >= vocab_size");
+    for (int b = 0; b < B; ++b) {
+        YK_ARG(q_starts[b + 1] - q_starts[b] >= (uint32_t)dt.nd, "fewer new tokens than device draft tokens");
+        for (uint32_t t = q_starts[b]; t < q_starts[b + 1] - dt.nd; ++t)
+            YK_ARG(tokens[t] < (uint32_t)c.vocab_size, "token id >= vocab_size");
+    }
     YK_ARG(R > 0, "no logit rows");
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     // Attention work lists (bf16 tensor-core path): global and windowed layers.
@@ -579,8 +614,7 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
     }
     const size_t nattn = it_g.size() + cb_g.size() + it_w.size() + cb_w.size();
     const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R + nattn;
-    YK_TRY(e->ensure_pinned(nmeta * 4));
-    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));  // staging buffer is free again
+    // (a device buffer still read by earlier launches is freed only after cudaFree's implicit synchronisation)
     if (nmeta > m->meta_cap) {
         if (m->meta) cudaFree(m->meta);
         m->meta = nullptr;
@@ -588,7 +622,10 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
         YK_CHECK_CUDA(cudaMalloc(&m->meta, std::max<size_t>(nmeta * 2, 4096) * 4));
         m->meta_cap = std::max<size_t>(nmeta * 2, 4096);
     }
-    int32_t* hm = (int32_t*)e->pinned;
+    int up_slot = 0;
+    uint8_t* up_host = nullptr;
+    YK_TRY(e->up_acquire(nmeta * 4, &up_slot, &up_host));  // no wait for the device: a ring of staging slots
+    int32_t* hm = (int32_t*)up_host;
     int32_t* h_tok = hm;
     int32_t* h_pos = h_tok + T;
     int32_t* h_slot = h_pos + T;
@@ -623,7 +660,7 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
             w += v->size();
         }
     }
-    YK_CHECK_CUDA(cudaMemcpyAsync(m->meta, hm, nmeta * 4, cudaMemcpyHostToDevice, e->stream));
+    YK_TRY(e->up_submit(up_slot, m->meta, nmeta * 4));
     {
         const int32_t* a = m->meta + attn_off;
         m->cur.attn_items[0] = a;
@@ -666,7 +703,7 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
     EpiParams es;
     es.kind = EPI_STORE;
     es.out = m->tp_y;
-    YK_TRY(launch_embed(m, m->cur.tokens, m->cur.pos, T));
+    YK_TRY(launch_embed(m, m->cur.tokens, m->cur.pos, T, dt));
     for (int l = 0; l < c.n_layers; ++l) {
         LayerWeights& L = m->layers[l];
         YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr, pend));
@@ -728,6 +765,28 @@ extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32
     m->last_rows = R;
     if (n_rows) *n_rows = R;
     return YK_OK;
+}
+
+
+extern "C" yk_status yk_forward_step(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
+                                     const uint32_t* q_starts, const uint32_t* ctx, int32_t B,
+                                     const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
+                                     int32_t* n_rows) {
+    return forward_impl(m, pool, tokens, T, q_starts, ctx, B, block_tables, max_blocks, last_n, n_rows, {});
+}
+
+extern "C" yk_status yk_forward_step_drafts(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
+                                            const uint32_t* q_starts, const uint32_t* ctx, int32_t B,
+                                            const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
+                                            yk_sampler* s, int32_t j0, int32_t nd, int32_t* n_rows) {
+    YK_ARG(s && nd > 0, "sampler / nd");
+    yk::DraftTokens dt;
+    dt.d = yk::sampler_device_drafts(s, B, &dt.k);
+    YK_ARG(dt.d != nullptr, "batch larger than the sampler's");
+    YK_ARG(j0 >= 0 && j0 + nd <= dt.k, "draft token range outside 0..k-1");
+    dt.j0 = j0;
+    dt.nd = nd;
+    return forward_impl(m, pool, tokens, T, q_starts, ctx, B, block_tables, max_blocks, last_n, n_rows, dt);
 }
 
 extern "C" yk_status yk_logits_copy_to_host(yk_model* m, int32_t row0, int32_t rows, float* host) {

@@ -56,8 +56,19 @@ struct yk_engine {
     int num_sms = 148;
     cudaStream_t stream = nullptr;
     uint32_t* d_err = nullptr;           // device error word
-    uint8_t* pinned = nullptr;           // host staging (uploads / downloads)
+    uint8_t* pinned = nullptr;           // host staging (downloads, and uploads that synchronise anyway)
     size_t pinned_bytes = 0;
+    // Ring of pinned upload slots: a per-step upload (forward metadata, sampler
+    // sequence ids) fills the next slot while earlier work still runs; a slot is
+    // reused once the event recorded after its copy has fired.
+    static constexpr int UP_SLOTS = 4;
+    struct UpSlot {
+        uint8_t* host = nullptr;
+        size_t bytes = 0;
+        cudaEvent_t done = nullptr;
+    };
+    UpSlot up[UP_SLOTS];
+    int up_next = 0;
     uint64_t launches = 0;
     PFN_tmapEncodeTiled encode_tiled = nullptr;
     bool pdl = true;                     // programmatic dependent launch (env YK_PDL=0 turns it off)
@@ -78,6 +89,10 @@ struct yk_engine {
     std::vector<cudaEvent_t> prof_free;
     ProfTotals prof[4];
     yk_status ensure_pinned(size_t bytes);
+    // Next upload slot of at least `bytes` (waits for that slot's previous copy);
+    // up_submit copies it to `dst` on the engine stream.
+    yk_status up_acquire(size_t bytes, int* slot, uint8_t** host);
+    yk_status up_submit(int slot, void* dst, size_t bytes);
     void prof_begin(int cls, double bytes, double flops);
     void prof_end();
     void prof_resolve();
@@ -181,6 +196,7 @@ struct yk_sampler {
     uint32_t* io = nullptr;     // small device io area
     unsigned long long* stamps = nullptr;  // test hook: per-CTA phase stamps of draft sampling / verify
     int stamps_cap = 0;
+    std::vector<uint32_t> dev_seq;  // the sequence ids last uploaded to io[0..B) (re-uploaded only on change)
 };
 
 // ---- internal launchers ----------------------------------------------------
@@ -256,7 +272,16 @@ void plan_attention(const yk_model_config& c, int num_sms, int waves, bool balan
                     int* n_slots);
 size_t attention_ws_floats_per_slot(int head_dim);
 yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool);
-yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T);
+// The last nd input tokens of every sequence taken from device-resident draft
+// tokens d[b * k + j0 + i] (the sampler's), instead of the uploaded ids.
+struct DraftTokens {
+    const uint32_t* d = nullptr;
+    int k = 0, j0 = 0, nd = 0;
+};
+yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T, const DraftTokens& dt = {});
+// Device array [B x k] of the draft tokens yk_draft_sample kept on the device
+// for a batch of B sequences.
+const uint32_t* sampler_device_drafts(const yk_sampler* s, int B, int* k);
 yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx, const float* add = nullptr);
 yk_status tp_allreduce_f32(yk_engine* e, float* buf, size_t count);
 void tp_destroy(yk_engine* e);

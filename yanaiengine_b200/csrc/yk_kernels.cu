@@ -7,10 +7,12 @@ namespace yk {
 // embedding_lookup_kernel (S/gemm.metal:326-341): h[t] = E[tokens[t]], fp32 residual stream.
 // Also the step's RoPE table: rope[t][i] = (cos, sin)(pos[t] / denom[i]), the
 // angle of dimension pair i at token t that every layer's QKV epilogue uses.
+// dt.d: the last dt.nd tokens of each sequence are device-resident draft tokens.
 template <typename WT>
 __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict__ tokens, float* __restrict__ h,
                              int d, int V, const int32_t* __restrict__ pos, const float* __restrict__ denom,
-                             float2* __restrict__ rope, int half_dh, uint32_t* err, Trace tr) {
+                             float2* __restrict__ rope, int half_dh, uint32_t* err, Trace tr, DraftTokens dt,
+                             const int32_t* __restrict__ seq_of, const int32_t* __restrict__ q_starts) {
     if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
@@ -21,7 +23,11 @@ __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict
         sincosf(__fdiv_rn((float)pos[t], denom[i]), &sn, &cs);
         rope[(size_t)t * half_dh + i] = make_float2(cs, sn);
     }
-    const int tok = tokens[t];
+    int tok = tokens[t];
+    if (dt.d) {
+        const int b = seq_of[t], qe = q_starts[b + 1];
+        if (t >= qe - dt.nd) tok = (int)dt.d[(size_t)b * dt.k + dt.j0 + (t - (qe - dt.nd))];
+    }
     if (tok < 0 || tok >= V) {
         if (threadIdx.x == 0) raise_err(err, YK_DEV_ERR_BOUNDS);
         return;
@@ -124,16 +130,17 @@ __global__ void fill_kernel(T* __restrict__ out, size_t n, float v) {
 }
 
 // Host launchers -------------------------------------------------------------
-yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T) {
+yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T, const DraftTokens& dt) {
     const auto& c = m->cfg;
     if (c.dtype == YK_DTYPE_BF16)
         YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<__nv_bfloat16>, T, 256, 0, (const __nv_bfloat16*)m->embed, tokens,
                                  m->h, c.d_model, c.vocab_size, pos, (const float*)m->rope_denom, m->rope_tab,
-                                 c.head_dim / 2, m->e->d_err, trace_next(m->e, TK_EMBED)));
+                                 c.head_dim / 2, m->e->d_err, trace_next(m->e, TK_EMBED), dt, m->cur.seq,
+                                 m->cur.q_starts));
     else
         YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<float>, T, 256, 0, (const float*)m->embed, tokens, m->h, c.d_model,
                                  c.vocab_size, pos, (const float*)m->rope_denom, m->rope_tab, c.head_dim / 2,
-                                 m->e->d_err, trace_next(m->e, TK_EMBED)));
+                                 m->e->d_err, trace_next(m->e, TK_EMBED), dt, m->cur.seq, m->cur.q_starts));
     m->e->launches++;
     return YK_OK;
 }

@@ -204,6 +204,7 @@ struct DraftArgs {
     const uint32_t* seq_ids;
     float* probs;
     uint32_t* tokens_out;
+    uint32_t* tokens_keep = nullptr;  // also [b * k + j] of the device-resident draft matrix, if set
     float4* part = nullptr;  // [rows x SMP_CHUNKS] per-chunk (max, sum, best, argmax bits)
     unsigned long long* stamps = nullptr;  // test hook: 8 words per CTA
     Trace tr;
@@ -302,6 +303,7 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
     if (threadIdx.x == 0) {
         if (a.j_fixed >= 0) a.tokens_out[b] = tok;
         else a.tokens_out[(size_t)b * a.k + j] = tok;
+        if (a.tokens_keep) a.tokens_keep[(size_t)b * a.k + j] = tok;
         trace_mark(a.tr, TR_END);
         if (stp) {
             stp[3] = globaltimer_ns();
@@ -502,18 +504,31 @@ static yk_status finish_verify(yk_sampler* s, int B, const IoLayout& L, uint32_t
     return YK_OK;
 }
 
+// Sequence ids (and host draft tokens, if given) to the device, through the
+// engine's upload ring: the host does not wait for earlier work.
 static yk_status upload_small(yk_sampler* s, int B, const uint32_t* seq_ids, const uint32_t* drafts,
                               const IoLayout& L) {
     yk_engine* e = s->e;
+    // the ids of every draft step of a batch are the same: upload them once
+    if (!drafts && s->dev_seq.size() == (size_t)B && std::memcmp(s->dev_seq.data(), seq_ids, (size_t)B * 4) == 0)
+        return YK_OK;
+    s->dev_seq.assign(seq_ids, seq_ids + B);
     const size_t n = (size_t)B + (drafts ? (size_t)B * s->k : 0);
-    YK_TRY(e->ensure_pinned(std::max<size_t>(n * 4, (size_t)B * (s->k + 2) * 4 + 64)));
-    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
-    std::memcpy(e->pinned, seq_ids, (size_t)B * 4);
-    if (drafts) std::memcpy(e->pinned + (size_t)B * 4, drafts, (size_t)B * s->k * 4);
-    YK_CHECK_CUDA(cudaMemcpyAsync(L.seq, e->pinned, n * 4, cudaMemcpyHostToDevice, e->stream));
-    // The pinned buffer is reused for the results; order the reuse after this copy.
-    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
-    return YK_OK;
+    int slot = 0;
+    uint8_t* host = nullptr;
+    YK_TRY(e->up_acquire(n * 4, &slot, &host));
+    std::memcpy(host, seq_ids, (size_t)B * 4);
+    if (drafts) std::memcpy(host + (size_t)B * 4, drafts, (size_t)B * s->k * 4);
+    return e->up_submit(slot, L.seq, n * 4);
+}
+
+// The draft tokens yk_draft_sample keeps on the device: [B x k] (column j is
+// written by the sample of draft step j), valid for this B until the next
+// call with another batch size.
+const uint32_t* yk::sampler_device_drafts(const yk_sampler* s, int B, int* k) {
+    if (B <= 0 || B > s->max_seqs) return nullptr;
+    *k = s->k;
+    return io_layout(const_cast<yk_sampler*>(s), B).drafts;
 }
 
 // Draft sampling of `rows` rows: chunked statistics, chunked probabilities, token.
@@ -534,7 +549,7 @@ static yk_status launch_draft(yk_sampler* s, DraftArgs a, int rows) {
 
 extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, int32_t j, float temperature,
                                      uint64_t seed, uint32_t step, const uint32_t* seq_ids, uint32_t* out_tokens) {
-    YK_ARG(s && draft && seq_ids && out_tokens, "null argument");
+    YK_ARG(s && draft && seq_ids, "null argument");
     YK_ARG(B > 0 && B <= s->max_seqs && j >= 0 && j < s->k, "B / j");
     YK_ARG(draft->cfg.vocab_size == s->vocab, "vocab mismatch");
     YK_ARG(draft->last_rows >= B, "draft logits hold fewer rows than B (forward with last_n = 1)");
@@ -555,8 +570,12 @@ extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, 
     a.seq_ids = L.seq;
     a.probs = s->probs;
     a.tokens_out = L.out;
+    // the tokens also stay on the device as draft column j ([B x k]) for the next
+    // draft forward (yk_forward_step_drafts) and the verification
+    a.tokens_keep = L.drafts;
     a.part = s->part;
     YK_TRY(launch_draft(s, a, B));
+    if (!out_tokens) return YK_OK;  // asynchronous: device checks are reported by the verification
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, (size_t)B * 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + (size_t)B * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
@@ -614,11 +633,12 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
 extern "C" yk_status yk_spec_verify(yk_sampler* s, yk_model* target, int32_t B, float temperature, uint64_t seed,
                                     uint32_t step, const uint32_t* seq_ids, const uint32_t* draft_tokens,
                                     uint32_t* out_tokens, int32_t* out_counts) {
-    YK_ARG(s && target && seq_ids && draft_tokens && out_tokens && out_counts, "null argument");
+    YK_ARG(s && target && seq_ids && out_tokens && out_counts, "null argument");
     YK_ARG(B > 0 && B <= s->max_seqs, "B");
     YK_ARG(target->cfg.vocab_size == s->vocab, "vocab mismatch");
     YK_ARG(target->last_rows == B * (s->k + 1), "target logits must hold k+1 rows per sequence (last_n = k+1)");
-    for (int i = 0; i < B * s->k; ++i) YK_ARG(draft_tokens[i] < (uint32_t)s->vocab, "draft token >= vocab");
+    if (draft_tokens)  // else: the device-resident drafts of this batch's yk_draft_sample calls
+        for (int i = 0; i < B * s->k; ++i) YK_ARG(draft_tokens[i] < (uint32_t)s->vocab, "draft token >= vocab");
     yk_engine* e = s->e;
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     IoLayout L = io_layout(s, B);

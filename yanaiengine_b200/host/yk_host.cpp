@@ -177,8 +177,10 @@ extern "C" yk_status ykh_submit_cached(ykh_scheduler* s, const uint32_t* prompt,
 
 // Builds the ragged batch for one forward: for each sequence the token list
 // `inputs[b]`, starting at cache position `start[b]`; reserves pages.
+// nd > 0: the last nd inputs of every sequence are placeholders for the draft
+// tokens j0.. that the sampler keeps on the device (no host round trip).
 static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std::vector<uint32_t>>& inputs,
-                         int last_n) {
+                         int last_n, int j0 = 0, int nd = 0) {
     const int B = (int)s->running.size();
     s->tokens.clear();
     s->qstarts.assign(1, 0);
@@ -199,9 +201,13 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
         std::copy(c->page_table.begin(), c->page_table.end(), s->tables.begin() + (size_t)b * max_pages);
     }
     int32_t rows = 0;
-    yk_status st = yk_forward_step(is_draft ? s->draft : s->target, is_draft ? s->dpool : s->tpool, s->tokens.data(),
-                                   (int32_t)s->tokens.size(), s->qstarts.data(), s->ctx.data(), B, s->tables.data(),
-                                   (int32_t)max_pages, last_n, &rows);
+    yk_model* m = is_draft ? s->draft : s->target;
+    yk_kv_pool* pool = is_draft ? s->dpool : s->tpool;
+    yk_status st = nd > 0 ? yk_forward_step_drafts(m, pool, s->tokens.data(), (int32_t)s->tokens.size(),
+                                                   s->qstarts.data(), s->ctx.data(), B, s->tables.data(),
+                                                   (int32_t)max_pages, last_n, s->sampler, j0, nd, &rows)
+                          : yk_forward_step(m, pool, s->tokens.data(), (int32_t)s->tokens.size(), s->qstarts.data(),
+                                            s->ctx.data(), B, s->tables.data(), (int32_t)max_pages, last_n, &rows);
     if (st != YK_OK) return st;
     for (int b = 0; b < B; ++b) {
         PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
@@ -233,10 +239,11 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
         s->seq_ids[b] = s->running[b]->id;
         N[b] = s->running[b]->total();
     }
-    // 1. DRAFT PHASE (:171-190): k draft forwards, sampling after each.
-    s->drafts.assign((size_t)B * k, 0);
+    // 1. DRAFT PHASE (:171-190): k draft forwards, sampling after each.  The drafted
+    // tokens stay on the device (the sampler keeps them; the next draft forward and
+    // the target forward read them there), so the whole phase is queued without
+    // waiting for the device.
     std::vector<std::vector<uint32_t>> inputs(B);
-    std::vector<uint32_t> tok(B);
     for (int j = 0; j < k; ++j) {
         for (int b = 0; b < B; ++b) {
             SequenceRequest* r = s->running[b].get();
@@ -245,27 +252,27 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
                 // every token the draft cache has not seen (the prompt on the first step)
                 for (int i = r->draft_cache->current_position; i < N[b]; ++i) inputs[b].push_back(r->at(i));
             } else {
-                inputs[b].push_back(s->drafts[(size_t)b * k + j - 1]);
+                inputs[b].push_back(0u);  // draft j-1 of this sequence, on the device
             }
         }
-        YK_TRY(forward(s, true, inputs, 1));
+        if (j == 0) YK_TRY(forward(s, true, inputs, 1));
+        else YK_TRY(forward(s, true, inputs, 1, j - 1, 1));
         YK_TRY(yk_draft_sample(s->sampler, s->draft, B, j, s->temperature, s->seed, s->step_no, s->seq_ids.data(),
-                               tok.data()));
-        for (int b = 0; b < B; ++b) s->drafts[(size_t)b * k + j] = tok[b];
+                               nullptr));
     }
     // 2-3. VERIFICATION SETUP + TARGET FORWARD (:192-210): unseen tokens + drafts.
     for (int b = 0; b < B; ++b) {
         SequenceRequest* r = s->running[b].get();
         inputs[b].clear();
         for (int i = r->cache->current_position; i < N[b]; ++i) inputs[b].push_back(r->at(i));
-        for (int j = 0; j < k; ++j) inputs[b].push_back(s->drafts[(size_t)b * k + j]);
+        for (int j = 0; j < k; ++j) inputs[b].push_back(0u);  // the k drafts, on the device
     }
-    YK_TRY(forward(s, false, inputs, k + 1));
+    YK_TRY(forward(s, false, inputs, k + 1, 0, k));
     // 4. VERIFICATION & ROLLBACK (:212-267).
     s->out_tokens.assign((size_t)B * (k + 1), 0);
     s->counts.assign(B, 0);
     YK_TRY(yk_spec_verify(s->sampler, s->target, B, s->temperature, s->seed, s->step_no, s->seq_ids.data(),
-                          s->drafts.data(), s->out_tokens.data(), s->counts.data()));
+                          nullptr, s->out_tokens.data(), s->counts.data()));
     int emitted = 0;
     for (int b = 0; b < B; ++b) {
         SequenceRequest* r = s->running[b].get();
