@@ -113,8 +113,13 @@ __device__ __forceinline__ long long chain_block_min(ChainSmem& cs, long long v)
 // n-1 if there is none (:72).  !search: returns -1 and *sum = final c.
 // Must be called by all CHAIN_THREADS threads of the block; f is evaluated
 // once per index, cooperatively, into the shared-memory ring.
-template <class F>
-__device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, float r, float* sum) {
+struct ChainNoPrefetch {
+    __device__ void operator()(long long) const {}
+};
+// pf(i): optional prefetch into L2 of the sources of f(i .. i+31); each fill
+// requests the round after the one it loads, so that round's loads hit L2.
+template <class F, class P = ChainNoPrefetch>
+__device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, float r, float* sum, P pf = P()) {
     enum { ZERO = 0, NORMAL = 1, SEQ = 2 };
     float c = 0.f;
     int mode = ZERO;
@@ -145,6 +150,11 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         for (int u = 0; u < CHAIN_EPT; ++u) {
             const long long i = from + (long long)u * CHAIN_THREADS;
             if (i < want) slot(i) = v[u];
+        }
+        // the next round's terms: one 32-element line per thread
+        if (threadIdx.x < CHAIN_ROUND / 32) {
+            const long long i = want + 32LL * threadIdx.x;
+            if (i < n) pf(i);
         }
         hi = max(hi, want);
         __syncthreads();

@@ -247,6 +247,9 @@ __device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
                  : "memory");
     return v;
 }
+// Non-binding prefetch of the 128-byte line holding p into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // Bulk copy (copy engine) of `bytes` (a multiple of 16; both addresses 16-byte
 // aligned) from this CTA's shared memory into the shared memory of a CTA of
 // the cluster (dst and bar: shared::cluster addresses from mapa); completes

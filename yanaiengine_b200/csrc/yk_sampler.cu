@@ -298,7 +298,8 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
         tok = (uint32_t)merge_chunks(a.part + (size_t)blockIdx.x * SMP_CHUNKS).arg;
     } else {
         const float r = uniform_at(a.seed, a.step, a.seq_ids[b], (uint32_t)j, SLOT_DRAFT);
-        tok = (uint32_t)block_chain(cs, [&](int64_t i) { return p[i]; }, V, true, r, nullptr);
+        tok = (uint32_t)block_chain(cs, [&](int64_t i) { return p[i]; }, V, true, r, nullptr,
+                                    [&](long long i) { prefetch_l2(p + i); });
     }
     if (threadIdx.x == 0) {
         if (a.j_fixed >= 0) a.tokens_out[b] = tok;
@@ -400,15 +401,22 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
         const float* pr = a.p + ((size_t)b * k + rej) * V;
         float S = 0.f;
         auto diff = [&](int64_t x) { return swift_max0(__fsub_rn(qval(rej, x), pr[x])); };
-        block_chain(cs, diff, V, false, 0.f, &S);
+        auto pf_diff = [&](long long x) {
+            prefetch_l2(qrow(rej) + x);
+            prefetch_l2(pr + x);
+        };
+        block_chain(cs, diff, V, false, 0.f, &S, pf_diff);
         const float r = uniform_at(a.seed, a.step, seq, (uint32_t)rej, SLOT_RESAMPLE);
         if (S > 0.0f)
-            tok = (uint32_t)block_chain(cs, [&](int64_t x) { return __fdiv_rn(diff(x), S); }, V, true, r, nullptr);
+            tok = (uint32_t)block_chain(cs, [&](int64_t x) { return __fdiv_rn(diff(x), S); }, V, true, r, nullptr,
+                                        pf_diff);
         else
-            tok = (uint32_t)block_chain(cs, [&](int64_t x) { return qval(rej, x); }, V, true, r, nullptr);
+            tok = (uint32_t)block_chain(cs, [&](int64_t x) { return qval(rej, x); }, V, true, r, nullptr,
+                                        [&](long long x) { prefetch_l2(qrow(rej) + x); });
     } else {
         const float r = uniform_at(a.seed, a.step, seq, (uint32_t)k, SLOT_BONUS);
-        tok = (uint32_t)block_chain(cs, [&](int64_t x) { return qval(k, x); }, V, true, r, nullptr);
+        tok = (uint32_t)block_chain(cs, [&](int64_t x) { return qval(k, x); }, V, true, r, nullptr,
+                                    [&](long long x) { prefetch_l2(qrow(k) + x); });
     }
     if (threadIdx.x == 0) {
         uint32_t* o = a.out + (size_t)b * (k + 1);
