@@ -124,15 +124,24 @@ def test_rejects_bad_block_id(engine):
         m.close()
 
 
-@pytest.mark.parametrize("knob", [("YK_GEMM_PUSH_MIN", "0"), ("YK_GEMM_VARIANT", "8")])
-def test_bf16_cluster_reduction_modes(oracle, monkeypatch, knob):
-    """Every cluster split-K reduction by copy-engine exchange (with the QKV RoPE rows
-    staged in shared memory), then every one by distributed-shared-memory loads;
-    64 prefill tokens and head_dim 128 give 128-token tiles split over 2+ CTAs."""
-    monkeypatch.setenv(*knob)
-    e = abi.Engine(0)  # reads the knob at creation
+@pytest.mark.parametrize("knobs", [
+    {"YK_GEMM_PUSH_MIN": "0"},   # cluster split-K, copy-engine exchange (QKV RoPE rows staged)
+    {"YK_GEMM_VARIANT": "8"},    # cluster split-K, distributed-shared-memory loads
+    {"YK_GEMM_VARIANT": "32"},   # no clusters: whole tiles straight from the accumulator
+    {"YK_GEMM_VARIANT": "33"},   # no clusters, pure stream-K: cut tiles finished by the last arriver
+    {"YK_FUSE_NORM": "0"},       # RMSNorm as separate kernels
+])
+def test_bf16_gemm_paths_with_fused_norm(oracle, monkeypatch, knobs):
+    """The bf16 forward through every GEMM work split and reduction, each carrying
+    the RMSNorm folded into the residual epilogue (x = bf16(h * gain), 32-row sums
+    of squares) and the next GEMM (1/rms per token), and with the norm unfused."""
+    for k, v in knobs.items():
+        monkeypatch.setenv(k, v)
+    e = abi.Engine(0)  # reads the knobs at creation
     try:
-        cfg = dict(TINY, head_dim=128, n_heads=4, n_kv_heads=2)
+        # 6 query heads x 128: o_proj has K = 768 (12 k-blocks over 2 tiles), so pure
+        # stream-K cuts its tiles and the residual epilogue runs in the last arriver
+        cfg = dict(TINY, head_dim=128, n_heads=6, n_kv_heads=2)
         _drive(e, oracle, cfg, abi.DTYPE_BF16, True, 2e-2, steps=2)
     finally:
         e.close()

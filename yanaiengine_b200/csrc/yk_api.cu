@@ -96,6 +96,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     if (const char* v = std::getenv("YK_PDL")) e->pdl = std::strcmp(v, "0") != 0;
     if (const char* v = std::getenv("YK_GEMM_VARIANT")) e->gemm_variant = std::atoi(v);
     if (const char* v = std::getenv("YK_GEMM_PUSH_MIN")) e->gemm_push_min = std::max(0, std::atoi(v));
+    if (const char* v = std::getenv("YK_FUSE_NORM")) e->fuse_norm = std::atoi(v) != 0;
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
     yk_status s = e->ensure_pinned((size_t)4 << 20);
@@ -298,6 +299,7 @@ static yk_status create_model(yk_engine* e, const yk_model_config* cfg, int tp_r
     ALLOC(m->logits, T * V * 4);
     ALLOC(m->rope_denom, dh / 2 * 4);
     ALLOC(m->rope_tab, T * (dh / 2) * sizeof(float2));
+    ALLOC(m->norm_ss, ((d + 31) / 32) * T * 4);
     if (tp_world > 1) ALLOC(m->tp_y, T * d * 4);
     m->gemm_ws_floats = (size_t)2 * e->num_sms * 128 * 256;
     ALLOC(m->gemm_ws, m->gemm_ws_floats * 4);
@@ -703,10 +705,30 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
     EpiParams es;
     es.kind = EPI_STORE;
     es.out = m->tp_y;
-    YK_TRY(launch_embed(m, m->cur.tokens, m->cur.pos, T, dt));
+    // RMSNorm folded into the GEMMs (bf16, one GPU): the residual epilogue (and the
+    // embedding) writes x = bf16(h * gain) and 32-row sums of squares; the next
+    // GEMM scales each token's accumulator by its 1/rms.  The final norm stays a
+    // kernel (it gathers the logit rows).
+    const bool fused = c.dtype == YK_DTYPE_BF16 && !tp && !c.ref_compat && T <= 256 && d % 32 == 0 && e->fuse_norm;
+    auto norm_in = [&](EpiParams& p) {
+        if (!fused) return;
+        p.in_ss = m->norm_ss;
+        p.in_groups = d / 32;
+        p.ss_ld = T;
+        p.in_d = (float)d;
+        p.in_eps = c.rms_eps;
+    };
+    auto norm_out = [&](EpiParams& p, const float* g) {
+        if (!fused || !g) return;
+        p.nx_g = g;
+        p.nx_out = m->xn;
+        p.nx_ss = m->norm_ss;
+        p.ss_ld = T;
+    };
+    YK_TRY(launch_embed(m, m->cur.tokens, m->cur.pos, T, dt, fused ? m->layers[0].n1 : nullptr));
     for (int l = 0; l < c.n_layers; ++l) {
         LayerWeights& L = m->layers[l];
-        YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr, pend));
+        if (!fused) YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr, pend));
         pend = nullptr;
         EpiParams eq;
         eq.kind = EPI_QKV;
@@ -724,6 +746,7 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         eq.block_elems = (long long)pool->block_elems;
         eq.layer_off = (long long)l * (long long)pool->layer_elems;
         eq.pool_blocks = pool->num_blocks;
+        norm_in(eq);
         YK_TRY(gemm_run(m, L.wqkv, &L.tm_qkv, m->xn, qd + 2 * kvd, d, T, eq));
         const bool windowed = c.window > 0 && (c.window_layer_parity < 0 || (l % 2) == c.window_layer_parity);
         YK_TRY(attention_run(m, pool, l, T, B, max_blocks, (windowed ? kv_win : kv_full) * kv_tok_bytes));
@@ -737,22 +760,27 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
             YK_TRY(tp_allreduce_f32(e, m->tp_y, (size_t)T * d));
             pend = m->tp_y;
         } else {
-            YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, er));
+            EpiParams eo = er;
+            norm_out(eo, L.n2);
+            YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, eo));
         }
-        YK_TRY(launch_rmsnorm(m, L.n2, T, nullptr, pend));
+        if (!fused) YK_TRY(launch_rmsnorm(m, L.n2, T, nullptr, pend));
         pend = nullptr;
         EpiParams eg;
         eg.kind = EPI_GLU;
         eg.ref_compat = c.ref_compat;
         eg.out = m->act;
         eg.act = c.act;
+        norm_in(eg);
         YK_TRY(gemm_run(m, L.wgu, &L.tm_gu, m->xn, 2 * F, d, T, eg));
         if (tp) {
             YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, es));
             YK_TRY(tp_allreduce_f32(e, m->tp_y, (size_t)T * d));
             pend = m->tp_y;
         } else {
-            YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, er));
+            EpiParams ed = er;
+            norm_out(ed, l + 1 < c.n_layers ? m->layers[l + 1].n1 : nullptr);
+            YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, ed));
         }
     }
     YK_TRY(launch_rmsnorm(m, m->final_norm, R, m->cur.rows, pend));

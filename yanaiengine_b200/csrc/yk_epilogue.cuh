@@ -17,6 +17,12 @@
 
 namespace yk {
 
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 __device__ __forceinline__ float compat_relu(float v) {
     v = v + 0.1f;
     return v > 0.f ? v : 0.f;
@@ -165,8 +171,9 @@ __device__ __forceinline__ int rope_dim(const EpiParams& p, int n) {
 
 // Drains 16 consecutive tokens j0.. of row n: one row per lane, all 32 lanes of
 // the warp call it together.  Fully unrolled; the residual epilogue issues its
-// 16 loads of the fp32 stream before any store.
-template <int KIND, typename AT>
+// 16 loads of the fp32 stream before any store.  FN: the residual epilogue also
+// writes the fused norm's x and 32-row sums of squares.
+template <int KIND, typename AT, bool FN = false>
 __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const float (&v)[16]) {
     if constexpr (KIND == EPI_QKV) {
         // rows (n, n^1) form one RoPE pair: the even lane writes the pair for tokens
@@ -219,7 +226,7 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
                 if (j < p.m_tok) o[(size_t)j * (p.n_out >> 1)] = from_f32<AT>((p.act == 1 ? act_gelu_tanh(g) : act_silu(g)) * u);
             }
         }
-    } else if constexpr (KIND == EPI_RESID) {
+    } else if constexpr (KIND == EPI_RESID && !FN) {
         if (n >= p.n_out) return;
         float hv[16];
 #pragma unroll
@@ -228,6 +235,26 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
 #pragma unroll
         for (int i = 0; i < 16; ++i)
             if (j0 + i < p.m_tok) p.h[(size_t)(j0 + i) * p.ld + n] = hv[i] + (p.ref_compat ? compat_relu(v[i]) : v[i]);
+    } else if constexpr (KIND == EPI_RESID) {
+        // (every lane of the warp runs this: the fused norm's group sums shuffle)
+        const bool valid = n < p.n_out;
+        float hv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (valid && j0 + i < p.m_tok) hv[i] = p.h[(size_t)(j0 + i) * p.ld + n];
+        const float g = valid ? p.nx_g[n] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const bool ok = valid && j0 + i < p.m_tok;
+            const float hn = ok ? hv[i] + (p.ref_compat ? compat_relu(v[i]) : v[i]) : 0.f;
+            if (ok) {
+                p.h[(size_t)(j0 + i) * p.ld + n] = hn;
+                reinterpret_cast<__nv_bfloat16*>(p.nx_out)[(size_t)(j0 + i) * p.ld + n] = __float2bfloat16_rn(hn * g);
+            }
+            const float ss = warp_sum_f(hn * hn);  // this warp's 32 rows form one group
+            if ((threadIdx.x & 31) == 0 && j0 + i < p.m_tok && (n & ~31) < p.n_out)
+                p.nx_ss[(size_t)(n >> 5) * p.ss_ld + j0 + i] = ss;
+        }
     } else {  // EPI_STORE, EPI_LOGITS
         if (n >= p.n_out) return;
         float* o = reinterpret_cast<float*>(p.out);
@@ -243,10 +270,30 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
     }
 }
 
-// Residual add of rows n..n+3 of token j whose current values h were loaded by the caller.
-__device__ __forceinline__ void epi_quad_resid(const EpiParams& p, int n, int j, float4 v, float4 h) {
+// Residual add of rows n..n+3 of token j whose current values h were loaded by
+// the caller.  FN: also the next GEMM's input bf16(h_new * g) (gains g loaded by
+// the caller); returns the sum of squares of the four new values.
+template <bool FN = false>
+__device__ __forceinline__ float epi_quad_resid(const EpiParams& p, int n, int j, float4 v, float4 h,
+                                                float4 g = float4{}) {
     if (p.ref_compat) { v.x = compat_relu(v.x); v.y = compat_relu(v.y); v.z = compat_relu(v.z); v.w = compat_relu(v.w); }
-    *reinterpret_cast<float4*>(p.h + (size_t)j * p.ld + n) = make_float4(h.x + v.x, h.y + v.y, h.z + v.z, h.w + v.w);
+    const float4 hn = make_float4(h.x + v.x, h.y + v.y, h.z + v.z, h.w + v.w);
+    *reinterpret_cast<float4*>(p.h + (size_t)j * p.ld + n) = hn;
+    if constexpr (FN) {
+        store4(reinterpret_cast<__nv_bfloat16*>(p.nx_out) + (size_t)j * p.ld + n, hn.x * g.x, hn.y * g.y, hn.z * g.z,
+               hn.w * g.w);
+        return hn.x * hn.x + hn.y * hn.y + hn.z * hn.z + hn.w * hn.w;
+    }
+    return 0.f;
+}
+// Fused norm: lanes 8g..8g+7 hold 4 rows each of the 32-row group starting at
+// their first lane's row n; the group's sum of squares for token j goes to
+// nx_ss[(n / 32) * ss_ld + j].  Every lane of the warp calls it.
+__device__ __forceinline__ void ss_quad_groups(const EpiParams& p, int n, int j, float ss, bool write) {
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    if (write && (threadIdx.x & 7) == 0) p.nx_ss[(size_t)(n >> 5) * p.ss_ld + j] = ss;
 }
 
 // QKV rows n..n+3 (n % 4 == 0) of token j with the (cos, sin) of their two RoPE
@@ -269,10 +316,7 @@ template <int KIND, typename AT>
 __device__ __forceinline__ void epi_quad(const EpiParams& p, int n, int j, float4 v) {
     if (j >= p.m_tok || n >= p.n_out) return;
     if constexpr (KIND == EPI_RESID) {
-        if (p.ref_compat) { v.x = compat_relu(v.x); v.y = compat_relu(v.y); v.z = compat_relu(v.z); v.w = compat_relu(v.w); }
-        float4* o = reinterpret_cast<float4*>(p.h + (size_t)j * p.ld + n);
-        const float4 h = *o;
-        *o = make_float4(h.x + v.x, h.y + v.y, h.z + v.z, h.w + v.w);
+        (void)epi_quad_resid<false>(p, n, j, v, *reinterpret_cast<const float4*>(p.h + (size_t)j * p.ld + n));
     } else if constexpr (KIND == EPI_STORE || KIND == EPI_LOGITS) {
         if (KIND == EPI_LOGITS && (p.ref_compat || p.cap > 0.f)) {
             v.x = logit_out(p, v.x); v.y = logit_out(p, v.y); v.z = logit_out(p, v.z); v.w = logit_out(p, v.w);

@@ -38,7 +38,8 @@ constexpr int TC_BK = 64;        // k per stage: one 128-byte swizzle row of bf1
 constexpr int TC_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
 constexpr int TC_SMEM_BUDGET = 200 * 1024;
 constexpr int TC_QKV_STAGE_TOK = 256;  // tokens whose QKV epilogue metadata is staged in shared memory
-constexpr int TC_SMEM_TAIL = 1024 + 256 + (2 * TC_QKV_STAGE_TOK + 128) * 4;  // align slack, barriers, QKV staging
+// align slack, barriers, QKV staging, per-token 1/rms of the fused norm
+constexpr int TC_SMEM_TAIL = 1024 + 256 + (2 * TC_QKV_STAGE_TOK + 128) * 4 + TC_QKV_STAGE_TOK * 4;
 
 struct TcArgs {
     int n_out, K, m_tok;
@@ -139,11 +140,13 @@ __device__ __forceinline__ void epi_bar_sync() {  // named barrier over the 4 ep
 // operand local (the QKV RoPE rows of tokens c0.. staged at rope_addr) short
 // rounds do, and their small unrolled body runs from a warm instruction cache
 // after the first round.
-template <int KIND, int CS, bool LOCAL>
+template <int KIND, int CS, bool LOCAL, bool FN>
 __device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams& ep, uint32_t red_addr,
                                                uint32_t recv_addr, uint32_t rope_addr, int rank, int slot_cols, int tm,
-                                               int tn, int c0, int c1, bool ok) {
-    constexpr int QN = (LOCAL && KIND == EPI_QKV) ? 2 : (CS >= 16 ? 1 : 16 / CS);
+                                               int tn, int c0, int c1, bool ok, const float* inv) {
+    constexpr int QN = (LOCAL && KIND == EPI_QKV)     ? 2
+                       : (KIND == EPI_RESID && FN) ? (CS >= 8 ? 1 : 8 / CS)  // (register budget: gains in flight too)
+                                                   : (CS >= 16 ? 1 : 16 / CS);
     const int nitems = (c1 - c0) * 32;  // (column, 4-row group) items
     uint32_t rb[CS];  // address of column c0 of rank s's partial (shared::cta if LOCAL, else shared::cluster)
 #pragma unroll
@@ -157,14 +160,18 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams&
     for (int base = threadIdx.x; base < nitems; base += TC_THREADS * QN) {
         float4 tv[QN][CS];
         float4 hv[(KIND == EPI_RESID || KIND == EPI_QKV) ? QN : 1];
+        float4 gv[(KIND == EPI_RESID && FN) ? QN : 1];
         if constexpr (KIND == EPI_RESID) {
-            // the residual stream values, in flight together with the partials
+            // the residual stream values (and the fused norm's gains), in flight
+            // together with the partials
 #pragma unroll
             for (int q = 0; q < QN; ++q) {
                 const int it = base + q * TC_THREADS;
                 const int n = tm * TC_BM + (it % 32) * 4, j = tn * a.BN + c0 + it / 32;
-                if (ok && it < nitems && j < a.epi.m_tok && n < a.epi.n_out)
+                if (ok && it < nitems && j < a.epi.m_tok && n < a.epi.n_out) {
                     hv[q] = *reinterpret_cast<const float4*>(a.epi.h + (size_t)j * a.epi.ld + n);
+                    if constexpr (FN) gv[q] = *reinterpret_cast<const float4*>(a.epi.nx_g + n);
+                }
             }
         } else if constexpr (KIND == EPI_QKV) {
             // the RoPE (cos, sin) of the quad's two pairs, in flight with the partials
@@ -208,8 +215,17 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams&
                     acc.w += tv[q][s].w;
                 }
                 const int n = tm * TC_BM + (it % 32) * 4, j = tn * a.BN + c0 + it / 32;
-                if constexpr (KIND == EPI_RESID) {
-                    if (j < a.epi.m_tok && n < a.epi.n_out) epi_quad_resid(a.epi, n, j, acc, hv[q]);
+                if constexpr (FN && KIND != EPI_RESID) {  // this token's 1/rms (the input was bf16(h * g))
+                    const float s = inv[j];
+                    acc = make_float4(acc.x * s, acc.y * s, acc.z * s, acc.w * s);
+                }
+                if constexpr (KIND == EPI_RESID && FN) {
+                    // (it, hence j, is the same on every lane of the warp: the group sums shuffle)
+                    const bool live = j < a.epi.m_tok && n < a.epi.n_out;
+                    const float ss = live ? epi_quad_resid<true>(a.epi, n, j, acc, hv[q], gv[q]) : 0.f;
+                    ss_quad_groups(a.epi, n, j, ss, j < a.epi.m_tok && (n & ~31) < a.epi.n_out);
+                } else if constexpr (KIND == EPI_RESID) {
+                    if (j < a.epi.m_tok && n < a.epi.n_out) epi_quad_resid<false>(a.epi, n, j, acc, hv[q]);
                 } else if constexpr (KIND == EPI_QKV) {
                     epi_quad_qkv<__nv_bfloat16>(ep, n, j, acc, hv[q]);
                 } else {
@@ -220,7 +236,9 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams&
     }
 }
 
-template <int KIND>
+// FN: the RMSNorm folded in (EpiParams nx_* for the residual kind, in_ss for the
+// kinds that consume its output).
+template <int KIND, bool FN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -246,6 +264,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr bool kStageQkv = KIND == EPI_QKV;
     int32_t* qkv_smem = reinterpret_cast<int32_t*>(tmem_slot + 8);  // past the slot and the 4 flags
     const bool stage_qkv = kStageQkv && a.epi.m_tok <= TC_QKV_STAGE_TOK;
+    // fused norm: per-token 1/rms of this GEMM's input (computed by the epilogue warps)
+    float* s_inv = reinterpret_cast<float*>(qkv_smem + 2 * TC_QKV_STAGE_TOK + 128);
+    const float* inv = (FN && KIND != EPI_RESID) ? s_inv : nullptr;  // (host: m_tok <= TC_QKV_STAGE_TOK)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -372,6 +393,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;           // TMEM lane quadrant this warp may read
         const int row = q * 32 + lane;    // output row within the tile
         const int et = threadIdx.x - 64;  // 0..127
+        if constexpr (FN && KIND != EPI_RESID) {
+            // 1 / rms of each token from the 32-row group sums of squares the previous
+            // GEMM wrote (a fixed summation order), while the mainloop runs
+            const int G = a.epi.in_groups, ld = a.epi.ss_ld;
+            for (int j = et; j < a.epi.m_tok; j += 128) {
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                int g = 0;
+                for (; g + 8 <= G; g += 8) {
+                    float v8[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v8[u] = a.epi.in_ss[(size_t)(g + u) * ld + j];
+                    s0 += v8[0] + v8[4];
+                    s1 += v8[1] + v8[5];
+                    s2 += v8[2] + v8[6];
+                    s3 += v8[3] + v8[7];
+                }
+                for (; g < G; ++g) s0 += a.epi.in_ss[(size_t)g * ld + j];
+                const float tot = (s0 + s1) + (s2 + s3);
+                s_inv[j] = 1.0f / sqrtf(tot / a.epi.in_d + a.epi.in_eps);
+            }
+            // (read after the first segment's barrier below, or the cluster barrier)
+        }
         int t, kb_b, kb_e;
         for (int seg = 0; tc_segment(a, sc, c, seg, t, kb_b, kb_e); ++seg) {
             const int st = seg & 1;
@@ -410,8 +453,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     tmem_ld16(taddr + (uint32_t)cc, r);
                     float v[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-                    drain16<KIND, __nv_bfloat16>(ep, n, j_base + cc, v);
+                    for (int i = 0; i < 16; ++i) {
+                        v[i] = __uint_as_float(r[i]);
+                        if constexpr (FN && KIND != EPI_RESID) v[i] *= inv[j_base + cc + i];
+                    }
+                    drain16<KIND, __nv_bfloat16, FN>(ep, n, j_base + cc, v);
                 }
             } else {
                 // tile cut across CTAs: publish this partial; the last arriver finishes the tile
@@ -471,8 +517,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const int col = cc + cq + 4 * i;
-                            if (col < BN) epi_quad<KIND, __nv_bfloat16>(ep, tm * TC_BM + r4, j_base + col, acc[i]);
+                            const int col = cc + cq + 4 * i;  // (the same on every lane of the warp)
+                            if (col >= BN) continue;
+                            const int n = tm * TC_BM + r4, j = j_base + col;
+                            float4 v = acc[i];
+                            if constexpr (FN && KIND != EPI_RESID) {
+                                const float s = inv[j];
+                                v = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
+                            }
+                            if constexpr (KIND == EPI_RESID && FN) {
+                                const bool live = j < ep.m_tok && n < ep.n_out;
+                                const float ss =
+                                    live ? epi_quad_resid<true>(ep, n, j, v,
+                                                                *reinterpret_cast<const float4*>(ep.h + (size_t)j * ep.ld + n),
+                                                                *reinterpret_cast<const float4*>(ep.nx_g + n))
+                                         : 0.f;
+                                ss_quad_groups(ep, n, j, ss, j < ep.m_tok && (n & ~31) < ep.n_out);
+                            } else {
+                                epi_quad<KIND, __nv_bfloat16>(ep, n, j, v);
+                            }
                         }
                     }
                     if (et == 0) a.counters[t] = 0u;
@@ -533,8 +596,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = false;
         }
 #define YK_CLUSTER_REDUCE(N)                                                                                        \
-    (push ? cluster_reduce<KIND, N, true>(a, ep, red_addr, recv_addr, rope_addr, rank, slot_cols, tm, tn, c0, c1, ok) \
-          : cluster_reduce<KIND, N, false>(a, ep, red_addr, recv_addr, rope_addr, rank, slot_cols, tm, tn, c0, c1, ok))
+    (push ? cluster_reduce<KIND, N, true, FN>(a, ep, red_addr, recv_addr, rope_addr, rank, slot_cols, tm, tn, c0, c1, \
+                                              ok, inv)                                                                \
+          : cluster_reduce<KIND, N, false, FN>(a, ep, red_addr, recv_addr, rope_addr, rank, slot_cols, tm, tn, c0, c1, \
+                                               ok, inv))
         switch (CS) {
             case 1: YK_CLUSTER_REDUCE(1); break;
             case 2: YK_CLUSTER_REDUCE(2); break;
@@ -644,14 +709,23 @@ static yk_status get_x_map(yk_model* m, const void* X, int K, int BN, const CUte
 
 template <int KIND>
 static yk_status launch_tc(const cudaLaunchConfig_t& cfg, const CUtensorMap* tmW, const CUtensorMap* tmX,
-                           const TcArgs& a) {
+                           const TcArgs& a, bool fn) {
     static bool attr = false;
     if (!attr) {
-        YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            TC_SMEM_BUDGET + 16384 + TC_SMEM_TAIL));
+        if constexpr (KIND == EPI_QKV || KIND == EPI_RESID || KIND == EPI_GLU)
+            YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<KIND, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               TC_SMEM_BUDGET + 16384 + TC_SMEM_TAIL));
         attr = true;
     }
-    YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<KIND>, *tmW, *tmX, a));
+    if constexpr (KIND == EPI_QKV || KIND == EPI_RESID || KIND == EPI_GLU) {
+        if (fn) {
+            YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<KIND, true>, *tmW, *tmX, a));
+            return YK_OK;
+        }
+    }
+    YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<KIND, false>, *tmW, *tmX, a));
     return YK_OK;
 }
 
@@ -665,7 +739,7 @@ static int cluster_capacity(yk_engine* e, int s) {
         dev = e->device;
     }
     if (cap[s] == 0) {
-        cudaFuncSetAttribute(gemm_tc_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(gemm_tc_kernel<EPI_STORE, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              TC_SMEM_BUDGET + 16384 + TC_SMEM_TAIL);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(s * 64);
@@ -679,7 +753,7 @@ static int cluster_capacity(yk_engine* e, int s) {
         cfg.attrs = at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EPI_STORE>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EPI_STORE, false>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = 1;
         }
@@ -750,7 +824,7 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
         for (int s = std::min(-force_grid, std::min(8, kb)); s >= 2 && cs == 0; --s)
             if (cluster_fits(s)) cs = s;
         YK_ARG(cs > 0, "no cluster size fits the shared-memory ring");
-    } else if (force_grid == 0 && tiles * 2 < e->num_sms) {
+    } else if (force_grid == 0 && tiles * 2 < e->num_sms && !(e->gemm_variant & 32)) {
         for (int s = (int)std::min<long long>(std::min(8, kb), e->num_sms / tiles); s >= 2 && cs == 0; --s)
             if (tiles <= cluster_capacity(e, s) && cluster_fits(s)) cs = s;
     }
@@ -840,12 +914,16 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
     }
     cfg.attrs = at;
     cfg.numAttrs = na;
+    // fused norm: the residual kind writes x / sums of squares, QKV and gate/up consume them
+    const bool fn = ep.kind == EPI_RESID ? ep.nx_out != nullptr : (ep.in_ss != nullptr);
+    if (fn && ep.kind == EPI_RESID) YK_ARG(ep.nx_g && ep.nx_ss && ep.ss_ld >= m_tok, "fused norm: outputs");
+    if (fn && ep.kind != EPI_RESID) YK_ARG(m_tok <= TC_QKV_STAGE_TOK && ep.ss_ld >= m_tok, "fused norm: input");
     switch (ep.kind) {
-        case EPI_QKV: YK_TRY(launch_tc<EPI_QKV>(cfg, tmW, tmX, a)); break;
-        case EPI_RESID: YK_TRY(launch_tc<EPI_RESID>(cfg, tmW, tmX, a)); break;
-        case EPI_GLU: YK_TRY(launch_tc<EPI_GLU>(cfg, tmW, tmX, a)); break;
-        case EPI_LOGITS: YK_TRY(launch_tc<EPI_LOGITS>(cfg, tmW, tmX, a)); break;
-        default: YK_TRY(launch_tc<EPI_STORE>(cfg, tmW, tmX, a)); break;
+        case EPI_QKV: YK_TRY(launch_tc<EPI_QKV>(cfg, tmW, tmX, a, fn)); break;
+        case EPI_RESID: YK_TRY(launch_tc<EPI_RESID>(cfg, tmW, tmX, a, fn)); break;
+        case EPI_GLU: YK_TRY(launch_tc<EPI_GLU>(cfg, tmW, tmX, a, fn)); break;
+        case EPI_LOGITS: YK_TRY(launch_tc<EPI_LOGITS>(cfg, tmW, tmX, a, false)); break;
+        default: YK_TRY(launch_tc<EPI_STORE>(cfg, tmW, tmX, a, false)); break;
     }
     e->launches++;
     return YK_OK;

@@ -75,11 +75,13 @@ struct yk_engine {
     int gemm_variant = 0;                // GEMM schedule tuning knob (env YK_GEMM_VARIANT): bit 0 = pure
                                          // stream-K instead of whole tiles + stream-K remainder; bit 2 =
                                          // cluster scheduling policy "spread"; bit 3 = cluster split-K
-                                         // reduction always by distributed-shared-memory loads
-    int gemm_push_min = 32768;           // cluster split-K: column shares of at least this many bytes are
+                                         // reduction always by distributed-shared-memory loads; bit 5 =
+                                         // no cluster split-K (whole tiles / stream-K for every shape)
+    int gemm_push_min = 16384;           // cluster split-K: column shares of at least this many bytes are
                                          // exchanged by copy engine (env YK_GEMM_PUSH_MIN)
     int attn_waves = 1;                  // attention items per resident CTA slot (env YK_ATTN_WAVES)
     bool attn_balanced = false;          // attention pieces <= average slot load (env YK_ATTN_PLAN=1)
+    bool fuse_norm = true;               // RMSNorm folded into the GEMMs around it (env YK_FUSE_NORM=0: off)
     bool profiling = false;
     void* nccl_comm = nullptr;           // tensor-parallel group (yk_tp_init), else null
     int tp_rank = 0, tp_world = 1;
@@ -141,6 +143,7 @@ struct yk_model {
     float* logits = nullptr;   // [T x V]
     float* rope_denom = nullptr;  // [dh/2]
     float2* rope_tab = nullptr;   // [max_tokens x dh/2] (cos, sin) of this step's token positions
+    float* norm_ss = nullptr;     // [d/32 x max_tokens] fused RMSNorm: 32-element group sums of squares
     // step metadata (device), packed as int32
     int32_t* meta = nullptr;
     size_t meta_cap = 0;       // int32 elements
@@ -259,6 +262,18 @@ struct EpiParams {
     int act = 0;
     // EPI_LOGITS: logits[j * n_out + n]
     float cap = 0.f;
+    // RMSNorm folded into the GEMMs around it (bf16 models).  EPI_RESID with
+    // nx_out: also writes the next GEMM's input nx_out[j * ld + n] =
+    // bf16(h_new * nx_g[n]) (the norm's gain; its 1/rms follows) and the sums of
+    // squares of h_new over each 32-row group: nx_ss[(n / 32) * ss_ld + j].
+    // in_ss: this GEMM's input is such an x; the accumulator of token j is scaled
+    // by 1 / sqrt(sum_g in_ss[g * ss_ld + j] / in_d + in_eps) first.
+    const float* nx_g = nullptr;
+    void* nx_out = nullptr;
+    float* nx_ss = nullptr;
+    const float* in_ss = nullptr;
+    int in_groups = 0, ss_ld = 0;  // in_groups: 32-row groups of the input dimension (d / 32)
+    float in_d = 0.f, in_eps = 0.f;
     uint32_t* err = nullptr;
 };
 
@@ -278,7 +293,10 @@ struct DraftTokens {
     const uint32_t* d = nullptr;
     int k = 0, j0 = 0, nd = 0;
 };
-yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T, const DraftTokens& dt = {});
+// norm_g: fused RMSNorm of the first layer (bf16): also x = bf16(h * norm_g) and
+// the 32-element group sums of squares (m->norm_ss, token stride T).
+yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T, const DraftTokens& dt = {},
+                       const float* norm_g = nullptr);
 // Device array [B x k] of the draft tokens yk_draft_sample kept on the device
 // for a batch of B sequences.
 const uint32_t* sampler_device_drafts(const yk_sampler* s, int B, int* k);

@@ -8,11 +8,18 @@ namespace yk {
 // Also the step's RoPE table: rope[t][i] = (cos, sin)(pos[t] / denom[i]), the
 // angle of dimension pair i at token t that every layer's QKV epilogue uses.
 // dt.d: the last dt.nd tokens of each sequence are device-resident draft tokens.
+// fn.g (fused RMSNorm): also the first GEMM's input x = bf16(h * g) and the sums
+// of squares of h over each 32-element group, fn.ss[(i / 32) * T + t].
+struct EmbedNorm {
+    const float* g = nullptr;
+    __nv_bfloat16* x = nullptr;
+    float* ss = nullptr;
+};
 template <typename WT>
 __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict__ tokens, float* __restrict__ h,
                              int d, int V, const int32_t* __restrict__ pos, const float* __restrict__ denom,
                              float2* __restrict__ rope, int half_dh, uint32_t* err, Trace tr, DraftTokens dt,
-                             const int32_t* __restrict__ seq_of, const int32_t* __restrict__ q_starts) {
+                             const int32_t* __restrict__ seq_of, const int32_t* __restrict__ q_starts, EmbedNorm fn) {
     if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
@@ -33,7 +40,24 @@ __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict
         return;
     }
     const WT* row = E + (size_t)tok * d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) h[(size_t)t * d + i] = to_f32(row[i]);
+    if (!fn.g) {
+        for (int i = threadIdx.x; i < d; i += blockDim.x) h[(size_t)t * d + i] = to_f32(row[i]);
+    } else {
+        // every thread runs every pass (warp sums); a warp's 32 elements form one group
+        for (int i0 = 0; i0 < d; i0 += blockDim.x) {
+            const int i = i0 + threadIdx.x;
+            float v = 0.f;
+            if (i < d) {
+                v = to_f32(row[i]);
+                h[(size_t)t * d + i] = v;
+                fn.x[(size_t)t * d + i] = __float2bfloat16_rn(v * fn.g[i]);
+            }
+            float ss = v * v;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if ((threadIdx.x & 31) == 0 && i < d) fn.ss[(size_t)(i >> 5) * gridDim.x + t] = ss;
+        }
+    }
     if (threadIdx.x == 0) trace_mark(tr, TR_END);
 }
 
@@ -130,17 +154,24 @@ __global__ void fill_kernel(T* __restrict__ out, size_t n, float v) {
 }
 
 // Host launchers -------------------------------------------------------------
-yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T, const DraftTokens& dt) {
+yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, int T, const DraftTokens& dt,
+                       const float* norm_g) {
     const auto& c = m->cfg;
+    EmbedNorm fn;
+    if (norm_g) {  // fused RMSNorm of the first layer (bf16)
+        fn.g = norm_g;
+        fn.x = (__nv_bfloat16*)m->xn;
+        fn.ss = m->norm_ss;
+    }
     if (c.dtype == YK_DTYPE_BF16)
         YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<__nv_bfloat16>, T, 256, 0, (const __nv_bfloat16*)m->embed, tokens,
                                  m->h, c.d_model, c.vocab_size, pos, (const float*)m->rope_denom, m->rope_tab,
                                  c.head_dim / 2, m->e->d_err, trace_next(m->e, TK_EMBED), dt, m->cur.seq,
-                                 m->cur.q_starts));
+                                 m->cur.q_starts, fn));
     else
         YK_CHECK_CUDA(launch_pdl(m->e, embed_kernel<float>, T, 256, 0, (const float*)m->embed, tokens, m->h, c.d_model,
                                  c.vocab_size, pos, (const float*)m->rope_denom, m->rope_tab, c.head_dim / 2,
-                                 m->e->d_err, trace_next(m->e, TK_EMBED), dt, m->cur.seq, m->cur.q_starts));
+                                 m->e->d_err, trace_next(m->e, TK_EMBED), dt, m->cur.seq, m->cur.q_starts, EmbedNorm{}));
     m->e->launches++;
     return YK_OK;
 }
