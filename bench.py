@@ -392,7 +392,8 @@ EPI_NAMES = {0: "store", 1: "qkv", 2: "resid", 3: "glu", 4: "logits"}
 def trace_name(k: int) -> str:
     base = TRACE_KINDS.get(k & 15, "other")
     if base == "gemm":
-        return f"gemm_{EPI_NAMES.get((k >> 4) & 15, '?')}_{128 * ((k >> 8) & 0xFFFF)}x{16 * (k >> 24)}"
+        name = f"gemm_{EPI_NAMES.get((k >> 4) & 15, '?')}_{128 * ((k >> 8) & 0xFFFF)}x{16 * ((k >> 24) & 0x7F)}"
+        return name + "+down" if k >> 31 else name  # bit 31: the chained gate/up + down_proj launch
     if base == "attention":
         return f"attention_dh{k >> 8}"
     return base

@@ -130,6 +130,8 @@ def test_rejects_bad_block_id(engine):
     {"YK_GEMM_VARIANT": "32"},   # no clusters: whole tiles straight from the accumulator
     {"YK_GEMM_VARIANT": "33"},   # no clusters, pure stream-K: cut tiles finished by the last arriver
     {"YK_FUSE_NORM": "0"},       # RMSNorm as separate kernels
+    {"YK_GEMM_CHAIN": "1"},      # gate/up and down_proj as one launch with a grid barrier
+    {"YK_GEMM_CHAIN": "1", "YK_FUSE_NORM": "0"},
 ])
 def test_bf16_gemm_paths_with_fused_norm(oracle, monkeypatch, knobs):
     """The bf16 forward through every GEMM work split and reduction, each carrying

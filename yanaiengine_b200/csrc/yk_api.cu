@@ -97,6 +97,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     if (const char* v = std::getenv("YK_GEMM_VARIANT")) e->gemm_variant = std::atoi(v);
     if (const char* v = std::getenv("YK_GEMM_PUSH_MIN")) e->gemm_push_min = std::max(0, std::atoi(v));
     if (const char* v = std::getenv("YK_FUSE_NORM")) e->fuse_norm = std::atoi(v) != 0;
+    if (const char* v = std::getenv("YK_GEMM_CHAIN")) e->gemm_chain = std::atoi(v) != 0;
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
     yk_status s = e->ensure_pinned((size_t)4 << 20);
@@ -376,6 +377,7 @@ extern "C" void yk_model_destroy(yk_model* m) {
     if (m->attn_counters) cudaFree(m->attn_counters);
     if (m->attn_stamps) cudaFree(m->attn_stamps);
     if (m->gemm_stamps) cudaFree(m->gemm_stamps);
+    if (m->chain_bar) cudaFree(m->chain_bar);
     if (m->gemm_counters) cudaFree(m->gemm_counters);
     delete m;
 }
@@ -772,6 +774,14 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         eg.out = m->act;
         eg.act = c.act;
         norm_in(eg);
+        if (!tp && e->gemm_chain && c.dtype == YK_DTYPE_BF16 && T <= 256) {
+            // gate/up and down_proj in one launch
+            EpiParams ed = er;
+            norm_out(ed, l + 1 < c.n_layers ? m->layers[l + 1].n1 : nullptr);
+            YK_TRY(gemm_chain_glu_down(m, L.wgu, &L.tm_gu, m->xn, 2 * F, d, L.wdown, &L.tm_down, m->act, d, F, T, eg,
+                                       ed));
+            continue;
+        }
         YK_TRY(gemm_run(m, L.wgu, &L.tm_gu, m->xn, 2 * F, d, T, eg));
         if (tp) {
             YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, es));

@@ -247,6 +247,16 @@ __device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
                  : "memory");
     return v;
 }
+// Acquire load of a global counter (gpu scope).
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Orders generic-proxy global writes (this thread's, and those it acquired) before
+// its later async-proxy (TMA) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // Non-binding prefetch of the 128-byte line holding p into L2.
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 

@@ -236,6 +236,138 @@ __device__ __forceinline__ void cluster_reduce(const TcArgs& a, const EpiParams&
     }
 }
 
+// Fused norm: 1 / rms of each token of this GEMM's input, from the 32-row group
+// sums of squares the previous GEMM wrote (a fixed summation order); the
+// epilogue warps run it (thread et of 128) while the mainloop streams.
+__device__ __forceinline__ void tc_inv_rms(const EpiParams& e, float* s_inv, int et) {
+    const EpiParams& ep = e;
+    const int G = ep.in_groups, ld = ep.ss_ld;
+    for (int j = et; j < ep.m_tok; j += 128) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int g = 0;
+        for (; g + 8 <= G; g += 8) {
+            float v8[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v8[u] = ep.in_ss[(size_t)(g + u) * ld + j];
+            s0 += v8[0] + v8[4];
+            s1 += v8[1] + v8[5];
+            s2 += v8[2] + v8[6];
+            s3 += v8[3] + v8[7];
+        }
+        for (; g < G; ++g) s0 += ep.in_ss[(size_t)g * ld + j];
+        const float tot = (s0 + s1) + (s2 + s3);
+        s_inv[j] = 1.0f / sqrtf(tot / ep.in_d + ep.in_eps);
+    }
+}
+
+// Epilogue of a whole tile held in TMEM (this warp's 32 rows at taddr): one row
+// per lane, 16 tokens per drain.
+template <int KIND, bool FN>
+__device__ __forceinline__ void tc_whole_tile(const EpiParams& ep, uint32_t taddr, int n, int j_base, int BN,
+                                              const float* inv) {
+    for (int cc = 0; cc < BN; cc += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + (uint32_t)cc, r);
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            v[i] = __uint_as_float(r[i]);
+            if constexpr (FN && KIND != EPI_RESID) v[i] *= inv[j_base + cc + i];
+        }
+        drain16<KIND, __nv_bfloat16, FN>(ep, n, j_base + cc, v);
+    }
+}
+
+// Epilogue of a segment that holds part of a tile cut across CTAs (stream-K):
+// publish this CTA's partial; the last arriver sums the partials in k order and
+// runs the epilogue.  All 128 epilogue threads call it.
+template <int KIND, bool FN, int FIX = 4>
+__device__ __forceinline__ void tc_cut_tile(const TcArgs& a, const EpiParams& ep, const float* inv, int c, int t,
+                                            uint32_t taddr, int row, int et, volatile int* flags) {
+    const int BN = a.BN;
+    const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+    const int j_base = tn * BN;
+    const long long RU = (long long)a.sk_tiles * a.kb_total;
+    const int c_lo = cta_of_unit((long long)t * a.kb_total, RU, a.sk_ctas);
+    const int c_hi = cta_of_unit((long long)(t + 1) * a.kb_total - 1, RU, a.sk_ctas);
+    const int nseg = c_hi - c_lo + 1;
+    float* mine = a.ws + (size_t)partial_slot(a, c, t) * TC_BM * BN;
+    for (int cc = 0; cc < BN; cc += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + (uint32_t)cc, r);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) __stcg(mine + (size_t)(cc + i) * TC_BM + row, __uint_as_float(r[i]));
+    }
+    __threadfence();
+    epi_bar_sync();
+    if (et == 0) flags[1] = (atomicAdd(&a.counters[t], 1u) == (uint32_t)(nseg - 1)) ? 1 : 0;
+    epi_bar_sync();
+    if (flags[1]) {
+        // Sum the nseg partials in k order (deterministic).  Thread et owns rows
+        // 4*(et&31)..+3 of columns (et>>5) + 4i, i < 8: float4 loads, 8 columns x
+        // up to FIX segments in flight per round, one vector store per quad.
+        __threadfence();
+        const int r4 = (et & 31) * 4, cq = et >> 5;
+        for (int cc = 0; cc < BN; cc += 32) {
+            float4 acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sg0 = 0; sg0 < nseg; sg0 += FIX) {
+                float4 tv[FIX][8];
+#pragma unroll
+                for (int s4 = 0; s4 < FIX; ++s4) {
+                    if (sg0 + s4 < nseg) {
+                        const float* src =
+                            a.ws + (size_t)partial_slot(a, c_lo + sg0 + s4, t) * TC_BM * BN + r4;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int col = cc + cq + 4 * i;
+                            if (col < BN)
+                                tv[s4][i] = __ldcg(reinterpret_cast<const float4*>(src + (size_t)col * TC_BM));
+                        }
+                    }
+                }
+#pragma unroll
+                for (int s4 = 0; s4 < FIX; ++s4) {
+                    if (sg0 + s4 < nseg) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            acc[i].x += tv[s4][i].x;
+                            acc[i].y += tv[s4][i].y;
+                            acc[i].z += tv[s4][i].z;
+                            acc[i].w += tv[s4][i].w;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int col = cc + cq + 4 * i;  // (the same on every lane of the warp)
+                if (col >= BN) continue;
+                const int n = tm * TC_BM + r4, j = j_base + col;
+                float4 v = acc[i];
+                if constexpr (FN && KIND != EPI_RESID) {
+                    const float s = inv[j];
+                    v = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
+                }
+                if constexpr (KIND == EPI_RESID && FN) {
+                    const bool live = j < ep.m_tok && n < ep.n_out;
+                    const float ss =
+                        live ? epi_quad_resid<true>(ep, n, j, v,
+                                                    *reinterpret_cast<const float4*>(ep.h + (size_t)j * ep.ld + n),
+                                                    *reinterpret_cast<const float4*>(ep.nx_g + n))
+                             : 0.f;
+                    ss_quad_groups(ep, n, j, ss, j < ep.m_tok && (n & ~31) < ep.n_out);
+                } else {
+                    epi_quad<KIND, __nv_bfloat16>(ep, n, j, v);
+                }
+            }
+        }
+        if (et == 0) a.counters[t] = 0u;
+    }
+    epi_bar_sync();  // flags[1] is rewritten by the next cut tile
+}
+
 // FN: the RMSNorm folded in (EpiParams nx_* for the residual kind, in_ss for the
 // kinds that consume its output).
 template <int KIND, bool FN>
@@ -393,28 +525,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;           // TMEM lane quadrant this warp may read
         const int row = q * 32 + lane;    // output row within the tile
         const int et = threadIdx.x - 64;  // 0..127
-        if constexpr (FN && KIND != EPI_RESID) {
-            // 1 / rms of each token from the 32-row group sums of squares the previous
-            // GEMM wrote (a fixed summation order), while the mainloop runs
-            const int G = a.epi.in_groups, ld = a.epi.ss_ld;
-            for (int j = et; j < a.epi.m_tok; j += 128) {
-                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-                int g = 0;
-                for (; g + 8 <= G; g += 8) {
-                    float v8[8];
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) v8[u] = a.epi.in_ss[(size_t)(g + u) * ld + j];
-                    s0 += v8[0] + v8[4];
-                    s1 += v8[1] + v8[5];
-                    s2 += v8[2] + v8[6];
-                    s3 += v8[3] + v8[7];
-                }
-                for (; g < G; ++g) s0 += a.epi.in_ss[(size_t)g * ld + j];
-                const float tot = (s0 + s1) + (s2 + s3);
-                s_inv[j] = 1.0f / sqrtf(tot / a.epi.in_d + a.epi.in_eps);
-            }
-            // (read after the first segment's barrier below, or the cluster barrier)
-        }
+        if constexpr (FN && KIND != EPI_RESID) tc_inv_rms(a.epi, s_inv, et);  // read after the first barrier below
         int t, kb_b, kb_e;
         for (int seg = 0; tc_segment(a, sc, c, seg, t, kb_b, kb_e); ++seg) {
             const int st = seg & 1;
@@ -447,100 +558,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 fence_proxy_async_smem();  // the copy engine reads the parked partial
             } else if (kb_b == 0 && kb_e == KB) {
-                // whole tile in this segment: straight from TMEM, one row per lane
-                for (int cc = 0; cc < BN; cc += 16) {
-                    uint32_t r[16];
-                    tmem_ld16(taddr + (uint32_t)cc, r);
-                    float v[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        v[i] = __uint_as_float(r[i]);
-                        if constexpr (FN && KIND != EPI_RESID) v[i] *= inv[j_base + cc + i];
-                    }
-                    drain16<KIND, __nv_bfloat16, FN>(ep, n, j_base + cc, v);
-                }
+                tc_whole_tile<KIND, FN>(ep, taddr, n, j_base, BN, inv);
             } else {
-                // tile cut across CTAs: publish this partial; the last arriver finishes the tile
-                const long long RU = (long long)a.sk_tiles * KB;
-                const int c_lo = cta_of_unit((long long)t * KB, RU, a.sk_ctas);
-                const int c_hi = cta_of_unit((long long)(t + 1) * KB - 1, RU, a.sk_ctas);
-                const int nseg = c_hi - c_lo + 1;
-                float* mine = a.ws + (size_t)partial_slot(a, c, t) * TC_BM * BN;
-                for (int cc = 0; cc < BN; cc += 16) {
-                    uint32_t r[16];
-                    tmem_ld16(taddr + (uint32_t)cc, r);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) __stcg(mine + (size_t)(cc + i) * TC_BM + row, __uint_as_float(r[i]));
-                }
-                __threadfence();
-                epi_bar_sync();
-                if (et == 0) flags[1] = (atomicAdd(&a.counters[t], 1u) == (uint32_t)(nseg - 1)) ? 1 : 0;
-                epi_bar_sync();
-                if (flags[1]) {
-                    // Sum the nseg partials in k order (deterministic).  Thread et owns rows
-                    // 4*(et&31)..+3 of columns (et>>5) + 4i, i < 8: float4 loads, 8 columns x
-                    // up to FIX segments in flight per round, one vector store per quad.
-                    constexpr int FIX = 4;
-                    __threadfence();
-                    const int r4 = (et & 31) * 4, cq = et >> 5;
-                    for (int cc = 0; cc < BN; cc += 32) {
-                        float4 acc[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        for (int sg0 = 0; sg0 < nseg; sg0 += FIX) {
-                            float4 tv[FIX][8];
-#pragma unroll
-                            for (int s4 = 0; s4 < FIX; ++s4) {
-                                if (sg0 + s4 < nseg) {
-                                    const float* src =
-                                        a.ws + (size_t)partial_slot(a, c_lo + sg0 + s4, t) * TC_BM * BN + r4;
-#pragma unroll
-                                    for (int i = 0; i < 8; ++i) {
-                                        const int col = cc + cq + 4 * i;
-                                        if (col < BN)
-                                            tv[s4][i] = __ldcg(reinterpret_cast<const float4*>(src + (size_t)col * TC_BM));
-                                    }
-                                }
-                            }
-#pragma unroll
-                            for (int s4 = 0; s4 < FIX; ++s4) {
-                                if (sg0 + s4 < nseg) {
-#pragma unroll
-                                    for (int i = 0; i < 8; ++i) {
-                                        acc[i].x += tv[s4][i].x;
-                                        acc[i].y += tv[s4][i].y;
-                                        acc[i].z += tv[s4][i].z;
-                                        acc[i].w += tv[s4][i].w;
-                                    }
-                                }
-                            }
-                        }
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int col = cc + cq + 4 * i;  // (the same on every lane of the warp)
-                            if (col >= BN) continue;
-                            const int n = tm * TC_BM + r4, j = j_base + col;
-                            float4 v = acc[i];
-                            if constexpr (FN && KIND != EPI_RESID) {
-                                const float s = inv[j];
-                                v = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
-                            }
-                            if constexpr (KIND == EPI_RESID && FN) {
-                                const bool live = j < ep.m_tok && n < ep.n_out;
-                                const float ss =
-                                    live ? epi_quad_resid<true>(ep, n, j, v,
-                                                                *reinterpret_cast<const float4*>(ep.h + (size_t)j * ep.ld + n),
-                                                                *reinterpret_cast<const float4*>(ep.nx_g + n))
-                                         : 0.f;
-                                ss_quad_groups(ep, n, j, ss, j < ep.m_tok && (n & ~31) < ep.n_out);
-                            } else {
-                                epi_quad<KIND, __nv_bfloat16>(ep, n, j, v);
-                            }
-                        }
-                    }
-                    if (et == 0) a.counters[t] = 0u;
-                }
-                epi_bar_sync();  // flags[1] is rewritten by the next cut tile
+                tc_cut_tile<KIND, FN>(a, ep, inv, c, t, taddr, row, et, flags);
             }
             tc_fence_before();
             mbar_arrive(smem_u32(&acc_empty[st]));
@@ -621,6 +641,277 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, 2 * a.tmem_cols);
     if (threadIdx.x == 0) trace_mark(a.tr, TR_END);
+}
+
+// ---------------------------------------------------------------------------
+// Two GEMMs chained in one persistent grid (gate/up then down_proj): one CTA
+// per SM, both stages with whole tiles / stream-K (no clusters), the ring and
+// the TMEM accumulators running on across the stage boundary.  A CTA that has
+// finished its stage-0 epilogue arrives on a grid-wide counter; the producer
+// streams stage 1's first weight k-blocks into the ring meanwhile and issues
+// their activation halves once every CTA has arrived (bounded wait).  The grid's
+// dependents are released only then (every CTA is resident by that point, so
+// the barrier cannot wait on a CTA that a dependent keeps off its SM).
+// ---------------------------------------------------------------------------
+struct ChainArgs {
+    uint32_t* bar;    // grid barrier counter (monotonic across launches)
+    uint32_t target;  // its value once every CTA of this launch finished stage 0
+};
+
+template <int K0, bool F0, int K1, bool F1>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_chain_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmX0,
+                      const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmX1,
+                      const TcArgs a0, const TcArgs a1, const ChainArgs ch) {
+    static_assert(K1 == EPI_RESID || !F1, "stage 1 consumes no folded norm");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int BN = a0.BN, S = a0.stages;  // (the host makes both stages' tiles and rings equal)
+    const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+    uint64_t* empty = full + S;
+    uint64_t* acc_full = empty + S;      // [2]
+    uint64_t* acc_empty = acc_full + 2;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 3);
+    volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] last arriver, [2..3] broadcast
+    float* s_inv = reinterpret_cast<float*>(tmem_slot + 8 + 2 * TC_QKV_STAGE_TOK + 128);
+    const float* inv = (F0 && K0 != EPI_RESID) ? s_inv : nullptr;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x;
+    const TcSched sc0 = tc_sched(a0, c), sc1 = tc_sched(a1, c);
+    int n0 = 0;  // stage-0 segments of this CTA
+    {
+        int tt, x, y;
+        while (tc_segment(a0, sc0, c, n0, tt, x, y)) ++n0;
+    }
+    // segment i of the chain: stage 0's, then stage 1's
+    auto seg_of = [&](int i, int& stage, int& t, int& k0, int& k1) -> bool {
+        if (i < n0) {
+            stage = 0;
+            return tc_segment(a0, sc0, c, i, t, k0, k1);
+        }
+        stage = 1;
+        return tc_segment(a1, sc1, c, i - n0, t, k0, k1);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&acc_full[s]), 1);
+            mbar_init(smem_u32(&acc_empty[s]), 128);
+        }
+        flags[0] = flags[1] = flags[2] = flags[3] = 0;
+        mbar_fence_init();
+        trace_mark(a0.tr, TR_ENTRY);
+    }
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 2 * a0.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x != 0) pdl_wait();
+    if (threadIdx.x == 32) trace_mark(a0.tr, TR_START);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            long long g = 0;
+            bool stop = false;
+            // stage 0, with the first ring of weights ahead of the dependency wait
+            long long pre = 0;
+            {
+                int t, k0, k1;
+                for (int i = 0; pre < S && tc_segment(a0, sc0, c, i, t, k0, k1); ++i)
+                    for (int kb = k0; kb < k1 && pre < S; ++kb, ++pre) {
+                        const uint32_t fb = smem_u32(&full[pre]);
+                        mbar_arrive_expect_tx(fb, stage_bytes);
+                        tma_load_2d(smem_u32(smem + (size_t)pre * stage_bytes), &tmW0, kb * TC_BK,
+                                    (t % a0.tiles_m) * TC_BM, fb, pol_w);
+                    }
+            }
+            pdl_wait();
+            auto slot_ready = [&](long long gg) -> bool {  // ring slot of k-block gg free again
+                const long long r = gg / S;
+                if (flags[0] || (r > 0 && !mbar_wait_bounded(smem_u32(&empty[gg % S]), (uint32_t)((r - 1) & 1)))) {
+                    if (!flags[0]) raise_err(a0.epi.err, YK_DEV_ERR_TIMEOUT);
+                    flags[0] = 1;
+                    return false;
+                }
+                return true;
+            };
+            {
+                int t, k0, k1;
+                for (int i = 0; !stop && tc_segment(a0, sc0, c, i, t, k0, k1); ++i) {
+                    const int tm = t % a0.tiles_m, tn = t / a0.tiles_m;
+                    for (int kb = k0; kb < k1; ++kb, ++g) {
+                        const uint32_t sdst = smem_u32(smem + (size_t)(g % S) * stage_bytes);
+                        const uint32_t fb = smem_u32(&full[g % S]);
+                        if (g >= pre) {
+                            if (!slot_ready(g)) { stop = true; break; }
+                            mbar_arrive_expect_tx(fb, stage_bytes);
+                            tma_load_2d(sdst, &tmW0, kb * TC_BK, tm * TC_BM, fb, pol_w);
+                        }
+                        tma_load_2d(sdst + 16384u, &tmX0, kb * TC_BK, tn * BN, fb, pol_x);
+                    }
+                }
+            }
+            // stage 1: weights of the first ring's worth of k-blocks now ...
+            int pend_kb[16], pend_tn[16];
+            long long g1 = g;
+            int npend = 0;
+            {
+                int t, k0, k1;
+                for (int i = 0; !stop && npend < S && tc_segment(a1, sc1, c, i, t, k0, k1); ++i)
+                    for (int kb = k0; kb < k1 && npend < S; ++kb) {
+                        if (!slot_ready(g)) { stop = true; break; }
+                        const uint32_t fb = smem_u32(&full[g % S]);
+                        mbar_arrive_expect_tx(fb, stage_bytes);
+                        tma_load_2d(smem_u32(smem + (size_t)(g % S) * stage_bytes), &tmW1, kb * TC_BK,
+                                    (t % a1.tiles_m) * TC_BM, fb, pol_w);
+                        pend_kb[npend] = kb;
+                        pend_tn[npend] = t / a1.tiles_m;
+                        ++npend;
+                        ++g;
+                    }
+            }
+            // ... their activations once every CTA has written its stage-0 output
+            bool passed = false;
+            {
+                const uint64_t t0 = globaltimer_ns();
+                for (uint32_t it = 0;; ++it) {
+                    if ((int32_t)(ld_acquire_gpu(ch.bar) - ch.target) >= 0) { passed = true; break; }
+                    if ((it & 63u) == 63u && globaltimer_ns() - t0 > YK_WAIT_BUDGET_NS) break;
+                }
+            }
+            if (!passed) {
+                raise_err(a0.epi.err, YK_DEV_ERR_TIMEOUT);
+                flags[0] = 1;
+            }
+            pdl_trigger();  // every CTA of the grid is resident and past stage 0
+            fence_proxy_async_global();
+            // (issued even after a failed wait, so that every armed slot completes)
+            for (int u = 0; u < npend; ++u) {
+                const long long gg = g1 + u;
+                tma_load_2d(smem_u32(smem + (size_t)(gg % S) * stage_bytes) + 16384u, &tmX1, pend_kb[u] * TC_BK,
+                            pend_tn[u] * BN, smem_u32(&full[gg % S]), pol_x);
+            }
+            {
+                int t, k0, k1;
+                int done = 0;  // k-blocks of stage 1 already issued
+                for (int i = 0; !stop && tc_segment(a1, sc1, c, i, t, k0, k1); ++i) {
+                    const int tm = t % a1.tiles_m, tn = t / a1.tiles_m;
+                    for (int kb = k0; kb < k1; ++kb) {
+                        if (done < npend) { ++done; continue; }
+                        if (!slot_ready(g)) { stop = true; break; }
+                        const uint32_t sdst = smem_u32(smem + (size_t)(g % S) * stage_bytes);
+                        const uint32_t fb = smem_u32(&full[g % S]);
+                        mbar_arrive_expect_tx(fb, stage_bytes);
+                        tma_load_2d(sdst, &tmW1, kb * TC_BK, tm * TC_BM, fb, pol_w);
+                        tma_load_2d(sdst + 16384u, &tmX1, kb * TC_BK, tn * BN, fb, pol_x);
+                        ++g;
+                    }
+                }
+            }
+            // Every issued copy must land before shared memory is reused or released.
+            for (long long j = max(0LL, g - S); j < g; ++j)
+                (void)mbar_wait_bounded(smem_u32(&full[j % S]), (uint32_t)((j / S) & 1));
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            long long g = 0;
+            int stage, t, k0, k1;
+            for (int seg = 0; !flags[0] && seg_of(seg, stage, t, k0, k1); ++seg) {
+                const int st = seg & 1;
+                if (seg >= 2 && !mbar_wait_bounded(smem_u32(&acc_empty[st]), (uint32_t)(((seg >> 1) - 1) & 1))) {
+                    flags[0] = 1;
+                    raise_err(a0.epi.err, YK_DEV_ERR_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)st * a0.tmem_cols;
+                const uint32_t idesc = stage == 0 ? a0.idesc : a1.idesc;
+                bool ok = true;
+                for (int kb = k0; kb < k1; ++kb, ++g) {
+                    const int s = (int)(g % S);
+                    if (!mbar_wait_bounded(smem_u32(&full[s]), (uint32_t)((g / S) & 1))) {
+                        flags[0] = 1;
+                        raise_err(a0.epi.err, YK_DEV_ERR_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t wsm = smem_u32(smem + (size_t)s * stage_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 16; ++kk)
+                        tc_mma_bf16(d, sw128_kmajor_desc(wsm + kk * 32), sw128_kmajor_desc(wsm + 16384u + kk * 32),
+                                    idesc, (kb > k0 || kk > 0) ? 1u : 0u);
+                    tc_commit(smem_u32(&empty[s]));
+                }
+                tc_commit(smem_u32(&acc_full[st]));
+                if (!ok) break;
+            }
+        }
+    } else {
+        // ---------------- epilogue: warps 2..5 ----------------
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const int et = threadIdx.x - 64;
+        if constexpr (F0 && K0 != EPI_RESID) tc_inv_rms(a0.epi, s_inv, et);  // read after the first barrier below
+        int stage, t, kb_b, kb_e;
+        bool arrived = false;
+        for (int seg = 0; seg_of(seg, stage, t, kb_b, kb_e); ++seg) {
+            if (stage == 1 && !arrived) {
+                // this CTA's stage-0 output is written: arrive on the grid barrier
+                __threadfence();
+                epi_bar_sync();
+                if (et == 0) atomicAdd(ch.bar, 1u);
+                arrived = true;
+            }
+            const int st = seg & 1;
+            if (et == 0) {
+                if (!mbar_wait_bounded(smem_u32(&acc_full[st]), (uint32_t)((seg >> 1) & 1))) {
+                    flags[0] = 1;
+                    raise_err(a0.epi.err, YK_DEV_ERR_TIMEOUT);
+                }
+                flags[2 + st] = flags[0];
+            }
+            epi_bar_sync();
+            if (flags[2 + st]) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem + (uint32_t)st * a0.tmem_cols + ((uint32_t)(q * 32) << 16);
+            const int tiles_m = stage == 0 ? a0.tiles_m : a1.tiles_m;
+            const int tm = t % tiles_m, tn = t / tiles_m;
+            const int n = tm * TC_BM + row;
+            if (stage == 0) {
+                if (kb_b == 0 && kb_e == a0.kb_total) tc_whole_tile<K0, F0>(a0.epi, taddr, n, tn * BN, BN, inv);
+                else tc_cut_tile<K0, F0, 2>(a0, a0.epi, inv, c, t, taddr, row, et, flags);
+            } else {
+                if (kb_b == 0 && kb_e == a1.kb_total) tc_whole_tile<K1, F1>(a1.epi, taddr, n, tn * BN, BN, nullptr);
+                else tc_cut_tile<K1, F1, 2>(a1, a1.epi, nullptr, c, t, taddr, row, et, flags);
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acc_empty[st]));
+        }
+        if (!arrived) {  // no stage-1 segment here (or an abort): arrive all the same
+            __threadfence();
+            epi_bar_sync();
+            if (et == 0) atomicAdd(ch.bar, 1u);
+        }
+    }
+
+    // ---------------- teardown ----------------
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 2 * a0.tmem_cols);
+    if (threadIdx.x == 0) trace_mark(a0.tr, TR_END);
 }
 
 // ---------------------------------------------------------------------------
@@ -925,6 +1216,131 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
         case EPI_LOGITS: YK_TRY(launch_tc<EPI_LOGITS>(cfg, tmW, tmX, a, false)); break;
         default: YK_TRY(launch_tc<EPI_STORE>(cfg, tmW, tmX, a, false)); break;
     }
+    e->launches++;
+    return YK_OK;
+}
+
+// Schedule of one chained stage: grid fixed at one CTA per SM, whole tiles
+// round-robin with the remainder stream-K (or all stream-K), no clusters.
+static yk_status chain_plan(yk_model* m, int n_out, int K, int m_tok, const EpiParams& ep_in, int grid, TcArgs* a) {
+    yk_engine* e = m->e;
+    EpiParams ep = ep_in;
+    ep.n_out = n_out;
+    ep.m_tok = m_tok;
+    ep.err = e->d_err;
+    YK_ARG(n_out % 4 == 0 && m_tok > 0 && m_tok <= 256 && m_tok <= m->cfg.max_tokens, "chained gemm shape");
+    const int BN = ((m_tok + 15) / 16) * 16;
+    const int tiles_m = (n_out + TC_BM - 1) / TC_BM;
+    const int kb = (K + TC_BK - 1) / TC_BK;
+    const long long tiles = tiles_m;
+    const long long waves = tiles / grid, rest = tiles % grid;
+    int sk_tiles = 0, sk_ctas = 0;
+    if (waves == 0 || (e->gemm_variant & 1)) {
+        // every stream-K CTA must get at least one k-block (a cut tile counts on a
+        // partial from each CTA of its range)
+        sk_tiles = (int)tiles;
+        sk_ctas = (int)std::min<long long>(grid, tiles * kb);
+    } else if (rest > 0) {
+        sk_tiles = (int)rest;
+        sk_ctas = (int)std::min<long long>(grid, std::max<long long>(1, rest * kb / 8));
+    }
+    YK_ARG((size_t)2 * sk_ctas * TC_BM * BN <= m->gemm_ws_floats, "split workspace too small");
+    uint32_t cols = 32;
+    while ((int)cols < BN) cols <<= 1;
+    const uint32_t stage_bytes = 16384u + (uint32_t)BN * 128u;
+    *a = TcArgs{};
+    a->n_out = n_out; a->K = K; a->m_tok = m_tok;
+    a->tiles_m = tiles_m; a->kb_total = kb;
+    a->BN = BN;
+    a->stages = std::max(2, std::min(8, (int)(TC_SMEM_BUDGET / stage_bytes)));
+    a->tiles = (int)tiles; a->grid = grid; a->cluster_s = 0;
+    a->sk_tiles = sk_tiles; a->sk_ctas = sk_ctas;
+    a->idesc = idesc_bf16_f32(TC_BM, BN);
+    a->tmem_cols = cols;
+    a->ws = m->gemm_ws;
+    a->epi = ep;
+    a->stamps = nullptr;
+    return YK_OK;
+}
+
+template <bool F0, bool F1>
+static yk_status launch_chain(const cudaLaunchConfig_t& cfg, const CUtensorMap* w0, const CUtensorMap* x0,
+                              const CUtensorMap* w1, const CUtensorMap* x1, const TcArgs& a0, const TcArgs& a1,
+                              const ChainArgs& ch) {
+    static bool attr = false;
+    if (!attr) {
+        YK_CHECK_CUDA(cudaFuncSetAttribute(gemm_chain_kernel<EPI_GLU, F0, EPI_RESID, F1>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           TC_SMEM_BUDGET + 16384 + TC_SMEM_TAIL));
+        attr = true;
+    }
+    YK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_chain_kernel<EPI_GLU, F0, EPI_RESID, F1>, *w0, *x0, *w1, *x1, a0, a1,
+                                     ch));
+    return YK_OK;
+}
+
+// gate/up (GLU epilogue, input X0) then down_proj (residual epilogue, input the
+// GLU output X1) in one persistent launch of one CTA per SM.
+yk_status gemm_chain_glu_down(yk_model* m, const void* Wgu, const CUtensorMap* tmWgu, const void* X0, int n_gu, int K0,
+                              const void* Wd, const CUtensorMap* tmWd, const void* X1, int n_d, int K1, int m_tok,
+                              const EpiParams& eg, const EpiParams& ed) {
+    yk_engine* e = m->e;
+    YK_ARG(m->cfg.dtype == YK_DTYPE_BF16, "chained GEMMs are bf16");
+    const int grid = e->num_sms;
+    TcArgs a0, a1;
+    YK_TRY(chain_plan(m, n_gu, K0, m_tok, eg, grid, &a0));
+    YK_TRY(chain_plan(m, n_d, K1, m_tok, ed, grid, &a1));
+    const int need = a0.tiles + a1.tiles;
+    if (need > m->gemm_counter_cap) {
+        YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+        if (m->gemm_counters) cudaFree(m->gemm_counters);
+        m->gemm_counters = nullptr;
+        m->gemm_counter_cap = 0;
+        YK_CHECK_CUDA(cudaMalloc(&m->gemm_counters, (size_t)need * 2 * 4));
+        YK_CHECK_CUDA(cudaMemset(m->gemm_counters, 0, (size_t)need * 2 * 4));
+        m->gemm_counter_cap = need * 2;
+    }
+    a0.counters = m->gemm_counters;
+    a1.counters = m->gemm_counters + a0.tiles;
+    const bool f0 = eg.in_ss != nullptr, f1 = ed.nx_out != nullptr;
+    if (f0) YK_ARG(m_tok <= TC_QKV_STAGE_TOK && eg.ss_ld >= m_tok, "fused norm: input");
+    if (f1) YK_ARG(ed.nx_g && ed.nx_ss && ed.ss_ld >= m_tok, "fused norm: outputs");
+    const CUtensorMap *x0 = nullptr, *x1 = nullptr;
+    YK_TRY(get_x_map(m, X0, K0, a0.BN, &x0));
+    YK_TRY(get_x_map(m, X1, K1, a1.BN, &x1));
+    if (!m->chain_bar) {
+        YK_CHECK_CUDA(cudaMalloc(&m->chain_bar, 4));
+        YK_CHECK_CUDA(cudaMemset(m->chain_bar, 0, 4));
+        m->chain_epoch = 0;
+    }
+    ChainArgs ch;
+    ch.bar = m->chain_bar;
+    ch.target = m->chain_epoch + (uint32_t)grid;  // (every CTA adds 1 once, whatever path it takes)
+    // trace kind: the gate/up shape (the launch covers both projections)
+    a0.tr = trace_next(e, TK_GEMM | ((uint32_t)EPI_GLU << 4) | ((uint32_t)a0.tiles_m << 8) |
+                              ((uint32_t)((m_tok + 15) / 16) << 24) | (1u << 31));
+    const uint32_t stage_bytes = 16384u + (uint32_t)a0.BN * 128u;
+    const size_t smem = (size_t)a0.stages * stage_bytes + TC_SMEM_TAIL;
+    const double es = 2.0;
+    ProfScope prof(e, YK_PROF_GEMM,
+                   ((double)n_gu + m_tok) * K0 * es + ((double)n_d + m_tok) * K1 * es + (double)m_tok * (n_gu / 2) * es +
+                       (double)m_tok * n_d * 8.0,
+                   2.0 * ((double)n_gu * K0 + (double)n_d * K1) * m_tok);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = e->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = (e->pdl && !e->profiling) ? 1 : 0;
+    if (f0 && f1) YK_TRY((launch_chain<true, true>(cfg, tmWgu, x0, tmWd, x1, a0, a1, ch)));
+    else if (f0) YK_TRY((launch_chain<true, false>(cfg, tmWgu, x0, tmWd, x1, a0, a1, ch)));
+    else if (f1) YK_TRY((launch_chain<false, true>(cfg, tmWgu, x0, tmWd, x1, a0, a1, ch)));
+    else YK_TRY((launch_chain<false, false>(cfg, tmWgu, x0, tmWd, x1, a0, a1, ch)));
+    m->chain_epoch = ch.target;  // only once the launch went in
     e->launches++;
     return YK_OK;
 }

@@ -82,6 +82,7 @@ struct yk_engine {
     int attn_waves = 1;                  // attention items per resident CTA slot (env YK_ATTN_WAVES)
     bool attn_balanced = false;          // attention pieces <= average slot load (env YK_ATTN_PLAN=1)
     bool fuse_norm = true;               // RMSNorm folded into the GEMMs around it (env YK_FUSE_NORM=0: off)
+    bool gemm_chain = false;             // gate/up + down_proj as one persistent launch (env YK_GEMM_CHAIN=1)
     bool profiling = false;
     void* nccl_comm = nullptr;           // tensor-parallel group (yk_tp_init), else null
     int tp_rank = 0, tp_world = 1;
@@ -162,6 +163,8 @@ struct yk_model {
     // GEMM phase timestamps (test hook only; null otherwise) and the last grid used
     unsigned long long* gemm_stamps = nullptr;
     int gemm_last_grid = 0;
+    uint32_t* chain_bar = nullptr;  // grid barrier counter of the chained gate/up + down launch
+    uint32_t chain_epoch = 0;       // its value after the last launch's barrier
     uint32_t gemm_stamp_kind = 0;  // test hook: only launches of this trace kind write gemm_stamps
     int gemm_stamp_cap = 0, gemm_stamp_grid = 0;
     // attention split-KV partials and per combine group arrival counters
@@ -279,6 +282,11 @@ struct EpiParams {
 
 yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const void* X, int n_out, int K, int m_tok,
                    const EpiParams& ep, int force_grid = 0);
+// gate/up (GLU epilogue) then down_proj (residual epilogue) in one persistent
+// launch (one CTA per SM, a grid barrier between them); m_tok <= 256.
+yk_status gemm_chain_glu_down(yk_model* m, const void* Wgu, const CUtensorMap* tmWgu, const void* X0, int n_gu, int K0,
+                              const void* Wd, const CUtensorMap* tmWd, const void* X1, int n_d, int K1, int m_tok,
+                              const EpiParams& eg, const EpiParams& ed);
 yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
 yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks,
                         double kv_bytes);
