@@ -42,6 +42,7 @@ typedef int32_t yk_status;
 
 #define YK_DTYPE_F32  0
 #define YK_DTYPE_BF16 1
+#define YK_DTYPE_F16  2  /* checkpoint sources only (yk_model_load_tensor)       */
 
 #define YK_ACT_SILU      0 /* SwiGLU, silu_kernel S/gemm.metal:405-413           */
 #define YK_ACT_GELU_TANH 1 /* GeGLU, gelu_kernel S/gemm.metal:231-241 (Gemma-2)  */
@@ -140,6 +141,52 @@ yk_status yk_model_set_tensor(yk_model* m, int32_t tensor, int32_t layer, const 
                               int32_t layout);
 /* Download one logical tensor as fp32 [out x in]. */
 yk_status yk_model_get_tensor(yk_model* m, int32_t tensor, int32_t layer, float* host);
+
+/* ---- checkpoints.  Replaces SafetensorsReader (S/SafetensorsReader.swift:18-128)
+ * and ModelLoader.loadLinearLayer (S/ModelLoader.swift:9-72). --------------- */
+typedef struct yk_safetensors yk_safetensors;
+typedef struct yk_tensor_info {
+    int32_t     dtype;          /* YK_DTYPE_F32 / BF16 / F16, or -1 (another dtype)   */
+    char        dtype_name[12]; /* as in the header: "F32", "BF16", "I8", ...          */
+    int32_t     ndim;
+    int64_t     shape[8];
+    const void* data;           /* the mapped bytes, valid until yk_safetensors_close */
+    uint64_t    nbytes;
+} yk_tensor_info;
+/* mmap a .safetensors file and parse its header (SafetensorsReader.open).  A
+ * header that does not parse, or whose entries' offsets leave the data block or
+ * disagree with dtype x shape, is YK_ERR_ARG (the reference trusts the file). */
+yk_status yk_safetensors_open(const char* path, yk_safetensors** out);
+void      yk_safetensors_close(yk_safetensors* st);
+int32_t   yk_safetensors_count(const yk_safetensors* st);
+/* Name of tensor i, 0 <= i < count, in name order (pointer valid until close). */
+yk_status yk_safetensors_name(const yk_safetensors* st, int32_t i, const char** name);
+/* tensorInfo + tensorData; YK_ERR_ARG if the name is absent. */
+yk_status yk_safetensors_info(const yk_safetensors* st, const char* name, yk_tensor_info* out);
+
+/* loadLinearLayer: upload one logical tensor from host memory in a checkpoint
+ * dtype (F32, BF16 or F16; converted on the device, round-to-nearest-even into
+ * bf16).  rows x cols is the stored shape of the FULL tensor: [out x in] for
+ * YK_LAYOUT_OUT_IN (PyTorch / safetensors), [in x out] for YK_LAYOUT_IN_OUT (the
+ * reference's LinearLayer); norms are [1 x d].  A tensor-parallel shard takes
+ * its window (its heads' / FFN rows of column-parallel weights, its columns of
+ * o_proj and down_proj). */
+yk_status yk_model_load_tensor(yk_model* m, int32_t tensor, int32_t layer, const void* host, int32_t src_dtype,
+                               int64_t rows, int64_t cols, int32_t layout);
+/* Q / K rows stored in rotate-half order (Hugging Face Llama checkpoints): row
+ * 2i + j of a head is read from stored row j * head_dim / 2 + i, so that RoPE's
+ * interleaved pairs (S/gemm.metal:674-682) rotate the same dimensions. */
+#define YK_LOAD_ROPE_HALF 1
+/* Every weight of the model from the files of a (sharded) checkpoint under the
+ * Hugging Face Llama / Gemma names (model.embed_tokens.weight,
+ * model.layers.N.self_attn.{q,k,v,o}_proj.weight, mlp.{gate,up,down}_proj.weight,
+ * input_layernorm.weight, post_attention_layernorm.weight, model.norm.weight,
+ * lm_head.weight -- absent: tied to the embedding).  norm_offset is added to
+ * every norm gain (1 for checkpoints that store gain - 1).  A missing tensor, a
+ * shape mismatch or a tensor in two files is YK_ERR_ARG; an unknown tensor of a
+ * decoder layer (a layer kind this module lacks) is YK_ERR_UNSUPPORTED. */
+yk_status yk_model_load_safetensors(yk_model* m, yk_safetensors* const* files, int32_t n_files, float norm_offset,
+                                    int32_t flags, int32_t* n_loaded);
 
 /* ---- paged KV pool.  Replaces BlockAllocator's MTLBuffers
  * (S/BlockAllocator.swift:13-36).  Block ids, the free list and the page

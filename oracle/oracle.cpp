@@ -58,6 +58,35 @@ extern "C" float orc_bf16_round(float x) {
     return r;
 }
 
+// S/ModelLoader.swift:75-100, one value at a time.
+extern "C" void orc_f16_to_f32(const uint16_t* h, size_t n, float* out) {
+    for (size_t i = 0; i < n; ++i) {
+        const uint32_t sign = (h[i] >> 15) & 1u, exponent = (h[i] >> 10) & 0x1fu, mantissa = h[i] & 0x3ffu;
+        uint32_t bits;
+        if (exponent == 0) {
+            if (mantissa == 0) {
+                bits = sign << 31;
+            } else {
+                // subnormal: shift the mantissa up to its implicit bit, lowering the exponent
+                int32_t e = 0;
+                uint32_t m = mantissa;
+                while ((m & 0x400u) == 0) {
+                    m <<= 1;
+                    e -= 1;
+                }
+                e += 1;
+                m &= ~0x400u;
+                bits = (sign << 31) | ((uint32_t)(e + 112) << 23) | (m << 13);
+            }
+        } else if (exponent == 31) {
+            bits = (sign << 31) | 0x7f800000u | (mantissa << 13);
+        } else {
+            bits = (sign << 31) | ((exponent + 112) << 23) | (mantissa << 13);
+        }
+        std::memcpy(&out[i], &bits, 4);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // SpeculativeSampler -- S/SpeculativeSampler.swift
 // ---------------------------------------------------------------------------

@@ -115,6 +115,11 @@ int orc_forward_step(const orc_cfg* c, const orc_weights* w, float* pool, int32_
 /* bf16 round-to-nearest-even, returned as fp32. */
 float orc_bf16_round(float x);
 
+/* IEEE half -> fp32, the reference's bit-level conversion of F16 checkpoint
+ * tensors (S/ModelLoader.swift:75-100: signed zero, subnormals normalised by
+ * shifting the mantissa, inf / nan kept); n values. */
+void orc_f16_to_f32(const uint16_t* h, size_t n, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -79,6 +79,8 @@ def lib():
                                        C.c_int32, _I, C.c_int32, C.c_int32, C.c_int, _F]
         L.orc_bf16_round.restype = C.c_float
         L.orc_bf16_round.argtypes = [C.c_float]
+        L.orc_f16_to_f32.restype = None
+        L.orc_f16_to_f32.argtypes = [C.POINTER(C.c_uint16), C.c_size_t, _F]
         _lib = L
     return _lib
 
@@ -207,3 +209,11 @@ class OracleModel:
         if rc != 0:
             raise ValueError("oracle forward rejected its arguments")
         return out
+
+
+def f16_to_f32(h):
+    """The reference's F16 checkpoint conversion (uint16 words -> fp32)."""
+    a = np.ascontiguousarray(np.asarray(h, dtype=np.uint16))
+    out = np.empty(a.shape, np.float32)
+    lib().orc_f16_to_f32(_p(a, C.c_uint16), a.size, _p(out, C.c_float))
+    return out

@@ -53,7 +53,27 @@ def _steps(seed=1):
     return steps
 
 
-def _worker(rank, uid, q):
+def _load_full(m, w):
+    """Every tensor through yk_model_load_tensor as the FULL tensor (bf16 words,
+    fp32 norms); the shard takes its window.  o_proj and down_proj arrive in the
+    reference's [in x out] layout, so the transposed window is covered too."""
+    def words(x):
+        return (np.ascontiguousarray(x, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+    m.load(abi.T_EMBED, 0, words(w["embed"]), abi.DTYPE_BF16)
+    m.load(abi.T_LM_HEAD, 0, words(w["lm_head"]), abi.DTYPE_BF16)
+    m.load(abi.T_FINAL_NORM, 0, w["final_norm"], abi.DTYPE_F32)
+    for l in range(CFG["n_layers"]):
+        for t, name in ((abi.T_WQ, "wq"), (abi.T_WK, "wk"), (abi.T_WV, "wv"), (abi.T_WGATE, "wg"),
+                        (abi.T_WUP, "wu")):
+            m.load(t, l, words(w[name][l]), abi.DTYPE_BF16)
+        for t, name in ((abi.T_WO, "wo"), (abi.T_WDOWN, "wd")):
+            m.load(t, l, np.ascontiguousarray(words(w[name][l]).T), abi.DTYPE_BF16, abi.LAYOUT_IN_OUT)
+        m.load(abi.T_NORM1, l, w["n1"][l], abi.DTYPE_F32)
+        m.load(abi.T_NORM2, l, w["n2"][l], abi.DTYPE_F32)
+
+
+def _worker(rank, uid, q, via_loader=False):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     try:
         e = abi.Engine(rank)
@@ -61,8 +81,14 @@ def _worker(rank, uid, q):
         c = abi.make_config(**CFG, dtype=abi.DTYPE_BF16, max_tokens=128, max_seqs=8)
         m = abi.Model(e, c, seed=3, tp=(rank, WORLD))
         w = _full_weights(CFG)
+        if via_loader:
+            _load_full(m, w)
         dh, F = CFG["head_dim"], CFG["ffn_dim"]
         hq, hk, fl = CFG["n_heads"] // WORLD * dh, CFG["n_kv_heads"] // WORLD * dh, F // WORLD
+        shard = {}
+        if via_loader:  # read back what the windows loaded, for the comparison below
+            for t in (abi.T_WQ, abi.T_WO, abi.T_WDOWN):
+                shard[t] = m.get(t, 1)
         m.set(abi.T_EMBED, 0, w["embed"])
         m.set(abi.T_LM_HEAD, 0, w["lm_head"])
         m.set(abi.T_FINAL_NORM, 0, w["final_norm"])
@@ -76,6 +102,8 @@ def _worker(rank, uid, q):
             m.set(abi.T_WDOWN, l, np.ascontiguousarray(w["wd"][l][:, rank * fl:(rank + 1) * fl]))
             m.set(abi.T_NORM1, l, w["n1"][l])
             m.set(abi.T_NORM2, l, w["n2"][l])
+        for t, got in shard.items():  # the loader's windows equal the per-shard uploads
+            assert np.array_equal(got, m.get(t, 1)), f"tensor {t} window differs"
         pool = abi.KVPool(e, m.cfg, NB)
         pt = PageTables(NB)
         out = []
@@ -92,7 +120,8 @@ def _worker(rank, uid, q):
         q.put((rank, None, None, repr(ex)))
 
 
-def test_tp2_forward_matches_oracle(oracle):
+@pytest.mark.parametrize("via_loader", [False, True])
+def test_tp2_forward_matches_oracle(oracle, via_loader):
     import torch
 
     if torch.cuda.device_count() < WORLD:
@@ -102,7 +131,7 @@ def test_tp2_forward_matches_oracle(oracle):
     uid = abi.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, uid, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, uid, q, via_loader)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = {}

@@ -15,7 +15,8 @@ LIB_PATH = PKG / "libyk.so"
 HOST_LIB_PATH = PKG / "libyk_host.so"
 
 YK_OK, YK_ERR_ARG, YK_ERR_OOM, YK_ERR_CUDA, YK_ERR_NCCL, YK_ERR_TIMEOUT, YK_ERR_DEVICE_CHECK, YK_ERR_UNSUPPORTED = range(8)
-DTYPE_F32, DTYPE_BF16 = 0, 1
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2  # F16: checkpoint sources only
+LOAD_ROPE_HALF = 1
 ACT_SILU, ACT_GELU_TANH = 0, 1
 BLOCK_SIZE = 16
 (T_EMBED, T_WQ, T_WK, T_WV, T_WO, T_WGATE, T_WUP, T_WDOWN, T_NORM1, T_NORM2, T_FINAL_NORM,
@@ -79,6 +80,14 @@ _PROTOS = {
     "yk_model_tensor_shape": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "yk_model_set_tensor": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P, C.c_int32]),
     "yk_model_get_tensor": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P]),
+    "yk_safetensors_open": (C.c_int32, [C.c_char_p, C.POINTER(_P)]),
+    "yk_safetensors_close": (None, [_P]),
+    "yk_safetensors_count": (C.c_int32, [_P]),
+    "yk_safetensors_name": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_char_p)]),
+    "yk_safetensors_info": (C.c_int32, [_P, C.c_char_p, C.c_void_p]),
+    "yk_model_load_tensor": (C.c_int32, [_P, C.c_int32, C.c_int32, _P, C.c_int32, C.c_int64, C.c_int64,
+                                         C.c_int32]),
+    "yk_model_load_safetensors": (C.c_int32, [_P, C.POINTER(_P), C.c_int32, C.c_float, C.c_int32, _I32P]),
     "yk_kv_pool_create": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_int32, C.POINTER(_P)]),
     "yk_kv_pool_destroy": (None, [_P]),
     "yk_kv_pool_num_blocks": (C.c_int32, [_P]),
@@ -314,6 +323,53 @@ class Engine:
             self.h = _P()
 
 
+class TensorInfo(C.Structure):
+    """yk_tensor_info (include/yk.h)."""
+    _fields_ = [("dtype", C.c_int32), ("dtype_name", C.c_char * 12), ("ndim", C.c_int32),
+                ("shape", C.c_int64 * 8), ("data", C.c_void_p), ("nbytes", C.c_uint64)]
+
+
+_NP_DTYPES = {"F32": np.float32, "F16": np.float16, "F64": np.float64, "I64": np.int64, "I32": np.int32,
+              "I16": np.int16, "I8": np.int8, "U8": np.uint8, "U16": np.uint16, "U32": np.uint32,
+              "U64": np.uint64, "BOOL": np.bool_, "BF16": np.uint16}  # BF16: the raw 16-bit words
+
+
+class SafeTensors:
+    """A mapped .safetensors file (SafetensorsReader): names, info, raw arrays."""
+
+    def __init__(self, path):
+        self.h = _P()
+        check(lib().yk_safetensors_open(str(path).encode(), C.byref(self.h)))
+
+    def __len__(self) -> int:
+        return int(lib().yk_safetensors_count(self.h))
+
+    def names(self) -> list[str]:
+        out = []
+        for i in range(len(self)):
+            n = C.c_char_p()
+            check(lib().yk_safetensors_name(self.h, i, C.byref(n)))
+            out.append(n.value.decode())
+        return out
+
+    def info(self, name: str) -> TensorInfo:
+        ti = TensorInfo()
+        check(lib().yk_safetensors_info(self.h, name.encode(), C.byref(ti)))
+        return ti
+
+    def array(self, name: str) -> np.ndarray:
+        """A copy of the tensor's bytes as a numpy array (BF16 as uint16 words)."""
+        ti = self.info(name)
+        dt = np.dtype(_NP_DTYPES[ti.dtype_name.decode()])
+        raw = C.string_at(ti.data, ti.nbytes) if ti.nbytes else b""
+        return np.frombuffer(raw, dtype=dt).reshape(tuple(ti.shape[: ti.ndim])).copy()
+
+    def close(self):
+        if self.h:
+            lib().yk_safetensors_close(self.h)
+            self.h = _P()
+
+
 class Model:
     def __init__(self, engine: Engine, cfg: ModelConfig, seed: int = 1, init_std: float = 0.02, tp=None):
         """tp = (rank, world): shard `rank` of a tensor-parallel target (the engine joined the group)."""
@@ -342,6 +398,20 @@ class Model:
     def set(self, t: int, layer: int, host: np.ndarray, layout: int = LAYOUT_OUT_IN):
         a = f32(host)
         check(lib().yk_model_set_tensor(self.h, t, layer, ptr(a, C.c_float), layout))
+
+    def load(self, t: int, layer: int, host: np.ndarray, src_dtype: int, layout: int = LAYOUT_OUT_IN):
+        """yk_model_load_tensor: host holds the full stored tensor (BF16 as uint16 words)."""
+        a = np.ascontiguousarray(host)
+        want = {DTYPE_F32: np.float32, DTYPE_BF16: np.uint16, DTYPE_F16: np.float16}[src_dtype]
+        assert a.dtype == want, (a.dtype, want)
+        rows, cols = (1, a.shape[0]) if a.ndim == 1 else a.shape
+        check(lib().yk_model_load_tensor(self.h, t, layer, a.ctypes.data_as(_P), src_dtype, rows, cols, layout))
+
+    def load_safetensors(self, files, norm_offset: float = 0.0, flags: int = 0) -> int:
+        arr = (_P * len(files))(*[f.h for f in files])
+        n = C.c_int32()
+        check(lib().yk_model_load_safetensors(self.h, arr, len(files), norm_offset, flags, C.byref(n)))
+        return n.value
 
     def forward(self, pool: "KVPool", tokens, q_starts, ctx, block_tables: np.ndarray, last_n: int = 0) -> int:
         tok, qs, cl = u32(tokens), u32(q_starts), u32(ctx)

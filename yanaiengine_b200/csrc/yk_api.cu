@@ -388,13 +388,7 @@ extern "C" yk_status yk_model_get_config(const yk_model* m, yk_model_config* out
     return YK_OK;
 }
 
-// Where a logical tensor lives: base pointer, first row, row pitch (in rows), rows, cols, element size.
-struct TensorLoc {
-    uint8_t* base;
-    size_t row0, pitch_rows, rows, cols, es;
-};
-
-static yk_status locate(const yk_model* m, int32_t t, int32_t layer, TensorLoc* L) {
+yk_status yk::locate_tensor(const yk_model* m, int32_t t, int32_t layer, TensorLoc* L) {
     const auto& c = m->cfg;
     const size_t d = c.d_model, dh = c.head_dim, qd = (size_t)c.n_heads * dh, kvd = (size_t)c.n_kv_heads * dh;
     const size_t es = m->esize;
@@ -421,8 +415,8 @@ static yk_status locate(const yk_model* m, int32_t t, int32_t layer, TensorLoc* 
 
 extern "C" yk_status yk_model_tensor_shape(const yk_model* m, int32_t t, int64_t* rows, int64_t* cols) {
     YK_ARG(m && rows && cols, "null handle");
-    TensorLoc L;
-    YK_TRY(locate(m, t, 0, &L));
+    yk::TensorLoc L;
+    YK_TRY(yk::locate_tensor(m, t, 0, &L));
     *rows = (int64_t)L.rows;
     *cols = (int64_t)L.cols;
     return YK_OK;
@@ -431,8 +425,8 @@ extern "C" yk_status yk_model_tensor_shape(const yk_model* m, int32_t t, int64_t
 extern "C" yk_status yk_model_set_tensor(yk_model* m, int32_t t, int32_t layer, const float* host, int32_t layout) {
     YK_ARG(m && host, "null handle");
     YK_ARG(layout == YK_LAYOUT_OUT_IN || layout == YK_LAYOUT_IN_OUT, "layout");
-    TensorLoc L;
-    YK_TRY(locate(m, t, layer, &L));
+    yk::TensorLoc L;
+    YK_TRY(yk::locate_tensor(m, t, layer, &L));
     yk_engine* e = m->e;
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     const size_t n = L.rows * L.cols;
@@ -452,8 +446,8 @@ extern "C" yk_status yk_model_set_tensor(yk_model* m, int32_t t, int32_t layer, 
 
 extern "C" yk_status yk_model_get_tensor(yk_model* m, int32_t t, int32_t layer, float* host) {
     YK_ARG(m && host, "null handle");
-    TensorLoc L;
-    YK_TRY(locate(m, t, layer, &L));
+    yk::TensorLoc L;
+    YK_TRY(yk::locate_tensor(m, t, layer, &L));
     yk_engine* e = m->e;
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     const size_t n = L.rows * L.cols;

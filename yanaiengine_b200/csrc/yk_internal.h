@@ -284,6 +284,13 @@ yk_status gemm_run(yk_model* m, const void* W, const CUtensorMap* tmW, const voi
                    const EpiParams& ep, int force_grid = 0);
 // gate/up (GLU epilogue) then down_proj (residual epilogue) in one persistent
 // launch (one CTA per SM, a grid barrier between them); m_tok <= 256.
+// Where a logical tensor (YK_T_*) lives: base pointer, first row, row pitch (in
+// rows), rows, cols, element size (gate / up rows interleave: pitch 2).
+struct TensorLoc {
+    uint8_t* base;
+    size_t row0, pitch_rows, rows, cols, es;
+};
+yk_status locate_tensor(const yk_model* m, int32_t t, int32_t layer, TensorLoc* L);
 yk_status gemm_chain_glu_down(yk_model* m, const void* Wgu, const CUtensorMap* tmWgu, const void* X0, int n_gu, int K0,
                               const void* Wd, const CUtensorMap* tmWd, const void* X1, int n_d, int K1, int m_tok,
                               const EpiParams& eg, const EpiParams& ed);
