@@ -46,6 +46,9 @@ WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (NCCL all-re
                 "8B-shape draft replicated, bf16, k=4, T=0.8, 128 seqs x 4096 ctx")
 METRIC = "accepted tokens/sec, 8B/1B-shape k=5 batch 32, at 1/2/4/8 B200; verify HBM GB/s"
 WORKLOAD = "spec-decode step: 8B-shape target + 1B-shape draft, bf16, k=5, T=0.8, 32 seqs/GPU, ctx U[512,2048]"
+METRIC_PREFILL = "prompt tokens/sec, first scheduler step (whole prompts), 8B/1B-shape k=5 batch 32"
+WORKLOAD_PREFILL = ("prefill step: the first Scheduler.step of 32 new sequences per GPU with U[512,2048]-token "
+                    "prompts: both models over the whole prompts, then one draft / verify round; bf16, k=5, T=0.8")
 
 
 def params_bytes(c: dict, es: int = 2) -> float:
@@ -230,8 +233,9 @@ def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
 def run_yk(args, world, rank, local):
@@ -327,6 +331,7 @@ def run_yk(args, world, rank, local):
     eng.profile(False)
     # in-situ breakdown of one more step from the launch trace (first CTA past the
     # grid dependency wait, last CTA exit per launch), programmatic launch on
+    ctx_before = [int(L) + len(sch.generated(int(sid))) for L, sid in zip(lens, mine)]
     breakdown = trace_breakdown(eng, sch)
 
     peaks = measured_peaks()
@@ -370,10 +375,140 @@ def run_yk(args, world, rank, local):
                          "peak_src": peaks["src"],
                          "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])},
             "attention": {"achieved_gbs": attn_gbs, "frac": attn_gbs / peaks["hbm_gbs"], "launches": attn["launches"]},
+            "verify_step": verify_roofline(TARGET_70B if tp else TARGET, ctx_before, k, world if tp else 1,
+                                           breakdown.get("verify_forward_us"), peaks),
             "step_breakdown": breakdown,
             "clocks": clk,
         }
     sch.close()
+    sampler.close()
+    dpool.close()
+    tpool.close()
+    draft.close()
+    target.close()
+    eng.close()
+    return res, lens
+
+
+def verify_roofline(cfg: dict, ctx_before, k: int, tp_world: int, us, peaks) -> dict | None:
+    """HBM roofline of the verify forward (the target's pass over the k + 1 new
+    tokens of every sequence), timed in situ from the launch trace: algorithmic
+    bytes = the target's streamed weights (LM head included; this rank's shard
+    under tensor parallelism) + every sequence's KV context read once (the new
+    tokens' K/V included)."""
+    if not us:
+        return None
+    kv_tok = 2 * cfg["n_kv_heads"] // tp_world * cfg["head_dim"] * 2 * cfg["n_layers"]  # bytes per token, all layers
+    w = params_bytes(cfg) - cfg["vocab_size"] * cfg["d_model"] * 2  # sharded part
+    weights = w / tp_world + cfg["vocab_size"] * cfg["d_model"] * 2
+    kv = sum(c + k + 1 for c in ctx_before) * kv_tok
+    ach = (weights + kv) / (us * 1e-6) / 1e9
+    return {"us": us, "bytes": weights + kv, "weight_bytes": weights, "kv_bytes": kv, "achieved_gbs": ach,
+            "peak_gbs": peaks["hbm_gbs"], "frac": ach / peaks["hbm_gbs"], "peak_src": peaks["src"]}
+
+
+def run_prefill(args, world, rank, local):
+    """--workload prefill: the first scheduler step of a fresh batch (the reference
+    feeds whole prompts there: S/Scheduler.swift:68-69,201-202).  Each timed step
+    is a new scheduler over the same 32 prompt lengths per GPU (weak scaling);
+    the KV pools and models are reused."""
+    from yanaiengine_b200 import abi, dp
+
+    import torch
+
+    k, B, T = args.k, args.batch, args.temperature
+    glens = dp.global_lengths(B, world, seed=7)
+    mine = dp.partition(glens, world)[rank]
+    lens = glens[mine]
+    tot = int(lens.sum())
+    eng = abi.Engine(local)
+    tcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=tot + B * (k + 1) + 64, max_seqs=B)
+    dcfg = abi.make_config(**DRAFT, dtype=abi.DTYPE_BF16, max_tokens=tot + B * (k + 1) + 64, max_seqs=B)
+    blocks = int(sum(np.ceil((lens + 2 * (k + 1) + 32) / 16))) + 64
+    target = abi.Model(eng, tcfg, seed=1, init_std=0.02)
+    draft = abi.Model(eng, dcfg, seed=2, init_std=0.02)
+    tpool = abi.KVPool(eng, target.cfg, blocks)
+    dpool = abi.KVPool(eng, dcfg, blocks)
+    sampler = abi.Sampler(eng, B, k, TARGET["vocab_size"])
+    rng = np.random.default_rng(7 + 1000 * rank)
+    prompts = [rng.integers(0, TARGET["vocab_size"], int(L)).tolist() for L in lens]
+
+    def fresh():
+        sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + rank)
+        for i, pr in enumerate(prompts):
+            sch.submit(pr, max_tokens=1 << 30, stop_token=-1, seq_id=int(mine[i]))
+        return sch
+
+    for _ in range(args.warmup):
+        sch = fresh()
+        sch.step()
+        sch.close()
+    eng.sync()
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.5)
+    launches0 = eng.launches()
+    dev_ms = wall = 0.0
+    h2d = 0
+    barrier(world)
+    for _ in range(args.steps):
+        sch = fresh()
+        eng.sync()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        sch.step()
+        ev1.record(stream)
+        eng.sync()
+        wall += time.perf_counter() - t0
+        dev_ms += ev0.elapsed_time(ev1)
+        # prompts (target and draft), positions and page tables in; tokens out
+        h2d += 2 * (tot + B * (k + 1)) * 4 * 3
+        sch.close()
+    barrier(world)
+    clk = clocks.stop() if rank == 0 else None
+    launches = eng.launches() - launches0
+    max_dev_s = allreduce_max(world, dev_ms / 1e3)
+    max_wall = allreduce_max(world, wall)
+    tot_tokens = allreduce_sum(world, float(tot * args.steps))
+    # tensor roofline of the GEMMs: one more step with per-launch CUDA events
+    eng.profile(True)
+    sch = fresh()
+    sch.step()
+    sch.close()
+    gemm = eng.profile_read(0)
+    attn = eng.profile_read(1)
+    eng.profile(False)
+    peaks = measured_peaks()
+    res = None
+    if rank == 0:
+        tflops = gemm["flops"] / (gemm["ms"] / 1e3) / 1e12 if gemm["ms"] > 0 else 0.0
+        res = {
+            "metric": METRIC_PREFILL, "value": tot_tokens / max_dev_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_dev_s * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init weights N(0,0.02), random prompt token ids",
+            "config": {"workload": WORKLOAD_PREFILL, "global_batch": B * world, "seqs_per_gpu": B,
+                       "prompt_tokens_per_gpu": tot, "k": k, "temperature": T, "parallelism": f"dp{world} (replicas)",
+                       "l2": "inputs larger than L2 (weights and prompts stream once per step)"},
+            "e2e": {"value": tot_tokens / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d / args.steps),
+                    "d2h_bytes_per_step": int(B * (k + 2) * 4 * (k + 1))},
+            "gpu_launches": int(launches),
+            # the GEMMs run back to back inside a ~1 s step under the power cap: the
+            # sustained cuBLAS figure is the denominator (the burst one beside it)
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops_sustained"],
+                         "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops_sustained"],
+                         "frac_of_burst": tflops / peaks["bf16_tflops"], "traffic": None, "kernel": "gemm_tc_kernel",
+                         "peak_src": peaks["src"] + " (sustained: a seconds-long step under the power cap)",
+                         "share_of_step": gemm["ms"] / (max_dev_s * 1e3 / args.steps),
+                         "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])},
+            "attention": {"ms": attn["ms"], "launches": attn["launches"]},
+            "cpu_baseline": None,
+            "clocks": clk,
+        }
     sampler.close()
     dpool.close()
     tpool.close()
@@ -417,14 +552,23 @@ def trace_breakdown(eng, sch, cap: int = 8192) -> dict:
     span = float(end.max() - start[0])
     out = {"step_us": span / 1e3, "launches": int(len(ids)), "busy_us": {}, "idle_us": 0.0, "count": {}}
     prev_end = start[0]
+    names, shares = [], []
     for k, s0, e0 in zip(kind, start, end):
         share = max(0, e0 - prev_end)
         idle = min(share, max(0, s0 - prev_end))
         name = trace_name(int(k))
+        names.append(name)
+        shares.append(share)
         out["busy_us"][name] = out["busy_us"].get(name, 0.0) + (share - idle) / 1e3
         out["count"][name] = out["count"].get(name, 0) + 1
         out["idle_us"] += idle / 1e3
         prev_end = max(prev_end, e0)
+    # the verify forward: the last embedding launch through the last LM-head GEMM (the
+    # target's layers, its final norm and its logits; hand-offs included)
+    last_lm = max((i for i, n in enumerate(names) if n.startswith("gemm_logits")), default=-1)
+    first = max((i for i, n in enumerate(names[: last_lm + 1]) if n == "embed"), default=-1)
+    if last_lm >= 0 and first >= 0:
+        out["verify_forward_us"] = round(sum(shares[first: last_lm + 1]) / 1e3, 1)
     out["busy_us"] = {k: round(v, 1) for k, v in sorted(out["busy_us"].items(), key=lambda x: -x[1])}
     out["idle_us"] = round(out["idle_us"], 1)
     out["step_us"] = round(out["step_us"], 1)
@@ -441,8 +585,9 @@ def main():
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--temperature", type=float, default=0.8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="8b-dp", choices=["8b-dp", "70b-tp"],
-                    help="8b-dp: the headline 8B/1B data-parallel step; 70b-tp: 70B-shape target over all GPUs")
+    ap.add_argument("--workload", default="8b-dp", choices=["8b-dp", "70b-tp", "prefill"],
+                    help="8b-dp: the headline 8B/1B data-parallel step; 70b-tp: 70B-shape target over all GPUs; "
+                         "prefill: the first scheduler step of a fresh batch (whole prompts)")
     args = ap.parse_args()
     if args.workload == "70b-tp":
         # the 70B configuration: batch 128, k = 4 (other flags as given)
@@ -476,7 +621,7 @@ def main():
         }))
         return
 
-    res, lens = run_yk(args, world, rank, local)
+    res, lens = (run_prefill if args.workload == "prefill" else run_yk)(args, world, rank, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline and args.workload == "8b-dp":
             sample = cpu_step_sample(lens, args.k, args.temperature, nthreads)

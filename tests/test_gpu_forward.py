@@ -27,17 +27,18 @@ def _greedy_agree(g, o, tol_abs):
     assert (np.argmax(g, 1)[clear] == np.argmax(o, 1)[clear]).all()
 
 
-def _drive(engine, oracle, cfg, dtype, emulate, tol, init_std=0.02, steps=3, k=4):
-    m, pool = gpu_model(engine, cfg, dtype, seed=3, num_blocks=NB, init_std=init_std)
+def _drive(engine, oracle, cfg, dtype, emulate, tol, init_std=0.02, steps=3, k=4,
+           prefill=((0, 17), (1, 40), (2, 5)), nb=NB, max_tokens=256):
+    m, pool = gpu_model(engine, cfg, dtype, seed=3, num_blocks=nb, init_std=init_std, max_tokens=max_tokens)
     try:
-        orc = oracle_twin(oracle, m, cfg, NB, emulate_bf16=emulate)
-        pt = PageTables(NB)
+        orc = oracle_twin(oracle, m, cfg, nb, emulate_bf16=emulate)
+        pt = PageTables(nb)
         rng = np.random.default_rng(1)
         V = cfg["vocab_size"]
         lens = {0: 0, 1: 0, 2: 0}
-        # ragged prefill: 3 sequences, 17 / 40 / 5 tokens (page-boundary crossings)
+        # ragged prefill: 3 sequences, by default 17 / 40 / 5 tokens (page-boundary crossings)
         batch = []
-        for sid, n in ((0, 17), (1, 40), (2, 5)):
+        for sid, n in prefill:
             batch.append((sid, rng.integers(0, V, n).tolist(), 0))
             lens[sid] = n
         g, o = forward_pair(m, pool, orc, pt, batch)
@@ -80,6 +81,15 @@ def test_fp32_tiny(engine, oracle):
 
 def test_bf16_tiny_vs_bf16_emulating_oracle(engine, oracle):
     _drive(engine, oracle, TINY, abi.DTYPE_BF16, True, 2e-2)
+
+
+def test_bf16_long_ragged_prefill(engine, oracle):
+    """Prefill inside the batch (the scheduler's first step feeds whole prompts,
+    S/Scheduler.swift:68-69,201-202): 1150 tokens in one step -- several 256-token
+    GEMM tiles, many 64-row attention query tiles per sequence, the RMSNorm kernels
+    instead of the folded norm -- then verify steps on the long contexts."""
+    _drive(engine, oracle, TINY, abi.DTYPE_BF16, True, 2e-2, steps=2,
+           prefill=((0, 300), (1, 700), (2, 150)), nb=96, max_tokens=1216)
 
 
 def test_bf16_tiny_vs_fp32_oracle(engine, oracle):
