@@ -54,10 +54,12 @@ yk_status yk_engine::up_acquire(size_t bytes, int* slot, uint8_t** host) {
     return YK_OK;
 }
 
-yk_status yk_engine::up_submit(int slot, void* dst, size_t bytes) {
+yk_status yk_engine::up_submit(int slot, void* dst, size_t bytes) { return up_submit_on(slot, dst, bytes, stream); }
+
+yk_status yk_engine::up_submit_on(int slot, void* dst, size_t bytes, cudaStream_t on) {
     UpSlot& u = up[slot];
-    YK_CHECK_CUDA(cudaMemcpyAsync(dst, u.host, bytes, cudaMemcpyHostToDevice, stream));
-    YK_CHECK_CUDA(cudaEventRecord(u.done, stream));
+    YK_CHECK_CUDA(cudaMemcpyAsync(dst, u.host, bytes, cudaMemcpyHostToDevice, on));
+    YK_CHECK_CUDA(cudaEventRecord(u.done, on));
     return YK_OK;
 }
 
@@ -82,6 +84,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     e->device = device;
     YK_CHECK_CUDA(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device));
     YK_CHECK_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    YK_CHECK_CUDA(cudaStreamCreateWithFlags(&e->up_stream, cudaStreamNonBlocking));
     YK_CHECK_CUDA(cudaMalloc(&e->d_err, sizeof(uint32_t)));
     YK_CHECK_CUDA(cudaMemset(e->d_err, 0, sizeof(uint32_t)));
     void* fn = nullptr;
@@ -98,6 +101,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     if (const char* v = std::getenv("YK_GEMM_PUSH_MIN")) e->gemm_push_min = std::max(0, std::atoi(v));
     if (const char* v = std::getenv("YK_FUSE_NORM")) e->fuse_norm = std::atoi(v) != 0;
     if (const char* v = std::getenv("YK_GEMM_CHAIN")) e->gemm_chain = std::atoi(v) != 0;
+    if (const char* v = std::getenv("YK_META_ASYNC")) e->meta_async = std::atoi(v) != 0;
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
     yk_status s = e->ensure_pinned((size_t)4 << 20);
@@ -110,6 +114,7 @@ extern "C" void yk_engine_destroy(yk_engine* e) {
     if (!e) return;
     cudaSetDevice(e->device);
     cudaStreamSynchronize(e->stream);
+    if (e->up_stream) cudaStreamSynchronize(e->up_stream);
     if (e->pinned) cudaFreeHost(e->pinned);
     for (auto& u : e->up) {
         if (u.host) cudaFreeHost(u.host);
@@ -119,6 +124,7 @@ extern "C" void yk_engine_destroy(yk_engine* e) {
     if (e->trace_rec) cudaFree(e->trace_rec);
     yk::tp_destroy(e);
     if (e->stream) cudaStreamDestroy(e->stream);
+    if (e->up_stream) cudaStreamDestroy(e->up_stream);
     delete e;
 }
 
@@ -372,7 +378,12 @@ extern "C" void yk_model_destroy(yk_model* m) {
     cudaSetDevice(m->e->device);
     cudaStreamSynchronize(m->e->stream);
     for (void* p : m->allocations) cudaFree(p);
-    if (m->meta) cudaFree(m->meta);
+    if (m->e->up_stream) cudaStreamSynchronize(m->e->up_stream);
+    for (int i = 0; i < yk_model::META_SLOTS; ++i) {
+        if (m->meta[i]) cudaFree(m->meta[i]);
+        if (m->meta_copied[i]) cudaEventDestroy(m->meta_copied[i]);
+        if (m->meta_free[i]) cudaEventDestroy(m->meta_free[i]);
+    }
     if (m->attn_ws) cudaFree(m->attn_ws);
     if (m->attn_counters) cudaFree(m->attn_counters);
     if (m->attn_stamps) cudaFree(m->attn_stamps);
@@ -612,14 +623,34 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
     }
     const size_t nattn = it_g.size() + cb_g.size() + it_w.size() + cb_w.size();
     const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R + nattn;
-    // (a device buffer still read by earlier launches is freed only after cudaFree's implicit synchronisation)
-    if (nmeta > m->meta_cap) {
-        if (m->meta) cudaFree(m->meta);
-        m->meta = nullptr;
-        m->meta_cap = 0;
-        YK_CHECK_CUDA(cudaMalloc(&m->meta, std::max<size_t>(nmeta * 2, 4096) * 4));
-        m->meta_cap = std::max<size_t>(nmeta * 2, 4096);
+    // Metadata slot of this call.  Async: the upload runs on the engine's upload
+    // stream as soon as the slot's previous forward (META_SLOTS calls ago) and the
+    // work enqueued after it are done, so it overlaps the kernels still running;
+    // the compute stream waits only for the copy's event.
+    const bool async = e->meta_async;
+    const int ms = async ? (int)(m->meta_calls % yk_model::META_SLOTS) : 0;
+    if (async) {
+        for (int i = 0; i < yk_model::META_SLOTS; ++i) {
+            if (!m->meta_copied[i]) YK_CHECK_CUDA(cudaEventCreateWithFlags(&m->meta_copied[i], cudaEventDisableTiming));
+            if (!m->meta_free[i]) YK_CHECK_CUDA(cudaEventCreateWithFlags(&m->meta_free[i], cudaEventDisableTiming));
+        }
+        // everything enqueued so far (the previous call's forward and whatever read
+        // its metadata after it) releases the previous call's slot
+        if (m->meta_calls > 0) {
+            const int prev = (int)((m->meta_calls - 1) % yk_model::META_SLOTS);
+            YK_CHECK_CUDA(cudaEventRecord(m->meta_free[prev], e->stream));
+        }
+        YK_CHECK_CUDA(cudaStreamWaitEvent(e->up_stream, m->meta_free[ms], 0));
     }
+    // (a device buffer still read by earlier launches is freed only after cudaFree's implicit synchronisation)
+    if (nmeta > m->meta_cap[ms]) {
+        if (m->meta[ms]) cudaFree(m->meta[ms]);
+        m->meta[ms] = nullptr;
+        m->meta_cap[ms] = 0;
+        YK_CHECK_CUDA(cudaMalloc(&m->meta[ms], std::max<size_t>(nmeta * 2, 4096) * 4));
+        m->meta_cap[ms] = std::max<size_t>(nmeta * 2, 4096);
+    }
+    int32_t* const meta = m->meta[ms];
     int up_slot = 0;
     uint8_t* up_host = nullptr;
     YK_TRY(e->up_acquire(nmeta * 4, &up_slot, &up_host));  // no wait for the device: a ring of staging slots
@@ -658,9 +689,16 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
             w += v->size();
         }
     }
-    YK_TRY(e->up_submit(up_slot, m->meta, nmeta * 4));
+    if (async) {
+        YK_TRY(e->up_submit_on(up_slot, meta, nmeta * 4, e->up_stream));
+        YK_CHECK_CUDA(cudaEventRecord(m->meta_copied[ms], e->up_stream));
+        YK_CHECK_CUDA(cudaStreamWaitEvent(e->stream, m->meta_copied[ms], 0));
+        m->meta_calls++;
+    } else {
+        YK_TRY(e->up_submit(up_slot, meta, nmeta * 4));
+    }
     {
-        const int32_t* a = m->meta + attn_off;
+        const int32_t* a = meta + attn_off;
         m->cur.attn_items[0] = a;
         m->cur.n_items[0] = (int)(it_g.size() / 7);
         a += it_g.size();
@@ -673,7 +711,7 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         m->cur.attn_comb[1] = a;
         m->cur.n_comb[1] = (int)(cb_w.size() / 5);
     }
-    const int32_t* dm = m->meta;
+    const int32_t* dm = meta;
     m->cur.tokens = dm;
     m->cur.pos = dm + T;
     m->cur.slot = dm + 2 * T;

@@ -55,6 +55,8 @@ struct yk_engine {
     int device = 0;
     int num_sms = 148;
     cudaStream_t stream = nullptr;
+    cudaStream_t up_stream = nullptr;    // forward metadata uploads, ahead of `stream` (event-ordered)
+    bool meta_async = true;              // env YK_META_ASYNC=0: upload on `stream`, in line
     uint32_t* d_err = nullptr;           // device error word
     uint8_t* pinned = nullptr;           // host staging (downloads, and uploads that synchronise anyway)
     size_t pinned_bytes = 0;
@@ -96,6 +98,8 @@ struct yk_engine {
     // up_submit copies it to `dst` on the engine stream.
     yk_status up_acquire(size_t bytes, int* slot, uint8_t** host);
     yk_status up_submit(int slot, void* dst, size_t bytes);
+    // the same copy on stream `on` (its done event recorded there)
+    yk_status up_submit_on(int slot, void* dst, size_t bytes, cudaStream_t on);
     void prof_begin(int cls, double bytes, double flops);
     void prof_end();
     void prof_resolve();
@@ -145,9 +149,15 @@ struct yk_model {
     float* rope_denom = nullptr;  // [dh/2]
     float2* rope_tab = nullptr;   // [max_tokens x dh/2] (cos, sin) of this step's token positions
     float* norm_ss = nullptr;     // [d/32 x max_tokens] fused RMSNorm: 32-element group sums of squares
-    // step metadata (device), packed as int32
-    int32_t* meta = nullptr;
-    size_t meta_cap = 0;       // int32 elements
+    // step metadata (device), packed as int32: a ring of buffers, one per forward
+    // call, so that the next call's upload (on the engine's upload stream) runs
+    // while this call's kernels still read theirs
+    static constexpr int META_SLOTS = 4;
+    int32_t* meta[META_SLOTS] = {};
+    size_t meta_cap[META_SLOTS] = {};          // int32 elements
+    cudaEvent_t meta_copied[META_SLOTS] = {};  // the slot's upload has landed (upload stream)
+    cudaEvent_t meta_free[META_SLOTS] = {};    // every reader of the slot's last forward is done (compute stream)
+    uint64_t meta_calls = 0;
     int32_t last_rows = 0;
     struct {
         const int32_t *tokens, *pos, *slot, *seq, *q_starts, *ctx, *bt, *rows;

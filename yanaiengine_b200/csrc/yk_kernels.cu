@@ -40,6 +40,52 @@ __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict
         return;
     }
     const WT* row = E + (size_t)tok * d;
+    if constexpr (sizeof(WT) == 2) {
+        if ((d & 31) == 0) {
+            // bf16: 8 consecutive elements per thread (one 16-byte load), every load of
+            // the row in flight at once; a 32-element group is 4 neighbouring lanes
+            for (int i0 = threadIdx.x * 8; i0 - threadIdx.x * 8 < d; i0 += blockDim.x * 8) {
+                const bool on = i0 < d;
+                float v[8];
+                if (on) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(row + i0);
+                    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        v[2 * k] = __uint_as_float(w[k] << 16);
+                        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+                    }
+                    float4* hr = reinterpret_cast<float4*>(h + (size_t)t * d + i0);
+                    hr[0] = make_float4(v[0], v[1], v[2], v[3]);
+                    hr[1] = make_float4(v[4], v[5], v[6], v[7]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) v[k] = 0.f;
+                }
+                if (fn.g) {
+                    float ss = 0.f;
+                    if (on) {
+                        const float4 g0 = *reinterpret_cast<const float4*>(fn.g + i0);
+                        const float4 g1 = *reinterpret_cast<const float4*>(fn.g + i0 + 4);
+                        const __nv_bfloat162 x0 = __floats2bfloat162_rn(v[0] * g0.x, v[1] * g0.y);
+                        const __nv_bfloat162 x1 = __floats2bfloat162_rn(v[2] * g0.z, v[3] * g0.w);
+                        const __nv_bfloat162 x2 = __floats2bfloat162_rn(v[4] * g1.x, v[5] * g1.y);
+                        const __nv_bfloat162 x3 = __floats2bfloat162_rn(v[6] * g1.z, v[7] * g1.w);
+                        *reinterpret_cast<uint4*>(fn.x + (size_t)t * d + i0) =
+                            make_uint4(*reinterpret_cast<const uint32_t*>(&x0), *reinterpret_cast<const uint32_t*>(&x1),
+                                       *reinterpret_cast<const uint32_t*>(&x2), *reinterpret_cast<const uint32_t*>(&x3));
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+                    }
+                    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                    if (on && (threadIdx.x & 3) == 0) fn.ss[(size_t)(i0 >> 5) * gridDim.x + t] = ss;
+                }
+            }
+            if (threadIdx.x == 0) trace_mark(tr, TR_END);
+            return;
+        }
+    }
     if (!fn.g) {
         for (int i = threadIdx.x; i < d; i += blockDim.x) h[(size_t)t * d + i] = to_f32(row[i]);
     } else {
