@@ -196,10 +196,12 @@ struct AttnCfg {
     // A consumer warp takes chunks of CP pages.  Stages: a multiple of 4*CP (4 =
     // every warps-per-m-tile value), so a consumer that waits only on its own
     // chunks never waits two phases ahead of a stage.
-    // Ring depth: with one query m-tile (decode-like, head_dim 64) each of the 4
-    // consumer warps owns every 4th chunk, so 16 pages keep two of its chunks in
-    // flight (a warp's chunk time is mostly page latency).
-    static constexpr int CP = DH == 256 ? 1 : 2;
+    // Ring depth: a warp's chunk time is mostly page latency, so what sets a
+    // CTA's rate is how many pages the ring holds beyond the ones in use.  With
+    // one-page chunks only one page per consuming warp is in use (decode-like,
+    // head_dim 64: 4 of 16 pages; verify, 2 m-tiles x 2 warps: 2 of 8), the rest
+    // stream ahead (two-page chunks: 1.5 % slower per step, target and draft).
+    static constexpr int CP = 1;
     static constexpr int S = DH == 256 ? 4 : (DH == 64 ? 16 : 8);
     static constexpr int CTAS_PER_SM = DH == 64 ? 3 : (DH == 128 ? 2 : 1);  // register-limited
     static constexpr int LDQ = DH + 8;                       // padded Q row (elements)
