@@ -201,11 +201,15 @@ struct AttnCfg {
     // one-page chunks only one page per consuming warp is in use (decode-like,
     // head_dim 64: 4 of 16 pages; verify, 2 m-tiles x 2 warps: 2 of 8), the rest
     // stream ahead (two-page chunks: 1.5 % slower per step, target and draft).
+    // head_dim 128: 12 pages (the Q tile lives in registers, so two CTAs per SM
+    // still fit; 8 pages: verify attention 46.8 -> 47.9 us).
     static constexpr int CP = 1;
-    static constexpr int S = DH == 256 ? 4 : (DH == 64 ? 16 : 8);
+    static constexpr int S = DH == 256 ? 4 : (DH == 64 ? 16 : 12);
     static constexpr int CTAS_PER_SM = DH == 64 ? 3 : (DH == 128 ? 2 : 1);  // register-limited
     static constexpr int LDQ = DH + 8;                       // padded Q row (elements)
-    static constexpr size_t Q_BYTES = (size_t)AT_ROWS * LDQ * 2;
+    // head_dim <= 128: Q goes straight from global memory into the score MMA's A
+    // fragments (registers), no shared-memory copy; the room goes to the ring
+    static constexpr size_t Q_BYTES = DH <= 128 ? 0 : (size_t)AT_ROWS * LDQ * 2;
     // after the page loop the ring holds the merge: per-warp O and (m, l), per-row
     // weights; or, for the last CTA of a split group, per-row split weights
     static constexpr size_t RED_BYTES = ((size_t)4 * 16 * DH + 4 * 16 * 2 + 64 * 4 + 64 * 2) * 4;
@@ -330,19 +334,21 @@ __global__ void __launch_bounds__(AT_THREADS, AttnCfg<DH>::CTAS_PER_SM)
     const int my_mt = warp / wpm, my_part = warp % wpm;
     const bool active = my_mt < MT;
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);
-    // stage Q (64 rows x DH, padded rows), zero rows beyond `rows`
-    constexpr int CPR = DH / 8;  // 16-byte chunks per row
-    for (int i = threadIdx.x; i < AT_ROWS * CPR; i += 128) {
-        const int r = i / CPR, c = i % CPR;
-        const int rr = qt * AT_ROWS + r;
-        const bool ok = r < rows;
-        const __nv_bfloat16* src = q;
-        if (ok) src = q + ((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + c * 8;
-        cp_async16(smem_u32(sQ + r * C::LDQ + c * 8), src, ok ? 16u : 0u);
+    if constexpr (DH > 128) {
+        // stage Q (64 rows x DH, padded rows), zero rows beyond `rows`
+        constexpr int CPR = DH / 8;  // 16-byte chunks per row
+        for (int i = threadIdx.x; i < AT_ROWS * CPR; i += 128) {
+            const int r = i / CPR, c = i % CPR;
+            const int rr = qt * AT_ROWS + r;
+            const bool ok = r < rows;
+            const __nv_bfloat16* src = q;
+            if (ok) src = q + ((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + c * 8;
+            cp_async16(smem_u32(sQ + r * C::LDQ + c * 8), src, ok ? 16u : 0u);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        consumer_bar();
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    consumer_bar();
 
     const int r0 = my_mt * 16 + (lane >> 2), r1 = r0 + 8;
     const int pos0 = (r0 < rows) ? ctx - n + (qt * AT_ROWS + r0) / G : -1;
@@ -364,10 +370,25 @@ __global__ void __launch_bounds__(AT_THREADS, AttnCfg<DH>::CTAS_PER_SM)
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     uint32_t qf[DH <= 128 ? KS : 1][4];
     if (DH <= 128 && active) {
+        // A fragments of the m16k16 tiles: registers {0,1,2,3} hold rows (r, r+8, r,
+        // r+8), columns (c, c, c+8, c+8) with r = lane/4, c = 2*(lane%4) -- the
+        // ldmatrix.x4 order; rows past `rows` are zero queries
+        const uint32_t* qrow[2] = {nullptr, nullptr};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = my_mt * 16 + (lane >> 2) + 8 * h;
+            const int rr = qt * AT_ROWS + r;
+            if (r < rows)
+                qrow[h] = reinterpret_cast<const uint32_t*>(
+                    q + ((size_t)(qs0 + rr / G) * p.H + (size_t)g * G + rr % G) * DH + 2 * (lane & 3));
+        }
 #pragma unroll
         for (int ks = 0; ks < (DH <= 128 ? KS : 1); ++ks) {
-            const uint32_t a = smem_u32(sQ + (my_mt * 16 + (lane & 15)) * C::LDQ + ks * 16 + (lane >> 4) * 8);
-            ldsm_x4(a, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+            // (L2 loads: Q was written by the previous kernel, after PDL overlap)
+            qf[ks][0] = qrow[0] ? __ldcg(qrow[0] + ks * 8) : 0u;
+            qf[ks][1] = qrow[1] ? __ldcg(qrow[1] + ks * 8) : 0u;
+            qf[ks][2] = qrow[0] ? __ldcg(qrow[0] + ks * 8 + 4) : 0u;
+            qf[ks][3] = qrow[1] ? __ldcg(qrow[1] + ks * 8 + 4) : 0u;
         }
     }
     constexpr int CP = C::CP;          // pages per chunk
