@@ -43,6 +43,19 @@ yk_status ykh_submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_
  * prefill. */
 yk_status ykh_submit_cached(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
                             int64_t stop_token, uint32_t seq_id);
+/* Streaming submission: the InferenceServer's per-request callbacks
+ * (onTokenGenerated / onCompletion, S/InferenceServer.swift:118-126,167-176) at
+ * the token-id level (detokenisation stays with the server).  on_tokens gets
+ * each step's emitted run of the request (accepted drafts + the target's
+ * token), in order; on_done is called once, when the request finishes (stop
+ * token or max_tokens), with its generated-token count.  Both run inside
+ * ykh_step on the calling thread, after the step's verification; either may be
+ * null.  The concatenated runs equal ykh_generated's list. */
+typedef void (*ykh_on_tokens)(void* user, uint32_t seq_id, const uint32_t* tokens, int32_t n);
+typedef void (*ykh_on_done)(void* user, uint32_t seq_id, int32_t n_generated);
+yk_status ykh_submit_stream(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
+                            int64_t stop_token, uint32_t seq_id, ykh_on_tokens on_tokens, ykh_on_done on_done,
+                            void* user);
 /* One speculative step over the running batch (admission as runLoop,
  * S/Scheduler.swift:122-129).  *emitted = tokens appended across the batch. */
 yk_status ykh_step(ykh_scheduler* s, int32_t* emitted);

@@ -127,3 +127,41 @@ def test_scheduler_sampled_batch_runs(engine):
         d.close()
         tp.close()
         t.close()
+
+
+def test_scheduler_streaming_callbacks(engine):
+    """ykh_submit_stream (the server's onTokenGenerated / onCompletion): every
+    step's emitted run arrives in order, the runs concatenate to the generated
+    list, completion fires once per request (stop token or max_tokens), and plain
+    and streaming requests share a batch."""
+    t, tp = gpu_model(engine, TINY, abi.DTYPE_BF16, seed=1, num_blocks=128, max_tokens=256, max_seqs=8)
+    d, dp = gpu_model(engine, dict(TINY, n_layers=1), abi.DTYPE_BF16, seed=2, num_blocks=128, max_tokens=256,
+                      max_seqs=8)
+    s = abi.Sampler(engine, 8, 4, TINY["vocab_size"])
+    sch = abi.Scheduler(t, tp, d, dp, s, 4, 0.8, 5)
+    runs, done = {}, {}
+    try:
+        rng = np.random.default_rng(1)
+        for i in range(4):
+            sch.submit_stream(rng.integers(0, 512, 12 + 5 * i).tolist(), max_tokens=15,
+                              on_tokens=lambda sid, toks: runs.setdefault(sid, []).append(toks),
+                              on_done=lambda sid, n: done.setdefault(sid, []).append(n), seq_id=i)
+        sch.submit(rng.integers(0, 512, 9).tolist(), max_tokens=15, stop_token=-1, seq_id=9)
+        for _ in range(40):
+            if sch.running() == 0 and sch.waiting() == 0:
+                break
+            sch.step()
+        assert sch.running() == 0 and sch.waiting() == 0
+        for i in range(4):
+            g = sch.generated(i)
+            assert [x for run in runs[i] for x in run] == g
+            assert all(1 <= len(run) <= 5 for run in runs[i])  # at most k + 1 tokens per step
+            assert done[i] == [len(g)] and len(g) >= 15
+        assert 9 not in runs and 9 not in done and len(sch.generated(9)) >= 15
+    finally:
+        sch.close()
+        s.close()
+        dp.close()
+        d.close()
+        tp.close()
+        t.close()

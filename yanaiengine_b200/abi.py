@@ -135,6 +135,8 @@ _HOST_PROTOS = {
     "ykh_scheduler_destroy": (None, [_P]),
     "ykh_submit": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
     "ykh_submit_cached": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
+    "ykh_submit_stream": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32, C.c_void_p,
+                                      C.c_void_p, C.c_void_p]),
     "ykh_step": (C.c_int32, [_P, _I32P]),
     "ykh_num_running": (C.c_int32, [_P]),
     "ykh_num_waiting": (C.c_int32, [_P]),
@@ -549,6 +551,23 @@ class Scheduler:
         p = u32(prompt)
         fn = host_lib().ykh_submit_cached if cached else host_lib().ykh_submit
         check(fn(self.h, ptr(p, C.c_uint32), len(p), max_tokens, stop_token, seq_id))
+
+    _ON_TOKENS = C.CFUNCTYPE(None, C.c_void_p, C.c_uint32, C.POINTER(C.c_uint32), C.c_int32)
+    _ON_DONE = C.CFUNCTYPE(None, C.c_void_p, C.c_uint32, C.c_int32)
+
+    def submit_stream(self, prompt, max_tokens: int, on_tokens=None, on_done=None, stop_token: int = -1,
+                      seq_id: int = 0):
+        """ykh_submit_stream: on_tokens(seq_id, list_of_token_ids) per emitted run,
+        on_done(seq_id, n_generated) once; called inside step()."""
+        p = u32(prompt)
+        ct = self._ON_TOKENS(lambda _u, sid, toks, n: on_tokens(int(sid), [toks[i] for i in range(n)])) \
+            if on_tokens else C.cast(None, self._ON_TOKENS)
+        cd = self._ON_DONE(lambda _u, sid, n: on_done(int(sid), int(n))) if on_done else C.cast(None, self._ON_DONE)
+        if not hasattr(self, "_callbacks"):
+            self._callbacks = []
+        self._callbacks.append((ct, cd))  # the C side keeps the pointers until the request is done
+        check(host_lib().ykh_submit_stream(self.h, ptr(p, C.c_uint32), len(p), max_tokens, stop_token, seq_id,
+                                           C.cast(ct, C.c_void_p), C.cast(cd, C.c_void_p), None))
 
     def step(self) -> int:
         e = C.c_int32()

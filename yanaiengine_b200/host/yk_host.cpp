@@ -93,6 +93,10 @@ struct SequenceRequest {
     int max_tokens = 0;
     int64_t stop_token = -1;
     bool finished = false;
+    // streaming (the server's onTokenGenerated / onCompletion), optional
+    ykh_on_tokens on_tokens = nullptr;
+    ykh_on_done on_done = nullptr;
+    void* user = nullptr;
     int total() const { return (int)(prompt.size() + generated.size()); }
     uint32_t at(int i) const { return i < (int)prompt.size() ? prompt[i] : generated[i - prompt.size()]; }
 };
@@ -146,10 +150,14 @@ extern "C" void ykh_scheduler_destroy(ykh_scheduler* s) {
 }
 
 static yk_status submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens, int64_t stop,
-                        uint32_t seq_id, bool cached) {
+                        uint32_t seq_id, bool cached, ykh_on_tokens on_tokens = nullptr,
+                        ykh_on_done on_done = nullptr, void* user = nullptr) {
     if (!s || !prompt || n <= 0) return YK_ERR_ARG;
     auto r = std::make_unique<SequenceRequest>();
     r->id = seq_id;
+    r->on_tokens = on_tokens;
+    r->on_done = on_done;
+    r->user = user;
     r->prompt.assign(prompt, prompt + n);
     r->max_tokens = max_tokens;
     r->stop_token = stop;
@@ -169,6 +177,11 @@ static yk_status submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int
 extern "C" yk_status ykh_submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
                                 int64_t stop_token, uint32_t seq_id) {
     return submit(s, prompt, n, max_tokens, stop_token, seq_id, false);
+}
+extern "C" yk_status ykh_submit_stream(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
+                                       int64_t stop_token, uint32_t seq_id, ykh_on_tokens on_tokens,
+                                       ykh_on_done on_done, void* user) {
+    return submit(s, prompt, n, max_tokens, stop_token, seq_id, false, on_tokens, on_done, user);
 }
 extern "C" yk_status ykh_submit_cached(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int32_t max_tokens,
                                        int64_t stop_token, uint32_t seq_id) {
@@ -287,6 +300,7 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
                 break;
             }
         if ((int)r->generated.size() >= r->max_tokens) r->finished = true;
+        if (r->on_tokens && cnt > 0) r->on_tokens(r->user, r->id, r->generated.data() + r->generated.size() - cnt, cnt);
         emitted += cnt;
         s->n_accepted += a;
     }
@@ -298,6 +312,7 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
         if ((*it)->finished) {
             (*it)->cache->reset();
             (*it)->draft_cache->reset();
+            if ((*it)->on_done) (*it)->on_done((*it)->user, (*it)->id, (int32_t)(*it)->generated.size());
             s->done.push_back(std::move(*it));
             it = s->running.erase(it);
         } else {
