@@ -65,6 +65,13 @@ int32_t   ykh_num_waiting(const ykh_scheduler* s);
 yk_status ykh_generated(const ykh_scheduler* s, uint32_t seq_id, uint32_t* out, int32_t cap, int32_t* n);
 /* Counters since creation: steps, emitted tokens, accepted draft tokens. */
 yk_status ykh_counters(const ykh_scheduler* s, int64_t* steps, int64_t* emitted, int64_t* accepted);
+/* Sliding-window block reclamation (on by default).  For a model whose every
+ * layer is windowed (window > 0, window_layer_parity < 0), each step returns
+ * the pages wholly before current_position - window + 1 to the allocator: no
+ * later query reads them.  The reference never frees them
+ * (S/PagedKVCache.swift:65-85).  A model with a global layer frees nothing
+ * (one page holds every layer's K/V). */
+yk_status ykh_set_window_reclaim(ykh_scheduler* s, int32_t on);
 /* BlockAllocator.usage of the target / draft pools (S/BlockAllocator.swift:56-58). */
 float     ykh_usage(const ykh_scheduler* s, int32_t draft);
 

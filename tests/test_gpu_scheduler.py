@@ -165,3 +165,53 @@ def test_scheduler_streaming_callbacks(engine):
         d.close()
         tp.close()
         t.close()
+
+
+def test_window_block_reclamation(engine):
+    """Every layer windowed (width 24): with reclamation the pages wholly before the
+    window go back to the allocator and are reused by the other sequence, and the
+    greedy tokens are identical to a run that keeps every page (no freed page is
+    ever read again)."""
+    cfg = dict(TINY, window=24, window_layer_parity=-1)
+    t, tp = gpu_model(engine, cfg, abi.DTYPE_BF16, seed=1, num_blocks=64, max_tokens=256, max_seqs=8)
+    d, dp = gpu_model(engine, dict(cfg, n_layers=1), abi.DTYPE_BF16, seed=2, num_blocks=64, max_tokens=256,
+                      max_seqs=8)
+    s = abi.Sampler(engine, 8, 4, TINY["vocab_size"])
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (40, 55)]
+
+    def run(reclaim):
+        sch = abi.Scheduler(t, tp, d, dp, s, 4, 0.0, 7)
+        try:
+            sch.set_window_reclaim(reclaim)
+            for i, pr in enumerate(prompts):
+                sch.submit(pr, max_tokens=80, stop_token=-1, seq_id=i)
+            usage = []
+            for _ in range(200):
+                if sch.running() == 0 and sch.waiting() == 0:
+                    break
+                sch.step()
+                usage.append((sch.usage(), sch.usage(draft=True)))
+            assert sch.running() == 0 and sch.waiting() == 0
+            return [sch.generated(i) for i in range(2)], usage
+        finally:
+            sch.close()
+
+    try:
+        keep, u_keep = run(False)
+        free, u_free = run(True)
+        assert keep == free
+        assert all(len(g) >= 80 for g in free)
+        n = min(len(u_keep), len(u_free))
+        # kept: all 17 pages of the two sequences at the end; reclaimed: the window's 2-3 pages
+        # plus the step's new tokens per sequence
+        assert max(u[0] for u in u_free[:n]) < 0.6 * max(u[0] for u in u_keep[:n])
+        assert max(u[1] for u in u_free[:n]) < 0.6 * max(u[1] for u in u_keep[:n])
+        assert u_free[-1] == (0.0, 0.0)
+        assert engine.device_error() == 0
+    finally:
+        s.close()
+        dp.close()
+        d.close()
+        tp.close()
+        t.close()

@@ -143,6 +143,7 @@ _HOST_PROTOS = {
     "ykh_generated": (C.c_int32, [_P, C.c_uint32, _U32P, C.c_int32, _I32P]),
     "ykh_counters": (C.c_int32, [_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "ykh_usage": (C.c_float, [_P, C.c_int32]),
+    "ykh_set_window_reclaim": (C.c_int32, [_P, C.c_int32]),
 }
 
 _lib = None
@@ -554,6 +555,9 @@ class Scheduler:
 
     _ON_TOKENS = C.CFUNCTYPE(None, C.c_void_p, C.c_uint32, C.POINTER(C.c_uint32), C.c_int32)
     _ON_DONE = C.CFUNCTYPE(None, C.c_void_p, C.c_uint32, C.c_int32)
+
+    def set_window_reclaim(self, on: bool):
+        check(host_lib().ykh_set_window_reclaim(self.h, 1 if on else 0))
 
     def submit_stream(self, prompt, max_tokens: int, on_tokens=None, on_done=None, stop_token: int = -1,
                       seq_id: int = 0):

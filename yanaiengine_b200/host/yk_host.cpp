@@ -68,16 +68,34 @@ class PagedKVCache {
         if (position > current_position) return;
         const int need = (position + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE;
         while ((int)page_table.size() > need) {
-            alloc_->deallocate(page_table.back());
+            if (page_table.back() >= 0) alloc_->deallocate(page_table.back());
             page_table.pop_back();
         }
+        dead_pages = std::min(dead_pages, (int)page_table.size());
         current_position = position;
     }
     void reset() {
-        for (int b : page_table) alloc_->deallocate(b);
+        for (int b : page_table)
+            if (b >= 0) alloc_->deallocate(b);
         page_table.clear();
         current_position = 0;
+        dead_pages = 0;
     }
+    // Sliding-window reclamation (every layer windowed, width w): a query at
+    // position p >= current_position reads keys from p - w + 1 on, so the pages
+    // wholly before current_position - w + 1 are never read again; they go back to
+    // the allocator and their table entries become -1 (sent as block 0: the
+    // attention's key range starts past them).  The reference never frees them
+    // (S/PagedKVCache.swift:65-85).
+    void reclaim_window(int w) {
+        const int first_live = current_position - w + 1;
+        const int dead = first_live > 0 ? std::min<int>(first_live / YK_BLOCK_SIZE, (int)page_table.size()) : 0;
+        for (; dead_pages < dead; ++dead_pages) {
+            if (page_table[dead_pages] >= 0) alloc_->deallocate(page_table[dead_pages]);
+            page_table[dead_pages] = -1;
+        }
+    }
+    int dead_pages = 0;
     std::vector<int> page_table;
     int current_position = 0;
 
@@ -117,6 +135,10 @@ struct ykh_scheduler {
     std::deque<std::unique_ptr<SequenceRequest>> waiting;
     std::vector<std::unique_ptr<SequenceRequest>> running, done;
     int64_t n_steps = 0, n_emitted = 0, n_accepted = 0;
+    // sliding-window reclamation: window width of a model whose every layer is
+    // windowed (0: some layer is global, nothing can be freed)
+    int t_window = 0, d_window = 0;
+    bool reclaim = true;
     // per-step scratch
     std::vector<uint32_t> tokens, qstarts, ctx, seq_ids, drafts, out_tokens;
     std::vector<int32_t> tables, counts;
@@ -137,6 +159,13 @@ extern "C" yk_status ykh_scheduler_create(yk_model* target, yk_kv_pool* tpool, y
     s->seed = seed;
     s->talloc = std::make_unique<BlockAllocator>(yk_kv_pool_num_blocks(tpool));
     s->dalloc = std::make_unique<BlockAllocator>(yk_kv_pool_num_blocks(dpool));
+    yk_model_config tc{}, dc{};
+    if (yk_model_get_config(target, &tc) != YK_OK || yk_model_get_config(draft, &dc) != YK_OK) {
+        delete s;
+        return YK_ERR_ARG;
+    }
+    s->t_window = tc.window > 0 && tc.window_layer_parity < 0 ? tc.window : 0;
+    s->d_window = dc.window > 0 && dc.window_layer_parity < 0 ? dc.window : 0;
     *out = s;
     return YK_OK;
 }
@@ -211,7 +240,8 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
     s->tables.assign((size_t)B * max_pages, 0);
     for (int b = 0; b < B; ++b) {
         PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
-        std::copy(c->page_table.begin(), c->page_table.end(), s->tables.begin() + (size_t)b * max_pages);
+        int32_t* row = s->tables.data() + (size_t)b * max_pages;
+        for (size_t i = 0; i < c->page_table.size(); ++i) row[i] = c->page_table[i] >= 0 ? c->page_table[i] : 0;
     }
     int32_t rows = 0;
     yk_model* m = is_draft ? s->draft : s->target;
@@ -300,6 +330,8 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
                 break;
             }
         if ((int)r->generated.size() >= r->max_tokens) r->finished = true;
+        if (s->reclaim && s->t_window > 0) r->cache->reclaim_window(s->t_window);
+        if (s->reclaim && s->d_window > 0) r->draft_cache->reclaim_window(s->d_window);
         if (r->on_tokens && cnt > 0) r->on_tokens(r->user, r->id, r->generated.data() + r->generated.size() - cnt, cnt);
         emitted += cnt;
         s->n_accepted += a;
@@ -320,6 +352,12 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
         }
     }
     if (emitted_out) *emitted_out = emitted;
+    return YK_OK;
+}
+
+extern "C" yk_status ykh_set_window_reclaim(ykh_scheduler* s, int32_t on) {
+    if (!s) return YK_ERR_ARG;
+    s->reclaim = on != 0;
     return YK_OK;
 }
 
