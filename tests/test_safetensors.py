@@ -145,3 +145,92 @@ def test_rope_half_row_map_preserves_attention_scores():
         ref = rope_half(q_h[:, s]) @ rope_half(k_h[:, s]).T
         got = rope_pairs(q_i[:, s]) @ rope_pairs(k_i[:, s]).T
         np.testing.assert_allclose(got, ref, rtol=1e-10, atol=1e-9)
+
+
+# ---------------------------------------------------------------------------
+# Property tests: the header parser faces untrusted files.
+# ---------------------------------------------------------------------------
+from hypothesis import HealthCheck, given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+_DT = {"F32": np.float32, "F16": np.float16, "I8": np.int8, "U8": np.uint8, "I32": np.int32, "I64": np.int64,
+       "F64": np.float64, "BF16": np.uint16}
+
+
+@settings(max_examples=60, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(st.dictionaries(st.text(min_size=1, max_size=12), st.tuples(st.sampled_from(sorted(_DT)),
+                       st.lists(st.integers(0, 5), min_size=0, max_size=3)), min_size=0, max_size=6))
+def test_reader_round_trip_property(tmp_path_factory, spec):
+    """Any set of tensors (names with any characters, any dtype, shapes with zeros)
+    reads back with the same names, dtypes, shapes and bytes."""
+    rng = np.random.default_rng(0)
+    tensors = {}
+    for name, (dt, shape) in spec.items():
+        if name == "__metadata__":
+            continue
+        a = (rng.integers(0, 100, shape) if np.issubdtype(_DT[dt], np.integer)
+             else rng.standard_normal(shape)).astype(_DT[dt])
+        tensors[name] = (dt, a)
+    path = tmp_path_factory.mktemp("st") / "p.safetensors"
+    write_safetensors(path, tensors)
+    if any("\x00" in n for n in tensors):  # C strings cannot carry the name: refused
+        with pytest.raises(abi.YKError) as ei:
+            abi.SafeTensors(path)
+        assert ei.value.status == 1 and "NUL" in str(ei.value)
+        return
+    stf = abi.SafeTensors(path)
+    try:
+        assert stf.names() == sorted(tensors)
+        for name, (dt, a) in tensors.items():
+            ti = stf.info(name)
+            assert ti.dtype_name.decode() == dt and tuple(ti.shape[: ti.ndim]) == a.shape
+            assert stf.array(name).tobytes() == a.tobytes()
+    finally:
+        stf.close()
+
+
+@settings(max_examples=150, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(st.binary(max_size=200), st.integers(0, 300), st.binary(max_size=64))
+def test_reader_never_trusts_a_header(tmp_path_factory, header, length, data):
+    """Arbitrary header bytes, a declared length that may lie, and trailing data:
+    open either succeeds with every entry inside the file or fails with
+    YK_ERR_ARG -- never a crash or a read past the mapping."""
+    path = tmp_path_factory.mktemp("bad") / "x.safetensors"
+    write_raw(path, header, data, length)
+    try:
+        stf = abi.SafeTensors(path)
+    except abi.YKError as e:
+        assert e.status == 1
+        return
+    try:
+        size = path.stat().st_size
+        for name in stf.names():
+            ti = stf.info(name)
+            assert ti.nbytes <= size
+            stf.array(name)
+    finally:
+        stf.close()
+
+
+@settings(max_examples=150, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(st.recursive(st.none() | st.booleans() | st.integers(-2**70, 2**70) | st.floats(allow_nan=False)
+                    | st.text(max_size=8),
+                    lambda ch: st.lists(ch, max_size=4) | st.dictionaries(st.text(max_size=6), ch, max_size=4),
+                    max_leaves=20))
+def test_reader_rejects_wrong_structures(tmp_path_factory, value):
+    """Well-formed JSON of any shape as the header: accepted only when it really
+    describes tensors inside the data block."""
+    import json as _json
+    path = tmp_path_factory.mktemp("js") / "j.safetensors"
+    write_raw(path, _json.dumps(value).encode(), b"\0" * 16)
+    try:
+        stf = abi.SafeTensors(path)
+    except abi.YKError as e:
+        assert e.status == 1
+        return
+    try:
+        for name in stf.names():
+            ti = stf.info(name)
+            assert ti.nbytes <= 16
+    finally:
+        stf.close()

@@ -333,6 +333,7 @@ extern "C" yk_status yk_safetensors_open(const char* path, yk_safetensors** out)
     for (const auto& kv : root.obj) {
         if (kv.first == "__metadata__") continue;
         const JVal& v = kv.second;
+        if (kv.first.find('\0') != std::string::npos) return st_fail(st, "an entry name contains a NUL character");
         if (v.kind != JVal::OBJ) return st_fail(st, "entry '" + kv.first + "' is not an object");
         const JVal* dt = member(v, "dtype");
         const JVal* sh = member(v, "shape");
