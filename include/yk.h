@@ -187,6 +187,11 @@ yk_status yk_model_load_tensor(yk_model* m, int32_t tensor, int32_t layer, const
  * decoder layer (a layer kind this module lacks) is YK_ERR_UNSUPPORTED. */
 yk_status yk_model_load_safetensors(yk_model* m, yk_safetensors* const* files, int32_t n_files, float norm_offset,
                                     int32_t flags, int32_t* n_loaded);
+/* The logical tensor (YK_T_*) and layer of a Hugging Face Llama / Gemma
+ * checkpoint name, as yk_model_load_safetensors maps it (for callers that walk a
+ * checkpoint themselves, e.g. a Swift ModelLoader calling yk_model_load_tensor);
+ * YK_ERR_ARG for any other name or a layer >= n_layers.  No device needed. */
+yk_status yk_hf_tensor_id(const char* name, int32_t n_layers, int32_t* tensor, int32_t* layer);
 
 /* ---- paged KV pool.  Replaces BlockAllocator's MTLBuffers
  * (S/BlockAllocator.swift:13-36).  Block ids, the free list and the page

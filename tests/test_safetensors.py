@@ -147,6 +147,30 @@ def test_rope_half_row_map_preserves_attention_scores():
         np.testing.assert_allclose(got, ref, rtol=1e-10, atol=1e-9)
 
 
+def test_hf_name_mapping():
+    """The checkpoint-name map of yk_model_load_safetensors (no device needed)."""
+    L = 4
+    cases = {
+        "model.embed_tokens.weight": (abi.T_EMBED, 0), "model.norm.weight": (abi.T_FINAL_NORM, 0),
+        "lm_head.weight": (abi.T_LM_HEAD, 0),
+        "model.layers.0.self_attn.q_proj.weight": (abi.T_WQ, 0), "model.layers.3.self_attn.k_proj.weight": (abi.T_WK, 3),
+        "model.layers.1.self_attn.v_proj.weight": (abi.T_WV, 1), "model.layers.2.self_attn.o_proj.weight": (abi.T_WO, 2),
+        "model.layers.0.mlp.gate_proj.weight": (abi.T_WGATE, 0), "model.layers.0.mlp.up_proj.weight": (abi.T_WUP, 0),
+        "model.layers.3.mlp.down_proj.weight": (abi.T_WDOWN, 3),
+        "model.layers.2.input_layernorm.weight": (abi.T_NORM1, 2),
+        "model.layers.2.post_attention_layernorm.weight": (abi.T_NORM2, 2),
+    }
+    for name, want in cases.items():
+        assert abi.hf_tensor_id(name, L) == want, name
+    for bad in ("model.layers.4.mlp.up_proj.weight",           # layer past the model
+                "model.layers.x.mlp.up_proj.weight", "model.layers..mlp.up_proj.weight",
+                "model.layers.0.pre_feedforward_layernorm.weight",  # Gemma-2 norm: no slot here
+                "model.layers.0.self_attn.q_proj.bias", "model.rotary_emb.inv_freq", "lm_head", ""):
+        with pytest.raises(abi.YKError) as ei:
+            abi.hf_tensor_id(bad, L)
+        assert ei.value.status == 1
+
+
 # ---------------------------------------------------------------------------
 # Property tests: the header parser faces untrusted files.
 # ---------------------------------------------------------------------------

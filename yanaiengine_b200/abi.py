@@ -88,6 +88,7 @@ _PROTOS = {
     "yk_model_load_tensor": (C.c_int32, [_P, C.c_int32, C.c_int32, _P, C.c_int32, C.c_int64, C.c_int64,
                                          C.c_int32]),
     "yk_model_load_safetensors": (C.c_int32, [_P, C.POINTER(_P), C.c_int32, C.c_float, C.c_int32, _I32P]),
+    "yk_hf_tensor_id": (C.c_int32, [C.c_char_p, C.c_int32, _I32P, _I32P]),
     "yk_kv_pool_create": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_int32, C.POINTER(_P)]),
     "yk_kv_pool_destroy": (None, [_P]),
     "yk_kv_pool_num_blocks": (C.c_int32, [_P]),
@@ -335,6 +336,13 @@ class TensorInfo(C.Structure):
 _NP_DTYPES = {"F32": np.float32, "F16": np.float16, "F64": np.float64, "I64": np.int64, "I32": np.int32,
               "I16": np.int16, "I8": np.int8, "U8": np.uint8, "U16": np.uint16, "U32": np.uint32,
               "U64": np.uint64, "BOOL": np.bool_, "BF16": np.uint16}  # BF16: the raw 16-bit words
+
+
+def hf_tensor_id(name: str, n_layers: int) -> tuple[int, int]:
+    """(tensor, layer) of a Hugging Face checkpoint name (yk_hf_tensor_id)."""
+    t, l = C.c_int32(), C.c_int32()
+    check(lib().yk_hf_tensor_id(name.encode(), n_layers, C.byref(t), C.byref(l)))
+    return t.value, l.value
 
 
 class SafeTensors:

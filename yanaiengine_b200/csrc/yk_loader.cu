@@ -674,6 +674,15 @@ static bool hf_tensor(const std::string& name, int n_layers, int32_t* t, int32_t
     return false;
 }
 
+extern "C" yk_status yk_hf_tensor_id(const char* name, int32_t n_layers, int32_t* tensor, int32_t* layer) {
+    YK_ARG(name && tensor && layer && n_layers > 0, "null argument");
+    if (!hf_tensor(name, n_layers, tensor, layer)) {
+        yk_set_error(std::string("'") + name + "' is not a weight of this module's layout");
+        return YK_ERR_ARG;
+    }
+    return YK_OK;
+}
+
 extern "C" yk_status yk_model_load_safetensors(yk_model* m, yk_safetensors* const* files, int32_t n_files,
                                                float norm_offset, int32_t flags, int32_t* n_loaded) {
     YK_ARG(m && files && n_files > 0, "null argument");
