@@ -199,13 +199,16 @@ struct AttnCfg {
     // Ring depth: a warp's chunk time is mostly page latency, so what sets a
     // CTA's rate is how many pages the ring holds beyond the ones in use.  With
     // one-page chunks only one page per consuming warp is in use (decode-like,
-    // head_dim 64: 4 of 16 pages; verify, 2 m-tiles x 2 warps: 2 of 8), the rest
+    // head_dim 64: 4 of 12 pages; verify, 2 m-tiles x 2 warps: 2 of 12), the rest
     // stream ahead (two-page chunks: 1.5 % slower per step, target and draft).
-    // head_dim 128: 12 pages (the Q tile lives in registers, so two CTAs per SM
-    // still fit; 8 pages: verify attention 46.8 -> 47.9 us).
+    // head_dim 128: 12 pages at 2 CTAs per SM (the Q tile lives in registers, so
+    // they fit; 8 pages: verify attention 46.8 -> 47.9 us; 3 CTAs per SM with 8
+    // pages: slower).  head_dim 64 (decode-shaped draft): resident slots matter
+    // more than depth there (the planner splits long spans over the spare slots):
+    // 4 CTAs per SM (96 registers) with 12 pages beat 3 with 16 and 2 with 24.
     static constexpr int CP = 1;
-    static constexpr int S = DH == 256 ? 4 : (DH == 64 ? 16 : 12);
-    static constexpr int CTAS_PER_SM = DH == 64 ? 3 : (DH == 128 ? 2 : 1);  // register-limited
+    static constexpr int S = DH == 256 ? 4 : 12;
+    static constexpr int CTAS_PER_SM = DH == 64 ? 4 : (DH == 128 ? 2 : 1);  // registers / shared memory
     static constexpr int LDQ = DH + 8;                       // padded Q row (elements)
     // head_dim <= 128: Q goes straight from global memory into the score MMA's A
     // fragments (registers), no shared-memory copy; the room goes to the ring
