@@ -1,0 +1,230 @@
+"""libyk_host.so's scheduling logic on the CPU: host/yk_host.cpp compiled with a
+stand-in for the six device entry points it calls (tests/host_stub/yk_stub.cpp),
+which checks every page table it is given.  Covers admission to completion, page
+accounting, sliding-window reclamation (which must never hand a forward a page it
+may still read) and the streaming callbacks.  No GPU."""
+from __future__ import annotations
+
+import ctypes as C
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+_P = C.c_void_p
+_U32P = C.POINTER(C.c_uint32)
+ON_TOKENS = C.CFUNCTYPE(None, C.c_void_p, C.c_uint32, _U32P, C.c_int32)
+ON_DONE = C.CFUNCTYPE(None, C.c_void_p, C.c_uint32, C.c_int32)
+K, V = 4, 1000
+
+
+@pytest.fixture(scope="module")
+def lib(tmp_path_factory):
+    cxx = shutil.which("g++")
+    if not cxx:
+        pytest.skip("g++ not found")
+    out = tmp_path_factory.mktemp("hoststub") / "libyk_host_stub.so"
+    subprocess.run([cxx, "-O1", "-std=c++17", "-fPIC", "-shared", "-Wl,-Bsymbolic", "-o", str(out),
+                    str(ROOT / "yanaiengine_b200" / "host" / "yk_host.cpp"), str(ROOT / "tests" / "host_stub" / "yk_stub.cpp"),
+                    f"-I{ROOT / 'include'}"], check=True, capture_output=True)
+    L = C.CDLL(str(out))
+    for name, res, args in (
+        ("stub_model", _P, [C.c_int, C.c_int, C.c_int, C.c_int]), ("stub_model_free", None, [_P]),
+        ("stub_pool", _P, [C.c_int]), ("stub_pool_free", None, [_P]),
+        ("stub_sampler", _P, [C.c_int, C.c_int]), ("stub_sampler_free", None, [_P]),
+        ("stub_stats", None, [C.POINTER(C.c_int64)] * 3), ("stub_reset", None, []),
+        ("ykh_scheduler_create", C.c_int32, [_P, _P, _P, _P, _P, C.c_int32, C.c_float, C.c_uint64, C.POINTER(_P)]),
+        ("ykh_scheduler_destroy", None, [_P]),
+        ("ykh_submit", C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
+        ("ykh_submit_stream", C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32, C.c_void_p,
+                                          C.c_void_p, C.c_void_p]),
+        ("ykh_step", C.c_int32, [_P, C.POINTER(C.c_int32)]),
+        ("ykh_num_running", C.c_int32, [_P]), ("ykh_num_waiting", C.c_int32, [_P]),
+        ("ykh_generated", C.c_int32, [_P, C.c_uint32, _U32P, C.c_int32, C.POINTER(C.c_int32)]),
+        ("ykh_usage", C.c_float, [_P, C.c_int32]),
+        ("ykh_set_window_reclaim", C.c_int32, [_P, C.c_int32]),
+    ):
+        f = getattr(L, name)
+        f.restype, f.argtypes = res, args
+    return L
+
+
+class Rig:
+    """A scheduler over stub models: target and draft share the window schedule."""
+
+    def __init__(self, L, blocks, window=0, parity=-1, reclaim=True):
+        self.L = L
+        self.t = L.stub_model(4, window, parity, V)
+        self.d = L.stub_model(2, window, parity, V)
+        self.tp, self.dp = L.stub_pool(blocks), L.stub_pool(blocks)
+        self.s = L.stub_sampler(K, V)
+        self.h = _P()
+        assert L.ykh_scheduler_create(self.t, self.tp, self.d, self.dp, self.s, K, 0.8, 1, C.byref(self.h)) == 0
+        assert L.ykh_set_window_reclaim(self.h, 1 if reclaim else 0) == 0
+        L.stub_reset()
+        self.keep = []
+
+    def submit(self, seq, n, max_tokens, stream=None):
+        p = (C.c_uint32 * n)(*[(seq * 17 + i) % V for i in range(n)])
+        if stream is None:
+            assert self.L.ykh_submit(self.h, p, n, max_tokens, -1, seq) == 0
+        else:
+            ct = ON_TOKENS(lambda _u, sid, toks, m: stream[0](int(sid), [toks[i] for i in range(m)]))
+            cd = ON_DONE(lambda _u, sid, m: stream[1](int(sid), int(m)))
+            self.keep.append((ct, cd))
+            assert self.L.ykh_submit_stream(self.h, p, n, max_tokens, -1, seq, C.cast(ct, C.c_void_p),
+                                            C.cast(cd, C.c_void_p), None) == 0
+
+    def run(self, max_steps=500):
+        usage = []
+        for _ in range(max_steps):
+            if self.L.ykh_num_running(self.h) == 0 and self.L.ykh_num_waiting(self.h) == 0:
+                return usage, 0
+            e = C.c_int32()
+            st = self.L.ykh_step(self.h, C.byref(e))
+            if st != 0:
+                return usage, st
+            usage.append(self.L.ykh_usage(self.h, 0))
+        return usage, -1
+
+    def generated(self, seq):
+        n = C.c_int32()
+        buf = (C.c_uint32 * 4096)()
+        assert self.L.ykh_generated(self.h, seq, buf, 4096, C.byref(n)) == 0
+        return list(buf[: n.value])
+
+    def stats(self):
+        v, f, p = C.c_int64(), C.c_int64(), C.c_int64()
+        self.L.stub_stats(C.byref(v), C.byref(f), C.byref(p))
+        return v.value, f.value, p.value
+
+    def close(self):
+        self.L.ykh_scheduler_destroy(self.h)
+        for x, free in ((self.t, self.L.stub_model_free), (self.d, self.L.stub_model_free),
+                        (self.tp, self.L.stub_pool_free), (self.dp, self.L.stub_pool_free),
+                        (self.s, self.L.stub_sampler_free)):
+            free(x)
+
+
+def test_batch_runs_to_completion(lib):
+    r = Rig(lib, blocks=256)
+    try:
+        for i in range(5):
+            r.submit(i, 10 + 13 * i, max_tokens=30)
+        usage, st = r.run()
+        assert st == 0
+        viol, fwd, pages = r.stats()
+        assert viol == 0 and fwd > 0 and pages > 0
+        for i in range(5):
+            assert 30 <= len(r.generated(i)) <= 30 + K
+        assert usage[-1] == 0.0  # every page back in the free list
+    finally:
+        r.close()
+
+
+def test_window_reclamation_bounds_memory_and_keeps_reads_valid(lib):
+    """Every layer windowed (24 tokens): 4 sequences of 30 + 200 tokens need ~60
+    pages each model without reclamation but fit in 40 with it; no forward is ever
+    handed a freed (or shared) page inside its window."""
+    off = Rig(lib, blocks=40, window=24, parity=-1, reclaim=False)
+    try:
+        for i in range(4):
+            off.submit(i, 30, max_tokens=200)
+        _, st = off.run()
+        assert st == 2  # YK_ERR_OOM: the pages of every past token are kept
+    finally:
+        off.close()
+    on = Rig(lib, blocks=40, window=24, parity=-1, reclaim=True)
+    try:
+        for i in range(4):
+            on.submit(i, 30, max_tokens=200)
+        usage, st = on.run()
+        assert st == 0
+        viol, fwd, pages = on.stats()
+        assert viol == 0 and pages > 0
+        assert max(usage) <= 4 * 4 / 40 + 1e-6  # at most ~4 live pages per sequence
+        assert all(len(on.generated(i)) >= 200 for i in range(4))
+        assert usage[-1] == 0.0
+    finally:
+        on.close()
+
+
+def test_alternating_windows_free_nothing(lib):
+    """Gemma's schedule (windowed on even layers only): a page holds every layer,
+    the global layers still read it, so nothing is reclaimed."""
+    a = Rig(lib, blocks=256, window=24, parity=0, reclaim=True)
+    b = Rig(lib, blocks=256, window=0, parity=-1, reclaim=True)
+    try:
+        for r in (a, b):
+            for i in range(3):
+                r.submit(i, 40, max_tokens=60)
+        ua, sa = a.run()
+        ub, sb = b.run()
+        assert sa == 0 and sb == 0 and ua == ub
+        assert a.stats()[0] == 0
+    finally:
+        a.close()
+        b.close()
+
+
+def test_streaming_runs_concatenate_to_generated(lib):
+    r = Rig(lib, blocks=256)
+    runs, done = {}, {}
+    cb = (lambda sid, toks: runs.setdefault(sid, []).append(toks), lambda sid, n: done.setdefault(sid, []).append(n))
+    try:
+        for i in range(3):
+            r.submit(i, 20 + 5 * i, max_tokens=25, stream=cb)
+        r.submit(7, 15, max_tokens=25)
+        _, st = r.run()
+        assert st == 0
+        for i in range(3):
+            g = r.generated(i)
+            assert [x for run in runs[i] for x in run] == g
+            assert all(1 <= len(run) <= K + 1 for run in runs[i])
+            assert done[i] == [len(g)]
+        assert 7 not in runs and 7 not in done
+    finally:
+        r.close()
+
+
+def test_deterministic(lib):
+    outs = []
+    for _ in range(2):
+        r = Rig(lib, blocks=128, window=24, parity=-1)
+        try:
+            for i in range(3):
+                r.submit(i, 33, max_tokens=50)
+            _, st = r.run()
+            assert st == 0
+            outs.append([r.generated(i) for i in range(3)])
+        finally:
+            r.close()
+    assert outs[0] == outs[1]
+
+
+def test_stub_catches_bad_tables(lib):
+    """The checker itself: a block read by two sequences, or one outside the pool,
+    counts as a violation (a planted mistake, on the CPU stand-in)."""
+    f = lib.yk_forward_step
+    f.restype = C.c_int32
+    f.argtypes = [_P, _P, _U32P, C.c_int32, _U32P, _U32P, C.c_int32, C.POINTER(C.c_int32), C.c_int32, C.c_int32,
+                  C.POINTER(C.c_int32)]
+    r = Rig(lib, blocks=8)
+    try:
+        toks = (C.c_uint32 * 2)(1, 2)
+        qs = (C.c_uint32 * 3)(0, 1, 2)
+        ctx = (C.c_uint32 * 2)(20, 20)  # two pages each
+        rows = C.c_int32()
+        ok = (C.c_int32 * 4)(0, 1, 2, 3)
+        assert f(r.t, r.tp, toks, 2, qs, ctx, 2, ok, 2, 0, C.byref(rows)) == 0
+        assert r.stats()[0] == 0
+        shared = (C.c_int32 * 4)(0, 1, 2, 1)  # block 1 in both sequences' windows
+        f(r.t, r.tp, toks, 2, qs, ctx, 2, shared, 2, 0, C.byref(rows))
+        assert r.stats()[0] == 1
+        outside = (C.c_int32 * 4)(0, 1, 2, 9)  # block 9 of an 8-block pool
+        f(r.t, r.tp, toks, 2, qs, ctx, 2, outside, 2, 0, C.byref(rows))
+        assert r.stats()[0] == 2
+    finally:
+        r.close()
