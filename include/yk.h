@@ -199,6 +199,19 @@ yk_status yk_hf_tensor_id(const char* name, int32_t n_layers, int32_t* tensor, i
  * covers every layer: pool layout [block][layer][K|V][kv_head][16][head_dim]. */
 yk_status yk_kv_pool_create(yk_engine* e, const yk_model_config* cfg, int32_t num_blocks,
                             yk_kv_pool** out);
+/* A pool for one kind of layer only: YK_POOL_GLOBAL_LAYERS holds the layers
+ * without a window, YK_POOL_WINDOWED_LAYERS the windowed ones (cfg.window,
+ * cfg.window_layer_parity), each block [its layers][K|V][kv head][16][dh].  With
+ * one pool of each kind (yk_forward_step_split) the windowed layers get their
+ * own page tables, so the pages before their window can be freed while the
+ * global layers keep every page (Gemma's alternating schedule; the reference
+ * never frees them, S/PagedKVCache.swift:65-85).  YK_POOL_ALL_LAYERS is
+ * yk_kv_pool_create. */
+#define YK_POOL_ALL_LAYERS      0
+#define YK_POOL_GLOBAL_LAYERS   1
+#define YK_POOL_WINDOWED_LAYERS 2
+yk_status yk_kv_pool_create_layers(yk_engine* e, const yk_model_config* cfg, int32_t num_blocks, int32_t layers,
+                                   yk_kv_pool** out);
 void      yk_kv_pool_destroy(yk_kv_pool* p);
 int32_t   yk_kv_pool_num_blocks(const yk_kv_pool* p);
 /* Fills every slot with N(0, std) values (synthetic context for benchmarks). */
@@ -231,6 +244,17 @@ yk_status yk_forward_step_drafts(yk_model* m, yk_kv_pool* pool, const uint32_t* 
                                  const uint32_t* q_starts, const uint32_t* context_lens, int32_t B,
                                  const int32_t* block_tables, int32_t max_blocks, int32_t last_n,
                                  yk_sampler* s, int32_t j0, int32_t nd, int32_t* n_rows);
+/* yk_forward_step over split pools: `pool` (YK_POOL_GLOBAL_LAYERS) with
+ * block_tables for the global layers, `wpool` (YK_POOL_WINDOWED_LAYERS) with
+ * wblock_tables for the windowed ones; both tables cover every position of each
+ * sequence (pages wholly before a windowed layer's window may hold any valid
+ * block id: they are not read).  s != NULL and nd > 0: the device-resident draft
+ * tokens of yk_forward_step_drafts. */
+yk_status yk_forward_step_split(yk_model* m, yk_kv_pool* pool, yk_kv_pool* wpool, const uint32_t* tokens, int32_t T,
+                                const uint32_t* q_starts, const uint32_t* context_lens, int32_t B,
+                                const int32_t* block_tables, int32_t max_blocks, const int32_t* wblock_tables,
+                                int32_t wmax_blocks, int32_t last_n, yk_sampler* s, int32_t j0, int32_t nd,
+                                int32_t* n_rows);
 /* Copies logits rows [row0, row0+rows) of the last forward step to host (tests). */
 yk_status yk_logits_copy_to_host(yk_model* m, int32_t row0, int32_t rows, float* host);
 

@@ -31,6 +31,16 @@ typedef struct ykh_scheduler ykh_scheduler;
 yk_status ykh_scheduler_create(yk_model* target, yk_kv_pool* target_pool, yk_model* draft, yk_kv_pool* draft_pool,
                                yk_sampler* sampler, int32_t k, float temperature, uint64_t seed,
                                ykh_scheduler** out);
+/* The same over split pools (a model with windowed and global layers, e.g.
+ * Gemma's alternating schedule): target_pool / draft_pool hold the global layers
+ * (YK_POOL_GLOBAL_LAYERS), target_wpool / draft_wpool the windowed ones
+ * (YK_POOL_WINDOWED_LAYERS), each with its own BlockAllocator and page tables;
+ * with window reclamation on, each step frees the windowed pools' pages wholly
+ * before the window.  Both models must have windowed layers. */
+yk_status ykh_scheduler_create_split(yk_model* target, yk_kv_pool* target_pool, yk_kv_pool* target_wpool,
+                                     yk_model* draft, yk_kv_pool* draft_pool, yk_kv_pool* draft_wpool,
+                                     yk_sampler* sampler, int32_t k, float temperature, uint64_t seed,
+                                     ykh_scheduler** out);
 void ykh_scheduler_destroy(ykh_scheduler* s);
 
 /* Scheduler.submit (S/Scheduler.swift:105).  stop_token < 0: none.  seq_id is
@@ -74,6 +84,8 @@ yk_status ykh_counters(const ykh_scheduler* s, int64_t* steps, int64_t* emitted,
 yk_status ykh_set_window_reclaim(ykh_scheduler* s, int32_t on);
 /* BlockAllocator.usage of the target / draft pools (S/BlockAllocator.swift:56-58). */
 float     ykh_usage(const ykh_scheduler* s, int32_t draft);
+/* Usage of the windowed-layer pools of a split scheduler (0 otherwise). */
+float     ykh_usage_windowed(const ykh_scheduler* s, int32_t draft);
 
 #ifdef __cplusplus
 }

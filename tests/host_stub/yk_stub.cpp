@@ -31,9 +31,10 @@ struct yk_sampler {
 namespace {
 int64_t g_violations = 0, g_forwards = 0, g_pages_checked = 0;
 
+// windowed_pool: the tables of a pool that holds only windowed layers.
 void check_tables(const yk_model* m, const yk_kv_pool* pool, const uint32_t* q_starts, const uint32_t* ctx, int B,
-                  const int32_t* tables, int max_blocks) {
-    const bool windowed = m->cfg.window > 0 && m->cfg.window_layer_parity < 0;
+                  const int32_t* tables, int max_blocks, bool windowed_pool = false) {
+    const bool windowed = windowed_pool || (m->cfg.window > 0 && m->cfg.window_layer_parity < 0);
     std::map<int, int> owner;
     for (int b = 0; b < B; ++b) {
         const int n = (int)(q_starts[b + 1] - q_starts[b]);
@@ -111,6 +112,17 @@ yk_status yk_forward_step_drafts(yk_model* m, yk_kv_pool* pool, const uint32_t* 
                                  const int32_t* block_tables, int32_t max_blocks, int32_t last_n, yk_sampler* s,
                                  int32_t j0, int32_t nd, int32_t* n_rows) {
     if (!s || j0 < 0 || nd < 0 || j0 + nd > s->k) ++g_violations;
+    return yk_forward_step(m, pool, tokens, T, q_starts, context_lens, B, block_tables, max_blocks, last_n, n_rows);
+}
+
+yk_status yk_forward_step_split(yk_model* m, yk_kv_pool* pool, yk_kv_pool* wpool, const uint32_t* tokens, int32_t T,
+                                const uint32_t* q_starts, const uint32_t* context_lens, int32_t B,
+                                const int32_t* block_tables, int32_t max_blocks, const int32_t* wblock_tables,
+                                int32_t wmax_blocks, int32_t last_n, yk_sampler* s, int32_t j0, int32_t nd,
+                                int32_t* n_rows) {
+    if (!wpool || m->cfg.window <= 0) ++g_violations;
+    if (s && (j0 < 0 || nd < 0 || j0 + nd > s->k)) ++g_violations;
+    check_tables(m, wpool, q_starts, context_lens, B, wblock_tables, wmax_blocks, true);
     return yk_forward_step(m, pool, tokens, T, q_starts, context_lens, B, block_tables, max_blocks, last_n, n_rows);
 }
 

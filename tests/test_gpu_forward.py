@@ -10,7 +10,7 @@ Greedy tokens must agree wherever the oracle's top-2 gap exceeds the error bound
 import numpy as np
 import pytest
 
-from helpers import TINY, PageTables, forward_pair, gpu_model, oracle_twin
+from helpers import TINY, PageTables, forward_pair, gpu_model, oracle_twin, step_inputs
 from yanaiengine_b200 import abi
 
 pytestmark = pytest.mark.gpu
@@ -157,3 +157,50 @@ def test_bf16_gemm_paths_with_fused_norm(oracle, monkeypatch, knobs):
         _drive(e, oracle, cfg, abi.DTYPE_BF16, True, 2e-2, steps=2)
     finally:
         e.close()
+
+
+def test_gemma_split_pools_vs_single_pool_oracle(engine, oracle):
+    """Split pools (yk_forward_step_split): the global layers' K/V in one pool, the
+    windowed layers' in another, each with its own page tables (different block
+    assignments), against the oracle's single pool: same logits within the bf16
+    bound, prefill and verify steps."""
+    cfg = dict(TINY, act=abi.ACT_GELU_TANH, attn_cap=50.0, final_cap=30.0, window=8, window_layer_parity=0,
+               head_dim=256, n_heads=2, n_kv_heads=1, rms_eps=1e-6)
+    c = abi.make_config(**cfg, dtype=abi.DTYPE_BF16, max_tokens=256, max_seqs=16)
+    m = abi.Model(engine, c, seed=3, init_std=0.08)
+    pg = abi.KVPool(engine, c, NB, abi.POOL_GLOBAL_LAYERS)
+    pw = abi.KVPool(engine, c, NB, abi.POOL_WINDOWED_LAYERS)
+    try:
+        orc = oracle_twin(oracle, m, cfg, NB, emulate_bf16=True)
+        pto, ptg, ptw = PageTables(NB), PageTables(NB), PageTables(NB)
+        ptw.free = list(np.random.default_rng(5).permutation(NB))  # a different block assignment
+        rng = np.random.default_rng(2)
+        V = cfg["vocab_size"]
+        lens = {0: 17, 1: 40, 2: 5}
+        steps = [[(sid, rng.integers(0, V, n).tolist(), 0) for sid, n in lens.items()]]
+        for _ in range(3):
+            st = []
+            for sid in (0, 1, 2):
+                st.append((sid, rng.integers(0, V, 5).tolist(), lens[sid]))
+                lens[sid] += 5
+            steps.append(st)
+        for i, batch in enumerate(steps):
+            last_n = 0 if i == 0 else 5
+            toks, qs, ctx, bt_o = step_inputs(pto, batch)
+            bt_g = step_inputs(ptg, batch)[3]
+            bt_w = step_inputs(ptw, batch)[3]
+            rows = m.forward_split(pg, pw, toks, qs, ctx, bt_g, bt_w, last_n)
+            g = m.logits(0, rows)
+            o = orc.forward(toks, qs, ctx, bt_o, last_n)
+            assert np.isfinite(g).all()
+            assert _rel(g, o) < 2e-2, f"step {i}: rel err {_rel(g, o):.3e}"
+        # the pools hold only their own layers
+        with pytest.raises(abi.YKError):
+            pw.read_page(0, 1, 0)  # layer 1 is global
+        with pytest.raises(abi.YKError):
+            m.forward(pg, toks, qs, ctx, bt_g, 5)  # a one-kind pool needs the split entry
+        assert engine.device_error() == 0
+    finally:
+        pw.close()
+        pg.close()
+        m.close()

@@ -215,3 +215,56 @@ def test_window_block_reclamation(engine):
         d.close()
         tp.close()
         t.close()
+
+
+def test_split_pools_reclaim_windowed_pages(engine):
+    """Alternating windows (even layers, width 24) over split pools with
+    reclamation: greedy tokens identical to single pools that keep every page,
+    and the windowed pools stay small."""
+    cfg = dict(TINY, window=24, window_layer_parity=0)
+    dcfg = dict(cfg, n_layers=2)
+    mk = lambda c, seed: abi.Model(engine, abi.make_config(**c, dtype=abi.DTYPE_BF16, max_tokens=256, max_seqs=8),
+                                   seed=seed, init_std=0.02)
+    t, d = mk(cfg, 1), mk(dcfg, 2)
+    s = abi.Sampler(engine, 8, 4, TINY["vocab_size"])
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (40, 55)]
+    pools = []
+
+    def pool(m, layers):
+        pools.append(abi.KVPool(engine, m.cfg, 64, layers))
+        return pools[-1]
+
+    def run(split):
+        if split:
+            sch = abi.Scheduler(t, pool(t, abi.POOL_GLOBAL_LAYERS), d, pool(d, abi.POOL_GLOBAL_LAYERS), s, 4, 0.0, 7,
+                                twpool=pool(t, abi.POOL_WINDOWED_LAYERS), dwpool=pool(d, abi.POOL_WINDOWED_LAYERS))
+        else:
+            sch = abi.Scheduler(t, pool(t, abi.POOL_ALL_LAYERS), d, pool(d, abi.POOL_ALL_LAYERS), s, 4, 0.0, 7)
+        try:
+            for i, pr in enumerate(prompts):
+                sch.submit(pr, max_tokens=80, stop_token=-1, seq_id=i)
+            wmax = 0.0
+            for _ in range(200):
+                if sch.running() == 0 and sch.waiting() == 0:
+                    break
+                sch.step()
+                wmax = max(wmax, sch.usage_windowed())
+            assert sch.running() == 0 and sch.waiting() == 0
+            return [sch.generated(i) for i in range(2)], wmax
+        finally:
+            sch.close()
+
+    try:
+        single, _ = run(False)
+        split, wmax = run(True)
+        assert single == split
+        assert all(len(g) >= 80 for g in split)
+        assert 0.0 < wmax <= 2 * 4 / 64 + 1e-6  # a few live pages per sequence
+        assert engine.device_error() == 0
+    finally:
+        for p in pools:
+            p.close()
+        s.close()
+        d.close()
+        t.close()

@@ -45,6 +45,9 @@ def lib(tmp_path_factory):
         ("ykh_generated", C.c_int32, [_P, C.c_uint32, _U32P, C.c_int32, C.POINTER(C.c_int32)]),
         ("ykh_usage", C.c_float, [_P, C.c_int32]),
         ("ykh_set_window_reclaim", C.c_int32, [_P, C.c_int32]),
+        ("ykh_scheduler_create_split", C.c_int32, [_P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_float, C.c_uint64,
+                                                   C.POINTER(_P)]),
+        ("ykh_usage_windowed", C.c_float, [_P, C.c_int32]),
     ):
         f = getattr(L, name)
         f.restype, f.argtypes = res, args
@@ -54,14 +57,21 @@ def lib(tmp_path_factory):
 class Rig:
     """A scheduler over stub models: target and draft share the window schedule."""
 
-    def __init__(self, L, blocks, window=0, parity=-1, reclaim=True):
+    def __init__(self, L, blocks, window=0, parity=-1, reclaim=True, wblocks=0):
+        """wblocks > 0: split pools (windowed layers in pools of wblocks blocks)."""
         self.L = L
         self.t = L.stub_model(4, window, parity, V)
         self.d = L.stub_model(2, window, parity, V)
         self.tp, self.dp = L.stub_pool(blocks), L.stub_pool(blocks)
+        self.twp = L.stub_pool(wblocks) if wblocks else None
+        self.dwp = L.stub_pool(wblocks) if wblocks else None
         self.s = L.stub_sampler(K, V)
         self.h = _P()
-        assert L.ykh_scheduler_create(self.t, self.tp, self.d, self.dp, self.s, K, 0.8, 1, C.byref(self.h)) == 0
+        if wblocks:
+            assert L.ykh_scheduler_create_split(self.t, self.tp, self.twp, self.d, self.dp, self.dwp, self.s, K, 0.8,
+                                                1, C.byref(self.h)) == 0
+        else:
+            assert L.ykh_scheduler_create(self.t, self.tp, self.d, self.dp, self.s, K, 0.8, 1, C.byref(self.h)) == 0
         assert L.ykh_set_window_reclaim(self.h, 1 if reclaim else 0) == 0
         L.stub_reset()
         self.keep = []
@@ -86,7 +96,8 @@ class Rig:
             st = self.L.ykh_step(self.h, C.byref(e))
             if st != 0:
                 return usage, st
-            usage.append(self.L.ykh_usage(self.h, 0))
+            usage.append((self.L.ykh_usage(self.h, 0), self.L.ykh_usage_windowed(self.h, 0),
+                          self.L.ykh_usage_windowed(self.h, 1)) if self.twp else self.L.ykh_usage(self.h, 0))
         return usage, -1
 
     def generated(self, seq):
@@ -106,6 +117,9 @@ class Rig:
                         (self.tp, self.L.stub_pool_free), (self.dp, self.L.stub_pool_free),
                         (self.s, self.L.stub_sampler_free)):
             free(x)
+        for x in (self.twp, self.dwp):
+            if x:
+                self.L.stub_pool_free(x)
 
 
 def test_batch_runs_to_completion(lib):
@@ -226,5 +240,40 @@ def test_stub_catches_bad_tables(lib):
         outside = (C.c_int32 * 4)(0, 1, 2, 9)  # block 9 of an 8-block pool
         f(r.t, r.tp, toks, 2, qs, ctx, 2, outside, 2, 0, C.byref(rows))
         assert r.stats()[0] == 2
+    finally:
+        r.close()
+
+
+def test_split_pools_free_windowed_pages(lib):
+    """Gemma's schedule (windowed on even layers) over split pools: the windowed
+    layers' pool stays at a few pages per sequence while the global layers' pool
+    keeps every page; every table each forward gets is valid for its reads."""
+    r = Rig(lib, blocks=256, window=24, parity=0, reclaim=True, wblocks=24)
+    try:
+        for i in range(4):
+            r.submit(i, 30, max_tokens=150)
+        usage, st = r.run()
+        assert st == 0
+        viol, fwd, pages = r.stats()
+        assert viol == 0 and pages > 0
+        assert max(u[1] for u in usage) <= 4 * 4 / 24 + 1e-6 and max(u[2] for u in usage) <= 4 * 4 / 24 + 1e-6
+        assert max(u[0] for u in usage) > 4 * 10 / 256  # the global layers keep their pages
+        assert usage[-1] == (0.0, 0.0, 0.0)
+        keep = Rig(lib, blocks=256, window=24, parity=0, reclaim=True)
+        try:
+            for i in range(4):
+                keep.submit(i, 30, max_tokens=150)
+            assert keep.run()[1] == 0
+            assert [r.generated(i) for i in range(4)] == [keep.generated(i) for i in range(4)]
+        finally:
+            keep.close()
+        # without reclamation the 24-block windowed pools run out
+        off = Rig(lib, blocks=256, window=24, parity=0, reclaim=False, wblocks=24)
+        try:
+            for i in range(4):
+                off.submit(i, 30, max_tokens=150)
+            assert off.run()[1] == 2
+        finally:
+            off.close()
     finally:
         r.close()

@@ -90,6 +90,9 @@ _PROTOS = {
     "yk_model_load_safetensors": (C.c_int32, [_P, C.POINTER(_P), C.c_int32, C.c_float, C.c_int32, _I32P]),
     "yk_hf_tensor_id": (C.c_int32, [C.c_char_p, C.c_int32, _I32P, _I32P]),
     "yk_kv_pool_create": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_int32, C.POINTER(_P)]),
+    "yk_kv_pool_create_layers": (C.c_int32, [_P, C.POINTER(ModelConfig), C.c_int32, C.c_int32, C.POINTER(_P)]),
+    "yk_forward_step_split": (C.c_int32, [_P, _P, _P, _U32P, C.c_int32, _U32P, _U32P, C.c_int32, _I32P, C.c_int32,
+                                          _I32P, C.c_int32, C.c_int32, _P, C.c_int32, C.c_int32, _I32P]),
     "yk_kv_pool_destroy": (None, [_P]),
     "yk_kv_pool_num_blocks": (C.c_int32, [_P]),
     "yk_kv_pool_fill_random": (C.c_int32, [_P, C.c_uint64, C.c_float]),
@@ -134,6 +137,9 @@ _PROTOS = {
 _HOST_PROTOS = {
     "ykh_scheduler_create": (C.c_int32, [_P, _P, _P, _P, _P, C.c_int32, C.c_float, C.c_uint64, C.POINTER(_P)]),
     "ykh_scheduler_destroy": (None, [_P]),
+    "ykh_scheduler_create_split": (C.c_int32, [_P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_float, C.c_uint64,
+                                               C.POINTER(_P)]),
+    "ykh_usage_windowed": (C.c_float, [_P, C.c_int32]),
     "ykh_submit": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
     "ykh_submit_cached": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
     "ykh_submit_stream": (C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32, C.c_void_p,
@@ -424,6 +430,18 @@ class Model:
         check(lib().yk_model_load_safetensors(self.h, arr, len(files), norm_offset, flags, C.byref(n)))
         return n.value
 
+    def forward_split(self, pool: "KVPool", wpool: "KVPool", tokens, q_starts, ctx, block_tables: np.ndarray,
+                      wblock_tables: np.ndarray, last_n: int = 0) -> int:
+        """yk_forward_step_split: global layers in `pool`, windowed ones in `wpool`."""
+        tok, qs, cl = u32(tokens), u32(q_starts), u32(ctx)
+        bt, wbt = i32(block_tables), i32(wblock_tables)
+        rows = C.c_int32()
+        check(lib().yk_forward_step_split(self.h, pool.h, wpool.h, ptr(tok, C.c_uint32), len(tok),
+                                          ptr(qs, C.c_uint32), ptr(cl, C.c_uint32), len(cl), ptr(bt, C.c_int32),
+                                          bt.shape[1], ptr(wbt, C.c_int32), wbt.shape[1], last_n, None, 0, 0,
+                                          C.byref(rows)))
+        return rows.value
+
     def forward(self, pool: "KVPool", tokens, q_starts, ctx, block_tables: np.ndarray, last_n: int = 0) -> int:
         tok, qs, cl = u32(tokens), u32(q_starts), u32(ctx)
         bt = i32(block_tables)
@@ -466,11 +484,15 @@ class Model:
             self.h = _P()
 
 
+POOL_ALL_LAYERS, POOL_GLOBAL_LAYERS, POOL_WINDOWED_LAYERS = 0, 1, 2
+
+
 class KVPool:
-    def __init__(self, engine: Engine, cfg: ModelConfig, num_blocks: int):
+    def __init__(self, engine: Engine, cfg: ModelConfig, num_blocks: int, layers: int = POOL_ALL_LAYERS):
+        """layers: POOL_ALL_LAYERS, or one kind of layer (yk_kv_pool_create_layers)."""
         self.cfg = cfg
         self.h = _P()
-        check(lib().yk_kv_pool_create(engine.h, C.byref(cfg), num_blocks, C.byref(self.h)))
+        check(lib().yk_kv_pool_create_layers(engine.h, C.byref(cfg), num_blocks, layers, C.byref(self.h)))
 
     def fill_random(self, seed: int, std: float):
         check(lib().yk_kv_pool_fill_random(self.h, seed, std))
@@ -551,10 +573,15 @@ class Scheduler:
     """libyk_host.so's Scheduler (restates S/Scheduler.swift's speculative loop)."""
 
     def __init__(self, target: Model, tpool: KVPool, draft: Model, dpool: KVPool, sampler: Sampler, k: int,
-                 temperature: float, seed: int):
+                 temperature: float, seed: int, twpool: KVPool | None = None, dwpool: KVPool | None = None):
+        """twpool / dwpool: windowed-layer pools (ykh_scheduler_create_split)."""
         self.h = _P()
-        check(host_lib().ykh_scheduler_create(target.h, tpool.h, draft.h, dpool.h, sampler.h, k, temperature, seed,
-                                              C.byref(self.h)))
+        if twpool is None:
+            check(host_lib().ykh_scheduler_create(target.h, tpool.h, draft.h, dpool.h, sampler.h, k, temperature, seed,
+                                                  C.byref(self.h)))
+        else:
+            check(host_lib().ykh_scheduler_create_split(target.h, tpool.h, twpool.h, draft.h, dpool.h, dwpool.h,
+                                                        sampler.h, k, temperature, seed, C.byref(self.h)))
 
     def submit(self, prompt, max_tokens: int, stop_token: int = -1, seq_id: int = 0, cached: bool = False):
         p = u32(prompt)
@@ -606,6 +633,9 @@ class Scheduler:
 
     def usage(self, draft: bool = False) -> float:
         return float(host_lib().ykh_usage(self.h, 1 if draft else 0))
+
+    def usage_windowed(self, draft: bool = False) -> float:
+        return float(host_lib().ykh_usage_windowed(self.h, 1 if draft else 0))
 
     def close(self):
         if self.h:

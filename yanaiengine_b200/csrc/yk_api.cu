@@ -476,19 +476,26 @@ extern "C" yk_status yk_model_get_tensor(yk_model* m, int32_t t, int32_t layer, 
 // ---------------------------------------------------------------------------
 // KV pool
 // ---------------------------------------------------------------------------
-extern "C" yk_status yk_kv_pool_create(yk_engine* e, const yk_model_config* cfg, int32_t num_blocks, yk_kv_pool** out) {
+extern "C" yk_status yk_kv_pool_create_layers(yk_engine* e, const yk_model_config* cfg, int32_t num_blocks,
+                                              int32_t layers, yk_kv_pool** out) {
     YK_ARG(e && out, "null handle");
     *out = nullptr;
     YK_TRY(validate_cfg(cfg));
     YK_ARG(num_blocks > 0, "num_blocks");
+    YK_ARG(layers >= YK_POOL_ALL_LAYERS && layers <= YK_POOL_WINDOWED_LAYERS, "layers (YK_POOL_*)");
+    int n_pool_layers = 0;
+    for (int l = 0; l < cfg->n_layers; ++l) n_pool_layers += yk::pool_layer_index(*cfg, layers, l) >= 0 ? 1 : 0;
+    YK_ARG(n_pool_layers > 0, "the model has no layer of this kind");
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     auto* p = new yk_kv_pool();
     p->e = e;
     p->cfg = *cfg;
     p->num_blocks = num_blocks;
+    p->kind = layers;
+    p->n_pool_layers = n_pool_layers;
     p->esize = cfg->dtype == YK_DTYPE_BF16 ? 2 : 4;
     p->layer_elems = (size_t)2 * cfg->n_kv_heads * YK_BLOCK_SIZE * cfg->head_dim;
-    p->block_elems = p->layer_elems * cfg->n_layers;
+    p->block_elems = p->layer_elems * n_pool_layers;
     const size_t bytes = p->block_elems * num_blocks * p->esize;
     cudaError_t err = cudaMalloc(&p->data, bytes);
     if (err != cudaSuccess) {
@@ -515,6 +522,10 @@ extern "C" yk_status yk_kv_pool_create(yk_engine* e, const yk_model_config* cfg,
     return YK_OK;
 }
 
+extern "C" yk_status yk_kv_pool_create(yk_engine* e, const yk_model_config* cfg, int32_t num_blocks, yk_kv_pool** out) {
+    return yk_kv_pool_create_layers(e, cfg, num_blocks, YK_POOL_ALL_LAYERS, out);
+}
+
 extern "C" void yk_kv_pool_destroy(yk_kv_pool* p) {
     if (!p) return;
     cudaSetDevice(p->e->device);
@@ -537,12 +548,14 @@ extern "C" yk_status yk_kv_pool_read_page(yk_kv_pool* p, int32_t block, int32_t 
     YK_ARG(p && host, "null handle");
     YK_ARG(block >= 0 && block < p->num_blocks && layer >= 0 && layer < p->cfg.n_layers && (kv == 0 || kv == 1),
            "page index");
+    const int pl = yk::pool_layer_index(p->cfg, p->kind, layer);
+    YK_ARG(pl >= 0, "the pool does not hold this layer");
     yk_engine* e = p->e;
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     const size_t n = (size_t)p->cfg.n_kv_heads * YK_BLOCK_SIZE * p->cfg.head_dim;
     YK_TRY(e->ensure_pinned(n * p->esize));
     YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
-    const uint8_t* src = (const uint8_t*)p->data + ((size_t)block * p->block_elems + (size_t)layer * p->layer_elems +
+    const uint8_t* src = (const uint8_t*)p->data + ((size_t)block * p->block_elems + (size_t)pl * p->layer_elems +
                                                     (size_t)kv * n) * p->esize;
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, src, n * p->esize, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
@@ -556,11 +569,33 @@ extern "C" yk_status yk_kv_pool_read_page(yk_kv_pool* p, int32_t block, int32_t 
 // ---------------------------------------------------------------------------
 // dt.d: the last dt.nd tokens of every sequence come from device-resident draft
 // tokens (tokens[] holds placeholders there); the host never waits for them.
+// Split pools (wpool != null): `pool` holds the global layers with block_tables,
+// `wpool` the windowed layers with wtables.
+struct WindowedPool {
+    yk_kv_pool* pool = nullptr;
+    const int32_t* tables = nullptr;
+    int32_t max_blocks = 0;
+};
+
 static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tokens, int32_t T,
                               const uint32_t* q_starts, const uint32_t* ctx, int32_t B, const int32_t* block_tables,
-                              int32_t max_blocks, int32_t last_n, int32_t* n_rows, const yk::DraftTokens& dt) {
+                              int32_t max_blocks, int32_t last_n, int32_t* n_rows, const yk::DraftTokens& dt,
+                              const WindowedPool& wp = {}) {
     YK_ARG(m && pool && tokens && q_starts && ctx && block_tables, "null argument");
     const auto& c = m->cfg;
+    yk_kv_pool* const wpool = wp.pool;
+    if (wpool) {
+        YK_ARG(wp.tables && wp.max_blocks > 0, "windowed page tables");
+        YK_ARG(pool->kind == YK_POOL_GLOBAL_LAYERS && wpool->kind == YK_POOL_WINDOWED_LAYERS,
+               "split pools: a YK_POOL_GLOBAL_LAYERS pool and a YK_POOL_WINDOWED_LAYERS pool");
+        YK_ARG(wpool->e == m->e && wpool->cfg.n_layers == c.n_layers && wpool->cfg.n_kv_heads == c.n_kv_heads &&
+                   wpool->cfg.head_dim == c.head_dim && wpool->cfg.dtype == c.dtype &&
+                   wpool->cfg.window == c.window && wpool->cfg.window_layer_parity == c.window_layer_parity &&
+                   pool->cfg.window == c.window && pool->cfg.window_layer_parity == c.window_layer_parity,
+               "windowed pool does not match the model");
+    } else {
+        YK_ARG(pool->kind == YK_POOL_ALL_LAYERS, "a pool of one layer kind needs yk_forward_step_split");
+    }
     yk_engine* e = m->e;
     YK_ARG(pool->e == e, "pool belongs to another engine");
     YK_ARG(pool->cfg.n_layers == c.n_layers && pool->cfg.n_kv_heads == c.n_kv_heads &&
@@ -580,6 +615,13 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         for (uint32_t p = 0; p < (ctx[b] + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE; ++p) {
             const int32_t blk = block_tables[(size_t)b * max_blocks + p];
             YK_ARG(blk >= 0 && blk < pool->num_blocks, "block id outside the pool");
+        }
+        if (wpool) {
+            YK_ARG((int64_t)(ctx[b] + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE <= wp.max_blocks, "windowed page table too short");
+            for (uint32_t p = 0; p < (ctx[b] + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE; ++p) {
+                const int32_t blk = wp.tables[(size_t)b * wp.max_blocks + p];
+                YK_ARG(blk >= 0 && blk < wpool->num_blocks, "block id outside the windowed pool");
+            }
         }
         R += last_n > 0 ? std::min<int>(last_n, (int)n) : (int)n;
     }
@@ -622,7 +664,8 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         }
     }
     const size_t nattn = it_g.size() + cb_g.size() + it_w.size() + cb_w.size();
-    const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R + nattn;
+    const size_t nsplit = wpool ? (size_t)T + (size_t)B * wp.max_blocks : 0;  // windowed slots + page tables
+    const size_t nmeta = (size_t)4 * T + (B + 1) + B + (size_t)B * max_blocks + R + nattn + nsplit;
     // Metadata slot of this call.  Async: the upload runs on the engine's upload
     // stream as soon as the slot's previous forward (META_SLOTS calls ago) and the
     // work enqueued after it are done, so it overlaps the kernels still running;
@@ -689,6 +732,19 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
             w += v->size();
         }
     }
+    int32_t* const h_wslot = h_attn + nattn;  // split pools only
+    int32_t* const h_wbt = h_wslot + T;
+    if (wpool) {
+        for (int b = 0; b < B; ++b) {
+            const int n = (int)(q_starts[b + 1] - q_starts[b]);
+            for (int i = 0; i < n; ++i) {
+                const int pos = (int)ctx[b] - n + i;
+                h_wslot[(int)q_starts[b] + i] =
+                    wp.tables[(size_t)b * wp.max_blocks + pos / YK_BLOCK_SIZE] * YK_BLOCK_SIZE + pos % YK_BLOCK_SIZE;
+            }
+        }
+        std::memcpy(h_wbt, wp.tables, (size_t)B * wp.max_blocks * 4);
+    }
     if (async) {
         YK_TRY(e->up_submit_on(up_slot, meta, nmeta * 4, e->up_stream));
         YK_CHECK_CUDA(cudaEventRecord(m->meta_copied[ms], e->up_stream));
@@ -712,6 +768,9 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         m->cur.n_comb[1] = (int)(cb_w.size() / 5);
     }
     const int32_t* dm = meta;
+    m->cur.wslot = wpool ? meta + (h_wslot - hm) : nullptr;
+    m->cur.wbt = wpool ? meta + (h_wbt - hm) : nullptr;
+    m->cur.wmax_blocks = wpool ? wp.max_blocks : 0;
     m->cur.tokens = dm;
     m->cur.pos = dm + T;
     m->cur.slot = dm + 2 * T;
@@ -772,18 +831,23 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         eq.kv_dim = kvd;
         eq.head_dim = dh;
         eq.n_kv = c.n_kv_heads;
+        const bool windowed = layer_windowed(c, l);
+        // split pools: the windowed layers' K/V live in wpool under their own page tables
+        const bool in_w = wpool && windowed;
+        yk_kv_pool* const lpool = in_w ? wpool : pool;
+        const int pl = pool_layer_index(c, lpool->kind, l);
         eq.pos = m->cur.pos;
-        eq.slot = m->cur.slot;
+        eq.slot = in_w ? m->cur.wslot : m->cur.slot;
         eq.rope_denom = m->rope_denom;
         eq.rope_tab = m->rope_tab;
-        eq.pool = pool->data;
-        eq.block_elems = (long long)pool->block_elems;
-        eq.layer_off = (long long)l * (long long)pool->layer_elems;
-        eq.pool_blocks = pool->num_blocks;
+        eq.pool = lpool->data;
+        eq.block_elems = (long long)lpool->block_elems;
+        eq.layer_off = (long long)pl * (long long)lpool->layer_elems;
+        eq.pool_blocks = lpool->num_blocks;
         norm_in(eq);
         YK_TRY(gemm_run(m, L.wqkv, &L.tm_qkv, m->xn, qd + 2 * kvd, d, T, eq));
-        const bool windowed = c.window > 0 && (c.window_layer_parity < 0 || (l % 2) == c.window_layer_parity);
-        YK_TRY(attention_run(m, pool, l, T, B, max_blocks, (windowed ? kv_win : kv_full) * kv_tok_bytes));
+        YK_TRY(attention_run(m, lpool, l, pl, in_w ? m->cur.wbt : m->cur.bt, T, B, in_w ? wp.max_blocks : max_blocks,
+                             (windowed ? kv_win : kv_full) * kv_tok_bytes));
         EpiParams er;
         er.kind = EPI_RESID;
         er.ref_compat = c.ref_compat;
@@ -857,6 +921,27 @@ extern "C" yk_status yk_forward_step_drafts(yk_model* m, yk_kv_pool* pool, const
     dt.j0 = j0;
     dt.nd = nd;
     return forward_impl(m, pool, tokens, T, q_starts, ctx, B, block_tables, max_blocks, last_n, n_rows, dt);
+}
+
+extern "C" yk_status yk_forward_step_split(yk_model* m, yk_kv_pool* pool, yk_kv_pool* wpool, const uint32_t* tokens,
+                                           int32_t T, const uint32_t* q_starts, const uint32_t* ctx, int32_t B,
+                                           const int32_t* block_tables, int32_t max_blocks,
+                                           const int32_t* wblock_tables, int32_t wmax_blocks, int32_t last_n,
+                                           yk_sampler* s, int32_t j0, int32_t nd, int32_t* n_rows) {
+    YK_ARG(wpool != nullptr, "null windowed pool");
+    yk::DraftTokens dt;
+    if (s && nd > 0) {
+        dt.d = yk::sampler_device_drafts(s, B, &dt.k);
+        YK_ARG(dt.d != nullptr, "batch larger than the sampler's");
+        YK_ARG(j0 >= 0 && j0 + nd <= dt.k, "draft token range outside 0..k-1");
+        dt.j0 = j0;
+        dt.nd = nd;
+    }
+    WindowedPool wp;
+    wp.pool = wpool;
+    wp.tables = wblock_tables;
+    wp.max_blocks = wmax_blocks;
+    return forward_impl(m, pool, tokens, T, q_starts, ctx, B, block_tables, max_blocks, last_n, n_rows, dt, wp);
 }
 
 extern "C" yk_status yk_logits_copy_to_host(yk_model* m, int32_t row0, int32_t rows, float* host) {

@@ -770,7 +770,10 @@ void plan_attention(const yk_model_config& c, int num_sms, int waves, bool balan
     *n_slots = slot;
 }
 
-yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks, double kv_bytes) {
+// layer: the model's layer (its window); pool_layer: its index within `pool`;
+// bt: the page tables of `pool` ([B x max_blocks]).
+yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int pool_layer, const int32_t* bt, int T, int B,
+                        int max_blocks, double kv_bytes) {
     (void)B;
     const auto& c = m->cfg;
     const double es = c.dtype == YK_DTYPE_BF16 ? 2.0 : 4.0;
@@ -783,15 +786,15 @@ yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, 
     p.pos = m->cur.pos;
     p.q_starts = m->cur.q_starts;
     p.ctx = m->cur.ctx;
-    p.block_tables = m->cur.bt;
+    p.block_tables = bt;
     p.max_blocks = max_blocks;
     p.T = T;
     p.H = c.n_heads;
     p.Hkv = c.n_kv_heads;
     p.dh = c.head_dim;
     p.block_elems = (long long)pool->block_elems;
-    p.layer_off = (long long)layer * (long long)pool->layer_elems;
-    p.layer = layer;
+    p.layer_off = (long long)pool_layer * (long long)pool->layer_elems;
+    p.layer = pool_layer;
     p.pool_blocks = pool->num_blocks;
     p.scale = 1.0f / sqrtf((float)c.head_dim);
     p.cap = c.attn_cap;
@@ -829,7 +832,7 @@ size_t attention_ws_floats_per_slot(int head_dim) { return (size_t)AT_ROWS * ws_
 // within a block ([layer][K|V][kv head][16 slots]), z = block; box 64 x 16 x 1.
 yk_status make_pool_map(yk_engine* e, yk_kv_pool* pool) {
     const auto& c = pool->cfg;
-    const cuuint64_t dims[3] = {(cuuint64_t)c.head_dim, (cuuint64_t)c.n_layers * 2 * c.n_kv_heads * 16,
+    const cuuint64_t dims[3] = {(cuuint64_t)c.head_dim, (cuuint64_t)pool->n_pool_layers * 2 * c.n_kv_heads * 16,
                                 (cuuint64_t)pool->num_blocks};
     const cuuint64_t strides[2] = {(cuuint64_t)c.head_dim * 2, (cuuint64_t)pool->block_elems * 2};
     const cuuint32_t box[3] = {64, 16, 1};

@@ -161,6 +161,8 @@ struct yk_model {
     int32_t last_rows = 0;
     struct {
         const int32_t *tokens, *pos, *slot, *seq, *q_starts, *ctx, *bt, *rows;
+        const int32_t *wslot, *wbt;  // split pools: the windowed layers' slots and page tables (else null)
+        int wmax_blocks;
         const int32_t* attn_items[2];  // [0] global layers, [1] windowed layers
         const int32_t* attn_comb[2];
         int n_items[2], n_comb[2];
@@ -199,7 +201,24 @@ struct yk_kv_pool {
     size_t layer_elems = 0;    // elements per layer within a block
     CUtensorMap tm{};          // bf16 pools: 3-D TMA map (head dim, row in block, block)
     bool has_tm = false;
+    int32_t kind = 0;          // YK_POOL_*: the layers a block holds
+    int32_t n_pool_layers = 0; // layers per block
 };
+namespace yk {
+// Whether layer l of cfg is windowed, and its index within a pool of `kind`
+// (-1: the pool does not hold it).
+inline bool layer_windowed(const yk_model_config& c, int l) {
+    return c.window > 0 && (c.window_layer_parity < 0 || (l % 2) == c.window_layer_parity);
+}
+inline int pool_layer_index(const yk_model_config& c, int kind, int l) {
+    if (kind == YK_POOL_ALL_LAYERS) return l;
+    const bool want_w = kind == YK_POOL_WINDOWED_LAYERS;
+    if (layer_windowed(c, l) != want_w) return -1;
+    int idx = 0;
+    for (int i = 0; i < l; ++i) idx += layer_windowed(c, i) == want_w ? 1 : 0;
+    return idx;
+}
+}  // namespace yk
 
 struct yk_sampler {
     yk_engine* e = nullptr;
@@ -305,7 +324,8 @@ yk_status gemm_chain_glu_down(yk_model* m, const void* Wgu, const CUtensorMap* t
                               const void* Wd, const CUtensorMap* tmWd, const void* X1, int n_d, int K1, int m_tok,
                               const EpiParams& eg, const EpiParams& ed);
 yk_status make_weight_map(yk_engine* e, CUtensorMap* map, const void* W, int rows, int K);
-yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int T, int B, int max_blocks,
+yk_status attention_run(yk_model* m, yk_kv_pool* pool, int layer, int pool_layer, const int32_t* bt, int T, int B,
+                        int max_blocks,
                         double kv_bytes);
 void plan_attention(const yk_model_config& c, int num_sms, int waves, bool balanced, const uint32_t* q_starts,
                     const uint32_t* ctx, int B, bool windowed, std::vector<int32_t>& items, std::vector<int32_t>& comb,

@@ -108,6 +108,9 @@ struct SequenceRequest {
     uint32_t id = 0;
     std::vector<uint32_t> prompt, generated;
     std::unique_ptr<PagedKVCache> cache, draft_cache;
+    // split pools: the windowed layers' page tables (same positions as cache /
+    // draft_cache), else null
+    std::unique_ptr<PagedKVCache> wcache, draft_wcache;
     int max_tokens = 0;
     int64_t stop_token = -1;
     bool finished = false;
@@ -132,6 +135,11 @@ struct ykh_scheduler {
     uint64_t seed = 0;
     uint32_t step_no = 0;
     std::unique_ptr<BlockAllocator> talloc, dalloc;
+    // split pools (ykh_scheduler_create_split): windowed-layer pools and allocators
+    yk_kv_pool* twpool = nullptr;
+    yk_kv_pool* dwpool = nullptr;
+    std::unique_ptr<BlockAllocator> twalloc, dwalloc;
+    int tw_width = 0, dw_width = 0;  // their window widths
     std::deque<std::unique_ptr<SequenceRequest>> waiting;
     std::vector<std::unique_ptr<SequenceRequest>> running, done;
     int64_t n_steps = 0, n_emitted = 0, n_accepted = 0;
@@ -141,7 +149,7 @@ struct ykh_scheduler {
     bool reclaim = true;
     // per-step scratch
     std::vector<uint32_t> tokens, qstarts, ctx, seq_ids, drafts, out_tokens;
-    std::vector<int32_t> tables, counts;
+    std::vector<int32_t> tables, wtables, counts;
 };
 
 extern "C" yk_status ykh_scheduler_create(yk_model* target, yk_kv_pool* tpool, yk_model* draft, yk_kv_pool* dpool,
@@ -170,6 +178,29 @@ extern "C" yk_status ykh_scheduler_create(yk_model* target, yk_kv_pool* tpool, y
     return YK_OK;
 }
 
+extern "C" yk_status ykh_scheduler_create_split(yk_model* target, yk_kv_pool* target_pool, yk_kv_pool* target_wpool,
+                                                yk_model* draft, yk_kv_pool* draft_pool, yk_kv_pool* draft_wpool,
+                                                yk_sampler* sampler, int32_t k, float temperature, uint64_t seed,
+                                                ykh_scheduler** out) {
+    if (!target_wpool || !draft_wpool || !out) return YK_ERR_ARG;
+    YK_TRY(ykh_scheduler_create(target, target_pool, draft, draft_pool, sampler, k, temperature, seed, out));
+    ykh_scheduler* s = *out;
+    yk_model_config tc{}, dc{};
+    if (yk_model_get_config(target, &tc) != YK_OK || yk_model_get_config(draft, &dc) != YK_OK || tc.window <= 0 ||
+        dc.window <= 0) {
+        ykh_scheduler_destroy(s);
+        *out = nullptr;
+        return YK_ERR_ARG;
+    }
+    s->twpool = target_wpool;
+    s->dwpool = draft_wpool;
+    s->twalloc = std::make_unique<BlockAllocator>(yk_kv_pool_num_blocks(target_wpool));
+    s->dwalloc = std::make_unique<BlockAllocator>(yk_kv_pool_num_blocks(draft_wpool));
+    s->tw_width = tc.window;
+    s->dw_width = dc.window;
+    return YK_OK;
+}
+
 extern "C" void ykh_scheduler_destroy(ykh_scheduler* s) {
     if (!s) return;
     s->waiting.clear();
@@ -192,10 +223,19 @@ static yk_status submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int
     r->stop_token = stop;
     r->cache = std::make_unique<PagedKVCache>(s->talloc.get());
     r->draft_cache = std::make_unique<PagedKVCache>(s->dalloc.get());
+    if (s->twpool) {
+        r->wcache = std::make_unique<PagedKVCache>(s->twalloc.get());
+        r->draft_wcache = std::make_unique<PagedKVCache>(s->dwalloc.get());
+    }
     if (cached) {
         if (!r->cache->reserve(n - 1) || !r->draft_cache->reserve(n - 1)) return YK_ERR_OOM;
         r->cache->current_position = n - 1;
         r->draft_cache->current_position = n - 1;
+        if (r->wcache) {
+            if (!r->wcache->reserve(n - 1) || !r->draft_wcache->reserve(n - 1)) return YK_ERR_OOM;
+            r->wcache->current_position = n - 1;
+            r->draft_wcache->current_position = n - 1;
+        }
         s->running.push_back(std::move(r));
     } else {
         s->waiting.push_back(std::move(r));
@@ -228,10 +268,17 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
     s->qstarts.assign(1, 0);
     s->ctx.clear();
     size_t max_pages = 1;
+    const bool split = s->twpool != nullptr;
+    size_t wmax_pages = 1;
     for (int b = 0; b < B; ++b) {
         PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
         const int n = (int)inputs[b].size();
         if (!c->reserve(c->current_position + n)) return YK_ERR_OOM;  // S/PagedKVCache.swift:31-33
+        if (split) {
+            PagedKVCache* wc = is_draft ? s->running[b]->draft_wcache.get() : s->running[b]->wcache.get();
+            if (!wc->reserve(wc->current_position + n)) return YK_ERR_OOM;
+            wmax_pages = std::max(wmax_pages, wc->page_table.size());
+        }
         s->tokens.insert(s->tokens.end(), inputs[b].begin(), inputs[b].end());
         s->qstarts.push_back((uint32_t)s->tokens.size());
         s->ctx.push_back((uint32_t)(c->current_position + n));
@@ -246,6 +293,24 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
     int32_t rows = 0;
     yk_model* m = is_draft ? s->draft : s->target;
     yk_kv_pool* pool = is_draft ? s->dpool : s->tpool;
+    if (split) {
+        s->wtables.assign((size_t)B * wmax_pages, 0);
+        for (int b = 0; b < B; ++b) {
+            PagedKVCache* wc = is_draft ? s->running[b]->draft_wcache.get() : s->running[b]->wcache.get();
+            int32_t* row = s->wtables.data() + (size_t)b * wmax_pages;
+            for (size_t i = 0; i < wc->page_table.size(); ++i) row[i] = wc->page_table[i] >= 0 ? wc->page_table[i] : 0;
+        }
+        YK_TRY(yk_forward_step_split(m, pool, is_draft ? s->dwpool : s->twpool, s->tokens.data(),
+                                     (int32_t)s->tokens.size(), s->qstarts.data(), s->ctx.data(), B, s->tables.data(),
+                                     (int32_t)max_pages, s->wtables.data(), (int32_t)wmax_pages, last_n,
+                                     nd > 0 ? s->sampler : nullptr, j0, nd, &rows));
+        for (int b = 0; b < B; ++b) {
+            SequenceRequest* r = s->running[b].get();
+            (is_draft ? r->draft_cache : r->cache)->current_position += (int)inputs[b].size();
+            (is_draft ? r->draft_wcache : r->wcache)->current_position += (int)inputs[b].size();
+        }
+        return YK_OK;
+    }
     yk_status st = nd > 0 ? yk_forward_step_drafts(m, pool, s->tokens.data(), (int32_t)s->tokens.size(),
                                                    s->qstarts.data(), s->ctx.data(), B, s->tables.data(),
                                                    (int32_t)max_pages, last_n, s->sampler, j0, nd, &rows)
@@ -269,6 +334,7 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
     YK_TRY(yk_model_get_config(s->draft, &dc));
     const int max_batch = std::min(tc.max_seqs, dc.max_seqs);
     while (!s->waiting.empty() && s->talloc->usage() < 0.9f && s->dalloc->usage() < 0.9f &&
+           (!s->twalloc || (s->twalloc->usage() < 0.9f && s->dwalloc->usage() < 0.9f)) &&
            (int)s->running.size() < max_batch) {
         s->running.push_back(std::move(s->waiting.front()));
         s->waiting.pop_front();
@@ -323,6 +389,14 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
         const int a = cnt - 1;  // accepted drafts
         r->cache->rollback(N[b] + a);
         r->draft_cache->rollback(std::min(r->draft_cache->current_position, N[b] + a));
+        if (r->wcache) {
+            r->wcache->rollback(N[b] + a);
+            r->draft_wcache->rollback(std::min(r->draft_wcache->current_position, N[b] + a));
+            if (s->reclaim) {  // every layer of these pools is windowed
+                r->wcache->reclaim_window(s->tw_width);
+                r->draft_wcache->reclaim_window(s->dw_width);
+            }
+        }
         for (int i = 0; i < cnt; ++i) r->generated.push_back(s->out_tokens[(size_t)b * (k + 1) + i]);
         for (int i = 0; i < cnt; ++i)
             if (r->stop_token >= 0 && s->out_tokens[(size_t)b * (k + 1) + i] == (uint32_t)r->stop_token) {
@@ -344,6 +418,10 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
         if ((*it)->finished) {
             (*it)->cache->reset();
             (*it)->draft_cache->reset();
+            if ((*it)->wcache) {
+                (*it)->wcache->reset();
+                (*it)->draft_wcache->reset();
+            }
             if ((*it)->on_done) (*it)->on_done((*it)->user, (*it)->id, (int32_t)(*it)->generated.size());
             s->done.push_back(std::move(*it));
             it = s->running.erase(it);
@@ -388,6 +466,11 @@ extern "C" yk_status ykh_counters(const ykh_scheduler* s, int64_t* steps, int64_
     if (emitted) *emitted = s->n_emitted;
     if (accepted) *accepted = s->n_accepted;
     return YK_OK;
+}
+
+extern "C" float ykh_usage_windowed(const ykh_scheduler* s, int32_t draft) {
+    if (!s || !s->twalloc) return 0.f;
+    return draft ? s->dwalloc->usage() : s->twalloc->usage();
 }
 
 extern "C" float ykh_usage(const ykh_scheduler* s, int32_t draft) {
