@@ -277,3 +277,34 @@ def test_split_pools_free_windowed_pages(lib):
             off.close()
     finally:
         r.close()
+
+
+from hypothesis import HealthCheck, given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+
+@settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(st.lists(st.tuples(st.integers(1, 70), st.integers(1, 60)), min_size=1, max_size=6),
+       st.sampled_from([(0, -1), (16, -1), (24, -1), (24, 0), (40, 1)]), st.booleans(), st.booleans(),
+       st.integers(24, 160))
+def test_scheduler_property(lib, reqs, schedule, reclaim, split, blocks):
+    """Random batches, window schedules, pool sizes, reclamation on/off, one or two
+    pools: a run either completes -- every request with at least max_tokens tokens,
+    every page returned, no forward ever handed an invalid or shared page -- or
+    stops with YK_ERR_OOM; it never corrupts the page tables."""
+    window, parity = schedule
+    split = split and window > 0 and parity >= 0  # split pools need global and windowed layers
+    r = Rig(lib, blocks=blocks, window=window, parity=parity, reclaim=reclaim, wblocks=blocks if split else 0)
+    try:
+        for i, (n, mt) in enumerate(reqs):
+            r.submit(i, n, max_tokens=mt)
+        usage, st_ = r.run(max_steps=400)
+        assert st_ in (0, 2), st_
+        assert r.stats()[0] == 0
+        if st_ == 0:
+            for i, (_, mt) in enumerate(reqs):
+                assert mt <= len(r.generated(i)) <= mt + K
+            last = usage[-1] if usage else 0.0
+            assert (last == (0.0, 0.0, 0.0)) if split else (last == 0.0)
+    finally:
+        r.close()
