@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import ctypes as C
 import shutil
+import os
 import subprocess
 from pathlib import Path
 
@@ -26,7 +27,11 @@ def lib(tmp_path_factory):
     if not cxx:
         pytest.skip("g++ not found")
     out = tmp_path_factory.mktemp("hoststub") / "libyk_host_stub.so"
-    subprocess.run([cxx, "-O1", "-std=c++17", "-fPIC", "-shared", "-Wl,-Bsymbolic", "-o", str(out),
+    # YKH_STUB_SANITIZE=1 builds with AddressSanitizer + UBSan; run pytest with
+    # LD_PRELOAD=$(g++ -print-file-name=libasan.so) so the runtime loads first.
+    san = ["-g", "-fno-omit-frame-pointer", "-fsanitize=address,undefined",
+           "-fno-sanitize-recover=undefined"] if os.environ.get("YKH_STUB_SANITIZE") else []
+    subprocess.run([cxx, "-O1", "-std=c++17", "-fPIC", "-shared", "-Wl,-Bsymbolic", *san, "-o", str(out),
                     str(ROOT / "yanaiengine_b200" / "host" / "yk_host.cpp"), str(ROOT / "tests" / "host_stub" / "yk_stub.cpp"),
                     f"-I{ROOT / 'include'}"], check=True, capture_output=True)
     L = C.CDLL(str(out))

@@ -258,3 +258,29 @@ def test_reader_rejects_wrong_structures(tmp_path_factory, value):
             assert ti.nbytes <= 16
     finally:
         stf.close()
+
+
+def test_reader_names_are_utf8(tmp_path):
+    """Header text is UTF-8 (JSON): multi-byte names, raw or escaped, come back
+    byte-identical; malformed sequences (a stray continuation byte, an overlong
+    form, a surrogate, a code point above U+10FFFF, a truncated sequence, 0xFF)
+    make the file invalid instead of reaching callers that decode names."""
+    arr = np.arange(2, dtype=np.float32)
+    p = tmp_path / "u.safetensors"
+    names = ["béta", "名前.weight", "x\U0001F600y", "߿ࠀ￿\U0010FFFF"]
+    hdr, data = header_and_data({n: ("F32", arr) for n in names})
+    for escaped in (False, True):
+        write_raw(p, json.dumps(hdr, ensure_ascii=escaped).encode(), data)
+        stf = abi.SafeTensors(p)
+        try:
+            assert stf.names() == sorted(names, key=lambda s: s.encode())
+            for n in names:
+                assert stf.array(n).tobytes() == arr.tobytes()
+        finally:
+            stf.close()
+    entry = b'": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]}}'
+    for bad in (b"\x80", b"a\xbfb", b"\xc0\xaf", b"\xc1\xbf", b"\xe0\x80\xaf", b"\xed\xa0\x80",
+                b"\xf0\x80\x80\xaf", b"\xf4\x90\x80\x80", b"\xf5\x80\x80\x80", b"\xe2\x82", b"\xe2\x82x",
+                b"\xff", b"\xfe"):
+        write_raw(p, b'{"' + bad + entry, data)
+        _expect_invalid(p, "not a JSON object")

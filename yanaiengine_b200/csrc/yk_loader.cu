@@ -88,6 +88,35 @@ class JParser {
             s += (char)(0x80 | (cp & 0x3F));
         }
     }
+    // One raw multi-byte character whose lead byte c was just consumed, appended to
+    // s if it is well-formed UTF-8 (RFC 3629: no overlong forms, no surrogates,
+    // nothing above U+10FFFF) -- JSON text is UTF-8, and names end up as C strings
+    // that callers decode as UTF-8.
+    bool utf8_seq(unsigned char c, std::string& s) {
+        int n;
+        unsigned char lo = 0x80, hi = 0xBF;  // range of the second byte
+        if (c >= 0xC2 && c <= 0xDF) n = 1;
+        else if (c >= 0xE0 && c <= 0xEF) {
+            n = 2;
+            if (c == 0xE0) lo = 0xA0;
+            if (c == 0xED) hi = 0x9F;
+        } else if (c >= 0xF0 && c <= 0xF4) {
+            n = 3;
+            if (c == 0xF0) lo = 0x90;
+            if (c == 0xF4) hi = 0x8F;
+        } else {
+            return false;
+        }
+        if (end_ - p_ < n) return false;
+        for (int k = 0; k < n; ++k) {
+            const unsigned char b = (unsigned char)p_[k];
+            if (k == 0 ? (b < lo || b > hi) : (b < 0x80 || b > 0xBF)) return false;
+        }
+        s += (char)c;
+        s.append(p_, (size_t)n);
+        p_ += n;
+        return true;
+    }
     bool hex4(unsigned& v) {
         if (end_ - p_ < 4) return false;
         v = 0;
@@ -108,6 +137,10 @@ class JParser {
             const unsigned char c = (unsigned char)*p_++;
             if (c == '"') return true;
             if (c < 0x20) return false;
+            if (c >= 0x80) {
+                if (!utf8_seq(c, s)) return false;
+                continue;
+            }
             if (c != '\\') {
                 s += (char)c;
                 continue;
