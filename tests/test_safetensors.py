@@ -164,6 +164,8 @@ def test_hf_name_mapping():
         assert abi.hf_tensor_id(name, L) == want, name
     for bad in ("model.layers.4.mlp.up_proj.weight",           # layer past the model
                 "model.layers.x.mlp.up_proj.weight", "model.layers..mlp.up_proj.weight",
+                "model.layers.03.mlp.up_proj.weight", "model.layers.00.mlp.up_proj.weight",  # one name per slot
+                "model.layers.+3.mlp.up_proj.weight", "model.layers.-0.mlp.up_proj.weight",
                 "model.layers.0.pre_feedforward_layernorm.weight",  # Gemma-2 norm: no slot here
                 "model.layers.0.self_attn.q_proj.bias", "model.rotary_emb.inv_freq", "lm_head", ""):
         with pytest.raises(abi.YKError) as ei:

@@ -694,7 +694,8 @@ static bool hf_tensor(const std::string& name, int n_layers, int32_t* t, int32_t
     if (name.compare(0, pre.size(), pre) != 0) return false;
     size_t p = pre.size(), q = p;
     while (q < name.size() && name[q] >= '0' && name[q] <= '9') ++q;
-    if (q == p || q - p > 6 || q >= name.size() || name[q] != '.') return false;
+    // canonical decimal only ("7", not "07"), so that one name maps to each slot
+    if (q == p || q - p > 6 || (name[p] == '0' && q - p > 1) || q >= name.size() || name[q] != '.') return false;
     const int l = std::atoi(name.substr(p, q - p).c_str());
     if (l >= n_layers) return false;
     const std::string rest = name.substr(q + 1);
