@@ -615,10 +615,11 @@ def main():
             args.batch = 128
         if "--k" not in sys.argv:
             args.k = 4
-    world, rank, local = dist_setup(args.gpus)
     nthreads = os.cpu_count() or 1
 
     if args.impl == "reference":
+        # CPU only: no process group and no GPU; under torchrun rank 0 alone runs
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
         lens = np.random.default_rng(7).integers(512, 2049, args.batch)
@@ -641,6 +642,7 @@ def main():
         }))
         return
 
+    world, rank, local = dist_setup(args.gpus)
     res, lens = (run_prefill if args.workload == "prefill" else run_yk)(args, world, rank, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline and args.workload == "8b-dp":
