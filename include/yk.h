@@ -130,7 +130,7 @@ yk_status yk_engine_profile_read(yk_engine* e, int32_t kernel_class, double* tot
 
 /* ---- model: LlamaModel / GemmaModel weights + forward workspaces. -------- */
 /* Random init on the device: matrices N(0, init_std) from Philox(seed), norms 1
- * (the reference fills U(-1,1): S/Tensor.swift:47-52 -- the configs ask for N(0,0.02)). */
+ * (the reference fills U(-1,1): S/Tensor.swift:47-52 -- the benchmark workloads use N(0,0.02)). */
 yk_status yk_model_create(yk_engine* e, const yk_model_config* cfg, uint64_t seed, float init_std,
                           yk_model** out);
 void      yk_model_destroy(yk_model* m);

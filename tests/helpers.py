@@ -10,11 +10,11 @@ TINY = dict(vocab_size=512, d_model=256, n_layers=2, n_heads=4, n_kv_heads=2, he
             rope_theta=10000.0, rms_eps=1e-5, attn_cap=0.0, final_cap=0.0, window=0, window_layer_parity=-1,
             act=abi.ACT_SILU, ref_compat=0)
 
-# BASELINE config 2 (tiny fp32 verify): target and draft.
-C2_TARGET = dict(vocab_size=32000, d_model=2048, n_layers=8, n_heads=32, n_kv_heads=8, head_dim=64, ffn_dim=5632,
+# Small fp32 speculative workload: a d=2048, 8-layer target and a d=512, 4-layer draft (V=32000).
+SMALL_F32_TARGET = dict(vocab_size=32000, d_model=2048, n_layers=8, n_heads=32, n_kv_heads=8, head_dim=64, ffn_dim=5632,
                  rope_theta=10000.0, rms_eps=1e-5, attn_cap=0.0, final_cap=0.0, window=0, window_layer_parity=-1,
                  act=abi.ACT_SILU, ref_compat=0)
-C2_DRAFT = dict(C2_TARGET, d_model=512, n_layers=4, n_heads=8, n_kv_heads=2, ffn_dim=1408)
+SMALL_F32_DRAFT = dict(SMALL_F32_TARGET, d_model=512, n_layers=4, n_heads=8, n_kv_heads=2, ffn_dim=1408)
 
 
 def gpu_model(engine, cfg: dict, dtype: int, seed: int, num_blocks: int, max_tokens: int = 256, max_seqs: int = 16,

@@ -29,7 +29,7 @@ def test_golden_verify_sequences(engine):
         assert out[0, : cnt[0]].tolist() == c["expect"]
 
 
-def _c1_probs(oracle, B, k, V, seed):
+def _sampler_probs(oracle, B, k, V, seed):
     rng = np.random.default_rng(seed)
     dl = rng.normal(0, 2.0, (B, k, V)).astype(np.float32)
     tl = rng.normal(0, 2.0, (B, k + 1, V)).astype(np.float32)
@@ -40,10 +40,10 @@ def _c1_probs(oracle, B, k, V, seed):
     return p, q, drafts
 
 
-def test_verify_probs_bit_exact_c1(engine, oracle):
-    """Config 1 shapes: 64 sequences, k=4, V=128256, N(0, 2^2) logits."""
+def test_verify_probs_bit_exact_64x4x128256(engine, oracle):
+    """Sampler shapes of the 8B/1B workload at 64 sequences: k=4, V=128256, N(0, 2^2) logits."""
     B, k, V = 64, 4, 128256
-    p, q, drafts = _c1_probs(oracle, B, k, V, 1234)
+    p, q, drafts = _sampler_probs(oracle, B, k, V, 1234)
     seq_ids = np.arange(B, dtype=np.uint32)
     s = abi.Sampler(engine, B, k, V)
     try:

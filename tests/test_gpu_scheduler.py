@@ -1,6 +1,6 @@
 """End-to-end draft->verify through libyk_host.so's Scheduler vs the oracle.
 
-Config 2 of the benchmark spec (tiny fp32 target + draft, batch 1, k=4, greedy,
+The small fp32 speculative workload (d=2048 target + d=512 draft, batch 1, k=4, greedy,
 prompt of 128 uniform ids, 16-token pages): the emitted tokens must be
 identical to the oracle's speculative run, and -- the defining property of
 greedy speculative decoding -- identical to plain greedy decoding of the target.
@@ -10,7 +10,7 @@ import os
 import numpy as np
 import pytest
 
-from helpers import C2_DRAFT, C2_TARGET, TINY, PageTables, gpu_model, oracle_twin, step_inputs
+from helpers import SMALL_F32_DRAFT, SMALL_F32_TARGET, TINY, PageTables, gpu_model, oracle_twin, step_inputs
 from yanaiengine_b200 import abi
 
 pytestmark = pytest.mark.gpu
@@ -81,8 +81,8 @@ def _run(engine, oracle, tcfg, dcfg, dtype, prompt_len, k, steps, seed_t, seed_d
         t.close()
 
 
-def test_c2_greedy_token_identical(engine, oracle):
-    got, orc_t, orc_d, prompt = _run(engine, oracle, C2_TARGET, C2_DRAFT, abi.DTYPE_F32, 128, 4, 5, 1, 2)
+def test_small_f32_greedy_token_identical(engine, oracle):
+    got, orc_t, orc_d, prompt = _run(engine, oracle, SMALL_F32_TARGET, SMALL_F32_DRAFT, abi.DTYPE_F32, 128, 4, 5, 1, 2)
     ref = oracle_greedy_spec(orc_t, orc_d, prompt, 4, 5)
     assert got == ref
     # greedy speculative decoding == greedy decoding of the target alone
