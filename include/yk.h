@@ -38,7 +38,7 @@ typedef int32_t yk_status;
 #define YK_ERR_NCCL         4  /* NCCL error (tensor-parallel target only)               */
 #define YK_ERR_TIMEOUT      5  /* a bounded device-side wait gave up                     */
 #define YK_ERR_DEVICE_CHECK 6  /* an in-kernel bounds check fired                        */
-#define YK_ERR_UNSUPPORTED  7  /* shape/dtype combination this build does not run        */
+#define YK_ERR_UNSUPPORTED  7  /* shape/dtype combination this module does not run       */
 
 #define YK_DTYPE_F32  0
 #define YK_DTYPE_BF16 1

@@ -2,7 +2,7 @@
  * oracle.h -- TEST INFRASTRUCTURE ONLY.
  *
  * CPU restatement of YanAIEngine's speculative draft->verify hot path, used as
- * the checker for the CUDA module (tests/, __graft_entry__.smoke() and the
+ * the reference the CUDA module is tested against (tests/, __graft_entry__.smoke() and the
  * cpu_baseline leg of bench.py).  Nothing in yanaiengine_b200/ links, loads or
  * calls this library; the product path fails loudly without its CUDA module.
  *
@@ -13,7 +13,10 @@
  *   - hand-derived known answers read off the reference source
  *     (tests/golden/sampler_kat.json, made by tests/golden/make_golden.py);
  *   - the one known answer the reference states: 20 appended tokens occupy
- *     2 pages of 16 (Sources/yanaiengine/PagedAttentionVerification.swift:27-36).
+ *     2 pages of 16 (Sources/yanaiengine/PagedAttentionVerification.swift:27-36);
+ *   - for orc_forward_step, an independent float64 numpy restatement that
+ *     recomputes every sequence from its whole history without pages
+ *     (tests/test_oracle_forward_numpy.py).
  *
  * Citations are relative to the reference project root; S/ = Sources/yanaiengine/.
  * Compiled with -O2 -ffp-contract=off and no fast-math so every fp32 operation

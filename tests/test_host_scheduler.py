@@ -224,7 +224,7 @@ def test_deterministic(lib):
 
 
 def test_stub_catches_bad_tables(lib):
-    """The checker itself: a block read by two sequences, or one outside the pool,
+    """The stand-in's page-table check itself: a block read by two sequences, or one outside the pool,
     counts as a violation (a planted mistake, on the CPU stand-in)."""
     f = lib.yk_forward_step
     f.restype = C.c_int32
