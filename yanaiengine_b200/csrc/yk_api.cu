@@ -152,34 +152,42 @@ extern "C" yk_status yk_engine_device_error(yk_engine* e, uint32_t* code) {
 
 extern "C" uint64_t yk_engine_launch_count(yk_engine* e) { return e ? e->launches : 0; }
 
-void yk_engine::prof_begin(int cls, double bytes, double flops) {
+int yk_engine::prof_begin(int cls, double bytes, double flops) {
     ProfRecord r{cls, nullptr, nullptr, bytes, flops};
     for (cudaEvent_t* ev : {&r.start, &r.stop}) {
         if (!prof_free.empty()) {
             *ev = prof_free.back();
             prof_free.pop_back();
-        } else {
-            cudaEventCreate(ev);
+        } else if (cudaEventCreate(ev) != cudaSuccess) {
+            *ev = nullptr;
         }
     }
-    cudaEventRecord(r.start, stream);
+    if (!r.start || !r.stop || cudaEventRecord(r.start, stream) != cudaSuccess) {
+        if (r.start) prof_free.push_back(r.start);
+        if (r.stop) prof_free.push_back(r.stop);
+        return -1;
+    }
     prof_pending.push_back(r);
+    return (int)prof_pending.size() - 1;
 }
 
-void yk_engine::prof_end() {
-    if (!prof_pending.empty()) cudaEventRecord(prof_pending.back().stop, stream);
+void yk_engine::prof_end(int rec) {
+    if (rec < 0 || rec >= (int)prof_pending.size()) return;
+    // a stop that cannot be recorded leaves the record without a duration: it is left out
+    if (cudaEventRecord(prof_pending[(size_t)rec].stop, stream) != cudaSuccess) prof_pending[(size_t)rec].failed = true;
 }
 
 void yk_engine::prof_resolve() {
     cudaStreamSynchronize(stream);
     for (auto& r : prof_pending) {
         float ms = 0.f;
-        cudaEventElapsedTime(&ms, r.start, r.stop);
-        ProfTotals& t = prof[r.cls & 3];
-        t.ms += ms;
-        t.bytes += r.bytes;
-        t.flops += r.flops;
-        t.launches++;
+        if (!r.failed && cudaEventElapsedTime(&ms, r.start, r.stop) == cudaSuccess) {
+            ProfTotals& t = prof[r.cls & 3];
+            t.ms += ms;
+            t.bytes += r.bytes;
+            t.flops += r.flops;
+            t.launches++;
+        }
         prof_free.push_back(r.start);
         prof_free.push_back(r.stop);
     }

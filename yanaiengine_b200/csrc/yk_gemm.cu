@@ -1391,9 +1391,14 @@ extern "C" yk_status ykt_gemm_bf16_timed(yk_engine* e, const uint16_t* W, const 
         yk_set_error("ykt_gemm_bf16: cudaMalloc failed");
         return YK_ERR_OOM;
     }
-    cudaMemset(m.gemm_counters, 0, (size_t)m.gemm_counter_cap * 4);
-    cudaMemcpy(dW, W, (size_t)n_out * K * 2, cudaMemcpyHostToDevice);
-    cudaMemcpy(dX, X, (size_t)m_tok * K * 2, cudaMemcpyHostToDevice);
+    cudaError_t up = cudaMemset(m.gemm_counters, 0, (size_t)m.gemm_counter_cap * 4);
+    if (up == cudaSuccess) up = cudaMemcpy(dW, W, (size_t)n_out * K * 2, cudaMemcpyHostToDevice);
+    if (up == cudaSuccess) up = cudaMemcpy(dX, X, (size_t)m_tok * K * 2, cudaMemcpyHostToDevice);
+    if (up != cudaSuccess) {
+        cleanup();
+        yk_set_error(std::string("ykt_gemm_bf16: upload failed: ") + cudaGetErrorString(up));
+        return YK_ERR_CUDA;
+    }
     CUtensorMap tmW;
     yk_status s = yk::make_weight_map(e, &tmW, dW, n_out, K);
     yk::EpiParams ep;

@@ -45,6 +45,7 @@ struct ProfRecord {
     int cls;
     cudaEvent_t start, stop;
     double bytes, flops;
+    bool failed = false;  // its stop event could not be recorded: left out of the totals
 };
 struct ProfTotals {
     double ms = 0, bytes = 0, flops = 0;
@@ -100,19 +101,22 @@ struct yk_engine {
     yk_status up_submit(int slot, void* dst, size_t bytes);
     // the same copy on stream `on` (its done event recorded there)
     yk_status up_submit_on(int slot, void* dst, size_t bytes, cudaStream_t on);
-    void prof_begin(int cls, double bytes, double flops);
-    void prof_end();
+    // Opens a timed record; returns its index, or -1 when its events could not
+    // be created or recorded (that launch then goes untimed).
+    int prof_begin(int cls, double bytes, double flops);
+    void prof_end(int rec);
     void prof_resolve();
 };
 
 // RAII bracket for one profiled launch.
 struct ProfScope {
     yk_engine* e;
+    int rec = -1;
     ProfScope(yk_engine* e_, int cls, double bytes, double flops) : e(e_) {
-        if (e->profiling) e->prof_begin(cls, bytes, flops);
+        if (e->profiling) rec = e->prof_begin(cls, bytes, flops);
     }
     ~ProfScope() {
-        if (e->profiling) e->prof_end();
+        if (rec >= 0) e->prof_end(rec);
     }
 };
 
