@@ -1,8 +1,8 @@
 /*
  * yk.h -- C-ABI of the B200 speculative draft->verify module (libyk.so).
  *
- * This is the boundary the reference's Swift host would bind (module map +
- * thin Swift shim).  Everything above it -- Scheduler's
+ * This is the boundary the reference's Swift host would bind (through a
+ * module map and a thin Swift shim).  Everything above it -- Scheduler's
  * draft/verify loop, SequenceRequest, PagedKVCache page tables and the
  * BlockAllocator free list -- stays on the host; everything below it runs as
  * hand-written sm_100a kernels on one CUDA stream per engine.
@@ -300,16 +300,21 @@ yk_status yk_sampler_read_probs(yk_sampler* s, int32_t b, int32_t j, float* host
  * serving loop that carves every free byte of HBM into its own arenas at
  * start-up cannot let a call allocate -- cudaMalloc may fail once the arenas
  * own the memory, and it can synchronise the device mid-step).
- * Same result as yk_spec_verify: verifySequence over target logits
- * [B x (k+1) x V] and draft probabilities [B x k x V] (as yk_draft_sample
- * keeps them), draft tokens [B x k], Philox stream ids [B]; outputs tokens
- * [B x (k+1)] and counts [B].  Every pointer is DEVICE memory of `device`;
- * the work is queued on `stream` (a cudaStream_t) and is complete when that
- * stream is.  Its only scratch is a fixed 64 KB static device array (held by
- * every GPU that loads libyk.so until exit), so B*(k+1) is limited to 4096
- * rows; larger calls fail with YK_ERR_ARG.  The first call on a device looks
- * the array's device address up (cudaGetSymbolAddress) and caches it.  All
- * calls on a device share the array: calls that overlap on the GPU race. */
+ * Same kernels and the same result, bit for bit, as yk_spec_verify:
+ * verifySequence over target logits [B x (k+1) x V] and draft probabilities
+ * [B x k x V] (as yk_draft_sample keeps them), draft tokens [B x k], Philox
+ * stream ids [B]; outputs tokens [B x (k+1)] and counts [B].  Every pointer is
+ * DEVICE memory of `device`; the work is queued on `stream` (a cudaStream_t)
+ * and is complete when that stream is.  A draft token >= V is never used as an
+ * index: that sequence's count is -1 and its tokens are not written.
+ * Its only scratch is a fixed 256 KB static device array (held by every GPU
+ * that loads libyk.so until exit), so B*(k+1) is limited to 2048 rows; larger
+ * calls fail with YK_ERR_ARG before anything is launched.  The first call on a
+ * device looks the array's device address up (cudaGetSymbolAddress) and caches
+ * it per context, so that first call should come before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race.
+ * A CUDA error left pending by earlier work on the calling thread is returned
+ * as YK_ERR_CUDA (its message says so) and nothing is launched. */
 yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream, const float* target_logits,
                                         const float* draft_probs, const uint32_t* draft_tokens,
                                         const uint32_t* seq_ids, int32_t B, int32_t k, int32_t V,

@@ -76,6 +76,13 @@ yk_status ykt_trace_read(yk_engine* e, uint64_t* host, int32_t cap, uint64_t* la
 yk_status ykt_sampler_stamps_enable(yk_sampler* s, int32_t cap);
 yk_status ykt_sampler_stamps_read(yk_sampler* s, uint64_t* host, int32_t cap);
 
+/* The target probabilities q[B x (k+1) x V] exactly as the last verification
+ * of yk_spec_sample_logits formed them from its logits (same chunk statistics,
+ * same per-element expression), temperature > 0: lets a test hold the
+ * logits-mode verification to bit-exact decisions against the oracle run on
+ * these rows. */
+yk_status ykt_sampler_target_probs(yk_sampler* s, int32_t B, float temperature, float* host);
+
 #ifdef __cplusplus
 }
 #endif

@@ -266,15 +266,32 @@ struct Ctx {
 // y[t][o] = sum_k W[o][k] * x[t][k], sequential in k (S/gemm.metal:6-34 order).
 void linear(const Ctx& cx, const float* W, int out_dim, int in_dim, const float* x, int T, float* y,
             bool compat_relu, bool compat_bias_only) {
+    auto store = [&](int t, int o, float s) {
+        if (compat_relu) { s = s + 0.1f; s = s > 0.0f ? s : 0.0f; }   // S/LinearLayer.swift:61,99-121
+        else if (compat_bias_only) s = s + 0.1f;                        // LMHead: bias, no ReLU
+        y[(size_t)t * out_dim + o] = s;
+    };
     parallel_for(out_dim, cx.nthreads, [&](int o) {
         const float* wr = W + (size_t)o * in_dim;
-        for (int t = 0; t < T; ++t) {
+        int t = 0;
+        // eight tokens' dot products side by side: each is still one sequential
+        // chain in k (same result as one at a time), but the chains overlap in time
+        constexpr int U = 8;
+        for (; t + U <= T; t += U) {
+            float s[U];
+            const float* xr[U];
+            for (int u = 0; u < U; ++u) { s[u] = 0.0f; xr[u] = x + (size_t)(t + u) * in_dim; }
+            for (int k = 0; k < in_dim; ++k) {
+                const float wk = wr[k];
+                for (int u = 0; u < U; ++u) s[u] += xr[u][k] * wk;
+            }
+            for (int u = 0; u < U; ++u) store(t + u, o, s[u]);
+        }
+        for (; t < T; ++t) {
             const float* xr = x + (size_t)t * in_dim;
             float s = 0.0f;
             for (int k = 0; k < in_dim; ++k) s += xr[k] * wr[k];
-            if (compat_relu) { s = s + 0.1f; s = s > 0.0f ? s : 0.0f; }   // S/LinearLayer.swift:61,99-121
-            else if (compat_bias_only) s = s + 0.1f;                        // LMHead: bias, no ReLU
-            y[(size_t)t * out_dim + o] = s;
+            store(t, o, s);
         }
     });
 }

@@ -80,12 +80,3 @@ def test_engine_without_a_gpu_reports_an_error():
     with pytest.raises(abi.YKError) as ei:
         abi.Engine(0)
     assert ei.value.status in (1, 3)
-
-
-def test_integration_index_lists_every_entry_point():
-    text = (ROOT / "INTEGRATION.md").read_text()
-    index = text[text.index("## 5. Entry-point index"):]
-    listed = set(re.findall(r"`((?:yk|ykh)_\w+)`", index))
-    names = declared(ROOT / "include" / "yk.h") | declared(ROOT / "include" / "yk_host.h")
-    assert not names - listed, f"entry points missing from the index: {sorted(names - listed)}"
-    assert not listed - names, f"index names undeclared entry points: {sorted(listed - names)}"

@@ -5,7 +5,9 @@ free byte of HBM to its own arenas at start-up -- so no call may cudaMalloc
 behind their back.  This entry point works only on buffers the caller passes in
 plus a fixed static scratch array.  The test checks, through the C-ABI, that two
 calls in a row (different inputs, sharing that scratch) give exactly the tokens
-and counts of the allocating entry point (yk_spec_sample_logits), and that an
+and counts of the allocating entry point (yk_spec_sample_logits: the same
+statistics and verification kernels), that a draft token outside the vocabulary
+only marks its sequence (count -1) and is never used as an index, and that an
 oversized batch is refused.  Device buffers come from torch (plumbing only).
 This file is named so pytest collects it last.
 """
@@ -63,6 +65,17 @@ def test_noalloc_verify_matches_allocating_entry(engine):
         np.testing.assert_array_equal(got_cnt, cnt)
         for i in range(B):
             assert got_out[i, : cnt[i]].tolist() == out[i, : cnt[i]].tolist()
+    # A draft token >= V (sequence 2): that sequence is marked, the others unchanged.
+    b = bufs[0]
+    bad = b["d"].clone()
+    bad[2, 1] = V
+    cnt2 = torch.full((B,), -7, dtype=torch.int32, device=dev)
+    abi.check(fn(0, C.c_void_p(stream.cuda_stream), b["tl"].data_ptr(), b["p"].data_ptr(), bad.data_ptr(),
+                 b["ids"].data_ptr(), B, k, V, b["T"], b["seed"], b["step"], b["out"].data_ptr(), cnt2.data_ptr()))
+    stream.synchronize()
+    exp_cnt = expected[0][5].copy()
+    exp_cnt[2] = -1
+    np.testing.assert_array_equal(cnt2.cpu().numpy(), exp_cnt)
     # Larger than the fixed scratch: refused before anything is launched.
     big = bufs[0]
     st = fn(0, C.c_void_p(stream.cuda_stream), big["tl"].data_ptr(), big["p"].data_ptr(), big["d"].data_ptr(),

@@ -130,6 +130,7 @@ _PROTOS = {
     "ykt_trace_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_sampler_stamps_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_sampler_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32]),
+    "ykt_sampler_target_probs": (C.c_int32, [_P, C.c_int32, C.c_float, C.POINTER(C.c_float)]),
     "ykt_trace_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, C.POINTER(C.c_uint64)]),
     "ykt_attention_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, _I32P]),
 }
@@ -551,6 +552,12 @@ class Sampler:
     def read_probs(self, b: int, j: int) -> np.ndarray:
         out = np.empty(self.vocab, dtype=np.float32)
         check(lib().yk_sampler_read_probs(self.h, b, j, ptr(out, C.c_float)))
+        return out
+
+    def target_probs(self, B: int, T: float) -> np.ndarray:
+        """Test hook: q[B x (k+1) x V] exactly as the last sample_logits verification formed it."""
+        out = np.empty((B, self.k + 1, self.vocab), dtype=np.float32)
+        check(lib().ykt_sampler_target_probs(self.h, B, T, ptr(out, C.c_float)))
         return out
 
     def stamps(self, cap: int = 0):

@@ -7,12 +7,14 @@
 // (paged_fused_attention_kernel :572).  K is stored already rotated.
 //
 // bf16 path: one CTA per work item (sequence, KV head, 64-row query tile,
-// key split).  The rows are the (token, query-head) pairs of one GQA group, so
+// key range).  The rows are the (token, query-head) pairs of one GQA group, so
 // the k+1 verify tokens x group heads share every K/V page the CTA streams.
-// 16-token pages are staged with cp.async into padded shared memory (double
-// buffered), scores and P.V run on tensor cores (mma.sync m16n8k16 bf16,
-// fp32 accumulate) with an online softmax in the log2 domain; split-KV
-// partials are merged by a log-sum-exp combine kernel.
+// A producer warp streams 16-token K and V pages by TMA (a 3-D tensor map over
+// the pool, 128-byte swizzle) into an mbarrier ring of pages; consumer warps
+// compute scores and P.V on tensor cores (mma.sync m16n8k16 bf16, fp32
+// accumulate) with an online softmax in the log2 domain.  Items cut along the
+// keys publish (M, L, O) partials and the last CTA of the group to finish
+// merges them in split order.
 // fp32 path: a SIMT kernel (one warp per token x head).
 #include <algorithm>
 #include <climits>

@@ -36,11 +36,6 @@ __device__ __forceinline__ float q_from_logit(float l, float T, float m, float s
     return __fdiv_rn(expf(__fsub_rn(scale_t(l, T), m)), s);
 }
 
-struct RowStats {
-    float m, s;
-    int arg;
-};
-
 // Block-wide (max, sum-exp, first argmax) of x_i = l_i / T over one row.
 // Each accumulator visits its indices in increasing order and merges keep the
 // smallest index among equal maxima (first maximum wins); float4 loads when the
@@ -60,11 +55,6 @@ struct RowStats4 {
     float m, s, best;
     int arg;
 };
-__device__ RowStats4 block_stats4(const float* __restrict__ row, int64_t V, int idx0, float T);
-__device__ RowStats block_row_stats(const float* __restrict__ row, int64_t V, float T) {
-    const RowStats4 r = block_stats4(row, V, 0, T);
-    return RowStats{r.m, r.s, r.arg == 0x7fffffff ? 0 : r.arg};
-}
 // (max, sum-exp, best raw value, first argmax) over row[0, V) whose first element
 // has index idx0 in its full row.
 __device__ RowStats4 block_stats4(const float* __restrict__ row, int64_t V, int idx0, float T) {
@@ -167,25 +157,6 @@ __device__ __forceinline__ RowStats4 merge_chunks(const float4* __restrict__ par
     }
     if (r.arg == 0x7fffffff) r.arg = 0;
     return r;
-}
-
-// ---------------------------------------------------------------------------
-// Row statistics for many rows: stats[r] = (max, sum, argmax).
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(SMP_THREADS) row_stats_kernel(const float* __restrict__ logits, int64_t V, float T,
-                                                                 float* __restrict__ stats, Trace tr) {
-    if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
-    pdl_trigger();
-    pdl_wait();
-    if (threadIdx.x == 0) trace_mark(tr, TR_START);
-    const int r = blockIdx.x;
-    const RowStats st = block_row_stats(logits + (size_t)r * V, V, T);
-    if (threadIdx.x == 0) {
-        stats[r * 4 + 0] = st.m;
-        stats[r * 4 + 1] = st.s;
-        stats[r * 4 + 2] = __int_as_float(st.arg);
-    }
-    if (threadIdx.x == 0) trace_mark(tr, TR_END);
 }
 
 // ---------------------------------------------------------------------------
@@ -334,10 +305,14 @@ struct VerifyArgs {
     uint32_t* out;          // [B x (k+1)]
     int32_t* counts;        // [B]
     const float4* qpart = nullptr;  // logits mode: per-chunk target row statistics (else `stats`)
+    uint32_t* err = nullptr;        // device error word (YK_DEV_ERR_BOUNDS on a draft token >= V), if any
     unsigned long long* stamps = nullptr;  // test hook: 8 words per CTA
     Trace tr;
 };
 
+// A draft token >= V (device-resident drafts are not checked by the host) is
+// never used as an index: the sequence gets count -1, no token, and the error
+// word (if given) the bounds bit.
 __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
     __shared__ ChainSmem cs;
     if (threadIdx.x == 0) trace_mark(a.tr, TR_ENTRY);
@@ -373,10 +348,11 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
         if (!a.from_logits) return qrow(i)[x];
         return q_from_logit(qrow(i)[x], T, st(i)[0], st(i)[1]);
     };
-    __shared__ int s_rej;
+    __shared__ int s_rej, s_bad;
     if (threadIdx.x == 0) {
-        int rej = k;
-        for (int i = 0; i < k; ++i) {
+        int rej = k, bad = 0;
+        for (int i = 0; i < k; ++i) bad |= (int64_t)a.drafts[(size_t)b * k + i] >= V;
+        for (int i = 0; i < k && !bad; ++i) {
             const uint32_t d = a.drafts[(size_t)b * k + i];
             bool acc;
             if (greedy) {
@@ -391,8 +367,17 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
             if (!acc) { rej = i; break; }
         }
         s_rej = rej;
+        s_bad = bad;
     }
     __syncthreads();
+    if (s_bad) {
+        if (threadIdx.x == 0) {
+            a.counts[b] = -1;
+            raise_err(a.err, YK_DEV_ERR_BOUNDS);
+            trace_mark(a.tr, TR_END);
+        }
+        return;
+    }
     const int rej = s_rej;
     uint32_t tok;
     if (greedy) {
@@ -631,6 +616,7 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
     a.seq_ids = L.seq;
     a.out = L.out;
     a.counts = L.counts;
+    a.err = e->d_err;
     a.tr = trace_next(e, TK_VERIFY);
     a.stamps = (s->stamps && B <= s->stamps_cap) ? s->stamps + (size_t)s->stamps_cap * 8 : nullptr;
     YK_CHECK_CUDA(launch_pdl(e, verify_kernel, B, SMP_THREADS, 0, a));
@@ -726,38 +712,74 @@ extern "C" yk_status yk_sampler_read_probs(yk_sampler* s, int32_t b, int32_t j, 
 // logit and probability buffers) at start-up.  For such a host a per-call
 // cudaMalloc is not an option: it can fail once the arenas own the memory, and
 // it may synchronise the whole device in the middle of a step.  This entry point
-// runs the same two kernels as yk_spec_verify on buffers the caller already owns
-// and keeps its only scratch -- the per-row softmax statistics -- in the fixed
-// array below.
+// runs the same two kernels as yk_spec_verify (chunked target-row statistics,
+// then verification) on buffers the caller already owns and keeps its only
+// scratch -- the per-chunk softmax statistics -- in the fixed array below, so
+// its results equal yk_spec_verify's bit for bit.
 // ---------------------------------------------------------------------------
 // Largest B * (k+1) (target logit rows) one call may verify.
-constexpr int YK_NOALLOC_MAX_ROWS = 4096;
+constexpr int YK_NOALLOC_MAX_ROWS = 2048;
 
-// (max, sum, argmax, unused) per target row: 64 KB that every GPU loading
-// libyk.so holds until the process exits.  Every call on a device shares it and
-// each call rewrites every row it reads before reading it, so nothing has to
-// start at zero; calls that overlap on the GPU race on it.
-static __device__ __align__(256) float g_noalloc_row_stats[YK_NOALLOC_MAX_ROWS * 4];
+// Per-chunk (max, sum, best, argmax bits) of every target row: 256 KB that every
+// GPU loading libyk.so holds until the process exits.  Every call on a device
+// shares it; each call rewrites every entry it reads before reading it (the
+// statistics kernel runs first on the same stream), so nothing has to start at
+// zero.  Calls that overlap on the GPU race on it.
+static __device__ __align__(256) float4 g_noalloc_row_part[YK_NOALLOC_MAX_ROWS * SMP_CHUNKS];
 
-// Device address of g_noalloc_row_stats per device.  In host code the array's
-// name is only a host-side stand-in, so the address is looked up once per device
-// with that device current, on the first call there.
-static float* g_noalloc_stats_addr[64] = {};
+// Device address of g_noalloc_row_part per device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up with the device
+// current, on the first call there (and again if the device's context was
+// replaced since, e.g. after cudaDeviceReset: the cache is keyed by the
+// context's unique id).
+struct NoallocScratch {
+    unsigned long long ctx_id = 0;
+    float4* part = nullptr;
+};
+static NoallocScratch g_noalloc_scratch[64];
 static std::mutex g_noalloc_mu;
 
-static yk_status noalloc_stats_address(int device, float** out) {
+typedef CUresult (*PFN_ctxGetCurrent)(CUcontext*);
+typedef CUresult (*PFN_ctxGetId)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context, 0 if it cannot be read.
+static unsigned long long current_ctx_id() {
+    static PFN_ctxGetCurrent get_cur = nullptr;
+    static PFN_ctxGetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_cur = (PFN_ctxGetCurrent)f;
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = (PFN_ctxGetId)f;
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_cur || !get_id || get_cur(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+static yk_status noalloc_part_address(int device, float4** out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     YK_ARG(device >= 0 && device < 64, "device index");
-    if (!g_noalloc_stats_addr[device]) {
+    NoallocScratch& sc = g_noalloc_scratch[device];
+    const unsigned long long id = current_ctx_id();
+    if (!sc.part || id == 0 || id != sc.ctx_id) {
         void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_row_stats);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_row_part);
         if (e != cudaSuccess || !p) {
-            yk_set_error(std::string("cudaGetSymbolAddress(row statistics): ") + cudaGetErrorString(e));
+            yk_set_error(std::string("cudaGetSymbolAddress(row statistics scratch): ") + cudaGetErrorString(e));
             return YK_ERR_CUDA;
         }
-        g_noalloc_stats_addr[device] = static_cast<float*>(p);
+        sc.part = static_cast<float4*>(p);
+        sc.ctx_id = id;
     }
-    *out = g_noalloc_stats_addr[device];
+    *out = sc.part;
     return YK_OK;
 }
 
@@ -773,18 +795,35 @@ extern "C" yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream,
                      " target rows exceed the fixed limit of " + std::to_string(YK_NOALLOC_MAX_ROWS));
         return YK_ERR_ARG;
     }
+    // An error left pending by earlier work on this thread is reported as such,
+    // before anything is launched, so it is not mistaken for this call's.
+    const cudaError_t pending = cudaGetLastError();
+    if (pending != cudaSuccess) {
+        yk_set_error(std::string("yk_spec_verify_logits_noalloc: a CUDA error from earlier work was pending "
+                                 "before this call (nothing launched): ") + cudaGetErrorString(pending));
+        return YK_ERR_CUDA;
+    }
     int prev = 0;
     YK_CHECK_CUDA(cudaGetDevice(&prev));
     YK_CHECK_CUDA(cudaSetDevice(device));
-    float* stats = nullptr;
-    yk_status s = noalloc_stats_address(device, &stats);
+    float4* part = nullptr;
+    yk_status s = noalloc_part_address(device, &part);
     if (s == YK_OK) {
         cudaStream_t st = static_cast<cudaStream_t>(stream);
-        row_stats_kernel<<<B * (k + 1), SMP_THREADS, 0, st>>>(target_logits, V, temperature > 0.f ? temperature : 1.0f,
-                                                              stats, Trace{});
+        DraftArgs d;  // chunked statistics of the k + 1 target rows of each sequence, as run_verify
+        d.logits = target_logits;
+        d.logit_row_stride = k + 1;
+        d.logit_row_j_mul = 1;
+        d.V = V;
+        d.k = k + 1;
+        d.j_fixed = -1;
+        d.T = temperature;
+        d.part = part;
+        draft_partial_kernel<<<dim3(B * (k + 1), SMP_CHUNKS), SMP_THREADS, 0, st>>>(d);
         VerifyArgs a;
         a.q = target_logits;
-        a.stats = stats;
+        a.stats = nullptr;
+        a.qpart = part;
         a.p = draft_probs;
         a.drafts = draft_tokens;
         a.V = V;
@@ -832,5 +871,36 @@ extern "C" yk_status ykt_sampler_stamps_read(yk_sampler* s, uint64_t* host, int3
     YK_CHECK_CUDA(cudaSetDevice(s->e->device));
     YK_CHECK_CUDA(cudaStreamSynchronize(s->e->stream));
     YK_CHECK_CUDA(cudaMemcpy(host, s->stamps, (size_t)cap * 2 * 8 * 8, cudaMemcpyDeviceToHost));
+    return YK_OK;
+}
+
+// Target probabilities exactly as the last verification formed them: the
+// probability pass of draft sampling over the target logits uploaded by
+// yk_spec_sample_logits with the chunk statistics that verification merged (the
+// same merge and the same q_from_logit per element), into a scratch buffer.
+extern "C" yk_status ykt_sampler_target_probs(yk_sampler* s, int32_t B, float temperature, float* host) {
+    YK_ARG(s && host && s->q, "arguments");
+    YK_ARG(B > 0 && B <= s->max_seqs && temperature > 0.f, "B / temperature");
+    yk_engine* e = s->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t n = (size_t)B * (s->k + 1) * s->vocab;
+    float* tmp = nullptr;
+    YK_CHECK_CUDA(cudaMalloc(&tmp, n * 4));
+    DraftArgs d;
+    d.logits = s->q;
+    d.logit_row_stride = s->k + 1;
+    d.logit_row_j_mul = 1;
+    d.V = s->vocab;
+    d.k = s->k + 1;
+    d.j_fixed = -1;
+    d.T = temperature;
+    d.probs = tmp;
+    d.part = s->part;
+    draft_prob_kernel<<<dim3(B * (s->k + 1), SMP_CHUNKS), SMP_THREADS, 0, e->stream>>>(d);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) err = cudaMemcpyAsync(host, tmp, n * 4, cudaMemcpyDeviceToHost, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    cudaFree(tmp);
+    YK_CHECK_CUDA(err);
     return YK_OK;
 }
