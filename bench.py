@@ -46,6 +46,10 @@ WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (NCCL all-re
                 "8B-shape draft replicated, bf16, k=4, T=0.8, 128 seqs x 4096 ctx")
 METRIC = "accepted tokens/sec, 8B/1B-shape k=5 batch 32, at 1/2/4/8 B200; verify HBM GB/s"
 WORKLOAD = "spec-decode step: 8B-shape target + 1B-shape draft, bf16, k=5, T=0.8, 32 seqs/GPU, ctx U[512,2048]"
+METRIC_STRONG = "accepted tokens/sec, 8B/1B-shape k=5, global batch 32 split across the GPUs"
+METRIC_SAMPLER = "accepted tokens/sec, rejection sampling only: 64 seqs, k=4, V=128256, fp32 N(0,2^2) logits, T=1"
+WORKLOAD_SAMPLER = ("sampler phase: draft sampling of k=4 tokens per sequence from fp32 draft logits + "
+                    "verifySequence against fp32 target logits, 64 seqs/GPU, V=128256, T=1.0")
 METRIC_PREFILL = "prompt tokens/sec, first scheduler step (whole prompts), 8B/1B-shape k=5 batch 32"
 WORKLOAD_PREFILL = ("prefill step: the first Scheduler.step of 32 new sequences per GPU with U[512,2048]-token "
                     "prompts: both models over the whole prompts, then one draft / verify round; bf16, k=5, T=0.8")
@@ -145,17 +149,22 @@ def _oracle_layer_model(oracle, cfg: dict, n_layers: int, vocab: int, rng):
 
 
 _SAMPLE_MODELS: dict = {}
+SAMPLE_FRACTION = 16  # one CPU sample = 1/16 of a step's work in every part
 
 
 def cpu_step_sample(ctx_lens, k: int, T: float, nthreads: int, seed: int = 0) -> dict:
-    """Times the oracle on: one target layer (verify shape), a 1/16 slice of the
-    target LM head, one draft layer (draft shape), a 1/16 slice of the draft LM
-    head, and the full sampler phase; returns the extrapolated step time."""
+    """Times the oracle on 1/16 of one speculative step, every part cut by the
+    same factor: 2 of the 32 target layers at the verify shape, 1/16 of the
+    target LM head's vocabulary rows, for each of the k draft iterations 1 of the
+    16 draft layers and 1/16 of the draft LM head, and the sampler phase of 2 of
+    the 32 sequences.  Returns the timed seconds and the sampled sequences'
+    emitted tokens."""
     sys.path.insert(0, str(ROOT / "tests"))
     import oracle_ffi as oracle
 
     rng = np.random.default_rng(seed)
     B = len(ctx_lens)
+    F = SAMPLE_FRACTION
     out = {}
 
     def time_forward(cfg, n_layers, vocab, n_new, last_n):
@@ -181,35 +190,52 @@ def cpu_step_sample(ctx_lens, k: int, T: float, nthreads: int, seed: int = 0) ->
         return time.perf_counter() - t0
 
     V = TARGET["vocab_size"]
-    out["target_layer_s"] = time_forward(TARGET, 1, 2, k + 1, k + 1)
-    out["target_lm_slice_s"] = time_forward(TARGET, 0, V // 16, k + 1, k + 1)
-    out["draft_layer_s"] = time_forward(DRAFT, 1, 2, 1, 1)
-    out["draft_lm_slice_s"] = time_forward(DRAFT, 0, V // 16, 1, 1)
-    # sampler phase on logits with the spread of random-init models (std 0.02 * sqrt(d) ~ 1.3)
-    dl = rng.standard_normal((B, k, V), dtype=np.float32) * np.float32(1.3)
-    tl = rng.standard_normal((B, k + 1, V), dtype=np.float32) * np.float32(1.3)
+    n_t = TARGET["n_layers"] // F
+    out["target_layers_s"] = time_forward(TARGET, n_t, 2, k + 1, k + 1)
+    out["target_lm_slice_s"] = time_forward(TARGET, 0, V // F, k + 1, k + 1)
+    out["draft_s"] = 0.0
+    for _ in range(k):
+        out["draft_s"] += time_forward(DRAFT, DRAFT["n_layers"] // F, 2, 1, 1)
+        out["draft_s"] += time_forward(DRAFT, 0, V // F, 1, 1)
+    # sampler phase of B / F sequences on logits with the spread of random-init
+    # models (std 0.02 * sqrt(d) ~ 1.3)
+    bs = max(1, B // F)
+    dl = rng.standard_normal((bs, k, V), dtype=np.float32) * np.float32(1.3)
+    tl = rng.standard_normal((bs, k + 1, V), dtype=np.float32) * np.float32(1.3)
     t0 = time.perf_counter()
-    _, _, cnt = oracle.spec_sample_batch(dl, tl, T, 1, 0, np.arange(B, dtype=np.uint32), nthreads)
+    _, _, cnt = oracle.spec_sample_batch(dl, tl, T, 1, seed, np.arange(bs, dtype=np.uint32), nthreads)
     out["sampler_s"] = time.perf_counter() - t0
-    out["emitted_per_step"] = float(cnt.sum())
-    step = (TARGET["n_layers"] * out["target_layer_s"] + 16 * out["target_lm_slice_s"] +
-            k * (DRAFT["n_layers"] * out["draft_layer_s"] + 16 * out["draft_lm_slice_s"]) + out["sampler_s"])
-    out["step_s"] = step
+    out["sampled_seqs"] = bs
+    out["sampled_emitted"] = float(cnt.sum())
+    out["sample_s"] = out["target_layers_s"] + out["target_lm_slice_s"] + out["draft_s"] + out["sampler_s"]
     return out
 
 
-def cpu_baseline_dict(sample: dict, nthreads: int, emitted_per_step: float) -> dict:
+def cpu_sample_value(samples: list, B: int) -> tuple[float, float]:
+    """(tokens/s of the timed samples, emitted tokens per full step): the step's
+    emitted tokens are estimated from every sampled sequence; a sample carries
+    1/16 of them, so its throughput is (emitted per step / 16) / sample time."""
+    per_seq = sum(x["sampled_emitted"] for x in samples) / max(1, sum(x["sampled_seqs"] for x in samples))
+    emitted = per_seq * B
+    sample_s = float(np.mean([x["sample_s"] for x in samples]))
+    return emitted / SAMPLE_FRACTION / sample_s, emitted
+
+
+def cpu_baseline_dict(samples: list, nthreads: int, B: int) -> dict:
+    val, emitted = cpu_sample_value(samples, B)
+    ms = 1e3 * float(np.mean([x["sample_s"] for x in samples]))
     return {
-        "value": emitted_per_step / sample["step_s"],
+        "value": val,
         "unit": "tokens/s",
         "cores": nthreads,
         "kind": "port",
         "sample": ("oracle (C++ restatement of S/SpeculativeSampler.swift, the draft sampling of "
-                   "S/Scheduler.swift and the fp32 verify forward) timed on 1 target layer at the verify shape, "
-                   "1 draft layer, 1/16 of each LM head and the full sampler phase for the same 32 sequences; "
-                   "extrapolated to 32+5x16 layers (weights and KV pages filled from a repeated N(0,0.02) / "
-                   "N(0,1) block; only the oracle calls are timed); "
-                   f"measured step {sample['step_s']:.1f} s"),
+                   "S/Scheduler.swift and the fp32 verify forward, all host threads) timed on 1/16 of a step in "
+                   "every part: 2 of 32 target layers at the verify shape, 1/16 of the target LM head, per draft "
+                   "iteration 1 of 16 draft layers and 1/16 of the draft LM head, the sampler phase of 2 of the "
+                   f"32 sequences; {ms:.0f} ms per sample, throughput = (emitted tokens per step / 16) / sample "
+                   f"time, {emitted:.1f} emitted tokens per step estimated from the sampled sequences"),
+        "extrapolated_full_step_ms": ms * SAMPLE_FRACTION,
     }
 
 
@@ -259,6 +285,10 @@ def measured_peaks() -> dict:
 
 
 def run_yk(args, world, rank, local):
+    """The speculative step: the weak-scaling headline (B sequences per GPU) and,
+    on more than one GPU, the same job at a fixed global batch of `strong_batch`
+    sequences split across the ranks (strong scaling); one engine and one pair of
+    models per rank serve both."""
     from yanaiengine_b200 import abi, dp
 
     k, B, T = args.k, args.batch, args.temperature
@@ -277,137 +307,179 @@ def run_yk(args, world, rank, local):
         eng.tp_init(bytes(uid.cpu().numpy()), rank, world)
         tcfg = abi.make_config(**TARGET_70B, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
         dcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
-        lens = np.full(B, 4096, dtype=np.int64)
-        mine = np.arange(B)
-        rng = np.random.default_rng(7)
     else:
         tcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
         dcfg = abi.make_config(**DRAFT, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
-        # the job's B x world sequences, split across ranks longest-first (B per rank)
-        glens = dp.global_lengths(B, world, seed=7)
-        mine = dp.partition(glens, world)[rank]
-        lens = glens[mine]
-        rng = np.random.default_rng(7 + 1000 * rank)
-    grow = (args.warmup + 2 * args.steps + 4) * (k + 1) + 32
-    blocks = int(sum(np.ceil((lens + grow) / 16))) + 64
     target = abi.Model(eng, tcfg, seed=1, init_std=0.02, tp=(rank, world) if tp else None)
     draft = abi.Model(eng, dcfg, seed=2, init_std=0.02)
-    tpool = abi.KVPool(eng, target.cfg, blocks)
-    dpool = abi.KVPool(eng, dcfg, blocks)
-    tpool.fill_random(11 + (rank if tp else 0), 1.0)
-    dpool.fill_random(12, 1.0)
-    sampler = abi.Sampler(eng, B, k, TARGET["vocab_size"])
-    sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + (0 if tp else rank))
-    for i, L in enumerate(lens):
-        sch.submit(rng.integers(0, TARGET["vocab_size"], int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
-                   seq_id=int(mine[i]), cached=True)
-    for _ in range(args.warmup):
-        sch.step()
-    eng.sync()
+    try:
+        if tp:
+            lens, mine = np.full(B, 4096, dtype=np.int64), np.arange(B)
+            res = spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B,
+                             np.random.default_rng(7), profile=True)
+        else:
+            # the job's B x world sequences, split across ranks longest-first (B per rank)
+            glens = dp.global_lengths(B, world, seed=7)
+            mine = dp.partition(glens, world)[rank]
+            lens = glens[mine]
+            res = spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B,
+                             np.random.default_rng(7 + 1000 * rank), profile=True)
+            if res is not None:
+                res["config"]["global_batch"] = B * world
+            if world > 1 and args.strong_batch > 0:
+                # strong scaling: the fixed global batch, strong_batch / world sequences per rank
+                G = args.strong_batch
+                sg = dp.global_lengths(-(-G // world), world, seed=7)[:G]
+                smine = dp.partition(sg, world)[rank]
+                st = spec_phase(args, world, rank, local, eng, target, draft, sg[smine], smine, len(smine),
+                                np.random.default_rng(9 + 1000 * rank), profile=False)
+                if rank == 0:
+                    res["strong"] = {k2: st[k2] for k2 in ("value", "ms_per_step", "e2e", "gpu_launches",
+                                                          "emitted_per_step", "verify_step", "accept_rate")}
+                    res["strong"].update({"scaling": "strong", "global_batch": G,
+                                          "seqs_per_gpu": f"{G // world}-{-(-G // world)}",
+                                          "unit": "tokens/s", "metric": METRIC_STRONG})
+    finally:
+        draft.close()
+        target.close()
+        eng.close()
+    return res, lens
+
+
+def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng, profile: bool):
+    """Warm-up and K timed steps of one batch (its own KV pools, sampler and
+    scheduler, freed at the end); with `profile`, also the per-launch roofline
+    pass.  Returns the bench line (rank 0) or None."""
+    from yanaiengine_b200 import abi
 
     import torch
 
-    torch.cuda.set_device(local)
-    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
-    if rank == 0:
-        clocks.start()
-        time.sleep(0.5)
-    _, em0, acc0 = sch.counters()
-    launches0 = eng.launches()
-    h2d = d2h = 0
-    barrier(world)
-    eng.sync()
-    t0 = time.perf_counter()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        n_running = sch.running()
-        # per-step host traffic through the C-ABI: token ids, positions, page tables in; tokens out
-        sch.step()
-        h2d += n_running * (2 * (k + 1) + 8) * 4 * (k + 1)
-        d2h += n_running * (k + 2) * 4 * (k + 1)
-    ev1.record(stream)
-    eng.sync()
-    wall = time.perf_counter() - t0
-    barrier(world)
-    dev_ms = ev0.elapsed_time(ev1)
-    clk = clocks.stop() if rank == 0 else None
-    _, em1, acc1 = sch.counters()
-    emitted = em1 - em0
-    launches = eng.launches() - launches0
-    max_dev_s = allreduce_max(world, dev_ms / 1e3)
-    max_wall = allreduce_max(world, wall)
-    # data parallel: every rank emits its own sequences' tokens; tensor parallel:
-    # all ranks emit the same tokens, counted once
-    tot_emitted = float(emitted) if tp else allreduce_sum(world, float(emitted))
+    k, T = args.k, args.temperature
+    tp = args.workload == "70b-tp"
+    grow = (args.warmup + 2 * args.steps + 4) * (k + 1) + 32
+    blocks = int(sum(np.ceil((lens + grow) / 16))) + 64
+    tpool = abi.KVPool(eng, target.cfg, blocks)
+    dpool = abi.KVPool(eng, draft.cfg, blocks)
+    sampler = abi.Sampler(eng, B, k, TARGET["vocab_size"])
+    sch = None
+    try:
+        tpool.fill_random(11 + (rank if tp else 0), 1.0)
+        dpool.fill_random(12, 1.0)
+        sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + (0 if tp else rank))
+        for i, L in enumerate(lens):
+            sch.submit(rng.integers(0, TARGET["vocab_size"], int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
+                       seq_id=int(mine[i]), cached=True)
+        for _ in range(args.warmup):
+            sch.step()
+        eng.sync()
 
-    # kernel roofline: a second pass of the same steps with per-launch CUDA events
-    eng.profile(True)
-    for _ in range(max(1, min(args.steps, 4))):
-        sch.step()
-    gemm = eng.profile_read(0)
-    attn = eng.profile_read(1)
-    eng.profile(False)
-    # in-situ breakdown of one more step from the launch trace (first CTA past the
-    # grid dependency wait, last CTA exit per launch), programmatic launch on
-    ctx_before = [int(L) + len(sch.generated(int(sid))) for L, sid in zip(lens, mine)]
-    breakdown = trace_breakdown(eng, sch)
+        torch.cuda.set_device(local)
+        stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
+        if rank == 0:
+            clocks.start()
+            time.sleep(0.5)
+        _, em0, acc0 = sch.counters()
+        launches0 = eng.launches()
+        h2d = d2h = 0
+        barrier(world)
+        eng.sync()
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            n_running = sch.running()
+            # per-step host traffic through the C-ABI: token ids, positions, page tables in; tokens out
+            sch.step()
+            h2d += n_running * (2 * (k + 1) + 8) * 4 * (k + 1)
+            d2h += n_running * (k + 2) * 4 * (k + 1)
+        ev1.record(stream)
+        eng.sync()
+        wall = time.perf_counter() - t0
+        barrier(world)
+        dev_ms = ev0.elapsed_time(ev1)
+        clk = clocks.stop() if rank == 0 else None
+        _, em1, acc1 = sch.counters()
+        emitted = em1 - em0
+        launches = eng.launches() - launches0
+        max_dev_s = allreduce_max(world, dev_ms / 1e3)
+        max_wall = allreduce_max(world, wall)
+        # data parallel: every rank emits its own sequences' tokens; tensor parallel:
+        # all ranks emit the same tokens, counted once
+        tot_emitted = float(emitted) if tp else allreduce_sum(world, float(emitted))
+        tot_accepted = float(acc1 - acc0) if tp else allreduce_sum(world, float(acc1 - acc0))
+        tot_seqs = float(B) if tp else allreduce_sum(world, float(B))
+
+        gemm = attn = None
+        if profile:
+            # kernel roofline: a second pass of the same steps with per-launch CUDA events
+            eng.profile(True)
+            for _ in range(max(1, min(args.steps, 4))):
+                sch.step()
+            gemm = eng.profile_read(0)
+            attn = eng.profile_read(1)
+            eng.profile(False)
+        # in-situ breakdown of one more step from the launch trace (first CTA past the
+        # grid dependency wait, last CTA exit per launch), programmatic launch on
+        ctx_before = [int(L) + len(sch.generated(int(sid))) for L, sid in zip(lens, mine)]
+        breakdown = trace_breakdown(eng, sch)
+    finally:
+        if sch is not None:
+            sch.close()
+        sampler.close()
+        dpool.close()
+        tpool.close()
 
     peaks = measured_peaks()
-    res = None
-    if rank == 0:
+    if rank != 0:
+        return None
+    step_ms = max_dev_s * 1e3 / args.steps
+    res = {
+        "metric": METRIC_70B if tp else METRIC,
+        "value": tot_emitted / max_dev_s,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "strong" if tp else "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: random-init weights N(0,0.02), random token ids, synthetic N(0,1) KV context",
+        "config": ({"workload": WORKLOAD_70B, "global_batch": B, "k": k, "temperature": T, "ctx": "4096 + growth",
+                    "parallelism": f"tp{world} target, draft replicated",
+                    "l2": "inputs larger than L2 (17.5 GB target shard + 16 GB draft per GPU per step)"}
+                   if tp else
+                   {"workload": WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B, "k": k,
+                    "temperature": T, "ctx": "U[512,2048] + growth", "parallelism": f"dp{world} (replicas)",
+                    "l2": "inputs larger than L2 (17.5 GB of weights streamed per step)"}),
+        "e2e": {"value": tot_emitted / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d / args.steps),
+                "d2h_bytes_per_step": int(d2h / args.steps)},
+        "gpu_launches": int(launches),
+        "accept_rate": float(tot_accepted / max(1.0, args.steps * tot_seqs * k)),
+        "emitted_per_step": float(tot_emitted / args.steps),
+        "verify_step": verify_roofline(TARGET_70B if tp else TARGET, ctx_before, k, world if tp else 1,
+                                       breakdown.get("verify_forward_us"), peaks),
+        "step_breakdown": breakdown,
+        "clocks": clk,
+    }
+    if gemm is not None:
         gemm_gbs = gemm["bytes"] / (gemm["ms"] / 1e3) / 1e9 if gemm["ms"] > 0 else 0.0
         attn_gbs = attn["bytes"] / (attn["ms"] / 1e3) / 1e9 if attn["ms"] > 0 else 0.0
-        step_ms = max_dev_s * 1e3 / args.steps
-        res = {
-            "metric": METRIC_70B if tp else METRIC,
-            "value": tot_emitted / max_dev_s,
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": step_ms,
-            "higher_is_better": True,
-            "scaling": "strong" if tp else "weak",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic: random-init weights N(0,0.02), random token ids, synthetic N(0,1) KV context",
-            "config": ({"workload": WORKLOAD_70B, "global_batch": B, "k": k, "temperature": T, "ctx": "4096 + growth",
-                        "parallelism": f"tp{world} target, draft replicated",
-                        "l2": "inputs larger than L2 (17.5 GB target shard + 16 GB draft per GPU per step)"}
-                       if tp else
-                       {"workload": WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B, "k": k,
-                        "temperature": T, "ctx": "U[512,2048] + growth", "parallelism": f"dp{world} (replicas)",
-                        "l2": "inputs larger than L2 (17.5 GB of weights streamed per step)"}),
-            "e2e": {"value": tot_emitted / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d / args.steps),
-                    "d2h_bytes_per_step": int(d2h / args.steps)},
-            "gpu_launches": int(launches),
-            "accept_rate": float((acc1 - acc0) / max(1, args.steps * B * k)),
-            "emitted_per_step": float(emitted / args.steps),
-            "roofline": {"bound": "hbm", "achieved": gemm_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gemm_gbs / peaks["hbm_gbs"],
-                         # ncu, 28672x4096x192 gate/up launch: DRAM read+write / algorithmic bytes = 1.018
-                         "traffic": GEMM_TRAFFIC_RATIO * gemm["bytes"] / max(1, gemm["launches"]),
-                         "traffic_src": "ncu dram bytes of the 28672x4096x192 gate/up launch / its algorithmic "
-                                        "bytes (1.018), applied to the average launch's algorithmic bytes",
-                         "kernel": "gemm_tc_kernel",
-                         "peak_src": peaks["src"],
-                         "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])},
-            "attention": {"achieved_gbs": attn_gbs, "frac": attn_gbs / peaks["hbm_gbs"], "launches": attn["launches"]},
-            "verify_step": verify_roofline(TARGET_70B if tp else TARGET, ctx_before, k, world if tp else 1,
-                                           breakdown.get("verify_forward_us"), peaks),
-            "step_breakdown": breakdown,
-            "clocks": clk,
-        }
-    sch.close()
-    sampler.close()
-    dpool.close()
-    tpool.close()
-    draft.close()
-    target.close()
-    eng.close()
-    return res, lens
+        res["roofline"] = {"bound": "hbm", "achieved": gemm_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                           "frac": gemm_gbs / peaks["hbm_gbs"],
+                           # ncu, 28672x4096x192 gate/up launch: DRAM read+write / algorithmic bytes = 1.018
+                           "traffic": GEMM_TRAFFIC_RATIO * gemm["bytes"] / max(1, gemm["launches"]),
+                           "traffic_src": "ncu dram bytes of the 28672x4096x192 gate/up launch / its algorithmic "
+                                          "bytes (1.018), applied to the average launch's algorithmic bytes",
+                           "kernel": "gemm_tc_kernel",
+                           "peak_src": peaks["src"],
+                           "launches": gemm["launches"],
+                           "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])}
+        res["attention"] = {"achieved_gbs": attn_gbs, "frac": attn_gbs / peaks["hbm_gbs"],
+                            "launches": attn["launches"]}
+    return res
 
 
 def verify_roofline(cfg: dict, ctx_before, k: int, tp_world: int, us, peaks) -> dict | None:
@@ -425,6 +497,160 @@ def verify_roofline(cfg: dict, ctx_before, k: int, tp_world: int, us, peaks) -> 
     ach = (weights + kv) / (us * 1e-6) / 1e9
     return {"us": us, "bytes": weights + kv, "weight_bytes": weights, "kv_bytes": kv, "achieved_gbs": ach,
             "peak_gbs": peaks["hbm_gbs"], "frac": ach / peaks["hbm_gbs"], "peak_src": peaks["src"]}
+
+
+def run_sampler(args, world, rank, local):
+    """--workload sampler: the rejection-sampling phase alone (draft sampling of
+    k tokens per sequence from fp32 draft logits, then verifySequence against fp32
+    target logits), 64 sequences per GPU, k = 4, V = 128256, logits i.i.d.
+    N(0, 2^2), T = 1.  `value`: the logits stay resident on the device
+    (yk_spec_sample_logits with NULL logits samples them again each step with a
+    new step index, so new uniforms); `e2e`: every step uploads both logit
+    tensors from pinned host memory through the same call."""
+    from yanaiengine_b200 import abi
+
+    import torch
+
+    k, B, T = args.k, args.batch, args.temperature
+    V = TARGET["vocab_size"]
+    eng = abi.Engine(local)
+    s = abi.Sampler(eng, B, k, V)
+    try:
+        rng = np.random.default_rng(1234 + rank)
+        dl = torch.empty((B, k, V), dtype=torch.float32, pin_memory=True).numpy()
+        tl = torch.empty((B, k + 1, V), dtype=torch.float32, pin_memory=True).numpy()
+        dl[:] = rng.standard_normal((B, k, V), dtype=np.float32) * np.float32(2.0)
+        tl[:] = rng.standard_normal((B, k + 1, V), dtype=np.float32) * np.float32(2.0)
+        ids = np.arange(B, dtype=np.uint32) + np.uint32(B * rank)
+        step_bytes = float(dl.nbytes + tl.nbytes)
+        for w in range(args.warmup):
+            s.sample_logits(dl, tl, T, 1234, 100000 + w, ids)
+        torch.cuda.set_device(local)
+        stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+        clocks = ClockSampler(list(range(world)) if rank == 0 else [local])
+        if rank == 0:
+            clocks.start()
+            time.sleep(0.5)
+        launches0 = eng.launches()
+        # device-resident inputs
+        barrier(world)
+        eng.sync()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        emitted = 0
+        ev0.record(stream)
+        for i in range(args.steps):
+            _, _, cnt = s.sample_logits(None, None, T, 1234, i, ids)
+            emitted += int(cnt.sum())
+        ev1.record(stream)
+        eng.sync()
+        dev_s = ev0.elapsed_time(ev1) / 1e3
+        launches = eng.launches() - launches0
+        # end to end: host logits uploaded inside every step
+        barrier(world)
+        t0 = time.perf_counter()
+        em_e2e = 0
+        for i in range(args.steps):
+            _, _, cnt = s.sample_logits(dl, tl, T, 1234, args.steps + i, ids)
+            em_e2e += int(cnt.sum())
+        wall = time.perf_counter() - t0
+        barrier(world)
+        clk = clocks.stop() if rank == 0 else None
+        # per-kernel shares of one more device-resident step (launch trace)
+        n0 = eng.launches()
+        eng.trace(64)
+        s.sample_logits(None, None, T, 1234, 2 * args.steps, ids)
+        rec, n1 = eng.trace_read()
+        eng.trace(0)
+        kinds = {}
+        for i in range(n0, n1):
+            r = rec[i % 64].astype(np.int64)
+            name = TRACE_KINDS.get(int(r[3]) & 15, "other")
+            kinds[name] = kinds.get(name, 0.0) + (r[2] - r[1]) / 1e3
+        max_dev = allreduce_max(world, dev_s)
+        max_wall = allreduce_max(world, wall)
+        tot = allreduce_sum(world, float(emitted))
+        tot_e2e = allreduce_sum(world, float(em_e2e))
+    finally:
+        s.close()
+        eng.close()
+    if rank != 0:
+        return None, None
+    peaks = measured_peaks()
+    ms = max_dev * 1e3 / args.steps
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    res = {
+        "metric": METRIC_SAMPLER, "value": tot / max_dev, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: fp32 logits i.i.d. N(0, 2^2) (numpy seed 1234 + rank), Philox uniforms",
+        "config": {"workload": WORKLOAD_SAMPLER, "global_batch": B * world, "seqs_per_gpu": B, "k": k, "vocab": V,
+                   "temperature": T, "l2": "inputs larger than L2 (295 MB of logits per step)"},
+        "e2e": {"value": tot_e2e / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": int(step_bytes + 4 * B),
+                "d2h_bytes_per_step": int(4 * (B * k + B * (k + 1) + B))},
+        "gpu_launches": int(launches),
+        "emitted_per_step": tot / args.steps,
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                     "kernel": "sampler phase: draft_partial_kernel, draft_prob_kernel, draft_sample_kernel, "
+                               "verify_kernel (algorithmic bytes = both logit tensors read once per step)",
+                     "peak_src": peaks["src"], "step_bytes": step_bytes},
+        "kernel_us": {k2: round(v, 1) for k2, v in kinds.items()},
+        "clocks": clk,
+    }
+    return res, None
+
+
+def sampler_cpu_baselines(args) -> dict:
+    """The oracle sampler (draft sampling + verifySequence, the reference's
+    SpeculativeSampler restated) on one step of the same workload: one thread
+    (the reference loops over sequences serially) and every host thread."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_ffi as oracle
+
+    k, B, T, V = args.k, args.batch, args.temperature, TARGET["vocab_size"]
+    rng = np.random.default_rng(1234)
+    dl = rng.standard_normal((B, k, V), dtype=np.float32) * np.float32(2.0)
+    tl = rng.standard_normal((B, k + 1, V), dtype=np.float32) * np.float32(2.0)
+    ids = np.arange(B, dtype=np.uint32)
+    out = {}
+    for nt in (1, os.cpu_count() or 1):
+        t0 = time.perf_counter()
+        _, _, cnt = oracle.spec_sample_batch(dl, tl, T, 1234, 0, ids, nt)
+        dt = time.perf_counter() - t0
+        out[nt] = {"value": float(cnt.sum()) / dt, "unit": "tokens/s", "cores": nt, "kind": "port",
+                   "sample": f"oracle sampler phase on one step of {B} sequences (k={k}, V={V}): {dt * 1e3:.0f} ms"}
+    return out
+
+
+def reference_sampler(args, world, nthreads):
+    """--impl reference --workload sampler: the oracle sampler (the reference's
+    SpeculativeSampler restated) on the same workload, all host threads, one
+    whole step per timed step."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_ffi as oracle
+
+    k, B, T, V = args.k, args.batch, args.temperature, TARGET["vocab_size"]
+    rng = np.random.default_rng(1234)
+    dl = rng.standard_normal((B, k, V), dtype=np.float32) * np.float32(2.0)
+    tl = rng.standard_normal((B, k + 1, V), dtype=np.float32) * np.float32(2.0)
+    ids = np.arange(B, dtype=np.uint32)
+    for w in range(args.warmup):
+        oracle.spec_sample_batch(dl, tl, T, 1234, 100000 + w, ids, nthreads)
+    em, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        _, _, cnt = oracle.spec_sample_batch(dl, tl, T, 1234, i, ids, nthreads)
+        em += int(cnt.sum())
+    dt = time.perf_counter() - t0
+    val = em / dt
+    print(json.dumps({
+        "metric": METRIC_SAMPLER, "value": val, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD_SAMPLER, "global_batch": B, "k": k, "vocab": V, "temperature": T},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                         "sample": f"oracle sampler phase, {args.steps} whole steps of {B} sequences"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
 
 
 def run_prefill(args, world, rank, local):
@@ -605,10 +831,22 @@ def main():
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--temperature", type=float, default=0.8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="8b-dp", choices=["8b-dp", "70b-tp", "prefill"],
+    ap.add_argument("--strong-batch", type=int, default=32,
+                    help="8b-dp on more than one GPU: also time this global batch split across the GPUs "
+                         "(strong scaling, reported as `strong`); 0 skips it")
+    ap.add_argument("--workload", default="8b-dp", choices=["8b-dp", "70b-tp", "prefill", "sampler"],
                     help="8b-dp: the headline 8B/1B data-parallel step; 70b-tp: 70B-shape target over all GPUs; "
-                         "prefill: the first scheduler step of a fresh batch (whole prompts)")
+                         "prefill: the first scheduler step of a fresh batch (whole prompts); sampler: the "
+                         "rejection-sampling phase alone (64 seqs, k=4, V=128256, fp32 N(0,4) logits)")
     args = ap.parse_args()
+    if args.workload == "sampler":
+        # the sampler-only configuration: 64 sequences, k = 4, T = 1 (other flags as given)
+        if "--batch" not in sys.argv:
+            args.batch = 64
+        if "--k" not in sys.argv:
+            args.k = 4
+        if "--temperature" not in sys.argv:
+            args.temperature = 1.0
     if args.workload == "70b-tp":
         # the 70B configuration: batch 128, k = 4 (other flags as given)
         if "--batch" not in sys.argv:
@@ -622,32 +860,41 @@ def main():
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
+        if args.workload == "sampler":
+            reference_sampler(args, world, nthreads)
+            return
         lens = np.random.default_rng(7).integers(512, 2049, args.batch)
         for w in range(args.warmup):  # untimed: builds the sample models, primes caches and threads
             cpu_step_sample(lens, args.k, args.temperature, nthreads, seed=1000 + w)
         samples = [cpu_step_sample(lens, args.k, args.temperature, nthreads, seed=s) for s in range(args.steps)]
-        step_s = float(np.mean([s["step_s"] for s in samples]))
-        emitted = float(np.mean([s["emitted_per_step"] for s in samples]))
-        val = emitted / step_s
-        cb = cpu_baseline_dict(samples[0], nthreads, emitted)
-        cb["value"] = val
+        cb = cpu_baseline_dict(samples, nthreads, args.batch)
+        val = cb["value"]
+        ms = 1e3 * float(np.mean([x["sample_s"] for x in samples]))
         print(json.dumps({
             "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": WORKLOAD, "global_batch": args.batch, "k": args.k,
-                       "temperature": args.temperature},
+                       "temperature": args.temperature,
+                       "step": "each timed step is one 1/16-of-a-step sample (see cpu_baseline.sample)"},
+            "extrapolated": True,
+            "extrapolated_full_step_ms": ms * SAMPLE_FRACTION,
             "cpu_baseline": cb,
             "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }))
         return
 
     world, rank, local = dist_setup(args.gpus)
-    res, lens = (run_prefill if args.workload == "prefill" else run_yk)(args, world, rank, local)
+    run = {"prefill": run_prefill, "sampler": run_sampler}.get(args.workload, run_yk)
+    res, lens = run(args, world, rank, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline and args.workload == "8b-dp":
-            sample = cpu_step_sample(lens, args.k, args.temperature, nthreads)
-            res["cpu_baseline"] = cpu_baseline_dict(sample, nthreads, sample["emitted_per_step"])
+            samples = [cpu_step_sample(lens, args.k, args.temperature, nthreads, seed=s) for s in range(2)]
+            res["cpu_baseline"] = cpu_baseline_dict(samples, nthreads, args.batch)
+        if world == 1 and not args.no_cpu_baseline and args.workload == "sampler":
+            cb = sampler_cpu_baselines(args)
+            res["cpu_baseline"] = cb[max(cb)]
+            res["cpu_baseline_1thread"] = cb[1]
         print(json.dumps(res))
     if world > 1:
         import torch.distributed as dist

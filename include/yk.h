@@ -287,7 +287,9 @@ yk_status yk_spec_verify_probs(yk_sampler* s, int32_t B, const float* p, const f
                                const uint32_t* seq_ids, uint32_t* out_tokens, int32_t* out_counts);
 /* Whole sampler phase of one step from host logits (draft sampling of k tokens
  * per sequence, then verification): draft_logits[B x k x V],
- * target_logits[B x (k+1) x V]. */
+ * target_logits[B x (k+1) x V].  Both NULL: the logits the previous call
+ * uploaded for this B are still on the device and are sampled again (with this
+ * call's seed / step), so the device phase can be run without the upload. */
 yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float* draft_logits,
                                 const float* target_logits, float temperature, uint64_t seed,
                                 uint32_t step, const uint32_t* seq_ids, uint32_t* draft_tokens_out,

@@ -271,23 +271,31 @@ void linear(const Ctx& cx, const float* W, int out_dim, int in_dim, const float*
         else if (compat_bias_only) s = s + 0.1f;                        // LMHead: bias, no ReLU
         y[(size_t)t * out_dim + o] = s;
     };
+    // Eight tokens' dot products side by side: each is still one sequential chain
+    // in k with a separate multiply and add (the same result as one at a time),
+    // but the eight chains overlap in time.  x is regrouped as [T/8][in_dim][8] so
+    // the eight tokens' k-th inputs are adjacent.
+    constexpr int U = 8;
+    const int G = T / U;
+    std::vector<float> xg((size_t)G * in_dim * U);
+    for (int g = 0; g < G; ++g)
+        for (int u = 0; u < U; ++u) {
+            const float* xr = x + (size_t)(g * U + u) * in_dim;
+            float* dst = xg.data() + (size_t)g * in_dim * U + u;
+            for (int k = 0; k < in_dim; ++k) dst[(size_t)k * U] = xr[k];
+        }
     parallel_for(out_dim, cx.nthreads, [&](int o) {
         const float* wr = W + (size_t)o * in_dim;
-        int t = 0;
-        // eight tokens' dot products side by side: each is still one sequential
-        // chain in k (same result as one at a time), but the chains overlap in time
-        constexpr int U = 8;
-        for (; t + U <= T; t += U) {
-            float s[U];
-            const float* xr[U];
-            for (int u = 0; u < U; ++u) { s[u] = 0.0f; xr[u] = x + (size_t)(t + u) * in_dim; }
+        for (int g = 0; g < G; ++g) {
+            const float* xk = xg.data() + (size_t)g * in_dim * U;
+            float s[U] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             for (int k = 0; k < in_dim; ++k) {
                 const float wk = wr[k];
-                for (int u = 0; u < U; ++u) s[u] += xr[u][k] * wk;
+                for (int u = 0; u < U; ++u) s[u] += xk[(size_t)k * U + u] * wk;
             }
-            for (int u = 0; u < U; ++u) store(t + u, o, s[u]);
+            for (int u = 0; u < U; ++u) store(g * U + u, o, s[u]);
         }
-        for (; t < T; ++t) {
+        for (int t = G * U; t < T; ++t) {
             const float* xr = x + (size_t)t * in_dim;
             float s = 0.0f;
             for (int k = 0; k < in_dim; ++k) s += xr[k] * wr[k];

@@ -524,15 +524,23 @@ class Sampler:
                                          step, ptr(s, C.c_uint32), ptr(out, C.c_uint32), ptr(cnt, C.c_int32)))
         return out, cnt
 
-    def sample_logits(self, dl: np.ndarray, tl: np.ndarray, T: float, seed: int, step: int, seq_ids):
-        B = dl.shape[0]
-        dl, tl, s = f32(dl), f32(tl), u32(seq_ids)
+    def sample_logits(self, dl, tl, T: float, seed: int, step: int, seq_ids):
+        """dl, tl: host logits [B x k x V], [B x (k+1) x V]; both None: the logits the
+        previous call uploaded (same B, from len(seq_ids)) are sampled again."""
+        s = u32(seq_ids)
+        B = len(s)
+        if dl is None:
+            pd = pt = None
+        else:
+            dl, tl = f32(dl), f32(tl)
+            if dl.shape[0] != B or tl.shape[0] != B:
+                raise ValueError("logits and seq_ids disagree on B")
+            pd, pt = ptr(dl, C.c_float), ptr(tl, C.c_float)
         drafts = np.zeros((B, self.k), dtype=np.uint32)
         out = np.zeros((B, self.k + 1), dtype=np.uint32)
         cnt = np.zeros(B, dtype=np.int32)
-        check(lib().yk_spec_sample_logits(self.h, B, ptr(dl, C.c_float), ptr(tl, C.c_float), T, seed, step,
-                                          ptr(s, C.c_uint32), ptr(drafts, C.c_uint32), ptr(out, C.c_uint32),
-                                          ptr(cnt, C.c_int32)))
+        check(lib().yk_spec_sample_logits(self.h, B, pd, pt, T, seed, step, ptr(s, C.c_uint32),
+                                          ptr(drafts, C.c_uint32), ptr(out, C.c_uint32), ptr(cnt, C.c_int32)))
         return drafts, out, cnt
 
     def draft_sample(self, model: Model, B: int, j: int, T: float, seed: int, step: int, seq_ids):

@@ -236,6 +236,7 @@ struct yk_sampler {
     unsigned long long* stamps = nullptr;  // test hook: per-CTA phase stamps of draft sampling / verify
     int stamps_cap = 0;
     std::vector<uint32_t> dev_seq;  // the sequence ids last uploaded to io[0..B) (re-uploaded only on change)
+    int32_t logits_B = 0;           // batch whose logits yk_spec_sample_logits last uploaded (dlogits, q)
 };
 
 // ---- internal launchers ----------------------------------------------------

@@ -653,6 +653,7 @@ extern "C" yk_status yk_spec_verify_probs(yk_sampler* s, int32_t B, const float*
     IoLayout L = io_layout(s, B);
     YK_TRY(upload_small(s, B, seq_ids, draft_tokens, L));
     YK_CHECK_CUDA(cudaMemcpyAsync(s->probs, p, (size_t)B * s->k * V * 4, cudaMemcpyHostToDevice, e->stream));
+    s->logits_B = 0;  // s->q now holds probabilities, not logits
     YK_CHECK_CUDA(cudaMemcpyAsync(s->q, q, (size_t)B * (s->k + 1) * V * 4, cudaMemcpyHostToDevice, e->stream));
     YK_TRY(run_verify(s, B, s->q, 0, 1.0f, seed, step, L));
     return finish_verify(s, B, L, out_tokens, out_counts);
@@ -662,9 +663,11 @@ extern "C" yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float
                                            const float* target_logits, float temperature, uint64_t seed,
                                            uint32_t step, const uint32_t* seq_ids, uint32_t* draft_tokens_out,
                                            uint32_t* out_tokens, int32_t* out_counts) {
-    YK_ARG(s && draft_logits && target_logits && seq_ids && draft_tokens_out && out_tokens && out_counts,
-           "null argument");
+    YK_ARG(s && seq_ids && draft_tokens_out && out_tokens && out_counts, "null argument");
+    YK_ARG((draft_logits == nullptr) == (target_logits == nullptr), "draft and target logits: both or neither");
     YK_ARG(B > 0 && B <= s->max_seqs, "B");
+    const bool resident = draft_logits == nullptr;
+    YK_ARG(!resident || s->logits_B == B, "no logits of this batch size are resident (pass host logits first)");
     yk_engine* e = s->e;
     YK_CHECK_CUDA(cudaSetDevice(e->device));
     const size_t V = s->vocab;
@@ -672,8 +675,14 @@ extern "C" yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float
     if (!s->dlogits) YK_CHECK_CUDA(cudaMalloc(&s->dlogits, (size_t)s->max_seqs * k * V * 4));
     IoLayout L = io_layout(s, B);
     YK_TRY(upload_small(s, B, seq_ids, nullptr, L));
-    YK_CHECK_CUDA(cudaMemcpyAsync(s->dlogits, draft_logits, (size_t)B * k * V * 4, cudaMemcpyHostToDevice, e->stream));
-    YK_CHECK_CUDA(cudaMemcpyAsync(s->q, target_logits, (size_t)B * (k + 1) * V * 4, cudaMemcpyHostToDevice, e->stream));
+    if (!resident) {
+        s->logits_B = 0;
+        YK_CHECK_CUDA(cudaMemcpyAsync(s->dlogits, draft_logits, (size_t)B * k * V * 4, cudaMemcpyHostToDevice,
+                                      e->stream));
+        YK_CHECK_CUDA(cudaMemcpyAsync(s->q, target_logits, (size_t)B * (k + 1) * V * 4, cudaMemcpyHostToDevice,
+                                      e->stream));
+        s->logits_B = B;
+    }
     DraftArgs a;
     a.logits = s->dlogits;
     a.logit_row_stride = k;
