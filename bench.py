@@ -410,14 +410,16 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
         tot_accepted = float(acc1 - acc0) if tp else allreduce_sum(world, float(acc1 - acc0))
         tot_seqs = float(B) if tp else allreduce_sum(world, float(B))
 
-        gemm = attn = None
+        gemm = attn = ar = None
+        prof_steps = max(1, min(args.steps, 4))
         if profile:
             # kernel roofline: a second pass of the same steps with per-launch CUDA events
             eng.profile(True)
-            for _ in range(max(1, min(args.steps, 4))):
+            for _ in range(prof_steps):
                 sch.step()
             gemm = eng.profile_read(0)
             attn = eng.profile_read(1)
+            ar = eng.profile_read(3)  # tensor-parallel all-reduce (NCCL), if any
             eng.profile(False)
         # in-situ breakdown of one more step from the launch trace (first CTA past the
         # grid dependency wait, last CTA exit per launch), programmatic launch on
@@ -479,6 +481,17 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
                            "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"])}
         res["attention"] = {"achieved_gbs": attn_gbs, "frac": attn_gbs / peaks["hbm_gbs"],
                             "launches": attn["launches"]}
+        if tp and ar is not None and ar["launches"] > 0:
+            ar_ms = ar["ms"] / prof_steps
+            res["allreduce"] = {
+                "ms_per_step": ar_ms, "launches_per_step": ar["launches"] / prof_steps,
+                "share_of_step": ar_ms / step_ms,
+                "payload": "fp32" if os.environ.get("YK_TP_PAYLOAD") == "f32" else "bf16",
+                # what one rank sends over NVLink in a ring all-reduce, per second of all-reduce time
+                "link_gbs": ar["bytes"] / (ar["ms"] / 1e3) / 1e9 if ar["ms"] > 0 else None,
+                "link_peak_gbs": 770.0,
+                "note": "CUDA events around each ncclAllReduce on the engine stream, in a second pass of "
+                        f"{prof_steps} steps without programmatic launch"}
     return res
 
 

@@ -119,7 +119,8 @@ uint64_t  yk_engine_launch_count(yk_engine* e);
 /* Kernel timing: while enabled, every launch of the classes below is bracketed
  * by CUDA events on the engine stream and its algorithmic bytes / flops are
  * accumulated.  Class 0 = tcgen05/SIMT GEMM, 1 = paged attention, 2 = sampler,
- * 3 = other (embedding, RMSNorm).  Reading resolves pending events (syncs). */
+ * 3 = other (the tensor-parallel all-reduce; bytes = what one rank moves over
+ * NVLink in a ring all-reduce).  Reading resolves pending events (syncs). */
 #define YK_PROF_GEMM    0
 #define YK_PROF_ATTN    1
 #define YK_PROF_SAMPLER 2
@@ -330,8 +331,16 @@ yk_status yk_spec_verify_logits_noalloc(int32_t device, void* stream, const floa
  * NVLink.  NCCL is loaded at run time (libnccl.so.2). */
 /* A new NCCL unique id (128 bytes) for rank 0 to hand to every rank. */
 yk_status yk_tp_unique_id(uint8_t id_out[128]);
-/* Joins the group: one engine per rank, all with the same id and world. */
+/* Joins the group: one engine per rank, all with the same id and world.  The
+ * set-up runs non-blocking and is abandoned (communicator aborted,
+ * YK_ERR_TIMEOUT) if the group is not complete within timeout_ms; the same
+ * deadline then bounds every wait on the engine's work (yk_engine_sync and the
+ * sampler's result reads): a stream whose collectives do not finish in time (a
+ * peer stopped taking part) ends with YK_ERR_TIMEOUT and the communicator
+ * aborted.  yk_tp_init uses 300 s.  The all-reduce payload is bf16 (env
+ * YK_TP_PAYLOAD=f32 at engine creation: fp32). */
 yk_status yk_tp_init(yk_engine* e, const uint8_t id[128], int32_t rank, int32_t world);
+yk_status yk_tp_init_timeout(yk_engine* e, const uint8_t id[128], int32_t rank, int32_t world, int64_t timeout_ms);
 /* Shard tp_rank of tp_world of the model `cfg`: query heads, KV heads and FFN
  * columns split evenly (n_kv_heads and ffn_dim divisible by tp_world); the
  * embedding, the norms and the LM head are replicated (same seed on every

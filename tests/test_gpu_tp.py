@@ -2,8 +2,15 @@
 all-reduce after o_proj and down_proj.  Each rank loads its slice of one full
 set of weights; the logits of both ranks must be identical (replicated LM head
 on the all-reduced stream) and must match the bf16-emulating oracle forward of
-the full model: max |dlogit| <= 2e-2 * max |logit|, as for the 1-GPU forward.
-Needs two GPUs (skipped otherwise)."""
+the full model: max |dlogit| <= 2e-2 * max |logit|, as for the 1-GPU forward,
+with the all-reduce payload in bf16 (the default) and in fp32.  Needs two GPUs
+(skipped otherwise).
+
+Failure handling (no GPU is faulted): a group whose second rank never joins
+ends set-up with YK_ERR_TIMEOUT on one GPU; on two GPUs, a rank that leaves
+between steps makes the other rank's next step end with YK_ERR_TIMEOUT (its
+collective cannot finish; the bounded wait aborts the communicator).  NVLS is
+off in every test here."""
 import os
 
 import numpy as np
@@ -73,8 +80,9 @@ def _load_full(m, w):
         m.load(abi.T_NORM2, l, w["n2"][l], abi.DTYPE_F32)
 
 
-def _worker(rank, uid, q, via_loader=False):
-    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+def _worker(rank, uid, q, via_loader=False, payload="bf16"):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["YK_TP_PAYLOAD"] = payload
     try:
         e = abi.Engine(rank)
         e.tp_init(uid, rank, WORLD)
@@ -120,8 +128,8 @@ def _worker(rank, uid, q, via_loader=False):
         q.put((rank, None, None, repr(ex)))
 
 
-@pytest.mark.parametrize("via_loader", [False, True])
-def test_tp2_forward_matches_oracle(oracle, via_loader):
+@pytest.mark.parametrize("via_loader,payload", [(False, "bf16"), (True, "bf16"), (False, "f32")])
+def test_tp2_forward_matches_oracle(oracle, via_loader, payload):
     import torch
 
     if torch.cuda.device_count() < WORLD:
@@ -131,7 +139,7 @@ def test_tp2_forward_matches_oracle(oracle, via_loader):
     uid = abi.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, uid, q, via_loader)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, uid, q, via_loader, payload)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = {}
@@ -157,4 +165,97 @@ def test_tp2_forward_matches_oracle(oracle, via_loader):
         g0, g1 = res[0][0][i], res[1][0][i]
         np.testing.assert_array_equal(g0, g1)  # both ranks hold the same all-reduced stream
         err = np.abs(g0 - o).max() / np.abs(o).max()
+        print(f"payload {payload} step {i}: max |dlogit| / max |logit| = {err:.3e}")
         assert err < 2e-2, f"step {i}: rel err {err:.3e}"
+
+
+def _init_alone(q):
+    """Rank 0 of a group of two whose rank 1 never calls init."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        e = abi.Engine(0)
+        try:
+            e.tp_init(abi.tp_unique_id(), 0, 2, timeout_ms=3000)
+            q.put(("joined", None))
+        except abi.YKError as ex:
+            # the engine stays usable after the aborted set-up
+            e.sync()
+            q.put((ex.status, abi.last_error()))
+        e.close()
+    except Exception as ex:
+        q.put(("error", repr(ex)))
+
+
+def test_tp_init_times_out_when_a_rank_never_joins():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_init_alone, args=(q,))
+    p.start()
+    try:
+        status, msg = q.get(timeout=120)
+    finally:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert status == abi.YK_ERR_TIMEOUT, (status, msg)
+    assert "not every rank joined" in msg
+
+
+def _leaver(rank, uid, q):
+    """Both ranks run one forward step; rank 1 then leaves (between steps, nothing
+    in flight) and rank 0 runs a second step whose all-reduce cannot finish."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        e = abi.Engine(rank)
+        e.tp_init(uid, rank, WORLD, timeout_ms=8000)
+        c = abi.make_config(**CFG, dtype=abi.DTYPE_BF16, max_tokens=128, max_seqs=8)
+        m = abi.Model(e, c, seed=3, tp=(rank, WORLD))
+        pool = abi.KVPool(e, m.cfg, NB)
+        pt = PageTables(NB)
+        steps = _steps()
+        toks, qs, ctx, bt = step_inputs(pt, steps[0])
+        m.forward(pool, toks, qs, ctx, bt, 0)
+        e.sync()
+        if rank == 1:
+            q.put((rank, "left"))
+            q.close()
+            q.join_thread()  # the message is out before the process goes
+            os._exit(0)  # leaves without tearing the group down, as a crashed rank would
+        toks, qs, ctx, bt = step_inputs(pt, steps[1])
+        try:
+            m.forward(pool, toks, qs, ctx, bt, 5)
+            e.sync()
+            q.put((rank, "finished"))
+        except abi.YKError as ex:
+            q.put((rank, ex.status))
+    except Exception as ex:
+        q.put((rank, repr(ex)))
+
+
+def test_tp_peer_leaving_ends_the_next_step_with_timeout():
+    import torch
+
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    uid = abi.tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_leaver, args=(r, uid, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(WORLD):
+            rank, what = q.get(timeout=180)
+            res[rank] = what
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[1] == "left"
+    assert res[0] == abi.YK_ERR_TIMEOUT, res[0]

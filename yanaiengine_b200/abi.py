@@ -75,6 +75,7 @@ _PROTOS = {
                                        C.POINTER(_P)]),
     "yk_tp_unique_id": (C.c_int32, [C.POINTER(C.c_uint8)]),
     "yk_tp_init": (C.c_int32, [_P, C.POINTER(C.c_uint8), C.c_int32, C.c_int32]),
+    "yk_tp_init_timeout": (C.c_int32, [_P, C.POINTER(C.c_uint8), C.c_int32, C.c_int32, C.c_int64]),
     "yk_model_destroy": (None, [_P]),
     "yk_model_get_config": (C.c_int32, [_P, C.POINTER(ModelConfig)]),
     "yk_model_tensor_shape": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
@@ -304,10 +305,14 @@ class Engine:
         check(lib().ykt_trace_read(self.h, ptr(out, C.c_uint64), self._trace_cap, C.byref(n)))
         return out, int(n.value)
 
-    def tp_init(self, uid: bytes, rank: int, world: int) -> None:
-        """Join a tensor-parallel NCCL group (uid from tp_unique_id on rank 0)."""
+    def tp_init(self, uid: bytes, rank: int, world: int, timeout_ms: int | None = None) -> None:
+        """Join a tensor-parallel NCCL group (uid from tp_unique_id on rank 0); set-up and
+        later waits on the group's work give up after timeout_ms (default 300 s)."""
         buf = (C.c_uint8 * 128).from_buffer_copy(uid)
-        check(lib().yk_tp_init(self.h, buf, rank, world))
+        if timeout_ms is None:
+            check(lib().yk_tp_init(self.h, buf, rank, world))
+        else:
+            check(lib().yk_tp_init_timeout(self.h, buf, rank, world, int(timeout_ms)))
 
     def sync(self):
         check(lib().yk_engine_sync(self.h))

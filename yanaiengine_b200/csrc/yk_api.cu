@@ -104,6 +104,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     if (const char* v = std::getenv("YK_META_ASYNC")) e->meta_async = std::atoi(v) != 0;
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
+    if (const char* v = std::getenv("YK_TP_PAYLOAD")) e->tp_bf16 = std::strcmp(v, "f32") != 0;
     yk_status s = e->ensure_pinned((size_t)4 << 20);
     if (s != YK_OK) { delete e; return s; }
     *out = e;
@@ -137,8 +138,7 @@ extern "C" yk_status yk_engine_stream(yk_engine* e, void** stream) {
 extern "C" yk_status yk_engine_sync(yk_engine* e) {
     YK_ARG(e, "null handle");
     YK_CHECK_CUDA(cudaSetDevice(e->device));
-    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
-    return YK_OK;
+    return yk::engine_sync_bounded(e);
 }
 
 extern "C" yk_status yk_engine_device_error(yk_engine* e, uint32_t* code) {
@@ -799,13 +799,15 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         kv_win += c.window > 0 ? std::min((double)ctx[b], (double)c.window + n - 1) : (double)ctx[b];
     }
     const double kv_tok_bytes = 2.0 * kvd * (double)m->esize;
-    // Tensor parallel: o_proj / down_proj write fp32 partials that are summed
-    // across the group; the sum is added to the residual stream by the next RMSNorm.
+    // Tensor parallel: o_proj / down_proj write partials (bf16, or fp32 with
+    // YK_TP_PAYLOAD=f32) that are summed across the group; the sum is added to the
+    // residual stream by the next RMSNorm.
     const bool tp = m->tp_world > 1;
-    const float* pend = nullptr;  // all-reduced partial not yet added to h
+    const void* pend = nullptr;  // all-reduced partial not yet added to h
     EpiParams es;
     es.kind = EPI_STORE;
     es.out = m->tp_y;
+    es.store_bf16 = e->tp_bf16 ? 1 : 0;
     // RMSNorm folded into the GEMMs (bf16, one GPU): the residual epilogue (and the
     // embedding) writes x = bf16(h * gain) and 32-row sums of squares; the next
     // GEMM scales each token's accumulator by its 1/rms.  The final norm stays a
@@ -829,7 +831,7 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
     YK_TRY(launch_embed(m, m->cur.tokens, m->cur.pos, T, dt, fused ? m->layers[0].n1 : nullptr));
     for (int l = 0; l < c.n_layers; ++l) {
         LayerWeights& L = m->layers[l];
-        if (!fused) YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr, pend));
+        if (!fused) YK_TRY(launch_rmsnorm(m, L.n1, T, nullptr, pend, e->tp_bf16));
         pend = nullptr;
         EpiParams eq;
         eq.kind = EPI_QKV;
@@ -863,14 +865,14 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         er.ld = d;
         if (tp) {
             YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, es));
-            YK_TRY(tp_allreduce_f32(e, m->tp_y, (size_t)T * d));
+            YK_TRY(tp_allreduce(e, m->tp_y, (size_t)T * d, e->tp_bf16));
             pend = m->tp_y;
         } else {
             EpiParams eo = er;
             norm_out(eo, L.n2);
             YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, eo));
         }
-        if (!fused) YK_TRY(launch_rmsnorm(m, L.n2, T, nullptr, pend));
+        if (!fused) YK_TRY(launch_rmsnorm(m, L.n2, T, nullptr, pend, e->tp_bf16));
         pend = nullptr;
         EpiParams eg;
         eg.kind = EPI_GLU;
@@ -889,7 +891,7 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         YK_TRY(gemm_run(m, L.wgu, &L.tm_gu, m->xn, 2 * F, d, T, eg));
         if (tp) {
             YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, es));
-            YK_TRY(tp_allreduce_f32(e, m->tp_y, (size_t)T * d));
+            YK_TRY(tp_allreduce(e, m->tp_y, (size_t)T * d, e->tp_bf16));
             pend = m->tp_y;
         } else {
             EpiParams ed = er;
@@ -897,7 +899,7 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
             YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, ed));
         }
     }
-    YK_TRY(launch_rmsnorm(m, m->final_norm, R, m->cur.rows, pend));
+    YK_TRY(launch_rmsnorm(m, m->final_norm, R, m->cur.rows, pend, e->tp_bf16));
     EpiParams el;
     el.kind = EPI_LOGITS;
     el.ref_compat = c.ref_compat;

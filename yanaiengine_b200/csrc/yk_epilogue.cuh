@@ -83,6 +83,12 @@ __device__ __forceinline__ void epi_pair(const EpiParams& p, int n, int j, float
     if (j >= p.m_tok || n >= p.n_out) return;
     if constexpr (KIND == EPI_STORE || KIND == EPI_LOGITS) {
         if constexpr (KIND == EPI_LOGITS) { v0 = logit_out(p, v0); v1 = logit_out(p, v1); }
+        if (KIND == EPI_STORE && p.store_bf16) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)j * p.n_out + n;
+            o[0] = __float2bfloat16_rn(v0);
+            if (n + 1 < p.n_out) o[1] = __float2bfloat16_rn(v1);
+            return;
+        }
         float* o = reinterpret_cast<float*>(p.out) + (size_t)j * p.n_out + n;
         o[0] = v0;
         if (n + 1 < p.n_out) o[1] = v1;
@@ -258,7 +264,12 @@ __device__ __forceinline__ void drain16(const EpiParams& p, int n, int j0, const
     } else {  // EPI_STORE, EPI_LOGITS
         if (n >= p.n_out) return;
         float* o = reinterpret_cast<float*>(p.out);
-        if (KIND == EPI_STORE || (!p.ref_compat && p.cap <= 0.f)) {  // plain store
+        if (KIND == EPI_STORE && p.store_bf16) {
+            __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (j0 + i < p.m_tok) ob[(size_t)(j0 + i) * p.n_out + n] = __float2bfloat16_rn(v[i]);
+        } else if (KIND == EPI_STORE || (!p.ref_compat && p.cap <= 0.f)) {  // plain store
 #pragma unroll
             for (int i = 0; i < 16; ++i)
                 if (j0 + i < p.m_tok) o[(size_t)(j0 + i) * p.n_out + n] = v[i];
@@ -320,6 +331,10 @@ __device__ __forceinline__ void epi_quad(const EpiParams& p, int n, int j, float
     } else if constexpr (KIND == EPI_STORE || KIND == EPI_LOGITS) {
         if (KIND == EPI_LOGITS && (p.ref_compat || p.cap > 0.f)) {
             v.x = logit_out(p, v.x); v.y = logit_out(p, v.y); v.z = logit_out(p, v.z); v.w = logit_out(p, v.w);
+        }
+        if (KIND == EPI_STORE && p.store_bf16) {
+            store4(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)j * p.n_out + n, v.x, v.y, v.z, v.w);
+            return;
         }
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)j * p.n_out + n) = v;
     } else if constexpr (KIND == EPI_GLU) {

@@ -89,6 +89,8 @@ struct yk_engine {
     bool profiling = false;
     void* nccl_comm = nullptr;           // tensor-parallel group (yk_tp_init), else null
     int tp_rank = 0, tp_world = 1;
+    bool tp_bf16 = true;                 // all-reduce payload bf16 (env YK_TP_PAYLOAD=f32: fp32)
+    int64_t tp_timeout_ms = 300000;      // deadline of group set-up and of a wait on the group's work
     void* trace_rec = nullptr;           // launch trace records (test hook), else null
     uint32_t trace_cap = 0;
     std::vector<ProfRecord> prof_pending;
@@ -281,8 +283,9 @@ struct EpiParams {
     int n_out = 0;          // valid output rows
     int m_tok = 0;          // valid tokens
     int ref_compat = 0;
-    // EPI_STORE: out[j * n_out + n] (activation dtype)
+    // EPI_STORE: out[j * n_out + n], fp32 (bf16 when store_bf16)
     void* out = nullptr;
+    int store_bf16 = 0;
     // EPI_QKV
     int q_dim = 0, kv_dim = 0, head_dim = 0, n_kv = 0;
     const int32_t* pos = nullptr;    // [m_tok] token positions
@@ -350,8 +353,15 @@ yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, i
 // Device array [B x k] of the draft tokens yk_draft_sample kept on the device
 // for a batch of B sequences.
 const uint32_t* sampler_device_drafts(const yk_sampler* s, int B, int* k);
-yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx, const float* add = nullptr);
-yk_status tp_allreduce_f32(yk_engine* e, float* buf, size_t count);
+// add: a pending residual [rows of h x d] added to h first (fp32, or bf16 when add_bf16)
+yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx, const void* add = nullptr,
+                         int add_bf16 = 0);
+// In-place sum over the tensor-parallel group of `count` fp32 (or bf16) values on the engine stream.
+yk_status tp_allreduce(yk_engine* e, void* buf, size_t count, bool bf16);
+// Waits for the engine stream; with a tensor-parallel group, bounded by the
+// group's deadline (the communicator is aborted and YK_ERR_TIMEOUT returned when
+// it runs out: a peer that stopped taking part leaves its collectives unfinished).
+yk_status engine_sync_bounded(yk_engine* e);
 void tp_destroy(yk_engine* e);
 yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed, uint32_t stream, float std,
                       bool constant);

@@ -124,7 +124,7 @@ template <typename AT>
 __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ g,
                                                             AT* __restrict__ y, int d, float eps,
                                                             const int32_t* __restrict__ rows,
-                                                            const float* __restrict__ add, Trace tr) {
+                                                            const void* __restrict__ add, int add_bf16, Trace tr) {
     if (threadIdx.x == 0) trace_mark(tr, TR_ENTRY);
     pdl_trigger();
     pdl_wait();
@@ -132,7 +132,10 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(float* __restrict__
     const int r = blockIdx.x;
     const int src = rows ? rows[r] : r;
     float* xr = x + (size_t)src * d;
-    const float* ar = add ? add + (size_t)src * d : nullptr;  // pending residual: x += add first
+    // pending residual (fp32, or bf16 when add_bf16): x += add first
+    const float* ar = add && !add_bf16 ? reinterpret_cast<const float*>(add) + (size_t)src * d : nullptr;
+    const __nv_bfloat16* ab =
+        add && add_bf16 ? reinterpret_cast<const __nv_bfloat16*>(add) + (size_t)src * d : nullptr;
     __shared__ float red[RN_THREADS / 32];
     float ss = 0.f;
     const bool vec = (d & 3) == 0 && d <= RN_THREADS * 4 * RN_VEC;
@@ -142,8 +145,16 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(float* __restrict__
         for (int k = 0; k < RN_VEC; ++k) {
             const int i = (threadIdx.x + k * RN_THREADS) * 4;
             xv[k] = i < d ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ar && i < d) {
-                const float4 av = *reinterpret_cast<const float4*>(ar + i);
+            if ((ar || ab) && i < d) {
+                float4 av;
+                if (ar) {
+                    av = *reinterpret_cast<const float4*>(ar + i);
+                } else {
+                    const uint2 raw = *reinterpret_cast<const uint2*>(ab + i);
+                    const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+                    const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+                    av = make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+                }
                 xv[k] = make_float4(xv[k].x + av.x, xv[k].y + av.y, xv[k].z + av.z, xv[k].w + av.w);
                 *reinterpret_cast<float4*>(xr + i) = xv[k];
             }
@@ -152,6 +163,7 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(float* __restrict__
     } else {
         for (int i = threadIdx.x; i < d; i += RN_THREADS) {
             if (ar) xr[i] += ar[i];
+            else if (ab) xr[i] += __bfloat162float(ab[i]);
             ss += xr[i] * xr[i];
         }
     }
@@ -222,15 +234,16 @@ yk_status launch_embed(yk_model* m, const int32_t* tokens, const int32_t* pos, i
     return YK_OK;
 }
 
-yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx, const float* add) {
+yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* row_idx, const void* add,
+                         int add_bf16) {
     const auto& c = m->cfg;
     if (c.dtype == YK_DTYPE_BF16)
         YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<__nv_bfloat16>, rows, RN_THREADS, 0, m->h, g,
-                                 (__nv_bfloat16*)m->xn, c.d_model, c.rms_eps, row_idx, add,
+                                 (__nv_bfloat16*)m->xn, c.d_model, c.rms_eps, row_idx, add, add_bf16,
                                  trace_next(m->e, TK_RMSNORM)));
     else
         YK_CHECK_CUDA(launch_pdl(m->e, rmsnorm_kernel<float>, rows, RN_THREADS, 0, m->h, g, (float*)m->xn, c.d_model,
-                                 c.rms_eps, row_idx, add, trace_next(m->e, TK_RMSNORM)));
+                                 c.rms_eps, row_idx, add, add_bf16, trace_next(m->e, TK_RMSNORM)));
     m->e->launches++;
     return YK_OK;
 }

@@ -484,7 +484,7 @@ static yk_status finish_verify(yk_sampler* s, int B, const IoLayout& L, uint32_t
     const size_t nout = (size_t)B * (k + 1) + B;
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, nout * 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + nout * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
-    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    YK_TRY(engine_sync_bounded(e));
     uint32_t err;
     std::memcpy(&err, e->pinned + nout * 4, 4);
     if (err) {
@@ -527,16 +527,26 @@ const uint32_t* yk::sampler_device_drafts(const yk_sampler* s, int B, int* k) {
 // Draft sampling of `rows` rows: chunked statistics, chunked probabilities, token.
 static yk_status launch_draft(yk_sampler* s, DraftArgs a, int rows) {
     yk_engine* e = s->e;
-    a.tr = trace_next(e, TK_ROW_STATS);
-    YK_CHECK_CUDA(launch_pdl(e, draft_partial_kernel, dim3(rows, SMP_CHUNKS), SMP_THREADS, 0, a));
-    e->launches++;
-    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
-    YK_CHECK_CUDA(launch_pdl(e, draft_prob_kernel, dim3(rows, SMP_CHUNKS), SMP_THREADS, 0, a));
-    e->launches++;
-    a.tr = trace_next(e, TK_DRAFT_SAMPLE);
-    a.stamps = (s->stamps && rows <= s->stamps_cap) ? s->stamps : nullptr;
-    YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, rows, SMP_THREADS, 0, a));
-    e->launches++;
+    const double row_bytes = (double)rows * a.V * 4;  // algorithmic bytes: logits read, probabilities written
+    {
+        ProfScope prof(e, YK_PROF_SAMPLER, row_bytes, 0.0);
+        a.tr = trace_next(e, TK_ROW_STATS);
+        YK_CHECK_CUDA(launch_pdl(e, draft_partial_kernel, dim3(rows, SMP_CHUNKS), SMP_THREADS, 0, a));
+        e->launches++;
+    }
+    {
+        ProfScope prof(e, YK_PROF_SAMPLER, 2.0 * row_bytes, 0.0);
+        a.tr = trace_next(e, TK_DRAFT_SAMPLE);
+        YK_CHECK_CUDA(launch_pdl(e, draft_prob_kernel, dim3(rows, SMP_CHUNKS), SMP_THREADS, 0, a));
+        e->launches++;
+    }
+    {
+        ProfScope prof(e, YK_PROF_SAMPLER, 0.0, 0.0);  // reads p up to the sampled index
+        a.tr = trace_next(e, TK_DRAFT_SAMPLE);
+        a.stamps = (s->stamps && rows <= s->stamps_cap) ? s->stamps : nullptr;
+        YK_CHECK_CUDA(launch_pdl(e, draft_sample_kernel, rows, SMP_THREADS, 0, a));
+        e->launches++;
+    }
     return YK_OK;
 }
 
@@ -571,7 +581,7 @@ extern "C" yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, 
     if (!out_tokens) return YK_OK;  // asynchronous: device checks are reported by the verification
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.out, (size_t)B * 4, cudaMemcpyDeviceToHost, e->stream));
     YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + (size_t)B * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
-    YK_CHECK_CUDA(cudaStreamSynchronize(e->stream));
+    YK_TRY(engine_sync_bounded(e));
     uint32_t err;
     std::memcpy(&err, e->pinned + (size_t)B * 4, 4);
     if (err) {
@@ -598,6 +608,7 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
         d.T = T;
         d.part = s->part;
         d.tr = trace_next(e, TK_ROW_STATS);
+        ProfScope prof(e, YK_PROF_SAMPLER, (double)B * (k + 1) * s->vocab * 4, 0.0);
         YK_CHECK_CUDA(launch_pdl(e, draft_partial_kernel, dim3(B * (k + 1), SMP_CHUNKS), SMP_THREADS, 0, d));
         e->launches++;
     }
@@ -619,6 +630,7 @@ static yk_status run_verify(yk_sampler* s, int B, const float* qsrc, int from_lo
     a.err = e->d_err;
     a.tr = trace_next(e, TK_VERIFY);
     a.stamps = (s->stamps && B <= s->stamps_cap) ? s->stamps + (size_t)s->stamps_cap * 8 : nullptr;
+    ProfScope prof(e, YK_PROF_SAMPLER, 0.0, 0.0);  // reads q, p at the drafts and a residual row up to the hit
     YK_CHECK_CUDA(launch_pdl(e, verify_kernel, B, SMP_THREADS, 0, a));
     e->launches++;
     return YK_OK;
