@@ -46,6 +46,15 @@ WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (NCCL all-re
                 "8B-shape draft replicated, bf16, k=4, T=0.8, 128 seqs x 4096 ctx")
 METRIC = "accepted tokens/sec, 8B/1B-shape k=5 batch 32, at 1/2/4/8 B200; verify HBM GB/s"
 WORKLOAD = "spec-decode step: 8B-shape target + 1B-shape draft, bf16, k=5, T=0.8, 32 seqs/GPU, ctx U[512,2048]"
+# --workload gemma: Gemma-2-9B-shape target with a Gemma-2-2B-shape draft
+GEMMA_TARGET = dict(vocab_size=256000, d_model=3584, n_layers=42, n_heads=16, n_kv_heads=8, head_dim=256,
+                    ffn_dim=14336, rope_theta=10000.0, rms_eps=1e-6, attn_cap=50.0, final_cap=30.0, window=4096,
+                    window_layer_parity=0, act=1, ref_compat=0)
+GEMMA_DRAFT = dict(GEMMA_TARGET, d_model=2304, n_layers=26, n_heads=8, n_kv_heads=4, ffn_dim=9216)
+METRIC_GEMMA = "accepted tokens/sec, Gemma-2-9B/2B-shape k=4 batch 64, ctx U[2k,8k]"
+WORKLOAD_GEMMA = ("spec-decode step: Gemma-2-9B-shape target + 2B-shape draft, bf16, GeGLU, attention cap 50, final "
+                  "cap 30, window 4096 on even layers (split KV pools, out-of-window pages reclaimed), V=256000, k=4, "
+                  "T=1.0, 64 seqs/GPU, ctx U[2048,8192]")
 METRIC_STRONG = "accepted tokens/sec, 8B/1B-shape k=5, global batch 32 split across the GPUs"
 METRIC_SAMPLER = "accepted tokens/sec, rejection sampling only: 64 seqs, k=4, V=128256, fp32 N(0,2^2) logits, T=1"
 WORKLOAD_SAMPLER = ("sampler phase: draft sampling of k=4 tokens per sequence from fp32 draft logits + "
@@ -308,8 +317,11 @@ def run_yk(args, world, rank, local):
         tcfg = abi.make_config(**TARGET_70B, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
         dcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
     else:
-        tcfg = abi.make_config(**TARGET, dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64, max_seqs=B)
-        dcfg = abi.make_config(**DRAFT, dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64, max_seqs=B)
+        gem = args.workload == "gemma"
+        tcfg = abi.make_config(**(GEMMA_TARGET if gem else TARGET), dtype=abi.DTYPE_BF16, max_tokens=B * (k + 1) + 64,
+                               max_seqs=B)
+        dcfg = abi.make_config(**(GEMMA_DRAFT if gem else DRAFT), dtype=abi.DTYPE_BF16, max_tokens=B * 2 + 64,
+                               max_seqs=B)
     target = abi.Model(eng, tcfg, seed=1, init_std=0.02, tp=(rank, world) if tp else None)
     draft = abi.Model(eng, dcfg, seed=2, init_std=0.02)
     try:
@@ -319,14 +331,15 @@ def run_yk(args, world, rank, local):
                              np.random.default_rng(7), profile=True)
         else:
             # the job's B x world sequences, split across ranks longest-first (B per rank)
-            glens = dp.global_lengths(B, world, seed=7)
+            glens = (dp.global_lengths(B, world, seed=7, lo=2048, hi=8192) if args.workload == "gemma"
+                     else dp.global_lengths(B, world, seed=7))
             mine = dp.partition(glens, world)[rank]
             lens = glens[mine]
             res = spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B,
                              np.random.default_rng(7 + 1000 * rank), profile=True)
             if res is not None:
                 res["config"]["global_batch"] = B * world
-            if world > 1 and args.strong_batch > 0:
+            if world > 1 and args.strong_batch > 0 and args.workload == "8b-dp":
                 # strong scaling: the fixed global batch, strong_batch / world sequences per rank
                 G = args.strong_batch
                 sg = dp.global_lengths(-(-G // world), world, seed=7)[:G]
@@ -356,18 +369,32 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
 
     k, T = args.k, args.temperature
     tp = args.workload == "70b-tp"
+    split = args.workload == "gemma"  # alternating windows: split pools, out-of-window pages reclaimed
+    V = target.cfg.vocab_size
     grow = (args.warmup + 2 * args.steps + 4) * (k + 1) + 32
     blocks = int(sum(np.ceil((lens + grow) / 16))) + 64
-    tpool = abi.KVPool(eng, target.cfg, blocks)
-    dpool = abi.KVPool(eng, draft.cfg, blocks)
-    sampler = abi.Sampler(eng, B, k, TARGET["vocab_size"])
+    twpool = dwpool = None
+    if split:
+        wblocks = len(lens) * (int(np.ceil((target.cfg.window + 2 * (k + 1) + 32) / 16)) + 2) + 64
+        tpool = abi.KVPool(eng, target.cfg, blocks, abi.POOL_GLOBAL_LAYERS)
+        twpool = abi.KVPool(eng, target.cfg, wblocks, abi.POOL_WINDOWED_LAYERS)
+        dpool = abi.KVPool(eng, draft.cfg, blocks, abi.POOL_GLOBAL_LAYERS)
+        dwpool = abi.KVPool(eng, draft.cfg, wblocks, abi.POOL_WINDOWED_LAYERS)
+    else:
+        tpool = abi.KVPool(eng, target.cfg, blocks)
+        dpool = abi.KVPool(eng, draft.cfg, blocks)
+    sampler = abi.Sampler(eng, B, k, V)
     sch = None
     try:
         tpool.fill_random(11 + (rank if tp else 0), 1.0)
         dpool.fill_random(12, 1.0)
-        sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + (0 if tp else rank))
+        if split:
+            twpool.fill_random(13, 1.0)
+            dwpool.fill_random(14, 1.0)
+        sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + (0 if tp else rank),
+                            twpool=twpool, dwpool=dwpool)
         for i, L in enumerate(lens):
-            sch.submit(rng.integers(0, TARGET["vocab_size"], int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
+            sch.submit(rng.integers(0, V, int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
                        seq_id=int(mine[i]), cached=True)
         for _ in range(args.warmup):
             sch.step()
@@ -429,15 +456,17 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
         if sch is not None:
             sch.close()
         sampler.close()
-        dpool.close()
-        tpool.close()
+        for p in (dwpool, twpool, dpool, tpool):
+            if p is not None:
+                p.close()
 
     peaks = measured_peaks()
     if rank != 0:
         return None
     step_ms = max_dev_s * 1e3 / args.steps
+    tcfg_d = TARGET_70B if tp else GEMMA_TARGET if split else TARGET
     res = {
-        "metric": METRIC_70B if tp else METRIC,
+        "metric": METRIC_70B if tp else METRIC_GEMMA if split else METRIC,
         "value": tot_emitted / max_dev_s,
         "unit": "tokens/s",
         "n_gpus": world,
@@ -453,15 +482,16 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
                     "parallelism": f"tp{world} target, draft replicated",
                     "l2": "inputs larger than L2 (17.5 GB target shard + 16 GB draft per GPU per step)"}
                    if tp else
-                   {"workload": WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B, "k": k,
-                    "temperature": T, "ctx": "U[512,2048] + growth", "parallelism": f"dp{world} (replicas)",
-                    "l2": "inputs larger than L2 (17.5 GB of weights streamed per step)"}),
+                   {"workload": WORKLOAD_GEMMA if split else WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B,
+                    "k": k, "temperature": T, "ctx": ("U[2048,8192]" if split else "U[512,2048]") + " + growth",
+                    "parallelism": f"dp{world} (replicas)",
+                    "l2": "inputs larger than L2 (GBs of weights streamed per step)"}),
         "e2e": {"value": tot_emitted / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d / args.steps),
                 "d2h_bytes_per_step": int(d2h / args.steps)},
         "gpu_launches": int(launches),
         "accept_rate": float(tot_accepted / max(1.0, args.steps * tot_seqs * k)),
         "emitted_per_step": float(tot_emitted / args.steps),
-        "verify_step": verify_roofline(TARGET_70B if tp else TARGET, ctx_before, k, world if tp else 1,
+        "verify_step": verify_roofline(tcfg_d, ctx_before, k, world if tp else 1,
                                        breakdown.get("verify_forward_us"), peaks),
         "step_breakdown": breakdown,
         "clocks": clk,
@@ -503,10 +533,14 @@ def verify_roofline(cfg: dict, ctx_before, k: int, tp_world: int, us, peaks) -> 
     tokens' K/V included)."""
     if not us:
         return None
-    kv_tok = 2 * cfg["n_kv_heads"] // tp_world * cfg["head_dim"] * 2 * cfg["n_layers"]  # bytes per token, all layers
+    kv_layer_tok = 2 * cfg["n_kv_heads"] // tp_world * cfg["head_dim"] * 2  # bytes per token per layer (K and V)
     w = params_bytes(cfg) - cfg["vocab_size"] * cfg["d_model"] * 2  # sharded part
     weights = w / tp_world + cfg["vocab_size"] * cfg["d_model"] * 2
-    kv = sum(c + k + 1 for c in ctx_before) * kv_tok
+    L, W, par = cfg["n_layers"], cfg.get("window", 0), cfg.get("window_layer_parity", -1)
+    n_win = 0 if W <= 0 else (L if par < 0 else sum(1 for l in range(L) if l % 2 == par))
+    # a windowed layer reads the keys inside the window of its queries (the last
+    # query's window plus the k earlier new tokens)
+    kv = sum((L - n_win) * (c + k + 1) + n_win * min(c + k + 1, W + k) for c in ctx_before) * kv_layer_tok
     ach = (weights + kv) / (us * 1e-6) / 1e9
     return {"us": us, "bytes": weights + kv, "weight_bytes": weights, "kv_bytes": kv, "achieved_gbs": ach,
             "peak_gbs": peaks["hbm_gbs"], "frac": ach / peaks["hbm_gbs"], "peak_src": peaks["src"]}
@@ -847,13 +881,22 @@ def main():
     ap.add_argument("--strong-batch", type=int, default=32,
                     help="8b-dp on more than one GPU: also time this global batch split across the GPUs "
                          "(strong scaling, reported as `strong`); 0 skips it")
-    ap.add_argument("--workload", default="8b-dp", choices=["8b-dp", "70b-tp", "prefill", "sampler"],
+    ap.add_argument("--workload", default="8b-dp", choices=["8b-dp", "70b-tp", "prefill", "sampler", "gemma"],
                     help="8b-dp: the headline 8B/1B data-parallel step; 70b-tp: 70B-shape target over all GPUs; "
                          "prefill: the first scheduler step of a fresh batch (whole prompts); sampler: the "
-                         "rejection-sampling phase alone (64 seqs, k=4, V=128256, fp32 N(0,4) logits)")
+                         "rejection-sampling phase alone (64 seqs, k=4, V=128256, fp32 N(0,4) logits); gemma: "
+                         "the Gemma-2-9B/2B-shape step (64 seqs/GPU, k=4, T=1, ctx U[2k,8k], split KV pools)")
     args = ap.parse_args()
     if args.workload == "sampler":
         # the sampler-only configuration: 64 sequences, k = 4, T = 1 (other flags as given)
+        if "--batch" not in sys.argv:
+            args.batch = 64
+        if "--k" not in sys.argv:
+            args.k = 4
+        if "--temperature" not in sys.argv:
+            args.temperature = 1.0
+    if args.workload == "gemma":
+        # the Gemma configuration: 64 sequences, k = 4, T = 1 (other flags as given)
         if "--batch" not in sys.argv:
             args.batch = 64
         if "--k" not in sys.argv:

@@ -76,6 +76,14 @@ yk_status ykt_trace_read(yk_engine* e, uint64_t* host, int32_t cap, uint64_t* la
 yk_status ykt_sampler_stamps_enable(yk_sampler* s, int32_t cap);
 yk_status ykt_sampler_stamps_read(yk_sampler* s, uint64_t* host, int32_t cap);
 
+/* The failure path of the bounded device waits: one kernel waits on a
+ * shared-memory barrier that nothing arrives at, with the wait every kernel
+ * uses but a budget of budget_ms (<= 2000); when it gives up the kernel records
+ * the timeout in the engine's error word and returns, and this call reports
+ * YK_ERR_TIMEOUT (clearing the word) with *waited_ms the kernel's wait.  The
+ * engine stays usable. */
+yk_status ykt_wait_timeout(yk_engine* e, int32_t budget_ms, double* waited_ms);
+
 /* The target probabilities q[B x (k+1) x V] exactly as the last verification
  * of yk_spec_sample_logits formed them from its logits (same chunk statistics,
  * same per-element expression), temperature > 0: lets a test hold the

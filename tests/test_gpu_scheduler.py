@@ -17,8 +17,9 @@ pytestmark = pytest.mark.gpu
 NTHREADS = max(4, os.cpu_count() or 4)
 
 
-def oracle_greedy_spec(orc_t, orc_d, prompt, k, steps):
-    """Restates ykh_step for one sequence with greedy draft sampling and verification."""
+def oracle_greedy_spec(orc_t, orc_d, prompt, k, steps, runs=None):
+    """Restates ykh_step for one sequence with greedy draft sampling and verification
+    (runs, if given, receives each step's emitted run)."""
     pt_t, pt_d = PageTables(orc_t.num_blocks), PageTables(orc_d.num_blocks)
     tokens = list(prompt)
     tpos = dpos = 0
@@ -44,6 +45,8 @@ def oracle_greedy_spec(orc_t, orc_d, prompt, k, steps):
         tpos = N + acc
         dpos = min(dpos, N + acc)
         tokens += out
+        if runs is not None:
+            runs.append(out)
     return tokens[len(prompt):]
 
 
@@ -158,6 +161,45 @@ def test_scheduler_streaming_callbacks(engine):
             assert all(1 <= len(run) <= 5 for run in runs[i])  # at most k + 1 tokens per step
             assert done[i] == [len(g)] and len(g) >= 15
         assert 9 not in runs and 9 not in done and len(sch.generated(9)) >= 15
+    finally:
+        sch.close()
+        s.close()
+        dp.close()
+        d.close()
+        tp.close()
+        t.close()
+
+
+def test_streaming_matches_oracle_spec_run(engine, oracle):
+    """The server path (S/InferenceServer.swift:118-126,167-176: onTokenGenerated per
+    token, onCompletion once) through ykh_submit_stream on the tiny fp32 greedy
+    pair with many rejections: every streamed run equals the oracle's speculative
+    step run, in order, and completion reports the generated count once."""
+    k, max_tokens = 4, 30
+    tcfg, dcfg = TINY, dict(TINY, n_layers=1)
+    t, tp = gpu_model(engine, tcfg, abi.DTYPE_F32, seed=5, num_blocks=64, max_tokens=48, max_seqs=4)
+    d, dp = gpu_model(engine, dcfg, abi.DTYPE_F32, seed=9, num_blocks=64, max_tokens=48, max_seqs=4)
+    s = abi.Sampler(engine, 4, k, tcfg["vocab_size"])
+    sch = abi.Scheduler(t, tp, d, dp, s, k, 0.0, 77)
+    runs, done = [], []
+    try:
+        prompt = np.random.default_rng(128).integers(0, tcfg["vocab_size"], 40).tolist()
+        sch.submit_stream(prompt, max_tokens=max_tokens, on_tokens=lambda sid, toks: runs.append((sid, toks)),
+                          on_done=lambda sid, n: done.append((sid, n)), seq_id=3)
+        for _ in range(max_tokens + 2):
+            if sch.running() == 0 and sch.waiting() == 0:
+                break
+            sch.step()
+        assert sch.running() == 0 and sch.waiting() == 0
+        orc_t = oracle_twin(oracle, t, tcfg, 64, emulate_bf16=False, nthreads=NTHREADS)
+        orc_d = oracle_twin(oracle, d, dcfg, 64, emulate_bf16=False, nthreads=NTHREADS)
+        ref_runs = []
+        oracle_greedy_spec(orc_t, orc_d, prompt, k, len(runs), ref_runs)
+        assert [sid for sid, _ in runs] == [3] * len(runs)
+        assert [toks for _, toks in runs] == ref_runs
+        streamed = [x for _, toks in runs for x in toks]
+        assert len(streamed) >= max_tokens and streamed == sch.generated(3)
+        assert done == [(3, len(streamed))]
     finally:
         sch.close()
         s.close()

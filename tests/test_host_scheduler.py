@@ -43,6 +43,7 @@ def lib(tmp_path_factory):
         ("ykh_scheduler_create", C.c_int32, [_P, _P, _P, _P, _P, C.c_int32, C.c_float, C.c_uint64, C.POINTER(_P)]),
         ("ykh_scheduler_destroy", None, [_P]),
         ("ykh_submit", C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
+        ("ykh_submit_cached", C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32]),
         ("ykh_submit_stream", C.c_int32, [_P, _U32P, C.c_int32, C.c_int32, C.c_int64, C.c_uint32, C.c_void_p,
                                           C.c_void_p, C.c_void_p]),
         ("ykh_step", C.c_int32, [_P, C.POINTER(C.c_int32)]),
@@ -81,8 +82,10 @@ class Rig:
         L.stub_reset()
         self.keep = []
 
-    def submit(self, seq, n, max_tokens, stream=None):
+    def submit(self, seq, n, max_tokens, stream=None, cached=False):
         p = (C.c_uint32 * n)(*[(seq * 17 + i) % V for i in range(n)])
+        if cached:
+            return self.L.ykh_submit_cached(self.h, p, n, max_tokens, -1, seq)
         if stream is None:
             assert self.L.ykh_submit(self.h, p, n, max_tokens, -1, seq) == 0
         else:
@@ -278,6 +281,39 @@ def test_split_pools_free_windowed_pages(lib):
             for i in range(4):
                 off.submit(i, 30, max_tokens=150)
             assert off.run()[1] == 2
+        finally:
+            off.close()
+    finally:
+        r.close()
+
+
+def test_cached_prompts_longer_than_the_window_over_split_pools(lib):
+    """Prompts already in the cache (the benchmark's synthetic contexts), longer
+    than the window, over split pools with reclamation: the windowed pools take
+    only the pages inside the window at admission (a windowed pool far smaller
+    than the prompts suffices), every table a forward gets is valid, and the
+    tokens equal those of the same run over one pool per model."""
+    r = Rig(lib, blocks=256, window=24, parity=0, reclaim=True, wblocks=16)
+    try:
+        for i in range(4):
+            assert r.submit(i, 90 + 7 * i, max_tokens=40, cached=True) == 0
+        usage, st = r.run()
+        assert st == 0
+        viol, fwd, pages = r.stats()
+        assert viol == 0 and fwd > 0
+        keep = Rig(lib, blocks=256, window=24, parity=0, reclaim=True)
+        try:
+            for i in range(4):
+                assert keep.submit(i, 90 + 7 * i, max_tokens=40, cached=True) == 0
+            assert keep.run()[1] == 0
+            assert [r.generated(i) for i in range(4)] == [keep.generated(i) for i in range(4)]
+        finally:
+            keep.close()
+        # without reclamation the 16-block windowed pools cannot hold the prompts
+        off = Rig(lib, blocks=256, window=24, parity=0, reclaim=False, wblocks=16)
+        try:
+            got = [off.submit(i, 90 + 7 * i, max_tokens=40, cached=True) for i in range(4)]
+            assert got[:2] == [0, 0] and 2 in got  # YK_ERR_OOM once the 16 blocks are used
         finally:
             off.close()
     finally:

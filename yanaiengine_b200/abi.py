@@ -131,6 +131,7 @@ _PROTOS = {
     "ykt_trace_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_sampler_stamps_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_sampler_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32]),
+    "ykt_wait_timeout": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_double)]),
     "ykt_sampler_target_probs": (C.c_int32, [_P, C.c_int32, C.c_float, C.POINTER(C.c_float)]),
     "ykt_trace_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, C.POINTER(C.c_uint64)]),
     "ykt_attention_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, _I32P]),
@@ -316,6 +317,13 @@ class Engine:
 
     def sync(self):
         check(lib().yk_engine_sync(self.h))
+
+    def wait_timeout(self, budget_ms: int) -> tuple[int, float]:
+        """Test hook: a bounded device wait on a barrier nothing arrives at; returns
+        (status, milliseconds the kernel waited)."""
+        ms = C.c_double()
+        st = lib().ykt_wait_timeout(self.h, budget_ms, C.byref(ms))
+        return st, ms.value
 
     def device_error(self) -> int:
         v = C.c_uint32()

@@ -142,14 +142,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // Waits for the phase of parity `parity` to complete.  Gives up after
-// YK_WAIT_BUDGET_NS (returns false) so no wait can hang the GPU.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// budget_ns (returns false) so no wait can hang the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded_ns(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0 && globaltimer_ns() - t0 > YK_WAIT_BUDGET_NS) return false;
+        if ((it & 255u) == 0 && globaltimer_ns() - t0 > budget_ns) return false;
     }
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    return mbar_wait_bounded_ns(bar, parity, YK_WAIT_BUDGET_NS);
 }
 
 // ---------------------------------------------------------------------------

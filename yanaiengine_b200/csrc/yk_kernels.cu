@@ -264,3 +264,47 @@ yk_status launch_init(yk_engine* e, void* p, size_t n, int dtype, uint64_t seed,
 }
 
 }  // namespace yk
+
+// ---------------------------------------------------------------------------
+// Test hook (include/yk_testing.h): the bounded-wait failure path.  One thread
+// waits on a shared-memory mbarrier that nothing ever arrives at, with the same
+// bounded wait every kernel uses but a budget of budget_ns; when the wait gives
+// up it records the timeout in the engine's error word and the kernel returns.
+// ---------------------------------------------------------------------------
+namespace yk {
+__global__ void wait_timeout_kernel(uint32_t* err, uint64_t budget_ns, unsigned long long* waited_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(smem_u32(&bar), 1);
+    mbar_fence_init();
+    const uint64_t t0 = globaltimer_ns();
+    if (!mbar_wait_bounded_ns(smem_u32(&bar), 0u, budget_ns)) raise_err(err, YK_DEV_ERR_TIMEOUT);
+    *waited_ns = globaltimer_ns() - t0;
+}
+}  // namespace yk
+
+#include "../../include/yk_testing.h"
+
+extern "C" yk_status ykt_wait_timeout(yk_engine* e, int32_t budget_ms, double* waited_ms) {
+    YK_ARG(e && budget_ms > 0 && budget_ms <= 2000, "arguments");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    unsigned long long* d = nullptr;
+    YK_CHECK_CUDA(cudaMalloc(&d, sizeof(unsigned long long)));
+    yk::wait_timeout_kernel<<<1, 32, 0, e->stream>>>(e->d_err, (uint64_t)budget_ms * 1000000ull, d);
+    e->launches++;
+    unsigned long long ns = 0;
+    uint32_t err = 0;
+    cudaError_t r = cudaGetLastError();
+    if (r == cudaSuccess) r = cudaMemcpyAsync(&ns, d, sizeof(ns), cudaMemcpyDeviceToHost, e->stream);
+    if (r == cudaSuccess) r = cudaMemcpyAsync(&err, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(e->stream);
+    cudaFree(d);
+    YK_CHECK_CUDA(r);
+    if (waited_ms) *waited_ms = (double)ns / 1e6;
+    if (err) {
+        YK_CHECK_CUDA(cudaMemset(e->d_err, 0, 4));
+        yk_set_error("a bounded device wait gave up (code " + std::to_string(err) + ")");
+        return (err & YK_DEV_ERR_TIMEOUT) ? YK_ERR_TIMEOUT : YK_ERR_DEVICE_CHECK;
+    }
+    return YK_OK;
+}

@@ -54,6 +54,17 @@ class PagedKVCache {
     explicit PagedKVCache(BlockAllocator* a) : alloc_(a) {}
     ~PagedKVCache() { reset(); }
     // Pages for positions < n (appendFromFull allocates at pos % 16 == 0, :29-35).
+    // A cache whose first n tokens are already held (a cached prompt) under window
+    // reclamation with width w: the pages wholly before the window of the next
+    // query (position n) are never read, so they get no block (-1) at all.
+    bool reserve_cached_window(int n, int w) {
+        const int first_live = n - w + 1;
+        const int need = (n + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE;
+        const int dead = first_live > 0 ? std::min(first_live / YK_BLOCK_SIZE, need) : 0;
+        while ((int)page_table.size() < dead) page_table.push_back(-1);
+        dead_pages = std::max(dead_pages, dead);
+        return reserve(n);
+    }
     bool reserve(int n) {
         const int need = (n + YK_BLOCK_SIZE - 1) / YK_BLOCK_SIZE;
         while ((int)page_table.size() < need) {
@@ -232,7 +243,11 @@ static yk_status submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int
         r->cache->current_position = n - 1;
         r->draft_cache->current_position = n - 1;
         if (r->wcache) {
-            if (!r->wcache->reserve(n - 1) || !r->draft_wcache->reserve(n - 1)) return YK_ERR_OOM;
+            // the windowed pools hold only the pages inside the window (with reclamation on)
+            const bool rw = s->reclaim;
+            if (!(rw ? r->wcache->reserve_cached_window(n - 1, s->tw_width) : r->wcache->reserve(n - 1)) ||
+                !(rw ? r->draft_wcache->reserve_cached_window(n - 1, s->dw_width) : r->draft_wcache->reserve(n - 1)))
+                return YK_ERR_OOM;
             r->wcache->current_position = n - 1;
             r->draft_wcache->current_position = n - 1;
         }
