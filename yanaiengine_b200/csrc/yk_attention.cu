@@ -208,9 +208,13 @@ struct AttnCfg {
     // pages: slower).  head_dim 64 (decode-shaped draft): resident slots matter
     // more than depth there (the planner splits long spans over the spare slots):
     // 4 CTAs per SM (96 registers) with 12 pages beat 3 with 16 and 2 with 24.
+    // head_dim 256 (Gemma): the consumer warps, not the ring, set the rate (8 or 12
+    // pages stream no faster than 4 at one CTA per SM, 34 GB/s per CTA); two CTAs per
+    // SM with 4-page rings (168 registers, a few spilled) stream 5.7 TB/s on the
+    // 9B-shape verify (657 -> 482 us per layer) and the 2B-shape decode 323 -> 276 us.
     static constexpr int CP = 1;
     static constexpr int S = DH == 256 ? 4 : 12;
-    static constexpr int CTAS_PER_SM = DH == 64 ? 4 : (DH == 128 ? 2 : 1);  // registers / shared memory
+    static constexpr int CTAS_PER_SM = DH == 64 ? 4 : 2;  // registers / shared memory
     static constexpr int LDQ = DH + 8;                       // padded Q row (elements)
     // head_dim <= 128: Q goes straight from global memory into the score MMA's A
     // fragments (registers), no shared-memory copy; the room goes to the ring
