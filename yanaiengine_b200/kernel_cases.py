@@ -3,11 +3,13 @@
     python -m yanaiengine_b200.kernel_cases attention [--dh 128 --group 4 --kv-heads 8 --seqs 32 --new 6]
     python -m yanaiengine_b200.kernel_cases gemm [--n 28672 --k 4096 --m 192]
     python -m yanaiengine_b200.kernel_cases sampler [--seqs 32 --k 5 --vocab 128256]
+    python -m yanaiengine_b200.kernel_cases forward [--shape draft|target --layers 4 --steps 3]
 
 `attention` builds a 2-layer bf16 model whose attention has the verify shape of
-the 8B-class target (or the 1B-class draft with --dh 64 --new 1), fills a KV
-pool with a synthetic context of U[512, 2048] tokens per sequence and runs
-forward steps; the pool holds about 1 GB, one layer's KV (170 MB at the target
+the 8B-class target (or the 1B-class draft with --dh 64 --new 1, the Gemma-2 9B
+target with --dh 256 --group 2 --seqs 64 --new 5 --ctx-lo 2048 --ctx-hi 8192),
+fills a KV pool with a synthetic context of U[ctx-lo, ctx-hi] (default
+U[512, 2048]) tokens per sequence and runs forward steps; the pool holds about 1 GB, one layer's KV (170 MB at the target
 shape) is larger than L2.  `gemm` runs the tcgen05 GEMM test hook on one layer
 shape with an L2 flush before each launch.  Both print one timing line.
 """
@@ -28,7 +30,7 @@ def attention(args) -> None:
                           head_dim=args.dh, ffn_dim=1024, rope_theta=500000.0, rms_eps=1e-5, dtype=abi.DTYPE_BF16,
                           max_tokens=max(64, args.seqs * args.new), max_seqs=args.seqs)
     rng = np.random.default_rng(0)
-    ctx = rng.integers(512, 2049, args.seqs)
+    ctx = rng.integers(args.ctx_lo, args.ctx_hi + 1, args.seqs)
     pages = [(int(c) + args.new * args.steps + 15) // 16 for c in ctx]
     nb = sum(pages) + 8
     m = abi.Model(e, cfg, seed=1)
@@ -103,6 +105,50 @@ def sampler(args) -> None:
     e.close()
 
 
+# Layer shapes of the speculative workload: the 1B-shape draft (decode, 1 new token
+# per sequence) and the 8B-shape target (verify, k + 1 = 6 new tokens per sequence).
+FWD_SHAPES = {
+    "draft": (dict(vocab_size=128256, d_model=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn_dim=8192), 1),
+    "target": (dict(vocab_size=128256, d_model=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336), 6),
+}
+
+
+def forward(args) -> None:
+    """A few forwards of a `--layers`-layer model of the draft or target shape over
+    32 sequences with U[512, 2048]-token synthetic contexts: every GEMM kind and the
+    attention of that shape, in situ (the ncu target for one launch of a kind)."""
+    e = abi.Engine(0)
+    shape, new = FWD_SHAPES[args.shape]
+    seqs = args.seqs
+    cfg = abi.make_config(**shape, n_layers=args.layers, rope_theta=500000.0, rms_eps=1e-5, dtype=abi.DTYPE_BF16,
+                          max_tokens=seqs * new + 64, max_seqs=seqs)
+    m = abi.Model(e, cfg, seed=1, init_std=0.02)
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(512, 2049, seqs)
+    pages = [(int(c) + new * (args.steps + 1) + 15) // 16 for c in ctx]
+    pool = abi.KVPool(e, cfg, sum(pages) + 8)
+    pool.fill_random(3, 1.0)
+    tables = np.zeros((seqs, max(pages)), np.int32)
+    nxt = 0
+    for b, n in enumerate(pages):
+        tables[b, :n] = np.arange(nxt, nxt + n)
+        nxt += n
+    times = []
+    for s in range(args.steps):
+        toks = rng.integers(0, shape["vocab_size"], seqs * new).tolist()
+        qs = list(range(0, seqs * new + 1, new))
+        e.sync()
+        t0 = time.perf_counter()
+        m.forward(pool, toks, qs, (ctx + new * (s + 1)).tolist(), tables, last_n=1)
+        e.sync()
+        times.append(time.perf_counter() - t0)
+    print(f"forward {args.shape} x {args.layers} layers, {seqs} seqs x {new} new tokens: "
+          f"{1e3 * min(times):.3f} ms per forward")
+    pool.close()
+    m.close()
+    e.close()
+
+
 def gemm(args) -> None:
     e = abi.Engine(0)
     rng = np.random.default_rng(0)
@@ -124,6 +170,8 @@ def main() -> None:
     a.add_argument("--seqs", type=int, default=32)
     a.add_argument("--new", type=int, default=6)
     a.add_argument("--steps", type=int, default=3)
+    a.add_argument("--ctx-lo", type=int, default=512)
+    a.add_argument("--ctx-hi", type=int, default=2048)
     a.add_argument("--stamps", action="store_true", help="per-CTA phase stamps of the last attention launch")
     sp = sub.add_parser("sampler")
     sp.add_argument("--seqs", type=int, default=32)
@@ -131,13 +179,18 @@ def main() -> None:
     sp.add_argument("--vocab", type=int, default=128256)
     sp.add_argument("--temperature", type=float, default=0.8)
     sp.add_argument("--steps", type=int, default=3)
+    f = sub.add_parser("forward")
+    f.add_argument("--shape", choices=sorted(FWD_SHAPES), default="draft")
+    f.add_argument("--layers", type=int, default=4)
+    f.add_argument("--seqs", type=int, default=32)
+    f.add_argument("--steps", type=int, default=3)
     g = sub.add_parser("gemm")
     g.add_argument("--n", type=int, default=28672)
     g.add_argument("--k", type=int, default=4096)
     g.add_argument("--m", type=int, default=192)
     g.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
-    {"attention": attention, "sampler": sampler, "gemm": gemm}[args.case](args)
+    {"attention": attention, "sampler": sampler, "gemm": gemm, "forward": forward}[args.case](args)
 
 
 if __name__ == "__main__":
