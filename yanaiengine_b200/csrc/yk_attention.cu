@@ -723,7 +723,16 @@ void plan_attention(const yk_model_config& c, int num_sms, int waves, bool balan
             max_pages = std::max(max_pages, (ke - kb + 15) / 16);
         }
     }
-    const long long target = (long long)num_sms * attention_ctas_per_sm(c.head_dim) * std::max(1, waves);
+    // Long spans (Gemma-shape contexts of thousands of tokens) go in two waves of
+    // half-size pieces: a piece's fixed cost (first page, partial merge: ~5 us) is
+    // small against its page loop there, and the longest piece no longer sets the
+    // end (9B/2B-shape step 86.4 -> 79.5 ms; 4 waves 81.4).  At the 8B/1B-shape
+    // verify and decode spans (tens of pages) one wave is faster.
+    long long span_pages = 0;
+    for (const auto& s : spans) span_pages += (s.ke - s.kb + 15) / 16;
+    const bool long_spans = !spans.empty() && span_pages >= 160LL * (long long)spans.size();
+    const long long target =
+        (long long)num_sms * attention_ctas_per_sm(c.head_dim) * std::max(1, waves) * (long_spans ? 2 : 1);
     auto splits = [&](const Span& s, int kp) {  // pieces of a span at kp pages per piece
         const int pages = (s.ke - s.kb + 15) / 16;
         return std::min(AT_MAX_SPLITS, (pages + kp - 1) / kp);
