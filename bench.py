@@ -43,7 +43,8 @@ GEMM_TRAFFIC_RATIO = 1.018  # measured DRAM bytes / algorithmic bytes of a GEMM 
 TARGET_70B = dict(TARGET, d_model=8192, n_layers=80, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672)
 METRIC_70B = "accepted tokens/sec, 70B-shape target (TP over all GPUs) + 8B-shape draft, k=4 batch 128"
 WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (NCCL all-reduce after o_proj / down_proj) + "
-                "8B-shape draft replicated, bf16, k=4, T=0.8, 128 seqs x 4096 ctx")
+                "8B-shape draft replicated on every rank, each rank drafting its slice of the sequences, bf16, k=4, "
+                "T=0.8, 128 seqs x 4096 ctx")
 METRIC = "accepted tokens/sec, 8B/1B-shape k=5 batch 32, at 1/2/4/8 B200; verify HBM GB/s"
 WORKLOAD = "spec-decode step: 8B-shape target + 1B-shape draft, bf16, k=5, T=0.8, 32 seqs/GPU, ctx U[512,2048]"
 # --workload gemma: Gemma-2-9B-shape target with a Gemma-2-2B-shape draft
@@ -373,6 +374,10 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
     V = target.cfg.vocab_size
     grow = (args.warmup + 2 * args.steps + 4) * (k + 1) + 32
     blocks = int(sum(np.ceil((lens + grow) / 16))) + 64
+    shard = tp and world > 1 and not args.no_draft_shard  # each rank drafts its slice of the batch
+    # with sharded drafting the draft pool holds one slice (the longest sequences, to be safe)
+    dblocks = (int(sum(np.sort(np.ceil((lens + grow) / 16))[::-1][: -(-len(lens) // world)])) + 64 if shard
+               else blocks)
     twpool = dwpool = None
     if split:
         wblocks = len(lens) * (int(np.ceil((target.cfg.window + 2 * (k + 1) + 32) / 16)) + 2) + 64
@@ -382,7 +387,7 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
         dwpool = abi.KVPool(eng, draft.cfg, wblocks, abi.POOL_WINDOWED_LAYERS)
     else:
         tpool = abi.KVPool(eng, target.cfg, blocks)
-        dpool = abi.KVPool(eng, draft.cfg, blocks)
+        dpool = abi.KVPool(eng, draft.cfg, dblocks)
     sampler = abi.Sampler(eng, B, k, V)
     sch = None
     try:
@@ -393,6 +398,8 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
             dwpool.fill_random(14, 1.0)
         sch = abi.Scheduler(target, tpool, draft, dpool, sampler, k, T, 1234 + (0 if tp else rank),
                             twpool=twpool, dwpool=dwpool)
+        if shard:
+            sch.set_draft_shard(eng, rank, world)
         for i, L in enumerate(lens):
             sch.submit(rng.integers(0, V, int(L)).tolist(), max_tokens=1 << 30, stop_token=-1,
                        seq_id=int(mine[i]), cached=True)
@@ -478,8 +485,12 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: random-init weights N(0,0.02), random token ids, synthetic N(0,1) KV context",
-        "config": ({"workload": WORKLOAD_70B, "global_batch": B, "k": k, "temperature": T, "ctx": "4096 + growth",
-                    "parallelism": f"tp{world} target, draft replicated",
+        "config": ({"workload": WORKLOAD_70B if not args.no_draft_shard else
+                    WORKLOAD_70B.replace("each rank drafting its slice of the sequences", "every rank drafting every "
+                                         "sequence"),
+                    "global_batch": B, "k": k, "temperature": T, "ctx": "4096 + growth",
+                    "parallelism": f"tp{world} target, draft replicated, drafting "
+                                   f"{'of every sequence on every rank' if args.no_draft_shard else 'sharded by sequence'}",
                     "l2": "inputs larger than L2 (17.5 GB target shard + 16 GB draft per GPU per step)"}
                    if tp else
                    {"workload": WORKLOAD_GEMMA if split else WORKLOAD, "global_batch": B * world, "seqs_per_gpu": B,
@@ -878,6 +889,8 @@ def main():
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--temperature", type=float, default=0.8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-draft-shard", action="store_true",
+                    help="70b-tp: every rank drafts every sequence (default: each rank drafts its slice)")
     ap.add_argument("--strong-batch", type=int, default=32,
                     help="8b-dp on more than one GPU: also time this global batch split across the GPUs "
                          "(strong scaling, reported as `strong`); 0 skips it")

@@ -295,6 +295,16 @@ yk_status yk_spec_sample_logits(yk_sampler* s, int32_t B, const float* draft_log
                                 const float* target_logits, float temperature, uint64_t seed,
                                 uint32_t step, const uint32_t* seq_ids, uint32_t* draft_tokens_out,
                                 uint32_t* out_tokens, int32_t* out_counts);
+/* verifySequence for sequences seq0 .. seq0+B-1 of `target`'s logits (rows
+ * (seq0+b)*(k+1)+i) against draft probabilities rows 0..B-1 of this sampler:
+ * a rank that drafted only its own slice of the batch verifies that slice
+ * (sequence-sharded drafting under tensor parallelism). */
+yk_status yk_spec_verify_range(yk_sampler* s, yk_model* target, int32_t seq0, int32_t B, float temperature,
+                               uint64_t seed, uint32_t step, const uint32_t* seq_ids, const uint32_t* draft_tokens,
+                               uint32_t* out_tokens, int32_t* out_counts);
+/* The [B x k] draft tokens yk_draft_sample kept on the device for batch size B
+ * (waits for the device; reports device checks raised during the draft phase). */
+yk_status yk_sampler_read_drafts(yk_sampler* s, int32_t B, uint32_t* out);
 /* Copies draft probabilities p[b][j][0..V) kept by yk_draft_sample (tests). */
 yk_status yk_sampler_read_probs(yk_sampler* s, int32_t b, int32_t j, float* host);
 
@@ -350,6 +360,11 @@ yk_status yk_tp_init_timeout(yk_engine* e, const uint8_t id[128], int32_t rank, 
  * down_proj, so every rank must run the same steps. */
 yk_status yk_model_create_tp(yk_engine* e, const yk_model_config* cfg, int32_t tp_rank, int32_t tp_world,
                              uint64_t seed, float init_std, yk_model** out);
+/* All-gather of `count` uint32 per rank over the group (host buffers; recv holds
+ * world x count values in rank order).  Waits for the engine stream, bounded by
+ * the group's deadline.  Used by the host scheduler to exchange drafted and
+ * verified tokens when each rank drafts its own slice of the batch. */
+yk_status yk_tp_allgather_u32(yk_engine* e, const uint32_t* send, int32_t count, uint32_t* recv);
 
 #ifdef __cplusplus
 }

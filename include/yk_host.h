@@ -82,6 +82,16 @@ yk_status ykh_counters(const ykh_scheduler* s, int64_t* steps, int64_t* emitted,
  * (S/PagedKVCache.swift:65-85).  A model with a global layer frees nothing
  * (one page holds every layer's K/V). */
 yk_status ykh_set_window_reclaim(ykh_scheduler* s, int32_t on);
+/* Sequence-sharded drafting for a tensor-parallel target (the draft model is
+ * replicated on every rank): every rank runs the same scheduler over the whole
+ * batch, but drafts only its slice (running sequences [B*rank/world,
+ * B*(rank+1)/world)) with its own draft pool and sampler rows, all-gathers the
+ * drafted tokens for the target's verify forward (which every rank runs over the
+ * whole batch), verifies its slice (yk_spec_verify_range) and all-gathers the
+ * results, so every rank updates every sequence identically.  `e` is the
+ * engine of the tensor-parallel group (yk_tp_allgather_u32); world = 1 turns it
+ * off.  The draft pool only needs room for one slice. */
+yk_status ykh_set_draft_shard(ykh_scheduler* s, yk_engine* e, int32_t rank, int32_t world);
 /* BlockAllocator.usage of the target / draft pools (S/BlockAllocator.swift:56-58). */
 float     ykh_usage(const ykh_scheduler* s, int32_t draft);
 /* Usage of the windowed-layer pools of a split scheduler (0 otherwise). */

@@ -1,18 +1,22 @@
-// yk_stub.cpp -- TEST INFRASTRUCTURE ONLY.  A CPU stand-in for the six libyk.so
+// yk_stub.cpp -- TEST INFRASTRUCTURE ONLY.  A CPU stand-in for the libyk.so
 // entry points that libyk_host.so's scheduler calls (yk_model_get_config,
-// yk_kv_pool_num_blocks, yk_forward_step[_drafts], yk_draft_sample,
-// yk_spec_verify), compiled together with host/yk_host.cpp into one test
-// library, so that the scheduling logic -- admission, page tables, rollback,
-// window reclamation, streaming -- runs without a GPU.
+// yk_kv_pool_num_blocks, yk_forward_step[_drafts|_split], yk_draft_sample,
+// yk_spec_verify[_range], yk_sampler_read_drafts, yk_tp_allgather_u32),
+// compiled together with host/yk_host.cpp into one test library, so that the
+// scheduling logic -- admission, page tables, rollback, window reclamation,
+// streaming, sequence-sharded drafting across emulated ranks -- runs without a GPU.
 //
 // The forward checks the page tables it is given: every page a query of the
 // call may read (all of the context; from first_query - window + 1 on when
 // every layer is windowed) must hold a block id inside the pool, and no block
 // may be read by two sequences of one call.  Draft tokens and verification are
 // deterministic functions of (sequence id, step, draft index).
+#include <atomic>
+#include <condition_variable>
 #include <cstdint>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <vector>
 
 #include "../../include/yk.h"
@@ -27,9 +31,22 @@ struct yk_sampler {
     int k, V;
     std::vector<uint32_t> drafts;  // [B x k] device-resident drafts
 };
+// A tensor-parallel group emulated in one process: each rank's scheduler runs on
+// its own thread, and the all-gather is a rendezvous of those threads.
+struct StubGroup {
+    std::mutex mu;
+    std::condition_variable cv;
+    int world = 1, arrived = 0, count = 0;
+    uint64_t gen = 0;
+    std::vector<uint32_t> slots[2];  // by generation parity: a slot is rewritten only after every rank read it
+};
+struct yk_engine {
+    StubGroup* group;
+    int rank;
+};
 
 namespace {
-int64_t g_violations = 0, g_forwards = 0, g_pages_checked = 0;
+std::atomic<int64_t> g_violations{0}, g_forwards{0}, g_pages_checked{0};
 
 // windowed_pool: the tables of a pool that holds only windowed layers.
 void check_tables(const yk_model* m, const yk_kv_pool* pool, const uint32_t* q_starts, const uint32_t* ctx, int B,
@@ -83,6 +100,40 @@ void stub_stats(int64_t* violations, int64_t* forwards, int64_t* pages) {
     *pages = g_pages_checked;
 }
 void stub_reset() { g_violations = g_forwards = g_pages_checked = 0; }
+StubGroup* stub_group(int world) {
+    auto* g = new StubGroup();
+    g->world = world;
+    return g;
+}
+void stub_group_free(StubGroup* g) { delete g; }
+yk_engine* stub_engine(StubGroup* g, int rank) { return new yk_engine{g, rank}; }
+void stub_engine_free(yk_engine* e) { delete e; }
+
+yk_status yk_tp_allgather_u32(yk_engine* e, const uint32_t* send, int32_t count, uint32_t* recv) {
+    if (!e || !send || !recv || count <= 0) return YK_ERR_ARG;
+    StubGroup& g = *e->group;
+    std::unique_lock<std::mutex> lk(g.mu);
+    const uint64_t my = g.gen;
+    std::vector<uint32_t>& buf = g.slots[my & 1];
+    if (g.arrived == 0) {
+        buf.assign((size_t)count * g.world, 0u);
+        g.count = count;
+    }
+    if (g.count != count) {
+        ++g_violations;
+        return YK_ERR_ARG;
+    }
+    std::memcpy(buf.data() + (size_t)e->rank * count, send, (size_t)count * 4);
+    if (++g.arrived == g.world) {
+        g.arrived = 0;
+        ++g.gen;
+        g.cv.notify_all();
+    } else {
+        g.cv.wait(lk, [&] { return g.gen != my; });
+    }
+    std::memcpy(recv, buf.data(), (size_t)count * g.world * 4);
+    return YK_OK;
+}
 
 yk_status yk_model_get_config(const yk_model* m, yk_model_config* out) {
     if (!m || !out) return YK_ERR_ARG;
@@ -140,6 +191,12 @@ yk_status yk_draft_sample(yk_sampler* s, yk_model* draft, int32_t B, int32_t j, 
     return YK_OK;
 }
 
+yk_status yk_sampler_read_drafts(yk_sampler* s, int32_t B, uint32_t* out) {
+    if (!s || !out || B <= 0 || (int)s->drafts.size() < B * s->k) return YK_ERR_ARG;
+    std::memcpy(out, s->drafts.data(), (size_t)B * s->k * 4);
+    return YK_OK;
+}
+
 yk_status yk_spec_verify(yk_sampler* s, yk_model* target, int32_t B, float temperature, uint64_t seed, uint32_t step,
                          const uint32_t* seq_ids, const uint32_t* draft_tokens, uint32_t* out_tokens,
                          int32_t* out_counts) {
@@ -155,6 +212,13 @@ yk_status yk_spec_verify(yk_sampler* s, yk_model* target, int32_t B, float tempe
         out_counts[b] = a + 1;
     }
     return YK_OK;
+}
+
+yk_status yk_spec_verify_range(yk_sampler* s, yk_model* target, int32_t seq0, int32_t B, float temperature,
+                               uint64_t seed, uint32_t step, const uint32_t* seq_ids, const uint32_t* draft_tokens,
+                               uint32_t* out_tokens, int32_t* out_counts) {
+    if (seq0 < 0 || !draft_tokens) ++g_violations;
+    return yk_spec_verify(s, target, B, temperature, seed, step, seq_ids, draft_tokens, out_tokens, out_counts);
 }
 
 }  // extern "C"

@@ -259,3 +259,80 @@ def test_tp_peer_leaving_ends_the_next_step_with_timeout():
                 p.kill()
     assert res[1] == "left"
     assert res[0] == abi.YK_ERR_TIMEOUT, res[0]
+
+
+def _spec_worker(rank, uid, q, shard):
+    """The speculative scheduler over a tensor-parallel fp32 target (this rank's
+    shard) and a replicated fp32 draft; shard: each rank drafts its slice."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        e = abi.Engine(rank)
+        e.tp_init(uid, rank, WORLD, timeout_ms=120000)
+        tc = abi.make_config(**CFG, dtype=abi.DTYPE_F32, max_tokens=256, max_seqs=8)
+        dcfg = dict(CFG, n_layers=1)
+        dc = abi.make_config(**dcfg, dtype=abi.DTYPE_F32, max_tokens=256, max_seqs=8)
+        t = abi.Model(e, tc, seed=3, tp=(rank, WORLD))
+        d = abi.Model(e, dc, seed=9)
+        tpool, dpool = abi.KVPool(e, t.cfg, 128), abi.KVPool(e, dc, 128)
+        s = abi.Sampler(e, 8, 4, CFG["vocab_size"])
+        sch = abi.Scheduler(t, tpool, d, dpool, s, 4, 0.8, 77)
+        if shard:
+            sch.set_draft_shard(e, rank, WORLD)
+        rng = np.random.default_rng(5)
+        for i in range(5):  # different lengths and budgets: slices move as sequences finish
+            sch.submit(rng.integers(0, CFG["vocab_size"], 10 + 7 * i).tolist(), max_tokens=12 + 5 * i,
+                       stop_token=-1, seq_id=i)
+        for _ in range(200):
+            if sch.running() == 0 and sch.waiting() == 0:
+                break
+            sch.step()
+        out = [sch.generated(i) for i in range(5)]
+        err = e.device_error()
+        sch.close()
+        s.close()
+        dpool.close()
+        tpool.close()
+        d.close()
+        t.close()
+        e.close()
+        q.put((rank, out, err, None))
+    except Exception as ex:
+        q.put((rank, None, None, repr(ex)))
+
+
+def test_tp2_sharded_drafting_tokens_equal_replicated():
+    """Sequence-sharded drafting (each rank drafts and verifies its slice, drafts and
+    results all-gathered) emits exactly the tokens of every rank drafting every
+    sequence: the draft's fp32 results do not depend on the batch it runs in, and
+    the uniforms are keyed by sequence id, not by rank."""
+    import torch
+
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    runs = {}
+    for shard in (False, True):
+        uid = abi.tp_unique_id()
+        q = ctx.Queue()
+        procs = [ctx.Process(target=_spec_worker, args=(r, uid, q, shard)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        res = {}
+        try:
+            for _ in range(WORLD):
+                rank, out, err, exc = q.get(timeout=240)
+                res[rank] = (out, err, exc)
+        finally:
+            for p in procs:
+                p.join(timeout=30)
+                if p.is_alive():
+                    p.kill()
+        for rank in range(WORLD):
+            assert res[rank][2] is None, res[rank][2]
+            assert res[rank][1] == 0
+        assert res[0][0] == res[1][0]  # every rank holds the same tokens
+        assert all(len(g) >= 12 for g in res[0][0])
+        runs[shard] = res[0][0]
+    assert runs[True] == runs[False]

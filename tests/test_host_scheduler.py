@@ -54,6 +54,9 @@ def lib(tmp_path_factory):
         ("ykh_scheduler_create_split", C.c_int32, [_P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_float, C.c_uint64,
                                                    C.POINTER(_P)]),
         ("ykh_usage_windowed", C.c_float, [_P, C.c_int32]),
+        ("stub_group", _P, [C.c_int]), ("stub_group_free", None, [_P]),
+        ("stub_engine", _P, [_P, C.c_int]), ("stub_engine_free", None, [_P]),
+        ("ykh_set_draft_shard", C.c_int32, [_P, _P, C.c_int32, C.c_int32]),
     ):
         f = getattr(L, name)
         f.restype, f.argtypes = res, args
@@ -63,12 +66,13 @@ def lib(tmp_path_factory):
 class Rig:
     """A scheduler over stub models: target and draft share the window schedule."""
 
-    def __init__(self, L, blocks, window=0, parity=-1, reclaim=True, wblocks=0):
-        """wblocks > 0: split pools (windowed layers in pools of wblocks blocks)."""
+    def __init__(self, L, blocks, window=0, parity=-1, reclaim=True, wblocks=0, shard=None, dblocks=None):
+        """wblocks > 0: split pools (windowed layers in pools of wblocks blocks);
+        shard = (engine, rank, world): sequence-sharded drafting; dblocks: draft pool size."""
         self.L = L
         self.t = L.stub_model(4, window, parity, V)
         self.d = L.stub_model(2, window, parity, V)
-        self.tp, self.dp = L.stub_pool(blocks), L.stub_pool(blocks)
+        self.tp, self.dp = L.stub_pool(blocks), L.stub_pool(dblocks or blocks)
         self.twp = L.stub_pool(wblocks) if wblocks else None
         self.dwp = L.stub_pool(wblocks) if wblocks else None
         self.s = L.stub_sampler(K, V)
@@ -79,7 +83,10 @@ class Rig:
         else:
             assert L.ykh_scheduler_create(self.t, self.tp, self.d, self.dp, self.s, K, 0.8, 1, C.byref(self.h)) == 0
         assert L.ykh_set_window_reclaim(self.h, 1 if reclaim else 0) == 0
-        L.stub_reset()
+        if shard is not None:
+            assert L.ykh_set_draft_shard(self.h, *shard) == 0
+        else:
+            L.stub_reset()
         self.keep = []
 
     def submit(self, seq, n, max_tokens, stream=None, cached=False):
@@ -318,6 +325,64 @@ def test_cached_prompts_longer_than_the_window_over_split_pools(lib):
             off.close()
     finally:
         r.close()
+
+
+def test_sharded_drafting_matches_one_rank(lib):
+    """Sequence-sharded drafting (tensor parallelism: every rank runs the scheduler
+    over the whole batch, drafts and verifies only its slice, all-gathers drafts and
+    results): ranks emulated as threads of one process with a rendezvous all-gather.
+    Every rank's tokens equal a single-rank run's; each rank's draft pool only needs
+    room for its slice; slices move when sequences finish at different times."""
+    import threading
+
+    reqs = [(i, 20 + 9 * i, 12 + 7 * (i % 4)) for i in range(7)]  # (seq, prompt length, max_tokens)
+    ref = Rig(lib, blocks=256)
+    try:
+        for sid, n, mt in reqs:
+            ref.submit(sid, n, max_tokens=mt)
+        assert ref.run()[1] == 0
+        want = [ref.generated(sid) for sid, _, _ in reqs]
+    finally:
+        ref.close()
+    for world, dblocks in ((2, 24), (3, 16)):
+        # a draft pool with room for about one slice of the batch: too small for all of it
+        small = Rig(lib, blocks=256, dblocks=dblocks)
+        try:
+            for sid, n, mt in reqs:
+                small.submit(sid, n, max_tokens=mt)
+            assert small.run()[1] == 2  # YK_ERR_OOM without sharding
+        finally:
+            small.close()
+        lib.stub_reset()
+        g = lib.stub_group(world)
+        engines = [lib.stub_engine(g, r) for r in range(world)]
+        rigs = [Rig(lib, blocks=256, shard=(engines[r], r, world), dblocks=dblocks) for r in range(world)]
+        status = [None] * world
+        try:
+            for rig in rigs:
+                for sid, n, mt in reqs:
+                    rig.submit(sid, n, max_tokens=mt)
+
+            def run(r):
+                status[r] = rigs[r].run()[1]
+
+            th = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+            for t in th:
+                t.start()
+            for t in th:
+                t.join(timeout=60)
+            assert not any(t.is_alive() for t in th)
+            assert status == [0] * world
+            for rig in rigs:
+                assert [rig.generated(sid) for sid, _, _ in reqs] == want
+            viol, fwd, _ = rigs[0].stats()
+            assert viol == 0 and fwd > 0
+        finally:
+            for rig in rigs:
+                rig.close()
+            for e in engines:
+                lib.stub_engine_free(e)
+            lib.stub_group_free(g)
 
 
 from hypothesis import HealthCheck, given, settings  # noqa: E402

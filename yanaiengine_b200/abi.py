@@ -114,6 +114,10 @@ _PROTOS = {
     "yk_spec_sample_logits": (C.c_int32, [_P, C.c_int32, _F32P, _F32P, C.c_float, C.c_uint64, C.c_uint32, _U32P,
                                           _U32P, _U32P, _I32P]),
     "yk_sampler_read_probs": (C.c_int32, [_P, C.c_int32, C.c_int32, _F32P]),
+    "yk_sampler_read_drafts": (C.c_int32, [_P, C.c_int32, _U32P]),
+    "yk_spec_verify_range": (C.c_int32, [_P, _P, C.c_int32, C.c_int32, C.c_float, C.c_uint64, C.c_uint32, _U32P, _U32P,
+                                         _U32P, _I32P]),
+    "yk_tp_allgather_u32": (C.c_int32, [_P, _U32P, C.c_int32, _U32P]),
     "yk_spec_verify_logits_noalloc": (C.c_int32, [C.c_int32, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32,
                                                   C.c_float, C.c_uint64, C.c_uint32, _P, _P]),
     # include/yk_testing.h
@@ -154,6 +158,7 @@ _HOST_PROTOS = {
     "ykh_counters": (C.c_int32, [_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "ykh_usage": (C.c_float, [_P, C.c_int32]),
     "ykh_set_window_reclaim": (C.c_int32, [_P, C.c_int32]),
+    "ykh_set_draft_shard": (C.c_int32, [_P, _P, C.c_int32, C.c_int32]),
 }
 
 _lib = None
@@ -621,6 +626,10 @@ class Scheduler:
 
     def set_window_reclaim(self, on: bool):
         check(host_lib().ykh_set_window_reclaim(self.h, 1 if on else 0))
+
+    def set_draft_shard(self, engine: "Engine", rank: int, world: int):
+        """Sequence-sharded drafting across a tensor-parallel group (ykh_set_draft_shard)."""
+        check(host_lib().ykh_set_draft_shard(self.h, engine.h, rank, world))
 
     def submit_stream(self, prompt, max_tokens: int, on_tokens=None, on_done=None, stop_token: int = -1,
                       seq_id: int = 0):

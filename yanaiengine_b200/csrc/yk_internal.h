@@ -91,6 +91,8 @@ struct yk_engine {
     int tp_rank = 0, tp_world = 1;
     bool tp_bf16 = true;                 // all-reduce payload bf16 (env YK_TP_PAYLOAD=f32: fp32)
     int64_t tp_timeout_ms = 300000;      // deadline of group set-up and of a wait on the group's work
+    uint32_t* tp_gather = nullptr;       // device staging of yk_tp_allgather_u32 (send, then recv)
+    size_t tp_gather_elems = 0;
     void* trace_rec = nullptr;           // launch trace records (test hook), else null
     uint32_t trace_cap = 0;
     std::vector<ProfRecord> prof_pending;

@@ -653,6 +653,46 @@ extern "C" yk_status yk_spec_verify(yk_sampler* s, yk_model* target, int32_t B, 
     return finish_verify(s, B, L, out_tokens, out_counts);
 }
 
+extern "C" yk_status yk_spec_verify_range(yk_sampler* s, yk_model* target, int32_t seq0, int32_t B, float temperature,
+                                          uint64_t seed, uint32_t step, const uint32_t* seq_ids,
+                                          const uint32_t* draft_tokens, uint32_t* out_tokens, int32_t* out_counts) {
+    YK_ARG(s && target && seq_ids && out_tokens && out_counts, "null argument");
+    YK_ARG(B > 0 && B <= s->max_seqs && seq0 >= 0, "B / seq0");
+    YK_ARG(target->cfg.vocab_size == s->vocab, "vocab mismatch");
+    YK_ARG(target->last_rows >= (seq0 + B) * (s->k + 1),
+           "target logits must hold k+1 rows for each of sequences seq0 .. seq0+B-1 (last_n = k+1)");
+    if (draft_tokens)
+        for (int i = 0; i < B * s->k; ++i) YK_ARG(draft_tokens[i] < (uint32_t)s->vocab, "draft token >= vocab");
+    yk_engine* e = s->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    IoLayout L = io_layout(s, B);
+    YK_TRY(upload_small(s, B, seq_ids, draft_tokens, L));
+    const float* rows = target->logits + (size_t)seq0 * (s->k + 1) * s->vocab;
+    YK_TRY(run_verify(s, B, rows, 1, temperature, seed, step, L));
+    return finish_verify(s, B, L, out_tokens, out_counts);
+}
+
+extern "C" yk_status yk_sampler_read_drafts(yk_sampler* s, int32_t B, uint32_t* out) {
+    YK_ARG(s && out, "null argument");
+    YK_ARG(B > 0 && B <= s->max_seqs, "B");
+    yk_engine* e = s->e;
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    IoLayout L = io_layout(s, B);
+    const size_t n = (size_t)B * s->k;
+    YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned, L.drafts, n * 4, cudaMemcpyDeviceToHost, e->stream));
+    YK_CHECK_CUDA(cudaMemcpyAsync(e->pinned + n * 4, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
+    YK_TRY(engine_sync_bounded(e));
+    uint32_t err;
+    std::memcpy(&err, e->pinned + n * 4, 4);
+    if (err) {
+        cudaMemset(e->d_err, 0, 4);
+        yk_set_error("device check fired during the draft phase (code " + std::to_string(err) + ")");
+        return (err & YK_DEV_ERR_TIMEOUT) ? YK_ERR_TIMEOUT : YK_ERR_DEVICE_CHECK;
+    }
+    std::memcpy(out, e->pinned, n * 4);
+    return YK_OK;
+}
+
 extern "C" yk_status yk_spec_verify_probs(yk_sampler* s, int32_t B, const float* p, const float* q,
                                           const uint32_t* draft_tokens, uint64_t seed, uint32_t step,
                                           const uint32_t* seq_ids, uint32_t* out_tokens, int32_t* out_counts) {

@@ -26,6 +26,7 @@ struct NcclApi {
     ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
     ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                                cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
     ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
@@ -45,11 +46,13 @@ const NcclApi& nccl() {
         api.comm_init_rank_config =
             reinterpret_cast<decltype(api.comm_init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
         api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
         api.get_async_error = reinterpret_cast<decltype(api.get_async_error)>(dlsym(h, "ncclCommGetAsyncError"));
         api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(h, "ncclCommAbort"));
         api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
         api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-        api.ok = api.get_unique_id && api.comm_init_rank_config && api.all_reduce && api.get_async_error &&
+        api.ok = api.get_unique_id && api.comm_init_rank_config && api.all_reduce && api.all_gather &&
+                 api.get_async_error &&
                  api.comm_abort && api.comm_destroy && api.error_string;
     });
     return api;
@@ -194,9 +197,49 @@ yk_status engine_sync_bounded(yk_engine* e) {
     }
 }
 
+}  // namespace yk
+
+extern "C" yk_status yk_tp_allgather_u32(yk_engine* e, const uint32_t* send, int32_t count, uint32_t* recv) {
+    YK_ARG(e && send && recv && count > 0, "arguments");
+    YK_ARG(e->nccl_comm, "engine has not joined a tensor-parallel group");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    const size_t need = (size_t)count * (1 + e->tp_world);
+    if (need > e->tp_gather_elems) {
+        YK_TRY(yk::engine_sync_bounded(e));
+        if (e->tp_gather) cudaFree(e->tp_gather);
+        e->tp_gather = nullptr;
+        e->tp_gather_elems = 0;
+        YK_CHECK_CUDA(cudaMalloc(&e->tp_gather, need * 4));
+        e->tp_gather_elems = need;
+    }
+    uint32_t* dsend = e->tp_gather;
+    uint32_t* drecv = e->tp_gather + count;
+    YK_CHECK_CUDA(cudaMemcpyAsync(dsend, send, (size_t)count * 4, cudaMemcpyHostToDevice, e->stream));
+    ncclComm_t comm = static_cast<ncclComm_t>(e->nccl_comm);
+    ncclResult_t r = nccl().all_gather(dsend, drecv, (size_t)count, ncclUint32, comm, e->stream);
+    if (r == ncclInProgress) {
+        bool timed_out = false;
+        r = poll_comm(comm, Clock::now() + std::chrono::milliseconds(e->tp_timeout_ms), &timed_out);
+        if (timed_out) {
+            nccl().comm_abort(comm);
+            e->nccl_comm = nullptr;
+            yk_set_error("ncclAllGather could not be enqueued in time (communicator aborted)");
+            return YK_ERR_TIMEOUT;
+        }
+    }
+    if (r != ncclSuccess) return nccl_fail("ncclAllGather", r);
+    YK_CHECK_CUDA(cudaMemcpyAsync(recv, drecv, (size_t)count * e->tp_world * 4, cudaMemcpyDeviceToHost, e->stream));
+    return yk::engine_sync_bounded(e);
+}
+
+namespace yk {
+
 void tp_destroy(yk_engine* e) {
     if (e->nccl_comm && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(e->nccl_comm));
     e->nccl_comm = nullptr;
+    if (e->tp_gather) cudaFree(e->tp_gather);
+    e->tp_gather = nullptr;
+    e->tp_gather_elems = 0;
 }
 
 }  // namespace yk

@@ -158,6 +158,11 @@ struct ykh_scheduler {
     // windowed (0: some layer is global, nothing can be freed)
     int t_window = 0, d_window = 0;
     bool reclaim = true;
+    // sequence-sharded drafting (ykh_set_draft_shard): this rank drafts and
+    // verifies running sequences [B*shard_rank/shard_world, B*(shard_rank+1)/shard_world)
+    yk_engine* shard_engine = nullptr;
+    int shard_rank = 0, shard_world = 1;
+    std::vector<uint32_t> gather_send, gather_recv;
     // per-step scratch
     std::vector<uint32_t> tokens, qstarts, ctx, seq_ids, drafts, out_tokens;
     std::vector<int32_t> tables, wtables, counts;
@@ -272,13 +277,15 @@ extern "C" yk_status ykh_submit_cached(ykh_scheduler* s, const uint32_t* prompt,
     return submit(s, prompt, n, max_tokens, stop_token, seq_id, true);
 }
 
-// Builds the ragged batch for one forward: for each sequence the token list
-// `inputs[b]`, starting at cache position `start[b]`; reserves pages.
-// nd > 0: the last nd inputs of every sequence are placeholders for the draft
-// tokens j0.. that the sampler keeps on the device (no host round trip).
+// Builds the ragged batch for one forward over the running sequences `idx`
+// (all of them when empty): for each the token list `inputs[i]`, starting at
+// cache position `start`; reserves pages.  nd > 0: the last nd inputs of every
+// sequence are placeholders for the draft tokens j0.. that the sampler keeps on
+// the device (no host round trip).
 static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std::vector<uint32_t>>& inputs,
-                         int last_n, int j0 = 0, int nd = 0) {
-    const int B = (int)s->running.size();
+                         int last_n, int j0 = 0, int nd = 0, const std::vector<int>& idx = {}) {
+    const int B = idx.empty() ? (int)s->running.size() : (int)idx.size();
+    auto req = [&](int b) { return s->running[idx.empty() ? b : idx[b]].get(); };
     s->tokens.clear();
     s->qstarts.assign(1, 0);
     s->ctx.clear();
@@ -286,11 +293,11 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
     const bool split = s->twpool != nullptr;
     size_t wmax_pages = 1;
     for (int b = 0; b < B; ++b) {
-        PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
+        PagedKVCache* c = is_draft ? req(b)->draft_cache.get() : req(b)->cache.get();
         const int n = (int)inputs[b].size();
         if (!c->reserve(c->current_position + n)) return YK_ERR_OOM;  // S/PagedKVCache.swift:31-33
         if (split) {
-            PagedKVCache* wc = is_draft ? s->running[b]->draft_wcache.get() : s->running[b]->wcache.get();
+            PagedKVCache* wc = is_draft ? req(b)->draft_wcache.get() : req(b)->wcache.get();
             if (!wc->reserve(wc->current_position + n)) return YK_ERR_OOM;
             wmax_pages = std::max(wmax_pages, wc->page_table.size());
         }
@@ -301,7 +308,7 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
     }
     s->tables.assign((size_t)B * max_pages, 0);
     for (int b = 0; b < B; ++b) {
-        PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
+        PagedKVCache* c = is_draft ? req(b)->draft_cache.get() : req(b)->cache.get();
         int32_t* row = s->tables.data() + (size_t)b * max_pages;
         for (size_t i = 0; i < c->page_table.size(); ++i) row[i] = c->page_table[i] >= 0 ? c->page_table[i] : 0;
     }
@@ -311,7 +318,7 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
     if (split) {
         s->wtables.assign((size_t)B * wmax_pages, 0);
         for (int b = 0; b < B; ++b) {
-            PagedKVCache* wc = is_draft ? s->running[b]->draft_wcache.get() : s->running[b]->wcache.get();
+            PagedKVCache* wc = is_draft ? req(b)->draft_wcache.get() : req(b)->wcache.get();
             int32_t* row = s->wtables.data() + (size_t)b * wmax_pages;
             for (size_t i = 0; i < wc->page_table.size(); ++i) row[i] = wc->page_table[i] >= 0 ? wc->page_table[i] : 0;
         }
@@ -320,7 +327,7 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
                                      (int32_t)max_pages, s->wtables.data(), (int32_t)wmax_pages, last_n,
                                      nd > 0 ? s->sampler : nullptr, j0, nd, &rows));
         for (int b = 0; b < B; ++b) {
-            SequenceRequest* r = s->running[b].get();
+            SequenceRequest* r = req(b);
             (is_draft ? r->draft_cache : r->cache)->current_position += (int)inputs[b].size();
             (is_draft ? r->draft_wcache : r->wcache)->current_position += (int)inputs[b].size();
         }
@@ -333,7 +340,7 @@ static yk_status forward(ykh_scheduler* s, bool is_draft, const std::vector<std:
                                             s->ctx.data(), B, s->tables.data(), (int32_t)max_pages, last_n, &rows);
     if (st != YK_OK) return st;
     for (int b = 0; b < B; ++b) {
-        PagedKVCache* c = is_draft ? s->running[b]->draft_cache.get() : s->running[b]->cache.get();
+        PagedKVCache* c = is_draft ? req(b)->draft_cache.get() : req(b)->cache.get();
         c->current_position += (int)inputs[b].size();
     }
     return YK_OK;
@@ -348,9 +355,11 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
     YK_TRY(yk_model_get_config(s->target, &tc));
     YK_TRY(yk_model_get_config(s->draft, &dc));
     const int max_batch = std::min(tc.max_seqs, dc.max_seqs);
-    while (!s->waiting.empty() && s->talloc->usage() < 0.9f && s->dalloc->usage() < 0.9f &&
-           (!s->twalloc || (s->twalloc->usage() < 0.9f && s->dwalloc->usage() < 0.9f)) &&
-           (int)s->running.size() < max_batch) {
+    // (sharded drafting: the draft pools hold different slices on different ranks,
+    // so admission looks at the target pools only, which every rank fills alike)
+    const bool dfull = s->shard_world == 1 && (s->dalloc->usage() >= 0.9f || (s->dwalloc && s->dwalloc->usage() >= 0.9f));
+    while (!s->waiting.empty() && s->talloc->usage() < 0.9f && !dfull &&
+           (!s->twalloc || s->twalloc->usage() < 0.9f) && (int)s->running.size() < max_batch) {
         s->running.push_back(std::move(s->waiting.front()));
         s->waiting.pop_front();
     }
@@ -363,53 +372,121 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
         s->seq_ids[b] = s->running[b]->id;
         N[b] = s->running[b]->total();
     }
+    const bool sharded = s->shard_world > 1;
+    // this rank's slice of the batch (all of it unless drafting is sharded)
+    const int lo = sharded ? (int)((int64_t)B * s->shard_rank / s->shard_world) : 0;
+    const int hi = sharded ? (int)((int64_t)B * (s->shard_rank + 1) / s->shard_world) : B;
+    const int Bs = hi - lo;
+    std::vector<int> own;
+    if (sharded) {
+        for (int b = lo; b < hi; ++b) own.push_back(b);
+        // a sequence outside this rank's slice keeps no draft pages here (slices
+        // move when sequences finish; a sequence that moves in is re-fed to the draft)
+        for (int b = 0; b < B; ++b)
+            if (b < lo || b >= hi) {
+                s->running[b]->draft_cache->reset();
+                if (s->running[b]->draft_wcache) s->running[b]->draft_wcache->reset();
+            }
+    }
+    std::vector<uint32_t> own_ids(s->seq_ids.begin() + lo, s->seq_ids.begin() + hi);
     // 1. DRAFT PHASE (:171-190): k draft forwards, sampling after each.  The drafted
     // tokens stay on the device (the sampler keeps them; the next draft forward and
     // the target forward read them there), so the whole phase is queued without
     // waiting for the device.
-    std::vector<std::vector<uint32_t>> inputs(B);
-    for (int j = 0; j < k; ++j) {
-        for (int b = 0; b < B; ++b) {
-            SequenceRequest* r = s->running[b].get();
-            inputs[b].clear();
+    std::vector<std::vector<uint32_t>> inputs(Bs);
+    for (int j = 0; j < k && Bs > 0; ++j) {
+        for (int i = 0; i < Bs; ++i) {
+            SequenceRequest* r = s->running[lo + i].get();
+            inputs[i].clear();
             if (j == 0) {
                 // every token the draft cache has not seen (the prompt on the first step)
-                for (int i = r->draft_cache->current_position; i < N[b]; ++i) inputs[b].push_back(r->at(i));
+                for (int t = r->draft_cache->current_position; t < N[lo + i]; ++t) inputs[i].push_back(r->at(t));
             } else {
-                inputs[b].push_back(0u);  // draft j-1 of this sequence, on the device
+                inputs[i].push_back(0u);  // draft j-1 of this sequence, on the device
             }
         }
-        if (j == 0) YK_TRY(forward(s, true, inputs, 1));
-        else YK_TRY(forward(s, true, inputs, 1, j - 1, 1));
-        YK_TRY(yk_draft_sample(s->sampler, s->draft, B, j, s->temperature, s->seed, s->step_no, s->seq_ids.data(),
+        if (j == 0) YK_TRY(forward(s, true, inputs, 1, 0, 0, own));
+        else YK_TRY(forward(s, true, inputs, 1, j - 1, 1, own));
+        YK_TRY(yk_draft_sample(s->sampler, s->draft, Bs, j, s->temperature, s->seed, s->step_no, own_ids.data(),
                                nullptr));
     }
+    // Sharded: every rank's drafts, for the target forward over the whole batch.
+    std::vector<uint32_t> all_drafts;
+    const int Bm = sharded ? (B + s->shard_world - 1) / s->shard_world : 0;  // largest slice
+    auto owner_of = [&](int b) {  // rank whose slice holds running sequence b, and b's row there
+        int q = (int)(((int64_t)b * s->shard_world) / B);
+        while ((int64_t)B * (q + 1) / s->shard_world <= b) ++q;
+        while ((int64_t)B * q / s->shard_world > b) --q;
+        return q;
+    };
+    if (sharded) {
+        s->gather_send.assign((size_t)Bm * k, 0u);
+        if (Bs > 0) YK_TRY(yk_sampler_read_drafts(s->sampler, Bs, s->gather_send.data()));
+        s->gather_recv.assign((size_t)Bm * k * s->shard_world, 0u);
+        YK_TRY(yk_tp_allgather_u32(s->shard_engine, s->gather_send.data(), Bm * k, s->gather_recv.data()));
+        all_drafts.resize((size_t)B * k);
+        for (int b = 0; b < B; ++b) {
+            const int q = owner_of(b);
+            const int row = b - (int)((int64_t)B * q / s->shard_world);
+            for (int j = 0; j < k; ++j)
+                all_drafts[(size_t)b * k + j] = s->gather_recv[((size_t)q * Bm + row) * k + j];
+        }
+    }
     // 2-3. VERIFICATION SETUP + TARGET FORWARD (:192-210): unseen tokens + drafts.
+    std::vector<std::vector<uint32_t>> tinputs(B);
     for (int b = 0; b < B; ++b) {
         SequenceRequest* r = s->running[b].get();
-        inputs[b].clear();
-        for (int i = r->cache->current_position; i < N[b]; ++i) inputs[b].push_back(r->at(i));
-        for (int j = 0; j < k; ++j) inputs[b].push_back(0u);  // the k drafts, on the device
+        for (int i = r->cache->current_position; i < N[b]; ++i) tinputs[b].push_back(r->at(i));
+        for (int j = 0; j < k; ++j)  // the k drafts: on the device, or (sharded) gathered on the host
+            tinputs[b].push_back(sharded ? all_drafts[(size_t)b * k + j] : 0u);
     }
-    YK_TRY(forward(s, false, inputs, k + 1, 0, k));
+    if (sharded) YK_TRY(forward(s, false, tinputs, k + 1));
+    else YK_TRY(forward(s, false, tinputs, k + 1, 0, k));
     // 4. VERIFICATION & ROLLBACK (:212-267).
     s->out_tokens.assign((size_t)B * (k + 1), 0);
     s->counts.assign(B, 0);
-    YK_TRY(yk_spec_verify(s->sampler, s->target, B, s->temperature, s->seed, s->step_no, s->seq_ids.data(),
-                          nullptr, s->out_tokens.data(), s->counts.data()));
+    if (!sharded) {
+        YK_TRY(yk_spec_verify(s->sampler, s->target, B, s->temperature, s->seed, s->step_no, s->seq_ids.data(),
+                              nullptr, s->out_tokens.data(), s->counts.data()));
+    } else {
+        // verify this rank's slice, then every rank's results to every rank
+        const int W = k + 2;  // per sequence: k+1 tokens, then the count
+        s->gather_send.assign((size_t)Bm * W, 0u);
+        if (Bs > 0) {
+            std::vector<uint32_t> out((size_t)Bs * (k + 1));
+            std::vector<int32_t> cnt(Bs);
+            YK_TRY(yk_spec_verify_range(s->sampler, s->target, lo, Bs, s->temperature, s->seed, s->step_no,
+                                        own_ids.data(), all_drafts.data() + (size_t)lo * k, out.data(), cnt.data()));
+            for (int i = 0; i < Bs; ++i) {
+                std::memcpy(&s->gather_send[(size_t)i * W], &out[(size_t)i * (k + 1)], (size_t)(k + 1) * 4);
+                s->gather_send[(size_t)i * W + k + 1] = (uint32_t)cnt[i];
+            }
+        }
+        s->gather_recv.assign((size_t)Bm * W * s->shard_world, 0u);
+        YK_TRY(yk_tp_allgather_u32(s->shard_engine, s->gather_send.data(), Bm * W, s->gather_recv.data()));
+        for (int b = 0; b < B; ++b) {
+            const int q = owner_of(b);
+            const int row = b - (int)((int64_t)B * q / s->shard_world);
+            const uint32_t* src = &s->gather_recv[((size_t)q * Bm + row) * W];
+            std::memcpy(&s->out_tokens[(size_t)b * (k + 1)], src, (size_t)(k + 1) * 4);
+            s->counts[b] = (int32_t)src[k + 1];
+            if (s->counts[b] < 1 || s->counts[b] > k + 1) return YK_ERR_DEVICE_CHECK;
+        }
+    }
     int emitted = 0;
     for (int b = 0; b < B; ++b) {
         SequenceRequest* r = s->running[b].get();
         const int cnt = s->counts[b];
         const int a = cnt - 1;  // accepted drafts
+        const bool drafted_here = b >= lo && b < hi;  // (its draft cache lives on this rank)
         r->cache->rollback(N[b] + a);
-        r->draft_cache->rollback(std::min(r->draft_cache->current_position, N[b] + a));
+        if (drafted_here) r->draft_cache->rollback(std::min(r->draft_cache->current_position, N[b] + a));
         if (r->wcache) {
             r->wcache->rollback(N[b] + a);
-            r->draft_wcache->rollback(std::min(r->draft_wcache->current_position, N[b] + a));
+            if (drafted_here) r->draft_wcache->rollback(std::min(r->draft_wcache->current_position, N[b] + a));
             if (s->reclaim) {  // every layer of these pools is windowed
                 r->wcache->reclaim_window(s->tw_width);
-                r->draft_wcache->reclaim_window(s->dw_width);
+                if (drafted_here) r->draft_wcache->reclaim_window(s->dw_width);
             }
         }
         for (int i = 0; i < cnt; ++i) r->generated.push_back(s->out_tokens[(size_t)b * (k + 1) + i]);
@@ -420,7 +497,7 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
             }
         if ((int)r->generated.size() >= r->max_tokens) r->finished = true;
         if (s->reclaim && s->t_window > 0) r->cache->reclaim_window(s->t_window);
-        if (s->reclaim && s->d_window > 0) r->draft_cache->reclaim_window(s->d_window);
+        if (s->reclaim && s->d_window > 0 && drafted_here) r->draft_cache->reclaim_window(s->d_window);
         if (r->on_tokens && cnt > 0) r->on_tokens(r->user, r->id, r->generated.data() + r->generated.size() - cnt, cnt);
         emitted += cnt;
         s->n_accepted += a;
@@ -445,6 +522,14 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
         }
     }
     if (emitted_out) *emitted_out = emitted;
+    return YK_OK;
+}
+
+extern "C" yk_status ykh_set_draft_shard(ykh_scheduler* s, yk_engine* e, int32_t rank, int32_t world) {
+    if (!s || world < 1 || rank < 0 || rank >= world || (world > 1 && !e)) return YK_ERR_ARG;
+    s->shard_engine = world > 1 ? e : nullptr;
+    s->shard_rank = world > 1 ? rank : 0;
+    s->shard_world = world;
     return YK_OK;
 }
 
