@@ -336,10 +336,17 @@ def test_sharded_drafting_matches_one_rank(lib):
     import threading
 
     reqs = [(i, 20 + 9 * i, 12 + 7 * (i % 4)) for i in range(7)]  # (seq, prompt length, max_tokens)
+    for cached in (False, True):
+        _sharded_case(lib, reqs, cached)
+
+
+def _sharded_case(lib, reqs, cached):
+    import threading
+
     ref = Rig(lib, blocks=256)
     try:
         for sid, n, mt in reqs:
-            ref.submit(sid, n, max_tokens=mt)
+            assert ref.submit(sid, n, max_tokens=mt, cached=cached) in (None, 0)
         assert ref.run()[1] == 0
         want = [ref.generated(sid) for sid, _, _ in reqs]
     finally:
@@ -348,9 +355,8 @@ def test_sharded_drafting_matches_one_rank(lib):
         # a draft pool with room for about one slice of the batch: too small for all of it
         small = Rig(lib, blocks=256, dblocks=dblocks)
         try:
-            for sid, n, mt in reqs:
-                small.submit(sid, n, max_tokens=mt)
-            assert small.run()[1] == 2  # YK_ERR_OOM without sharding
+            st = [small.submit(sid, n, max_tokens=mt, cached=cached) for sid, n, mt in reqs]
+            assert 2 in st or small.run()[1] == 2  # YK_ERR_OOM without sharding
         finally:
             small.close()
         lib.stub_reset()
@@ -361,7 +367,7 @@ def test_sharded_drafting_matches_one_rank(lib):
         try:
             for rig in rigs:
                 for sid, n, mt in reqs:
-                    rig.submit(sid, n, max_tokens=mt)
+                    assert rig.submit(sid, n, max_tokens=mt, cached=cached) in (None, 0)
 
             def run(r):
                 status[r] = rigs[r].run()[1]

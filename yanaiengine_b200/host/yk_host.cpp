@@ -124,6 +124,9 @@ struct SequenceRequest {
     std::unique_ptr<PagedKVCache> wcache, draft_wcache;
     int max_tokens = 0;
     int64_t stop_token = -1;
+    // a cached prompt under sharded drafting: the draft cache of whichever rank
+    // drafts this sequence first takes these tokens as held (its pages reserved then)
+    int draft_cached = 0;
     bool finished = false;
     // streaming (the server's onTokenGenerated / onCompletion), optional
     ykh_on_tokens on_tokens = nullptr;
@@ -243,7 +246,19 @@ static yk_status submit(ykh_scheduler* s, const uint32_t* prompt, int32_t n, int
         r->wcache = std::make_unique<PagedKVCache>(s->twalloc.get());
         r->draft_wcache = std::make_unique<PagedKVCache>(s->dwalloc.get());
     }
-    if (cached) {
+    if (cached && s->shard_world > 1) {
+        // sharded drafting: the draft side is reserved by the rank whose slice the
+        // sequence lands in, at its first step (the draft pools hold one slice each)
+        if (!r->cache->reserve(n - 1)) return YK_ERR_OOM;
+        r->cache->current_position = n - 1;
+        r->draft_cached = n - 1;
+        if (r->wcache) {
+            if (!(s->reclaim ? r->wcache->reserve_cached_window(n - 1, s->tw_width) : r->wcache->reserve(n - 1)))
+                return YK_ERR_OOM;
+            r->wcache->current_position = n - 1;
+        }
+        s->running.push_back(std::move(r));
+    } else if (cached) {
         if (!r->cache->reserve(n - 1) || !r->draft_cache->reserve(n - 1)) return YK_ERR_OOM;
         r->cache->current_position = n - 1;
         r->draft_cache->current_position = n - 1;
@@ -389,6 +404,22 @@ extern "C" yk_status ykh_step(ykh_scheduler* s, int32_t* emitted_out) {
             }
     }
     std::vector<uint32_t> own_ids(s->seq_ids.begin() + lo, s->seq_ids.begin() + hi);
+    if (sharded)
+        for (int b = lo; b < hi; ++b) {  // cached prompts reach this rank's draft cache at their first step
+            SequenceRequest* r = s->running[b].get();
+            if (r->draft_cached > 0 && r->generated.empty() && r->draft_cache->current_position == 0) {
+                const int n = r->draft_cached;
+                if (!r->draft_cache->reserve(n)) return YK_ERR_OOM;
+                r->draft_cache->current_position = n;
+                if (r->draft_wcache) {
+                    if (!(s->reclaim ? r->draft_wcache->reserve_cached_window(n, s->dw_width)
+                                     : r->draft_wcache->reserve(n)))
+                        return YK_ERR_OOM;
+                    r->draft_wcache->current_position = n;
+                }
+            }
+            r->draft_cached = 0;
+        }
     // 1. DRAFT PHASE (:171-190): k draft forwards, sampling after each.  The drafted
     // tokens stay on the device (the sampler keeps them; the next draft forward and
     // the target forward read them there), so the whole phase is queued without
