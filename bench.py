@@ -1,6 +1,6 @@
 """Benchmark: accepted tokens/s of the speculative draft->verify step.
 
-Workload (the benchmark spec's 8B/1B configuration): Llama-3-8B-shape target
+Workload (the 8B/1B speculative configuration): Llama-3-8B-shape target
 (32 layers, d 4096, 32/8 heads x 128, FFN 14336) with a Llama-3.2-1B-shape
 draft (16 layers, d 2048, 32/8 x 64, FFN 8192), bf16 weights N(0, 0.02), fp32
 accumulation, RoPE theta 5e5, vocab 128256, k = 5, temperature 0.8, 16-token
@@ -17,6 +17,13 @@ is bracketed by barriers and the max over ranks is reported.
 
 --impl reference: the reference's CPU implementation of the same step (the
 oracle restatement, all host threads), one bounded sample per step.
+
+Other workloads (--workload): sampler (the rejection-sampling phase alone, 64
+sequences, k=4, V=128256), gemma (Gemma-2-9B/2B shape, 64 sequences, split KV
+pools), 70b-tp (70B-shape target tensor-parallel over all ranks, drafting
+sharded by sequence), prefill (the first scheduler step of a fresh batch).
+Under more than one GPU the 8b-dp run also times a global batch of 32 split
+over the ranks (the line's `strong` object).
 """
 from __future__ import annotations
 
