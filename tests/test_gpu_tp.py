@@ -6,6 +6,9 @@ the full model: max |dlogit| <= 2e-2 * max |logit|, as for the 1-GPU forward,
 with the all-reduce payload in bf16 (the default) and in fp32.  Needs two GPUs
 (skipped otherwise).
 
+The all-reduce is the group's own two-shot kernel over NVLink peer memory by
+default (bf16 payload) and NCCL's otherwise; both are checked against the oracle.
+
 Failure handling (no GPU is faulted): a group whose second rank never joins
 ends set-up with YK_ERR_TIMEOUT on one GPU; on two GPUs, a rank that leaves
 between steps makes the other rank's next step end with YK_ERR_TIMEOUT (its
@@ -80,9 +83,10 @@ def _load_full(m, w):
         m.load(abi.T_NORM2, l, w["n2"][l], abi.DTYPE_F32)
 
 
-def _worker(rank, uid, q, via_loader=False, payload="bf16"):
+def _worker(rank, uid, q, via_loader=False, payload="bf16", ar="own"):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["YK_TP_PAYLOAD"] = payload
+    os.environ["YK_TP_AR"] = ar
     try:
         e = abi.Engine(rank)
         e.tp_init(uid, rank, WORLD)
@@ -128,8 +132,11 @@ def _worker(rank, uid, q, via_loader=False, payload="bf16"):
         q.put((rank, None, None, repr(ex)))
 
 
-@pytest.mark.parametrize("via_loader,payload", [(False, "bf16"), (True, "bf16"), (False, "f32")])
-def test_tp2_forward_matches_oracle(oracle, via_loader, payload):
+@pytest.mark.parametrize("via_loader,payload,ar", [(False, "bf16", "own"), (True, "bf16", "own"),
+                                                    (False, "bf16", "nccl"), (False, "f32", "nccl")])
+def test_tp2_forward_matches_oracle(oracle, via_loader, payload, ar):
+    """ar: the all-reduce after o_proj / down_proj, the group's own kernel over NVLink
+    peer memory (bf16, the default) or NCCL's."""
     import torch
 
     if torch.cuda.device_count() < WORLD:
@@ -139,7 +146,7 @@ def test_tp2_forward_matches_oracle(oracle, via_loader, payload):
     uid = abi.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, uid, q, via_loader, payload)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, uid, q, via_loader, payload, ar)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = {}
@@ -165,7 +172,7 @@ def test_tp2_forward_matches_oracle(oracle, via_loader, payload):
         g0, g1 = res[0][0][i], res[1][0][i]
         np.testing.assert_array_equal(g0, g1)  # both ranks hold the same all-reduced stream
         err = np.abs(g0 - o).max() / np.abs(o).max()
-        print(f"payload {payload} step {i}: max |dlogit| / max |logit| = {err:.3e}")
+        print(f"payload {payload} ({ar} all-reduce) step {i}: max |dlogit| / max |logit| = {err:.3e}")
         assert err < 2e-2, f"step {i}: rel err {err:.3e}"
 
 
@@ -205,8 +212,11 @@ def test_tp_init_times_out_when_a_rank_never_joins():
 
 def _leaver(rank, uid, q):
     """Both ranks run one forward step; rank 1 then leaves (between steps, nothing
-    in flight) and rank 0 runs a second step whose all-reduce cannot finish."""
+    in flight) and rank 0 runs a second step whose all-reduce cannot finish.  NCCL's
+    all-reduce: the group's own kernel reads and writes the peers' memory, which a
+    rank that exits releases."""
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["YK_TP_AR"] = "nccl"
     try:
         e = abi.Engine(rank)
         e.tp_init(uid, rank, WORLD, timeout_ms=8000)

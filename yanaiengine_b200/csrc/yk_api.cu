@@ -105,6 +105,7 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
     if (const char* v = std::getenv("YK_TP_PAYLOAD")) e->tp_bf16 = std::strcmp(v, "f32") != 0;
+    if (const char* v = std::getenv("YK_TP_AR")) e->tp_ar_own = std::strcmp(v, "nccl") != 0;
     yk_status s = e->ensure_pinned((size_t)4 << 20);
     if (s != YK_OK) { delete e; return s; }
     *out = e;
@@ -808,6 +809,15 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
     es.kind = EPI_STORE;
     es.out = m->tp_y;
     es.store_bf16 = e->tp_bf16 ? 1 : 0;
+    // the group's own all-reduce over NVLink peer memory (bf16 payload): the GEMM
+    // writes its partial into this rank's shared slot, the all-reduce kernel sums
+    // every rank's slot into tp_y
+    const bool own_ar = tp && e->tp_bf16 && tp_ar_enabled(e);
+    if (own_ar) YK_TRY(tp_ar_reserve(e, (size_t)T * d));
+    auto tp_reduce = [&]() -> yk_status {
+        if (own_ar) return tp_ar_run(e, (size_t)T * d, reinterpret_cast<__nv_bfloat16*>(m->tp_y));
+        return tp_allreduce(e, m->tp_y, (size_t)T * d, e->tp_bf16);
+    };
     // RMSNorm folded into the GEMMs (bf16, one GPU): the residual epilogue (and the
     // embedding) writes x = bf16(h * gain) and 32-row sums of squares; the next
     // GEMM scales each token's accumulator by its 1/rms.  The final norm stays a
@@ -864,8 +874,9 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         er.h = m->h;
         er.ld = d;
         if (tp) {
+            if (own_ar) es.out = tp_ar_slot(e);
             YK_TRY(gemm_run(m, L.wo, &L.tm_o, m->att, d, qd, T, es));
-            YK_TRY(tp_allreduce(e, m->tp_y, (size_t)T * d, e->tp_bf16));
+            YK_TRY(tp_reduce());
             pend = m->tp_y;
         } else {
             EpiParams eo = er;
@@ -890,8 +901,9 @@ static yk_status forward_impl(yk_model* m, yk_kv_pool* pool, const uint32_t* tok
         }
         YK_TRY(gemm_run(m, L.wgu, &L.tm_gu, m->xn, 2 * F, d, T, eg));
         if (tp) {
+            if (own_ar) es.out = tp_ar_slot(e);
             YK_TRY(gemm_run(m, L.wdown, &L.tm_down, m->act, d, F, T, es));
-            YK_TRY(tp_allreduce(e, m->tp_y, (size_t)T * d, e->tp_bf16));
+            YK_TRY(tp_reduce());
             pend = m->tp_y;
         } else {
             EpiParams ed = er;

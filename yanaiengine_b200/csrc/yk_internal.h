@@ -93,6 +93,16 @@ struct yk_engine {
     int64_t tp_timeout_ms = 300000;      // deadline of group set-up and of a wait on the group's work
     uint32_t* tp_gather = nullptr;       // device staging of yk_tp_allgather_u32 (send, then recv)
     size_t tp_gather_elems = 0;
+    // The group's own all-reduce over NVLink peer memory (env YK_TP_AR=nccl: NCCL's):
+    // each rank's buffer [flags 4 KB | 2 partial slots | 2 reduced slots] of ar_cap bytes
+    // per slot, shared with the other ranks through CUDA IPC.
+    bool tp_ar_own = true;
+    size_t ar_cap = 0;
+    uint8_t* ar_local = nullptr;
+    std::vector<void*> ar_opened;        // the peers' buffers as mapped here (null for this rank)
+    uint8_t** ar_bufs = nullptr;         // device array: every rank's buffer, as mapped here
+    uint32_t ar_epoch = 0;
+    unsigned long long ar_ctr_base = 0;  // value of this rank's CTA counter before the next all-reduce
     void* trace_rec = nullptr;           // launch trace records (test hook), else null
     uint32_t trace_cap = 0;
     std::vector<ProfRecord> prof_pending;
@@ -360,6 +370,13 @@ yk_status launch_rmsnorm(yk_model* m, const float* g, int rows, const int32_t* r
                          int add_bf16 = 0);
 // In-place sum over the tensor-parallel group of `count` fp32 (or bf16) values on the engine stream.
 yk_status tp_allreduce(yk_engine* e, void* buf, size_t count, bool bf16);
+// The group's own bf16 all-reduce: `count` values this rank wrote into tp_ar_slot
+// (the partial slot of the next call) are summed over the ranks, in rank order
+// (every rank gets the same values), into `out`.
+bool tp_ar_enabled(const yk_engine* e);
+yk_status tp_ar_reserve(yk_engine* e, size_t count);  // collective: every rank, same count
+__nv_bfloat16* tp_ar_slot(yk_engine* e);
+yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out);
 // Waits for the engine stream; with a tensor-parallel group, bounded by the
 // group's deadline (the communicator is aborted and YK_ERR_TIMEOUT returned when
 // it runs out: a peer that stopped taking part leaves its collectives unfinished).

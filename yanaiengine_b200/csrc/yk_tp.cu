@@ -234,7 +234,198 @@ extern "C" yk_status yk_tp_allgather_u32(yk_engine* e, const uint32_t* send, int
 
 namespace yk {
 
+// ---------------------------------------------------------------------------
+// The group's own all-reduce over NVLink peer memory (two-shot).  Every rank's
+// buffer (CUDA IPC, mapped by every other rank): a flag area, two partial slots
+// and two reduced slots (alternating by call, so a rank that runs ahead never
+// overwrites what a slower peer still reads).  Per call, on every rank:
+//   A. after the GEMM wrote its bf16 partial into this rank's partial slot, raise
+//      "partial ready" in every rank's flag area (system-scope release);
+//   B. once every rank's partial is ready: sum this rank's 1/w of the elements
+//      over all ranks' partials in rank order 0..w-1 (peer loads, fp32 sums,
+//      one bf16 rounding) into this rank's reduced slot; the last CTA to finish
+//      raises "reduced ready" everywhere;
+//   C. once every rank's share is reduced: copy every rank's reduced share
+//      (peer loads) into `out`.
+// Every rank thus holds the same bytes.  Each wait is bounded (the device error
+// word gets the timeout bit and the kernel returns).  Plain loads and stores
+// only: no TMA, no multicast.  All CTAs of the grid are resident together (one
+// per SM at most), so the CTAs waiting in B / C never block one still to run.
+// ---------------------------------------------------------------------------
+constexpr int AR_THREADS = 512;
+constexpr size_t AR_FLAGS = 4096;   // flag area: A flags [0, 64), C flags [64, 128), CTA counter at 256 (u64)
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Thread 0: waits until flags[q] == epoch for every rank q (this rank's flag area).
+__device__ __forceinline__ bool ar_wait_all(const uint32_t* flags, int w, uint32_t epoch, uint32_t* err) {
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < w; ++q) {
+        for (uint32_t it = 0;; ++it) {
+            if (ld_acquire_sys(flags + q) == epoch) break;
+            if ((it & 63u) == 63u && globaltimer_ns() - t0 > YK_WAIT_BUDGET_NS) {
+                raise_err(err, YK_DEV_ERR_TIMEOUT);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const* bufs, int rank, int w,
+                                                                 size_t count, size_t cap, uint32_t epoch,
+                                                                 unsigned long long ctr_target,
+                                                                 __nv_bfloat16* out, uint32_t* err) {
+    pdl_trigger();
+    pdl_wait();  // the partial (the previous kernel's output) is complete
+    __shared__ int s_ok;
+    const int slot = (int)(epoch & 1u);
+    uint8_t* mine = bufs[rank];
+    uint32_t* flags = reinterpret_cast<uint32_t*>(mine);
+    auto part = [&](int q) { return reinterpret_cast<const uint4*>(bufs[q] + AR_FLAGS + (size_t)slot * cap); };
+    auto red = [&](int q) { return reinterpret_cast<uint4*>(bufs[q] + AR_FLAGS + (size_t)(2 + slot) * cap); };
+    const size_t nv = count / 8;                 // 16-byte vectors (count is a multiple of 8)
+    const size_t share = (nv + w - 1) / w;       // vectors per rank's share
+    // A: this rank's partial is ready
+    if (blockIdx.x == 0 && threadIdx.x < w) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<uint32_t*>(bufs[threadIdx.x]) + rank, epoch);
+    }
+    if (threadIdx.x == 0) s_ok = ar_wait_all(flags, w, epoch, err) ? 1 : 0;
+    __syncthreads();
+    if (!s_ok) return;
+    // B: this rank's share, summed over the ranks in order
+    const size_t v0 = (size_t)rank * share, v1 = v0 + share < nv ? v0 + share : nv;
+    for (size_t v = v0 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1; v += (size_t)gridDim.x * blockDim.x) {
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int q = 0; q < w; ++q) {
+            const uint4 x = part(q)[v];
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc[2 * i] += __low2float(h[i]);
+                acc[2 * i + 1] += __high2float(h[i]);
+            }
+        }
+        uint4 y;
+        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&y);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        red(rank)[v] = y;
+    }
+    // the last CTA done with B raises "reduced ready" on every rank
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        unsigned long long* ctr = reinterpret_cast<unsigned long long*>(mine + 256);
+        if (atomicAdd(ctr, 1ULL) == ctr_target) {
+            __threadfence_system();
+            for (int q = 0; q < w; ++q) st_release_sys(reinterpret_cast<uint32_t*>(bufs[q]) + 64 + rank, epoch);
+        }
+        s_ok = ar_wait_all(flags + 64, w, epoch, err) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    // C: every rank's reduced share into out
+    uint4* o4 = reinterpret_cast<uint4*>(out);
+    for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (size_t)gridDim.x * blockDim.x)
+        o4[v] = red((int)(v / share))[v];
+}
+
+bool tp_ar_enabled(const yk_engine* e) { return e->nccl_comm && e->tp_world > 1 && e->tp_ar_own; }
+
+static void ar_release(yk_engine* e) {
+    for (void* p : e->ar_opened)
+        if (p) cudaIpcCloseMemHandle(p);
+    e->ar_opened.clear();
+    if (e->ar_bufs) cudaFree(e->ar_bufs);
+    if (e->ar_local) cudaFree(e->ar_local);
+    e->ar_bufs = nullptr;
+    e->ar_local = nullptr;
+    e->ar_cap = 0;
+}
+
+yk_status tp_ar_reserve(yk_engine* e, size_t count) {
+    const size_t need = ((count * 2 + 255) / 256) * 256;
+    if (need <= e->ar_cap) return YK_OK;
+    YK_TRY(engine_sync_bounded(e));
+    if (e->ar_local) {
+        // every rank is past its last use of the old buffers before any is released
+        uint32_t one = 1, all[64];
+        YK_TRY(yk_tp_allgather_u32(e, &one, 1, all));
+        ar_release(e);
+    }
+    const size_t bytes = AR_FLAGS + 4 * need;
+    YK_CHECK_CUDA(cudaMalloc(&e->ar_local, bytes));
+    YK_CHECK_CUDA(cudaMemset(e->ar_local, 0, bytes));
+    cudaIpcMemHandle_t h;
+    YK_CHECK_CUDA(cudaIpcGetMemHandle(&h, e->ar_local));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle is 64 bytes");
+    std::vector<uint32_t> all((size_t)16 * e->tp_world);
+    YK_TRY(yk_tp_allgather_u32(e, reinterpret_cast<const uint32_t*>(&h), 16, all.data()));
+    std::vector<uint8_t*> ptrs(e->tp_world, nullptr);
+    e->ar_opened.assign(e->tp_world, nullptr);
+    for (int q = 0; q < e->tp_world; ++q) {
+        if (q == e->tp_rank) {
+            ptrs[q] = e->ar_local;
+            continue;
+        }
+        cudaIpcMemHandle_t hq;
+        std::memcpy(&hq, all.data() + (size_t)16 * q, sizeof(hq));
+        void* p = nullptr;
+        const cudaError_t r = cudaIpcOpenMemHandle(&p, hq, cudaIpcMemLazyEnablePeerAccess);
+        if (r != cudaSuccess) {
+            ar_release(e);
+            yk_set_error(std::string("cudaIpcOpenMemHandle (all-reduce buffer of rank ") + std::to_string(q) +
+                         "): " + cudaGetErrorString(r));
+            return YK_ERR_CUDA;
+        }
+        e->ar_opened[q] = p;
+        ptrs[q] = static_cast<uint8_t*>(p);
+    }
+    YK_CHECK_CUDA(cudaMalloc(&e->ar_bufs, sizeof(uint8_t*) * e->tp_world));
+    YK_CHECK_CUDA(cudaMemcpy(e->ar_bufs, ptrs.data(), sizeof(uint8_t*) * e->tp_world, cudaMemcpyHostToDevice));
+    e->ar_cap = need;
+    e->ar_ctr_base = 0;
+    return YK_OK;
+}
+
+__nv_bfloat16* tp_ar_slot(yk_engine* e) {
+    const uint32_t next = e->ar_epoch + 1 == 0 ? 1 : e->ar_epoch + 1;
+    return reinterpret_cast<__nv_bfloat16*>(e->ar_local + AR_FLAGS + (size_t)(next & 1u) * e->ar_cap);
+}
+
+yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out) {
+    YK_ARG(count % 8 == 0 && count * 2 <= e->ar_cap, "all-reduce size");
+    e->ar_epoch = e->ar_epoch + 1 == 0 ? 1 : e->ar_epoch + 1;
+    const int grid = e->num_sms;
+    const double payload = (double)count * 2;
+    ProfScope prof(e, YK_PROF_OTHER, 2.0 * (e->tp_world - 1) / e->tp_world * payload, 0.0);
+    YK_CHECK_CUDA(launch_pdl(e, ar_two_shot_kernel, grid, AR_THREADS, 0, (uint8_t* const*)e->ar_bufs, e->tp_rank,
+                             e->tp_world, count, e->ar_cap, e->ar_epoch, e->ar_ctr_base + (unsigned long long)grid - 1,
+                             out, e->d_err));
+    e->ar_ctr_base += (unsigned long long)grid;
+    e->launches++;
+    return YK_OK;
+}
+
 void tp_destroy(yk_engine* e) {
+    if (e->ar_local) {
+        // no rank may still read this rank's buffer when it is released
+        if (e->nccl_comm && engine_sync_bounded(e) == YK_OK) {
+            uint32_t one = 1, all[64];
+            (void)yk_tp_allgather_u32(e, &one, 1, all);
+        }
+        ar_release(e);
+    }
     if (e->nccl_comm && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(e->nccl_comm));
     e->nccl_comm = nullptr;
     if (e->tp_gather) cudaFree(e->tp_gather);
