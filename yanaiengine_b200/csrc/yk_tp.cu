@@ -253,7 +253,8 @@ namespace yk {
 // per SM at most), so the CTAs waiting in B / C never block one still to run.
 // ---------------------------------------------------------------------------
 constexpr int AR_THREADS = 512;
-constexpr size_t AR_FLAGS = 4096;   // flag area: A flags [0, 64), C flags [64, 128), CTA counter at 256 (u64)
+constexpr size_t AR_FLAGS = 4096;   // flag area (u32 words): A flags [0, 64), C flags [64, 128); the CTA
+                                    // counter (u64) at byte 1024
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const*
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        unsigned long long* ctr = reinterpret_cast<unsigned long long*>(mine + 256);
+        unsigned long long* ctr = reinterpret_cast<unsigned long long*>(mine + 1024);
         if (atomicAdd(ctr, 1ULL) == ctr_target) {
             __threadfence_system();
             for (int q = 0; q < w; ++q) st_release_sys(reinterpret_cast<uint32_t*>(bufs[q]) + 64 + rank, epoch);
