@@ -49,7 +49,7 @@ DRAFT = dict(TARGET, d_model=2048, n_layers=16, n_heads=32, n_kv_heads=8, head_d
 GEMM_TRAFFIC_RATIO = 1.018  # measured DRAM bytes / algorithmic bytes of a GEMM launch (ncu capture)
 TARGET_70B = dict(TARGET, d_model=8192, n_layers=80, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672)
 METRIC_70B = "accepted tokens/sec, 70B-shape target (TP over all GPUs) + 8B-shape draft, k=4 batch 128"
-WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (NCCL all-reduce after o_proj / down_proj) + "
+WORKLOAD_70B = ("spec-decode step: 70B-shape target tensor-parallel (all-reduce over NVLink after o_proj / down_proj) + "
                 "8B-shape draft replicated on every rank, each rank drafting its slice of the sequences, bf16, k=4, "
                 "T=0.8, 128 seqs x 4096 ctx")
 METRIC = "accepted tokens/sec, 8B/1B-shape k=5 batch 32, at 1/2/4/8 B200; verify HBM GB/s"
@@ -540,10 +540,12 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
                 "ms_per_step": ar_ms, "launches_per_step": ar["launches"] / prof_steps,
                 "share_of_step": ar_ms / step_ms,
                 "payload": "fp32" if os.environ.get("YK_TP_PAYLOAD") == "f32" else "bf16",
+                "kind": ("ncclAllReduce" if os.environ.get("YK_TP_AR") == "nccl" or os.environ.get("YK_TP_PAYLOAD") == "f32"
+                         else "own two-shot kernel over NVLink peer memory"),
                 # what one rank sends over NVLink in a ring all-reduce, per second of all-reduce time
                 "link_gbs": ar["bytes"] / (ar["ms"] / 1e3) / 1e9 if ar["ms"] > 0 else None,
                 "link_peak_gbs": 770.0,
-                "note": "CUDA events around each ncclAllReduce on the engine stream, in a second pass of "
+                "note": "CUDA events around each all-reduce on the engine stream, in a second pass of "
                         f"{prof_steps} steps without programmatic launch"}
     return res
 
