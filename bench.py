@@ -465,7 +465,7 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
                 sch.step()
             gemm = eng.profile_read(0)
             attn = eng.profile_read(1)
-            ar = eng.profile_read(3)  # tensor-parallel all-reduce (NCCL), if any
+            ar = eng.profile_read(3)  # tensor-parallel all-reduce (own kernel or NCCL), if any
             eng.profile(False)
         # in-situ breakdown of one more step from the launch trace (first CTA past the
         # grid dependency wait, last CTA exit per launch), programmatic launch on

@@ -292,6 +292,9 @@ __device__ __forceinline__ float4 lds_v4(uint32_t addr) {
 __device__ __forceinline__ void cluster_sync_any() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
+// The two halves of cluster_sync_any, for work that overlaps the barrier.
+__device__ __forceinline__ void cluster_arrive_any() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait_any() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, K-major operand tile written by TMA with
 // 128-byte swizzle: rows of 128 B, 8-row swizzle atoms of 1024 B stacked

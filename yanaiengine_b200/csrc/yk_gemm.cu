@@ -611,9 +611,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         }
         bool ok = flags[0] == 0;
-        if (push && !mbar_wait_bounded(rbar, 0u)) {
-            raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
-            ok = false;
+        if (push) {
+            if (!mbar_wait_bounded(rbar, 0u)) {
+                raise_err(a.epi.err, YK_DEV_ERR_TIMEOUT);
+                ok = false;
+            }
+            // Every byte sent to this CTA has landed, so every peer's copy to it has
+            // read its source: the closing barrier's arrival can go now, and the
+            // reduction below (local operands only) overlaps its latency.
+            cluster_arrive_any();
         }
 #define YK_CLUSTER_REDUCE(N)                                                                                        \
     (push ? cluster_reduce<KIND, N, true, FN>(a, ep, red_addr, recv_addr, rope_addr, rank, slot_cols, tm, tn, c0, c1, \
@@ -631,7 +637,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             default: YK_CLUSTER_REDUCE(8); break;
         }
 #undef YK_CLUSTER_REDUCE
-        cluster_sync_any();  // no peer still reads (or copies out of) this CTA's shared memory
+        // no peer still reads (or copies out of) this CTA's shared memory
+        if (push) cluster_wait_any(); else cluster_sync_any();
         if (threadIdx.x == 64) stamp(a, ST_EPI_DONE);
     }
 
