@@ -84,6 +84,18 @@ yk_status ykt_sampler_stamps_read(yk_sampler* s, uint64_t* host, int32_t cap);
  * engine stays usable. */
 yk_status ykt_wait_timeout(yk_engine* e, int32_t budget_ms, double* waited_ms);
 
+/* The tensor-parallel all-reduce alone: 3 untimed calls, then `iters` calls
+ * back to back on the engine stream over `count` bf16 elements (a multiple of
+ * 8), timed with CUDA events; *ms_per_call = the average.  own != 0: the
+ * group's own kernel over NVLink peer memory; 0: ncclAllReduce.  With own
+ * and stamps_out (8 words, may be NULL), one more call records the kernel's
+ * global-timer stamps (ns): CTA 0's entry, dependency resolved, every
+ * partial ready, its share reduced, every share reduced, end; [6] the last
+ * CTA's arrival; [7] unused.  Every rank of the group calls it with the same
+ * arguments (it is a collective). */
+yk_status ykt_tp_allreduce_timed(yk_engine* e, int64_t count, int32_t iters, int32_t own, double* ms_per_call,
+                                 uint64_t* stamps_out);
+
 /* The target probabilities q[B x (k+1) x V] exactly as the last verification
  * of yk_spec_sample_logits formed them from its logits (same chunk statistics,
  * same per-element expression), temperature > 0: lets a test hold the

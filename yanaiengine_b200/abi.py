@@ -136,6 +136,8 @@ _PROTOS = {
     "ykt_sampler_stamps_enable": (C.c_int32, [_P, C.c_int32]),
     "ykt_sampler_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32]),
     "ykt_wait_timeout": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_double)]),
+    "ykt_tp_allreduce_timed": (C.c_int32, [_P, C.c_int64, C.c_int32, C.c_int32, C.POINTER(C.c_double),
+                                           C.POINTER(C.c_uint64)]),
     "ykt_sampler_target_probs": (C.c_int32, [_P, C.c_int32, C.c_float, C.POINTER(C.c_float)]),
     "ykt_trace_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, C.POINTER(C.c_uint64)]),
     "ykt_attention_stamps_read": (C.c_int32, [_P, C.POINTER(C.c_uint64), C.c_int32, _I32P]),
@@ -329,6 +331,15 @@ class Engine:
         ms = C.c_double()
         st = lib().ykt_wait_timeout(self.h, budget_ms, C.byref(ms))
         return st, ms.value
+
+    def tp_allreduce_timed(self, count: int, iters: int, own: bool):
+        """Test hook (collective): (milliseconds per all-reduce of `count` bf16
+        elements over `iters` calls back to back, phase stamps of one more call in ns
+        or None); own: the group's kernel, else ncclAllReduce."""
+        ms = C.c_double()
+        st = (C.c_uint64 * 8)()
+        check(lib().ykt_tp_allreduce_timed(self.h, int(count), int(iters), 1 if own else 0, C.byref(ms), st))
+        return ms.value, ([int(x) for x in st] if own else None)
 
     def device_error(self) -> int:
         v = C.c_uint32()

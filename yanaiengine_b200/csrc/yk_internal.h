@@ -376,7 +376,7 @@ yk_status tp_allreduce(yk_engine* e, void* buf, size_t count, bool bf16);
 bool tp_ar_enabled(const yk_engine* e);
 yk_status tp_ar_reserve(yk_engine* e, size_t count);  // collective: every rank, same count
 __nv_bfloat16* tp_ar_slot(yk_engine* e);
-yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out);
+yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out, unsigned long long* stamps = nullptr);
 // Waits for the engine stream; with a tensor-parallel group, bounded by the
 // group's deadline (the communicator is aborted and YK_ERR_TIMEOUT returned when
 // it runs out: a peer that stopped taking part leaves its collectives unfinished).

@@ -71,15 +71,23 @@ using Clock = std::chrono::steady_clock;
 ncclResult_t poll_comm(ncclComm_t comm, Clock::time_point deadline, bool* timed_out) {
     *timed_out = false;
     ncclResult_t st = ncclInProgress;
+    // An enqueue completes within microseconds: spin (yielding) for the first
+    // millisecond, so that back-to-back collectives are not paced by the sleep;
+    // longer operations (group set-up) are polled every 200 us.
+    const Clock::time_point spin_until = Clock::now() + std::chrono::milliseconds(1);
     while (true) {
         const ncclResult_t r = nccl().get_async_error(comm, &st);
         if (r != ncclSuccess) return r;
         if (st != ncclInProgress) return st;
-        if (Clock::now() > deadline) {
+        const Clock::time_point now = Clock::now();
+        if (now > deadline) {
             *timed_out = true;
             return ncclInProgress;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        if (now < spin_until)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(200));
     }
 }
 
@@ -279,12 +287,80 @@ __device__ __forceinline__ bool ar_wait_all(const uint32_t* flags, int w, uint32
     return true;
 }
 
+// Phases B and C for a group of W ranks.  A thread takes U = 8 / W indices i
+// of a share at a time and issues all U x W of their 16-byte peer loads before
+// it uses any, so each thread keeps that many NVLink round trips in flight
+// (one load at a time left the 8-rank all-reduce of 10.5 MB latency-bound).
+// B: red(rank)[v0 + i] = bf16(sum over q = 0..W-1 in order of part(q)[v0 + i]).
+// C: out[q * share + i] = red(q)[q * share + i] for every rank q.
+template <int W>
+__device__ __forceinline__ void ar_phase(bool reduce, uint8_t* const* bufs, int rank, int slot, size_t cap,
+                                         size_t nv, size_t share, uint4* o4) {
+    constexpr int U = 8 / W;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t v0 = (size_t)rank * share;
+    const size_t n_b = v0 >= nv ? 0 : (v0 + share < nv ? share : nv - v0);  // this rank's share in B
+    const size_t n_i = reduce ? n_b : share;
+    const uint4* src[W];
+#pragma unroll
+    for (int q = 0; q < W; ++q)
+        src[q] = reinterpret_cast<const uint4*>(bufs[q] + AR_FLAGS + (size_t)(reduce ? slot : 2 + slot) * cap);
+    for (size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n_i; i0 += U * stride) {
+        uint4 x[U][W];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t i = i0 + (size_t)u * stride;
+#pragma unroll
+            for (int q = 0; q < W; ++q) {
+                const size_t v = reduce ? v0 + i : (size_t)q * share + i;
+                if (i < n_i && v < nv) x[u][q] = src[q][v];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const size_t i = i0 + (size_t)u * stride;
+            if (i >= n_i) continue;
+            if (reduce) {
+                float acc[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+                for (int q = 0; q < W; ++q) {
+                    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x[u][q]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[2 * e] += __low2float(h[e]);
+                        acc[2 * e + 1] += __high2float(h[e]);
+                    }
+                }
+                uint4 y;
+                __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&y);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+                reinterpret_cast<uint4*>(bufs[rank] + AR_FLAGS + (size_t)(2 + slot) * cap)[v0 + i] = y;
+            } else {
+#pragma unroll
+                for (int q = 0; q < W; ++q) {
+                    const size_t v = (size_t)q * share + i;
+                    if (v < nv) o4[v] = x[u][q];
+                }
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const* bufs, int rank, int w,
                                                                  size_t count, size_t cap, uint32_t epoch,
                                                                  unsigned long long ctr_target,
-                                                                 __nv_bfloat16* out, uint32_t* err) {
+                                                                 __nv_bfloat16* out, uint32_t* err,
+                                                                 unsigned long long* stamps) {
+    // stamps (test hook; null otherwise): CTA 0's entry, dependency, "partial ready"
+    // seen, share reduced, "reduced ready" seen, end; [6] the last CTA's arrival
+    const bool st0 = stamps && blockIdx.x == 0 && threadIdx.x == 0;
+    if (st0) stamps[0] = globaltimer_ns();
     pdl_trigger();
     pdl_wait();  // the partial (the previous kernel's output) is complete
+    if (st0) stamps[1] = globaltimer_ns();
     __shared__ int s_ok;
     const int slot = (int)(epoch & 1u);
     uint8_t* mine = bufs[rank];
@@ -301,33 +377,45 @@ __global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const*
     if (threadIdx.x == 0) s_ok = ar_wait_all(flags, w, epoch, err) ? 1 : 0;
     __syncthreads();
     if (!s_ok) return;
+    if (st0) stamps[2] = globaltimer_ns();
     // B: this rank's share, summed over the ranks in order
-    const size_t v0 = (size_t)rank * share, v1 = v0 + share < nv ? v0 + share : nv;
-    for (size_t v = v0 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1; v += (size_t)gridDim.x * blockDim.x) {
-        float acc[8];
+    uint4* o4 = reinterpret_cast<uint4*>(out);
+    switch (w) {
+        case 2: ar_phase<2>(true, bufs, rank, slot, cap, nv, share, o4); break;
+        case 4: ar_phase<4>(true, bufs, rank, slot, cap, nv, share, o4); break;
+        case 8: ar_phase<8>(true, bufs, rank, slot, cap, nv, share, o4); break;
+        default: {
+            const size_t v0 = (size_t)rank * share, v1 = v0 + share < nv ? v0 + share : nv;
+            for (size_t v = v0 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1;
+                 v += (size_t)gridDim.x * blockDim.x) {
+                float acc[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int q = 0; q < w; ++q) {
-            const uint4 x = part(q)[v];
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+                for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+                for (int q = 0; q < w; ++q) {
+                    const uint4 x = part(q)[v];
+                    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                acc[2 * i] += __low2float(h[i]);
-                acc[2 * i + 1] += __high2float(h[i]);
+                    for (int i = 0; i < 4; ++i) {
+                        acc[2 * i] += __low2float(h[i]);
+                        acc[2 * i + 1] += __high2float(h[i]);
+                    }
+                }
+                uint4 y;
+                __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&y);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+                red(rank)[v] = y;
             }
         }
-        uint4 y;
-        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&y);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-        red(rank)[v] = y;
     }
     // the last CTA done with B raises "reduced ready" on every rank
     __syncthreads();
+    if (st0) stamps[3] = globaltimer_ns();
     if (threadIdx.x == 0) {
         __threadfence();
         unsigned long long* ctr = reinterpret_cast<unsigned long long*>(mine + 1024);
         if (atomicAdd(ctr, 1ULL) == ctr_target) {
+            if (stamps) stamps[6] = globaltimer_ns();
             __threadfence_system();
             for (int q = 0; q < w; ++q) st_release_sys(reinterpret_cast<uint32_t*>(bufs[q]) + 64 + rank, epoch);
         }
@@ -335,10 +423,20 @@ __global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const*
     }
     __syncthreads();
     if (!s_ok) return;
+    if (st0) stamps[4] = globaltimer_ns();
     // C: every rank's reduced share into out
-    uint4* o4 = reinterpret_cast<uint4*>(out);
-    for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (size_t)gridDim.x * blockDim.x)
-        o4[v] = red((int)(v / share))[v];
+    switch (w) {
+        case 2: ar_phase<2>(false, bufs, rank, slot, cap, nv, share, o4); break;
+        case 4: ar_phase<4>(false, bufs, rank, slot, cap, nv, share, o4); break;
+        case 8: ar_phase<8>(false, bufs, rank, slot, cap, nv, share, o4); break;
+        default:
+            for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (size_t)gridDim.x * blockDim.x)
+                o4[v] = red((int)(v / share))[v];
+    }
+    if (stamps && blockIdx.x == 0) {
+        __syncthreads();
+        if (threadIdx.x == 0) stamps[5] = globaltimer_ns();
+    }
 }
 
 bool tp_ar_enabled(const yk_engine* e) { return e->nccl_comm && e->tp_world > 1 && e->tp_ar_own; }
@@ -404,7 +502,7 @@ __nv_bfloat16* tp_ar_slot(yk_engine* e) {
     return reinterpret_cast<__nv_bfloat16*>(e->ar_local + AR_FLAGS + (size_t)(next & 1u) * e->ar_cap);
 }
 
-yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out) {
+yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out, unsigned long long* stamps) {
     YK_ARG(count % 8 == 0 && count * 2 <= e->ar_cap, "all-reduce size");
     e->ar_epoch = e->ar_epoch + 1 == 0 ? 1 : e->ar_epoch + 1;
     const int grid = e->num_sms;
@@ -412,7 +510,7 @@ yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out) {
     ProfScope prof(e, YK_PROF_OTHER, 2.0 * (e->tp_world - 1) / e->tp_world * payload, 0.0);
     YK_CHECK_CUDA(launch_pdl(e, ar_two_shot_kernel, grid, AR_THREADS, 0, (uint8_t* const*)e->ar_bufs, e->tp_rank,
                              e->tp_world, count, e->ar_cap, e->ar_epoch, e->ar_ctr_base + (unsigned long long)grid - 1,
-                             out, e->d_err));
+                             out, e->d_err, stamps));
     e->ar_ctr_base += (unsigned long long)grid;
     e->launches++;
     return YK_OK;
@@ -435,3 +533,58 @@ void tp_destroy(yk_engine* e) {
 }
 
 }  // namespace yk
+
+// ---------------------------------------------------------------------------
+// Test hook (include/yk_testing.h): the all-reduce alone, back to back.
+// ---------------------------------------------------------------------------
+#include "../../include/yk_testing.h"
+
+extern "C" yk_status ykt_tp_allreduce_timed(yk_engine* e, int64_t count, int32_t iters, int32_t own,
+                                            double* ms_per_call, uint64_t* stamps_out) {
+    YK_ARG(e && ms_per_call && count > 0 && count % 8 == 0 && iters > 0, "arguments");
+    YK_ARG(e->nccl_comm && e->tp_world > 1, "engine has not joined a tensor-parallel group");
+    YK_CHECK_CUDA(cudaSetDevice(e->device));
+    if (own) YK_TRY(yk::tp_ar_reserve(e, (size_t)count));
+    __nv_bfloat16* buf = nullptr;
+    YK_CHECK_CUDA(cudaMalloc(&buf, (size_t)count * 2));
+    unsigned long long* dst = nullptr;
+    if (cudaMalloc(&dst, 8 * sizeof(unsigned long long)) != cudaSuccess) {
+        cudaFree(buf);
+        yk_set_error("cudaMalloc (stamps) failed");
+        return YK_ERR_CUDA;
+    }
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    yk_status st = YK_OK;
+    auto call = [&]() -> yk_status {
+        return own ? yk::tp_ar_run(e, (size_t)count, buf) : yk::tp_allreduce(e, buf, (size_t)count, true);
+    };
+    auto run = [&]() -> yk_status {
+        YK_CHECK_CUDA(cudaMemsetAsync(buf, 0, (size_t)count * 2, e->stream));
+        for (int i = 0; i < 3; ++i) YK_TRY(call());
+        YK_TRY(yk::engine_sync_bounded(e));
+        YK_CHECK_CUDA(cudaEventCreate(&t0));
+        YK_CHECK_CUDA(cudaEventCreate(&t1));
+        YK_CHECK_CUDA(cudaEventRecord(t0, e->stream));
+        for (int i = 0; i < iters; ++i) YK_TRY(call());
+        YK_CHECK_CUDA(cudaEventRecord(t1, e->stream));
+        YK_TRY(yk::engine_sync_bounded(e));
+        float ms = 0.f;
+        YK_CHECK_CUDA(cudaEventElapsedTime(&ms, t0, t1));
+        *ms_per_call = (double)ms / iters;
+        if (own && stamps_out) {
+            // one more call with the kernel's phase stamps
+            YK_CHECK_CUDA(cudaMemsetAsync(dst, 0, 8 * sizeof(unsigned long long), e->stream));
+            YK_TRY(yk::tp_ar_run(e, (size_t)count, buf, dst));
+            YK_TRY(yk::engine_sync_bounded(e));
+            YK_CHECK_CUDA(cudaMemcpy(stamps_out, dst, 8 * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+        }
+        return YK_OK;
+    };
+    st = run();
+    if (t0) cudaEventDestroy(t0);
+    if (t1) cudaEventDestroy(t1);
+    if (st == YK_OK) st = yk::engine_sync_bounded(e);
+    cudaFree(buf);
+    cudaFree(dst);
+    return st;
+}

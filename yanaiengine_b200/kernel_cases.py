@@ -4,6 +4,7 @@
     python -m yanaiengine_b200.kernel_cases gemm [--n 28672 --k 4096 --m 192]
     python -m yanaiengine_b200.kernel_cases sampler [--seqs 32 --k 5 --vocab 128256]
     python -m yanaiengine_b200.kernel_cases forward [--shape draft|target --layers 4 --steps 3]
+    torchrun --nproc-per-node N -m yanaiengine_b200.kernel_cases allreduce [--tokens 16 80 128 640 --d 8192]
 
 `attention` builds a 2-layer bf16 model whose attention has the verify shape of
 the 8B-class target (or the 1B-class draft with --dh 64 --new 1, the Gemma-2 9B
@@ -12,10 +13,13 @@ fills a KV pool with a synthetic context of U[ctx-lo, ctx-hi] (default
 U[512, 2048]) tokens per sequence and runs forward steps; the pool holds about 1 GB, one layer's KV (170 MB at the target
 shape) is larger than L2.  `gemm` runs the tcgen05 GEMM test hook on one layer
 shape with an L2 flush before each launch.  Both print one timing line.
+`allreduce` times the tensor-parallel all-reduce of [tokens x d] bf16 alone,
+the group's own kernel against ncclAllReduce.
 """
 from __future__ import annotations
 
 import argparse
+import os
 import time
 
 import numpy as np
@@ -160,6 +164,49 @@ def gemm(args) -> None:
     e.close()
 
 
+def allreduce(args) -> None:
+    """The tensor-parallel all-reduce alone, under torchrun (one rank per GPU):
+    per message size, the group's own kernel and ncclAllReduce, each timed over
+    back-to-back calls (max over ranks)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2:
+        raise SystemExit("allreduce: run under torchrun with two or more ranks")
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    e = abi.Engine(local)
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(abi.tp_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    e.tp_init(bytes(uid.cpu().numpy()), rank, world)
+    for tokens in args.tokens:
+        count = tokens * args.d
+        row, st = [], None
+        for own in (True, False):
+            t, s = e.tp_allreduce_timed(count, args.iters, own)
+            st = s if own else st
+            ms = torch.tensor([t], device="cuda")
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            row.append(float(ms.item()))
+        if rank == 0:
+            mb = count * 2 / 1e6
+            bus = lambda ms: 2 * (world - 1) / world * count * 2 / (ms / 1e3) / 1e9  # ring-equivalent GB/s
+            print(f"all-reduce w={world} [{tokens} x {args.d}] bf16 {mb:.2f} MB: own {1e3 * row[0]:.1f} us "
+                  f"({bus(row[0]):.0f} GB/s bus), nccl {1e3 * row[1]:.1f} us ({bus(row[1]):.0f} GB/s bus)")
+            rel = [(x - st[0]) / 1e3 if x else float("nan") for x in st[:7]]
+            print(f"  own, one call on rank 0 (us from CTA 0's entry): dependency {rel[1]:.1f}, partials ready "
+                  f"{rel[2]:.1f}, share reduced {rel[3]:.1f}, last CTA {rel[6]:.1f}, shares ready {rel[4]:.1f}, "
+                  f"end {rel[5]:.1f}")
+    e.close()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="case", required=True)
@@ -189,8 +236,12 @@ def main() -> None:
     g.add_argument("--k", type=int, default=4096)
     g.add_argument("--m", type=int, default=192)
     g.add_argument("--reps", type=int, default=3)
+    ar = sub.add_parser("allreduce")
+    ar.add_argument("--tokens", type=int, nargs="+", default=[16, 80, 128, 640])
+    ar.add_argument("--d", type=int, default=8192)
+    ar.add_argument("--iters", type=int, default=50)
     args = ap.parse_args()
-    {"attention": attention, "sampler": sampler, "gemm": gemm, "forward": forward}[args.case](args)
+    {"attention": attention, "sampler": sampler, "gemm": gemm, "forward": forward, "allreduce": allreduce}[args.case](args)
 
 
 if __name__ == "__main__":
