@@ -348,7 +348,10 @@ yk_status yk_tp_unique_id(uint8_t id_out[128]);
  * sampler's result reads): a stream whose collectives do not finish in time (a
  * peer stopped taking part) ends with YK_ERR_TIMEOUT and the communicator
  * aborted.  yk_tp_init uses 300 s.  The all-reduce payload is bf16 (env
- * YK_TP_PAYLOAD=f32 at engine creation: fp32). */
+ * YK_TP_PAYLOAD=f32 at engine creation: fp32, through NCCL).  The bf16
+ * all-reduce is the module's own kernel over NVLink peer memory (one shot at
+ * two ranks, two-shot above); env YK_TP_AR=nccl uses ncclAllReduce, and
+ * YK_TP_AR=twoshot the two-shot form at two ranks too. */
 yk_status yk_tp_init(yk_engine* e, const uint8_t id[128], int32_t rank, int32_t world);
 yk_status yk_tp_init_timeout(yk_engine* e, const uint8_t id[128], int32_t rank, int32_t world, int64_t timeout_ms);
 /* Shard tp_rank of tp_world of the model `cfg`: query heads, KV heads and FFN

@@ -133,10 +133,12 @@ def _worker(rank, uid, q, via_loader=False, payload="bf16", ar="own"):
 
 
 @pytest.mark.parametrize("via_loader,payload,ar", [(False, "bf16", "own"), (True, "bf16", "own"),
-                                                    (False, "bf16", "nccl"), (False, "f32", "nccl")])
+                                                    (False, "bf16", "twoshot"), (False, "bf16", "nccl"),
+                                                    (False, "f32", "nccl")])
 def test_tp2_forward_matches_oracle(oracle, via_loader, payload, ar):
     """ar: the all-reduce after o_proj / down_proj, the group's own kernel over NVLink
-    peer memory (bf16, the default) or NCCL's."""
+    peer memory (bf16, the default: one shot at two ranks; "twoshot": the two-phase
+    form every message size above the one-shot bound takes) or NCCL's."""
     import torch
 
     if torch.cuda.device_count() < WORLD:

@@ -105,7 +105,10 @@ extern "C" yk_status yk_engine_create(int32_t device, yk_engine** out) {
     if (const char* v = std::getenv("YK_ATTN_WAVES")) e->attn_waves = std::max(1, std::atoi(v));
     if (const char* v = std::getenv("YK_ATTN_PLAN")) e->attn_balanced = std::atoi(v) == 1;
     if (const char* v = std::getenv("YK_TP_PAYLOAD")) e->tp_bf16 = std::strcmp(v, "f32") != 0;
-    if (const char* v = std::getenv("YK_TP_AR")) e->tp_ar_own = std::strcmp(v, "nccl") != 0;
+    if (const char* v = std::getenv("YK_TP_AR")) {
+        e->tp_ar_own = std::strcmp(v, "nccl") != 0;
+        if (std::strcmp(v, "twoshot") == 0) e->ar_one_shot = false;
+    }
     yk_status s = e->ensure_pinned((size_t)4 << 20);
     if (s != YK_OK) { delete e; return s; }
     *out = e;

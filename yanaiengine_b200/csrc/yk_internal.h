@@ -97,6 +97,9 @@ struct yk_engine {
     // each rank's buffer [flags 4 KB | 2 partial slots | 2 reduced slots] of ar_cap bytes
     // per slot, shared with the other ranks through CUDA IPC.
     bool tp_ar_own = true;
+    // own all-reduce at two ranks: one shot (each rank sums both whole partials)
+    // instead of two-shot; YK_TP_AR=twoshot turns it off
+    bool ar_one_shot = true;
     size_t ar_cap = 0;
     uint8_t* ar_local = nullptr;
     std::vector<void*> ar_opened;        // the peers' buffers as mapped here (null for this rank)

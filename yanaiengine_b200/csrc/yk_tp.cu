@@ -243,10 +243,10 @@ extern "C" yk_status yk_tp_allgather_u32(yk_engine* e, const uint32_t* send, int
 namespace yk {
 
 // ---------------------------------------------------------------------------
-// The group's own all-reduce over NVLink peer memory (two-shot).  Every rank's
-// buffer (CUDA IPC, mapped by every other rank): a flag area, two partial slots
-// and two reduced slots (alternating by call, so a rank that runs ahead never
-// overwrites what a slower peer still reads).  Per call, on every rank:
+// The group's own all-reduce over NVLink peer memory.  Every rank's buffer (CUDA
+// IPC, mapped by every other rank): a flag area, two partial slots and two
+// reduced slots (alternating by call, so a rank that runs ahead never overwrites
+// what a slower peer still reads).  Per call, on every rank (two-shot):
 //   A. after the GEMM wrote its bf16 partial into this rank's partial slot, raise
 //      "partial ready" in every rank's flag area (system-scope release);
 //   B. once every rank's partial is ready: sum this rank's 1/w of the elements
@@ -255,6 +255,12 @@ namespace yk {
 //      raises "reduced ready" everywhere;
 //   C. once every rank's share is reduced: copy every rank's reduced share
 //      (peer loads) into `out`.
+// One shot at w = 2, where both forms read the same bytes from the peer: after
+// A, every rank sums every element over all ranks' partials in rank order
+// straight into `out`; no B/C hand-off, no second flag exchange.  (At larger w
+// it reads (w - 1) x the payload from the peers; two-shot is kept there.)  A partial slot is rewritten two calls later,
+// after the writer has seen every peer's "partial ready" of the call between,
+// which each peer raises only once its reads of this call are done.
 // Every rank thus holds the same bytes.  Each wait is bounded (the device error
 // word gets the timeout bit and the kernel returns).  Plain loads and stores
 // only: no TMA, no multicast.  All CTAs of the grid are resident together (one
@@ -287,20 +293,24 @@ __device__ __forceinline__ bool ar_wait_all(const uint32_t* flags, int w, uint32
     return true;
 }
 
-// Phases B and C for a group of W ranks.  A thread takes U = 8 / W indices i
-// of a share at a time and issues all U x W of their 16-byte peer loads before
-// it uses any, so each thread keeps that many NVLink round trips in flight
-// (one load at a time left the 8-rank all-reduce of 10.5 MB latency-bound).
-// B: red(rank)[v0 + i] = bf16(sum over q = 0..W-1 in order of part(q)[v0 + i]).
-// C: out[q * share + i] = red(q)[q * share + i] for every rank q.
+// Phases for a group of W ranks.  A thread takes U = 8 / W indices i at a time
+// and issues all U x W of their 16-byte peer loads before it uses any, so each
+// thread keeps that many NVLink round trips in flight (one load at a time left
+// the 8-rank all-reduce of 10.5 MB latency-bound).
+//   AR_SHARE (two-shot B): red(rank)[v0 + i] = bf16(sum over q = 0..W-1 in order
+//     of part(q)[v0 + i]), i over this rank's share;
+//   AR_GATHER (two-shot C): out[q * share + i] = red(q)[q * share + i] for every q;
+//   AR_ALL (one shot): out[i] = bf16(sum over q in order of part(q)[i]), every i.
+enum ArMode { AR_SHARE = 0, AR_GATHER = 1, AR_ALL = 2 };
 template <int W>
-__device__ __forceinline__ void ar_phase(bool reduce, uint8_t* const* bufs, int rank, int slot, size_t cap,
+__device__ __forceinline__ void ar_phase(int mode, uint8_t* const* bufs, int rank, int slot, size_t cap,
                                          size_t nv, size_t share, uint4* o4) {
     constexpr int U = 8 / W;
+    const bool reduce = mode != AR_GATHER;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
-    const size_t v0 = (size_t)rank * share;
+    const size_t v0 = mode == AR_SHARE ? (size_t)rank * share : 0;
     const size_t n_b = v0 >= nv ? 0 : (v0 + share < nv ? share : nv - v0);  // this rank's share in B
-    const size_t n_i = reduce ? n_b : share;
+    const size_t n_i = mode == AR_SHARE ? n_b : (mode == AR_GATHER ? share : nv);
     const uint4* src[W];
 #pragma unroll
     for (int q = 0; q < W; ++q)
@@ -337,7 +347,8 @@ __device__ __forceinline__ void ar_phase(bool reduce, uint8_t* const* bufs, int 
                 __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&y);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) o[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
-                reinterpret_cast<uint4*>(bufs[rank] + AR_FLAGS + (size_t)(2 + slot) * cap)[v0 + i] = y;
+                if (mode == AR_ALL) o4[i] = y;
+                else reinterpret_cast<uint4*>(bufs[rank] + AR_FLAGS + (size_t)(2 + slot) * cap)[v0 + i] = y;
             } else {
 #pragma unroll
                 for (int q = 0; q < W; ++q) {
@@ -349,13 +360,55 @@ __device__ __forceinline__ void ar_phase(bool reduce, uint8_t* const* bufs, int 
     }
 }
 
-__global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const* bufs, int rank, int w,
-                                                                 size_t count, size_t cap, uint32_t epoch,
-                                                                 unsigned long long ctr_target,
-                                                                 __nv_bfloat16* out, uint32_t* err,
-                                                                 unsigned long long* stamps) {
+// Generic group size (not 2, 4 or 8): one vector at a time, same sums.
+__device__ __noinline__ void ar_phase_any(int mode, uint8_t* const* bufs, int rank, int w, int slot, size_t cap,
+                                          size_t nv, size_t share, uint4* o4) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t v0 = mode == AR_SHARE ? (size_t)rank * share : 0;
+    const size_t v1 = mode == AR_SHARE ? (v0 + share < nv ? v0 + share : nv) : nv;
+    for (size_t v = v0 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1; v += stride) {
+        if (mode == AR_GATHER) {
+            o4[v] = reinterpret_cast<const uint4*>(bufs[(int)(v / share)] + AR_FLAGS + (size_t)(2 + slot) * cap)[v];
+            continue;
+        }
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int q = 0; q < w; ++q) {
+            const uint4 x = reinterpret_cast<const uint4*>(bufs[q] + AR_FLAGS + (size_t)slot * cap)[v];
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc[2 * i] += __low2float(h[i]);
+                acc[2 * i + 1] += __high2float(h[i]);
+            }
+        }
+        uint4 y;
+        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&y);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        if (mode == AR_ALL) o4[v] = y;
+        else reinterpret_cast<uint4*>(bufs[rank] + AR_FLAGS + (size_t)(2 + slot) * cap)[v] = y;
+    }
+}
+
+__device__ __forceinline__ void ar_run_phase(int mode, uint8_t* const* bufs, int rank, int w, int slot, size_t cap,
+                                             size_t nv, size_t share, uint4* o4) {
+    switch (w) {
+        case 2: ar_phase<2>(mode, bufs, rank, slot, cap, nv, share, o4); break;
+        case 4: ar_phase<4>(mode, bufs, rank, slot, cap, nv, share, o4); break;
+        case 8: ar_phase<8>(mode, bufs, rank, slot, cap, nv, share, o4); break;
+        default: ar_phase_any(mode, bufs, rank, w, slot, cap, nv, share, o4);
+    }
+}
+
+__global__ void __launch_bounds__(AR_THREADS) ar_peer_kernel(uint8_t* const* bufs, int rank, int w, size_t count,
+                                                             size_t cap, uint32_t epoch, int one_shot,
+                                                             unsigned long long ctr_target, __nv_bfloat16* out,
+                                                             uint32_t* err, unsigned long long* stamps) {
     // stamps (test hook; null otherwise): CTA 0's entry, dependency, "partial ready"
-    // seen, share reduced, "reduced ready" seen, end; [6] the last CTA's arrival
+    // seen, share (one shot: everything) reduced, "reduced ready" seen, end; [6] the
+    // last CTA's arrival
     const bool st0 = stamps && blockIdx.x == 0 && threadIdx.x == 0;
     if (st0) stamps[0] = globaltimer_ns();
     pdl_trigger();
@@ -365,10 +418,9 @@ __global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const*
     const int slot = (int)(epoch & 1u);
     uint8_t* mine = bufs[rank];
     uint32_t* flags = reinterpret_cast<uint32_t*>(mine);
-    auto part = [&](int q) { return reinterpret_cast<const uint4*>(bufs[q] + AR_FLAGS + (size_t)slot * cap); };
-    auto red = [&](int q) { return reinterpret_cast<uint4*>(bufs[q] + AR_FLAGS + (size_t)(2 + slot) * cap); };
     const size_t nv = count / 8;                 // 16-byte vectors (count is a multiple of 8)
     const size_t share = (nv + w - 1) / w;       // vectors per rank's share
+    uint4* o4 = reinterpret_cast<uint4*>(out);
     // A: this rank's partial is ready
     if (blockIdx.x == 0 && threadIdx.x < w) {
         __threadfence_system();
@@ -378,36 +430,17 @@ __global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const*
     __syncthreads();
     if (!s_ok) return;
     if (st0) stamps[2] = globaltimer_ns();
-    // B: this rank's share, summed over the ranks in order
-    uint4* o4 = reinterpret_cast<uint4*>(out);
-    switch (w) {
-        case 2: ar_phase<2>(true, bufs, rank, slot, cap, nv, share, o4); break;
-        case 4: ar_phase<4>(true, bufs, rank, slot, cap, nv, share, o4); break;
-        case 8: ar_phase<8>(true, bufs, rank, slot, cap, nv, share, o4); break;
-        default: {
-            const size_t v0 = (size_t)rank * share, v1 = v0 + share < nv ? v0 + share : nv;
-            for (size_t v = v0 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1;
-                 v += (size_t)gridDim.x * blockDim.x) {
-                float acc[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-                for (int q = 0; q < w; ++q) {
-                    const uint4 x = part(q)[v];
-                    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        acc[2 * i] += __low2float(h[i]);
-                        acc[2 * i + 1] += __high2float(h[i]);
-                    }
-                }
-                uint4 y;
-                __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&y);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-                red(rank)[v] = y;
-            }
+    if (one_shot) {
+        // every element, summed over the ranks in order, straight into out
+        ar_run_phase(AR_ALL, bufs, rank, w, slot, cap, nv, share, o4);
+        if (stamps && blockIdx.x == 0) {
+            __syncthreads();
+            if (threadIdx.x == 0) stamps[3] = stamps[5] = globaltimer_ns();
         }
+        return;
     }
+    // B: this rank's share, summed over the ranks in order
+    ar_run_phase(AR_SHARE, bufs, rank, w, slot, cap, nv, share, o4);
     // the last CTA done with B raises "reduced ready" on every rank
     __syncthreads();
     if (st0) stamps[3] = globaltimer_ns();
@@ -425,14 +458,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_two_shot_kernel(uint8_t* const*
     if (!s_ok) return;
     if (st0) stamps[4] = globaltimer_ns();
     // C: every rank's reduced share into out
-    switch (w) {
-        case 2: ar_phase<2>(false, bufs, rank, slot, cap, nv, share, o4); break;
-        case 4: ar_phase<4>(false, bufs, rank, slot, cap, nv, share, o4); break;
-        case 8: ar_phase<8>(false, bufs, rank, slot, cap, nv, share, o4); break;
-        default:
-            for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (size_t)gridDim.x * blockDim.x)
-                o4[v] = red((int)(v / share))[v];
-    }
+    ar_run_phase(AR_GATHER, bufs, rank, w, slot, cap, nv, share, o4);
     if (stamps && blockIdx.x == 0) {
         __syncthreads();
         if (threadIdx.x == 0) stamps[5] = globaltimer_ns();
@@ -507,11 +533,13 @@ yk_status tp_ar_run(yk_engine* e, size_t count, __nv_bfloat16* out, unsigned lon
     e->ar_epoch = e->ar_epoch + 1 == 0 ? 1 : e->ar_epoch + 1;
     const int grid = e->num_sms;
     const double payload = (double)count * 2;
-    ProfScope prof(e, YK_PROF_OTHER, 2.0 * (e->tp_world - 1) / e->tp_world * payload, 0.0);
-    YK_CHECK_CUDA(launch_pdl(e, ar_two_shot_kernel, grid, AR_THREADS, 0, (uint8_t* const*)e->ar_bufs, e->tp_rank,
-                             e->tp_world, count, e->ar_cap, e->ar_epoch, e->ar_ctr_base + (unsigned long long)grid - 1,
-                             out, e->d_err, stamps));
-    e->ar_ctr_base += (unsigned long long)grid;
+    // (the same choice on every rank: same group size and setting)
+    const bool one_shot = e->ar_one_shot && e->tp_world == 2;
+    ProfScope prof(e, YK_PROF_OTHER, (one_shot ? 1.0 : 2.0 / e->tp_world) * (e->tp_world - 1) * payload, 0.0);
+    YK_CHECK_CUDA(launch_pdl(e, ar_peer_kernel, grid, AR_THREADS, 0, (uint8_t* const*)e->ar_bufs, e->tp_rank,
+                             e->tp_world, count, e->ar_cap, e->ar_epoch, one_shot ? 1 : 0,
+                             e->ar_ctr_base + (unsigned long long)grid - 1, out, e->d_err, stamps));
+    if (!one_shot) e->ar_ctr_base += (unsigned long long)grid;
     e->launches++;
     return YK_OK;
 }
