@@ -541,7 +541,8 @@ def spec_phase(args, world, rank, local, eng, target, draft, lens, mine, B, rng,
                 "share_of_step": ar_ms / step_ms,
                 "payload": "fp32" if os.environ.get("YK_TP_PAYLOAD") == "f32" else "bf16",
                 "kind": ("ncclAllReduce" if os.environ.get("YK_TP_AR") == "nccl" or os.environ.get("YK_TP_PAYLOAD") == "f32"
-                         else "own two-shot kernel over NVLink peer memory"),
+                         else "own kernel over NVLink peer memory, "
+                         + ("one shot" if world == 2 and os.environ.get("YK_TP_AR") != "twoshot" else "two-shot")),
                 # what one rank sends over NVLink in a ring all-reduce, per second of all-reduce time
                 "link_gbs": ar["bytes"] / (ar["ms"] / 1e3) / 1e9 if ar["ms"] > 0 else None,
                 "link_peak_gbs": 770.0,
