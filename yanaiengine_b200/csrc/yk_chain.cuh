@@ -182,24 +182,47 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         fill();
         const int cnt = (int)min(n - pos, limit);
         if (threadIdx.x == 0) {
-            // eight terms loaded ahead of the eight dependent additions
+            // SG terms loaded together, then their SG dependent additions, then one
+            // test over the SG running values for the first step that reaches r or
+            // turns NaN (the additions past it are discarded); a per-step test and
+            // branch inside the chain cost about 70 cycles per term.
+            constexpr int SG = 16;
             float cc = c;
             long long fnd = -1;
             int t = 0;
-            bool stop = false;
-            for (int t0 = 0; t0 < cnt && !stop; t0 += 8) {
-                float v[8];
+            for (int t0 = 0; t0 < cnt; t0 += SG) {
+                const int nv = min(SG, cnt - t0);
+                float v[SG], s[SG];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = t0 + u < cnt ? slot(pos + t0 + u) : 0.f;
+                for (int u = 0; u < SG; ++u) v[u] = u < nv ? slot(pos + t0 + u) : 0.f;
+                float a = cc, last = cc;
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    if (!stop && t0 + u < cnt) {
-                        cc = __fadd_rn(cc, v[u]);
-                        t = t0 + u + 1;
-                        if (search && r <= cc) { fnd = pos + t0 + u; stop = true; }
-                        else if (isnan(cc)) { t = (int)(n - pos); stop = true; }
-                    }
+                for (int u = 0; u < SG; ++u) {
+                    a = __fadd_rn(a, v[u]);
+                    s[u] = a;
+                    if (u == nv - 1) last = a;
                 }
+                // (compile-time indices only: a runtime-indexed s[] would go to local memory)
+                int first = SG;
+                float at_first = 0.f;
+#pragma unroll
+                for (int u = SG - 1; u >= 0; --u)
+                    if (u < nv && ((search && r <= s[u]) || isnan(s[u]))) {
+                        first = u;
+                        at_first = s[u];
+                    }
+                if (first < SG) {
+                    cc = at_first;
+                    if (search && r <= cc) {
+                        fnd = pos + t0 + first;
+                        t = t0 + first + 1;
+                    } else {
+                        t = (int)(n - pos);  // NaN is absorbing
+                    }
+                    break;
+                }
+                cc = last;
+                t = t0 + nv;
             }
             cs.c_seq = cc;
             cs.pos_seq = pos + t;
