@@ -72,7 +72,8 @@ yk_status ykt_trace_read(yk_engine* e, uint64_t* host, int32_t cap, uint64_t* la
  * sampling kernel writes 8 words per CTA at [cta] and the verify kernel at
  * [cap + cta]: %globaltimer at start, row statistics done, probabilities
  * written, end; chain rounds, chain rounds ended by a special step,
- * sequential segments; the sampled token (draft).  read copies 2 x cap x 8. */
+ * sequential segments (low 32 bits) and rounding ties resolved in rounds
+ * (high 32 bits); the sampled token (draft).  read copies 2 x cap x 8. */
 yk_status ykt_sampler_stamps_enable(yk_sampler* s, int32_t cap);
 yk_status ykt_sampler_stamps_read(yk_sampler* s, uint64_t* host, int32_t cap);
 

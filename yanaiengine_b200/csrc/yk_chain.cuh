@@ -52,7 +52,7 @@ struct ChainSmem {
     float c_seq;
     long long pos_seq;
     long long found_seq;
-    int n_rounds, n_special, n_seq;  // work counters (read by the sampler's stamp test hook)
+    int n_rounds, n_special, n_seq, n_ties;  // work counters (read by the sampler's stamp test hook)
 };
 
 __device__ __forceinline__ uint32_t chain_sat(uint32_t a, uint32_t b) {
@@ -312,6 +312,7 @@ __device__ long long block_chain(ChainSmem& cs, F f, long long n, bool search, f
         // ties: rank in the round, parity of the prefix through each, resolved by thread 0
         uint32_t dstart = 0, dtotal = 0;
         if (ntie != 0) {
+            if (threadIdx.x == 0) cs.n_ties += (int)ntie;
             uint32_t rk = rank0;
 #pragma unroll
             for (int j = 0; j < CHAIN_EPT; ++j) {

@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
     unsigned long long* stp = a.stamps ? a.stamps + (size_t)blockIdx.x * 8 : nullptr;
     if (threadIdx.x == 0) {
         trace_mark(a.tr, TR_START);
-        cs.n_rounds = cs.n_special = cs.n_seq = 0;
+        cs.n_rounds = cs.n_special = cs.n_seq = cs.n_ties = 0;
         if (stp) stp[0] = globaltimer_ns();
     }
     int b, j;
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(SMP_THREADS) draft_sample_kernel(DraftArgs a) 
             stp[3] = globaltimer_ns();
             stp[4] = (unsigned long long)cs.n_rounds;
             stp[5] = (unsigned long long)cs.n_special;
-            stp[6] = (unsigned long long)cs.n_seq;
+            stp[6] = (unsigned long long)cs.n_seq | ((unsigned long long)cs.n_ties << 32);
             stp[7] = tok;
         }
     }
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
     unsigned long long* stp = a.stamps ? a.stamps + (size_t)blockIdx.x * 8 : nullptr;
     if (threadIdx.x == 0) {
         trace_mark(a.tr, TR_START);
-        cs.n_rounds = cs.n_special = cs.n_seq = 0;
+        cs.n_rounds = cs.n_special = cs.n_seq = cs.n_ties = 0;
         if (stp) stp[0] = globaltimer_ns();
     }
     const int b = blockIdx.x;
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_kernel(VerifyArgs a) {
         stp[3] = globaltimer_ns();
         stp[4] = (unsigned long long)cs.n_rounds;
         stp[5] = (unsigned long long)cs.n_special;
-        stp[6] = (unsigned long long)cs.n_seq;
+        stp[6] = (unsigned long long)cs.n_seq | ((unsigned long long)cs.n_ties << 32);
     }
     if (threadIdx.x == 0) trace_mark(a.tr, TR_END);
 }

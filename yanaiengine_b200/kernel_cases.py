@@ -82,12 +82,12 @@ def attention(args) -> None:
 
 def sampler(args) -> None:
     """Draft sampling of B x k rows and verification of B sequences from synthetic
-    N(0, 2^2) logits (yk_spec_sample_logits), with per-CTA phase stamps."""
+    N(0, s^2) logits (s = --logit-std, default 2) (yk_spec_sample_logits), with per-CTA phase stamps."""
     e = abi.Engine(0)
     B, k, V = args.seqs, args.k, args.vocab
     rng = np.random.default_rng(0)
-    dl = rng.normal(0, 2.0, (B, k, V)).astype(np.float32)
-    tl = rng.normal(0, 2.0, (B, k + 1, V)).astype(np.float32)
+    dl = rng.normal(0, args.logit_std, (B, k, V)).astype(np.float32)
+    tl = rng.normal(0, args.logit_std, (B, k + 1, V)).astype(np.float32)
     s = abi.Sampler(e, B, k, V)
     s.stamps(B * k)
     seq = np.arange(B, dtype=np.uint32)
@@ -100,11 +100,15 @@ def sampler(args) -> None:
     d, v = d.astype(np.int64), v[:B].astype(np.int64)
     ph = lambda a, i, j: np.median((a[:, j] - a[:, i]) / 1e3)
     print(f"sampler B={B} k={k} V={V} T={args.temperature}: call {1e3 * min(times):.2f} ms (with host copies)")
+    seq_d, ties_d = d[:, 6] & 0xFFFFFFFF, d[:, 6] >> 32
+    ties_v = v[:, 6] >> 32
     print(f"  draft token CTAs {len(d)}: chain {ph(d, 2, 3):.1f} us "
           f"(max {np.max((d[:, 3] - d[:, 2]) / 1e3):.1f}); rounds median {np.median(d[:, 4]):.0f} max {d[:, 4].max()}, "
-          f"special {np.median(d[:, 5]):.0f}, sequential {np.median(d[:, 6]):.0f}; span {(d[:, 3].max() - d[:, 0].min()) / 1e3:.1f} us")
+          f"special {np.median(d[:, 5]):.0f}, sequential {np.median(seq_d):.0f}, ties {np.median(ties_d):.0f}; "
+          f"span {(d[:, 3].max() - d[:, 0].min()) / 1e3:.1f} us")
     print(f"  verify CTAs {len(v)}: total {ph(v, 0, 3):.1f} us (max {np.max((v[:, 3] - v[:, 0]) / 1e3):.1f}); "
-          f"rounds median {np.median(v[:, 4]):.0f} max {v[:, 4].max()}, special {np.median(v[:, 5]):.0f}")
+          f"rounds median {np.median(v[:, 4]):.0f} max {v[:, 4].max()}, special {np.median(v[:, 5]):.0f}, "
+          f"ties {np.median(ties_v):.0f}")
     s.close()
     e.close()
 
@@ -226,6 +230,8 @@ def main() -> None:
     sp.add_argument("--vocab", type=int, default=128256)
     sp.add_argument("--temperature", type=float, default=0.8)
     sp.add_argument("--steps", type=int, default=3)
+    sp.add_argument("--logit-std", type=float, default=2.0,
+                    help="std of the synthetic N(0, s^2) logits (small: near-uniform rows, as from random-init models)")
     f = sub.add_parser("forward")
     f.add_argument("--shape", choices=sorted(FWD_SHAPES), default="draft")
     f.add_argument("--layers", type=int, default=4)
