@@ -92,6 +92,14 @@ def test_bf16_long_ragged_prefill(engine, oracle):
            prefill=((0, 300), (1, 700), (2, 150)), nb=96, max_tokens=1216)
 
 
+def test_wide_rows(engine, oracle):
+    """d_model 8192, the 70B shape's rows: the RMSNorm kernel keeps the widest rows in
+    registers (every norm unfused in fp32; the final norm's bf16 store in bf16)."""
+    cfg = dict(TINY, d_model=8192, n_layers=1, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=512)
+    _drive(engine, oracle, cfg, abi.DTYPE_F32, False, 1e-3, steps=1)
+    _drive(engine, oracle, cfg, abi.DTYPE_BF16, True, 2e-2, steps=1)
+
+
 def test_bf16_tiny_vs_fp32_oracle(engine, oracle):
     _drive(engine, oracle, TINY, abi.DTYPE_BF16, False, 5e-2)
 

@@ -111,7 +111,9 @@ __global__ void embed_kernel(const WT* __restrict__ E, const int32_t* __restrict
 // one CTA per row, fp32 statistics.  rows != nullptr gathers input rows.  The
 // row stays in registers (float4 loads, up to RN_VEC vectors per thread): one
 // read of x, one block reduction, one bf16/fp32 write.
-constexpr int RN_THREADS = 256, RN_VEC = 4;  // rows up to 4096 elements in registers
+// rows up to 8192 elements (the 70B shape's d_model) in registers; wider rows
+// take the strided loop, which re-reads the row
+constexpr int RN_THREADS = 256, RN_VEC = 8;
 __device__ __forceinline__ void store4(float* y, float a, float b, float c, float d) {
     *reinterpret_cast<float4*>(y) = make_float4(a, b, c, d);
 }
